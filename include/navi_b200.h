@@ -1,0 +1,196 @@
+/* navi_b200.h -- C ABI of the B200 (sm_100a) frame-decode engine.
+ *
+ * The reference engine (navi-tts) exposes its hot path as C++ classes; this
+ * header is the flat C boundary those classes sit on here, so a C, cgo, JNI or
+ * ctypes host can drive the same path.  Every entry point names the reference
+ * interface it replaces.  All functions return NAVI_OK or a status code;
+ * navi_last_error() gives the calling thread's message for the last failure.
+ * Device pointers are plain addresses on the navi_device's GPU.  A handle is
+ * used from one host thread at a time; handles on different GPUs are
+ * independent (request-parallel serving pins one device per thread).
+ */
+#ifndef NAVI_B200_H
+#define NAVI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---- status codes (reference: navi::Error thrown at setup, FrameResult{ok,error}
+ *      on the request path; runtime/common/error.h:10-14, model/qwen3tts/frame.h:38-44) */
+enum {
+    NAVI_OK = 0,
+    NAVI_E_ARG = 1,       /* bad argument */
+    NAVI_E_CUDA = 2,      /* a CUDA runtime call failed */
+    NAVI_E_FORMAT = 3,    /* .navi file unreadable, or its tensor table does not match the model */
+    NAVI_E_TIMEOUT = 4,   /* a device-side wait passed its deadline; the frame failed, state is clean */
+    NAVI_E_KV_FULL = 5,   /* n_past >= the KV cache's max_pos */
+    NAVI_E_LAUNCH = 6,    /* the cooperative launch was refused */
+    NAVI_E_SHAPE = 7,     /* model shape outside what the kernels are built for */
+    NAVI_E_NOMEM = 8      /* device memory exhausted */
+};
+
+enum { NAVI_RNG_PCG = 0, NAVI_RNG_PHILOX = 1 };
+
+typedef struct navi_device navi_device;
+typedef struct navi_weights navi_weights;
+typedef struct navi_frame navi_frame;
+
+/* ---- library ------------------------------------------------------------------------- */
+
+const char * navi_version(void);
+/* Message of the calling thread's last failed call ("" if none). */
+const char * navi_last_error(void);
+
+/* ---- device: replaces navi::Device (runtime/device/device.h:43-66, device.cpp:77-108) --- */
+
+typedef struct navi_device_info {
+    int ordinal;
+    char name[128];
+    int cc_major, cc_minor;
+    int multiprocessors;
+    int cooperative_launch;
+    size_t smem_per_block_optin;
+    size_t l2_bytes;
+    size_t vram_total, vram_free;
+} navi_device_info;
+
+int navi_device_count(int * n);
+/* Opens GPU `ordinal` (explicit, for request-parallel pinning): requires sm_100,
+ * cooperative launch; sets spin-wait scheduling; creates the engine stream. */
+int navi_device_open(int ordinal, navi_device ** out);
+int navi_device_get_info(const navi_device * dev, navi_device_info * info);
+/* The engine's cudaStream_t. */
+void * navi_device_stream(const navi_device * dev);
+void navi_device_close(navi_device * dev);
+
+/* ---- weights: replaces NaviFile + read_params + validate + DeviceWeights::upload
+ *      (runtime/weights/navi_file.h:40-83, device_weights.h:30-61, model/qwen3tts/params.h:17-95) */
+
+typedef struct navi_transformer_params {
+    int hidden, n_layer, n_head, n_kv_head, head_dim, ff, vocab, max_pos;
+    float rms_eps;
+    double rope_theta;
+} navi_transformer_params;
+
+typedef struct navi_params {
+    navi_transformer_params talker, cp, vocoder;
+    int text_vocab, text_hidden, n_code_groups;
+    int tts_bos_id, tts_eos_id, tts_pad_id;
+    int codec_bos_id, codec_eos_id, codec_pad_id;
+    int codec_think_id, codec_nothink_id, codec_think_bos_id, codec_think_eos_id;
+    int vq_latent, vq_codebook_dim, vq_codebook_size, vq_n_q, vq_n_semantic;
+    int decoder_dim, sliding_window;
+    int upsample_rates[4], upsampling_ratios[2];
+    int codec_upsample, sample_rate;
+    float temperature, top_p, repetition_penalty, cp_temperature, cp_top_p;
+    int top_k, cp_top_k;
+} navi_params;
+
+/* mmaps a .navi v1 file, validates its tensor table against the model its KV
+ * section describes, and uploads every weight into one 256-byte-aligned device
+ * arena (q/k/v and gate/up of each talker / code-predictor layer adjacent). */
+int navi_weights_upload(navi_device * dev, const char * path, navi_weights ** out);
+int navi_weights_get_params(const navi_weights * w, navi_params * p);
+/* Device address of a tensor by its .navi name (NULL if absent); dtype per the .navi codes. */
+const void * navi_weights_tensor(const navi_weights * w, const char * name, int * dtype, int * ndim, uint64_t dims[4]);
+uint64_t navi_weights_bytes(const navi_weights * w);
+void navi_weights_free(navi_weights * w);
+
+/* ---- KV cache: replaces navi::qwen3tts::KvCache (model/qwen3tts/talker.h:20-24);
+ *      per layer [max_pos][kv_dim] f16, K stored after RoPE. k/v are host arrays of
+ *      n_layer device pointers. */
+
+typedef struct navi_kv {
+    int n_layer, max_pos, kv_dim, n_used;
+    uint16_t ** k;
+    uint16_t ** v;
+} navi_kv;
+
+int navi_kv_create(navi_device * dev, int n_layer, int max_pos, int kv_dim, navi_kv ** out);
+void navi_kv_destroy(navi_kv * kv);
+
+/* ---- frame: replaces navi::qwen3tts::Frame (model/qwen3tts/frame.h:24-71) --------------- */
+
+typedef struct navi_sampling {      /* Sampling, frame.h:24-31, plus top-p and the stream choice */
+    float temperature;              /* <= 0: greedy */
+    int top_k;                      /* 0 or >= vocab: off */
+    float top_p;                    /* outside (0, 1): off */
+    float repetition_penalty;       /* <= 0: off; over codebook-0 ids seen this request */
+    float cp_temperature;
+    int cp_top_k;
+    float cp_top_p;
+    int min_frames;                 /* EOS suppressed before this many frames */
+    int rng;                        /* NAVI_RNG_PCG (the reference's stream) or NAVI_RNG_PHILOX */
+} navi_sampling;
+
+typedef struct navi_frame_opts {    /* FrameOptions, frame.h:33-36 */
+    int blocks_per_mp;              /* 1 */
+    uint64_t deadline_us;           /* longest any single device-side wait may take; 0: 200000 */
+} navi_frame_opts;
+
+typedef struct navi_frame_result {  /* FrameResult, frame.h:38-44 */
+    int ok;
+    int eos;
+    int32_t codes[16];
+    double us;                      /* device time of the launch */
+    int status;                     /* NAVI_OK or the failure's status code */
+} navi_frame_result;
+
+/* Frame::create (frame.hip:684-774) */
+int navi_frame_create(navi_device * dev, const navi_weights * w, const navi_frame_opts * opts, navi_frame ** out);
+/* Frame::reset (frame.hip:783-785): clears the repetition set for a new request. */
+int navi_frame_reset(navi_frame * f);
+/* Frame::run_first (frame.hip:787-796): frame 0 from the prefill's post-norm hidden and logits. */
+int navi_frame_run_first(navi_frame * f, const float * d_hidden, const float * d_logits, const float * d_trailing,
+                         const navi_sampling * s, uint64_t seed, int frame_index, navi_frame_result * r);
+/* Frame::run (frame.hip:798-810): talker step at n_past on the previous frame's step embedding. */
+int navi_frame_run(navi_frame * f, navi_kv * kv, int n_past, const float * d_trailing, const navi_sampling * s,
+                   uint64_t seed, int frame_index, navi_frame_result * r);
+/* Enqueue-only form of navi_frame_run (no host synchronisation, no result): for
+ * pipelined loops; navi_frame_collect() then returns the last enqueued frame's result. */
+int navi_frame_enqueue(navi_frame * f, navi_kv * kv, int n_past, const float * d_trailing, const navi_sampling * s,
+                       uint64_t seed, int frame_index);
+int navi_frame_collect(navi_frame * f, navi_frame_result * r);
+/* Frame::d_step_out: the next frame's step embedding [hidden] (valid until the next run). */
+const float * navi_frame_step_out(const navi_frame * f);
+/* Overrides the step embedding the next navi_frame_run starts from (device [hidden]). */
+int navi_frame_set_step_in(navi_frame * f, const float * d_step);
+/* Frame::grid_blocks / occupancy_per_mp */
+int navi_frame_grid_blocks(const navi_frame * f);
+void navi_frame_destroy(navi_frame * f);
+
+/* Inspection of the last frame (host copies): the talker's post-norm hidden [hidden],
+ * its codec logits [talker vocab], and the 15 code-predictor logit rows [15][cp vocab].
+ * Any pointer may be NULL. The reference keeps these in its Work buffers (frame.hip:51-70). */
+int navi_frame_inspect(const navi_frame * f, float * h_hidden, float * h_logits, float * h_clogits);
+
+/* Phase trace (the reference's NAVI_FRAME_PROFILE, frame.hip:522-529, 612-650, made a
+ * runtime switch): when enabled, CTA 0 records %globaltimer (ns) at the start of each
+ * launch and at the end of every phase. navi_frame_profile copies the last launch's
+ * trace: out[0] = start, out[1 + p] = end of phase p; *n = phases + 1. */
+int navi_frame_set_profile(navi_frame * f, int enable);
+int navi_frame_profile(const navi_frame * f, uint64_t * out, int cap, int * n);
+
+/* The device sampler alone, on device logits (one CTA), for parity checks of the
+ * draw: codebook 0 applies the codebook-0 modifications with `seen` (device u8[V]
+ * or NULL). Writes the chosen id to *out. */
+int navi_sample_logits(navi_device * dev, const float * d_logits, int vocab, const navi_sampling * s, uint64_t seed,
+                       int frame_index, int codebook, int suppress_from, int eos_id, const uint8_t * d_seen, int32_t * out);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NAVI_B200_H */

@@ -1,0 +1,332 @@
+// extern "C" entry points of include/navi_b200.h over the C++ classes.
+#include "../../include/navi_b200.h"
+
+#include "frame.hpp"
+#include "runtime.hpp"
+
+#include <cstring>
+#include <memory>
+#include <string>
+
+struct navi_device {
+    std::unique_ptr<navi::Device> dev;
+};
+struct navi_weights {
+    navi::DeviceWeights * w = nullptr;
+    int ordinal = 0;
+};
+struct navi_frame {
+    std::unique_ptr<navi::qwen3tts::Frame> f;
+    navi_device * dev = nullptr;
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+int set_err(int st, const std::string & m) {
+    g_err = m;
+    return st;
+}
+
+template <class F> int guard(F && fn) {
+    try {
+        return fn();
+    } catch (const navi::Error & e) {
+        return set_err(e.status ? e.status : NAVI_E_ARG, e.what());
+    } catch (const std::exception & e) {
+        return set_err(NAVI_E_ARG, e.what());
+    }
+}
+
+navi::qwen3tts::Sampling to_sampling(const navi_sampling * s) {
+    navi::qwen3tts::Sampling o;
+    if (!s) return o;
+    o.temperature = s->temperature; o.top_k = s->top_k; o.top_p = s->top_p; o.repetition_penalty = s->repetition_penalty;
+    o.cp_temperature = s->cp_temperature; o.cp_top_k = s->cp_top_k; o.cp_top_p = s->cp_top_p; o.min_frames = s->min_frames;
+    o.rng = s->rng;
+    return o;
+}
+
+void to_result(const navi::qwen3tts::FrameResult & r, navi_frame_result * out) {
+    if (!out) return;
+    std::memset(out, 0, sizeof(*out));
+    out->ok = r.ok ? 1 : 0;
+    out->eos = r.eos ? 1 : 0;
+    std::memcpy(out->codes, r.codes, sizeof(out->codes));
+    out->us = r.us;
+    out->status = r.ok ? NAVI_OK : r.status;
+}
+
+void fill_tp(navi_transformer_params & d, const navi::TransformerParams & s) {
+    d.hidden = s.hidden; d.n_layer = s.n_layer; d.n_head = s.n_head; d.n_kv_head = s.n_kv_head; d.head_dim = s.head_dim;
+    d.ff = s.ff; d.vocab = s.vocab; d.max_pos = s.max_pos; d.rms_eps = s.rms_eps; d.rope_theta = s.rope_theta;
+}
+
+} // namespace
+
+extern "C" {
+
+const char * navi_version(void) { return "navi-b200 0.1 (sm_100a)"; }
+const char * navi_last_error(void) { return g_err.c_str(); }
+
+int navi_device_count(int * n) {
+    return guard([&]() -> int {
+        if (!n) return set_err(NAVI_E_ARG, "n is NULL");
+        const cudaError_t e = cudaGetDeviceCount(n);
+        if (e == cudaErrorNoDevice) { *n = 0; (void) cudaGetLastError(); return NAVI_OK; }
+        NAVI_CUDA(e);
+        return NAVI_OK;
+    });
+}
+
+int navi_device_open(int ordinal, navi_device ** out) {
+    return guard([&]() -> int {
+        if (!out) return set_err(NAVI_E_ARG, "out is NULL");
+        auto d = std::make_unique<navi_device>();
+        d->dev = std::make_unique<navi::Device>(ordinal);
+        *out = d.release();
+        return NAVI_OK;
+    });
+}
+
+int navi_device_get_info(const navi_device * dev, navi_device_info * info) {
+    return guard([&]() -> int {
+        if (!dev || !info) return set_err(NAVI_E_ARG, "NULL argument");
+        const auto & i = dev->dev->info();
+        std::memset(info, 0, sizeof(*info));
+        info->ordinal = i.ordinal;
+        std::strncpy(info->name, i.name.c_str(), sizeof(info->name) - 1);
+        info->cc_major = i.cc_major;
+        info->cc_minor = i.cc_minor;
+        info->multiprocessors = i.multiprocessors;
+        info->cooperative_launch = i.cooperative_launch;
+        info->smem_per_block_optin = i.smem_optin;
+        info->l2_bytes = i.l2_bytes;
+        info->vram_total = i.vram_total;
+        info->vram_free = i.vram_free;
+        return NAVI_OK;
+    });
+}
+
+void * navi_device_stream(const navi_device * dev) { return dev ? static_cast<void *>(dev->dev->stream()) : nullptr; }
+
+void navi_device_close(navi_device * dev) { delete dev; }
+
+int navi_weights_upload(navi_device * dev, const char * path, navi_weights ** out) {
+    return guard([&]() -> int {
+        if (!dev || !path || !out) return set_err(NAVI_E_ARG, "NULL argument");
+        navi::NaviFile f = navi::NaviFile::open(path);
+        navi::Params p = navi::read_params(f);
+        const navi::Validation v = navi::validate(f, p);
+        if (!v.ok()) {
+            std::string m = std::string(path) + ": tensor table does not match the model";
+            if (!v.missing.empty()) m += " (missing " + v.missing[0] + ")";
+            else m += " (shape mismatch " + v.shape_mismatch[0] + ")";
+            return set_err(NAVI_E_FORMAT, m);
+        }
+        auto w = std::make_unique<navi_weights>();
+        w->w = navi::DeviceWeights::upload(*dev->dev, f, navi::fused_groups(p));
+        w->w->params_ = p;
+        w->ordinal = dev->dev->info().ordinal;
+        *out = w.release();
+        return NAVI_OK;
+    });
+}
+
+int navi_weights_get_params(const navi_weights * w, navi_params * o) {
+    return guard([&]() -> int {
+        if (!w || !o) return set_err(NAVI_E_ARG, "NULL argument");
+        const navi::Params & p = w->w->params();
+        std::memset(o, 0, sizeof(*o));
+        fill_tp(o->talker, p.talker);
+        fill_tp(o->cp, p.cp);
+        fill_tp(o->vocoder, p.vocoder);
+        o->text_vocab = p.text_vocab; o->text_hidden = p.text_hidden; o->n_code_groups = p.n_code_groups;
+        o->tts_bos_id = p.tts_bos_id; o->tts_eos_id = p.tts_eos_id; o->tts_pad_id = p.tts_pad_id;
+        o->codec_bos_id = p.codec_bos_id; o->codec_eos_id = p.codec_eos_id; o->codec_pad_id = p.codec_pad_id;
+        o->codec_think_id = p.codec_think_id; o->codec_nothink_id = p.codec_nothink_id;
+        o->codec_think_bos_id = p.codec_think_bos_id; o->codec_think_eos_id = p.codec_think_eos_id;
+        o->vq_latent = p.vq_latent; o->vq_codebook_dim = p.vq_codebook_dim; o->vq_codebook_size = p.vq_codebook_size;
+        o->vq_n_q = p.vq_n_q; o->vq_n_semantic = p.vq_n_semantic; o->decoder_dim = p.decoder_dim; o->sliding_window = p.sliding_window;
+        for (size_t i = 0; i < p.upsample_rates.size() && i < 4; ++i) o->upsample_rates[i] = p.upsample_rates[i];
+        for (size_t i = 0; i < p.upsampling_ratios.size() && i < 2; ++i) o->upsampling_ratios[i] = p.upsampling_ratios[i];
+        o->codec_upsample = p.codec_upsample; o->sample_rate = p.codec_sample_rate;
+        o->temperature = p.temperature; o->top_p = p.top_p; o->repetition_penalty = p.repetition_penalty;
+        o->cp_temperature = p.cp_temperature; o->cp_top_p = p.cp_top_p; o->top_k = p.top_k; o->cp_top_k = p.cp_top_k;
+        return NAVI_OK;
+    });
+}
+
+const void * navi_weights_tensor(const navi_weights * w, const char * name, int * dtype, int * ndim, uint64_t dims[4]) {
+    if (!w || !name) return nullptr;
+    const navi::DeviceTensor * t = w->w->find(name);
+    if (!t) return nullptr;
+    if (dtype) *dtype = static_cast<int>(t->info.dtype);
+    if (ndim) *ndim = static_cast<int>(t->info.dims.size());
+    if (dims)
+        for (size_t i = 0; i < 4; ++i) dims[i] = i < t->info.dims.size() ? t->info.dims[i] : 0;
+    return t->ptr;
+}
+
+uint64_t navi_weights_bytes(const navi_weights * w) { return w ? w->w->bytes() : 0; }
+
+void navi_weights_free(navi_weights * w) {
+    if (!w) return;
+    delete w->w;
+    delete w;
+}
+
+int navi_kv_create(navi_device * dev, int n_layer, int max_pos, int kv_dim, navi_kv ** out) {
+    return guard([&]() -> int {
+        if (!dev || !out || n_layer <= 0 || max_pos <= 0 || kv_dim <= 0) return set_err(NAVI_E_ARG, "bad KV shape");
+        dev->dev->make_current();
+        auto kv = std::make_unique<navi_kv>();
+        kv->n_layer = n_layer; kv->max_pos = max_pos; kv->kv_dim = kv_dim; kv->n_used = 0;
+        kv->k = new uint16_t *[n_layer]();
+        kv->v = new uint16_t *[n_layer]();
+        const size_t bytes = static_cast<size_t>(max_pos) * kv_dim * 2;
+        for (int l = 0; l < n_layer; ++l) {
+            NAVI_CUDA(cudaMalloc(reinterpret_cast<void **>(&kv->k[l]), bytes));
+            NAVI_CUDA(cudaMalloc(reinterpret_cast<void **>(&kv->v[l]), bytes));
+            NAVI_CUDA(cudaMemset(kv->k[l], 0, bytes));
+            NAVI_CUDA(cudaMemset(kv->v[l], 0, bytes));
+        }
+        *out = kv.release();
+        return NAVI_OK;
+    });
+}
+
+void navi_kv_destroy(navi_kv * kv) {
+    if (!kv) return;
+    for (int l = 0; l < kv->n_layer; ++l) {
+        if (kv->k) cudaFree(kv->k[l]);
+        if (kv->v) cudaFree(kv->v[l]);
+    }
+    delete[] kv->k;
+    delete[] kv->v;
+    delete kv;
+}
+
+int navi_frame_create(navi_device * dev, const navi_weights * w, const navi_frame_opts * opts, navi_frame ** out) {
+    return guard([&]() -> int {
+        if (!dev || !w || !out) return set_err(NAVI_E_ARG, "NULL argument");
+        navi::qwen3tts::FrameOptions o;
+        if (opts) {
+            o.blocks_per_mp = opts->blocks_per_mp > 0 ? opts->blocks_per_mp : 1;
+            o.deadline_us = opts->deadline_us;
+        }
+        auto f = std::make_unique<navi_frame>();
+        f->f = navi::qwen3tts::Frame::create(*dev->dev, *w->w, o);
+        f->dev = dev;
+        *out = f.release();
+        return NAVI_OK;
+    });
+}
+
+int navi_frame_reset(navi_frame * f) {
+    return guard([&]() -> int {
+        if (!f) return set_err(NAVI_E_ARG, "NULL frame");
+        f->f->reset();
+        return NAVI_OK;
+    });
+}
+
+static navi::qwen3tts::KvCache as_kv(navi_kv * kv) {
+    navi::qwen3tts::KvCache k;
+    k.n_layer = kv->n_layer; k.max_pos = kv->max_pos; k.kv_dim = kv->kv_dim; k.k = kv->k; k.v = kv->v; k.n_used = kv->n_used;
+    return k;
+}
+
+int navi_frame_run_first(navi_frame * f, const float * d_hidden, const float * d_logits, const float * d_trailing,
+                         const navi_sampling * s, uint64_t seed, int frame_index, navi_frame_result * r) {
+    return guard([&]() -> int {
+        if (!f || !d_hidden || !d_logits || !d_trailing) return set_err(NAVI_E_ARG, "NULL argument");
+        const auto res = f->f->run_first(d_hidden, d_logits, d_trailing, to_sampling(s), seed, frame_index);
+        to_result(res, r);
+        return res.ok ? NAVI_OK : set_err(res.status, res.error);
+    });
+}
+
+int navi_frame_run(navi_frame * f, navi_kv * kv, int n_past, const float * d_trailing, const navi_sampling * s, uint64_t seed,
+                   int frame_index, navi_frame_result * r) {
+    return guard([&]() -> int {
+        if (!f || !kv || !d_trailing) return set_err(NAVI_E_ARG, "NULL argument");
+        auto k = as_kv(kv);
+        const auto res = f->f->run(k, n_past, d_trailing, to_sampling(s), seed, frame_index);
+        kv->n_used = k.n_used;
+        to_result(res, r);
+        return res.ok ? NAVI_OK : set_err(res.status, res.error);
+    });
+}
+
+int navi_frame_enqueue(navi_frame * f, navi_kv * kv, int n_past, const float * d_trailing, const navi_sampling * s, uint64_t seed,
+                       int frame_index) {
+    return guard([&]() -> int {
+        if (!f || !kv || !d_trailing) return set_err(NAVI_E_ARG, "NULL argument");
+        auto k = as_kv(kv);
+        std::string err;
+        const int st = f->f->enqueue(k, n_past, d_trailing, to_sampling(s), seed, frame_index, err);
+        kv->n_used = k.n_used;
+        return st == NAVI_OK ? NAVI_OK : set_err(st, err);
+    });
+}
+
+int navi_frame_collect(navi_frame * f, navi_frame_result * r) {
+    return guard([&]() -> int {
+        if (!f) return set_err(NAVI_E_ARG, "NULL frame");
+        const auto res = f->f->collect();
+        to_result(res, r);
+        return res.ok ? NAVI_OK : set_err(res.status, res.error);
+    });
+}
+
+const float * navi_frame_step_out(const navi_frame * f) { return f ? f->f->d_step_out() : nullptr; }
+
+int navi_frame_set_step_in(navi_frame * f, const float * d_step) {
+    return guard([&]() -> int {
+        if (!f || !d_step) return set_err(NAVI_E_ARG, "NULL argument");
+        f->f->set_step_in(d_step);
+        return NAVI_OK;
+    });
+}
+
+int navi_frame_grid_blocks(const navi_frame * f) { return f ? f->f->grid_blocks() : 0; }
+
+void navi_frame_destroy(navi_frame * f) { delete f; }
+
+int navi_frame_inspect(const navi_frame * f, float * h_hidden, float * h_logits, float * h_clogits) {
+    return guard([&]() -> int {
+        if (!f) return set_err(NAVI_E_ARG, "NULL frame");
+        f->f->inspect(h_hidden, h_logits, h_clogits);
+        return NAVI_OK;
+    });
+}
+
+int navi_frame_set_profile(navi_frame * f, int enable) {
+    return guard([&]() -> int {
+        if (!f) return set_err(NAVI_E_ARG, "NULL frame");
+        f->f->set_profile(enable != 0);
+        return NAVI_OK;
+    });
+}
+
+int navi_frame_profile(const navi_frame * f, uint64_t * out, int cap, int * n) {
+    return guard([&]() -> int {
+        if (!f || !out || !n) return set_err(NAVI_E_ARG, "NULL argument");
+        *n = f->f->profile(out, cap);
+        return NAVI_OK;
+    });
+}
+
+int navi_sample_logits(navi_device * dev, const float * d_logits, int vocab, const navi_sampling * s, uint64_t seed, int frame_index,
+                       int codebook, int suppress_from, int eos_id, const uint8_t * d_seen, int32_t * out) {
+    return guard([&]() -> int {
+        if (!dev || !d_logits || !out || vocab <= 0) return set_err(NAVI_E_ARG, "bad argument");
+        *out = navi::qwen3tts::Frame::sample(*dev->dev, d_logits, vocab, to_sampling(s), seed, frame_index, codebook, suppress_from,
+                                             eos_id, d_seen);
+        return NAVI_OK;
+    });
+}
+
+} // extern "C"

@@ -1,0 +1,438 @@
+// Host side of the persistent frame kernel: weight tables, the phase programs, the
+// exchange and cache buffers, and one cooperative launch per frame
+// (reference: Frame::create / launch / run_first / run, model/qwen3tts/frame.hip:653-810).
+#include "frame.hpp"
+#include "frame_kernel.cuh"
+
+#include "../../include/navi_b200.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+namespace navi::fk {
+__global__ void k_frame(const __grid_constant__ Args A);
+__global__ void k_sample(const float * logits, int V, navi::dev::SampleCfg cfg, int * out);
+} // namespace navi::fk
+
+namespace navi::qwen3tts {
+
+using namespace navi::fk;
+
+namespace {
+
+uint64_t pcg_draw_seed(uint64_t seed, int frame_index, int codebook) {
+    const uint64_t tl = navi::dev::splitmix64(seed ^ (static_cast<uint64_t>(static_cast<int64_t>(frame_index)) * 0xA24BAED4963EE407ull));
+    if (codebook == 0) return tl;
+    const uint64_t cp = navi::dev::splitmix64(tl ^ 0x9FB21C651E98DF25ull);
+    return cp + static_cast<uint64_t>(codebook) * 0xD1B54A32D192ED03ull;
+}
+
+int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+} // namespace
+
+struct Frame::Impl {
+    int ordinal = 0;
+    cudaStream_t stream = nullptr;
+    Dims d{};
+    ModelW * dmw = nullptr;
+    Phase * prog_full = nullptr;
+    Phase * prog_first = nullptr;
+    int n_full = 0, n_first = 0;
+    Work w{};
+    float * inv_t = nullptr, * inv_c = nullptr;
+    float * step[2] = {nullptr, nullptr};
+    int cur = 0;
+    uint32_t tag = 0;
+    uint32_t last_tag = 0;
+    bool pending = false;
+    int grid = 0;
+    uint32_t ring = 0, scratch_floats = 0, part_floats = 0, smem = 0;
+    uint64_t timeout_ns = 0;
+    int eos = 0, suppress_from = 0;
+    size_t ll_bytes = 0;
+    uint64_t * ll_base = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    int32_t * h_out = nullptr;   // pinned: 16 codes + 4 control words
+    unsigned long long * prof = nullptr;
+    bool prof_on = false;
+    int last_nphase = 0;
+    std::vector<void *> owned;
+
+    template <class T> T * alloc(size_t n) {
+        void * p = nullptr;
+        NAVI_CUDA(cudaMalloc(&p, n * sizeof(T)));
+        NAVI_CUDA(cudaMemset(p, 0, n * sizeof(T)));
+        owned.push_back(p);
+        return static_cast<T *>(p);
+    }
+
+    int attn_split(int n_past) const {
+        const int cap = std::max(1, std::min(MAX_SPLIT, grid / d.NKV));
+        return std::max(1, std::min(cap, cdiv(n_past + 1, 64)));
+    }
+
+    int launch(const float * step_in, const float * hidden_in, const float * logits_in, const float * trailing, KvCache * kv,
+               int n_past, const Sampling & s, uint64_t seed, int frame_index, std::string & err) {
+        NAVI_CUDA(cudaSetDevice(ordinal));
+        Args A{};
+        const bool first = hidden_in != nullptr;
+        A.prog = first ? prog_first : prog_full;
+        A.nphase = first ? n_first : n_full;
+        A.mw = dmw;
+        A.d = d;
+        A.w = w;
+        if (tag > 0xF0000000u) {   // tags about to wrap: clear every exchange word once
+            NAVI_CUDA(cudaMemsetAsync(ll_base, 0, ll_bytes, stream));
+            NAVI_CUDA(cudaMemsetAsync(w.ctl, 0, 16, stream));
+            tag = 0;
+        }
+        tag += 4096;
+        A.tag_base = tag;
+        A.n_past = n_past;
+        A.attn_split = attn_split(n_past);
+        A.step_in = step_in;
+        A.hidden_in = hidden_in;
+        A.logits_in = logits_in;
+        A.trailing = trailing;
+        const int out = cur ^ 1;
+        A.step_out = step[out];
+        if (kv) {
+            for (int l = 0; l < d.TL; ++l) {
+                A.kc[l] = reinterpret_cast<__half *>(kv->k[l]);
+                A.vc[l] = reinterpret_cast<__half *>(kv->v[l]);
+            }
+        }
+        A.inv_freq_t = inv_t;
+        A.inv_freq_c = inv_c;
+        A.temp = s.temperature; A.top_p = s.top_p; A.rep = s.repetition_penalty; A.top_k = s.top_k;
+        A.cp_temp = s.cp_temperature; A.cp_top_p = s.cp_top_p; A.cp_top_k = s.cp_top_k;
+        A.min_frames = s.min_frames; A.rng = s.rng; A.seed = seed; A.frame_index = frame_index;
+        for (int cb = 0; cb < NCB; ++cb) A.pcg_seed[cb] = pcg_draw_seed(seed, frame_index, cb);
+        A.eos_id = eos;
+        A.suppress_from = suppress_from;
+        A.timeout_ns = timeout_ns;
+        A.ring_bytes = ring;
+        A.scratch_floats = scratch_floats;
+        A.part_floats = part_floats;
+        A.prof = prof_on ? prof : nullptr;
+        last_nphase = A.nphase;
+        NAVI_CUDA(cudaEventRecord(ev0, stream));
+        void * args[] = {&A};
+        const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(&k_frame), dim3(grid), dim3(NTHR), args, smem, stream);
+        if (e != cudaSuccess) {
+            (void) cudaGetLastError();
+            err = std::string("cooperative launch failed: ") + cudaGetErrorString(e);
+            return NAVI_E_LAUNCH;
+        }
+        NAVI_CUDA(cudaEventRecord(ev1, stream));
+        NAVI_CUDA(cudaMemcpyAsync(h_out, w.codes, NCB * sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
+        NAVI_CUDA(cudaMemcpyAsync(h_out + NCB, w.ctl, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
+        cur = out;
+        last_tag = tag;
+        pending = true;
+        return NAVI_OK;
+    }
+
+    FrameResult collect() {
+        FrameResult r;
+        if (!pending) { r.status = NAVI_E_ARG; r.error = "no frame enqueued"; return r; }
+        pending = false;
+        NAVI_CUDA(cudaSetDevice(ordinal));
+        NAVI_CUDA(cudaStreamSynchronize(stream));
+        float ms = 0.f;
+        NAVI_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
+        r.us = ms * 1000.0;
+        const uint32_t * ctl = reinterpret_cast<const uint32_t *>(h_out + NCB);
+        if (ctl[2] == last_tag || ctl[0] != last_tag) {
+            r.status = NAVI_E_TIMEOUT;
+            r.error = "device wait timed out in phase " + std::to_string(ctl[1]) + " (CTA " + std::to_string(ctl[3]) +
+                      "): the cooperative grid could not run to completion";
+            return r;
+        }
+        std::memcpy(r.codes, h_out, sizeof(r.codes));
+        r.eos = r.codes[0] == eos;
+        r.ok = true;
+        return r;
+    }
+};
+
+std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & wts, const FrameOptions & opt) {
+    std::unique_ptr<Frame> f(new Frame());
+    f->impl_ = std::make_unique<Impl>();
+    Impl & I = *f->impl_;
+    dev.make_current();
+    I.ordinal = dev.info().ordinal;
+    I.stream = dev.stream();
+    const Params & p = wts.params();
+    const auto & tp = p.talker;
+    const auto & cp = p.cp;
+    // shapes the kernel is built for
+    if (tp.hidden != cp.hidden || tp.n_head != cp.n_head || tp.n_kv_head != cp.n_kv_head || tp.head_dim != cp.head_dim || tp.ff != cp.ff)
+        fail("frame: the talker and code predictor must share hidden/heads/head_dim/ff", NAVI_E_SHAPE);
+    if (tp.n_layer > MAX_TL || cp.n_layer > MAX_CP) fail("frame: too many layers for the kernel", NAVI_E_SHAPE);
+    if (p.n_code_groups != NCB) fail("frame: the kernel is built for 16 codebooks", NAVI_E_SHAPE);
+    if (tp.head_dim != 64 && tp.head_dim != 128) fail("frame: head_dim must be 64 or 128", NAVI_E_SHAPE);
+    if (tp.n_head % tp.n_kv_head != 0 || tp.n_head / tp.n_kv_head > MAX_GROUP) fail("frame: unsupported GQA grouping", NAVI_E_SHAPE);
+    const int Q = tp.n_head * tp.head_dim, KV = tp.n_kv_head * tp.head_dim;
+    if (tp.hidden % 256 || Q % 256 || tp.ff % 256) fail("frame: hidden, n_head*head_dim and ff must be multiples of 256", NAVI_E_SHAPE);
+    if (opt.blocks_per_mp != 1) fail("frame: blocks_per_mp must be 1 (one CTA per SM)", NAVI_E_ARG);
+    Dims & d = I.d;
+    d.H = tp.hidden; d.NH = tp.n_head; d.NKV = tp.n_kv_head; d.HD = tp.head_dim; d.F = tp.ff;
+    d.TV = tp.vocab; d.CV = cp.vocab; d.TL = tp.n_layer; d.CL = cp.n_layer;
+    d.Q = Q; d.KV = KV; d.QKV = Q + 2 * KV; d.GROUP = tp.n_head / tp.n_kv_head;
+    d.eps_t = tp.rms_eps; d.eps_c = cp.rms_eps;
+    I.grid = dev.info().multiprocessors * opt.blocks_per_mp;
+    if (d.NKV > I.grid) fail("frame: more KV heads than CTAs", NAVI_E_SHAPE);
+    I.eos = p.codec_eos_id;
+    I.suppress_from = tp.vocab - 1024;   // HF suppress_tokens = range(vocab - 1024, vocab) minus EOS (frame.hip:760)
+    I.timeout_ns = (opt.deadline_us ? opt.deadline_us : 200000ull) * 1000ull;
+
+    // weight tables
+    ModelW hw{};
+    auto f16p = [&](const std::string & n) { return reinterpret_cast<const __half *>(wts.get(n).ptr); };
+    auto f32p = [&](const std::string & n) { return wts.get(n).as<float>(); };
+    auto layer = [&](const std::string & prefix, int l) {
+        const std::string lp = prefix + ".layers." + std::to_string(l) + ".";
+        LayerW L{};
+        L.ln1 = f32p(lp + "input_layernorm.weight");
+        L.ln2 = f32p(lp + "post_attention_layernorm.weight");
+        L.qn = f32p(lp + "self_attn.q_norm.weight");
+        L.kn = f32p(lp + "self_attn.k_norm.weight");
+        const __half * wq = f16p(lp + "self_attn.q_proj.weight");
+        const __half * wk = f16p(lp + "self_attn.k_proj.weight");
+        const __half * wv = f16p(lp + "self_attn.v_proj.weight");
+        if (wk != wq + static_cast<size_t>(Q) * d.H || wv != wk + static_cast<size_t>(KV) * d.H)
+            fail("frame: q/k/v of " + lp + " are not adjacent in the weight arena", NAVI_E_FORMAT);
+        L.wqkv = wq;
+        L.wo = f16p(lp + "self_attn.o_proj.weight");
+        L.wg = f16p(lp + "mlp.gate_proj.weight");
+        L.wu = f16p(lp + "mlp.up_proj.weight");
+        L.wd = f16p(lp + "mlp.down_proj.weight");
+        return L;
+    };
+    for (int l = 0; l < d.TL; ++l) hw.tl[l] = layer("talker.model", l);
+    for (int l = 0; l < d.CL; ++l) hw.cp[l] = layer("talker.code_predictor.model", l);
+    hw.tl_norm = f32p("talker.model.norm.weight");
+    hw.cp_norm = f32p("talker.code_predictor.model.norm.weight");
+    hw.codec_head = f16p("talker.codec_head.weight");
+    hw.tl_emb = f16p("talker.model.codec_embedding.weight");
+    for (int i = 0; i < NCB - 1; ++i) {
+        hw.cp_emb[i] = f16p("talker.code_predictor.model.codec_embedding." + std::to_string(i) + ".weight");
+        hw.lm_head[i] = f16p("talker.code_predictor.lm_head." + std::to_string(i) + ".weight");
+    }
+    I.dmw = I.alloc<ModelW>(1);
+    NAVI_CUDA(cudaMemcpy(I.dmw, &hw, sizeof(ModelW), cudaMemcpyHostToDevice));
+
+    // phase programs: with the talker step, and frame 0 (code predictor only)
+    auto build = [&](bool with_talker) {
+        std::vector<Phase> v;
+        if (with_talker) {
+            for (int l = 0; l < d.TL; ++l)
+                for (uint8_t op : {TQKV, TATTN, TO, TGU, TDOWN}) v.push_back({op, 1, static_cast<uint8_t>(l), 0});
+            v.push_back({THEAD, 1, 0, 0});
+        }
+        for (int l = 0; l < d.CL; ++l)
+            for (uint8_t op : {CQKV, CATTN, CO, CGU, CDOWN}) v.push_back({op, 2, static_cast<uint8_t>(l), 0});
+        v.push_back({CHEAD, 2, 0, 1});
+        for (int pos = 2; pos < NCB; ++pos) {
+            for (int l = 0; l < d.CL; ++l)
+                for (uint8_t op : {CQKV, CATTN, CO, CGU, CDOWN}) v.push_back({op, 1, static_cast<uint8_t>(l), static_cast<uint8_t>(pos)});
+            v.push_back({CHEAD, 1, 0, static_cast<uint8_t>(pos)});
+        }
+        v.push_back({FINAL, 1, 0, 0});
+        return v;
+    };
+    const auto pf = build(true), p0 = build(false);
+    I.n_full = static_cast<int>(pf.size());
+    I.n_first = static_cast<int>(p0.size());
+    if (I.n_full >= 4096) fail("frame: phase program too long", NAVI_E_SHAPE);
+    I.prog_full = I.alloc<Phase>(pf.size());
+    I.prog_first = I.alloc<Phase>(p0.size());
+    NAVI_CUDA(cudaMemcpy(I.prog_full, pf.data(), pf.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+    NAVI_CUDA(cudaMemcpy(I.prog_first, p0.data(), p0.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+
+    // exchange words (one allocation, cleared when tags wrap)
+    const size_t n_x = 2ull * d.H, n_qkv = 2ull * d.QKV, n_attn = 2ull * d.Q, n_h = 2ull * d.F, n_lg = d.TV,
+                 n_clg = static_cast<size_t>(NCB - 1) * d.CV, n_part = static_cast<size_t>(d.NKV) * MAX_SPLIT * 2 * MAX_GROUP * (d.HD + 2);
+    const size_t n_ll = n_x + n_qkv + n_attn + n_h + n_lg + n_clg + n_part;
+    I.ll_base = I.alloc<uint64_t>(n_ll);
+    I.ll_bytes = n_ll * sizeof(uint64_t);
+    uint64_t * q = I.ll_base;
+    I.w.x = q; q += n_x;
+    I.w.qkv = q; q += n_qkv;
+    I.w.attn = q; q += n_attn;
+    I.w.h = q; q += n_h;
+    I.w.logits = q; q += n_lg;
+    I.w.clogits = q; q += n_clg;
+    I.w.part = q;
+    I.w.ckc = I.alloc<__half>(static_cast<size_t>(d.CL) * NCB * KV);
+    I.w.cvc = I.alloc<__half>(static_cast<size_t>(d.CL) * NCB * KV);
+    I.w.seen = I.alloc<uint8_t>(d.TV);
+    I.w.codes = I.alloc<int32_t>(NCB);
+    I.w.hidden = I.alloc<float>(d.H);
+    I.w.ctl = I.alloc<unsigned>(4);
+    I.step[0] = I.alloc<float>(d.H);
+    I.step[1] = I.alloc<float>(d.H);
+    // RoPE inverse frequencies theta^(-2t/hd), computed in double, stored as f32
+    auto inv = [&](double theta) {
+        std::vector<float> v(d.HD / 2);
+        for (int t = 0; t < d.HD / 2; ++t) v[t] = static_cast<float>(1.0 / std::pow(theta, 2.0 * t / d.HD));
+        float * dv = I.alloc<float>(v.size());
+        NAVI_CUDA(cudaMemcpy(dv, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+        return dv;
+    };
+    I.inv_t = inv(tp.rope_theta);
+    I.inv_c = inv(cp.rope_theta);
+
+    // shared memory: everything but the ring is sized from the shapes; the ring takes the rest
+    const int G = I.grid, Vmax = std::max(d.TV, d.CV);
+    const uint32_t xin = 2u * std::max(d.H, std::max(d.Q, d.F));
+    const uint32_t samp = 4u * Vmax + (Vmax + 3) / 4 + 256 + 64;
+    const uint32_t att = 2u * MAX_GROUP * d.HD + 4u * d.HD + static_cast<uint32_t>(NCW) * 2 * d.GROUP * (d.HD + 2);
+    I.scratch_floats = std::max(xin, std::max(samp, att));
+    auto part_need = [&](int rows, int cols, int ncol) { return static_cast<uint32_t>(ncol * rows * (cols / 256)); };
+    I.part_floats = std::max({part_need(cdiv(d.QKV, G), d.H, 2), part_need(cdiv(d.H, G), d.Q, 2), part_need(2 * cdiv(d.F, G), d.H, 2),
+                              part_need(cdiv(d.H, G), d.F, 2), part_need(cdiv(d.TV, G), d.H, 1), part_need(cdiv(d.CV, G), d.H, 1)});
+    const SmemLayout L0 = smem_layout(d, 0, I.scratch_floats, I.part_floats);
+    const uint32_t optin = static_cast<uint32_t>(dev.info().smem_optin);
+    if (L0.total + 16384 > optin) fail("frame: shared memory too small for the model shape", NAVI_E_SHAPE);
+    I.ring = (optin - L0.total) / 128 * 128;
+    const uint32_t max_chunk = std::max({static_cast<uint32_t>(cdiv(d.QKV, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.H, G) * d.Q * 2),
+                                         static_cast<uint32_t>(2 * cdiv(d.F, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.H, G) * d.F * 2),
+                                         static_cast<uint32_t>(cdiv(d.TV, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.CV, G) * d.H * 2)});
+    if (max_chunk > I.ring) fail("frame: a phase's weight slice does not fit the shared-memory ring", NAVI_E_SHAPE);
+    I.smem = smem_layout(d, I.ring, I.scratch_floats, I.part_floats).total;
+    NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_frame), cudaFuncAttributeMaxDynamicSharedMemorySize, I.smem));
+    int occ = 0;
+    NAVI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, reinterpret_cast<const void *>(&k_frame), NTHR, I.smem));
+    if (occ < 1) fail("frame: k_frame cannot be resident with " + std::to_string(I.smem) + " bytes of shared memory", NAVI_E_SHAPE);
+    NAVI_CUDA(cudaEventCreate(&I.ev0));
+    NAVI_CUDA(cudaEventCreate(&I.ev1));
+    void * h = nullptr;
+    NAVI_CUDA(cudaMallocHost(&h, (NCB + 4) * sizeof(int32_t)));
+    I.h_out = static_cast<int32_t *>(h);
+    return f;
+}
+
+Frame::~Frame() {
+    if (!impl_) return;
+    cudaSetDevice(impl_->ordinal);
+    if (impl_->pending) cudaStreamSynchronize(impl_->stream);
+    if (impl_->ev0) cudaEventDestroy(impl_->ev0);
+    if (impl_->ev1) cudaEventDestroy(impl_->ev1);
+    if (impl_->h_out) cudaFreeHost(impl_->h_out);
+    for (void * p : impl_->owned) cudaFree(p);
+}
+
+void Frame::reset() {
+    NAVI_CUDA(cudaSetDevice(impl_->ordinal));
+    NAVI_CUDA(cudaMemsetAsync(impl_->w.seen, 0, static_cast<size_t>(impl_->d.TV), impl_->stream));
+}
+
+FrameResult Frame::run_first(const float * d_hidden, const float * d_logits, const float * d_trailing, const Sampling & s,
+                             uint64_t seed, int frame_index) {
+    Impl & I = *impl_;
+    std::string err;
+    const int st = I.launch(nullptr, d_hidden, d_logits, d_trailing, nullptr, 0, s, seed, frame_index, err);
+    if (st != NAVI_OK) { FrameResult r; r.status = st; r.error = err; return r; }
+    return I.collect();
+}
+
+int Frame::enqueue(KvCache & kv, int n_past, const float * d_trailing, const Sampling & s, uint64_t seed, int frame_index,
+                   std::string & err) {
+    Impl & I = *impl_;
+    if (n_past < 0 || n_past >= kv.max_pos) { err = "KV cache full"; return NAVI_E_KV_FULL; }
+    if (kv.n_layer != I.d.TL || kv.kv_dim != I.d.KV) { err = "KV cache layout does not match the talker"; return NAVI_E_ARG; }
+    const int st = I.launch(I.step[I.cur], nullptr, nullptr, d_trailing, &kv, n_past, s, seed, frame_index, err);
+    if (st == NAVI_OK) kv.n_used = n_past + 1;
+    return st;
+}
+
+FrameResult Frame::run(KvCache & kv, int n_past, const float * d_trailing, const Sampling & s, uint64_t seed, int frame_index) {
+    std::string err;
+    const int st = enqueue(kv, n_past, d_trailing, s, seed, frame_index, err);
+    if (st != NAVI_OK) { FrameResult r; r.status = st; r.error = err; return r; }
+    return impl_->collect();
+}
+
+FrameResult Frame::collect() { return impl_->collect(); }
+
+const float * Frame::d_step_out() const { return impl_->step[impl_->cur]; }
+
+void Frame::set_step_in(const float * d_step) {
+    Impl & I = *impl_;
+    NAVI_CUDA(cudaSetDevice(I.ordinal));
+    NAVI_CUDA(cudaMemcpyAsync(I.step[I.cur], d_step, static_cast<size_t>(I.d.H) * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+}
+
+int Frame::grid_blocks() const { return impl_->grid; }
+
+void Frame::set_profile(bool on) {
+    Impl & I = *impl_;
+    if (on && !I.prof) I.prof = I.alloc<unsigned long long>(4097);
+    I.prof_on = on;
+}
+
+int Frame::profile(uint64_t * out, int cap) const {
+    const Impl & I = *impl_;
+    if (!I.prof) return 0;
+    NAVI_CUDA(cudaSetDevice(I.ordinal));
+    NAVI_CUDA(cudaStreamSynchronize(I.stream));
+    const int n = std::min(cap, I.last_nphase + 1);
+    std::vector<unsigned long long> tmp(I.last_nphase + 1);
+    NAVI_CUDA(cudaMemcpy(tmp.data(), I.prof, tmp.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+    // device layout: [p] = end of phase p, [nphase] = start; reorder to start first
+    if (n > 0) out[0] = tmp[I.last_nphase];
+    for (int p = 0; p + 1 < n; ++p) out[p + 1] = tmp[p];
+    return n;
+}
+
+void Frame::inspect(float * hidden, float * logits, float * clogits) const {
+    const Impl & I = *impl_;
+    NAVI_CUDA(cudaSetDevice(I.ordinal));
+    NAVI_CUDA(cudaStreamSynchronize(I.stream));
+    if (hidden) NAVI_CUDA(cudaMemcpy(hidden, I.w.hidden, static_cast<size_t>(I.d.H) * sizeof(float), cudaMemcpyDeviceToHost));
+    auto unpack = [](const uint64_t * src, size_t n, float * dst) {
+        std::vector<uint64_t> tmp(n);
+        NAVI_CUDA(cudaMemcpy(tmp.data(), src, n * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < n; ++i) {
+            const uint32_t b = static_cast<uint32_t>(tmp[i]);
+            std::memcpy(&dst[i], &b, 4);
+        }
+    };
+    if (logits) unpack(I.w.logits, static_cast<size_t>(I.d.TV), logits);
+    if (clogits) unpack(I.w.clogits, static_cast<size_t>(NCB - 1) * I.d.CV, clogits);
+}
+
+int Frame::sample(const Device & dev, const float * d_logits, int vocab, const Sampling & s, uint64_t seed, int frame_index,
+                  int codebook, int suppress_from, int eos_id, const uint8_t * d_seen) {
+    dev.make_current();
+    navi::dev::SampleCfg c{};
+    if (codebook == 0) {
+        c.temperature = s.temperature; c.top_k = s.top_k; c.top_p = s.top_p;
+        c.talker_mods = 1; c.suppress_from = suppress_from; c.eos_id = eos_id; c.min_frames = s.min_frames;
+        c.repetition_penalty = d_seen ? s.repetition_penalty : 0.f;
+        c.seen = d_seen;
+    } else {
+        c.temperature = s.cp_temperature; c.top_k = s.cp_top_k; c.top_p = s.cp_top_p;
+    }
+    c.rng = s.rng; c.seed = seed; c.frame_index = frame_index; c.codebook = codebook;
+    c.pcg_seed = pcg_draw_seed(seed, frame_index, codebook);
+    int * d_out = nullptr;
+    NAVI_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&d_out), sizeof(int), dev.stream()));
+    const size_t smem = (4ull * vocab + (vocab + 3) / 4 + 256 + 64) * sizeof(float);
+    NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_sample), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(smem)));
+    k_sample<<<1, NCT, smem, dev.stream()>>>(d_logits, vocab, c, d_out);
+    NAVI_CUDA(cudaGetLastError());
+    int h = -1;
+    NAVI_CUDA(cudaMemcpyAsync(&h, d_out, sizeof(int), cudaMemcpyDeviceToHost, dev.stream()));
+    NAVI_CUDA(cudaFreeAsync(d_out, dev.stream()));
+    NAVI_CUDA(cudaStreamSynchronize(dev.stream()));
+    return h;
+}
+
+} // namespace navi::qwen3tts

@@ -1,0 +1,242 @@
+"""Python mirror of the reference engine's classes over the C ABI.
+
+Device      <- navi::Device        (runtime/device/device.h:43-66)
+Weights     <- NaviFile + DeviceWeights + Params (runtime/weights/*, model/qwen3tts/params.h)
+KvCache     <- navi::qwen3tts::KvCache (model/qwen3tts/talker.h:20-24)
+Frame       <- navi::qwen3tts::Frame   (model/qwen3tts/frame.h:46-71)
+
+Same method names and argument meaning; failures raise NaviError carrying the
+C status code (the reference throws navi::Error at setup and returns
+FrameResult{ok=false} on the request path; Frame.run here returns the result
+with ok=False and status set, and raises only on setup/argument errors).
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import byref, c_int, c_int32, c_uint16, c_void_p, POINTER
+from dataclasses import dataclass, field
+
+from . import capi
+from .capi import check, lib
+
+
+@dataclass
+class Sampling:
+    """navi::qwen3tts::Sampling (frame.h:24-31) plus top-p and the RNG stream."""
+    temperature: float = 0.9
+    top_k: int = 50
+    top_p: float = 1.0
+    repetition_penalty: float = 1.05
+    cp_temperature: float = 0.9
+    cp_top_k: int = 50
+    cp_top_p: float = 1.0
+    min_frames: int = 2
+    rng: int = capi.NAVI_RNG_PCG
+
+    def c(self) -> capi.Sampling:
+        return capi.Sampling(self.temperature, self.top_k, self.top_p, self.repetition_penalty, self.cp_temperature,
+                             self.cp_top_k, self.cp_top_p, self.min_frames, self.rng)
+
+
+@dataclass
+class FrameResult:
+    ok: bool
+    eos: bool
+    codes: list
+    us: float
+    status: int
+    error: str = ""
+
+
+class Device:
+    def __init__(self, ordinal: int = 0):
+        h = c_void_p()
+        check(lib().navi_device_open(ordinal, byref(h)))
+        self.h = h
+        info = capi.DeviceInfo()
+        check(lib().navi_device_get_info(self.h, byref(info)))
+        self.info = info
+
+    @staticmethod
+    def count() -> int:
+        n = c_int(0)
+        check(lib().navi_device_count(byref(n)))
+        return n.value
+
+    @property
+    def stream(self) -> int:
+        return lib().navi_device_stream(self.h)
+
+    def close(self):
+        if self.h:
+            lib().navi_device_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Weights:
+    def __init__(self, dev: Device, path: str):
+        h = c_void_p()
+        check(lib().navi_weights_upload(dev.h, str(path).encode(), byref(h)))
+        self.h = h
+        self.dev = dev
+        p = capi.Params()
+        check(lib().navi_weights_get_params(self.h, byref(p)))
+        self.params = p
+
+    def tensor(self, name: str) -> int:
+        return lib().navi_weights_tensor(self.h, name.encode(), None, None, None) or 0
+
+    @property
+    def nbytes(self) -> int:
+        return lib().navi_weights_bytes(self.h)
+
+    def close(self):
+        if self.h:
+            lib().navi_weights_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class KvCache:
+    """Per layer [max_pos][kv_dim] f16 device buffers. Either allocated by the library
+    (from_device) or wrapping caller-owned device tensors (wrap), e.g. torch tensors."""
+
+    def __init__(self):
+        self._owned = None
+        self._keep = None
+        self.s = None
+
+    @staticmethod
+    def create(dev: Device, n_layer: int, max_pos: int, kv_dim: int) -> "KvCache":
+        kv = KvCache()
+        ptr = POINTER(capi.KV)()
+        check(lib().navi_kv_create(dev.h, n_layer, max_pos, kv_dim, byref(ptr)))
+        kv._owned = ptr
+        kv.s = ptr.contents
+        return kv
+
+    @staticmethod
+    def wrap(k_ptrs, v_ptrs, max_pos: int, kv_dim: int, n_used: int = 0, keepalive=None) -> "KvCache":
+        kv = KvCache()
+        n = len(k_ptrs)
+        ka = (POINTER(c_uint16) * n)(*[ctypes.cast(c_void_p(p), POINTER(c_uint16)) for p in k_ptrs])
+        va = (POINTER(c_uint16) * n)(*[ctypes.cast(c_void_p(p), POINTER(c_uint16)) for p in v_ptrs])
+        kv.s = capi.KV(n, max_pos, kv_dim, n_used, ka, va)
+        kv._keep = (ka, va, keepalive)
+        return kv
+
+    def ptr(self):
+        return self._owned if self._owned is not None else byref(self.s)
+
+    @property
+    def n_used(self) -> int:
+        return self.s.n_used
+
+    def close(self):
+        if self._owned is not None:
+            lib().navi_kv_destroy(self._owned)
+            self._owned = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _result(r: capi.FrameResult, st: int) -> FrameResult:
+    err = "" if st == capi.NAVI_OK else lib().navi_last_error().decode(errors="replace")
+    return FrameResult(bool(r.ok), bool(r.eos), list(r.codes), r.us, r.status if st == capi.NAVI_OK else st, err)
+
+
+class Frame:
+    """The persistent frame kernel: talker step -> cb0 sample -> 15 code-predictor steps."""
+
+    def __init__(self, dev: Device, w: Weights, deadline_us: int = 0, blocks_per_mp: int = 1):
+        h = c_void_p()
+        opts = capi.FrameOpts(blocks_per_mp, deadline_us)
+        check(lib().navi_frame_create(dev.h, w.h, byref(opts), byref(h)))
+        self.h, self.dev, self.w = h, dev, w
+
+    def reset(self):
+        check(lib().navi_frame_reset(self.h))
+
+    def run_first(self, d_hidden: int, d_logits: int, d_trailing: int, s: Sampling, seed: int, frame_index: int) -> FrameResult:
+        r = capi.FrameResult()
+        st = lib().navi_frame_run_first(self.h, c_void_p(d_hidden), c_void_p(d_logits), c_void_p(d_trailing), byref(s.c()),
+                                        seed, frame_index, byref(r))
+        return _result(r, st)
+
+    def run(self, kv: KvCache, n_past: int, d_trailing: int, s: Sampling, seed: int, frame_index: int) -> FrameResult:
+        r = capi.FrameResult()
+        st = lib().navi_frame_run(self.h, kv.ptr(), n_past, c_void_p(d_trailing), byref(s.c()), seed, frame_index, byref(r))
+        return _result(r, st)
+
+    def enqueue(self, kv: KvCache, n_past: int, d_trailing: int, s: Sampling, seed: int, frame_index: int) -> None:
+        check(lib().navi_frame_enqueue(self.h, kv.ptr(), n_past, c_void_p(d_trailing), byref(s.c()), seed, frame_index))
+
+    def collect(self) -> FrameResult:
+        r = capi.FrameResult()
+        st = lib().navi_frame_collect(self.h, byref(r))
+        return _result(r, st)
+
+    def d_step_out(self) -> int:
+        return lib().navi_frame_step_out(self.h)
+
+    def set_step_in(self, d_step: int) -> None:
+        check(lib().navi_frame_set_step_in(self.h, c_void_p(d_step)))
+
+    def grid_blocks(self) -> int:
+        return lib().navi_frame_grid_blocks(self.h)
+
+    def inspect(self):
+        """(hidden [H], logits [TV], clogits [15, CV]) of the last frame, as numpy arrays."""
+        import numpy as np
+        p = self.w.params
+        hid = np.zeros(p.talker.hidden, np.float32)
+        lg = np.zeros(p.talker.vocab, np.float32)
+        clg = np.zeros((15, p.cp.vocab), np.float32)
+        check(lib().navi_frame_inspect(self.h, hid.ctypes.data, lg.ctypes.data, clg.ctypes.data))
+        return hid, lg, clg
+
+    def set_profile(self, on: bool = True) -> None:
+        check(lib().navi_frame_set_profile(self.h, 1 if on else 0))
+
+    def profile(self):
+        """Per-phase durations (us) of the last launch, measured on CTA 0."""
+        import numpy as np
+        buf = (ctypes.c_uint64 * 4097)()
+        n = c_int(0)
+        check(lib().navi_frame_profile(self.h, buf, 4097, byref(n)))
+        t = np.array(buf[:n.value], dtype=np.float64)
+        return np.diff(t) / 1000.0
+
+    def close(self):
+        if self.h:
+            lib().navi_frame_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def sample_logits(dev: Device, d_logits: int, vocab: int, s: Sampling, seed: int, frame_index: int, codebook: int,
+                  suppress_from: int = 0, eos_id: int = -1, d_seen: int = 0) -> int:
+    out = c_int32(-1)
+    check(lib().navi_sample_logits(dev.h, c_void_p(d_logits), vocab, byref(s.c()), seed, frame_index, codebook, suppress_from,
+                                   eos_id, c_void_p(d_seen) if d_seen else None, byref(out)))
+    return out.value
