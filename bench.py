@@ -1,0 +1,312 @@
+#!/usr/bin/env python3
+"""Frame-decode benchmark: the navi-tts per-frame hot path on B200.
+
+One step = one 12.5 Hz frame at batch 1: the 28-layer talker decode step at KV length L
+(configs[1]) + codebook-0 sampling + the 15-step code predictor with top-k 50 / top-p 0.9
+/ temperature 0.9 on the Philox stream + the next step embedding, i.e. one
+launch of the persistent frame kernel.  The metric is box frames/s (1000 / ms per frame
+per GPU, summed over GPUs); every GPU decodes its own independent stream (request-parallel
+replicas, no inter-GPU traffic), so scaling is weak.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--kv L] [--impl ours|reference]
+
+`value`  device time of K back-to-back frames (CUDA events on the engine stream; weights and
+         KV already in HBM; per-frame working set ~1.1 GB, larger than the 126 MB L2).
+`e2e`    the same frames through the public C ABI, synchronous per frame, with the trailing
+         text row copied host->device from pinned memory and the 16 codes read back each frame.
+`--impl reference` times the CPU oracle (PyTorch fp32 restatement of the reference's math,
+         oracle/model.py) on a bounded sample of the same workload on the host's cores: the
+         reference's own engine is HIP-only (RDNA3) and cannot run here.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "navi-tts_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "frames/s, batch-1 frame decode (talker step + 15-step code predictor + sampling)"
+BENCH_NAVI = os.environ.get("NAVI_BENCH_NAVI", "/tmp/navi_bench_full.navi")
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def algorithmic_bytes(p, L: int) -> int:
+    """HBM bytes one frame must read at KV length L, 15 code-predictor weight passes:
+    talker layers + final norm + codec_head, the KV cache rows 0..L of every layer,
+    15 x (code-predictor layers + final norm) + 15 lm_heads (one per codebook)."""
+    def layers(t):
+        H, Q, K, F, D = t.hidden, t.n_head * t.head_dim, t.n_kv_head * t.head_dim, t.ff, t.head_dim
+        per = 2 * (Q * H + 2 * K * H + H * Q + 3 * F * H) + 4 * (2 * H + 2 * D)
+        return t.n_layer * per
+    tl, cp = p.talker, p.cp
+    talker = layers(tl) + 4 * tl.hidden + 2 * tl.vocab * tl.hidden
+    kv = tl.n_layer * 2 * (L + 1) * tl.n_kv_head * tl.head_dim * 2
+    cpb = 15 * (layers(cp) + 4 * cp.hidden) + 15 * 2 * cp.vocab * cp.hidden
+    return talker + kv + cpb
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (SM clock, max clock, throttle reasons)."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9 and parts[0] == str(self.gpu):
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit())
+        mx = max(float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(self.rows), "power_w_max": max(float(r[3]) for r in self.rows if r[3].replace(".", "").isdigit())}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic(L: int):
+    """dram bytes per frame-kernel launch from the committed ncu summary, if any."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "frame_kernel_traffic.json")) as f:
+            j = json.load(f)
+        return j.get(str(L)) or j.get("default")
+    except Exception:
+        return None
+
+
+def ensure_weights(rank: int, world: int):
+    from navi_b200 import model_spec
+    if rank == 0 and not os.path.exists(BENCH_NAVI):
+        model_spec.write_synthetic(BENCH_NAVI, model_spec.full_config(1024))
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_baseline(L: int, n_frames: int = 3):
+    """The oracle (PyTorch fp32 on the host cores) on a bounded sample of the same frame."""
+    import numpy as np
+    import torch
+    from oracle import model as om
+    torch.set_num_threads(os.cpu_count() or 1)
+    W = om.Weights.from_navi(BENCH_NAVI)
+    tl = W.tl
+    kvd = tl.n_kv_head * tl.head_dim
+    g = torch.Generator().manual_seed(L)
+    kv = [(torch.randn(L + 1, kvd, generator=g).half().float(), torch.randn(L + 1, kvd, generator=g).half().float())
+          for _ in range(tl.n_layer)]
+    step = torch.randn(tl.hidden, generator=g)
+    trailing = torch.randn(tl.hidden, generator=g)
+    s = om.Sampling(top_p=0.9, cp_top_p=0.9, rng=1)
+    seen = np.zeros(tl.vocab, np.uint8)
+    om.frame(W, step_in=step, kv=kv, n_past=L, trailing=trailing, s=s, seed=1, frame_index=0, seen=seen)   # warm-up
+    t0 = time.perf_counter()
+    for i in range(n_frames):
+        out = om.frame(W, step_in=step, kv=kv, n_past=L, trailing=trailing, s=s, seed=1, frame_index=i + 1, seen=seen)
+        step = out.step_out
+    dt = time.perf_counter() - t0
+    return {"value": n_frames / dt, "unit": "frames/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n_frames} full frames (28-layer talker step at KV {L} + 15-step code predictor + sampling), "
+                      f"PyTorch fp32 oracle, {torch.get_num_threads()} threads, after 1 warm-up frame"}
+
+
+def run_reference(args):
+    rank, local, world = dist_env()
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", init_method="env://")
+    if rank != 0:
+        return
+    ensure_weights(0, 1)
+    cb = cpu_baseline(args.kv, n_frames=max(1, min(args.steps, 3)))
+    line = {"metric": METRIC, "value": cb["value"], "unit": "frames/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, random KV)",
+            "config": {"workload": f"configs[1]+[2] frame at KV {args.kv}", "kv_len": args.kv, "batch": 1},
+            "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=900))
+    ensure_weights(rank, world)
+    from navi_b200 import engine
+
+    dev = engine.Device(local)
+    w = engine.Weights(dev, BENCH_NAVI)
+    frame = engine.Frame(dev, w)
+    p = w.params
+    tl = p.talker
+    kvd = tl.n_kv_head * tl.head_dim
+    max_pos = max(2048, args.kv) + 1
+    g = torch.Generator(device=f"cuda:{local}").manual_seed(1000 + rank)
+    k = [torch.randn(max_pos, kvd, generator=g, device=f"cuda:{local}").half() for _ in range(tl.n_layer)]
+    v = [torch.randn(max_pos, kvd, generator=g, device=f"cuda:{local}").half() for _ in range(tl.n_layer)]
+    kv = engine.KvCache.wrap([t.data_ptr() for t in k], [t.data_ptr() for t in v], max_pos, kvd, keepalive=(k, v))
+    step0 = torch.randn(tl.hidden, generator=g, device=f"cuda:{local}")
+    trailing = torch.randn(tl.hidden, generator=g, device=f"cuda:{local}")
+    s = engine.Sampling(temperature=0.9, top_k=50, top_p=0.9, repetition_penalty=1.05, cp_temperature=0.9, cp_top_k=50,
+                        cp_top_p=0.9, min_frames=2, rng=1)
+    stream = torch.cuda.ExternalStream(dev.stream, device=f"cuda:{local}")
+    seed = 20260 + rank
+
+    def frames(n, L, start):
+        for i in range(n):
+            frame.enqueue(kv, L, trailing.data_ptr(), s, seed, start + i)
+
+    def device_time(n, L):
+        frame.set_step_in(step0.data_ptr())
+        frame.reset()
+        frames(args.warmup, L, 0)
+        r = frame.collect()
+        assert r.ok, r.error
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(local)
+        if dist:
+            dist.barrier()
+        e0.record(stream)
+        frames(n, L, args.warmup)
+        e1.record(stream)
+        r = frame.collect()
+        torch.cuda.synchronize(local)
+        assert r.ok, r.error
+        return e0.elapsed_time(e1) / n   # ms per frame
+
+    L = args.kv
+    with ClockSampler(local) as clk:
+        ms = device_time(args.steps, L)
+    # e2e: public C ABI, synchronous per frame, host trailing row in, codes out
+    h_trailing = torch.empty(tl.hidden, dtype=torch.float32, pin_memory=True)
+    h_trailing.copy_(trailing.cpu())
+    d_trailing = torch.empty_like(trailing)
+    frame.set_step_in(step0.data_ptr())
+    frame.reset()
+    for i in range(args.warmup):
+        frame.run(kv, L, trailing.data_ptr(), s, seed, i)
+    torch.cuda.synchronize(local)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        with torch.cuda.stream(stream):
+            d_trailing.copy_(h_trailing, non_blocking=True)
+        r = frame.run(kv, L, d_trailing.data_ptr(), s, seed, args.warmup + i)
+        assert r.ok, r.error
+    e2e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
+    # the KV-length sweep of configs[1] (device time, fewer frames)
+    sweep = {}
+    for Ls in (64, 512, 2048):
+        sweep[str(Ls)] = round(device_time(max(10, args.steps // 4), Ls), 4)
+    # per-phase profile of one frame (CTA 0), for the record
+    frame.set_profile(True)
+    frame.run(kv, L, trailing.data_ptr(), s, seed, 10_000)
+    prof = frame.profile()
+    frame.set_profile(False)
+
+    t = torch.tensor([ms, e2e_ms], device=f"cuda:{local}", dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0]), float(t[1])
+    if rank == 0:
+        ab = algorithmic_bytes(p, L)
+        peak, kind = measured_peak()
+        achieved = ab / (ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": world * 1000.0 / ms, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 weights / f32 math", "data": "synthetic (seeded random-init weights N(0,0.02), random f16 KV)",
+            "config": {"workload": f"configs[1]+[2]: 28-layer talker step at KV {L} + 15-step code predictor, "
+                                   f"top-k 50 / top-p 0.9 / T 0.9, Philox", "kv_len": L, "batch": 1,
+                       "parallelism": f"request-parallel replicas x{world}",
+                       "l2": "per-frame working set ~1.1 GB > 126 MB L2 (no flush needed)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": ncu_traffic(L), "peak_kind": kind,
+                         "algorithmic_bytes": ab},
+            "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "frames/s", "h2d_bytes_per_step": 4 * tl.hidden,
+                    "d2h_bytes_per_step": 16 * 4 + 16},
+            "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+            "kv_sweep_ms_per_frame": sweep,
+            "phase_profile_us": {"total": round(float(prof.sum()), 1), "n_phases": int(len(prof)),
+                                 "median": round(float(np.median(prof)), 2), "max": round(float(prof.max()), 2)},
+        }
+        if args.cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(L)
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--kv", type=int, default=512)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

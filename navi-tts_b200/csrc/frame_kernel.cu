@@ -154,11 +154,16 @@ __device__ void producer(const Args & A, Sm & S) {
         }
         uint32_t total = 0;
         for (int i = 0; i < ns; ++i) total += seg[i].bytes;
-        uint64_t off = issued % RB;
-        if (off + total > RB) { issued += RB - off; off = 0; }
+        // The chunk takes virtual bytes [head, head + total) of the ring stream, contiguous in
+        // shared memory (a chunk that would straddle the end starts the next lap). It may
+        // only overwrite bytes whose data chunk the consumers have released; skipped tail
+        // bytes hold no data, hence the min() with the end of the issued data.
+        uint64_t head = issued;
+        if (head % RB + total > RB) head += RB - head % RB;
+        const uint64_t need = head + total > RB ? min(head + total - RB, issued) : 0;
         uint64_t t0 = 0;
         uint32_t spins = 0;
-        while (issued + total - S.ctrl->released > RB || chunk - S.ctrl->consumed >= NSLOT) {
+        while (S.ctrl->released < need || chunk - S.ctrl->consumed >= NSLOT) {
             if (S.ctrl->abort) { aborted = true; break; }
             if ((++spins & 63u) == 0) {
                 const uint64_t now = globaltimer();
@@ -169,11 +174,11 @@ __device__ void producer(const Args & A, Sm & S) {
         }
         if (aborted) break;
         const int slot = chunk % NSLOT;
-        S.meta_off[slot] = static_cast<uint32_t>(off);
-        issued += total;
+        S.meta_off[slot] = static_cast<uint32_t>(head % RB);
+        issued = head + total;
         S.meta_end[slot] = issued;
         mbar_arrive_expect_tx(&S.bars[slot], total);
-        uint32_t dst = static_cast<uint32_t>(off);
+        uint32_t dst = static_cast<uint32_t>(head % RB);
         for (int i = 0; i < ns; ++i) {
             const char * src = static_cast<const char *>(seg[i].src);
             for (uint32_t o = 0; o < seg[i].bytes; o += PIECE) {

@@ -25,3 +25,13 @@ def small_navi(tmp_path_factory):
     path = tmp_path_factory.mktemp("navi") / "small.navi"
     model_spec.write_synthetic(path, model_spec.small_config())
     return str(path)
+
+
+@pytest.fixture(scope="session")
+def full_navi(tmp_path_factory):
+    """The benchmark-size model (configs[1]-[3] shapes), written once per session (~2 GB)."""
+    from navi_b200 import model_spec
+    path = os.environ.get("NAVI_BENCH_NAVI", "/tmp/navi_bench_full.navi")
+    if not os.path.exists(path):
+        model_spec.write_synthetic(path, model_spec.full_config(1024))
+    return path

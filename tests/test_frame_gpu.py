@@ -137,3 +137,28 @@ def test_kv_full_is_reported(small_navi):
     trailing = torch.randn(S.H).cuda()
     r = S.frame.run(S.kv, 16, trailing.data_ptr(), engine.Sampling(), 0, 1)
     assert not r.ok and r.status == capi.NAVI_E_KV_FULL
+
+
+@pytest.mark.parametrize("n_past", [64, 512])
+def test_full_size_frame_matches_oracle(full_navi, n_past):
+    """configs[1]+[2] shapes: 28-layer talker at KV length n_past, 5-layer code predictor."""
+    S = Setup(full_navi, max_pos=2049)
+    S.fill_kv(n_past, seed=7)
+    kv_o = S.oracle_kv()
+    torch.manual_seed(4)
+    step_in, trailing = torch.randn(S.H), torch.randn(S.H)
+    sd, td = step_in.cuda(), trailing.cuda()
+    s = engine.Sampling(top_p=0.9, cp_top_p=0.9, rng=capi.NAVI_RNG_PHILOX)
+    S.frame.reset()
+    S.frame.set_step_in(sd.data_ptr())
+    r = S.frame.run(S.kv, n_past, td.data_ptr(), s, 99, 3)
+    assert r.ok, r.error
+    hid, lg, clg = S.frame.inspect()
+    hid_o, lg_o = om.talker_step(S.W, step_in, kv_o, n_past)
+    assert om.rel_l2(hid, hid_o) < REL_L2_TIGHT, om.rel_l2(hid, hid_o)
+    assert om.rel_l2(lg, lg_o) < REL_L2_TIGHT, om.rel_l2(lg, lg_o)
+    _check_codes(S, r.codes, lg, clg, s, 99, 3, np.zeros(S.TV, np.uint8))
+    _, clo = om.code_predictor(S.W, torch.from_numpy(hid), r.codes[0], oracle_sampling(s), 99, 3, teacher_codes=r.codes)
+    worst = max(om.rel_l2(clg[k], clo[k]) for k in range(15))
+    assert worst < REL_L2_TIGHT, worst
+    assert om.rel_l2(S.step_out(), om.step_embedding(S.W, r.codes, trailing)) < 1e-6

@@ -1,0 +1,85 @@
+"""Host-side model of the frame kernel's weight ring (producer warp vs consumer warps).
+
+The producer streams each phase's weight slice into a shared-memory ring; a chunk that
+would straddle the ring's end starts the next lap, and it may only overwrite bytes whose
+data chunk the consumers have released (the rule in navi-tts_b200/csrc/frame_kernel.cu,
+producer()).  This test replays that rule over the full-size phase program for several
+CTAs and ring sizes and checks that the stream never deadlocks and never overwrites
+unreleased data -- a property the GPU can only show by timing out.
+"""
+import pytest
+
+from navi_b200 import model_spec
+
+NSLOT = 16
+
+
+def phase_chunks(cfg, b, G):
+    """Weight bytes per phase on CTA b of G (0 for phases without weights), program order."""
+    tl, cp = cfg.talker, cfg.cp
+    H, Q, KV, F = tl.hidden, tl.n_head * tl.head_dim, tl.n_kv_head * tl.head_dim, tl.ff
+    QKV = Q + 2 * KV
+
+    def rows(R):
+        return (R * (b + 1)) // G - (R * b) // G
+    layer = [rows(QKV) * H * 2, 0, rows(H) * Q * 2, 2 * rows(F) * H * 2, rows(H) * F * 2]
+    out = []
+    for _ in range(tl.n_layer):
+        out += layer
+    out.append(rows(tl.vocab) * H * 2)
+    for _pass in range(15):
+        for _ in range(cp.n_layer):
+            out += layer
+        out.append(rows(cp.vocab) * H * 2)
+    out.append(0)
+    return [c for c in out if c > 0]
+
+
+def simulate(chunks, RB):
+    """Producer issues greedily under the ring rule; consumer frees one chunk per step.
+    Returns the number of chunks consumed (== len(chunks) unless the stream stalls)."""
+    issued, released, consumed = 0, 0, 0
+    meta = {}
+    nxt = 0
+    live = []   # (virtual start, virtual end) of issued, unreleased chunks
+    while consumed < len(chunks):
+        progressed = False
+        while nxt < len(chunks):
+            total = chunks[nxt]
+            head = issued
+            if head % RB + total > RB:
+                head += RB - head % RB
+            need = min(head + total - RB, issued) if head + total > RB else 0
+            if released < need or nxt - consumed >= NSLOT:
+                break
+            # the physical bytes [head % RB, +total) must not hold unreleased data
+            p0, p1 = head % RB, head % RB + total
+            for s, e in live:
+                q0, q1 = s % RB, s % RB + (e - s)
+                assert not (p0 < q1 and q0 < p1), ("overwrites live data", nxt, s, e, head)
+            meta[nxt] = head + total
+            live.append((head, head + total))
+            issued = head + total
+            nxt += 1
+            progressed = True
+        if consumed < nxt:
+            released = meta[consumed]
+            live.pop(0)
+            consumed += 1
+            progressed = True
+        if not progressed:
+            break
+    return consumed
+
+
+@pytest.mark.parametrize("G", [148, 132, 100])
+@pytest.mark.parametrize("ring_kb", [100, 160, 200])
+def test_ring_never_stalls_full_size(G, ring_kb):
+    cfg = model_spec.full_config(1024)
+    RB = ring_kb * 1024
+    for b in (0, 1, G // 2, G - 1):
+        chunks = phase_chunks(cfg, b, G)
+        if max(chunks) > RB:
+            continue   # Frame::create refuses such a ring
+        assert simulate(chunks, RB) == len(chunks), (b, G, ring_kb)
+
