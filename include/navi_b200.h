@@ -173,10 +173,11 @@ void navi_frame_destroy(navi_frame * f);
 int navi_frame_inspect(const navi_frame * f, float * h_hidden, float * h_logits, float * h_clogits);
 
 /* Phase trace (the reference's NAVI_FRAME_PROFILE, frame.hip:522-529, 612-650, made a
- * runtime switch): when enabled, CTA 0 records %globaltimer (ns) at the start of each
- * launch and at the end of every phase. navi_frame_profile copies the last launch's
- * trace: out[0] = start, out[1 + p] = end of phase p; *n = phases + 1. */
-int navi_frame_set_profile(navi_frame * f, int enable);
+ * runtime switch): when enabled, CTA `cta` records %globaltimer (ns) at the start of each
+ * launch and four stamps per phase (inputs ready, weights ready, dot products done, end).
+ * navi_frame_profile copies the last launch's trace: out[0] = start, out[1 + 4p + k] =
+ * stamp k of phase p; *n = 4 * phases + 1. */
+int navi_frame_set_profile(navi_frame * f, int enable, int cta);
 int navi_frame_profile(const navi_frame * f, uint64_t * out, int cap, int * n);
 
 /* The device sampler alone, on device logits (one CTA), for parity checks of the

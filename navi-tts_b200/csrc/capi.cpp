@@ -303,10 +303,10 @@ int navi_frame_inspect(const navi_frame * f, float * h_hidden, float * h_logits,
     });
 }
 
-int navi_frame_set_profile(navi_frame * f, int enable) {
+int navi_frame_set_profile(navi_frame * f, int enable, int cta) {
     return guard([&]() -> int {
         if (!f) return set_err(NAVI_E_ARG, "NULL frame");
-        f->f->set_profile(enable != 0);
+        f->f->set_profile(enable != 0, cta);
         return NAVI_OK;
     });
 }

@@ -13,6 +13,21 @@
 
 namespace navi::fk {
 __global__ void k_frame(const __grid_constant__ Args A);
+
+// Re-lays out an R x K row-major f16 matrix into per-CTA slices (layout in frame_kernel.cuh):
+// each thread moves one 8-column chunk (16 bytes).
+__global__ void k_slice_layout(const __half * __restrict__ W, __half * __restrict__ out, int R, int K, int G) {
+    const int nk = K / 8;
+    const size_t units = static_cast<size_t>(R) * nk;
+    for (size_t u = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; u < units; u += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int r = static_cast<int>(u / nk), kc = static_cast<int>(u % nk);
+        const int b = static_cast<int>((static_cast<long long>(r + 1) * G + R - 1) / R) - 1;   // the CTA whose rows hold r
+        int r0, r1;
+        split_rows(R, b, G, r0, r1);
+        const size_t dst = static_cast<size_t>(r0) * K + (static_cast<size_t>(kc) * (r1 - r0) + (r - r0)) * 8;
+        *reinterpret_cast<uint4 *>(out + dst) = *reinterpret_cast<const uint4 *>(W + static_cast<size_t>(r) * K + kc * 8);
+    }
+}
 __global__ void k_sample(const float * logits, int V, navi::dev::SampleCfg cfg, int * out);
 } // namespace navi::fk
 
@@ -38,6 +53,7 @@ struct Frame::Impl {
     cudaStream_t stream = nullptr;
     Dims d{};
     ModelW * dmw = nullptr;
+    __half * wslices = nullptr;   // the frame's copy of its weight matrices in per-CTA slice layout
     Phase * prog_full = nullptr;
     Phase * prog_first = nullptr;
     int n_full = 0, n_first = 0;
@@ -58,6 +74,7 @@ struct Frame::Impl {
     int32_t * h_out = nullptr;   // pinned: 16 codes + 4 control words
     unsigned long long * prof = nullptr;
     bool prof_on = false;
+    int prof_cta = 0;
     int last_nphase = 0;
     std::vector<void *> owned;
 
@@ -69,9 +86,12 @@ struct Frame::Impl {
         return static_cast<T *>(p);
     }
 
-    int attn_split(int n_past) const {
-        const int cap = std::max(1, std::min(MAX_SPLIT, grid / d.NKV));
-        return std::max(1, std::min(cap, cdiv(n_past + 1, 64)));
+    // Talker attention: cached positions in splits of `chunk` (16, more when the KV is so long
+    // that 16-position splits would outnumber the CTAs), one split per CTA.
+    void attn_plan(int n_past, int & split, int & chunk) const {
+        const int cap = std::min(MAX_SPLIT, grid);
+        chunk = std::max(16, cdiv(n_past, cap));
+        split = std::max(1, cdiv(n_past, chunk));
     }
 
     int launch(const float * step_in, const float * hidden_in, const float * logits_in, const float * trailing, KvCache * kv,
@@ -92,7 +112,15 @@ struct Frame::Impl {
         tag += 4096;
         A.tag_base = tag;
         A.n_past = n_past;
-        A.attn_split = attn_split(n_past);
+        attn_plan(n_past, A.attn_split, A.attn_chunk);
+        if (!first) {
+            const uint64_t kvb = 2ull * A.attn_chunk * d.KV * 2 + 5ull * d.HD * 2;
+            if (kvb > ring) {
+                err = "KV length " + std::to_string(n_past) + " needs " + std::to_string(kvb) + "-byte attention slices; the ring holds " +
+                      std::to_string(ring);
+                return NAVI_E_KV_FULL;
+            }
+        }
         A.step_in = step_in;
         A.hidden_in = hidden_in;
         A.logits_in = logits_in;
@@ -118,6 +146,7 @@ struct Frame::Impl {
         A.scratch_floats = scratch_floats;
         A.part_floats = part_floats;
         A.prof = prof_on ? prof : nullptr;
+        A.prof_cta = prof_cta;
         last_nphase = A.nphase;
         NAVI_CUDA(cudaEventRecord(ev0, stream));
         void * args[] = {&A};
@@ -184,13 +213,27 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     d.TV = tp.vocab; d.CV = cp.vocab; d.TL = tp.n_layer; d.CL = cp.n_layer;
     d.Q = Q; d.KV = KV; d.QKV = Q + 2 * KV; d.GROUP = tp.n_head / tp.n_kv_head;
     d.eps_t = tp.rms_eps; d.eps_c = cp.rms_eps;
-    I.grid = dev.info().multiprocessors * opt.blocks_per_mp;
-    if (d.NKV > I.grid) fail("frame: more KV heads than CTAs", NAVI_E_SHAPE);
+    if (d.NKV > dev.info().multiprocessors) fail("frame: more KV heads than CTAs", NAVI_E_SHAPE);
     I.eos = p.codec_eos_id;
     I.suppress_from = tp.vocab - 1024;   // HF suppress_tokens = range(vocab - 1024, vocab) minus EOS (frame.hip:760)
     I.timeout_ns = (opt.deadline_us ? opt.deadline_us : 200000ull) * 1000ull;
 
-    // weight tables
+    // weight tables: the frame streams its own copy of every matrix, re-laid out per CTA slice
+    I.grid = dev.info().multiprocessors * opt.blocks_per_mp;
+    const int Gs = I.grid;
+    size_t slice_elems = 0;
+    const size_t per_layer = static_cast<size_t>(d.QKV) * d.H + static_cast<size_t>(d.H) * d.Q + 2ull * d.F * d.H + static_cast<size_t>(d.H) * d.F;
+    slice_elems = per_layer * (d.TL + d.CL) + static_cast<size_t>(d.TV) * d.H + static_cast<size_t>(NCB - 1) * d.CV * d.H;
+    I.wslices = I.alloc<__half>(slice_elems);
+    size_t slice_at = 0;
+    auto sliced = [&](const __half * W, int R, int K) {
+        __half * out = I.wslices + slice_at;
+        slice_at += static_cast<size_t>(R) * K;
+        if (K % 8) fail("frame: matrix width must be a multiple of 8", NAVI_E_SHAPE);
+        k_slice_layout<<<1184, 256, 0, I.stream>>>(W, out, R, K, Gs);
+        NAVI_CUDA(cudaGetLastError());
+        return static_cast<const __half *>(out);
+    };
     ModelW hw{};
     auto f16p = [&](const std::string & n) { return reinterpret_cast<const __half *>(wts.get(n).ptr); };
     auto f32p = [&](const std::string & n) { return wts.get(n).as<float>(); };
@@ -206,23 +249,24 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
         const __half * wv = f16p(lp + "self_attn.v_proj.weight");
         if (wk != wq + static_cast<size_t>(Q) * d.H || wv != wk + static_cast<size_t>(KV) * d.H)
             fail("frame: q/k/v of " + lp + " are not adjacent in the weight arena", NAVI_E_FORMAT);
-        L.wqkv = wq;
-        L.wo = f16p(lp + "self_attn.o_proj.weight");
-        L.wg = f16p(lp + "mlp.gate_proj.weight");
-        L.wu = f16p(lp + "mlp.up_proj.weight");
-        L.wd = f16p(lp + "mlp.down_proj.weight");
+        L.wqkv = sliced(wq, d.QKV, d.H);
+        L.wo = sliced(f16p(lp + "self_attn.o_proj.weight"), d.H, d.Q);
+        L.wg = sliced(f16p(lp + "mlp.gate_proj.weight"), d.F, d.H);
+        L.wu = sliced(f16p(lp + "mlp.up_proj.weight"), d.F, d.H);
+        L.wd = sliced(f16p(lp + "mlp.down_proj.weight"), d.H, d.F);
         return L;
     };
     for (int l = 0; l < d.TL; ++l) hw.tl[l] = layer("talker.model", l);
     for (int l = 0; l < d.CL; ++l) hw.cp[l] = layer("talker.code_predictor.model", l);
     hw.tl_norm = f32p("talker.model.norm.weight");
     hw.cp_norm = f32p("talker.code_predictor.model.norm.weight");
-    hw.codec_head = f16p("talker.codec_head.weight");
+    hw.codec_head = sliced(f16p("talker.codec_head.weight"), d.TV, d.H);
     hw.tl_emb = f16p("talker.model.codec_embedding.weight");
     for (int i = 0; i < NCB - 1; ++i) {
         hw.cp_emb[i] = f16p("talker.code_predictor.model.codec_embedding." + std::to_string(i) + ".weight");
-        hw.lm_head[i] = f16p("talker.code_predictor.lm_head." + std::to_string(i) + ".weight");
+        hw.lm_head[i] = sliced(f16p("talker.code_predictor.lm_head." + std::to_string(i) + ".weight"), d.CV, d.H);
     }
+    NAVI_CUDA(cudaStreamSynchronize(I.stream));
     I.dmw = I.alloc<ModelW>(1);
     NAVI_CUDA(cudaMemcpy(I.dmw, &hw, sizeof(ModelW), cudaMemcpyHostToDevice));
 
@@ -256,7 +300,7 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
 
     // exchange words (one allocation, cleared when tags wrap)
     const size_t n_x = 2ull * d.H, n_qkv = 2ull * d.QKV, n_attn = 2ull * d.Q, n_h = 2ull * d.F, n_lg = d.TV,
-                 n_clg = static_cast<size_t>(NCB - 1) * d.CV, n_part = static_cast<size_t>(d.NKV) * MAX_SPLIT * 2 * MAX_GROUP * (d.HD + 2);
+                 n_clg = static_cast<size_t>(NCB - 1) * d.CV, n_part = static_cast<size_t>(MAX_SPLIT) * d.NH * (d.HD + 2);
     const size_t n_ll = n_x + n_qkv + n_attn + n_h + n_lg + n_clg + n_part;
     I.ll_base = I.alloc<uint64_t>(n_ll);
     I.ll_bytes = n_ll * sizeof(uint64_t);
@@ -268,8 +312,6 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     I.w.logits = q; q += n_lg;
     I.w.clogits = q; q += n_clg;
     I.w.part = q;
-    I.w.ckc = I.alloc<__half>(static_cast<size_t>(d.CL) * NCB * KV);
-    I.w.cvc = I.alloc<__half>(static_cast<size_t>(d.CL) * NCB * KV);
     I.w.seen = I.alloc<uint8_t>(d.TV);
     I.w.codes = I.alloc<int32_t>(NCB);
     I.w.hidden = I.alloc<float>(d.H);
@@ -291,18 +333,20 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     const int G = I.grid, Vmax = std::max(d.TV, d.CV);
     const uint32_t xin = 2u * std::max(d.H, std::max(d.Q, d.F));
     const uint32_t samp = 4u * Vmax + (Vmax + 3) / 4 + 256 + 64;
-    const uint32_t att = 2u * MAX_GROUP * d.HD + 4u * d.HD + static_cast<uint32_t>(NCW) * 2 * d.GROUP * (d.HD + 2);
+    const uint32_t att = std::max(2u * MAX_GROUP * d.HD + 4u * d.HD,
+                                  static_cast<uint32_t>(d.NH * d.HD + 3 * d.KV + 64 + 2 * MAX_SPLIT + NCT));
     I.scratch_floats = std::max(xin, std::max(samp, att));
-    auto part_need = [&](int rows, int cols, int ncol) { return static_cast<uint32_t>(ncol * rows * (cols / 256)); };
-    I.part_floats = std::max({part_need(cdiv(d.QKV, G), d.H, 2), part_need(cdiv(d.H, G), d.Q, 2), part_need(2 * cdiv(d.F, G), d.H, 2),
-                              part_need(cdiv(d.H, G), d.F, 2), part_need(cdiv(d.TV, G), d.H, 1), part_need(cdiv(d.CV, G), d.H, 1)});
+    const int max_nr = std::max({cdiv(d.QKV, G), cdiv(d.H, G), cdiv(d.F, G), cdiv(d.TV, G), cdiv(d.CV, G)});
+    I.part_floats = static_cast<uint32_t>(NCW * 4 * max_nr);
     const SmemLayout L0 = smem_layout(d, 0, I.scratch_floats, I.part_floats);
     const uint32_t optin = static_cast<uint32_t>(dev.info().smem_optin);
     if (L0.total + 16384 > optin) fail("frame: shared memory too small for the model shape", NAVI_E_SHAPE);
     I.ring = (optin - L0.total) / 128 * 128;
-    const uint32_t max_chunk = std::max({static_cast<uint32_t>(cdiv(d.QKV, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.H, G) * d.Q * 2),
-                                         static_cast<uint32_t>(2 * cdiv(d.F, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.H, G) * d.F * 2),
-                                         static_cast<uint32_t>(cdiv(d.TV, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.CV, G) * d.H * 2)});
+    const uint32_t H4 = 4u * d.H;
+    const uint32_t max_chunk = std::max({H4 + static_cast<uint32_t>(cdiv(d.QKV, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.H, G) * d.Q * 2),
+                                         H4 + static_cast<uint32_t>(2 * cdiv(d.F, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.H, G) * d.F * 2),
+                                         H4 + static_cast<uint32_t>(cdiv(d.TV, G) * d.H * 2), H4 + static_cast<uint32_t>(cdiv(d.CV, G) * d.H * 2),
+                                         static_cast<uint32_t>(2 * 16 * d.KV * 2 + 5 * d.HD * 2)});
     if (max_chunk > I.ring) fail("frame: a phase's weight slice does not fit the shared-memory ring", NAVI_E_SHAPE);
     I.smem = smem_layout(d, I.ring, I.scratch_floats, I.part_floats).total;
     NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_frame), cudaFuncAttributeMaxDynamicSharedMemorySize, I.smem));
@@ -370,10 +414,11 @@ void Frame::set_step_in(const float * d_step) {
 
 int Frame::grid_blocks() const { return impl_->grid; }
 
-void Frame::set_profile(bool on) {
+void Frame::set_profile(bool on, int cta) {
     Impl & I = *impl_;
-    if (on && !I.prof) I.prof = I.alloc<unsigned long long>(4097);
+    if (on && !I.prof) I.prof = I.alloc<unsigned long long>(4 * 4096 + 1);
     I.prof_on = on;
+    I.prof_cta = std::max(0, std::min(cta, I.grid - 1));
 }
 
 int Frame::profile(uint64_t * out, int cap) const {
@@ -381,12 +426,13 @@ int Frame::profile(uint64_t * out, int cap) const {
     if (!I.prof) return 0;
     NAVI_CUDA(cudaSetDevice(I.ordinal));
     NAVI_CUDA(cudaStreamSynchronize(I.stream));
-    const int n = std::min(cap, I.last_nphase + 1);
-    std::vector<unsigned long long> tmp(I.last_nphase + 1);
+    const int total = 4 * I.last_nphase + 1;
+    std::vector<unsigned long long> tmp(total);
     NAVI_CUDA(cudaMemcpy(tmp.data(), I.prof, tmp.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
-    // device layout: [p] = end of phase p, [nphase] = start; reorder to start first
-    if (n > 0) out[0] = tmp[I.last_nphase];
-    for (int p = 0; p + 1 < n; ++p) out[p + 1] = tmp[p];
+    // out[0] = launch start, out[1 + 4p + k] = stamp k of phase p
+    const int n = std::min(cap, total);
+    if (n > 0) out[0] = tmp[4 * I.last_nphase];
+    for (int i = 0; i + 1 < n; ++i) out[i + 1] = tmp[i];
     return n;
 }
 

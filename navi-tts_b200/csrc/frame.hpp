@@ -62,8 +62,8 @@ public:
     int grid_blocks() const;
     // host copies of the last frame's talker hidden, logits and code-predictor logits
     void inspect(float * hidden, float * logits, float * clogits) const;
-    // phase trace: start + end of every phase of the last launch (ns, CTA 0)
-    void set_profile(bool on);
+    // phase trace of the last launch on CTA `cta` (ns): start, then 4 stamps per phase
+    void set_profile(bool on, int cta = 0);
     int profile(uint64_t * out, int cap) const;
     // the device sampler alone (one CTA) on device logits
     static int sample(const Device & dev, const float * d_logits, int vocab, const Sampling & s, uint64_t seed, int frame_index,

@@ -24,6 +24,7 @@ struct Sm {
     float * hid;
     float * part;
     float * scratch;
+    __half * cpkv;
     uint8_t * ring;
 };
 
@@ -38,6 +39,7 @@ __device__ __forceinline__ Sm carve(char * base, const SmemLayout & L) {
     s.hid = reinterpret_cast<float *>(base + L.hid);
     s.part = reinterpret_cast<float *>(base + L.part);
     s.scratch = reinterpret_cast<float *>(base + L.scratch);
+    s.cpkv = reinterpret_cast<__half *>(base + L.cpkv);
     s.ring = reinterpret_cast<uint8_t *>(base + L.ring);
     return s;
 }
@@ -77,17 +79,6 @@ __device__ __forceinline__ bool consumers_ok(Sm & S, bool ok) {
     return !any_fail;
 }
 
-// n words -> dst (smem) by all consumer threads; ends with a (deciding) consumer barrier.
-__device__ bool ll_vec(const uint64_t * src, int n, uint32_t tag, float * dst, const Args & A, Sm & S, int phase) {
-    bool ok = true;
-    for (int i = threadIdx.x; i < n && ok; i += NCT) {
-        float v;
-        ok = ll_get(src + i, tag, v, A, S, phase);
-        dst[i] = v;
-    }
-    return consumers_ok(S, ok);
-}
-
 // ---- ring ------------------------------------------------------------------------------------
 
 __device__ bool wait_chunk(const Args & A, Sm & S, int chunk, int phase) {
@@ -116,42 +107,21 @@ __device__ __forceinline__ void release_chunk(Sm & S, int chunk) {
     }
 }
 
-__device__ void prefetch_kv(const Args & A, const Phase & ph, int b) {
-    const Dims & d = A.d;
-    const int Sp = A.attn_split;
-    if (b >= d.NKV * Sp) return;
-    int a0, a1;
-    split_rows(A.n_past + 1, b % Sp, Sp, a0, a1);
-    a1 = min(a1, A.n_past);
-    if (a1 <= a0) return;
-    const size_t row = static_cast<size_t>(d.KV) * 2;
-    const char * kp = reinterpret_cast<const char *>(A.kc[ph.layer]) + static_cast<size_t>(a0) * row;
-    const char * vp = reinterpret_cast<const char *>(A.vc[ph.layer]) + static_cast<size_t>(a0) * row;
-    const size_t bytes = static_cast<size_t>(a1 - a0) * row;
-    for (size_t o = 0; o < bytes; o += 65536) {
-        const uint32_t n = static_cast<uint32_t>(min(static_cast<size_t>(65536), bytes - o));
-        bulk_prefetch_l2(kp + o, n);
-        bulk_prefetch_l2(vp + o, n);
-    }
-}
-
 __device__ void producer(const Args & A, Sm & S) {
     if ((threadIdx.x & 31) != 0) return;
     const ModelW & W = *A.mw;
     const int G = gridDim.x, b = blockIdx.x;
+    const Rows R = cta_rows(A.d, b, G);
     const uint32_t RB = A.ring_bytes;
     uint64_t issued = 0;
     int chunk = 0;
     bool aborted = false;
     for (int p = 0; p < A.nphase && !aborted; ++p) {
         const Phase ph = A.prog[p];
-        Seg seg[2];
+        Seg seg[MAX_SEG];
         int r0, r1;
-        const int ns = phase_segments(A, W, ph, b, G, seg, r0, r1);
-        if (ns == 0) {
-            if (ph.op == TATTN) prefetch_kv(A, ph, b);
-            continue;
-        }
+        const int ns = phase_segments(A, W, ph, b, R, seg, r0, r1);
+        if (ns == 0) continue;
         uint32_t total = 0;
         for (int i = 0; i < ns; ++i) total += seg[i].bytes;
         // The chunk takes virtual bytes [head, head + total) of the ring stream, contiguous in
@@ -206,87 +176,194 @@ __device__ void producer(const Args & A, Sm & S) {
 
 // ---- consumer building blocks ---------------------------------------------------------------------
 
-// y-partials of rows [0, nrows) of a row-major f16 matrix in shared memory against NC input
-// columns. Work item = 4 rows x 256 columns; lane covers columns {4l..4l+3} and {128+4l..}.
-// part[(c * nrows + row) * nseg + seg]. Caller follows with a consumer barrier.
-template <int NC>
-__device__ void gemv_part(const __half * Ws, int nrows, int ncols, const float * xin, int xstride, float * part) {
+__device__ __forceinline__ uint32_t tag_of(uint64_t w) { return static_cast<uint32_t>(w >> 32); }
+__device__ __forceinline__ float val_of(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+
+// Fetches exchange words [0, n) (n even) carrying `tag` into dst[0, n): thread t takes the
+// pairs at 2t + 2*NCT*k, issues up to 4 pair loads at once, then re-polls only stale pairs.
+// Returns this thread's success (the caller decides with a barrier). ll_each() visits the
+// same elements in the same thread, so a transform needs no barrier in between.
+__device__ __noinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag, float * dst, const Args & A, Sm & S, int phase) {
+    constexpr int MAXK = 4;
+    for (int base = 2 * threadIdx.x; base < n; base += 2 * NCT * MAXK) {
+        uint64_t w[MAXK][2];
+#pragma unroll
+        for (int k = 0; k < MAXK; ++k) {
+            const int i = base + 2 * NCT * k;
+            if (i < n) ll_load2(src + i, w[k][0], w[k][1]);
+        }
+#pragma unroll
+        for (int k = 0; k < MAXK; ++k) {
+            const int i = base + 2 * NCT * k;
+            if (i >= n) continue;
+            if (tag_of(w[k][0]) != tag || tag_of(w[k][1]) != tag) {
+                const uint64_t t0 = globaltimer();
+                uint32_t spins = 0;
+                for (;;) {
+                    ll_load2(src + i, w[k][0], w[k][1]);
+                    if (tag_of(w[k][0]) == tag && tag_of(w[k][1]) == tag) break;
+                    if ((++spins & 31u) == 0) {
+                        if (S.ctrl->abort || launch_aborted(A)) return false;
+                        if (globaltimer() - t0 > A.timeout_ns) { raise_abort(A, S, phase); return false; }
+                    }
+                }
+            }
+            dst[i] = val_of(w[k][0]);
+            dst[i + 1] = val_of(w[k][1]);
+        }
+    }
+    return true;
+}
+
+// Visits i over the elements ll_fetch(n) gave this thread.
+template <class F>
+__device__ __forceinline__ void ll_each(int n, F && fn) {
+    for (int i = 2 * threadIdx.x; i < n; i += 2 * NCT) {
+        fn(i);
+        fn(i + 1);
+    }
+}
+
+// Per-thread wait for ring chunk `chunk` (no barrier).
+__device__ __forceinline__ bool wait_chunk_local(const Args & A, Sm & S, int chunk, int phase) {
+    const int slot = chunk % NSLOT;
+    const uint32_t parity = static_cast<uint32_t>((chunk / NSLOT) & 1);
+    if (mbar_try_wait(&S.bars[slot], parity)) return true;
+    const uint64_t t0 = globaltimer();
+    uint32_t spins = 0;
+    while (!mbar_try_wait(&S.bars[slot], parity)) {
+        if ((++spins & 15u) == 0) {
+            if (S.ctrl->abort || launch_aborted(A)) return false;
+            if (globaltimer() - t0 > A.timeout_ns) { raise_abort(A, S, phase); return false; }
+        }
+    }
+    return true;
+}
+
+// Dot products of the rows of a CTA slice ([K/8][nr][8] f16 in shared memory, see
+// frame_kernel.cuh) with NC input columns xin (f32, stride xstride). PAIR: the slice is
+// followed by a second one of the same shape (gate, then up) and unit u is the row pair.
+// Lane (row, j) with row = lane % R2, j = lane / R2 (R2 = 32 / J rows per round, both powers
+// of two, so the lane split is shifts and masks: the GPU has no integer divider and a runtime
+// division costs tens of instructions) takes 8-column chunks of its warp's K range,
+// j-interleaved, so the live lanes of a warp read consecutive 16-byte words; x chunks are
+// broadcasts. Per-warp sums are folded over j with shuffles, written to
+// part[warp][value][row], and after a consumer barrier thread (value, row) adds the NCW warp
+// sums in warp order and calls epi(unit, column, y[, y_pair]).
+template <int NC, bool PAIR, class Epi>
+__device__ __forceinline__ void gemv_slice(const __half * Ws, int nr, int K, const float * xin, int xstride, float * part, Epi && epi) {
+    constexpr int NV = NC * (PAIR ? 2 : 1);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nseg = ncols >> 8, ngrp = (nrows + 3) >> 2, nitems = ngrp * nseg;
-    for (int it = warp; it < nitems; it += NCW) {
-        const int grp = it / nseg, seg = it - grp * nseg;
-        const int col = seg * 256 + lane * 4;
-        float4 xa[NC], xb[NC];
+    const int nk = K >> 3;
+    // J lanes per row: the largest power of two with 2 * J * nr > 32 >= J * nr, i.e. at
+    // least half of the lanes live; R2 = 32 / J row slots per round
+    int lj = 0;
+    while (lj < 5 && (2 << lj) * nr <= 32) ++lj;
+    const int J = 1 << lj, lr = 5 - lj, R2 = 1 << lr;
+    const int k0 = (nk * warp) / NCW, k1 = (nk * (warp + 1)) / NCW;   // NCW is a constant: no division
+    const size_t cs = static_cast<size_t>(J) * nr * 8;                 // halves between a lane's chunks
+    const size_t up = static_cast<size_t>(nk) * nr * 8;                // gate -> up slice
+    const int j = lane >> lr;
+    // rows beyond 32 lanes (small grids) are taken in rounds of R2
+    for (int rb = 0; rb < nr; rb += R2) {
+        const int row = rb + (lane & (R2 - 1));
+        const bool live = row < nr;
+        float acc[NV];
 #pragma unroll
-        for (int c = 0; c < NC; ++c) {
-            xa[c] = *reinterpret_cast<const float4 *>(xin + c * xstride + col);
-            xb[c] = *reinterpret_cast<const float4 *>(xin + c * xstride + col + 128);
-        }
-        float acc[4][NC];
+        for (int v = 0; v < NV; ++v) acc[v] = 0.f;
+        if (live) {
+            // this lane's chunks: k0 + j, k0 + j + J, ... < k1; four per step, loads first
+            const __half * pw = Ws + (static_cast<size_t>(k0 + j) * nr + row) * 8;
+            const float * px = xin + (k0 + j) * 8;
+            const int cnt = (k0 + j < k1) ? (k1 - (k0 + j) + J - 1) >> lj : 0;
+            float a4[4][NV];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int row = grp * 4 + r;
-            if (row < nrows) {
-                const __half * wr = Ws + static_cast<size_t>(row) * ncols + col;
-                const uint2 wa = *reinterpret_cast<const uint2 *>(wr);
-                const uint2 wb = *reinterpret_cast<const uint2 *>(wr + 128);
+            for (int q = 0; q < 4; ++q)
 #pragma unroll
-                for (int c = 0; c < NC; ++c) acc[r][c] = dot4h(wa, xa[c]) + dot4h(wb, xb[c]);
-            } else {
+                for (int v = 0; v < NV; ++v) a4[q][v] = 0.f;
+            int i = 0;
+            for (; i + 4 <= cnt; i += 4) {
+                uint4 wa[4], wb[4];
+                float4 xa[4][NC], xb[4][NC];
 #pragma unroll
-                for (int c = 0; c < NC; ++c) acc[r][c] = 0.f;
+                for (int q = 0; q < 4; ++q) {
+                    wa[q] = *reinterpret_cast<const uint4 *>(pw + q * cs);
+                    if constexpr (PAIR) wb[q] = *reinterpret_cast<const uint4 *>(pw + up + q * cs);
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) {
+                        xa[q][c] = *reinterpret_cast<const float4 *>(px + c * xstride + q * J * 8);
+                        xb[q][c] = *reinterpret_cast<const float4 *>(px + c * xstride + q * J * 8 + 4);
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) {
+                        a4[q][c * (PAIR ? 2 : 1)] += dot8h(wa[q], xa[q][c], xb[q][c]);
+                        if constexpr (PAIR) a4[q][c * 2 + 1] += dot8h(wb[q], xa[q][c], xb[q][c]);
+                    }
+                pw += 4 * cs;
+                px += 4 * J * 8;
             }
-        }
+            for (; i < cnt; ++i) {
+                const uint4 wa = *reinterpret_cast<const uint4 *>(pw);
+                uint4 wb = make_uint4(0, 0, 0, 0);
+                if constexpr (PAIR) wb = *reinterpret_cast<const uint4 *>(pw + up);
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int c = 0; c < NC; ++c) acc[r][c] = warp_sum(acc[r][c]);
-        if (lane == 0) {
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const int row = grp * 4 + r;
-                if (row < nrows)
-#pragma unroll
-                    for (int c = 0; c < NC; ++c) part[(c * nrows + row) * nseg + seg] = acc[r][c];
+                for (int c = 0; c < NC; ++c) {
+                    const float4 xa = *reinterpret_cast<const float4 *>(px + c * xstride);
+                    const float4 xb = *reinterpret_cast<const float4 *>(px + c * xstride + 4);
+                    a4[0][c * (PAIR ? 2 : 1)] += dot8h(wa, xa, xb);
+                    if constexpr (PAIR) a4[0][c * 2 + 1] += dot8h(wb, xa, xb);
+                }
+                pw += cs;
+                px += J * 8;
             }
-        }
-    }
-}
-
-__device__ __forceinline__ float part_sum(const float * part, int c, int row, int nrows, int nseg) {
-    const float * p = part + (c * nrows + row) * nseg;
-    float s = 0.f;
-    for (int k = 0; k < nseg; ++k) s += p[k];
-    return s;
-}
-
-__device__ __forceinline__ void run_gemv(int ncol, const __half * Ws, int nrows, int ncols, const float * xin, int xstride,
-                                         float * part) {
-    if (ncol == 2) gemv_part<2>(Ws, nrows, ncols, xin, xstride, part);
-    else gemv_part<1>(Ws, nrows, ncols, xin, xstride, part);
-}
-
-// out[c] = x[c] * rsqrt(mean(x[c]^2) + eps) * w for c < ncol (x, out in shared memory).
-__device__ void rmsnorm_cols(Sm & S, const float * x, int xstride, const float * w, float eps, int ncol, int n, float * out,
-                             int ostride) {
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    float ss[2] = {0.f, 0.f};
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-        if (c >= ncol) continue;
-        for (int i = tid; i < n; i += NCT) { const float v = x[c * xstride + i]; ss[c] += v * v; }
-        ss[c] = warp_sum(ss[c]);
-        if (lane == 0) S.ctrl->red[c][wid] = ss[c];
+            for (int v = 0; v < NV; ++v) acc[v] = (a4[0][v] + a4[1][v]) + (a4[2][v] + a4[3][v]);
+        }
+        // fold the J lanes of each row (lanes row, row + R2, ...); dead lanes hold zeros
+        for (int s = 16; s >= R2; s >>= 1)
+#pragma unroll
+            for (int v = 0; v < NV; ++v) acc[v] += __shfl_down_sync(0xffffffffu, acc[v], s);
+        if (live && j == 0)
+#pragma unroll
+            for (int v = 0; v < NV; ++v) part[(warp * NV + v) * nr + row] = acc[v];
     }
     named_sync(BID, NCT);
-    for (int c = 0; c < ncol; ++c) {
-        float t = 0.f;
+    // column c is summed by the threads [c * TPC, (c + 1) * TPC), TPC a constant
+    constexpr int TPC = NCT / NC;
+    const int c = threadIdx.x / TPC;
+    if (c < NC)
+        for (int row = threadIdx.x - c * TPC; row < nr; row += TPC) {
+            float y = 0.f, y2 = 0.f;
 #pragma unroll
-        for (int k = 0; k < NCW; ++k) t += S.ctrl->red[c][k];
-        const float scale = rsqrtf(t / static_cast<float>(n) + eps);
-        for (int i = tid; i < n; i += NCT) out[c * ostride + i] = x[c * xstride + i] * scale * __ldg(w + i);
+            for (int w = 0; w < NCW; ++w) {
+                y += part[(w * NV + c * (PAIR ? 2 : 1)) * nr + row];
+                if constexpr (PAIR) y2 += part[(w * NV + c * 2 + 1) * nr + row];
+            }
+            epi(row, c, y, y2);
+        }
+}
+
+// Sum of squares of this thread's part of column c, folded into the CTA scratch; the total
+// is read after the next consumer barrier (norm_total).
+__device__ __forceinline__ void norm_partial(Sm & S, float ss0, float ss1, int ncol) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (ncol > 0) {
+        const float t = warp_sum(ss0);
+        if (lane == 0) S.ctrl->red[0][wid] = t;
     }
-    named_sync(BID, NCT);
+    if (ncol > 1) {
+        const float t = warp_sum(ss1);
+        if (lane == 0) S.ctrl->red[1][wid] = t;
+    }
+}
+__device__ __forceinline__ float norm_scale(Sm & S, int c, int n, float eps) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < NCW; ++k) t += S.ctrl->red[c][k];
+    return rsqrtf(t / static_cast<float>(n) + eps);
 }
 
 __device__ __forceinline__ void row_f16_to_smem(const __half * row, int n, float * dst) {
@@ -323,222 +400,258 @@ __device__ SampleCfg sample_cfg(const Args & A, int codebook) {
     return c;
 }
 
-// ---- attention phase (q/k norm + RoPE + KV store + split-KV GQA attention) ----------------------------
+// Trace stamp k (0..3) of phase p on the traced CTA: 0 inputs ready, 1 weights ready,
+// 2 dot products done, 3 phase end (attention: 0 gathered, 1 normed, 2 attended, 3 combined).
+__device__ __forceinline__ void stamp(const Args & A, int p, int k) {
+    if (A.prof && blockIdx.x == A.prof_cta && threadIdx.x == 0) A.prof[4 * p + k] = globaltimer();
+}
 
-__device__ bool attention_phase(const Args & A, Sm & S, const Phase & ph, bool talker, uint32_t tag, uint32_t ptag, int p) {
+// ---- attention -------------------------------------------------------------------------------------
+
+// Per-head RMSNorm + rotate-half RoPE at position `pos` of a head vector in shared memory,
+// by one warp (frame.hip:312-346: norm before RoPE, pairs (i, i + hd/2)). round16: store
+// the result rounded to f16 (K, as the cache holds it).
+__device__ __forceinline__ void warp_norm_rope(float * vec, const float * nw, const float * inv_freq, int HD, float eps, int pos,
+                                               bool round16) {
+    const int lane = threadIdx.x & 31, EPL = HD / 32;
+    float e[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        e[t] = t < EPL ? vec[lane + 32 * t] : 0.f;
+        ss += e[t] * e[t];
+    }
+    ss = warp_sum(ss);
+    const float scale = rsqrtf(ss / static_cast<float>(HD) + eps);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) if (t < EPL) e[t] = e[t] * scale * nw[lane + 32 * t];
+    const float fpos = static_cast<float>(pos);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        if (t >= EPL / 2) continue;
+        const int i = lane + 32 * t;
+        float sn, cs;
+        sincosf(fpos * inv_freq[i], &sn, &cs);
+        const float x0 = e[t], x1 = (EPL == 4) ? e[t + 2] : e[t + 1];
+        float r0 = x0 * cs - x1 * sn, r1 = x0 * sn + x1 * cs;
+        if (round16) { r0 = f16_round(r0); r1 = f16_round(r1); }
+        vec[i] = r0;
+        vec[i + HD / 2] = r1;
+    }
+}
+
+// Attention of query q (registers: dims [DPL*lane, +DPL)) over `n` K/V rows (f16 in shared
+// memory, row stride `stride` halves): m = max score, l = sum e^(s - m), acc = lane-local
+// dims of sum e^(s - m) v. Positions go in blocks of 16: the 16 scores come from four
+// transposed 4-way reductions and are broadcast, so the block costs one softmax update.
+template <int DPL>
+__device__ __forceinline__ void warp_attend(const float * q, const __half * K, const __half * V, int stride, int n, float scale,
+                                            float & m, float & l, float * acc) {
+    const int lane = threadIdx.x & 31;
+    m = -INFINITY;
+    l = 0.f;
+#pragma unroll
+    for (int t = 0; t < DPL; ++t) acc[t] = 0.f;
+    for (int j0 = 0; j0 < n; j0 += 16) {
+        float sc[16];
+#pragma unroll
+        for (int bq = 0; bq < 4; ++bq) {
+            float part[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int j = j0 + bq * 4 + jj;
+                float dsum = 0.f;
+                if (j < n) {
+                    const __half * kr = K + static_cast<size_t>(j) * stride + lane * DPL;
+#pragma unroll
+                    for (int t = 0; t < DPL; ++t) dsum += q[t] * __half2float(kr[t]);
+                }
+                part[jj] = dsum;
+            }
+            const float r = warp_sum_multi<4>(part);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) sc[bq * 4 + jj] = __shfl_sync(0xffffffffu, r, jj * 8) * scale;
+        }
+        const int nb = min(16, n - j0);
+        float mb = m;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) if (j < nb) mb = fmaxf(mb, sc[j]);
+        const float corr = expf(m - mb);
+        l *= corr;
+#pragma unroll
+        for (int t = 0; t < DPL; ++t) acc[t] *= corr;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (j >= nb) continue;
+            const float e = expf(sc[j] - mb);
+            l += e;
+            const __half * vr = V + static_cast<size_t>(j0 + j) * stride + lane * DPL;
+#pragma unroll
+            for (int t = 0; t < DPL; ++t) acc[t] += e * __half2float(vr[t]);
+        }
+        m = mb;
+    }
+}
+
+// Talker attention at position n_past (frame.hip:350-385): CTA s < attn_split takes the
+// cached positions [s*chunk, ...) for every head, from its ring chunk (K/V rows streamed by
+// the producer); the last split also takes the new position. Partials (m, l, acc) go to
+// the exchange words; CTA G-NH+h combines head h in split order. A single split writes the
+// output directly.
+__device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, const uint8_t * chunk_base, uint32_t tag, uint32_t ptag,
+                                 int p) {
     const Dims & d = A.d;
-    const ModelW & W = *A.mw;
-    const int HD = d.HD, GR = d.GROUP, ncol = ph.ncol, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int Sp = talker ? A.attn_split : 1;
-    const int b = blockIdx.x;
-    if (b >= d.NKV * Sp) return true;
-    const int g = b / Sp, s = b - g * Sp;
-    const int pos = talker ? A.n_past : ph.pos;
-    const LayerW & L = talker ? W.tl[ph.layer] : W.cp[ph.layer];
-    const float eps = talker ? d.eps_t : d.eps_c;
-    const float * inv_freq = talker ? A.inv_freq_t : A.inv_freq_c;
-    __half * kc = talker ? A.kc[ph.layer] : A.w.ckc + static_cast<size_t>(ph.layer) * NCB * d.KV;
-    __half * vc = talker ? A.vc[ph.layer] : A.w.cvc + static_cast<size_t>(ph.layer) * NCB * d.KV;
-    float * qs = S.scratch;                        // [2][MAX_GROUP][HD]
-    float * ks = qs + 2 * MAX_GROUP * HD;          // [2][HD]
-    float * vs = ks + 2 * HD;                      // [2][HD]
-    float * wst = vs + 2 * HD;                     // [NCW][2][MAX_GROUP][HD + 2]
-    const int WST = HD + 2;
-    // 1. this KV head's raw q (GROUP heads), k, v for each column
-    {
-        const int per = (GR + 2) * HD;
-        bool ok = true;
-        for (int i = tid; i < ncol * per && ok; i += NCT) {
-            const int c = i / per, rem = i - c * per, j = rem / HD, e = rem - j * HD;
-            const uint64_t * src = A.w.qkv + static_cast<size_t>(c) * d.QKV;
-            int idx;
-            float * dst;
-            if (j < GR) { idx = (g * GR + j) * HD + e; dst = qs + (c * MAX_GROUP + j) * HD + e; }
-            else if (j == GR) { idx = d.Q + g * HD + e; dst = ks + c * HD + e; }
-            else { idx = d.Q + d.KV + g * HD + e; dst = vs + c * HD + e; }
-            float v;
-            ok = ll_get(src + idx, ptag, v, A, S, p);
-            *dst = v;
-        }
-        if (!consumers_ok(S, ok)) return false;
-    }
-    // 2. per-head RMSNorm of q and k, RoPE at pos + c, f16 rounding of k and v
-    {
-        const int nvec = ncol * (GR + 1);
-        const int EPL = HD / 32;   // elements per lane: lane + 32 t
-        for (int v = warp; v < nvec; v += NCW) {
-            const int c = v / (GR + 1), j = v - c * (GR + 1);
-            float * vec = j < GR ? qs + (c * MAX_GROUP + j) * HD : ks + c * HD;
-            const float * nw = j < GR ? L.qn : L.kn;
-            float e[4];
-            float ss = 0.f;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                e[t] = t < EPL ? vec[lane + 32 * t] : 0.f;
-                ss += e[t] * e[t];
-            }
-            ss = warp_sum(ss);
-            const float scale = rsqrtf(ss / static_cast<float>(HD) + eps);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) if (t < EPL) e[t] = e[t] * scale * __ldg(nw + lane + 32 * t);
-            const float fpos = static_cast<float>(pos + c);
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-                if (t >= EPL / 2) continue;
-                const int i = lane + 32 * t;   // pairs (i, i + HD/2)
-                const float ang = fpos * __ldg(inv_freq + i);
-                float sn, cs;
-                sincosf(ang, &sn, &cs);
-                const float x0 = e[t], x1 = (EPL == 4) ? e[t + 2] : e[t + 1];
-                float r0 = x0 * cs - x1 * sn, r1 = x0 * sn + x1 * cs;
-                if (j == GR) { r0 = f16_round(r0); r1 = f16_round(r1); }
-                vec[i] = r0;
-                vec[i + HD / 2] = r1;
-            }
-        }
-        for (int i = tid; i < ncol * HD; i += NCT) vs[i] = f16_round(vs[i]);
-        named_sync(BID, NCT);
-    }
-    // 3. the new positions' K/V rows (the split holding them)
-    if (s == Sp - 1) {
-        for (int i = tid; i < ncol * HD; i += NCT) {
-            const int c = i / HD, e = i - c * HD;
-            const size_t o = static_cast<size_t>(pos + c) * d.KV + g * HD + e;
-            kc[o] = __float2half_rn(ks[i]);
-            vc[o] = __float2half_rn(vs[i]);
-        }
-    }
-    // 4. online-softmax attention over this split's positions, one position per warp per step
-    int a0, a1;
-    split_rows(pos + ncol, s, Sp, a0, a1);
+    const int HD = d.HD, NH = d.NH, GR = d.GROUP, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = gridDim.x, b = blockIdx.x, Sp = A.attn_split, pos = A.n_past;
     const float scale = rsqrtf(static_cast<float>(HD));
-    {
-        const int DPL = HD / 32;   // contiguous dims per lane
-        float qreg[2][MAX_GROUP][4];
-        float m[2][MAX_GROUP], l[2][MAX_GROUP], acc[2][MAX_GROUP][4];
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int j = 0; j < MAX_GROUP; ++j) {
-                m[c][j] = -INFINITY; l[c][j] = 0.f;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    acc[c][j][t] = 0.f;
-                    qreg[c][j][t] = (c < ncol && j < GR && t < DPL) ? qs[(c * MAX_GROUP + j) * HD + lane * DPL + t] : 0.f;
-                }
-            }
-        for (int jp = a0 + warp; jp < a1; jp += NCW) {
-            float kv[4] = {0.f, 0.f, 0.f, 0.f}, vv[4] = {0.f, 0.f, 0.f, 0.f};
-            if (jp < pos) {
-                const __half * kr = kc + static_cast<size_t>(jp) * d.KV + g * HD + lane * DPL;
-                const __half * vr = vc + static_cast<size_t>(jp) * d.KV + g * HD + lane * DPL;
-                if (DPL == 4) {
-                    const uint2 ku = talker ? __ldg(reinterpret_cast<const uint2 *>(kr)) : __ldcg(reinterpret_cast<const uint2 *>(kr));
-                    const uint2 vu = talker ? __ldg(reinterpret_cast<const uint2 *>(vr)) : __ldcg(reinterpret_cast<const uint2 *>(vr));
-                    const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&ku.x)), k1 = __half22float2(*reinterpret_cast<const __half2 *>(&ku.y));
-                    const float2 v0 = __half22float2(*reinterpret_cast<const __half2 *>(&vu.x)), v1 = __half22float2(*reinterpret_cast<const __half2 *>(&vu.y));
-                    kv[0] = k0.x; kv[1] = k0.y; kv[2] = k1.x; kv[3] = k1.y;
-                    vv[0] = v0.x; vv[1] = v0.y; vv[2] = v1.x; vv[3] = v1.y;
-                } else {
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        if (t >= DPL) continue;
-                        kv[t] = __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short *>(kr + t))));
-                        vv[t] = __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short *>(vr + t))));
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    if (t >= DPL) continue;
-                    kv[t] = ks[(jp - pos) * HD + lane * DPL + t];
-                    vv[t] = vs[(jp - pos) * HD + lane * DPL + t];
-                }
-            }
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                if (c >= ncol || jp > pos + c) continue;
-#pragma unroll
-                for (int j = 0; j < MAX_GROUP; ++j) {
-                    if (j >= GR) continue;
-                    float dsum = 0.f;
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) dsum += qreg[c][j][t] * kv[t];
-                    const float sc = warp_sum(dsum) * scale;
-                    const float mn = fmaxf(m[c][j], sc);
-                    const float corr = expf(m[c][j] - mn), pe = expf(sc - mn);
-                    l[c][j] = l[c][j] * corr + pe;
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) acc[c][j][t] = acc[c][j][t] * corr + pe * vv[t];
-                    m[c][j] = mn;
-                }
-            }
-        }
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int j = 0; j < MAX_GROUP; ++j) {
-                if (c >= ncol || j >= GR) continue;
-                float * st = wst + ((warp * 2 + c) * GR + j) * WST;
-                if (lane == 0) { st[0] = m[c][j]; st[1] = l[c][j]; }
-#pragma unroll
-                for (int t = 0; t < 4; ++t) if (t < DPL) st[2 + lane * DPL + t] = acc[c][j][t];
-            }
+    const uint32_t WST = HD + 2;
+    if (b < Sp) {
+        const float * qn = reinterpret_cast<const float *>(chunk_base);
+        const float * kn = qn + HD;
+        const float * inv = kn + HD;
+        const __half * Kc = reinterpret_cast<const __half *>(chunk_base + (2 * HD + HD / 2) * 4);
+        int r0 = min(b * A.attn_chunk, pos), r1 = min(r0 + A.attn_chunk, pos);
+        const int nc = r1 - r0;
+        const __half * Vc = Kc + static_cast<size_t>(nc) * d.KV;
+        const bool last = b == Sp - 1;
+        float * qs = S.scratch;                 // [NH][HD]
+        float * ks = qs + NH * HD;              // [NKV][HD] new position
+        float * vs = ks + d.KV;                 // [NKV][HD]
+        __half * kh = reinterpret_cast<__half *>(vs + d.KV);   // new K/V rows as f16 [2][KV]
+        // inputs: q of every head, and (last split) k, v of the new position
+        const int nin = last ? d.QKV : d.Q;
+        const bool ok = ll_fetch(A.w.qkv, nin, ptag, qs, A, S, p);   // q|k|v contiguous in both layouts
+        if (!consumers_ok(S, ok)) return false;
+        stamp(A, p, 0);
+        for (int v = warp; v < NH + (last ? d.NKV : 0); v += NCW)
+            warp_norm_rope(v < NH ? qs + v * HD : ks + (v - NH) * HD, v < NH ? qn : kn, inv, HD, d.eps_t, pos, v >= NH);
         named_sync(BID, NCT);
-    }
-    // 5. combine the warps (fixed order) into this split's partial, or the final output
-    {
-        const int nout = ncol * GR * HD;
-        uint64_t * part = A.w.part + static_cast<size_t>(g * MAX_SPLIT + s) * 2 * MAX_GROUP * WST;
-        for (int i = tid; i < nout; i += NCT) {
-            const int c = i / (GR * HD), rem = i - c * GR * HD, j = rem / HD, e = rem - j * HD;
-            float M = -INFINITY;
-            for (int w = 0; w < NCW; ++w) M = fmaxf(M, wst[((w * 2 + c) * GR + j) * WST]);
-            float Ls = 0.f, As = 0.f;
-            if (M != -INFINITY) {
-                for (int w = 0; w < NCW; ++w) {
-                    const float * st = wst + ((w * 2 + c) * GR + j) * WST;
-                    if (st[0] == -INFINITY) continue;
-                    const float f = expf(st[0] - M);
-                    Ls += st[1] * f;
-                    As += st[2 + e] * f;
-                }
+        if (last) {
+            for (int i = tid; i < d.KV; i += NCT) {
+                const __half kq = __float2half_rn(ks[i]), vq = __float2half_rn(vs[i]);
+                kh[i] = kq;
+                kh[d.KV + i] = vq;
+                A.kc[ph.layer][static_cast<size_t>(pos) * d.KV + i] = kq;
+                A.vc[ph.layer][static_cast<size_t>(pos) * d.KV + i] = vq;
             }
+            named_sync(BID, NCT);
+        }
+        stamp(A, p, 1);
+        // one warp per head: cached positions from the chunk, then the new one
+        for (int h = warp; h < NH; h += NCW) {
+            const int g = h / GR;
+            float q[4], acc[4], m, l;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) q[t] = (t < HD / 32) ? qs[h * HD + lane * (HD / 32) + t] : 0.f;
+            if (HD == 128) warp_attend<4>(q, Kc + g * HD, Vc + g * HD, d.KV, nc, scale, m, l, acc);
+            else warp_attend<2>(q, Kc + g * HD, Vc + g * HD, d.KV, nc, scale, m, l, acc);
+            if (last) {
+                float m2, l2, a2[4];
+                if (HD == 128) warp_attend<4>(q, kh + g * HD, kh + d.KV + g * HD, 0, 1, scale, m2, l2, a2);
+                else warp_attend<2>(q, kh + g * HD, kh + d.KV + g * HD, 0, 1, scale, m2, l2, a2);
+                const float mn = fmaxf(m, m2), f1 = expf(m - mn), f2 = expf(m2 - mn);
+                l = l * f1 + l2 * f2;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) acc[t] = acc[t] * f1 + a2[t] * f2;
+                m = mn;
+            }
+            const int DPL = HD / 32;
             if (Sp == 1) {
-                ll_store(A.w.attn + static_cast<size_t>(c) * d.Q + (g * GR + j) * HD + e, As / Ls, tag);
+                for (int t = 0; t < DPL; ++t) ll_store(A.w.attn + h * HD + lane * DPL + t, acc[t] / l, tag);
             } else {
-                uint64_t * pp = part + (c * MAX_GROUP + j) * WST;
-                if (e == 0) { ll_store(pp + 0, M, tag); ll_store(pp + 1, Ls, tag); }
-                ll_store(pp + 2 + e, As, tag);
+                uint64_t * pp = A.w.part + (static_cast<size_t>(b) * NH + h) * WST;
+                if (lane == 0) { ll_store(pp, m, tag); ll_store(pp + 1, l, tag); }
+                for (int t = 0; t < DPL; ++t) ll_store(pp + 2 + lane * DPL + t, acc[t], tag);
             }
         }
+        stamp(A, p, 2);
     }
-    if (Sp > 1 && s == 0) {
-        const int nout = ncol * GR * HD;
+    // combine: CTA G - NH + h reduces head h over the splits, in split order
+    const int h = b - (G - NH);
+    if (Sp > 1 && h >= 0) {
+        named_sync(BID, NCT);                   // this CTA's own split (if any) is done with its scratch
+        float * ms = S.scratch + NH * HD + 3 * d.KV + 64;   // [MAX_SPLIT] m, [MAX_SPLIT] l, [NCT/HD][HD] sums
+        float * ls = ms + MAX_SPLIT;
+        float * ps = ls + MAX_SPLIT;
         bool ok = true;
-        for (int i = tid; i < nout && ok; i += NCT) {
-            const int c = i / (GR * HD), rem = i - c * GR * HD, j = rem / HD, e = rem - j * HD;
-            float Ms[MAX_SPLIT], Lv[MAX_SPLIT], Av[MAX_SPLIT];
-            float M = -INFINITY;
-            for (int k = 0; k < Sp && ok; ++k) {
-                const uint64_t * pp = A.w.part + (static_cast<size_t>(g * MAX_SPLIT + k) * 2 * MAX_GROUP + c * MAX_GROUP + j) * WST;
-                ok = ll_get(pp + 0, tag, Ms[k], A, S, p) && ll_get(pp + 1, tag, Lv[k], A, S, p) && ll_get(pp + 2 + e, tag, Av[k], A, S, p);
-                M = fmaxf(M, Ms[k]);
-            }
-            if (!ok) break;
-            float Ls = 0.f, As = 0.f;
-            for (int k = 0; k < Sp; ++k) {
-                if (Ms[k] == -INFINITY) continue;
-                const float f = expf(Ms[k] - M);
-                Ls += Lv[k] * f;
-                As += Av[k] * f;
-            }
-            ll_store(A.w.attn + static_cast<size_t>(c) * d.Q + (g * GR + j) * HD + e, As / Ls, tag);
+        for (int k = tid; k < Sp && ok; k += NCT) {
+            const uint64_t * pp = A.w.part + (static_cast<size_t>(k) * NH + h) * WST;
+            ok = ll_get(pp, tag, ms[k], A, S, p) && ll_get(pp + 1, tag, ls[k], A, S, p);
         }
         if (!consumers_ok(S, ok)) return false;
-    } else {
+        float M = -INFINITY;
+        for (int k = 0; k < Sp; ++k) M = fmaxf(M, ms[k]);
+        // thread (e, q): dim e, splits q, q+4, ...
+        const int e = tid % HD, qq = tid / HD, NQ = NCT / HD;
+        float a = 0.f;
+        for (int k = qq; k < Sp && ok; k += NQ) {
+            float v;
+            ok = ll_get(A.w.part + (static_cast<size_t>(k) * NH + h) * WST + 2 + e, tag, v, A, S, p);
+            a += v * expf(ms[k] - M);
+        }
+        ps[qq * HD + e] = a;
+        if (!consumers_ok(S, ok)) return false;
+        if (tid < HD) {
+            float L = 0.f, num = 0.f;
+            for (int k = 0; k < Sp; ++k) L += ls[k] * expf(ms[k] - M);
+            for (int q2 = 0; q2 < NQ; ++q2) num += ps[q2 * HD + tid];
+            ll_store(A.w.attn + h * HD + tid, num / L, tag);
+        }
         named_sync(BID, NCT);
     }
+    return true;
+}
+
+// Code-predictor attention at positions pos..pos+ncol-1 (frame.hip:555-575: its own KV,
+// positions 0..15, reset every frame): KV head g = CTA g keeps that head's K/V for every
+// layer in shared memory across the frame's positions.
+__device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, const uint8_t * chunk_base, uint32_t tag, uint32_t ptag,
+                             int p) {
+    const Dims & d = A.d;
+    const int HD = d.HD, GR = d.GROUP, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ncol = ph.ncol, pos = ph.pos;
+    const int g = blockIdx.x;
+    if (g >= d.NKV) return true;
+    const float * qn = reinterpret_cast<const float *>(chunk_base);
+    const float * kn = qn + HD;
+    const float * inv = kn + HD;
+    __half * kv = S.cpkv + static_cast<size_t>(ph.layer) * NCB * 2 * HD;   // [pos][K,V][HD]
+    float * qs = S.scratch;                 // [2][GR][HD]
+    float * ks = qs + 2 * MAX_GROUP * HD;   // [2][HD]
+    float * vs = ks + 2 * HD;               // [2][HD]
+    bool ok = true;
+    for (int c = 0; c < ncol && ok; ++c) {
+        const uint64_t * src = A.w.qkv + static_cast<size_t>(c) * d.QKV;
+        float * qd = qs + c * MAX_GROUP * HD;
+        ok = ll_fetch(src + g * GR * HD, GR * HD, ptag, qd, A, S, p) && ll_fetch(src + d.Q + g * HD, HD, ptag, ks + c * HD, A, S, p) &&
+             ll_fetch(src + d.Q + d.KV + g * HD, HD, ptag, vs + c * HD, A, S, p);
+    }
+    if (!consumers_ok(S, ok)) return false;
+    stamp(A, p, 0);
+    for (int v = warp; v < ncol * (GR + 1); v += NCW) {
+        const int c = v / (GR + 1), j = v - c * (GR + 1);
+        warp_norm_rope(j < GR ? qs + (c * MAX_GROUP + j) * HD : ks + c * HD, j < GR ? qn : kn, inv, HD, d.eps_c, pos + c, j == GR);
+    }
+    named_sync(BID, NCT);
+    for (int i = tid; i < ncol * HD; i += NCT) {
+        const int c = i / HD, e = i - c * HD;
+        kv[(static_cast<size_t>(pos + c) * 2 + 0) * HD + e] = __float2half_rn(ks[i]);
+        kv[(static_cast<size_t>(pos + c) * 2 + 1) * HD + e] = __float2half_rn(vs[i]);
+    }
+    named_sync(BID, NCT);
+    stamp(A, p, 1);
+    const float scale = rsqrtf(static_cast<float>(HD));
+    for (int v = warp; v < ncol * GR; v += NCW) {
+        const int c = v / GR, j = v - c * GR;
+        float q[4], acc[4], m, l;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) q[t] = (t < HD / 32) ? qs[(c * MAX_GROUP + j) * HD + lane * (HD / 32) + t] : 0.f;
+        if (HD == 128) warp_attend<4>(q, kv, kv + HD, 2 * HD, pos + c + 1, scale, m, l, acc);
+        else warp_attend<2>(q, kv, kv + HD, 2 * HD, pos + c + 1, scale, m, l, acc);
+        const int DPL = HD / 32;
+        for (int t = 0; t < DPL; ++t) ll_store(A.w.attn + static_cast<size_t>(c) * d.Q + (g * GR + j) * HD + lane * DPL + t, acc[t] / l, tag);
+    }
+    stamp(A, p, 2);
+    named_sync(BID, NCT);
     return true;
 }
 
@@ -551,170 +664,200 @@ __device__ void consumer(const Args & A, Sm & S) {
     const int XS = max(d.H, max(d.Q, d.F));   // xin column stride
     const int Vmax = max(d.TV, d.CV);
     float * xin = S.scratch;
+    const Rows R = cta_rows(d, b, G);
     int chunk = 0;
     for (int p = 0; p < A.nphase; ++p) {
         const Phase ph = A.prog[p];
         const uint32_t tag = A.tag_base + static_cast<uint32_t>(p), ptag = tag - 1u;
-        const bool talker = ph.op <= THEAD;
         const int ncol = ph.ncol;
-        Seg seg[2];
+        Seg seg[MAX_SEG];
         int r0, r1;
-        const int ns = phase_segments(A, W, ph, b, G, seg, r0, r1);
+        const int ns = phase_segments(A, W, ph, b, R, seg, r0, r1);
         const int nr = r1 - r0;
-        const LayerW * L = ph.op <= TDOWN ? &W.tl[ph.layer] : (ph.op >= CQKV && ph.op <= CDOWN ? &W.cp[ph.layer] : nullptr);
-        const float eps = talker ? d.eps_t : d.eps_c;
 
         if (ph.op == TATTN || ph.op == CATTN) {
-            if (!attention_phase(A, S, ph, talker, tag, ptag, p)) break;
-            if (A.prof && b == 0 && tid == 0) A.prof[p] = globaltimer();
+            const uint8_t * cb = nullptr;
+            if (ns > 0) {
+                if (!wait_chunk(A, S, chunk, p)) break;
+                cb = S.ring + S.meta_off[chunk % NSLOT];
+            }
+            const bool ok = ph.op == TATTN ? talker_attention(A, S, ph, cb, tag, ptag, p) : cp_attention(A, S, ph, cb, tag, ptag, p);
+            if (!ok) break;
+            if (ns > 0) {
+                named_sync(BID, NCT);
+                release_chunk(S, chunk);
+                ++chunk;
+            }
+            stamp(A, p, 3);
             continue;
         }
 
-        // ---- prologue: this phase's inputs into shared memory
-        bool ok = true;
+        if (ph.op == FINAL) {
+            const SampleScratch sc = sampler_scratch(S, Vmax);
+            const bool ok = ll_fetch(A.w.clogits + static_cast<size_t>(NCB - 2) * d.CV, d.CV, ptag, sc.s, A, S, p);
+            if (!consumers_ok(S, ok)) break;
+            stamp(A, p, 0);
+            const int code = sample_cta<NCT>(d.CV, sample_cfg(A, NCB - 1), sc, BID);
+            if (tid == 0) S.codes[NCB - 1] = code;
+            named_sync(BID, NCT);
+            for (int i = R.h0 + tid; i < R.h1; i += NCT) {
+                float v = __half2float(W.tl_emb[static_cast<size_t>(S.codes[0]) * d.H + i]);
+                for (int cb = 0; cb < NCB - 1; ++cb)
+                    v = __fadd_rn(v, __half2float(W.cp_emb[cb][static_cast<size_t>(S.codes[cb + 1]) * d.H + i]));
+                v = __fadd_rn(v, __ldcg(A.trailing + i));
+                A.step_out[i] = v;
+            }
+            if (b == 0 && tid < NCB) A.w.codes[tid] = S.codes[tid];
+            if (b == 0 && tid == 0) {
+                if (S.codes[0] != A.eos_id) A.w.seen[S.codes[0]] = 1;
+                __threadfence();
+                st_relaxed_u32(&A.w.ctl[0], A.tag_base);
+            }
+            stamp(A, p, 3);
+            continue;
+        }
+
+        // ---- GEMV phases: chunk [norm weights][rows], inputs staged with the norm weights,
+        // one barrier, dot products with the epilogue in the lanes that hold the sums
+        const bool has_norm = ph.op == TQKV || ph.op == CQKV || ph.op == TGU || ph.op == CGU || ph.op == THEAD || ph.op == CHEAD;
+        bool ok = ns > 0 ? wait_chunk_local(A, S, chunk, p) : true;
+        const uint8_t * cbase = S.ring + S.meta_off[chunk % NSLOT];
+        const float * nw = reinterpret_cast<const float *>(cbase);
+        const __half * Ws = reinterpret_cast<const __half *>(cbase + (has_norm ? d.H * 4 : 0));
+        float ss0 = 0.f, ss1 = 0.f;   // sums of squares of this thread's inputs, per column
+        int nnorm = 0;                // columns whose norm scale is needed
+        auto stage = [&](int c, int i, float v) {
+            S.xres[c * d.H + i] = v;
+            xin[c * XS + i] = v * nw[i];
+            if (c == 0) ss0 += v * v;
+            else ss1 += v * v;
+        };
+        // after ll_fetch of column c into xres: the same thread stages its elements
+        auto stage_fetched = [&](int c) { ll_each(d.H, [&](int i) { stage(c, i, S.xres[c * d.H + i]); }); };
         switch (ph.op) {
             case TQKV: case CQKV: {
+                nnorm = ncol;
                 if (ph.layer == 0 && ph.op == TQKV) {
-                    for (int i = tid; i < d.H; i += NCT) S.xres[i] = __ldcg(A.step_in + i);
-                    named_sync(BID, NCT);
+                    if (ok)
+                        for (int i = tid; i < d.H; i += NCT) stage(0, i, __ldcg(A.step_in + i));
                 } else if (ph.layer == 0 && ph.pos == 0) {
                     // code-predictor positions 0 and 1: sample codebook 0 first
                     const SampleScratch sc = sampler_scratch(S, Vmax);
+                    bool okl = true;
                     if (A.logits_in) {
                         for (int i = tid; i < d.TV; i += NCT) sc.s[i] = __ldcg(A.logits_in + i);
-                        named_sync(BID, NCT);
                     } else {
-                        ok = ll_vec(A.w.logits, d.TV, ptag, sc.s, A, S, p);
-                        if (!ok) break;
+                        okl = ll_fetch(A.w.logits, d.TV, ptag, sc.s, A, S, p);
                     }
-                    const int cb0 = sample_cta(d.TV, sample_cfg(A, 0), sc, BID);
+                    if (!consumers_ok(S, okl && ok)) { ok = false; break; }
+                    const int cb0 = sample_cta<NCT>(d.TV, sample_cfg(A, 0), sc, BID);
                     if (tid == 0) S.codes[0] = cb0;
                     for (int i = tid; i < d.H; i += NCT) {
-                        S.xres[i] = A.hidden_in ? __ldcg(A.hidden_in + i) : S.hid[i];
-                        S.xres[d.H + i] = __half2float(W.tl_emb[static_cast<size_t>(cb0) * d.H + i]);
+                        stage(0, i, A.hidden_in ? __ldcg(A.hidden_in + i) : S.hid[i]);
+                        stage(1, i, __half2float(W.tl_emb[static_cast<size_t>(cb0) * d.H + i]));
                     }
-                    named_sync(BID, NCT);
                 } else if (ph.layer == 0) {
                     const SampleScratch sc = sampler_scratch(S, Vmax);
-                    ok = ll_vec(A.w.clogits + static_cast<size_t>(ph.pos - 2) * d.CV, d.CV, ptag, sc.s, A, S, p);
-                    if (!ok) break;
-                    const int code = sample_cta(d.CV, sample_cfg(A, ph.pos - 1), sc, BID);
+                    const bool okl = ll_fetch(A.w.clogits + static_cast<size_t>(ph.pos - 2) * d.CV, d.CV, ptag, sc.s, A, S, p);
+                    if (!consumers_ok(S, okl && ok)) { ok = false; break; }
+                    const int code = sample_cta<NCT>(d.CV, sample_cfg(A, ph.pos - 1), sc, BID);
                     if (tid == 0) S.codes[ph.pos - 1] = code;
-                    row_f16_to_smem(W.cp_emb[ph.pos - 2] + static_cast<size_t>(code) * d.H, d.H, S.xres);
-                    named_sync(BID, NCT);
+                    const __half * row = W.cp_emb[ph.pos - 2] + static_cast<size_t>(code) * d.H;
+                    for (int i = tid; i < d.H; i += NCT) stage(0, i, __half2float(row[i]));
                 } else {
-                    for (int c = 0; c < ncol && ok; ++c) ok = ll_vec(A.w.x + static_cast<size_t>(c) * d.H, d.H, ptag, S.xres + c * d.H, A, S, p);
-                    if (!ok) break;
+                    for (int c = 0; c < ncol && ok; ++c) {
+                        ok = ll_fetch(A.w.x + static_cast<size_t>(c) * d.H, d.H, ptag, S.xres + c * d.H, A, S, p);
+                        if (ok) stage_fetched(c);
+                    }
                 }
-                rmsnorm_cols(S, S.xres, d.H, L->ln1, eps, ncol, d.H, xin, XS);
                 break;
             }
-            case TO: case CO:
-                for (int c = 0; c < ncol && ok; ++c) ok = ll_vec(A.w.attn + static_cast<size_t>(c) * d.Q, d.Q, ptag, xin + c * XS, A, S, p);
-                break;
             case TGU: case CGU:
-                for (int c = 0; c < ncol && ok; ++c) ok = ll_vec(A.w.x + static_cast<size_t>(c) * d.H, d.H, ptag, S.xres + c * d.H, A, S, p);
-                if (ok) rmsnorm_cols(S, S.xres, d.H, L->ln2, eps, ncol, d.H, xin, XS);
+                nnorm = ncol;
+                for (int c = 0; c < ncol && ok; ++c) {
+                    ok = ll_fetch(A.w.x + static_cast<size_t>(c) * d.H, d.H, ptag, S.xres + c * d.H, A, S, p);
+                    if (ok) stage_fetched(c);
+                }
+                break;
+            case TO: case CO:
+                for (int c = 0; c < ncol && ok; ++c) ok = ll_fetch(A.w.attn + static_cast<size_t>(c) * d.Q, d.Q, ptag, xin + c * XS, A, S, p);
                 break;
             case TDOWN: case CDOWN:
-                for (int c = 0; c < ncol && ok; ++c) ok = ll_vec(A.w.h + static_cast<size_t>(c) * d.F, d.F, ptag, xin + c * XS, A, S, p);
+                for (int c = 0; c < ncol && ok; ++c) ok = ll_fetch(A.w.h + static_cast<size_t>(c) * d.F, d.F, ptag, xin + c * XS, A, S, p);
                 break;
             case THEAD:
-                ok = ll_vec(A.w.x, d.H, ptag, S.xres, A, S, p);
-                if (!ok) break;
-                rmsnorm_cols(S, S.xres, d.H, W.tl_norm, d.eps_t, 1, d.H, xin, XS);
-                for (int i = tid; i < d.H; i += NCT) {
-                    S.hid[i] = xin[i];
-                    if (b == 0) A.w.hidden[i] = xin[i];
-                }
-                break;
-            case CHEAD: {
-                const int cc = ncol - 1;
-                ok = ll_vec(A.w.x + static_cast<size_t>(cc) * d.H, d.H, ptag, S.xres, A, S, p);
-                if (!ok) break;
-                rmsnorm_cols(S, S.xres, d.H, W.cp_norm, d.eps_c, 1, d.H, xin, XS);
-                break;
-            }
-            case FINAL: {
-                const SampleScratch sc = sampler_scratch(S, Vmax);
-                ok = ll_vec(A.w.clogits + static_cast<size_t>(NCB - 2) * d.CV, d.CV, ptag, sc.s, A, S, p);
-                if (!ok) break;
-                const int code = sample_cta(d.CV, sample_cfg(A, NCB - 1), sc, BID);
-                if (tid == 0) S.codes[NCB - 1] = code;
-                named_sync(BID, NCT);
-                int e0, e1;
-                split_rows(d.H, b, G, e0, e1);
-                for (int i = e0 + tid; i < e1; i += NCT) {
-                    float v = __half2float(W.tl_emb[static_cast<size_t>(S.codes[0]) * d.H + i]);
-                    for (int cb = 0; cb < NCB - 1; ++cb)
-                        v = __fadd_rn(v, __half2float(W.cp_emb[cb][static_cast<size_t>(S.codes[cb + 1]) * d.H + i]));
-                    v = __fadd_rn(v, __ldcg(A.trailing + i));
-                    A.step_out[i] = v;
-                }
-                if (b == 0 && tid < NCB) A.w.codes[tid] = S.codes[tid];
-                if (b == 0 && tid == 0) {
-                    if (S.codes[0] != A.eos_id) A.w.seen[S.codes[0]] = 1;
-                    __threadfence();
-                    st_relaxed_u32(&A.w.ctl[0], A.tag_base);
-                }
-                break;
-            }
-            default: break;
-        }
-        if (!ok) break;
-        if (ns == 0) {
-            if (A.prof && b == 0 && tid == 0) A.prof[p] = globaltimer();
-            continue;
-        }
-
-        // ---- weights of this phase, then the dot products
-        if (!wait_chunk(A, S, chunk, p)) break;
-        const __half * Ws = reinterpret_cast<const __half *>(S.ring + S.meta_off[chunk % NSLOT]);
-        int nrows = nr, ncols = d.H;
-        if (ph.op == TO || ph.op == CO) ncols = d.Q;
-        else if (ph.op == TDOWN || ph.op == CDOWN) ncols = d.F;
-        else if (ph.op == TGU || ph.op == CGU) nrows = 2 * nr;
-        const int gcol = (ph.op == THEAD || ph.op == CHEAD) ? 1 : ncol;
-        const int nseg = ncols >> 8;
-        run_gemv(gcol, Ws, nrows, ncols, xin, XS, S.part);
-        named_sync(BID, NCT);
-        release_chunk(S, chunk);
-        ++chunk;
-
-        // ---- epilogue: outputs to the exchange words
-        const uint32_t t = tag;
-        switch (ph.op) {
-            case TQKV: case CQKV:
-                for (int k = tid; k < ncol * nr; k += NCT) {
-                    const int c = k / nr, r = k - c * nr;
-                    ll_store(A.w.qkv + static_cast<size_t>(c) * d.QKV + r0 + r, part_sum(S.part, c, r, nrows, nseg), t);
-                }
-                break;
-            case TO: case CO: case TDOWN: case CDOWN:
-                for (int k = tid; k < ncol * nr; k += NCT) {
-                    const int c = k / nr, r = k - c * nr;
-                    const float x = S.xres[c * d.H + r0 + r] + part_sum(S.part, c, r, nrows, nseg);
-                    ll_store(A.w.x + static_cast<size_t>(c) * d.H + r0 + r, x, t);
-                }
-                break;
-            case TGU: case CGU:
-                for (int k = tid; k < ncol * nr; k += NCT) {
-                    const int c = k / nr, r = k - c * nr;
-                    const float gv = part_sum(S.part, c, r, nrows, nseg), uv = part_sum(S.part, c, nr + r, nrows, nseg);
-                    ll_store(A.w.h + static_cast<size_t>(c) * d.F + r0 + r, gv / (1.f + expf(-gv)) * uv, t);
-                }
-                break;
-            case THEAD:
-                for (int r = tid; r < nr; r += NCT) ll_store(A.w.logits + r0 + r, part_sum(S.part, 0, r, nrows, nseg), t);
+                nnorm = 1;
+                ok = ok && ll_fetch(A.w.x, d.H, ptag, S.xres, A, S, p);
+                if (ok) stage_fetched(0);
                 break;
             case CHEAD:
-                for (int r = tid; r < nr; r += NCT)
-                    ll_store(A.w.clogits + static_cast<size_t>(ph.pos - 1) * d.CV + r0 + r, part_sum(S.part, 0, r, nrows, nseg), t);
+                nnorm = 1;
+                ok = ok && ll_fetch(A.w.x + static_cast<size_t>(ncol - 1) * d.H, d.H, ptag, S.xres, A, S, p);
+                if (ok) stage_fetched(0);
                 break;
             default: break;
         }
-        named_sync(BID, NCT);   // xres and the partials are rewritten by the next prologue
-        if (A.prof && b == 0 && tid == 0) A.prof[p] = globaltimer();
+        norm_partial(S, ss0, ss1, nnorm);
+        if (!consumers_ok(S, ok)) break;
+        stamp(A, p, 0);
+        const float eps = (ph.op <= THEAD) ? d.eps_t : d.eps_c;
+        const float sc0 = nnorm > 0 ? norm_scale(S, 0, d.H, eps) : 1.f;
+        const float sc1 = nnorm > 1 ? norm_scale(S, 1, d.H, eps) : 1.f;
+        const int gcol = (ph.op == THEAD || ph.op == CHEAD) ? 1 : ncol;
+        const uint32_t t = tag;
+        switch (ph.op) {
+            case TQKV: case CQKV: {
+                auto epi = [&](int u, int c, float y, float) {
+                    ll_store(A.w.qkv + static_cast<size_t>(c) * d.QKV + r0 + u, y * (c ? sc1 : sc0), t);
+                };
+                if (gcol == 2) gemv_slice<2, false>(Ws, nr, d.H, xin, XS, S.part, epi);
+                else gemv_slice<1, false>(Ws, nr, d.H, xin, XS, S.part, epi);
+                break;
+            }
+            case TO: case CO: case TDOWN: case CDOWN: {
+                const int K = (ph.op == TO || ph.op == CO) ? d.Q : d.F;
+                auto epi = [&](int u, int c, float y, float) {
+                    ll_store(A.w.x + static_cast<size_t>(c) * d.H + r0 + u, S.xres[c * d.H + r0 + u] + y, t);
+                };
+                if (gcol == 2) gemv_slice<2, false>(Ws, nr, K, xin, XS, S.part, epi);
+                else gemv_slice<1, false>(Ws, nr, K, xin, XS, S.part, epi);
+                break;
+            }
+            case TGU: case CGU: {
+                auto epi = [&](int u, int c, float g, float up) {
+                    const float s = c ? sc1 : sc0;
+                    g *= s;
+                    up *= s;
+                    ll_store(A.w.h + static_cast<size_t>(c) * d.F + r0 + u, g / (1.f + expf(-g)) * up, t);
+                };
+                if (gcol == 2) gemv_slice<2, true>(Ws, nr, d.H, xin, XS, S.part, epi);
+                else gemv_slice<1, true>(Ws, nr, d.H, xin, XS, S.part, epi);
+                break;
+            }
+            case THEAD: {
+                for (int i = tid; i < d.H; i += NCT) {
+                    const float hv = xin[i] * sc0;
+                    S.hid[i] = hv;
+                    if (b == 0) A.w.hidden[i] = hv;
+                }
+                gemv_slice<1, false>(Ws, nr, d.H, xin, XS, S.part,
+                                     [&](int u, int, float y, float) { ll_store(A.w.logits + r0 + u, y * sc0, t); });
+                break;
+            }
+            case CHEAD:
+                gemv_slice<1, false>(Ws, nr, d.H, xin, XS, S.part, [&](int u, int, float y, float) {
+                    ll_store(A.w.clogits + static_cast<size_t>(ph.pos - 1) * d.CV + r0 + u, y * sc0, t);
+                });
+                break;
+            default: break;
+        }
+        stamp(A, p, 2);
+        named_sync(BID, NCT);   // the chunk, xin and xres are reused from here on
+        if (ns > 0) {
+            release_chunk(S, chunk);
+            ++chunk;
+        }
+        stamp(A, p, 3);
     }
 }
 
@@ -730,7 +873,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_frame(const __grid_constant__ Args 
         fence_mbar_init();
     }
     __syncthreads();
-    if (A.prof && blockIdx.x == 0 && threadIdx.x == 0) A.prof[A.nphase] = globaltimer();
+    if (A.prof && blockIdx.x == A.prof_cta && threadIdx.x == 0) A.prof[4 * A.nphase] = globaltimer();
     if (threadIdx.x >= NCT) producer(A, S);
     else consumer(A, S);
 }
@@ -748,7 +891,7 @@ __global__ void __launch_bounds__(NCT, 1) k_sample(const float * logits, int V, 
     sc.red = sbuf + 4 * V + (V + 3) / 4 + 256;
     for (int i = threadIdx.x; i < V; i += NCT) sc.s[i] = logits[i];
     named_sync(BID, NCT);
-    const int c = sample_cta(V, cfg, sc, BID);
+    const int c = sample_cta<NCT>(V, cfg, sc, BID);
     if (threadIdx.x == 0) *out = c;
 }
 

@@ -33,7 +33,7 @@
 
 namespace navi::fk {
 
-constexpr int NCW = 16;                 // consumer warps
+constexpr int NCW = 12;                 // consumer warps
 constexpr int NCT = NCW * 32;           // consumer threads
 constexpr int NTHR = NCT + 32;          // + the producer warp
 constexpr int BID = 1;                  // named barrier of the consumer threads
@@ -41,7 +41,8 @@ constexpr int MAX_TL = 32;              // talker layers
 constexpr int MAX_CP = 8;               // code-predictor layers
 constexpr int NCB = 16;                 // codebooks per frame
 constexpr int NSLOT = 16;               // ring slots (mbarriers)
-constexpr int MAX_SPLIT = 18;           // attention splits per KV head
+constexpr int MAX_SPLIT = 148;          // talker attention splits (one per CTA at most)
+constexpr int MAX_SEG = 5;              // weight segments per phase chunk
 constexpr int MAX_GROUP = 4;            // q heads per KV head
 constexpr uint32_t PIECE = 32768;       // bulk copies are issued in pieces of at most this
 constexpr uint32_t CTRL_BYTES = 256;    // per-CTA control block in shared memory
@@ -84,8 +85,7 @@ struct Work {
     uint64_t * h;        // [2][F]
     uint64_t * logits;   // [TV]
     uint64_t * clogits;  // [15][CV]
-    uint64_t * part;     // [NKV][MAX_SPLIT][2][GROUP][HD + 2]
-    __half * ckc, * cvc; // [CL][16][KV]
+    uint64_t * part;     // [MAX_SPLIT][NH][HD + 2] talker attention partials (m, l, acc)
     uint8_t * seen;      // [TV]
     int32_t * codes;     // [16]
     float * hidden;      // [H] talker post-norm hidden of the last talker step
@@ -100,7 +100,8 @@ struct Args {
     Work w;
     uint32_t tag_base;
     int n_past;        // talker position
-    int attn_split;    // talker attention splits per KV head
+    int attn_split;    // talker attention splits (CTAs 0..attn_split-1)
+    int attn_chunk;    // cached positions per split
     const float * step_in;     // talker input row (frames >= 1)
     const float * hidden_in;   // frame 0: the prefill's post-norm hidden
     const float * logits_in;   // frame 0: the prefill's codec logits
@@ -124,14 +125,19 @@ struct Args {
     uint32_t ring_bytes;
     uint32_t scratch_floats;
     uint32_t part_floats;
-    unsigned long long * prof;   // optional: [nphase] globaltimer at the end of each phase on CTA 0
+    unsigned long long * prof;   // optional trace: [4 * nphase + 1] globaltimer stamps on CTA prof_cta
+    int prof_cta;
 };
 
 // ---- shared-memory layout (identical on host and device) ---------------------------------
 
 struct SmemLayout {
-    uint32_t bars, meta_off, meta_end, ctrl, codes, xres, hid, part, scratch, ring, total;
+    uint32_t bars, meta_off, meta_end, ctrl, codes, xres, hid, part, scratch, cpkv, ring, total;
 };
+
+// The code predictor's K/V for one KV head, kept in shared memory across the
+// positions of a frame: [layer][position][K, V][head_dim] f16.
+__host__ __device__ inline uint32_t cpkv_bytes(const Dims & d) { return static_cast<uint32_t>(d.CL) * NCB * 2 * d.HD * 2; }
 
 __host__ __device__ inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
@@ -148,6 +154,7 @@ __host__ __device__ inline SmemLayout smem_layout(const Dims & d, uint32_t ring_
     L.hid = o;      o += d.H * 4;
     L.part = o;     o += align_up(part_floats * 4, 16);
     L.scratch = o;  o += align_up(scratch_floats * 4, 16);
+    L.cpkv = o;     o += align_up(cpkv_bytes(d), 16);
     o = align_up(o, 128);
     L.ring = o;     o += ring_bytes;
     L.total = o;
@@ -155,6 +162,10 @@ __host__ __device__ inline SmemLayout smem_layout(const Dims & d, uint32_t ring_
 }
 
 // Rows [r0, r1) of an R-row matrix that CTA b of G owns.
+// Frame weight matrices are re-laid out per CTA slice: the rows [r0, r1) of CTA b keep their
+// bytes [r0 * K, r1 * K) (the same HBM range the producer streams) but inside the slice
+// element (r, k) sits at ((k / 8) * (r1 - r0) + (r - r0)) * 8 + k % 8, so that in shared
+// memory lane = row reads 16 consecutive bytes per 8-column chunk without bank conflicts.
 __host__ __device__ inline void split_rows(int R, int b, int G, int & r0, int & r1) {
     r0 = static_cast<int>((static_cast<long long>(R) * b) / G);
     r1 = static_cast<int>((static_cast<long long>(R) * (b + 1)) / G);
@@ -165,42 +176,83 @@ struct Seg {
     uint32_t bytes;
 };
 
-// The weight bytes phase p needs on CTA b (0, 1 or 2 contiguous segments).
-__host__ __device__ inline int phase_segments(const Args & A, const ModelW & W, const Phase & ph, int b, int G, Seg * s,
+// This CTA's rows of every matrix shape the phases use (computed once per launch: the
+// 64-bit divisions of split_rows stay off the per-phase path).
+struct Rows {
+    int qkv0, qkv1, h0, h1, f0, f1, tv0, tv1, cv0, cv1;
+};
+__host__ __device__ inline Rows cta_rows(const Dims & d, int b, int G) {
+    Rows r;
+    split_rows(d.QKV, b, G, r.qkv0, r.qkv1);
+    split_rows(d.H, b, G, r.h0, r.h1);
+    split_rows(d.F, b, G, r.f0, r.f1);
+    split_rows(d.TV, b, G, r.tv0, r.tv1);
+    split_rows(d.CV, b, G, r.cv0, r.cv1);
+    return r;
+}
+
+// The bytes phase `ph` streams into CTA b's ring chunk, in order (up to MAX_SEG contiguous
+// segments, each a multiple of 16 bytes): the phase's norm weights first, then its weight
+// rows [r0, r1); for talker attention, q/k norm weights, the RoPE table and the K and V
+// rows of the split's cached positions. Returns the number of segments (0: no chunk).
+__host__ __device__ inline int phase_segments(const Args & A, const ModelW & W, const Phase & ph, int b, const Rows & R, Seg * s,
                                               int & r0, int & r1) {
     const Dims & d = A.d;
-    const bool tl = ph.op <= THEAD;
     const LayerW * L = nullptr;
     if (ph.op <= TDOWN) L = &W.tl[ph.layer];
     else if (ph.op >= CQKV && ph.op <= CDOWN) L = &W.cp[ph.layer];
-    (void) tl;
+    const uint32_t H4 = static_cast<uint32_t>(d.H) * 4, HD4 = static_cast<uint32_t>(d.HD) * 4;
     r0 = r1 = 0;
     switch (ph.op) {
         case TQKV: case CQKV:
-            split_rows(d.QKV, b, G, r0, r1);
-            s[0] = {L->wqkv + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
-            return r1 > r0 ? 1 : 0;
+            r0 = R.qkv0; r1 = R.qkv1;
+            s[0] = {L->ln1, H4};
+            s[1] = {L->wqkv + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
+            return r1 > r0 ? 2 : 0;
         case TO: case CO:
-            split_rows(d.H, b, G, r0, r1);
+            r0 = R.h0; r1 = R.h1;
             s[0] = {L->wo + static_cast<size_t>(r0) * d.Q, static_cast<uint32_t>((r1 - r0) * d.Q * 2)};
             return r1 > r0 ? 1 : 0;
         case TGU: case CGU:
-            split_rows(d.F, b, G, r0, r1);
-            s[0] = {L->wg + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
-            s[1] = {L->wu + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
-            return r1 > r0 ? 2 : 0;
+            r0 = R.f0; r1 = R.f1;
+            s[0] = {L->ln2, H4};
+            s[1] = {L->wg + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
+            s[2] = {L->wu + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
+            return r1 > r0 ? 3 : 0;
         case TDOWN: case CDOWN:
-            split_rows(d.H, b, G, r0, r1);
+            r0 = R.h0; r1 = R.h1;
             s[0] = {L->wd + static_cast<size_t>(r0) * d.F, static_cast<uint32_t>((r1 - r0) * d.F * 2)};
             return r1 > r0 ? 1 : 0;
         case THEAD:
-            split_rows(d.TV, b, G, r0, r1);
-            s[0] = {W.codec_head + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
-            return r1 > r0 ? 1 : 0;
+            r0 = R.tv0; r1 = R.tv1;
+            s[0] = {W.tl_norm, H4};
+            s[1] = {W.codec_head + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
+            return r1 > r0 ? 2 : 0;
         case CHEAD:
-            split_rows(d.CV, b, G, r0, r1);
-            s[0] = {W.lm_head[ph.pos - 1] + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
-            return r1 > r0 ? 1 : 0;
+            r0 = R.cv0; r1 = R.cv1;
+            s[0] = {W.cp_norm, H4};
+            s[1] = {W.lm_head[ph.pos - 1] + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
+            return r1 > r0 ? 2 : 0;
+        case TATTN: {
+            if (b >= A.attn_split) return 0;
+            s[0] = {L->qn, HD4};
+            s[1] = {L->kn, HD4};
+            s[2] = {A.inv_freq_t, HD4 / 2};
+            // cached positions [r0, r1) of this split
+            r0 = min(b * A.attn_chunk, A.n_past);
+            r1 = min(r0 + A.attn_chunk, A.n_past);
+            if (r1 <= r0) return 3;
+            const size_t row = static_cast<size_t>(d.KV);
+            s[3] = {A.kc[ph.layer] + static_cast<size_t>(r0) * row, static_cast<uint32_t>((r1 - r0) * d.KV * 2)};
+            s[4] = {A.vc[ph.layer] + static_cast<size_t>(r0) * row, static_cast<uint32_t>((r1 - r0) * d.KV * 2)};
+            return 5;
+        }
+        case CATTN:
+            if (b >= d.NKV) return 0;
+            s[0] = {L->qn, HD4};
+            s[1] = {L->kn, HD4};
+            s[2] = {A.inv_freq_c, HD4 / 2};
+            return 3;
         default:
             return 0;
     }

@@ -22,7 +22,6 @@
 
 namespace navi::dev {
 
-constexpr int SAMPLER_THREADS = 512;
 
 struct SampleCfg {
     float temperature;   // <= 0: greedy
@@ -124,11 +123,12 @@ __device__ __forceinline__ float key_float(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
-// Samples from S.s[0..V) (the raw logits on entry). Must be called by all 512
-// consumer threads (barrier id `bid`); every thread returns the chosen id.
-static __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, int bid) {
+// Samples from S.s[0..V) (the raw logits on entry). Must be called by all NT threads
+// (NT a multiple of 32, >= 256; barrier id `bid`); every thread returns the chosen id.
+template <int NT>
+__device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, int bid) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    constexpr int NT = SAMPLER_THREADS;
+    static_assert(NT % 32 == 0 && NT >= 256 && NT <= 1024, "sampler thread count");
     float * s = S.s;
     float * red = S.red;
     int * ired = reinterpret_cast<int *>(S.red);

@@ -88,7 +88,7 @@ SIGNATURES = [
     ("navi_frame_grid_blocks", c_int, [c_void_p]),
     ("navi_frame_destroy", None, [c_void_p]),
     ("navi_frame_inspect", c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
-    ("navi_frame_set_profile", c_int, [c_void_p, c_int]),
+    ("navi_frame_set_profile", c_int, [c_void_p, c_int, c_int]),
     ("navi_frame_profile", c_int, [c_void_p, POINTER(c_uint64), c_int, POINTER(c_int)]),
     ("navi_sample_logits", c_int, [c_void_p, c_void_p, c_int, POINTER(Sampling), c_uint64, c_int, c_int, c_int, c_int,
                                    c_void_p, POINTER(c_int32)]),

@@ -210,17 +210,24 @@ class Frame:
         check(lib().navi_frame_inspect(self.h, hid.ctypes.data, lg.ctypes.data, clg.ctypes.data))
         return hid, lg, clg
 
-    def set_profile(self, on: bool = True) -> None:
-        check(lib().navi_frame_set_profile(self.h, 1 if on else 0))
+    def set_profile(self, on: bool = True, cta: int = 0) -> None:
+        check(lib().navi_frame_set_profile(self.h, 1 if on else 0, cta))
+
+    def profile_raw(self):
+        """Stamps of the last launch on the traced CTA: (start_ns, array [phases, 4] in ns)."""
+        import numpy as np
+        buf = (ctypes.c_uint64 * (4 * 4096 + 1))()
+        n = c_int(0)
+        check(lib().navi_frame_profile(self.h, buf, 4 * 4096 + 1, byref(n)))
+        a = np.array(buf[:n.value], dtype=np.float64)
+        return a[0], a[1:].reshape(-1, 4)
 
     def profile(self):
-        """Per-phase durations (us) of the last launch, measured on CTA 0."""
+        """Per-phase durations (us) of the last launch on the traced CTA."""
         import numpy as np
-        buf = (ctypes.c_uint64 * 4097)()
-        n = c_int(0)
-        check(lib().navi_frame_profile(self.h, buf, 4097, byref(n)))
-        t = np.array(buf[:n.value], dtype=np.float64)
-        return np.diff(t) / 1000.0
+        t0, st = self.profile_raw()
+        ends = np.concatenate([[t0], st[:, 3]])
+        return np.diff(ends) / 1000.0
 
     def close(self):
         if self.h:

@@ -14,24 +14,31 @@ from navi_b200 import model_spec
 NSLOT = 16
 
 
-def phase_chunks(cfg, b, G):
-    """Weight bytes per phase on CTA b of G (0 for phases without weights), program order."""
+def phase_chunks(cfg, b, G, n_past=512):
+    """Chunk bytes per phase on CTA b of G (phases without a chunk dropped), program order:
+    norm weights ride with QKV / gate-up / heads; talker attention carries q/k norms, the
+    RoPE table and the split's K and V rows (16 positions per split)."""
     tl, cp = cfg.talker, cfg.cp
-    H, Q, KV, F = tl.hidden, tl.n_head * tl.head_dim, tl.n_kv_head * tl.head_dim, tl.ff
+    H, Q, KV, F, HD = tl.hidden, tl.n_head * tl.head_dim, tl.n_kv_head * tl.head_dim, tl.ff, tl.head_dim
     QKV = Q + 2 * KV
 
     def rows(R):
         return (R * (b + 1)) // G - (R * b) // G
-    layer = [rows(QKV) * H * 2, 0, rows(H) * Q * 2, 2 * rows(F) * H * 2, rows(H) * F * 2]
+    chunk = max(16, -(-n_past // min(148, G)))
+    split = max(1, -(-n_past // chunk))
+    r0 = min(b * chunk, n_past)
+    r1 = min(r0 + chunk, n_past)
+    tattn = (2 * HD * 4 + HD * 2 + 2 * (r1 - r0) * KV * 2) if b < split else 0
+    cattn = (2 * HD * 4 + HD * 2) if b < tl.n_kv_head else 0
+    qkv, o, gu, down = H * 4 + rows(QKV) * H * 2, rows(H) * Q * 2, H * 4 + 2 * rows(F) * H * 2, rows(H) * F * 2
     out = []
     for _ in range(tl.n_layer):
-        out += layer
-    out.append(rows(tl.vocab) * H * 2)
+        out += [qkv, tattn, o, gu, down]
+    out.append(H * 4 + rows(tl.vocab) * H * 2)
     for _pass in range(15):
         for _ in range(cp.n_layer):
-            out += layer
-        out.append(rows(cp.vocab) * H * 2)
-    out.append(0)
+            out += [qkv, cattn, o, gu, down]
+        out.append(H * 4 + rows(cp.vocab) * H * 2)
     return [c for c in out if c > 0]
 
 
@@ -73,12 +80,13 @@ def simulate(chunks, RB):
 
 
 @pytest.mark.parametrize("G", [148, 132, 100])
-@pytest.mark.parametrize("ring_kb", [100, 160, 200])
-def test_ring_never_stalls_full_size(G, ring_kb):
+@pytest.mark.parametrize("ring_kb", [100, 120, 160])
+@pytest.mark.parametrize("n_past", [0, 64, 512, 2048])
+def test_ring_never_stalls_full_size(G, ring_kb, n_past):
     cfg = model_spec.full_config(1024)
     RB = ring_kb * 1024
     for b in (0, 1, G // 2, G - 1):
-        chunks = phase_chunks(cfg, b, G)
+        chunks = phase_chunks(cfg, b, G, n_past)
         if max(chunks) > RB:
             continue   # Frame::create refuses such a ring
         assert simulate(chunks, RB) == len(chunks), (b, G, ring_kb)
