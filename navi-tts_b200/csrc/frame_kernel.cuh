@@ -5,7 +5,7 @@
 // What it computes is the reference's k_frame (model/qwen3tts/frame.hip:517-579);
 // how it is organised is B200-specific:
 //
-//  * One CTA per SM (148), 16 consumer warps + 1 producer warp.
+//  * One CTA per SM (148), 12 consumer warps + 1 producer warp.
 //  * The producer warp walks the same phase program as the consumers and streams
 //    this CTA's slice of every weight matrix (rows [r0, r1) of the matrix; weights
 //    never depend on activations) into a shared-memory ring with cp.async.bulk on
@@ -15,9 +15,11 @@
 //    {value, tag} in L2 (tag = launch base + phase index); a consumer polls exactly
 //    the words it needs until the tag matches. One L2 round trip per dependency
 //    instead of a barrier plus a reload.
-//  * q/k RMSNorm + RoPE + the KV store are fused into the attention phase; attention
-//    is split over KV ranges (flash-decoding) with a fixed-order combine by the
-//    split-0 CTA of each KV head.
+//  * q/k RMSNorm + RoPE + the KV store are fused into the attention phase. Talker
+//    attention is split over KV position ranges (flash-decoding; each split CTA
+//    streams its K/V rows through the ring like weights) with a fixed-order combine
+//    by one CTA per query head; code-predictor attention (<= 16 positions) runs in one
+//    CTA per KV head on K/V kept in shared memory.
 //  * Sampling runs redundantly in every CTA (bit-identical inputs, deterministic
 //    code), so the next phase starts without a barrier.
 //  * Code-predictor positions 0 and 1 run as one 2-column pass over the weights.

@@ -1,4 +1,4 @@
-// The frame sampler, run by the 512 consumer threads of a CTA.
+// The frame sampler, run by the NT consumer threads of a CTA.
 //
 // Semantics follow the reference's device sampler (model/qwen3tts/frame.hip):
 // codebook-0 logit modifications tl_modified_logit (413-419); greedy argmax with
