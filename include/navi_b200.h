@@ -186,6 +186,19 @@ int navi_frame_profile(const navi_frame * f, uint64_t * out, int cap, int * n);
 int navi_sample_logits(navi_device * dev, const float * d_logits, int vocab, const navi_sampling * s, uint64_t seed,
                        int frame_index, int codebook, int suppress_from, int eos_id, const uint8_t * d_seen, int32_t * out);
 
+/* No counterpart in the reference.  navi_sample_logits without any device allocation, for
+ * hosts that may not allocate after start-up (real-time audio threads, memory-reserved
+ * serving processes): the working arrays and the result word live in one static device
+ * array of the library (NAVI_SAMPLE_STATIC_MAX_VOCAB logits, about 545 KB).  Same
+ * arguments and result as navi_sample_logits; vocab above the limit returns NAVI_E_ARG.
+ * The first call on a device takes the array's address (set-up) and should precede any
+ * stream capture there.  Calls on one device share the array: the library serialises them
+ * with a per-device host lock, and overlapping use of the array by other means races. */
+#define NAVI_SAMPLE_STATIC_MAX_VOCAB 32768
+int navi_sample_logits_static(navi_device * dev, const float * d_logits, int vocab, const navi_sampling * s, uint64_t seed,
+                              int frame_index, int codebook, int suppress_from, int eos_id, const uint8_t * d_seen,
+                              int32_t * out);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

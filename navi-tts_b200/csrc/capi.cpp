@@ -3,6 +3,7 @@
 
 #include "frame.hpp"
 #include "runtime.hpp"
+#include "sample_static.hpp"
 
 #include <cstring>
 #include <memory>
@@ -325,6 +326,18 @@ int navi_sample_logits(navi_device * dev, const float * d_logits, int vocab, con
         if (!dev || !d_logits || !out || vocab <= 0) return set_err(NAVI_E_ARG, "bad argument");
         *out = navi::qwen3tts::Frame::sample(*dev->dev, d_logits, vocab, to_sampling(s), seed, frame_index, codebook, suppress_from,
                                              eos_id, d_seen);
+        return NAVI_OK;
+    });
+}
+
+int navi_sample_logits_static(navi_device * dev, const float * d_logits, int vocab, const navi_sampling * s, uint64_t seed,
+                              int frame_index, int codebook, int suppress_from, int eos_id, const uint8_t * d_seen,
+                              int32_t * out) {
+    static_assert(NAVI_SAMPLE_STATIC_MAX_VOCAB == navi::qwen3tts::SAMPLE_STATIC_MAX_VOCAB, "limit in the header");
+    return guard([&]() -> int {
+        if (!dev || !d_logits || !out) return set_err(NAVI_E_ARG, "bad argument");
+        *out = navi::qwen3tts::sample_static(*dev->dev, d_logits, vocab, to_sampling(s), seed, frame_index, codebook,
+                                             suppress_from, eos_id, d_seen);
         return NAVI_OK;
     });
 }

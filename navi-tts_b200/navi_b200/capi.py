@@ -13,6 +13,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libnavi_b20
 
 NAVI_OK, NAVI_E_ARG, NAVI_E_CUDA, NAVI_E_FORMAT, NAVI_E_TIMEOUT, NAVI_E_KV_FULL, NAVI_E_LAUNCH, NAVI_E_SHAPE, NAVI_E_NOMEM = range(9)
 NAVI_RNG_PCG, NAVI_RNG_PHILOX = 0, 1
+NAVI_SAMPLE_STATIC_MAX_VOCAB = 32768
 
 
 class DeviceInfo(ctypes.Structure):
@@ -92,6 +93,8 @@ SIGNATURES = [
     ("navi_frame_profile", c_int, [c_void_p, POINTER(c_uint64), c_int, POINTER(c_int)]),
     ("navi_sample_logits", c_int, [c_void_p, c_void_p, c_int, POINTER(Sampling), c_uint64, c_int, c_int, c_int, c_int,
                                    c_void_p, POINTER(c_int32)]),
+    ("navi_sample_logits_static", c_int, [c_void_p, c_void_p, c_int, POINTER(Sampling), c_uint64, c_int, c_int, c_int,
+                                          c_int, c_void_p, POINTER(c_int32)]),
 ]
 
 _lib = None

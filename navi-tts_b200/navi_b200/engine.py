@@ -247,3 +247,13 @@ def sample_logits(dev: Device, d_logits: int, vocab: int, s: Sampling, seed: int
     check(lib().navi_sample_logits(dev.h, c_void_p(d_logits), vocab, byref(s.c()), seed, frame_index, codebook, suppress_from,
                                    eos_id, c_void_p(d_seen) if d_seen else None, byref(out)))
     return out.value
+
+
+def sample_logits_static(dev: Device, d_logits: int, vocab: int, s: Sampling, seed: int, frame_index: int, codebook: int,
+                         suppress_from: int = 0, eos_id: int = -1, d_seen: int = 0) -> int:
+    """sample_logits without any device allocation (static scratch of the library,
+    vocab <= NAVI_SAMPLE_STATIC_MAX_VOCAB)."""
+    out = c_int32(-1)
+    check(lib().navi_sample_logits_static(dev.h, c_void_p(d_logits), vocab, byref(s.c()), seed, frame_index, codebook,
+                                          suppress_from, eos_id, c_void_p(d_seen) if d_seen else None, byref(out)))
+    return out.value
