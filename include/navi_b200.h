@@ -173,10 +173,11 @@ void navi_frame_destroy(navi_frame * f);
 int navi_frame_inspect(const navi_frame * f, float * h_hidden, float * h_logits, float * h_clogits);
 
 /* Phase trace (the reference's NAVI_FRAME_PROFILE, frame.hip:522-529, 612-650, made a
- * runtime switch): when enabled, CTA `cta` records %globaltimer (ns) at the start of each
- * launch and four stamps per phase (inputs ready, weights ready, dot products done, end).
- * navi_frame_profile copies the last launch's trace: out[0] = start, out[1 + 4p + k] =
- * stamp k of phase p; *n = 4 * phases + 1. */
+ * runtime switch): when enabled, CTA `cta` (every CTA if cta < 0) records %globaltimer (ns)
+ * at the start of each launch and four stamps per phase (inputs ready, weights ready, dot
+ * products done, end). navi_frame_profile copies the last launch's trace, one block of
+ * 4 * phases + 1 words per traced CTA (as many whole blocks as `cap` holds): block[0] =
+ * start, block[1 + 4p + k] = stamp k of phase p; *n = the words written. */
 int navi_frame_set_profile(navi_frame * f, int enable, int cta);
 int navi_frame_profile(const navi_frame * f, uint64_t * out, int cap, int * n);
 

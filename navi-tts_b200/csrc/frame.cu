@@ -46,6 +46,17 @@ uint64_t pcg_draw_seed(uint64_t seed, int frame_index, int codebook) {
 
 int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// cos[hd/2] then sin[hd/2] of RoPE at integer position pos: the angle is the f32 product
+// pos * inv_freq (as the reference forms it), cos and sin are taken in double and rounded.
+void rope_row(const std::vector<float> & inv_freq, int pos, float * out) {
+    const size_t h2 = inv_freq.size();
+    for (size_t i = 0; i < h2; ++i) {
+        const float ang = static_cast<float>(pos) * inv_freq[i];
+        out[i] = static_cast<float>(std::cos(static_cast<double>(ang)));
+        out[h2 + i] = static_cast<float>(std::sin(static_cast<double>(ang)));
+    }
+}
+
 } // namespace
 
 struct Frame::Impl {
@@ -59,6 +70,8 @@ struct Frame::Impl {
     int n_full = 0, n_first = 0;
     Work w{};
     float * inv_t = nullptr, * inv_c = nullptr;
+    std::vector<float> inv_t_h, inv_c_h;   // host copies (RoPE tables)
+    float * rope_c = nullptr;               // [NCB][HD] code-predictor cos | sin at positions 0..15
     float * step[2] = {nullptr, nullptr};
     int cur = 0;
     uint32_t tag = 0;
@@ -86,11 +99,12 @@ struct Frame::Impl {
         return static_cast<T *>(p);
     }
 
-    // Talker attention: cached positions in splits of `chunk` (16, more when the KV is so long
-    // that 16-position splits would outnumber the CTAs), one split per CTA.
+    // Talker attention: every KV head's cached positions in `split` ranges of `chunk`
+    // positions (at least 8 per split, at most grid / NKV splits per head), one range per CTA.
     void attn_plan(int n_past, int & split, int & chunk) const {
-        const int cap = std::min(MAX_SPLIT, grid);
-        chunk = std::max(16, cdiv(n_past, cap));
+        const int per_head = std::max(1, std::min(MAX_SPLIT, grid / d.NKV));
+        split = std::min(per_head, std::max(1, cdiv(n_past, 8)));
+        chunk = std::max(1, cdiv(n_past, split));
         split = std::max(1, cdiv(n_past, chunk));
     }
 
@@ -114,7 +128,12 @@ struct Frame::Impl {
         A.n_past = n_past;
         attn_plan(n_past, A.attn_split, A.attn_chunk);
         if (!first) {
-            const uint64_t kvb = 2ull * A.attn_chunk * d.KV * 2 + 5ull * d.HD * 2;
+            if (A.attn_chunk + 1 > MAX_ATTN_CHUNK + 1) {
+                err = "KV length " + std::to_string(n_past) + " needs " + std::to_string(A.attn_chunk) +
+                      " positions per attention split; the kernel takes at most " + std::to_string(MAX_ATTN_CHUNK);
+                return NAVI_E_KV_FULL;
+            }
+            const uint64_t kvb = 2ull * A.attn_chunk * d.HD * 2 + 2ull * d.HD * 4;
             if (kvb > ring) {
                 err = "KV length " + std::to_string(n_past) + " needs " + std::to_string(kvb) + "-byte attention slices; the ring holds " +
                       std::to_string(ring);
@@ -135,6 +154,8 @@ struct Frame::Impl {
         }
         A.inv_freq_t = inv_t;
         A.inv_freq_c = inv_c;
+        A.rope_c = rope_c;
+        if (!first) rope_row(inv_t_h, n_past, A.rope_t);
         A.temp = s.temperature; A.top_p = s.top_p; A.rep = s.repetition_penalty; A.top_k = s.top_k;
         A.cp_temp = s.cp_temperature; A.cp_top_p = s.cp_top_p; A.cp_top_k = s.cp_top_k;
         A.min_frames = s.min_frames; A.rng = s.rng; A.seed = seed; A.frame_index = frame_index;
@@ -146,6 +167,7 @@ struct Frame::Impl {
         A.scratch_floats = scratch_floats;
         A.part_floats = part_floats;
         A.prof = prof_on ? prof : nullptr;
+        if (prof_on) NAVI_CUDA(cudaMemsetAsync(prof, 0, static_cast<size_t>(PROF_STRIDE) * grid * sizeof(unsigned long long), stream));
         A.prof_cta = prof_cta;
         last_nphase = A.nphase;
         NAVI_CUDA(cudaEventRecord(ev0, stream));
@@ -203,8 +225,11 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
         fail("frame: the talker and code predictor must share hidden/heads/head_dim/ff", NAVI_E_SHAPE);
     if (tp.n_layer > MAX_TL || cp.n_layer > MAX_CP) fail("frame: too many layers for the kernel", NAVI_E_SHAPE);
     if (p.n_code_groups != NCB) fail("frame: the kernel is built for 16 codebooks", NAVI_E_SHAPE);
-    if (tp.head_dim != 64 && tp.head_dim != 128) fail("frame: head_dim must be 64 or 128", NAVI_E_SHAPE);
-    if (tp.n_head % tp.n_kv_head != 0 || tp.n_head / tp.n_kv_head > MAX_GROUP) fail("frame: unsupported GQA grouping", NAVI_E_SHAPE);
+    // the attention code is specialised at compile time (shape-generic code ran several times slower)
+    if (tp.head_dim != KHD || tp.n_head != KGR * tp.n_kv_head)
+        fail("frame: the kernel is built for head_dim " + std::to_string(KHD) + " and " + std::to_string(KGR) +
+                 " query heads per KV head",
+             NAVI_E_SHAPE);
     const int Q = tp.n_head * tp.head_dim, KV = tp.n_kv_head * tp.head_dim;
     if (tp.hidden % 256 || Q % 256 || tp.ff % 256) fail("frame: hidden, n_head*head_dim and ff must be multiples of 256", NAVI_E_SHAPE);
     if (opt.blocks_per_mp != 1) fail("frame: blocks_per_mp must be 1 (one CTA per SM)", NAVI_E_ARG);
@@ -319,22 +344,33 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     I.step[0] = I.alloc<float>(d.H);
     I.step[1] = I.alloc<float>(d.H);
     // RoPE inverse frequencies theta^(-2t/hd), computed in double, stored as f32
-    auto inv = [&](double theta) {
-        std::vector<float> v(d.HD / 2);
+    auto inv = [&](double theta, std::vector<float> & v) {
+        v.resize(d.HD / 2);
         for (int t = 0; t < d.HD / 2; ++t) v[t] = static_cast<float>(1.0 / std::pow(theta, 2.0 * t / d.HD));
         float * dv = I.alloc<float>(v.size());
         NAVI_CUDA(cudaMemcpy(dv, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
         return dv;
     };
-    I.inv_t = inv(tp.rope_theta);
-    I.inv_c = inv(cp.rope_theta);
+    I.inv_t = inv(tp.rope_theta, I.inv_t_h);
+    I.inv_c = inv(cp.rope_theta, I.inv_c_h);
+    {
+        std::vector<float> tab(static_cast<size_t>(NCB) * d.HD);
+        for (int pos = 0; pos < NCB; ++pos) rope_row(I.inv_c_h, pos, tab.data() + static_cast<size_t>(pos) * d.HD);
+        I.rope_c = I.alloc<float>(tab.size());
+        NAVI_CUDA(cudaMemcpy(I.rope_c, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice));
+    }
 
     // shared memory: everything but the ring is sized from the shapes; the ring takes the rest
     const int G = I.grid, Vmax = std::max(d.TV, d.CV);
     const uint32_t xin = 2u * std::max(d.H, std::max(d.Q, d.F));
     const uint32_t samp = 4u * Vmax + (Vmax + 3) / 4 + 256 + 64;
-    const uint32_t att = std::max(2u * MAX_GROUP * d.HD + 4u * d.HD,
-                                  static_cast<uint32_t>(d.NH * d.HD + 3 * d.KV + 64 + 2 * MAX_SPLIT + NCT));
+    // attention scratch: code predictor [q, k, v, scores, m/l, per-warp P.V]; talker split
+    // [q, k, v, new K/V row, m/l, per-warp P.V, scores]; talker combine [m, l, sums]
+    const uint32_t pvf = static_cast<uint32_t>(NCW * MAX_GROUP * d.HD);
+    const uint32_t att = std::max({2u * MAX_GROUP * d.HD + 4u * d.HD + 2u * MAX_GROUP * NCB + 4u * MAX_GROUP + pvf,
+                                   static_cast<uint32_t>(MAX_GROUP * d.HD + 3 * d.HD + 2 * MAX_GROUP) + pvf +
+                                       static_cast<uint32_t>(MAX_GROUP * (MAX_ATTN_CHUNK + 1)),
+                                   static_cast<uint32_t>(2 * MAX_SPLIT + NCT)});
     I.scratch_floats = std::max(xin, std::max(samp, att));
     const int max_nr = std::max({cdiv(d.QKV, G), cdiv(d.H, G), cdiv(d.F, G), cdiv(d.TV, G), cdiv(d.CV, G)});
     I.part_floats = static_cast<uint32_t>(NCW * 4 * max_nr);
@@ -346,7 +382,7 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     const uint32_t max_chunk = std::max({H4 + static_cast<uint32_t>(cdiv(d.QKV, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.H, G) * d.Q * 2),
                                          H4 + static_cast<uint32_t>(2 * cdiv(d.F, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.H, G) * d.F * 2),
                                          H4 + static_cast<uint32_t>(cdiv(d.TV, G) * d.H * 2), H4 + static_cast<uint32_t>(cdiv(d.CV, G) * d.H * 2),
-                                         static_cast<uint32_t>(2 * 16 * d.KV * 2 + 5 * d.HD * 2)});
+                                         static_cast<uint32_t>(2 * 8 * d.HD * 2 + 2 * d.HD * 4)});
     if (max_chunk > I.ring) fail("frame: a phase's weight slice does not fit the shared-memory ring", NAVI_E_SHAPE);
     I.smem = smem_layout(d, I.ring, I.scratch_floats, I.part_floats).total;
     NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_frame), cudaFuncAttributeMaxDynamicSharedMemorySize, I.smem));
@@ -416,9 +452,9 @@ int Frame::grid_blocks() const { return impl_->grid; }
 
 void Frame::set_profile(bool on, int cta) {
     Impl & I = *impl_;
-    if (on && !I.prof) I.prof = I.alloc<unsigned long long>(4 * 4096 + 1);
+    if (on && !I.prof) I.prof = I.alloc<unsigned long long>(static_cast<size_t>(PROF_STRIDE) * I.grid);
     I.prof_on = on;
-    I.prof_cta = std::max(0, std::min(cta, I.grid - 1));
+    I.prof_cta = cta < 0 ? -1 : std::min(cta, I.grid - 1);
 }
 
 int Frame::profile(uint64_t * out, int cap) const {
@@ -426,13 +462,18 @@ int Frame::profile(uint64_t * out, int cap) const {
     if (!I.prof) return 0;
     NAVI_CUDA(cudaSetDevice(I.ordinal));
     NAVI_CUDA(cudaStreamSynchronize(I.stream));
-    const int total = 4 * I.last_nphase + 1;
-    std::vector<unsigned long long> tmp(total);
+    // per traced CTA: out[0] = launch start, out[1 + 4p + k] = stamp k of phase p
+    const int per = 4 * I.last_nphase + 1;
+    const int nct = I.prof_cta < 0 ? I.grid : 1;
+    std::vector<unsigned long long> tmp(static_cast<size_t>(PROF_STRIDE) * nct);
     NAVI_CUDA(cudaMemcpy(tmp.data(), I.prof, tmp.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
-    // out[0] = launch start, out[1 + 4p + k] = stamp k of phase p
-    const int n = std::min(cap, total);
-    if (n > 0) out[0] = tmp[4 * I.last_nphase];
-    for (int i = 0; i + 1 < n; ++i) out[i + 1] = tmp[i];
+    int n = 0;
+    for (int c = 0; c < nct && n + per <= cap; ++c) {
+        const unsigned long long * src = tmp.data() + static_cast<size_t>(c) * PROF_STRIDE;
+        out[n] = src[4 * I.last_nphase];
+        for (int i = 0; i + 1 < per; ++i) out[n + 1 + i] = src[i];
+        n += per;
+    }
     return n;
 }
 

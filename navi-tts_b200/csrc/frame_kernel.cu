@@ -48,7 +48,7 @@ __device__ __forceinline__ Sm carve(char * base, const SmemLayout & L) {
 
 __device__ __forceinline__ bool launch_aborted(const Args & A) { return ld_relaxed_u32(&A.w.ctl[2]) == A.tag_base; }
 
-__device__ void raise_abort(const Args & A, Sm & S, int phase) {
+__device__ __noinline__ void raise_abort(const Args & A, int phase) {
     st_relaxed_u32(&A.w.ctl[1], static_cast<uint32_t>(phase));
     st_relaxed_u32(&A.w.ctl[3], blockIdx.x);
     __threadfence();
@@ -64,10 +64,9 @@ __device__ __forceinline__ bool ll_get(const uint64_t * p, uint32_t tag, float &
     for (;;) {
         w = ll_load(p);
         if (static_cast<uint32_t>(w >> 32) == tag) { out = __uint_as_float(static_cast<uint32_t>(w)); return true; }
-        if ((++spins & 31u) == 0) {
-            if (S.ctrl->abort || launch_aborted(A)) return false;
-            if (globaltimer() - t0 > A.timeout_ns) { raise_abort(A, S, phase); return false; }
-        }
+        ++spins;
+        if ((spins & 3u) == 0 && globaltimer() - t0 > A.timeout_ns) { raise_abort(A, phase); return false; }
+        if ((spins & 31u) == 0 && (S.ctrl->abort || launch_aborted(A))) return false;
     }
 }
 
@@ -91,7 +90,7 @@ __device__ bool wait_chunk(const Args & A, Sm & S, int chunk, int phase) {
         while (!mbar_try_wait(&S.bars[slot], parity)) {
             if ((++spins & 15u) == 0) {
                 if (S.ctrl->abort || launch_aborted(A)) { ok = false; break; }
-                if (globaltimer() - t0 > A.timeout_ns) { raise_abort(A, S, phase); ok = false; break; }
+                if (globaltimer() - t0 > A.timeout_ns) { raise_abort(A, phase); ok = false; break; }
             }
         }
     }
@@ -123,7 +122,7 @@ __device__ void producer(const Args & A, Sm & S) {
         const int ns = phase_segments(A, W, ph, b, R, seg, r0, r1);
         if (ns == 0) continue;
         uint32_t total = 0;
-        for (int i = 0; i < ns; ++i) total += seg[i].bytes;
+        for (int i = 0; i < ns; ++i) total += seg[i].bytes * seg[i].rows;
         // The chunk takes virtual bytes [head, head + total) of the ring stream, contiguous in
         // shared memory (a chunk that would straddle the end starts the next lap). It may
         // only overwrite bytes whose data chunk the consumers have released; skipped tail
@@ -138,7 +137,7 @@ __device__ void producer(const Args & A, Sm & S) {
             if ((++spins & 63u) == 0) {
                 const uint64_t now = globaltimer();
                 if (t0 == 0) t0 = now;
-                else if (now - t0 > 4 * A.timeout_ns) { raise_abort(A, S, p); S.ctrl->abort = 1; aborted = true; break; }
+                else if (now - t0 > 4 * A.timeout_ns) { raise_abort(A, p); S.ctrl->abort = 1; aborted = true; break; }
             }
             __nanosleep(64);
         }
@@ -150,12 +149,14 @@ __device__ void producer(const Args & A, Sm & S) {
         mbar_arrive_expect_tx(&S.bars[slot], total);
         uint32_t dst = static_cast<uint32_t>(head % RB);
         for (int i = 0; i < ns; ++i) {
-            const char * src = static_cast<const char *>(seg[i].src);
-            for (uint32_t o = 0; o < seg[i].bytes; o += PIECE) {
-                const uint32_t n = min(PIECE, seg[i].bytes - o);
-                bulk_g2s(S.ring + dst + o, src + o, n, &S.bars[slot]);
+            for (uint32_t r = 0; r < seg[i].rows; ++r) {
+                const char * src = static_cast<const char *>(seg[i].src) + static_cast<size_t>(r) * seg[i].stride;
+                for (uint32_t o = 0; o < seg[i].bytes; o += PIECE) {
+                    const uint32_t n = min(PIECE, seg[i].bytes - o);
+                    bulk_g2s(S.ring + dst + o, src + o, n, &S.bars[slot]);
+                }
+                dst += seg[i].bytes;
             }
-            dst += seg[i].bytes;
         }
         ++chunk;
     }
@@ -180,36 +181,43 @@ __device__ __forceinline__ uint32_t tag_of(uint64_t w) { return static_cast<uint
 __device__ __forceinline__ float val_of(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
 
 // Fetches exchange words [0, n) (n even) carrying `tag` into dst[0, n): thread t takes the
-// pairs at 2t + 2*NCT*k, issues up to 4 pair loads at once, then re-polls only stale pairs.
+// pairs at 2t + 2*NCT*k, issues up to 4 pair loads at once, then re-issues every stale pair
+// together until all carry the tag (one L2 round trip per poll, not one per stale pair).
 // Returns this thread's success (the caller decides with a barrier). ll_each() visits the
 // same elements in the same thread, so a transform needs no barrier in between.
-__device__ __noinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag, float * dst, const Args & A, Sm & S, int phase) {
+__device__ __noinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag, float * dst, const Args & A, Ctrl * ctrl, int phase) {
     constexpr int MAXK = 4;
     for (int base = 2 * threadIdx.x; base < n; base += 2 * NCT * MAXK) {
         uint64_t w[MAXK][2];
+        unsigned pend = 0;
 #pragma unroll
         for (int k = 0; k < MAXK; ++k) {
             const int i = base + 2 * NCT * k;
-            if (i < n) ll_load2(src + i, w[k][0], w[k][1]);
+            if (i < n) {
+                ll_load2(src + i, w[k][0], w[k][1]);
+                pend |= 1u << k;
+            }
         }
+        uint64_t t0 = 0;
+        uint32_t spins = 0;
+        for (;;) {
 #pragma unroll
-        for (int k = 0; k < MAXK; ++k) {
-            const int i = base + 2 * NCT * k;
-            if (i >= n) continue;
-            if (tag_of(w[k][0]) != tag || tag_of(w[k][1]) != tag) {
-                const uint64_t t0 = globaltimer();
-                uint32_t spins = 0;
-                for (;;) {
-                    ll_load2(src + i, w[k][0], w[k][1]);
-                    if (tag_of(w[k][0]) == tag && tag_of(w[k][1]) == tag) break;
-                    if ((++spins & 31u) == 0) {
-                        if (S.ctrl->abort || launch_aborted(A)) return false;
-                        if (globaltimer() - t0 > A.timeout_ns) { raise_abort(A, S, phase); return false; }
-                    }
+            for (int k = 0; k < MAXK; ++k) {
+                if (((pend >> k) & 1u) && tag_of(w[k][0]) == tag && tag_of(w[k][1]) == tag) {
+                    const int i = base + 2 * NCT * k;
+                    dst[i] = val_of(w[k][0]);
+                    dst[i + 1] = val_of(w[k][1]);
+                    pend &= ~(1u << k);
                 }
             }
-            dst[i] = val_of(w[k][0]);
-            dst[i + 1] = val_of(w[k][1]);
+            if (!pend) break;
+            if (t0 == 0) t0 = globaltimer();
+#pragma unroll
+            for (int k = 0; k < MAXK; ++k)
+                if ((pend >> k) & 1u) ll_load2(src + base + 2 * NCT * k, w[k][0], w[k][1]);
+            ++spins;
+            if ((spins & 3u) == 0 && globaltimer() - t0 > A.timeout_ns) { raise_abort(A, phase); return false; }
+            if ((spins & 31u) == 0 && (ctrl->abort || launch_aborted(A))) return false;
         }
     }
     return true;
@@ -234,7 +242,7 @@ __device__ __forceinline__ bool wait_chunk_local(const Args & A, Sm & S, int chu
     while (!mbar_try_wait(&S.bars[slot], parity)) {
         if ((++spins & 15u) == 0) {
             if (S.ctrl->abort || launch_aborted(A)) return false;
-            if (globaltimer() - t0 > A.timeout_ns) { raise_abort(A, S, phase); return false; }
+            if (globaltimer() - t0 > A.timeout_ns) { raise_abort(A, phase); return false; }
         }
     }
     return true;
@@ -402,18 +410,23 @@ __device__ SampleCfg sample_cfg(const Args & A, int codebook) {
 
 // Trace stamp k (0..3) of phase p on the traced CTA: 0 inputs ready, 1 weights ready,
 // 2 dot products done, 3 phase end (attention: 0 gathered, 1 normed, 2 attended, 3 combined).
+__device__ __forceinline__ unsigned long long * prof_base(const Args & A) {
+    if (!A.prof || threadIdx.x != 0) return nullptr;
+    if (A.prof_cta < 0) return A.prof + static_cast<size_t>(blockIdx.x) * PROF_STRIDE;
+    return blockIdx.x == A.prof_cta ? A.prof : nullptr;
+}
 __device__ __forceinline__ void stamp(const Args & A, int p, int k) {
-    if (A.prof && blockIdx.x == A.prof_cta && threadIdx.x == 0) A.prof[4 * p + k] = globaltimer();
+    if (unsigned long long * pb = prof_base(A)) pb[4 * p + k] = globaltimer();
 }
 
 // ---- attention -------------------------------------------------------------------------------------
 
-// Per-head RMSNorm + rotate-half RoPE at position `pos` of a head vector in shared memory,
-// by one warp (frame.hip:312-346: norm before RoPE, pairs (i, i + hd/2)). round16: store
-// the result rounded to f16 (K, as the cache holds it).
-__device__ __forceinline__ void warp_norm_rope(float * vec, const float * nw, const float * inv_freq, int HD, float eps, int pos,
-                                               bool round16) {
-    const int lane = threadIdx.x & 31, EPL = HD / 32;
+// Per-head RMSNorm + rotate-half RoPE of a head vector in shared memory, by one warp
+// (frame.hip:312-346: norm before RoPE, pairs (i, i + hd/2)). cs holds this position's
+// cos[hd/2] then sin[hd/2] (host-computed: f32 angle pos * inv_freq, cos/sin in double,
+// rounded to f32). round16: store the result rounded to f16 (K, as the cache holds it).
+__device__ __forceinline__ void warp_norm_rope(float * vec, const float * nw, const float * cs, int HD, float eps, bool round16) {
+    const int lane = threadIdx.x & 31, EPL = HD / 32, H2 = HD / 2;
     float e[4];
     float ss = 0.f;
 #pragma unroll
@@ -425,152 +438,240 @@ __device__ __forceinline__ void warp_norm_rope(float * vec, const float * nw, co
     const float scale = rsqrtf(ss / static_cast<float>(HD) + eps);
 #pragma unroll
     for (int t = 0; t < 4; ++t) if (t < EPL) e[t] = e[t] * scale * nw[lane + 32 * t];
-    const float fpos = static_cast<float>(pos);
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
         if (t >= EPL / 2) continue;
         const int i = lane + 32 * t;
-        float sn, cs;
-        sincosf(fpos * inv_freq[i], &sn, &cs);
+        const float c = cs[i], sn = cs[H2 + i];
         const float x0 = e[t], x1 = (EPL == 4) ? e[t + 2] : e[t + 1];
-        float r0 = x0 * cs - x1 * sn, r1 = x0 * sn + x1 * cs;
+        float r0 = x0 * c - x1 * sn, r1 = x0 * sn + x1 * c;
         if (round16) { r0 = f16_round(r0); r1 = f16_round(r1); }
         vec[i] = r0;
-        vec[i + HD / 2] = r1;
+        vec[i + H2] = r1;
     }
 }
 
-// Attention of query q (registers: dims [DPL*lane, +DPL)) over `n` K/V rows (f16 in shared
-// memory, row stride `stride` halves): m = max score, l = sum e^(s - m), acc = lane-local
-// dims of sum e^(s - m) v. Positions go in blocks of 16: the 16 scores come from four
-// transposed 4-way reductions and are broadcast, so the block costs one softmax update.
-template <int DPL>
-__device__ __forceinline__ void warp_attend(const float * q, const __half * K, const __half * V, int stride, int n, float scale,
-                                            float & m, float & l, float * acc) {
-    const int lane = threadIdx.x & 31;
-    m = -INFINITY;
-    l = 0.f;
+// Scaled scores q_j . K_t for the GR query heads j of `ngroups` groups (a KV head, or a
+// code-predictor column) and positions t < n. Lane groups of LPI = HD/8 lanes take one
+// (group, position) at a time, each lane 8 dims (one 16-byte K load); group g = stream %
+// ngroups keeps its queries in registers and walks positions t0, t0 + per, ... four at a
+// time, so the shuffle reductions of 4 x GR dots overlap. krow(g, t): K row (f16, HD);
+// qbase(g): query of head j at + j * HD (f32); sc_at(g, t): score of head j at + j * jstride.
+// Requires ngroups <= NCW * 32 / LPI. Every lane of a warp runs the same rounds.
+template <class KRow, class QBase, class ScAt>
+__device__ __forceinline__ void attn_scores(int ngroups, int n, int GR, int HD, float scale, int jstride, KRow && krow, QBase && qbase,
+                                            ScAt && sc_at) {
+    constexpr int B = 4;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int LPI = HD / 8, IPW = 32 / LPI, sub = lane / LPI, sl = lane % LPI;
+    const int per = (NCW * IPW) / ngroups;
+    const int hw = warp * IPW + sub, g = hw % ngroups, t0 = hw / ngroups;
+    const bool live = hw < per * ngroups;
+    float q[MAX_GROUP][8];
+    const float * qb = qbase(g);
 #pragma unroll
-    for (int t = 0; t < DPL; ++t) acc[t] = 0.f;
-    for (int j0 = 0; j0 < n; j0 += 16) {
-        float sc[16];
+    for (int j = 0; j < MAX_GROUP; ++j) {
+        if (j < GR && live) {
+            const float4 a = *reinterpret_cast<const float4 *>(qb + j * HD + sl * 8);
+            const float4 c = *reinterpret_cast<const float4 *>(qb + j * HD + sl * 8 + 4);
+            q[j][0] = a.x; q[j][1] = a.y; q[j][2] = a.z; q[j][3] = a.w;
+            q[j][4] = c.x; q[j][5] = c.y; q[j][6] = c.z; q[j][7] = c.w;
+        } else {
 #pragma unroll
-        for (int bq = 0; bq < 4; ++bq) {
-            float part[4];
+            for (int i = 0; i < 8; ++i) q[j][i] = 0.f;
+        }
+    }
+    for (int k = 0; k * per < n; k += B) {
+        float dots[B][MAX_GROUP];
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                const int j = j0 + bq * 4 + jj;
-                float dsum = 0.f;
-                if (j < n) {
-                    const __half * kr = K + static_cast<size_t>(j) * stride + lane * DPL;
+        for (int bb = 0; bb < B; ++bb) {
+            const int t = t0 + (k + bb) * per;
+            float kf[8];
+            if (live && t < n) {
+                const uint4 kw = *reinterpret_cast<const uint4 *>(krow(g, t) + sl * 8);
+                const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&kw.x));
+                const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&kw.y));
+                const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&kw.z));
+                const float2 f3 = __half22float2(*reinterpret_cast<const __half2 *>(&kw.w));
+                kf[0] = f0.x; kf[1] = f0.y; kf[2] = f1.x; kf[3] = f1.y; kf[4] = f2.x; kf[5] = f2.y; kf[6] = f3.x; kf[7] = f3.y;
+            } else {
 #pragma unroll
-                    for (int t = 0; t < DPL; ++t) dsum += q[t] * __half2float(kr[t]);
-                }
-                part[jj] = dsum;
+                for (int i = 0; i < 8; ++i) kf[i] = 0.f;
             }
-            const float r = warp_sum_multi<4>(part);
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) sc[bq * 4 + jj] = __shfl_sync(0xffffffffu, r, jj * 8) * scale;
+            for (int j = 0; j < MAX_GROUP; ++j) {
+                float a = 0.f;
+                if (j < GR)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) a = fmaf(q[j][i], kf[i], a);
+                dots[bb][j] = a;
+            }
         }
-        const int nb = min(16, n - j0);
-        float mb = m;
+        for (int o = LPI / 2; o > 0; o >>= 1)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) if (j < nb) mb = fmaxf(mb, sc[j]);
-        const float corr = expf(m - mb);
-        l *= corr;
+            for (int bb = 0; bb < B; ++bb)
 #pragma unroll
-        for (int t = 0; t < DPL; ++t) acc[t] *= corr;
+                for (int j = 0; j < MAX_GROUP; ++j)
+                    if (j < GR) dots[bb][j] += __shfl_xor_sync(0xffffffffu, dots[bb][j], o);
+        if (sl == 0 && live) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            if (j >= nb) continue;
-            const float e = expf(sc[j] - mb);
-            l += e;
-            const __half * vr = V + static_cast<size_t>(j0 + j) * stride + lane * DPL;
+            for (int bb = 0; bb < B; ++bb) {
+                const int t = t0 + (k + bb) * per;
+                if (t < n) {
+                    float * dst = sc_at(g, t);
 #pragma unroll
-            for (int t = 0; t < DPL; ++t) acc[t] += e * __half2float(vr[t]);
+                    for (int j = 0; j < MAX_GROUP; ++j) if (j < GR) dst[j * jstride] = dots[bb][j] * scale;
+                }
+            }
         }
-        m = mb;
     }
 }
 
-// Talker attention at position n_past (frame.hip:350-385): CTA s < attn_split takes the
-// cached positions [s*chunk, ...) for every head, from its ring chunk (K/V rows streamed by
-// the producer); the last split also takes the new position. Partials (m, l, acc) go to
-// the exchange words; CTA G-NH+h combines head h in split order. A single split writes the
-// output directly.
+// Softmax rows: row r (< nrows) holds n_of(r) scores at sc + r * stride; they are replaced by
+// e^(s - m), and ml[2r], ml[2r+1] get m and l = sum e^(s - m). One warp per row.
+template <class NOf>
+__device__ __forceinline__ void attn_softmax(float * sc, int stride, int nrows, NOf && n_of, float * ml) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int r = warp; r < nrows; r += NCW) {
+        const int n = n_of(r);
+        float * row = sc + r * stride;
+        float m = -INFINITY;
+        for (int t = lane; t < n; t += 32) m = fmaxf(m, row[t]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int t = lane; t < n; t += 32) {
+            const float e = expf(row[t] - m);
+            row[t] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) { ml[2 * r] = m; ml[2 * r + 1] = l; }
+    }
+}
+
+// sum over positions of p_j[t] * V_t for the GR heads j of each of `ngroups` groups: warp w
+// takes group w % ngroups and the positions t = w / ngroups + k * (NCW / ngroups), lane e4
+// dims [4 e4, 4 e4 + 4) (HD == 128) -- so a warp reads one contiguous V row slice per step.
+// The per-warp sums go to pv[w][j][HD]; after a barrier, emit(g, j, e, sum) gets the total
+// of every (g, j < GR, e < HD), summed over the warps of g in warp order. ngroups divides NCW.
+template <class NOf, class PAt, class VRow, class Emit>
+__device__ __forceinline__ void attn_pv(int ngroups, int GR, int HD, NOf && n_of, PAt && p_at, VRow && vrow, float * pv, Emit && emit) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int WPG = NCW / ngroups, g = warp % ngroups, tq = warp / ngroups, E4 = HD / 4;
+    const int n = n_of(g);
+    float acc[MAX_GROUP][4];
+#pragma unroll
+    for (int j = 0; j < MAX_GROUP; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
+    if (lane < E4) {
+        for (int t = tq; t < n; t += WPG) {
+            const uint2 vw = *reinterpret_cast<const uint2 *>(vrow(g, t) + lane * 4);
+            const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vw.x));
+            const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vw.y));
+#pragma unroll
+            for (int j = 0; j < MAX_GROUP; ++j) {
+                if (j >= GR) continue;
+                const float pt = p_at(g, j)[t];
+                acc[j][0] = fmaf(pt, v01.x, acc[j][0]);
+                acc[j][1] = fmaf(pt, v01.y, acc[j][1]);
+                acc[j][2] = fmaf(pt, v23.x, acc[j][2]);
+                acc[j][3] = fmaf(pt, v23.y, acc[j][3]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < MAX_GROUP; ++j)
+            if (j < GR) *reinterpret_cast<float4 *>(pv + (warp * MAX_GROUP + j) * HD + lane * 4) = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+    }
+    named_sync(BID, NCT);
+    for (int u = threadIdx.x; u < ngroups * GR * HD; u += NCT) {
+        const int e = u % HD, gj = u / HD, gg = gj / GR, j = gj - gg * GR;
+        float sum = 0.f;
+        for (int w = gg; w < NCW; w += ngroups) sum += pv[(w * MAX_GROUP + j) * HD + e];
+        emit(gg, j, e, sum);
+    }
+}
+
+// Talker attention at position n_past (frame.hip:350-385), split over KV heads and cached
+// positions: CTA b < NKV * S (S = attn_split) takes KV head g = b / S and the positions
+// [s * chunk, (s + 1) * chunk) of split s = b % S, streamed into its ring chunk as that head's
+// 256-byte K and V row slices; split S-1 also takes the new position (and writes its K/V
+// row of head g). Scores, softmax and P.V run as CTA-wide passes over the GR query heads of
+// g. Partials (m, l, acc) go to the exchange words; CTA G-NH+h combines head h in split
+// order. A single split writes the output directly.
 __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, const uint8_t * chunk_base, uint32_t tag, uint32_t ptag,
                                  int p) {
     const Dims & d = A.d;
-    const int HD = d.HD, NH = d.NH, GR = d.GROUP, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int HD = KHD, GR = KGR;
+    const int NH = d.NH, tid = threadIdx.x;
     const int G = gridDim.x, b = blockIdx.x, Sp = A.attn_split, pos = A.n_past;
     const float scale = rsqrtf(static_cast<float>(HD));
     const uint32_t WST = HD + 2;
-    if (b < Sp) {
+    const int NPS = A.attn_chunk + 1;                  // score slots per head
+    float * qs = S.scratch;                            // [GR][HD]
+    float * ks = qs + MAX_GROUP * HD;                  // [HD] new position
+    float * vs = ks + HD;                              // [HD]
+    __half * kh = reinterpret_cast<__half *>(vs + HD); // new K/V row slice as f16 [2][HD]
+    float * ml = vs + 2 * HD;                          // [GR][2]
+    float * pv = ml + 2 * MAX_GROUP;                   // [NCW][MAX_GROUP][HD]
+    float * sc = pv + NCW * MAX_GROUP * HD;            // [GR][NPS] scores, then e^(s - m)
+    if (b < d.NKV * Sp) {
+        const int g = b / Sp, sp = b - g * Sp;
         const float * qn = reinterpret_cast<const float *>(chunk_base);
         const float * kn = qn + HD;
-        const float * inv = kn + HD;
-        const __half * Kc = reinterpret_cast<const __half *>(chunk_base + (2 * HD + HD / 2) * 4);
-        int r0 = min(b * A.attn_chunk, pos), r1 = min(r0 + A.attn_chunk, pos);
+        const __half * Kc = reinterpret_cast<const __half *>(chunk_base + 2 * HD * 4);
+        const int r0 = min(sp * A.attn_chunk, pos), r1 = min(r0 + A.attn_chunk, pos);
         const int nc = r1 - r0;
-        const __half * Vc = Kc + static_cast<size_t>(nc) * d.KV;
-        const bool last = b == Sp - 1;
-        float * qs = S.scratch;                 // [NH][HD]
-        float * ks = qs + NH * HD;              // [NKV][HD] new position
-        float * vs = ks + d.KV;                 // [NKV][HD]
-        __half * kh = reinterpret_cast<__half *>(vs + d.KV);   // new K/V rows as f16 [2][KV]
-        // inputs: q of every head, and (last split) k, v of the new position
-        const int nin = last ? d.QKV : d.Q;
-        const bool ok = ll_fetch(A.w.qkv, nin, ptag, qs, A, S, p);   // q|k|v contiguous in both layouts
+        const __half * Vc = Kc + static_cast<size_t>(nc) * HD;
+        const bool last = sp == Sp - 1;
+        const int n = nc + (last ? 1 : 0);
+        // inputs: q of the group's heads, and (last split) k, v of head g at the new position
+        bool ok = ll_fetch(A.w.qkv + g * GR * HD, GR * HD, ptag, qs, A, S.ctrl, p);
+        if (last) {
+            ok = ok && ll_fetch(A.w.qkv + d.Q + g * HD, HD, ptag, ks, A, S.ctrl, p);
+            ok = ok && ll_fetch(A.w.qkv + d.Q + d.KV + g * HD, HD, ptag, vs, A, S.ctrl, p);
+        }
         if (!consumers_ok(S, ok)) return false;
         stamp(A, p, 0);
-        for (int v = warp; v < NH + (last ? d.NKV : 0); v += NCW)
-            warp_norm_rope(v < NH ? qs + v * HD : ks + (v - NH) * HD, v < NH ? qn : kn, inv, HD, d.eps_t, pos, v >= NH);
+        const int warp = tid >> 5;
+        if (warp < GR + (last ? 1 : 0))
+            warp_norm_rope(warp < GR ? qs + warp * HD : ks, warp < GR ? qn : kn, A.rope_t, HD, d.eps_t, warp >= GR);
         named_sync(BID, NCT);
         if (last) {
-            for (int i = tid; i < d.KV; i += NCT) {
+            for (int i = tid; i < HD; i += NCT) {
                 const __half kq = __float2half_rn(ks[i]), vq = __float2half_rn(vs[i]);
                 kh[i] = kq;
-                kh[d.KV + i] = vq;
-                A.kc[ph.layer][static_cast<size_t>(pos) * d.KV + i] = kq;
-                A.vc[ph.layer][static_cast<size_t>(pos) * d.KV + i] = vq;
+                kh[HD + i] = vq;
+                A.kc[ph.layer][static_cast<size_t>(pos) * d.KV + g * HD + i] = kq;
+                A.vc[ph.layer][static_cast<size_t>(pos) * d.KV + g * HD + i] = vq;
             }
             named_sync(BID, NCT);
         }
         stamp(A, p, 1);
-        // one warp per head: cached positions from the chunk, then the new one
-        for (int h = warp; h < NH; h += NCW) {
-            const int g = h / GR;
-            float q[4], acc[4], m, l;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) q[t] = (t < HD / 32) ? qs[h * HD + lane * (HD / 32) + t] : 0.f;
-            if (HD == 128) warp_attend<4>(q, Kc + g * HD, Vc + g * HD, d.KV, nc, scale, m, l, acc);
-            else warp_attend<2>(q, Kc + g * HD, Vc + g * HD, d.KV, nc, scale, m, l, acc);
-            if (last) {
-                float m2, l2, a2[4];
-                if (HD == 128) warp_attend<4>(q, kh + g * HD, kh + d.KV + g * HD, 0, 1, scale, m2, l2, a2);
-                else warp_attend<2>(q, kh + g * HD, kh + d.KV + g * HD, 0, 1, scale, m2, l2, a2);
-                const float mn = fmaxf(m, m2), f1 = expf(m - mn), f2 = expf(m2 - mn);
-                l = l * f1 + l2 * f2;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) acc[t] = acc[t] * f1 + a2[t] * f2;
-                m = mn;
-            }
-            const int DPL = HD / 32;
-            if (Sp == 1) {
-                for (int t = 0; t < DPL; ++t) ll_store(A.w.attn + h * HD + lane * DPL + t, acc[t] / l, tag);
-            } else {
-                uint64_t * pp = A.w.part + (static_cast<size_t>(b) * NH + h) * WST;
-                if (lane == 0) { ll_store(pp, m, tag); ll_store(pp + 1, l, tag); }
-                for (int t = 0; t < DPL; ++t) ll_store(pp + 2 + lane * DPL + t, acc[t], tag);
-            }
-        }
+        attn_scores(1, n, GR, HD, scale, NPS, [&](int, int t) { return t < nc ? Kc + static_cast<size_t>(t) * HD : kh; },
+                    [&](int) { return static_cast<const float *>(qs); }, [&](int, int t) { return sc + t; });
+        named_sync(BID, NCT);
+        attn_softmax(sc, NPS, GR, [&](int) { return n; }, ml);
+        named_sync(BID, NCT);
+        attn_pv(1, GR, HD, [&](int) { return n; }, [&](int, int j) { return static_cast<const float *>(sc + j * NPS); },
+                [&](int, int t) { return t < nc ? Vc + static_cast<size_t>(t) * HD : kh + HD; }, pv,
+                [&](int, int j, int e, float sum) {
+                    const int h = g * GR + j;
+                    if (Sp == 1) {
+                        ll_store(A.w.attn + h * HD + e, sum / ml[2 * j + 1], tag);
+                    } else {
+                        uint64_t * pp = A.w.part + (static_cast<size_t>(sp) * NH + h) * WST;
+                        ll_store(pp + 2 + e, sum, tag);
+                        if (e == 0) { ll_store(pp, ml[2 * j], tag); ll_store(pp + 1, ml[2 * j + 1], tag); }
+                    }
+                });
         stamp(A, p, 2);
     }
     // combine: CTA G - NH + h reduces head h over the splits, in split order
     const int h = b - (G - NH);
     if (Sp > 1 && h >= 0) {
         named_sync(BID, NCT);                   // this CTA's own split (if any) is done with its scratch
-        float * ms = S.scratch + NH * HD + 3 * d.KV + 64;   // [MAX_SPLIT] m, [MAX_SPLIT] l, [NCT/HD][HD] sums
+        float * ms = S.scratch;                 // [MAX_SPLIT] m, [MAX_SPLIT] l, [NCT/HD][HD] sums
         float * ls = ms + MAX_SPLIT;
         float * ps = ls + MAX_SPLIT;
         bool ok = true;
@@ -581,7 +682,7 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, const
         if (!consumers_ok(S, ok)) return false;
         float M = -INFINITY;
         for (int k = 0; k < Sp; ++k) M = fmaxf(M, ms[k]);
-        // thread (e, q): dim e, splits q, q+4, ...
+        // thread (e, q): dim e, splits q, q+NQ, ...
         const int e = tid % HD, qq = tid / HD, NQ = NCT / HD;
         float a = 0.f;
         for (int k = qq; k < Sp && ok; k += NQ) {
@@ -608,28 +709,32 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, const
 __device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, const uint8_t * chunk_base, uint32_t tag, uint32_t ptag,
                              int p) {
     const Dims & d = A.d;
-    const int HD = d.HD, GR = d.GROUP, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ncol = ph.ncol, pos = ph.pos;
+    constexpr int HD = KHD, GR = KGR;
+    const int tid = threadIdx.x, ncol = ph.ncol, pos = ph.pos;
     const int g = blockIdx.x;
     if (g >= d.NKV) return true;
     const float * qn = reinterpret_cast<const float *>(chunk_base);
     const float * kn = qn + HD;
-    const float * inv = kn + HD;
     __half * kv = S.cpkv + static_cast<size_t>(ph.layer) * NCB * 2 * HD;   // [pos][K,V][HD]
-    float * qs = S.scratch;                 // [2][GR][HD]
+    float * qs = S.scratch;                 // [2][MAX_GROUP][HD]
     float * ks = qs + 2 * MAX_GROUP * HD;   // [2][HD]
     float * vs = ks + 2 * HD;               // [2][HD]
+    float * sc = vs + 2 * HD;               // [2][MAX_GROUP][NCB] scores, then e^(s - m)
+    float * ml = sc + 2 * MAX_GROUP * NCB;  // [2][MAX_GROUP][2]
+    float * pv = ml + 4 * MAX_GROUP;        // [NCW][MAX_GROUP][HD]
     bool ok = true;
     for (int c = 0; c < ncol && ok; ++c) {
         const uint64_t * src = A.w.qkv + static_cast<size_t>(c) * d.QKV;
         float * qd = qs + c * MAX_GROUP * HD;
-        ok = ll_fetch(src + g * GR * HD, GR * HD, ptag, qd, A, S, p) && ll_fetch(src + d.Q + g * HD, HD, ptag, ks + c * HD, A, S, p) &&
-             ll_fetch(src + d.Q + d.KV + g * HD, HD, ptag, vs + c * HD, A, S, p);
+        ok = ll_fetch(src + g * GR * HD, GR * HD, ptag, qd, A, S.ctrl, p) && ll_fetch(src + d.Q + g * HD, HD, ptag, ks + c * HD, A, S.ctrl, p) &&
+             ll_fetch(src + d.Q + d.KV + g * HD, HD, ptag, vs + c * HD, A, S.ctrl, p);
     }
     if (!consumers_ok(S, ok)) return false;
     stamp(A, p, 0);
-    for (int v = warp; v < ncol * (GR + 1); v += NCW) {
+    for (int v = tid >> 5; v < ncol * (GR + 1); v += NCW) {
         const int c = v / (GR + 1), j = v - c * (GR + 1);
-        warp_norm_rope(j < GR ? qs + (c * MAX_GROUP + j) * HD : ks + c * HD, j < GR ? qn : kn, inv, HD, d.eps_c, pos + c, j == GR);
+        warp_norm_rope(j < GR ? qs + (c * MAX_GROUP + j) * HD : ks + c * HD, j < GR ? qn : kn, A.rope_c + (pos + c) * HD, HD, d.eps_c,
+                       j == GR);
     }
     named_sync(BID, NCT);
     for (int i = tid; i < ncol * HD; i += NCT) {
@@ -640,16 +745,19 @@ __device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, const uin
     named_sync(BID, NCT);
     stamp(A, p, 1);
     const float scale = rsqrtf(static_cast<float>(HD));
-    for (int v = warp; v < ncol * GR; v += NCW) {
-        const int c = v / GR, j = v - c * GR;
-        float q[4], acc[4], m, l;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) q[t] = (t < HD / 32) ? qs[(c * MAX_GROUP + j) * HD + lane * (HD / 32) + t] : 0.f;
-        if (HD == 128) warp_attend<4>(q, kv, kv + HD, 2 * HD, pos + c + 1, scale, m, l, acc);
-        else warp_attend<2>(q, kv, kv + HD, 2 * HD, pos + c + 1, scale, m, l, acc);
-        const int DPL = HD / 32;
-        for (int t = 0; t < DPL; ++t) ll_store(A.w.attn + static_cast<size_t>(c) * d.Q + (g * GR + j) * HD + lane * DPL + t, acc[t] / l, tag);
-    }
+    // column c attends to positions 0..pos+c (causal within the 2-column pass)
+    attn_scores(ncol, pos + ncol, GR, HD, scale, NCB, [&](int, int t) { return kv + static_cast<size_t>(t) * 2 * HD; },
+                [&](int c) { return static_cast<const float *>(qs + c * MAX_GROUP * HD); },
+                [&](int c, int t) { return sc + c * MAX_GROUP * NCB + t; });
+    named_sync(BID, NCT);
+    attn_softmax(sc, NCB, ncol * MAX_GROUP, [&](int r) { return (r % MAX_GROUP) < GR ? pos + 1 + r / MAX_GROUP : 0; }, ml);
+    named_sync(BID, NCT);
+    attn_pv(ncol, GR, HD, [&](int c) { return pos + 1 + c; },
+            [&](int c, int j) { return static_cast<const float *>(sc + (c * MAX_GROUP + j) * NCB); },
+            [&](int, int t) { return static_cast<const __half *>(kv + (static_cast<size_t>(t) * 2 + 1) * HD); }, pv,
+            [&](int c, int j, int e, float sum) {
+                ll_store(A.w.attn + static_cast<size_t>(c) * d.Q + (g * GR + j) * HD + e, sum / ml[2 * (c * MAX_GROUP + j) + 1], tag);
+            });
     stamp(A, p, 2);
     named_sync(BID, NCT);
     return true;
@@ -694,7 +802,7 @@ __device__ void consumer(const Args & A, Sm & S) {
 
         if (ph.op == FINAL) {
             const SampleScratch sc = sampler_scratch(S, Vmax);
-            const bool ok = ll_fetch(A.w.clogits + static_cast<size_t>(NCB - 2) * d.CV, d.CV, ptag, sc.s, A, S, p);
+            const bool ok = ll_fetch(A.w.clogits + static_cast<size_t>(NCB - 2) * d.CV, d.CV, ptag, sc.s, A, S.ctrl, p);
             if (!consumers_ok(S, ok)) break;
             stamp(A, p, 0);
             const int code = sample_cta<NCT>(d.CV, sample_cfg(A, NCB - 1), sc, BID);
@@ -721,6 +829,7 @@ __device__ void consumer(const Args & A, Sm & S) {
         // one barrier, dot products with the epilogue in the lanes that hold the sums
         const bool has_norm = ph.op == TQKV || ph.op == CQKV || ph.op == TGU || ph.op == CGU || ph.op == THEAD || ph.op == CHEAD;
         bool ok = ns > 0 ? wait_chunk_local(A, S, chunk, p) : true;
+        stamp(A, p, 1);
         const uint8_t * cbase = S.ring + S.meta_off[chunk % NSLOT];
         const float * nw = reinterpret_cast<const float *>(cbase);
         const __half * Ws = reinterpret_cast<const __half *>(cbase + (has_norm ? d.H * 4 : 0));
@@ -747,7 +856,7 @@ __device__ void consumer(const Args & A, Sm & S) {
                     if (A.logits_in) {
                         for (int i = tid; i < d.TV; i += NCT) sc.s[i] = __ldcg(A.logits_in + i);
                     } else {
-                        okl = ll_fetch(A.w.logits, d.TV, ptag, sc.s, A, S, p);
+                        okl = ll_fetch(A.w.logits, d.TV, ptag, sc.s, A, S.ctrl, p);
                     }
                     if (!consumers_ok(S, okl && ok)) { ok = false; break; }
                     const int cb0 = sample_cta<NCT>(d.TV, sample_cfg(A, 0), sc, BID);
@@ -758,7 +867,7 @@ __device__ void consumer(const Args & A, Sm & S) {
                     }
                 } else if (ph.layer == 0) {
                     const SampleScratch sc = sampler_scratch(S, Vmax);
-                    const bool okl = ll_fetch(A.w.clogits + static_cast<size_t>(ph.pos - 2) * d.CV, d.CV, ptag, sc.s, A, S, p);
+                    const bool okl = ll_fetch(A.w.clogits + static_cast<size_t>(ph.pos - 2) * d.CV, d.CV, ptag, sc.s, A, S.ctrl, p);
                     if (!consumers_ok(S, okl && ok)) { ok = false; break; }
                     const int code = sample_cta<NCT>(d.CV, sample_cfg(A, ph.pos - 1), sc, BID);
                     if (tid == 0) S.codes[ph.pos - 1] = code;
@@ -766,7 +875,7 @@ __device__ void consumer(const Args & A, Sm & S) {
                     for (int i = tid; i < d.H; i += NCT) stage(0, i, __half2float(row[i]));
                 } else {
                     for (int c = 0; c < ncol && ok; ++c) {
-                        ok = ll_fetch(A.w.x + static_cast<size_t>(c) * d.H, d.H, ptag, S.xres + c * d.H, A, S, p);
+                        ok = ll_fetch(A.w.x + static_cast<size_t>(c) * d.H, d.H, ptag, S.xres + c * d.H, A, S.ctrl, p);
                         if (ok) stage_fetched(c);
                     }
                 }
@@ -775,24 +884,24 @@ __device__ void consumer(const Args & A, Sm & S) {
             case TGU: case CGU:
                 nnorm = ncol;
                 for (int c = 0; c < ncol && ok; ++c) {
-                    ok = ll_fetch(A.w.x + static_cast<size_t>(c) * d.H, d.H, ptag, S.xres + c * d.H, A, S, p);
+                    ok = ll_fetch(A.w.x + static_cast<size_t>(c) * d.H, d.H, ptag, S.xres + c * d.H, A, S.ctrl, p);
                     if (ok) stage_fetched(c);
                 }
                 break;
             case TO: case CO:
-                for (int c = 0; c < ncol && ok; ++c) ok = ll_fetch(A.w.attn + static_cast<size_t>(c) * d.Q, d.Q, ptag, xin + c * XS, A, S, p);
+                for (int c = 0; c < ncol && ok; ++c) ok = ll_fetch(A.w.attn + static_cast<size_t>(c) * d.Q, d.Q, ptag, xin + c * XS, A, S.ctrl, p);
                 break;
             case TDOWN: case CDOWN:
-                for (int c = 0; c < ncol && ok; ++c) ok = ll_fetch(A.w.h + static_cast<size_t>(c) * d.F, d.F, ptag, xin + c * XS, A, S, p);
+                for (int c = 0; c < ncol && ok; ++c) ok = ll_fetch(A.w.h + static_cast<size_t>(c) * d.F, d.F, ptag, xin + c * XS, A, S.ctrl, p);
                 break;
             case THEAD:
                 nnorm = 1;
-                ok = ok && ll_fetch(A.w.x, d.H, ptag, S.xres, A, S, p);
+                ok = ok && ll_fetch(A.w.x, d.H, ptag, S.xres, A, S.ctrl, p);
                 if (ok) stage_fetched(0);
                 break;
             case CHEAD:
                 nnorm = 1;
-                ok = ok && ll_fetch(A.w.x + static_cast<size_t>(ncol - 1) * d.H, d.H, ptag, S.xres, A, S, p);
+                ok = ok && ll_fetch(A.w.x + static_cast<size_t>(ncol - 1) * d.H, d.H, ptag, S.xres, A, S.ctrl, p);
                 if (ok) stage_fetched(0);
                 break;
             default: break;
@@ -873,7 +982,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_frame(const __grid_constant__ Args 
         fence_mbar_init();
     }
     __syncthreads();
-    if (A.prof && blockIdx.x == A.prof_cta && threadIdx.x == 0) A.prof[4 * A.nphase] = globaltimer();
+    if (unsigned long long * pb = prof_base(A)) pb[4 * A.nphase] = globaltimer();
     if (threadIdx.x >= NCT) producer(A, S);
     else consumer(A, S);
 }

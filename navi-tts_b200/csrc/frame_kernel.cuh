@@ -43,11 +43,15 @@ constexpr int MAX_TL = 32;              // talker layers
 constexpr int MAX_CP = 8;               // code-predictor layers
 constexpr int NCB = 16;                 // codebooks per frame
 constexpr int NSLOT = 16;               // ring slots (mbarriers)
-constexpr int MAX_SPLIT = 148;          // talker attention splits (one per CTA at most)
+constexpr int MAX_SPLIT = 148;          // talker attention splits per KV head
+constexpr int MAX_ATTN_CHUNK = 511;     // cached positions per talker attention split
 constexpr int MAX_SEG = 5;              // weight segments per phase chunk
 constexpr int MAX_GROUP = 4;            // q heads per KV head
+constexpr int KHD = 128;                // head_dim the attention code is compiled for
+constexpr int KGR = 2;                  // query heads per KV head the attention code is compiled for
 constexpr uint32_t PIECE = 32768;       // bulk copies are issued in pieces of at most this
 constexpr uint32_t CTRL_BYTES = 256;    // per-CTA control block in shared memory
+constexpr int PROF_STRIDE = 4 * 4096 + 1;   // trace words per CTA: 4 stamps x phases, then the start
 
 enum Op : uint8_t { TQKV, TATTN, TO, TGU, TDOWN, THEAD, CQKV, CATTN, CO, CGU, CDOWN, CHEAD, FINAL };
 
@@ -102,7 +106,8 @@ struct Args {
     Work w;
     uint32_t tag_base;
     int n_past;        // talker position
-    int attn_split;    // talker attention splits (CTAs 0..attn_split-1)
+    int attn_split;    // talker attention splits per KV head: CTA b < NKV * attn_split takes KV head
+                       // b / attn_split and its split b % attn_split
     int attn_chunk;    // cached positions per split
     const float * step_in;     // talker input row (frames >= 1)
     const float * hidden_in;   // frame 0: the prefill's post-norm hidden
@@ -113,6 +118,8 @@ struct Args {
     __half * vc[MAX_TL];
     const float * inv_freq_t;  // [HD/2]
     const float * inv_freq_c;
+    float rope_t[128];         // talker position n_past: cos[HD/2], then sin[HD/2]
+    const float * rope_c;      // code predictor, positions 0..15: [NCB][HD] = cos[HD/2], sin[HD/2]
     // sampling
     float temp, top_p, rep;
     int top_k;
@@ -127,8 +134,8 @@ struct Args {
     uint32_t ring_bytes;
     uint32_t scratch_floats;
     uint32_t part_floats;
-    unsigned long long * prof;   // optional trace: [4 * nphase + 1] globaltimer stamps on CTA prof_cta
-    int prof_cta;
+    unsigned long long * prof;   // optional trace: [4 * nphase + 1] globaltimer stamps on CTA prof_cta,
+    int prof_cta;                // or, prof_cta < 0, on every CTA b at prof + b * PROF_STRIDE
 };
 
 // ---- shared-memory layout (identical on host and device) ---------------------------------
@@ -173,9 +180,13 @@ __host__ __device__ inline void split_rows(int R, int b, int G, int & r0, int & 
     r1 = static_cast<int>((static_cast<long long>(R) * (b + 1)) / G);
 }
 
+// A run of `rows` copies of `bytes` each, from src, src + stride, ... (bytes and stride
+// multiples of 16), packed back to back in the chunk.
 struct Seg {
     const void * src;
     uint32_t bytes;
+    uint32_t rows = 1;
+    uint32_t stride = 0;
 };
 
 // This CTA's rows of every matrix shape the phases use (computed once per launch: the
@@ -193,10 +204,11 @@ __host__ __device__ inline Rows cta_rows(const Dims & d, int b, int G) {
     return r;
 }
 
-// The bytes phase `ph` streams into CTA b's ring chunk, in order (up to MAX_SEG contiguous
-// segments, each a multiple of 16 bytes): the phase's norm weights first, then its weight
-// rows [r0, r1); for talker attention, q/k norm weights, the RoPE table and the K and V
-// rows of the split's cached positions. Returns the number of segments (0: no chunk).
+// The bytes phase `ph` streams into CTA b's ring chunk, in order (up to MAX_SEG segments,
+// each a multiple of 16 bytes): the phase's norm weights first, then its weight rows
+// [r0, r1); for attention, the q/k norm weights, then (talker) this split's KV head slice
+// [HD] of the K and of the V rows of its cached positions [r0, r1). Returns the number of
+// segments (0: no chunk).
 __host__ __device__ inline int phase_segments(const Args & A, const ModelW & W, const Phase & ph, int b, const Rows & R, Seg * s,
                                               int & r0, int & r1) {
     const Dims & d = A.d;
@@ -236,25 +248,26 @@ __host__ __device__ inline int phase_segments(const Args & A, const ModelW & W, 
             s[1] = {W.lm_head[ph.pos - 1] + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
             return r1 > r0 ? 2 : 0;
         case TATTN: {
-            if (b >= A.attn_split) return 0;
+            const int S = A.attn_split;
+            if (b >= d.NKV * S) return 0;
+            const int g = b / S, sp = b - g * S;
             s[0] = {L->qn, HD4};
             s[1] = {L->kn, HD4};
-            s[2] = {A.inv_freq_t, HD4 / 2};
-            // cached positions [r0, r1) of this split
-            r0 = min(b * A.attn_chunk, A.n_past);
+            // cached positions [r0, r1) of this split, KV head g
+            r0 = min(sp * A.attn_chunk, A.n_past);
             r1 = min(r0 + A.attn_chunk, A.n_past);
-            if (r1 <= r0) return 3;
-            const size_t row = static_cast<size_t>(d.KV);
-            s[3] = {A.kc[ph.layer] + static_cast<size_t>(r0) * row, static_cast<uint32_t>((r1 - r0) * d.KV * 2)};
-            s[4] = {A.vc[ph.layer] + static_cast<size_t>(r0) * row, static_cast<uint32_t>((r1 - r0) * d.KV * 2)};
-            return 5;
+            if (r1 <= r0) return 2;
+            const size_t off = static_cast<size_t>(r0) * d.KV + static_cast<size_t>(g) * d.HD;
+            const uint32_t rows = static_cast<uint32_t>(r1 - r0), rb = static_cast<uint32_t>(d.HD) * 2, st = static_cast<uint32_t>(d.KV) * 2;
+            s[2] = {A.kc[ph.layer] + off, rb, rows, st};
+            s[3] = {A.vc[ph.layer] + off, rb, rows, st};
+            return 4;
         }
         case CATTN:
             if (b >= d.NKV) return 0;
             s[0] = {L->qn, HD4};
             s[1] = {L->kn, HD4};
-            s[2] = {A.inv_freq_c, HD4 / 2};
-            return 3;
+            return 2;
         default:
             return 0;
     }

@@ -9,7 +9,8 @@ import ctypes
 import os
 from ctypes import POINTER, c_char, c_char_p, c_double, c_float, c_int, c_int32, c_size_t, c_uint8, c_uint16, c_uint64, c_void_p
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libnavi_b200.so")
+# NAVI_B200_LIB overrides the library path (e.g. a variant build); the default is the in-tree build.
+LIB_PATH = os.environ.get("NAVI_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "libnavi_b200.so")
 
 NAVI_OK, NAVI_E_ARG, NAVI_E_CUDA, NAVI_E_FORMAT, NAVI_E_TIMEOUT, NAVI_E_KV_FULL, NAVI_E_LAUNCH, NAVI_E_SHAPE, NAVI_E_NOMEM = range(9)
 NAVI_RNG_PCG, NAVI_RNG_PHILOX = 0, 1

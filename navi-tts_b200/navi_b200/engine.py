@@ -222,6 +222,18 @@ class Frame:
         a = np.array(buf[:n.value], dtype=np.float64)
         return a[0], a[1:].reshape(-1, 4)
 
+    def profile_all(self):
+        """Stamps of the last launch on every CTA (after set_profile(True, -1)):
+        (start_ns [G], array [G, phases, 4] in ns)."""
+        import numpy as np
+        G = self.grid_blocks()
+        cap = G * (4 * 4096 + 1)
+        buf = (ctypes.c_uint64 * cap)()
+        n = c_int(0)
+        check(lib().navi_frame_profile(self.h, buf, cap, byref(n)))
+        a = np.array(buf[:n.value], dtype=np.float64).reshape(G, -1)
+        return a[:, 0], a[:, 1:].reshape(G, -1, 4)
+
     def profile(self):
         """Per-phase durations (us) of the last launch on the traced CTA."""
         import numpy as np

@@ -16,20 +16,24 @@ NSLOT = 16
 
 def phase_chunks(cfg, b, G, n_past=512):
     """Chunk bytes per phase on CTA b of G (phases without a chunk dropped), program order:
-    norm weights ride with QKV / gate-up / heads; talker attention carries q/k norms, the
-    RoPE table and the split's K and V rows (16 positions per split)."""
+    norm weights ride with QKV / gate-up / heads; talker attention carries q/k norms and
+    its KV head's slice of the split's K and V rows (Frame::Impl::attn_plan's splits)."""
     tl, cp = cfg.talker, cfg.cp
     H, Q, KV, F, HD = tl.hidden, tl.n_head * tl.head_dim, tl.n_kv_head * tl.head_dim, tl.ff, tl.head_dim
     QKV = Q + 2 * KV
 
     def rows(R):
         return (R * (b + 1)) // G - (R * b) // G
-    chunk = max(16, -(-n_past // min(148, G)))
+    NKV = tl.n_kv_head
+    per_head = max(1, min(148, G // NKV))
+    split = min(per_head, max(1, -(-n_past // 8)))
+    chunk = max(1, -(-n_past // split))
     split = max(1, -(-n_past // chunk))
-    r0 = min(b * chunk, n_past)
+    sp = b % split
+    r0 = min(sp * chunk, n_past)
     r1 = min(r0 + chunk, n_past)
-    tattn = (2 * HD * 4 + HD * 2 + 2 * (r1 - r0) * KV * 2) if b < split else 0
-    cattn = (2 * HD * 4 + HD * 2) if b < tl.n_kv_head else 0
+    tattn = (2 * HD * 4 + 2 * (r1 - r0) * HD * 2) if b < NKV * split else 0
+    cattn = 2 * HD * 4 if b < NKV else 0
     qkv, o, gu, down = H * 4 + rows(QKV) * H * 2, rows(H) * Q * 2, H * 4 + 2 * rows(F) * H * 2, rows(H) * F * 2
     out = []
     for _ in range(tl.n_layer):
