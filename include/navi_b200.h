@@ -190,7 +190,7 @@ int navi_sample_logits(navi_device * dev, const float * d_logits, int vocab, con
 /* No counterpart in the reference.  navi_sample_logits without any device allocation, for
  * hosts that may not allocate after start-up (real-time audio threads, memory-reserved
  * serving processes): the working arrays and the result word live in one static device
- * array of the library (NAVI_SAMPLE_STATIC_MAX_VOCAB logits, about 545 KB).  Same
+ * array of the library (NAVI_SAMPLE_STATIC_MAX_VOCAB logits, about 515 KB).  Same
  * arguments and result as navi_sample_logits; vocab above the limit returns NAVI_E_ARG.
  * The first call on a device takes the array's address (set-up) and should precede any
  * stream capture there.  Calls on one device share the array: the library serialises them

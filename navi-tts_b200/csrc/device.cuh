@@ -80,6 +80,25 @@ __device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t 
                  "l"(src), "r"(bytes), "r"(smem_addr(bar))
                  : "memory");
 }
+// The same copy with an L2 eviction policy (from l2_policy) for the lines it reads.
+__device__ __forceinline__ void bulk_g2s_hint(void * dst, const void * src, uint32_t bytes, uint64_t * bar, uint64_t policy) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+                 : "memory");
+}
+// L2 policies: keep (evict_last) for data read again soon, stream (evict_first) for data
+// read once per frame, so the streamed bytes do not push out the kept ones.
+__device__ __forceinline__ uint64_t l2_policy_keep() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_stream() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
 __device__ __forceinline__ void bulk_prefetch_l2(const void * src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }

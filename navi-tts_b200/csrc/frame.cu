@@ -8,6 +8,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -79,6 +80,7 @@ struct Frame::Impl {
     bool pending = false;
     int grid = 0;
     uint32_t ring = 0, scratch_floats = 0, part_floats = 0, smem = 0;
+    int cp_keep_layers = 0;   // code-predictor layers held in L2 by cache policy
     uint64_t timeout_ns = 0;
     int eos = 0, suppress_from = 0;
     size_t ll_bytes = 0;
@@ -164,6 +166,7 @@ struct Frame::Impl {
         A.suppress_from = suppress_from;
         A.timeout_ns = timeout_ns;
         A.ring_bytes = ring;
+        A.cp_keep_layers = cp_keep_layers;
         A.scratch_floats = scratch_floats;
         A.part_floats = part_floats;
         A.prof = prof_on ? prof : nullptr;
@@ -238,7 +241,7 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     d.TV = tp.vocab; d.CV = cp.vocab; d.TL = tp.n_layer; d.CL = cp.n_layer;
     d.Q = Q; d.KV = KV; d.QKV = Q + 2 * KV; d.GROUP = tp.n_head / tp.n_kv_head;
     d.eps_t = tp.rms_eps; d.eps_c = cp.rms_eps;
-    if (d.NKV > dev.info().multiprocessors) fail("frame: more KV heads than CTAs", NAVI_E_SHAPE);
+    if (d.NKV * d.CL > dev.info().multiprocessors) fail("frame: code-predictor attention needs a CTA per (KV head, layer)", NAVI_E_SHAPE);
     I.eos = p.codec_eos_id;
     I.suppress_from = tp.vocab - 1024;   // HF suppress_tokens = range(vocab - 1024, vocab) minus EOS (frame.hip:760)
     I.timeout_ns = (opt.deadline_us ? opt.deadline_us : 200000ull) * 1000ull;
@@ -363,7 +366,7 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     // shared memory: everything but the ring is sized from the shapes; the ring takes the rest
     const int G = I.grid, Vmax = std::max(d.TV, d.CV);
     const uint32_t xin = 2u * std::max(d.H, std::max(d.Q, d.F));
-    const uint32_t samp = 4u * Vmax + (Vmax + 3) / 4 + 256 + 64;
+    const uint32_t samp = navi::dev::sample_scratch_floats(Vmax);
     // attention scratch: code predictor [q, k, v, scores, m/l, per-warp P.V]; talker split
     // [q, k, v, new K/V row, m/l, per-warp P.V, scores]; talker combine [m, l, sums]
     const uint32_t pvf = static_cast<uint32_t>(NCW * MAX_GROUP * d.HD);
@@ -385,6 +388,15 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
                                          static_cast<uint32_t>(2 * 8 * d.HD * 2 + 2 * d.HD * 4)});
     if (max_chunk > I.ring) fail("frame: a phase's weight slice does not fit the shared-memory ring", NAVI_E_SHAPE);
     I.smem = smem_layout(d, I.ring, I.scratch_floats, I.part_floats).total;
+    // The code predictor's weights are read 15 times a frame; as many whole layers as fit in
+    // about 70% of L2 are marked evict-last (NAVI_L2_KEEP_LAYERS overrides the count).
+    {
+        const double layer_bytes = 2.0 * (static_cast<double>(d.QKV) * d.H + static_cast<double>(d.H) * d.Q + 2.0 * d.F * d.H +
+                                          static_cast<double>(d.H) * d.F);
+        int keep = static_cast<int>(0.7 * static_cast<double>(dev.info().l2_bytes) / layer_bytes);
+        if (const char * env = std::getenv("NAVI_L2_KEEP_LAYERS")) keep = std::atoi(env);
+        I.cp_keep_layers = std::max(0, std::min(keep, d.CL));
+    }
     NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_frame), cudaFuncAttributeMaxDynamicSharedMemorySize, I.smem));
     int occ = 0;
     NAVI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, reinterpret_cast<const void *>(&k_frame), NTHR, I.smem));
@@ -510,7 +522,7 @@ int Frame::sample(const Device & dev, const float * d_logits, int vocab, const S
     c.pcg_seed = pcg_draw_seed(seed, frame_index, codebook);
     int * d_out = nullptr;
     NAVI_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&d_out), sizeof(int), dev.stream()));
-    const size_t smem = (4ull * vocab + (vocab + 3) / 4 + 256 + 64) * sizeof(float);
+    const size_t smem = static_cast<size_t>(navi::dev::sample_scratch_floats(vocab)) * sizeof(float);
     NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_sample), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(smem)));
     k_sample<<<1, NCT, smem, dev.stream()>>>(d_logits, vocab, c, d_out);

@@ -115,6 +115,9 @@ __device__ void producer(const Args & A, Sm & S) {
     uint64_t issued = 0;
     int chunk = 0;
     bool aborted = false;
+    // code-predictor layers below cp_keep_layers are read 15 times a frame: keep them in L2;
+    // everything else (talker weights, KV rows, heads) is read once and streams through
+    const uint64_t keep = l2_policy_keep(), stream = l2_policy_stream();
     for (int p = 0; p < A.nphase && !aborted; ++p) {
         const Phase ph = A.prog[p];
         Seg seg[MAX_SEG];
@@ -148,12 +151,14 @@ __device__ void producer(const Args & A, Sm & S) {
         S.meta_end[slot] = issued;
         mbar_arrive_expect_tx(&S.bars[slot], total);
         uint32_t dst = static_cast<uint32_t>(head % RB);
+        const bool kept = ph.op >= CQKV && ph.op <= CDOWN && ph.layer < A.cp_keep_layers;
+        const uint64_t pol = kept ? keep : stream;
         for (int i = 0; i < ns; ++i) {
             for (uint32_t r = 0; r < seg[i].rows; ++r) {
                 const char * src = static_cast<const char *>(seg[i].src) + static_cast<size_t>(r) * seg[i].stride;
                 for (uint32_t o = 0; o < seg[i].bytes; o += PIECE) {
                     const uint32_t n = min(PIECE, seg[i].bytes - o);
-                    bulk_g2s(S.ring + dst + o, src + o, n, &S.bars[slot]);
+                    bulk_g2s_hint(S.ring + dst + o, src + o, n, &S.bars[slot], pol);
                 }
                 dst += seg[i].bytes;
             }
@@ -378,18 +383,7 @@ __device__ __forceinline__ void row_f16_to_smem(const __half * row, int n, float
     for (int i = threadIdx.x; i < n; i += NCT) dst[i] = __half2float(row[i]);
 }
 
-__device__ SampleScratch sampler_scratch(Sm & S, int Vmax) {
-    SampleScratch sc;
-    float * base = S.scratch;
-    sc.s = base;
-    sc.e = base + Vmax;
-    sc.idx = reinterpret_cast<int *>(base + 2 * Vmax);
-    sc.ord = reinterpret_cast<int *>(base + 3 * Vmax);
-    sc.keep = reinterpret_cast<uint8_t *>(base + 4 * Vmax);
-    sc.hist = reinterpret_cast<unsigned *>(base + 4 * Vmax + (Vmax + 3) / 4);
-    sc.red = base + 4 * Vmax + (Vmax + 3) / 4 + 256;
-    return sc;
-}
+__device__ SampleScratch sampler_scratch(Sm & S, int Vmax) { return sampler_layout(S.scratch, Vmax); }
 
 __device__ SampleCfg sample_cfg(const Args & A, int codebook) {
     SampleCfg c{};
@@ -704,18 +698,18 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, const
 }
 
 // Code-predictor attention at positions pos..pos+ncol-1 (frame.hip:555-575: its own KV,
-// positions 0..15, reset every frame): KV head g = CTA g keeps that head's K/V for every
-// layer in shared memory across the frame's positions.
+// positions 0..15, reset every frame): the CTA cp_attn_cta(layer, g) keeps the K/V of KV
+// head g of that layer in shared memory across the frame's positions.
 __device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, const uint8_t * chunk_base, uint32_t tag, uint32_t ptag,
                              int p) {
     const Dims & d = A.d;
     constexpr int HD = KHD, GR = KGR;
     const int tid = threadIdx.x, ncol = ph.ncol, pos = ph.pos;
-    const int g = blockIdx.x;
-    if (g >= d.NKV) return true;
+    const int g = blockIdx.x - cp_attn_cta(d, ph.layer, 0);
+    if (g < 0 || g >= d.NKV) return true;
     const float * qn = reinterpret_cast<const float *>(chunk_base);
     const float * kn = qn + HD;
-    __half * kv = S.cpkv + static_cast<size_t>(ph.layer) * NCB * 2 * HD;   // [pos][K,V][HD]
+    __half * kv = S.cpkv;                   // [pos][K,V][HD] of (g, layer)
     float * qs = S.scratch;                 // [2][MAX_GROUP][HD]
     float * ks = qs + 2 * MAX_GROUP * HD;   // [2][HD]
     float * vs = ks + 2 * HD;               // [2][HD]
@@ -990,14 +984,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_frame(const __grid_constant__ Args 
 // A standalone launch of the device sampler on given logits (one CTA), for parity tests.
 __global__ void __launch_bounds__(NCT, 1) k_sample(const float * logits, int V, SampleCfg cfg, int * out) {
     extern __shared__ __align__(16) float sbuf[];
-    SampleScratch sc;
-    sc.s = sbuf;
-    sc.e = sbuf + V;
-    sc.idx = reinterpret_cast<int *>(sbuf + 2 * V);
-    sc.ord = reinterpret_cast<int *>(sbuf + 3 * V);
-    sc.keep = reinterpret_cast<uint8_t *>(sbuf + 4 * V);
-    sc.hist = reinterpret_cast<unsigned *>(sbuf + 4 * V + (V + 3) / 4);
-    sc.red = sbuf + 4 * V + (V + 3) / 4 + 256;
+    const SampleScratch sc = sampler_layout(sbuf, V);
     for (int i = threadIdx.x; i < V; i += NCT) sc.s[i] = logits[i];
     named_sync(BID, NCT);
     const int c = sample_cta<NCT>(V, cfg, sc, BID);

@@ -132,6 +132,7 @@ struct Args {
     int eos_id, suppress_from;
     uint64_t timeout_ns;
     uint32_t ring_bytes;
+    int cp_keep_layers;        // code-predictor layers whose weights the producer asks L2 to keep
     uint32_t scratch_floats;
     uint32_t part_floats;
     unsigned long long * prof;   // optional trace: [4 * nphase + 1] globaltimer stamps on CTA prof_cta,
@@ -144,9 +145,12 @@ struct SmemLayout {
     uint32_t bars, meta_off, meta_end, ctrl, codes, xres, hid, part, scratch, cpkv, ring, total;
 };
 
-// The code predictor's K/V for one KV head, kept in shared memory across the
-// positions of a frame: [layer][position][K, V][head_dim] f16.
-__host__ __device__ inline uint32_t cpkv_bytes(const Dims & d) { return static_cast<uint32_t>(d.CL) * NCB * 2 * d.HD * 2; }
+// The code predictor's K/V of one (KV head, layer), kept in shared memory across the
+// positions of a frame by the CTA that attends for it: [position][K, V][head_dim] f16.
+__host__ __device__ inline uint32_t cpkv_bytes(const Dims & d) { return static_cast<uint32_t>(NCB) * 2 * d.HD * 2; }
+
+// The CTA that runs code-predictor attention for KV head g of layer l.
+__host__ __device__ inline int cp_attn_cta(const Dims & d, int l, int g) { return l * d.NKV + g; }
 
 __host__ __device__ inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
@@ -264,7 +268,7 @@ __host__ __device__ inline int phase_segments(const Args & A, const ModelW & W, 
             return 4;
         }
         case CATTN:
-            if (b >= d.NKV) return 0;
+            if (b < cp_attn_cta(d, ph.layer, 0) || b >= cp_attn_cta(d, ph.layer, d.NKV)) return 0;
             s[0] = {L->qn, HD4};
             s[1] = {L->kn, HD4};
             return 2;

@@ -6,17 +6,17 @@
 // calls that may block in the driver or grow a memory pool, and a serving process that
 // reserves every device byte for weights and KV caches at start-up, where any later
 // allocation can fail under memory pressure.  This variant allocates nothing:
-// the result word and the working arrays (logits copy, exp values, candidate ids, value
-// order, keep flags) live in one file-scope device array of fixed size; only the 256-bin
-// histogram and the 64-word reduction buffer sit in static shared memory.
+// the result word and all of the sampler's working arrays (logits copy, exp values,
+// candidate ids and ranks, histograms, reduction words) live in
+// one file-scope device array of fixed size.
 //
 // Set-up: the first call on a device, with that device current, takes the array's
 // device address with cudaGetSymbolAddress (which may load the module) and caches it, so
 // the first call per device should come before any stream capture on that device.
 //
 // Zeroing: no part of the scratch has to start at zero.  The kernel writes the logits
-// copy and every other working word before it reads it, clears the histogram before each
-// radix pass, and writes the result word unconditionally.
+// copy and every other working word before it reads it, clears the histograms at the start
+// of each call, and writes the result word unconditionally.
 //
 // Sharing: all calls on one device use the same array, so two calls in flight at once
 // would race on it.  This file holds a per-device host lock from launch until the result
@@ -38,23 +38,13 @@ using namespace navi::dev;
 
 constexpr size_t SAMPLE_STATIC_OUT_BYTES = 256;   // result word, padded to keep the arrays 256-byte aligned
 constexpr size_t SAMPLE_STATIC_BYTES =
-    SAMPLE_STATIC_OUT_BYTES + static_cast<size_t>(navi::qwen3tts::SAMPLE_STATIC_MAX_VOCAB) * (4 * sizeof(float) + 1);
+    SAMPLE_STATIC_OUT_BYTES + static_cast<size_t>(sample_scratch_floats(navi::qwen3tts::SAMPLE_STATIC_MAX_VOCAB)) * sizeof(float);
 
 static __device__ __align__(256) unsigned char g_sample_scratch[SAMPLE_STATIC_BYTES];
 
 // One CTA of NCT threads; the arrays are laid out for this call's vocabulary V.
 __global__ void __launch_bounds__(NCT, 1) k_sample_static(const float * logits, int V, SampleCfg cfg, unsigned char * scratch) {
-    __shared__ unsigned hist[256];
-    __shared__ __align__(16) float red[64];
-    float * base = reinterpret_cast<float *>(scratch + SAMPLE_STATIC_OUT_BYTES);
-    SampleScratch sc;
-    sc.s = base;
-    sc.e = base + V;
-    sc.idx = reinterpret_cast<int *>(base + 2 * static_cast<size_t>(V));
-    sc.ord = reinterpret_cast<int *>(base + 3 * static_cast<size_t>(V));
-    sc.keep = reinterpret_cast<uint8_t *>(base + 4 * static_cast<size_t>(V));
-    sc.hist = hist;
-    sc.red = red;
+    const SampleScratch sc = sampler_layout(reinterpret_cast<float *>(scratch + SAMPLE_STATIC_OUT_BYTES), V);
     for (int i = threadIdx.x; i < V; i += NCT) sc.s[i] = logits[i];
     named_sync(BID, NCT);
     const int c = sample_cta<NCT>(V, cfg, sc, BID);

@@ -40,14 +40,29 @@ struct SampleCfg {
 };
 
 struct SampleScratch {
-    float * s;        // [V] in: logits; out: modified, tempered values
-    float * e;        // [V]
-    int * idx;        // [V] candidate ids in index order
-    int * ord;        // [V] candidates in value order (top-p)
-    uint8_t * keep;   // [V]
-    unsigned * hist;  // [256]
+    float * s;        // [V] in: logits; then the modified, tempered values; then (top-p) keep flags
+    float * e;        // [V] e^(v - max) of the candidates, 0 elsewhere
+    int * idx;        // [V] candidate ids (nonzero e) in index order
+    int * ord;        // [V] compaction counts; then (top-p) candidate positions by rank
+    unsigned * hist;  // [2][256] radix histograms
     float * red;      // [64]
 };
+
+// Floats of shared or global scratch the sampler takes for V logits (the layout of
+// sampler_layout below).
+__host__ __device__ constexpr uint32_t sample_scratch_floats(int V) { return 4u * V + 512 + 64; }
+
+// The scratch arrays at base (16-byte aligned).
+__host__ __device__ inline SampleScratch sampler_layout(float * base, int V) {
+    SampleScratch sc;
+    sc.s = base;
+    sc.e = base + V;
+    sc.idx = reinterpret_cast<int *>(base + 2 * V);
+    sc.ord = reinterpret_cast<int *>(base + 3 * V);
+    sc.hist = reinterpret_cast<unsigned *>(base + 4 * V);
+    sc.red = base + 4 * V + 512;
+    return sc;
+}
 
 // exp(x), exactly specified: Cody-Waite reduction x = n*ln2 + r (fdlibm hi/lo split
 // of ln2), a degree-7 Taylor polynomial for e^r by Horner's rule with fused
@@ -125,15 +140,35 @@ __device__ __forceinline__ float key_float(uint32_t k) {
 
 // Samples from S.s[0..V) (the raw logits on entry). Must be called by all NT threads
 // (NT a multiple of 32, >= 256; barrier id `bid`); every thread returns the chosen id.
+//
+// Work plan (the result is the host oracle's, bit for bit):
+//  1. modifications and temperature, block max (1 barrier);
+//  2. k-th largest key by 8-bit radix passes, top byte first, one warp resolving the
+//     digit from the histogram (2 barriers per pass). The passes
+//     stop early once the bin holding the k-th key holds exactly the keys still needed:
+//     then every key of that bin is a candidate and a threshold with the low bits zero
+//     selects the same set (not used when that threshold would be +0, where -0 compares
+//     equal);
+//  3. e = exp(v - max) over candidates, compacted in index order by ballots and one
+//     warp-0 scan (3 barriers);
+//  4. the normaliser in the reference's 256-thread order, 1 barrier;
+//  5. top-p: candidate ranks in parallel; the sequential sums (top-p cut, renormaliser,
+//     draw) in warp 0, values passed lane to lane by shuffles.
 template <int NT>
 __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, int bid) {
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    constexpr int NW = NT / 32;
     static_assert(NT % 32 == 0 && NT >= 256 && NT <= 1024, "sampler thread count");
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     float * s = S.s;
+    float * e = S.e;
+    int * ci = S.idx;
     float * red = S.red;
     int * ired = reinterpret_cast<int *>(S.red);
-    // 1. codebook-0 modifications, temperature
+    unsigned * hist = S.hist;
+    const unsigned lt_mask = (1u << lane) - 1u;
+    // 1. codebook-0 modifications, temperature, max; histograms cleared for step 2
     const bool greedy = c.temperature <= 0.f;
+    for (int i = tid; i < 512; i += NT) hist[i] = 0u;
     float lmax = -INFINITY;
     for (int i = tid; i < V; i += NT) {
         float v = s[i];
@@ -151,154 +186,221 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
     named_sync(bid, NT);
     float mx = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < NT / 32; ++w) mx = fmaxf(mx, red[w]);
-    named_sync(bid, NT);
+    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, red[w]);
     if (greedy) {
         // lowest index holding the maximum (index 0 when every value is -inf)
         int best = V;
         for (int i = tid; i < V; i += NT) if (s[i] == mx) { best = i; break; }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
-        if (lane == 0) ired[wid] = best;
+        if (lane == 0) ired[32 + wid] = best;
         named_sync(bid, NT);
         int b = V;
 #pragma unroll
-        for (int w = 0; w < NT / 32; ++w) b = min(b, ired[w]);
+        for (int w = 0; w < NW; ++w) b = min(b, ired[32 + w]);
         named_sync(bid, NT);
         return b >= V ? 0 : b;
     }
-    // 2. exact k-th largest key (4 passes of 8 bits), threshold
+    // 2. k-th largest key, top byte first
     float threshold = -INFINITY;
     if (c.top_k > 0 && c.top_k < V) {
         uint32_t prefix = 0, mask = 0;
         int need = c.top_k;
         for (int pass = 3; pass >= 0; --pass) {
             const int shift = pass * 8;
-            if (tid < 256) S.hist[tid] = 0;
-            named_sync(bid, NT);
+            unsigned * h = hist + (pass & 1) * 256;
             for (int i = tid; i < V; i += NT) {
                 const uint32_t key = float_key(s[i]);
-                if ((key & mask) == prefix) atomicAdd(&S.hist[(key >> shift) & 0xFFu], 1u);
+                if ((key & mask) == prefix) atomicAdd(&h[(key >> shift) & 0xFFu], 1u);
             }
             named_sync(bid, NT);
-            // threads 0..255: t owns digit 255 - t; inclusive scan of counts from the top digit down
-            int cnt = 0, incl = 0;
-            if (tid < 256) {
-                cnt = static_cast<int>(S.hist[255 - tid]);
-                incl = cnt;
+            const int slot = 16 + 3 * (3 - pass);
+            if (wid == 0) {
+                // lane l holds digits 255 - 8l - k (k < 8), counted from the top digit down
+                int cnt[8], tot = 0;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) { cnt[k] = static_cast<int>(h[255 - 8 * lane - k]); tot += cnt[k]; }
+                int incl = tot;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
                     const int v = __shfl_up_sync(0xffffffffu, incl, o);
                     if (lane >= o) incl += v;
                 }
-                if (lane == 31) ired[wid] = incl;
+                const int above = incl - tot;
+                if (above < need && incl >= need) {
+                    int a = above;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        if (a + cnt[k] >= need) {
+                            ired[slot] = 255 - 8 * lane - k;
+                            ired[slot + 1] = need - a;
+                            ired[slot + 2] = cnt[k];
+                            break;
+                        }
+                        a += cnt[k];
+                    }
+                }
+                // this buffer is used again two passes on
+#pragma unroll
+                for (int k = 0; k < 8; ++k) h[8 * lane + k] = 0u;
             }
             named_sync(bid, NT);
-            if (tid < 256) {
-                int above = incl - cnt;
-                for (int w = 0; w < wid; ++w) above += ired[w];
-                if (above < need && above + cnt >= need) { ired[16] = 255 - tid; ired[17] = need - above; }
-            }
-            named_sync(bid, NT);
-            need = ired[17];
-            prefix |= static_cast<uint32_t>(ired[16]) << shift;
+            need = ired[slot + 1];
+            prefix |= static_cast<uint32_t>(ired[slot]) << shift;
             mask |= 0xFFu << shift;
-            named_sync(bid, NT);
+            if (ired[slot + 2] == need && key_float(prefix) != 0.0f) break;
         }
         threshold = key_float(prefix);
     }
-    // 3. e_i over candidates
-    for (int i = tid; i < V; i += NT) S.e[i] = (s[i] >= threshold) ? exp_spec(__fsub_rn(s[i], mx)) : 0.0f;
+    // 3. e over candidates; nonzero e compacted in index order
+    const int R = (V + NT - 1) / NT;
+    int * cnt = S.ord;   // [R][NW] nonzero counts per (round, warp), i.e. per 32 consecutive ids
+    for (int k = 0; k < R; ++k) {
+        const int i = k * NT + tid;
+        float ev = 0.f;
+        if (i < V) {
+            const float v = s[i];
+            if (v >= threshold) ev = exp_spec(__fsub_rn(v, mx));
+            e[i] = ev;
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, ev != 0.f);
+        if (lane == 0) cnt[k * NW + wid] = __popc(m);
+    }
+    named_sync(bid, NT);
+    if (wid == 0) {
+        int run = 0;
+        for (int b0 = 0; b0 < R * NW; b0 += 32) {
+            const int x = b0 + lane < R * NW ? cnt[b0 + lane] : 0;
+            int incl = x;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            if (b0 + lane < R * NW) cnt[b0 + lane] = run + incl - x;
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) ired[61] = run;
+    }
+    named_sync(bid, NT);
+    for (int k = 0; k < R; ++k) {
+        const int i = k * NT + tid;
+        const bool nz = i < V && e[i] != 0.f;
+        const unsigned m = __ballot_sync(0xffffffffu, nz);
+        if (nz) ci[cnt[k * NW + wid] + __popc(m & lt_mask)] = i;
+    }
+    const int n = ired[61];
     named_sync(bid, NT);
     // 4. normaliser in the reference's 256-thread block_sum order
     if (tid < 256) {
         float acc = 0.f;
-        for (int i = tid; i < V; i += 256) acc = __fadd_rn(acc, S.e[i]);
+        for (int i = tid; i < V; i += 256) acc = __fadd_rn(acc, e[i]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
         if (lane == 0) red[32 + wid] = acc;
     }
     named_sync(bid, NT);
-    if (wid == 0) {
-        float v = lane < 8 ? red[32 + lane] : 0.f;
+    float ssum = lane < 8 ? red[32 + lane] : 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (lane == 0) red[48] = v;
-    }
-    named_sync(bid, NT);
-    const float ssum = red[48];
+    for (int o = 16; o > 0; o >>= 1) ssum = __fadd_rn(ssum, __shfl_xor_sync(0xffffffffu, ssum, o));
     const float inv = __fdiv_rn(1.0f, ssum);
-    // 5. compact the nonzero e_i in index order
-    int total = 0;
-    for (int base = 0; base < V; base += NT) {
-        const int i = base + tid;
-        const bool nz = i < V && S.e[i] != 0.f;
-        const unsigned m = __ballot_sync(0xffffffffu, nz);
-        if (lane == 0) ired[wid] = __popc(m);
-        named_sync(bid, NT);
-        int before = total;
-        for (int w = 0; w < wid; ++w) before += ired[w];
-        if (nz) S.idx[before + __popc(m & ((1u << lane) - 1u))] = i;
-        int t = 0;
-#pragma unroll
-        for (int w = 0; w < NT / 32; ++w) t += ired[w];
-        total += t;
-        named_sync(bid, NT);
-    }
-    const int n = total;
-    const float u = draw_uniform(c);
     const bool nucleus = c.top_p > 0.f && c.top_p < 1.f;
+    int * ord = S.ord;   // top-p: candidate position of each rank
     if (nucleus) {
-        // rank of each candidate in (value desc, index asc) order
-        for (int j = tid; j < n; j += NT) {
-            const int ij = S.idx[j];
-            const float vj = s[ij];
+        // rank of candidate j in (value desc, index asc) order; positions are in index order.
+        // Each warp passes 32 candidate values at a time round its lanes.
+        for (int j0 = 0; j0 < n; j0 += NT) {
+            const int j = j0 + tid;
+            const float vj = j < n ? s[ci[j]] : 0.f;
             int r = 0;
-            for (int m = 0; m < n; ++m) {
-                const int im = S.idx[m];
-                const float vm = s[im];
-                r += (vm > vj || (vm == vj && im < ij)) ? 1 : 0;
+            for (int m0 = 0; m0 < n; m0 += 32) {
+                const float vl = m0 + lane < n ? s[ci[m0 + lane]] : 0.f;
+                const int mq = min(32, n - m0);
+#pragma unroll 1
+                for (int q = 0; q < mq; ++q) {
+                    const float vm = __shfl_sync(0xffffffffu, vl, q);
+                    r += (vm > vj || (vm == vj && m0 + q < j)) ? 1 : 0;
+                }
             }
-            S.ord[r] = ij;
+            if (j < n) ord[r] = j;
         }
-        for (int i = tid; i < V; i += NT) S.keep[i] = 0;
         named_sync(bid, NT);
     }
-    if (tid == 0) {
+    if (wid == 0) {
+        // Sequential sums in warp 0: every lane runs the same chain on values the lanes load
+        // 32 at a time and pass round by shuffles, so the loads never sit on the chain.
+        const float u = draw_uniform(c);
         int chosen;
         if (nucleus) {
+            // the shortest prefix by rank whose cumulative probability reaches top_p: ranks <= R
             float cum = 0.f;
-            for (int r = 0; r < n; ++r) {
-                const int i = S.ord[r];
-                cum = __fadd_rn(cum, __fmul_rn(S.e[i], inv));
-                S.keep[i] = 1;
-                if (cum >= c.top_p) break;
+            int R = n - 1;
+            bool done = false;
+            for (int r0 = 0; r0 < n && !done; r0 += 32) {
+                const float p = r0 + lane < n ? __fmul_rn(e[ci[ord[r0 + lane]]], inv) : 0.f;
+                const int mq = min(32, n - r0);
+#pragma unroll 1
+                for (int q = 0; q < mq && !done; ++q) {
+                    cum = __fadd_rn(cum, __shfl_sync(0xffffffffu, p, q));
+                    if (cum >= c.top_p) { R = r0 + q; done = true; }
+                }
             }
+            // keep flags by candidate position (the values in s are no longer needed)
+            float * kept = s;
+            for (int j = lane; j < n; j += 32) kept[j] = 0.f;
+            __syncwarp();
+            for (int r = lane; r <= R; r += 32) kept[ord[r]] = 1.f;
+            __syncwarp();
+            // renormalise over the kept candidates, in index order; adding the 0 of a dropped
+            // candidate leaves a sum unchanged
             float ksum = 0.f;
             int last = V - 1;
-            for (int j = 0; j < n; ++j) {
-                const int i = S.idx[j];
-                if (S.keep[i]) { ksum = __fadd_rn(ksum, S.e[i]); last = i; }
+            for (int j0 = 0; j0 < n; j0 += 32) {
+                const int j = j0 + lane;
+                const bool kp = j < n && kept[j] != 0.f;
+                const int ii = j < n ? ci[j] : 0;
+                const float ev = kp ? e[ii] : 0.f;
+                const unsigned km = __ballot_sync(0xffffffffu, kp);
+                const int mq = min(32, n - j0);
+#pragma unroll 1
+                for (int q = 0; q < mq; ++q) ksum = __fadd_rn(ksum, __shfl_sync(0xffffffffu, ev, q));
+                if (km) last = __shfl_sync(0xffffffffu, ii, 31 - __clz(km));
             }
             const float kinv = __fdiv_rn(1.0f, ksum);
             chosen = last;
             float c2 = 0.f;
-            for (int j = 0; j < n; ++j) {
-                const int i = S.idx[j];
-                if (!S.keep[i]) continue;
-                c2 = __fadd_rn(c2, __fmul_rn(S.e[i], kinv));
-                if (c2 >= u) { chosen = i; break; }
+            done = false;
+            for (int j0 = 0; j0 < n && !done; j0 += 32) {
+                const int j = j0 + lane;
+                const bool kp = j < n && kept[j] != 0.f;
+                const int ii = j < n ? ci[j] : 0;
+                const float pv = kp ? __fmul_rn(e[ii], kinv) : 0.f;
+                const unsigned km = __ballot_sync(0xffffffffu, kp);
+                const int mq = min(32, n - j0);
+#pragma unroll 1
+                for (int q = 0; q < mq && !done; ++q) {
+                    if (!((km >> q) & 1u)) continue;
+                    c2 = __fadd_rn(c2, __shfl_sync(0xffffffffu, pv, q));
+                    if (c2 >= u) { chosen = __shfl_sync(0xffffffffu, ii, q); done = true; }
+                }
             }
         } else {
             chosen = V - 1;
             float cum = 0.f;
-            for (int j = 0; j < n; ++j) {
-                const int i = S.idx[j];
-                cum = __fadd_rn(cum, __fmul_rn(S.e[i], inv));
-                if (cum >= u) { chosen = i; break; }
+            bool done = false;
+            for (int j0 = 0; j0 < n && !done; j0 += 32) {
+                const int j = j0 + lane;
+                const int ii = j < n ? ci[j] : 0;
+                const float p = j < n ? __fmul_rn(e[ii], inv) : 0.f;
+                const int mq = min(32, n - j0);
+#pragma unroll 1
+                for (int q = 0; q < mq && !done; ++q) {
+                    cum = __fadd_rn(cum, __shfl_sync(0xffffffffu, p, q));
+                    if (cum >= u) { chosen = __shfl_sync(0xffffffffu, ii, q); done = true; }
+                }
             }
         }
-        ired[60] = chosen;
+        if (lane == 0) ired[60] = chosen;
     }
     named_sync(bid, NT);
     const int chosen = ired[60];

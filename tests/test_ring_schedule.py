@@ -33,15 +33,15 @@ def phase_chunks(cfg, b, G, n_past=512):
     r0 = min(sp * chunk, n_past)
     r1 = min(r0 + chunk, n_past)
     tattn = (2 * HD * 4 + 2 * (r1 - r0) * HD * 2) if b < NKV * split else 0
-    cattn = 2 * HD * 4 if b < NKV else 0
+    cattn_layers = {l for l in range(cp.n_layer) if l * NKV <= b < (l + 1) * NKV}   # CTA l * NKV + g
     qkv, o, gu, down = H * 4 + rows(QKV) * H * 2, rows(H) * Q * 2, H * 4 + 2 * rows(F) * H * 2, rows(H) * F * 2
     out = []
     for _ in range(tl.n_layer):
         out += [qkv, tattn, o, gu, down]
     out.append(H * 4 + rows(tl.vocab) * H * 2)
     for _pass in range(15):
-        for _ in range(cp.n_layer):
-            out += [qkv, cattn, o, gu, down]
+        for l in range(cp.n_layer):
+            out += [qkv, 2 * HD * 4 if l in cattn_layers else 0, o, gu, down]
         out.append(H * 4 + rows(cp.vocab) * H * 2)
     return [c for c in out if c > 0]
 
