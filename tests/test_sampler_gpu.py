@@ -74,3 +74,27 @@ def test_codebook0_draw_with_modifications(dev, fi, rs):
         if fi < 2:
             assert got != eos
         assert got < V - 1024 or got == eos
+
+
+def test_device_draws_match_golden_fixture(dev):
+    """The device sampler returns the committed ids of tests/golden/sampler_golden.json (the
+    sampler specification's draws, fixed when the fixture was written)."""
+    import json
+    import os
+    import sys
+    golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    sys.path.insert(0, golden)
+    from make_golden import case_logits, case_seen
+    with open(os.path.join(golden, "sampler_golden.json")) as f:
+        cases = json.load(f)["cases"]
+    for c in cases:
+        V, cb = c["V"], c["codebook"]
+        s = engine.Sampling(temperature=c["temperature"], top_k=c["top_k"], top_p=c["top_p"], cp_temperature=c["temperature"],
+                            cp_top_k=c["top_k"], cp_top_p=c["top_p"], rng=c["rng"])
+        d = torch.from_numpy(case_logits(c)).cuda()
+        if cb == 0:
+            sd = torch.from_numpy(case_seen(c)).cuda()
+            got = engine.sample_logits(dev, d.data_ptr(), V, s, c["seed"], c["frame_index"], 0, V - 1024, V - 1022, sd.data_ptr())
+        else:
+            got = engine.sample_logits(dev, d.data_ptr(), V, s, c["seed"], c["frame_index"], cb)
+        assert got == c["id"], c
