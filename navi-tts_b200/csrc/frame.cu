@@ -368,12 +368,12 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     const uint32_t xin = 2u * std::max(d.H, std::max(d.Q, d.F));
     const uint32_t samp = navi::dev::sample_scratch_floats(Vmax);
     // attention scratch: code predictor [q, k, v, scores, m/l, per-warp P.V]; talker split
-    // [q, k, v, new K/V row, m/l, per-warp P.V, scores]; talker combine [m, l, sums]
+    // [q, k, v, new K/V row, m/l, per-warp P.V, scores]; talker combine [splits][m, l, acc]
     const uint32_t pvf = static_cast<uint32_t>(NCW * MAX_GROUP * d.HD);
     const uint32_t att = std::max({2u * MAX_GROUP * d.HD + 4u * d.HD + 2u * MAX_GROUP * NCB + 4u * MAX_GROUP + pvf,
                                    static_cast<uint32_t>(MAX_GROUP * d.HD + 3 * d.HD + 2 * MAX_GROUP) + pvf +
                                        static_cast<uint32_t>(MAX_GROUP * (MAX_ATTN_CHUNK + 1)),
-                                   static_cast<uint32_t>(2 * MAX_SPLIT + NCT)});
+                                   static_cast<uint32_t>(std::min(MAX_SPLIT, I.grid / d.NKV) * (d.HD + 2))});
     I.scratch_floats = std::max(xin, std::max(samp, att));
     const int max_nr = std::max({cdiv(d.QKV, G), cdiv(d.H, G), cdiv(d.F, G), cdiv(d.TV, G), cdiv(d.CV, G)});
     I.part_floats = static_cast<uint32_t>(NCW * 4 * max_nr);

@@ -17,7 +17,8 @@ static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block outgrows its shared-mem
 struct Sm {
     uint64_t * bars;
     uint64_t * meta_end;
-    uint32_t * meta_off;
+    uint32_t * meta_off;     // physical offset of the chunk's logical byte 0
+    uint32_t * meta_split;   // logical offset where the chunk continues at the ring's start
     Ctrl * ctrl;
     int * codes;
     float * xres;
@@ -33,6 +34,7 @@ __device__ __forceinline__ Sm carve(char * base, const SmemLayout & L) {
     s.bars = reinterpret_cast<uint64_t *>(base + L.bars);
     s.meta_end = reinterpret_cast<uint64_t *>(base + L.meta_end);
     s.meta_off = reinterpret_cast<uint32_t *>(base + L.meta_off);
+    s.meta_split = reinterpret_cast<uint32_t *>(base + L.meta_split);
     s.ctrl = reinterpret_cast<Ctrl *>(base + L.ctrl);
     s.codes = reinterpret_cast<int *>(base + L.codes);
     s.xres = reinterpret_cast<float *>(base + L.xres);
@@ -53,21 +55,6 @@ __device__ __noinline__ void raise_abort(const Args & A, int phase) {
     st_relaxed_u32(&A.w.ctl[3], blockIdx.x);
     __threadfence();
     st_relaxed_u32(&A.w.ctl[2], A.tag_base);
-}
-
-// Polls one exchange word until it carries `tag`. False when the launch is aborting.
-__device__ __forceinline__ bool ll_get(const uint64_t * p, uint32_t tag, float & out, const Args & A, Sm & S, int phase) {
-    uint64_t w = ll_load(p);
-    if (static_cast<uint32_t>(w >> 32) == tag) { out = __uint_as_float(static_cast<uint32_t>(w)); return true; }
-    const uint64_t t0 = globaltimer();
-    uint32_t spins = 0;
-    for (;;) {
-        w = ll_load(p);
-        if (static_cast<uint32_t>(w >> 32) == tag) { out = __uint_as_float(static_cast<uint32_t>(w)); return true; }
-        ++spins;
-        if ((spins & 3u) == 0 && globaltimer() - t0 > A.timeout_ns) { raise_abort(A, phase); return false; }
-        if ((spins & 31u) == 0 && (S.ctrl->abort || launch_aborted(A))) return false;
-    }
 }
 
 // Consumer barrier that also decides, uniformly, whether any consumer thread failed.
@@ -106,6 +93,13 @@ __device__ __forceinline__ void release_chunk(Sm & S, int chunk) {
     }
 }
 
+// Address of logical byte x of ring chunk `chunk` (see the producer's cut).
+__device__ __forceinline__ const uint8_t * chunk_at(const Sm & S, int chunk, uint32_t x) {
+    const int slot = chunk % NSLOT;
+    const uint32_t cut = S.meta_split[slot];
+    return S.ring + (x < cut ? S.meta_off[slot] + x : x - cut);
+}
+
 __device__ void producer(const Args & A, Sm & S) {
     if ((threadIdx.x & 31) != 0) return;
     const ModelW & W = *A.mw;
@@ -126,13 +120,21 @@ __device__ void producer(const Args & A, Sm & S) {
         if (ns == 0) continue;
         uint32_t total = 0;
         for (int i = 0; i < ns; ++i) total += seg[i].bytes * seg[i].rows;
-        // The chunk takes virtual bytes [head, head + total) of the ring stream, contiguous in
-        // shared memory (a chunk that would straddle the end starts the next lap). It may
-        // only overwrite bytes whose data chunk the consumers have released; skipped tail
-        // bytes hold no data, hence the min() with the end of the issued data.
-        uint64_t head = issued;
-        if (head % RB + total > RB) head += RB - head % RB;
-        const uint64_t need = head + total > RB ? min(head + total - RB, issued) : 0;
+        // The chunk takes the next bytes of the ring stream. When it does not fit before the
+        // ring's end it is cut once (chunk_split): its first part fills the end, the rest
+        // continues at the ring's start, and the bytes between the cut point's offset and the
+        // end stay unused. It may only overwrite bytes whose chunk the consumers have
+        // released; unused bytes hold no data, hence the min() with the end of the issued data.
+        const uint64_t head = issued;
+        const uint32_t pos = static_cast<uint32_t>(head % RB);
+        uint32_t cut = total;
+        uint64_t end = head + total;
+        if (pos + total > RB) {
+            cut = chunk_split(seg, ns, RB - pos);
+            if (total - cut > pos) cut = 0;   // the rest would reach the first part: start over
+            end = head + (RB - pos) + (total - cut);
+        }
+        const uint64_t need = end > RB ? min(end - RB, issued) : 0;
         uint64_t t0 = 0;
         uint32_t spins = 0;
         while (S.ctrl->released < need || chunk - S.ctrl->consumed >= NSLOT) {
@@ -146,21 +148,27 @@ __device__ void producer(const Args & A, Sm & S) {
         }
         if (aborted) break;
         const int slot = chunk % NSLOT;
-        S.meta_off[slot] = static_cast<uint32_t>(head % RB);
-        issued = head + total;
+        S.meta_off[slot] = cut > 0 ? pos : 0u;
+        S.meta_split[slot] = cut;
+        issued = end;
         S.meta_end[slot] = issued;
         mbar_arrive_expect_tx(&S.bars[slot], total);
-        uint32_t dst = static_cast<uint32_t>(head % RB);
         const bool kept = ph.op >= CQKV && ph.op <= CDOWN && ph.layer < A.cp_keep_layers;
         const uint64_t pol = kept ? keep : stream;
+        uint32_t lo = 0;   // logical offset of the next byte
         for (int i = 0; i < ns; ++i) {
             for (uint32_t r = 0; r < seg[i].rows; ++r) {
                 const char * src = static_cast<const char *>(seg[i].src) + static_cast<size_t>(r) * seg[i].stride;
-                for (uint32_t o = 0; o < seg[i].bytes; o += PIECE) {
-                    const uint32_t n = min(PIECE, seg[i].bytes - o);
-                    bulk_g2s_hint(S.ring + dst + o, src + o, n, &S.bars[slot], pol);
+                for (uint32_t o = 0; o < seg[i].bytes;) {
+                    // up to PIECE bytes, not across the cut
+                    const uint32_t x = lo + o;
+                    uint32_t n = min(PIECE, seg[i].bytes - o);
+                    if (x < cut) n = min(n, cut - x);
+                    const uint32_t phys = x < cut ? S.meta_off[slot] + x : x - cut;
+                    bulk_g2s_hint(S.ring + phys, src + o, n, &S.bars[slot], pol);
+                    o += n;
                 }
-                dst += seg[i].bytes;
+                lo += seg[i].bytes;
             }
         }
         ++chunk;
@@ -185,21 +193,29 @@ __device__ void producer(const Args & A, Sm & S) {
 __device__ __forceinline__ uint32_t tag_of(uint64_t w) { return static_cast<uint32_t>(w >> 32); }
 __device__ __forceinline__ float val_of(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
 
-// Fetches exchange words [0, n) (n even) carrying `tag` into dst[0, n): thread t takes the
-// pairs at 2t + 2*NCT*k, issues up to 4 pair loads at once, then re-issues every stale pair
-// together until all carry the tag (one L2 round trip per poll, not one per stale pair).
-// Returns this thread's success (the caller decides with a barrier). ll_each() visits the
-// same elements in the same thread, so a transform needs no barrier in between.
-__device__ __noinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag, float * dst, const Args & A, Ctrl * ctrl, int phase) {
+// Fetches exchange words carrying `tag` into dst: `rows` runs of `len` words (len even),
+// run r at src + r * stride (stride even), packed back to back in dst. Thread t takes the
+// word pairs 2t + 2*NCT*k of the packed order, issues up to 4 pair loads at once, then
+// re-issues every stale pair together until all carry the tag (one L2 round trip per poll,
+// not one per stale pair). Returns this thread's success (the caller decides with a
+// barrier). ll_each() visits the same elements of a single run in the same thread, so a
+// transform needs no barrier in between.
+__device__ __noinline__ bool ll_fetch_rows(const uint64_t * src, int rows, int len, int stride, uint32_t tag, float * dst, const Args & A,
+                                           Ctrl * ctrl, int phase) {
     constexpr int MAXK = 4;
+    const int n = rows * len;
     for (int base = 2 * threadIdx.x; base < n; base += 2 * NCT * MAXK) {
         uint64_t w[MAXK][2];
+        const uint64_t * at[MAXK];
         unsigned pend = 0;
 #pragma unroll
         for (int k = 0; k < MAXK; ++k) {
             const int i = base + 2 * NCT * k;
+            at[k] = nullptr;
             if (i < n) {
-                ll_load2(src + i, w[k][0], w[k][1]);
+                const int r = rows == 1 ? 0 : i / len;
+                at[k] = src + static_cast<size_t>(r) * stride + (i - r * len);
+                ll_load2(at[k], w[k][0], w[k][1]);
                 pend |= 1u << k;
             }
         }
@@ -219,13 +235,18 @@ __device__ __noinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag,
             if (t0 == 0) t0 = globaltimer();
 #pragma unroll
             for (int k = 0; k < MAXK; ++k)
-                if ((pend >> k) & 1u) ll_load2(src + base + 2 * NCT * k, w[k][0], w[k][1]);
+                if ((pend >> k) & 1u) ll_load2(at[k], w[k][0], w[k][1]);
             ++spins;
             if ((spins & 3u) == 0 && globaltimer() - t0 > A.timeout_ns) { raise_abort(A, phase); return false; }
             if ((spins & 31u) == 0 && (ctrl->abort || launch_aborted(A))) return false;
         }
     }
     return true;
+}
+
+// Exchange words [0, n) (n even) into dst[0, n): one run of ll_fetch_rows.
+__device__ __forceinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag, float * dst, const Args & A, Ctrl * ctrl, int phase) {
+    return ll_fetch_rows(src, 1, n, 0, tag, dst, A, ctrl, phase);
 }
 
 // Visits i over the elements ll_fetch(n) gave this thread.
@@ -263,8 +284,8 @@ __device__ __forceinline__ bool wait_chunk_local(const Args & A, Sm & S, int chu
 // broadcasts. Per-warp sums are folded over j with shuffles, written to
 // part[warp][value][row], and after a consumer barrier thread (value, row) adds the NCW warp
 // sums in warp order and calls epi(unit, column, y[, y_pair]).
-template <int NC, bool PAIR, class Epi>
-__device__ __forceinline__ void gemv_slice(const __half * Ws, int nr, int K, const float * xin, int xstride, float * part, Epi && epi) {
+template <int NC, bool PAIR, class At, class Epi>
+__device__ __forceinline__ void gemv_slice(At && at, uint32_t woff, int nr, int K, const float * xin, int xstride, float * part, Epi && epi) {
     constexpr int NV = NC * (PAIR ? 2 : 1);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nk = K >> 3;
@@ -275,8 +296,11 @@ __device__ __forceinline__ void gemv_slice(const __half * Ws, int nr, int K, con
     const int J = 1 << lj, lr = 5 - lj, R2 = 1 << lr;
     const int k0 = (nk * warp) / NCW, k1 = (nk * (warp + 1)) / NCW;   // NCW is a constant: no division
     const size_t cs = static_cast<size_t>(J) * nr * 8;                 // halves between a lane's chunks
-    const size_t up = static_cast<size_t>(nk) * nr * 8;                // gate -> up slice
     const int j = lane >> lr;
+    // this warp's K range of the slice (and of the up slice after it), each contiguous in the ring
+    const uint32_t kb = static_cast<uint32_t>(nr) * 16u;
+    const __half * wa = reinterpret_cast<const __half *>(at(woff + static_cast<uint32_t>(k0) * kb));
+    const __half * wb = PAIR ? reinterpret_cast<const __half *>(at(woff + static_cast<uint32_t>(nk + k0) * kb)) : wa;
     // rows beyond 32 lanes (small grids) are taken in rounds of R2
     for (int rb = 0; rb < nr; rb += R2) {
         const int row = rb + (lane & (R2 - 1));
@@ -286,7 +310,8 @@ __device__ __forceinline__ void gemv_slice(const __half * Ws, int nr, int K, con
         for (int v = 0; v < NV; ++v) acc[v] = 0.f;
         if (live) {
             // this lane's chunks: k0 + j, k0 + j + J, ... < k1; four per step, loads first
-            const __half * pw = Ws + (static_cast<size_t>(k0 + j) * nr + row) * 8;
+            const __half * pw = wa + (static_cast<size_t>(j) * nr + row) * 8;
+            const __half * pu = wb + (static_cast<size_t>(j) * nr + row) * 8;
             const float * px = xin + (k0 + j) * 8;
             const int cnt = (k0 + j < k1) ? (k1 - (k0 + j) + J - 1) >> lj : 0;
             float a4[4][NV];
@@ -296,12 +321,12 @@ __device__ __forceinline__ void gemv_slice(const __half * Ws, int nr, int K, con
                 for (int v = 0; v < NV; ++v) a4[q][v] = 0.f;
             int i = 0;
             for (; i + 4 <= cnt; i += 4) {
-                uint4 wa[4], wb[4];
+                uint4 ga[4], gb[4];
                 float4 xa[4][NC], xb[4][NC];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    wa[q] = *reinterpret_cast<const uint4 *>(pw + q * cs);
-                    if constexpr (PAIR) wb[q] = *reinterpret_cast<const uint4 *>(pw + up + q * cs);
+                    ga[q] = *reinterpret_cast<const uint4 *>(pw + q * cs);
+                    if constexpr (PAIR) gb[q] = *reinterpret_cast<const uint4 *>(pu + q * cs);
 #pragma unroll
                     for (int c = 0; c < NC; ++c) {
                         xa[q][c] = *reinterpret_cast<const float4 *>(px + c * xstride + q * J * 8);
@@ -312,24 +337,26 @@ __device__ __forceinline__ void gemv_slice(const __half * Ws, int nr, int K, con
                 for (int q = 0; q < 4; ++q)
 #pragma unroll
                     for (int c = 0; c < NC; ++c) {
-                        a4[q][c * (PAIR ? 2 : 1)] += dot8h(wa[q], xa[q][c], xb[q][c]);
-                        if constexpr (PAIR) a4[q][c * 2 + 1] += dot8h(wb[q], xa[q][c], xb[q][c]);
+                        a4[q][c * (PAIR ? 2 : 1)] += dot8h(ga[q], xa[q][c], xb[q][c]);
+                        if constexpr (PAIR) a4[q][c * 2 + 1] += dot8h(gb[q], xa[q][c], xb[q][c]);
                     }
                 pw += 4 * cs;
+                pu += 4 * cs;
                 px += 4 * J * 8;
             }
             for (; i < cnt; ++i) {
-                const uint4 wa = *reinterpret_cast<const uint4 *>(pw);
-                uint4 wb = make_uint4(0, 0, 0, 0);
-                if constexpr (PAIR) wb = *reinterpret_cast<const uint4 *>(pw + up);
+                const uint4 ga1 = *reinterpret_cast<const uint4 *>(pw);
+                uint4 gb1 = make_uint4(0, 0, 0, 0);
+                if constexpr (PAIR) gb1 = *reinterpret_cast<const uint4 *>(pu);
 #pragma unroll
                 for (int c = 0; c < NC; ++c) {
                     const float4 xa = *reinterpret_cast<const float4 *>(px + c * xstride);
                     const float4 xb = *reinterpret_cast<const float4 *>(px + c * xstride + 4);
-                    a4[0][c * (PAIR ? 2 : 1)] += dot8h(wa, xa, xb);
-                    if constexpr (PAIR) a4[0][c * 2 + 1] += dot8h(wb, xa, xb);
+                    a4[0][c * (PAIR ? 2 : 1)] += dot8h(ga1, xa, xb);
+                    if constexpr (PAIR) a4[0][c * 2 + 1] += dot8h(gb1, xa, xb);
                 }
                 pw += cs;
+                pu += cs;
                 px += J * 8;
             }
 #pragma unroll
@@ -593,8 +620,7 @@ __device__ __forceinline__ void attn_pv(int ngroups, int GR, int HD, NOf && n_of
 // row of head g). Scores, softmax and P.V run as CTA-wide passes over the GR query heads of
 // g. Partials (m, l, acc) go to the exchange words; CTA G-NH+h combines head h in split
 // order. A single split writes the output directly.
-__device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, const uint8_t * chunk_base, uint32_t tag, uint32_t ptag,
-                                 int p) {
+__device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int chunk, uint32_t tag, uint32_t ptag, int p) {
     const Dims & d = A.d;
     constexpr int HD = KHD, GR = KGR;
     const int NH = d.NH, tid = threadIdx.x;
@@ -611,12 +637,13 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, const
     float * sc = pv + NCW * MAX_GROUP * HD;            // [GR][NPS] scores, then e^(s - m)
     if (b < d.NKV * Sp) {
         const int g = b / Sp, sp = b - g * Sp;
-        const float * qn = reinterpret_cast<const float *>(chunk_base);
-        const float * kn = qn + HD;
-        const __half * Kc = reinterpret_cast<const __half *>(chunk_base + 2 * HD * 4);
+        // chunk segments: q norm, k norm, K rows, V rows (the chunk is only ever cut between them)
         const int r0 = min(sp * A.attn_chunk, pos), r1 = min(r0 + A.attn_chunk, pos);
         const int nc = r1 - r0;
-        const __half * Vc = Kc + static_cast<size_t>(nc) * HD;
+        const float * qn = reinterpret_cast<const float *>(chunk_at(S, chunk, 0));
+        const float * kn = reinterpret_cast<const float *>(chunk_at(S, chunk, HD * 4));
+        const __half * Kc = reinterpret_cast<const __half *>(chunk_at(S, chunk, 2 * HD * 4));
+        const __half * Vc = reinterpret_cast<const __half *>(chunk_at(S, chunk, 2 * HD * 4 + nc * HD * 2));
         const bool last = sp == Sp - 1;
         const int n = nc + (last ? 1 : 0);
         // inputs: q of the group's heads, and (last split) k, v of head g at the new position
@@ -665,31 +692,18 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, const
     const int h = b - (G - NH);
     if (Sp > 1 && h >= 0) {
         named_sync(BID, NCT);                   // this CTA's own split (if any) is done with its scratch
-        float * ms = S.scratch;                 // [MAX_SPLIT] m, [MAX_SPLIT] l, [NCT/HD][HD] sums
-        float * ls = ms + MAX_SPLIT;
-        float * ps = ls + MAX_SPLIT;
-        bool ok = true;
-        for (int k = tid; k < Sp && ok; k += NCT) {
-            const uint64_t * pp = A.w.part + (static_cast<size_t>(k) * NH + h) * WST;
-            ok = ll_get(pp, tag, ms[k], A, S, p) && ll_get(pp + 1, tag, ls[k], A, S, p);
-        }
-        if (!consumers_ok(S, ok)) return false;
-        float M = -INFINITY;
-        for (int k = 0; k < Sp; ++k) M = fmaxf(M, ms[k]);
-        // thread (e, q): dim e, splits q, q+NQ, ...
-        const int e = tid % HD, qq = tid / HD, NQ = NCT / HD;
-        float a = 0.f;
-        for (int k = qq; k < Sp && ok; k += NQ) {
-            float v;
-            ok = ll_get(A.w.part + (static_cast<size_t>(k) * NH + h) * WST + 2 + e, tag, v, A, S, p);
-            a += v * expf(ms[k] - M);
-        }
-        ps[qq * HD + e] = a;
+        float * pb = S.scratch;                 // [Sp][WST]: m, l, acc[HD] of every split
+        const bool ok = ll_fetch_rows(A.w.part + static_cast<size_t>(h) * WST, Sp, WST, NH * WST, tag, pb, A, S.ctrl, p);
         if (!consumers_ok(S, ok)) return false;
         if (tid < HD) {
+            float M = -INFINITY;
+            for (int k = 0; k < Sp; ++k) M = fmaxf(M, pb[k * WST]);
             float L = 0.f, num = 0.f;
-            for (int k = 0; k < Sp; ++k) L += ls[k] * expf(ms[k] - M);
-            for (int q2 = 0; q2 < NQ; ++q2) num += ps[q2 * HD + tid];
+            for (int k = 0; k < Sp; ++k) {
+                const float wk = expf(pb[k * WST] - M);
+                L += pb[k * WST + 1] * wk;
+                num += pb[k * WST + 2 + tid] * wk;
+            }
             ll_store(A.w.attn + h * HD + tid, num / L, tag);
         }
         named_sync(BID, NCT);
@@ -700,15 +714,14 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, const
 // Code-predictor attention at positions pos..pos+ncol-1 (frame.hip:555-575: its own KV,
 // positions 0..15, reset every frame): the CTA cp_attn_cta(layer, g) keeps the K/V of KV
 // head g of that layer in shared memory across the frame's positions.
-__device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, const uint8_t * chunk_base, uint32_t tag, uint32_t ptag,
-                             int p) {
+__device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, int chunk, uint32_t tag, uint32_t ptag, int p) {
     const Dims & d = A.d;
     constexpr int HD = KHD, GR = KGR;
     const int tid = threadIdx.x, ncol = ph.ncol, pos = ph.pos;
     const int g = blockIdx.x - cp_attn_cta(d, ph.layer, 0);
     if (g < 0 || g >= d.NKV) return true;
-    const float * qn = reinterpret_cast<const float *>(chunk_base);
-    const float * kn = qn + HD;
+    const float * qn = reinterpret_cast<const float *>(chunk_at(S, chunk, 0));
+    const float * kn = reinterpret_cast<const float *>(chunk_at(S, chunk, HD * 4));
     __half * kv = S.cpkv;                   // [pos][K,V][HD] of (g, layer)
     float * qs = S.scratch;                 // [2][MAX_GROUP][HD]
     float * ks = qs + 2 * MAX_GROUP * HD;   // [2][HD]
@@ -778,12 +791,8 @@ __device__ void consumer(const Args & A, Sm & S) {
         const int nr = r1 - r0;
 
         if (ph.op == TATTN || ph.op == CATTN) {
-            const uint8_t * cb = nullptr;
-            if (ns > 0) {
-                if (!wait_chunk(A, S, chunk, p)) break;
-                cb = S.ring + S.meta_off[chunk % NSLOT];
-            }
-            const bool ok = ph.op == TATTN ? talker_attention(A, S, ph, cb, tag, ptag, p) : cp_attention(A, S, ph, cb, tag, ptag, p);
+            if (ns > 0 && !wait_chunk(A, S, chunk, p)) break;
+            const bool ok = ph.op == TATTN ? talker_attention(A, S, ph, chunk, tag, ptag, p) : cp_attention(A, S, ph, chunk, tag, ptag, p);
             if (!ok) break;
             if (ns > 0) {
                 named_sync(BID, NCT);
@@ -824,9 +833,9 @@ __device__ void consumer(const Args & A, Sm & S) {
         const bool has_norm = ph.op == TQKV || ph.op == CQKV || ph.op == TGU || ph.op == CGU || ph.op == THEAD || ph.op == CHEAD;
         bool ok = ns > 0 ? wait_chunk_local(A, S, chunk, p) : true;
         stamp(A, p, 1);
-        const uint8_t * cbase = S.ring + S.meta_off[chunk % NSLOT];
-        const float * nw = reinterpret_cast<const float *>(cbase);
-        const __half * Ws = reinterpret_cast<const __half *>(cbase + (has_norm ? d.H * 4 : 0));
+        const float * nw = reinterpret_cast<const float *>(chunk_at(S, chunk, 0));
+        const uint32_t woff = has_norm ? d.H * 4 : 0;     // the weight slice follows the norm weights
+        const auto at = [&](uint32_t x) { return chunk_at(S, chunk, x); };
         float ss0 = 0.f, ss1 = 0.f;   // sums of squares of this thread's inputs, per column
         int nnorm = 0;                // columns whose norm scale is needed
         auto stage = [&](int c, int i, float v) {
@@ -913,8 +922,8 @@ __device__ void consumer(const Args & A, Sm & S) {
                 auto epi = [&](int u, int c, float y, float) {
                     ll_store(A.w.qkv + static_cast<size_t>(c) * d.QKV + r0 + u, y * (c ? sc1 : sc0), t);
                 };
-                if (gcol == 2) gemv_slice<2, false>(Ws, nr, d.H, xin, XS, S.part, epi);
-                else gemv_slice<1, false>(Ws, nr, d.H, xin, XS, S.part, epi);
+                if (gcol == 2) gemv_slice<2, false>(at, woff, nr, d.H, xin, XS, S.part, epi);
+                else gemv_slice<1, false>(at, woff, nr, d.H, xin, XS, S.part, epi);
                 break;
             }
             case TO: case CO: case TDOWN: case CDOWN: {
@@ -922,8 +931,8 @@ __device__ void consumer(const Args & A, Sm & S) {
                 auto epi = [&](int u, int c, float y, float) {
                     ll_store(A.w.x + static_cast<size_t>(c) * d.H + r0 + u, S.xres[c * d.H + r0 + u] + y, t);
                 };
-                if (gcol == 2) gemv_slice<2, false>(Ws, nr, K, xin, XS, S.part, epi);
-                else gemv_slice<1, false>(Ws, nr, K, xin, XS, S.part, epi);
+                if (gcol == 2) gemv_slice<2, false>(at, woff, nr, K, xin, XS, S.part, epi);
+                else gemv_slice<1, false>(at, woff, nr, K, xin, XS, S.part, epi);
                 break;
             }
             case TGU: case CGU: {
@@ -933,8 +942,8 @@ __device__ void consumer(const Args & A, Sm & S) {
                     up *= s;
                     ll_store(A.w.h + static_cast<size_t>(c) * d.F + r0 + u, g / (1.f + expf(-g)) * up, t);
                 };
-                if (gcol == 2) gemv_slice<2, true>(Ws, nr, d.H, xin, XS, S.part, epi);
-                else gemv_slice<1, true>(Ws, nr, d.H, xin, XS, S.part, epi);
+                if (gcol == 2) gemv_slice<2, true>(at, woff, nr, d.H, xin, XS, S.part, epi);
+                else gemv_slice<1, true>(at, woff, nr, d.H, xin, XS, S.part, epi);
                 break;
             }
             case THEAD: {
@@ -943,12 +952,12 @@ __device__ void consumer(const Args & A, Sm & S) {
                     S.hid[i] = hv;
                     if (b == 0) A.w.hidden[i] = hv;
                 }
-                gemv_slice<1, false>(Ws, nr, d.H, xin, XS, S.part,
+                gemv_slice<1, false>(at, woff, nr, d.H, xin, XS, S.part,
                                      [&](int u, int, float y, float) { ll_store(A.w.logits + r0 + u, y * sc0, t); });
                 break;
             }
             case CHEAD:
-                gemv_slice<1, false>(Ws, nr, d.H, xin, XS, S.part, [&](int u, int, float y, float) {
+                gemv_slice<1, false>(at, woff, nr, d.H, xin, XS, S.part, [&](int u, int, float y, float) {
                     ll_store(A.w.clogits + static_cast<size_t>(ph.pos - 1) * d.CV + r0 + u, y * sc0, t);
                 });
                 break;

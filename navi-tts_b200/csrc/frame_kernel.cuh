@@ -142,7 +142,7 @@ struct Args {
 // ---- shared-memory layout (identical on host and device) ---------------------------------
 
 struct SmemLayout {
-    uint32_t bars, meta_off, meta_end, ctrl, codes, xres, hid, part, scratch, cpkv, ring, total;
+    uint32_t bars, meta_off, meta_split, meta_end, ctrl, codes, xres, hid, part, scratch, cpkv, ring, total;
 };
 
 // The code predictor's K/V of one (KV head, layer), kept in shared memory across the
@@ -160,6 +160,7 @@ __host__ __device__ inline SmemLayout smem_layout(const Dims & d, uint32_t ring_
     L.bars = o;     o += NSLOT * 8;
     L.meta_end = o; o += NSLOT * 8;
     L.meta_off = o; o += NSLOT * 4;
+    L.meta_split = o; o += NSLOT * 4;
     L.ctrl = o;     o += CTRL_BYTES;
     L.codes = o;    o += NCB * 4;
     o = align_up(o, 16);
@@ -191,7 +192,28 @@ struct Seg {
     uint32_t bytes;
     uint32_t rows = 1;
     uint32_t stride = 0;
+    uint32_t nr = 0;      // a weight slice [K/8][nr][8] f16 of nr rows (0: other data)
 };
+
+// Where a chunk may be cut when it does not fit before the end of the ring: at the start
+// of any segment, and inside a weight slice at the first k-chunk of any consumer warp's
+// K range (so every warp still reads one contiguous run). Returns the largest such logical
+// offset <= room (0: the whole chunk starts over at the ring's start).
+__host__ __device__ inline uint32_t chunk_split(const Seg * s, int ns, uint32_t room) {
+    uint32_t best = 0, o = 0;
+    for (int i = 0; i < ns; ++i) {
+        if (o <= room) best = o;
+        if (s[i].nr > 0 && s[i].rows == 1) {
+            const uint32_t kstep = s[i].nr * 16u, nk = s[i].bytes / kstep;
+            for (int w = 1; w < NCW; ++w) {
+                const uint32_t at = o + (nk * static_cast<uint32_t>(w) / NCW) * kstep;
+                if (at <= room && at > best) best = at;
+            }
+        }
+        o += s[i].bytes * s[i].rows;
+    }
+    return best;
+}
 
 // This CTA's rows of every matrix shape the phases use (computed once per launch: the
 // 64-bit divisions of split_rows stay off the per-phase path).
@@ -225,31 +247,32 @@ __host__ __device__ inline int phase_segments(const Args & A, const ModelW & W, 
         case TQKV: case CQKV:
             r0 = R.qkv0; r1 = R.qkv1;
             s[0] = {L->ln1, H4};
-            s[1] = {L->wqkv + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
+            s[1] = {L->wqkv + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2), 1, 0, static_cast<uint32_t>(r1 - r0)};
             return r1 > r0 ? 2 : 0;
         case TO: case CO:
             r0 = R.h0; r1 = R.h1;
-            s[0] = {L->wo + static_cast<size_t>(r0) * d.Q, static_cast<uint32_t>((r1 - r0) * d.Q * 2)};
+            s[0] = {L->wo + static_cast<size_t>(r0) * d.Q, static_cast<uint32_t>((r1 - r0) * d.Q * 2), 1, 0, static_cast<uint32_t>(r1 - r0)};
             return r1 > r0 ? 1 : 0;
         case TGU: case CGU:
             r0 = R.f0; r1 = R.f1;
             s[0] = {L->ln2, H4};
-            s[1] = {L->wg + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
-            s[2] = {L->wu + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
+            s[1] = {L->wg + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2), 1, 0, static_cast<uint32_t>(r1 - r0)};
+            s[2] = {L->wu + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2), 1, 0, static_cast<uint32_t>(r1 - r0)};
             return r1 > r0 ? 3 : 0;
         case TDOWN: case CDOWN:
             r0 = R.h0; r1 = R.h1;
-            s[0] = {L->wd + static_cast<size_t>(r0) * d.F, static_cast<uint32_t>((r1 - r0) * d.F * 2)};
+            s[0] = {L->wd + static_cast<size_t>(r0) * d.F, static_cast<uint32_t>((r1 - r0) * d.F * 2), 1, 0, static_cast<uint32_t>(r1 - r0)};
             return r1 > r0 ? 1 : 0;
         case THEAD:
             r0 = R.tv0; r1 = R.tv1;
             s[0] = {W.tl_norm, H4};
-            s[1] = {W.codec_head + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
+            s[1] = {W.codec_head + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2), 1, 0, static_cast<uint32_t>(r1 - r0)};
             return r1 > r0 ? 2 : 0;
         case CHEAD:
             r0 = R.cv0; r1 = R.cv1;
             s[0] = {W.cp_norm, H4};
-            s[1] = {W.lm_head[ph.pos - 1] + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2)};
+            s[1] = {W.lm_head[ph.pos - 1] + static_cast<size_t>(r0) * d.H, static_cast<uint32_t>((r1 - r0) * d.H * 2), 1, 0,
+                    static_cast<uint32_t>(r1 - r0)};
             return r1 > r0 ? 2 : 0;
         case TATTN: {
             const int S = A.attn_split;
