@@ -193,29 +193,73 @@ __device__ void producer(const Args & A, Sm & S) {
 __device__ __forceinline__ uint32_t tag_of(uint64_t w) { return static_cast<uint32_t>(w >> 32); }
 __device__ __forceinline__ float val_of(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
 
-// Fetches exchange words carrying `tag` into dst: `rows` runs of `len` words (len even),
-// run r at src + r * stride (stride even), packed back to back in dst. Thread t takes the
-// word pairs 2t + 2*NCT*k of the packed order, issues up to 4 pair loads at once, then
-// re-issues every stale pair together until all carry the tag (one L2 round trip per poll,
-// not one per stale pair). Returns this thread's success (the caller decides with a
-// barrier). ll_each() visits the same elements of a single run in the same thread, so a
-// transform needs no barrier in between.
-__device__ __noinline__ bool ll_fetch_rows(const uint64_t * src, int rows, int len, int stride, uint32_t tag, float * dst, const Args & A,
-                                           Ctrl * ctrl, int phase) {
+// Fetches exchange words carrying `tag` into dst. The words are rows of `len` words (len
+// even): `cols` column blocks (block c at src + c * csrc, its rows at dst + c * cdst), each
+// with na rows at offa + r * stra and then nb rows at offb + r * strb (source offsets, even),
+// written as consecutive rows of ldst floats. Thread t takes the word pairs 2t + 2*NCT*k of
+// the packed order (block, row, word), issues up to 4 pair loads at once, then re-issues
+// every stale pair together until all carry the tag: one L2 round trip per poll for all of
+// a phase's inputs. Returns this thread's success (the caller decides with a barrier).
+// ll_each() visits the same packed elements in the same thread, so a transform needs no
+// barrier in between.
+__device__ __noinline__ bool ll_fetch_plan(const uint64_t * src, int cols, int csrc, int cdst, int na, int offa, int stra, int nb, int offb,
+                                           int strb, int len, int ldst, uint32_t tag, float * dst, const Args & A, Ctrl * ctrl, int phase) {
     constexpr int MAXK = 4;
-    const int n = rows * len;
+    const int rpc = na + nb, n = cols * rpc * len;
     for (int base = 2 * threadIdx.x; base < n; base += 2 * NCT * MAXK) {
         uint64_t w[MAXK][2];
         const uint64_t * at[MAXK];
+        float * to[MAXK];
         unsigned pend = 0;
 #pragma unroll
         for (int k = 0; k < MAXK; ++k) {
             const int i = base + 2 * NCT * k;
             at[k] = nullptr;
+            to[k] = nullptr;
             if (i < n) {
-                const int r = rows == 1 ? 0 : i / len;
-                at[k] = src + static_cast<size_t>(r) * stride + (i - r * len);
+                const int R = i / len, e = i - R * len, c = R / rpc, rr = R - c * rpc;
+                at[k] = src + static_cast<size_t>(c) * csrc + (rr < na ? offa + rr * stra : offb + (rr - na) * strb) + e;
+                to[k] = dst + static_cast<size_t>(c) * cdst + rr * ldst + e;
                 ll_load2(at[k], w[k][0], w[k][1]);
+                pend |= 1u << k;
+            }
+        }
+        uint64_t t0 = 0;
+        uint32_t spins = 0;
+        for (;;) {
+#pragma unroll
+            for (int k = 0; k < MAXK; ++k) {
+                if (((pend >> k) & 1u) && tag_of(w[k][0]) == tag && tag_of(w[k][1]) == tag) {
+                    to[k][0] = val_of(w[k][0]);
+                    to[k][1] = val_of(w[k][1]);
+                    pend &= ~(1u << k);
+                }
+            }
+            if (!pend) break;
+            if (t0 == 0) t0 = globaltimer();
+#pragma unroll
+            for (int k = 0; k < MAXK; ++k)
+                if ((pend >> k) & 1u) ll_load2(at[k], w[k][0], w[k][1]);
+            ++spins;
+            if ((spins & 3u) == 0 && globaltimer() - t0 > A.timeout_ns) { raise_abort(A, phase); return false; }
+            if ((spins & 31u) == 0 && (ctrl->abort || launch_aborted(A))) return false;
+        }
+    }
+    return true;
+}
+
+// Exchange words [0, n) (n even) into dst[0, n): ll_fetch_plan's single-run case without
+// its index arithmetic (the common case: one input vector per phase).
+__device__ __noinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag, float * dst, const Args & A, Ctrl * ctrl, int phase) {
+    constexpr int MAXK = 4;
+    for (int base = 2 * threadIdx.x; base < n; base += 2 * NCT * MAXK) {
+        uint64_t w[MAXK][2];
+        unsigned pend = 0;
+#pragma unroll
+        for (int k = 0; k < MAXK; ++k) {
+            const int i = base + 2 * NCT * k;
+            if (i < n) {
+                ll_load2(src + i, w[k][0], w[k][1]);
                 pend |= 1u << k;
             }
         }
@@ -235,7 +279,7 @@ __device__ __noinline__ bool ll_fetch_rows(const uint64_t * src, int rows, int l
             if (t0 == 0) t0 = globaltimer();
 #pragma unroll
             for (int k = 0; k < MAXK; ++k)
-                if ((pend >> k) & 1u) ll_load2(at[k], w[k][0], w[k][1]);
+                if ((pend >> k) & 1u) ll_load2(src + base + 2 * NCT * k, w[k][0], w[k][1]);
             ++spins;
             if ((spins & 3u) == 0 && globaltimer() - t0 > A.timeout_ns) { raise_abort(A, phase); return false; }
             if ((spins & 31u) == 0 && (ctrl->abort || launch_aborted(A))) return false;
@@ -244,12 +288,14 @@ __device__ __noinline__ bool ll_fetch_rows(const uint64_t * src, int rows, int l
     return true;
 }
 
-// Exchange words [0, n) (n even) into dst[0, n): one run of ll_fetch_rows.
-__device__ __forceinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag, float * dst, const Args & A, Ctrl * ctrl, int phase) {
-    return ll_fetch_rows(src, 1, n, 0, tag, dst, A, ctrl, phase);
+// `cols` runs of len words at src + c * len into dst + c * dstride (one column: ll_fetch).
+__device__ __forceinline__ bool ll_fetch_cols(const uint64_t * src, int cols, int len, float * dst, int dstride, uint32_t tag, const Args & A,
+                                              Ctrl * ctrl, int phase) {
+    if (cols == 1) return ll_fetch(src, len, tag, dst, A, ctrl, phase);
+    return ll_fetch_plan(src, cols, len, dstride, 1, 0, 0, 0, 0, 0, len, len, tag, dst, A, ctrl, phase);
 }
 
-// Visits i over the elements ll_fetch(n) gave this thread.
+// Visits the packed indices i < n that ll_fetch_plan gave this thread.
 template <class F>
 __device__ __forceinline__ void ll_each(int n, F && fn) {
     for (int i = 2 * threadIdx.x; i < n; i += 2 * NCT) {
@@ -629,7 +675,7 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int c
     const uint32_t WST = HD + 2;
     const int NPS = A.attn_chunk + 1;                  // score slots per head
     float * qs = S.scratch;                            // [GR][HD]
-    float * ks = qs + MAX_GROUP * HD;                  // [HD] new position
+    float * ks = qs + GR * HD;                         // [HD] new position
     float * vs = ks + HD;                              // [HD]
     __half * kh = reinterpret_cast<__half *>(vs + HD); // new K/V row slice as f16 [2][HD]
     float * ml = vs + 2 * HD;                          // [GR][2]
@@ -647,11 +693,9 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int c
         const bool last = sp == Sp - 1;
         const int n = nc + (last ? 1 : 0);
         // inputs: q of the group's heads, and (last split) k, v of head g at the new position
-        bool ok = ll_fetch(A.w.qkv + g * GR * HD, GR * HD, ptag, qs, A, S.ctrl, p);
-        if (last) {
-            ok = ok && ll_fetch(A.w.qkv + d.Q + g * HD, HD, ptag, ks, A, S.ctrl, p);
-            ok = ok && ll_fetch(A.w.qkv + d.Q + d.KV + g * HD, HD, ptag, vs, A, S.ctrl, p);
-        }
+        // rows of HD words: the group's q heads, then (last split) k and v of head g
+        const bool ok = ll_fetch_plan(A.w.qkv, 1, 0, 0, GR, g * GR * HD, HD, last ? 2 : 0, d.Q + g * HD, d.KV, HD, HD, ptag, qs, A,
+                                      S.ctrl, p);
         if (!consumers_ok(S, ok)) return false;
         stamp(A, p, 0);
         const int warp = tid >> 5;
@@ -693,7 +737,8 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int c
     if (Sp > 1 && h >= 0) {
         named_sync(BID, NCT);                   // this CTA's own split (if any) is done with its scratch
         float * pb = S.scratch;                 // [Sp][WST]: m, l, acc[HD] of every split
-        const bool ok = ll_fetch_rows(A.w.part + static_cast<size_t>(h) * WST, Sp, WST, NH * WST, tag, pb, A, S.ctrl, p);
+        const bool ok = ll_fetch_plan(A.w.part + static_cast<size_t>(h) * WST, Sp, NH * WST, WST, 1, 0, 0, 0, 0, 0, WST, WST, tag, pb, A,
+                                      S.ctrl, p);
         if (!consumers_ok(S, ok)) return false;
         if (tid < HD) {
             float M = -INFINITY;
@@ -723,38 +768,34 @@ __device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, int chunk
     const float * qn = reinterpret_cast<const float *>(chunk_at(S, chunk, 0));
     const float * kn = reinterpret_cast<const float *>(chunk_at(S, chunk, HD * 4));
     __half * kv = S.cpkv;                   // [pos][K,V][HD] of (g, layer)
-    float * qs = S.scratch;                 // [2][MAX_GROUP][HD]
-    float * ks = qs + 2 * MAX_GROUP * HD;   // [2][HD]
-    float * vs = ks + 2 * HD;               // [2][HD]
-    float * sc = vs + 2 * HD;               // [2][MAX_GROUP][NCB] scores, then e^(s - m)
+    float * qkv = S.scratch;                // [2][GR + 2][HD]: per column the q heads, k, v
+    const auto qof = [&](int c) { return qkv + c * (GR + 2) * HD; };
+    const auto kof = [&](int c) { return qkv + (c * (GR + 2) + GR) * HD; };
+    const auto vof = [&](int c) { return qkv + (c * (GR + 2) + GR + 1) * HD; };
+    float * sc = qkv + 2 * (GR + 2) * HD;   // [2][MAX_GROUP][NCB] scores, then e^(s - m)
     float * ml = sc + 2 * MAX_GROUP * NCB;  // [2][MAX_GROUP][2]
     float * pv = ml + 4 * MAX_GROUP;        // [NCW][MAX_GROUP][HD]
-    bool ok = true;
-    for (int c = 0; c < ncol && ok; ++c) {
-        const uint64_t * src = A.w.qkv + static_cast<size_t>(c) * d.QKV;
-        float * qd = qs + c * MAX_GROUP * HD;
-        ok = ll_fetch(src + g * GR * HD, GR * HD, ptag, qd, A, S.ctrl, p) && ll_fetch(src + d.Q + g * HD, HD, ptag, ks + c * HD, A, S.ctrl, p) &&
-             ll_fetch(src + d.Q + d.KV + g * HD, HD, ptag, vs + c * HD, A, S.ctrl, p);
-    }
+    // per column: the group's q heads, then k and v of head g (rows of HD words)
+    const bool ok = ll_fetch_plan(A.w.qkv, ncol, d.QKV, (GR + 2) * HD, GR, g * GR * HD, HD, 2, d.Q + g * HD, d.KV, HD, HD, ptag, qkv, A,
+                                  S.ctrl, p);
     if (!consumers_ok(S, ok)) return false;
     stamp(A, p, 0);
     for (int v = tid >> 5; v < ncol * (GR + 1); v += NCW) {
         const int c = v / (GR + 1), j = v - c * (GR + 1);
-        warp_norm_rope(j < GR ? qs + (c * MAX_GROUP + j) * HD : ks + c * HD, j < GR ? qn : kn, A.rope_c + (pos + c) * HD, HD, d.eps_c,
-                       j == GR);
+        warp_norm_rope(j < GR ? qof(c) + j * HD : kof(c), j < GR ? qn : kn, A.rope_c + (pos + c) * HD, HD, d.eps_c, j == GR);
     }
     named_sync(BID, NCT);
     for (int i = tid; i < ncol * HD; i += NCT) {
         const int c = i / HD, e = i - c * HD;
-        kv[(static_cast<size_t>(pos + c) * 2 + 0) * HD + e] = __float2half_rn(ks[i]);
-        kv[(static_cast<size_t>(pos + c) * 2 + 1) * HD + e] = __float2half_rn(vs[i]);
+        kv[(static_cast<size_t>(pos + c) * 2 + 0) * HD + e] = __float2half_rn(kof(c)[e]);
+        kv[(static_cast<size_t>(pos + c) * 2 + 1) * HD + e] = __float2half_rn(vof(c)[e]);
     }
     named_sync(BID, NCT);
     stamp(A, p, 1);
     const float scale = rsqrtf(static_cast<float>(HD));
     // column c attends to positions 0..pos+c (causal within the 2-column pass)
     attn_scores(ncol, pos + ncol, GR, HD, scale, NCB, [&](int, int t) { return kv + static_cast<size_t>(t) * 2 * HD; },
-                [&](int c) { return static_cast<const float *>(qs + c * MAX_GROUP * HD); },
+                [&](int c) { return static_cast<const float *>(qof(c)); },
                 [&](int c, int t) { return sc + c * MAX_GROUP * NCB + t; });
     named_sync(BID, NCT);
     attn_softmax(sc, NCB, ncol * MAX_GROUP, [&](int r) { return (r % MAX_GROUP) < GR ? pos + 1 + r / MAX_GROUP : 0; }, ml);
@@ -844,8 +885,13 @@ __device__ void consumer(const Args & A, Sm & S) {
             if (c == 0) ss0 += v * v;
             else ss1 += v * v;
         };
-        // after ll_fetch of column c into xres: the same thread stages its elements
-        auto stage_fetched = [&](int c) { ll_each(d.H, [&](int i) { stage(c, i, S.xres[c * d.H + i]); }); };
+        // after ll_fetch_cols of nc columns into xres: the same thread stages its elements
+        auto stage_fetched = [&](int nc) {
+            ll_each(nc * d.H, [&](int i) {
+                const int c = i >= d.H ? 1 : 0;
+                stage(c, i - c * d.H, S.xres[i]);
+            });
+        };
         switch (ph.op) {
             case TQKV: case CQKV: {
                 nnorm = ncol;
@@ -876,36 +922,34 @@ __device__ void consumer(const Args & A, Sm & S) {
                     if (tid == 0) S.codes[ph.pos - 1] = code;
                     const __half * row = W.cp_emb[ph.pos - 2] + static_cast<size_t>(code) * d.H;
                     for (int i = tid; i < d.H; i += NCT) stage(0, i, __half2float(row[i]));
-                } else {
-                    for (int c = 0; c < ncol && ok; ++c) {
-                        ok = ll_fetch(A.w.x + static_cast<size_t>(c) * d.H, d.H, ptag, S.xres + c * d.H, A, S.ctrl, p);
-                        if (ok) stage_fetched(c);
-                    }
+                } else if (ok) {
+                    ok = ll_fetch_cols(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
+                    if (ok) stage_fetched(ncol);
                 }
                 break;
             }
             case TGU: case CGU:
                 nnorm = ncol;
-                for (int c = 0; c < ncol && ok; ++c) {
-                    ok = ll_fetch(A.w.x + static_cast<size_t>(c) * d.H, d.H, ptag, S.xres + c * d.H, A, S.ctrl, p);
-                    if (ok) stage_fetched(c);
+                if (ok) {
+                    ok = ll_fetch_cols(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
+                    if (ok) stage_fetched(ncol);
                 }
                 break;
             case TO: case CO:
-                for (int c = 0; c < ncol && ok; ++c) ok = ll_fetch(A.w.attn + static_cast<size_t>(c) * d.Q, d.Q, ptag, xin + c * XS, A, S.ctrl, p);
+                if (ok) ok = ll_fetch_cols(A.w.attn, ncol, d.Q, xin, XS, ptag, A, S.ctrl, p);
                 break;
             case TDOWN: case CDOWN:
-                for (int c = 0; c < ncol && ok; ++c) ok = ll_fetch(A.w.h + static_cast<size_t>(c) * d.F, d.F, ptag, xin + c * XS, A, S.ctrl, p);
+                if (ok) ok = ll_fetch_cols(A.w.h, ncol, d.F, xin, XS, ptag, A, S.ctrl, p);
                 break;
             case THEAD:
                 nnorm = 1;
                 ok = ok && ll_fetch(A.w.x, d.H, ptag, S.xres, A, S.ctrl, p);
-                if (ok) stage_fetched(0);
+                if (ok) stage_fetched(1);
                 break;
             case CHEAD:
                 nnorm = 1;
                 ok = ok && ll_fetch(A.w.x + static_cast<size_t>(ncol - 1) * d.H, d.H, ptag, S.xres, A, S.ctrl, p);
-                if (ok) stage_fetched(0);
+                if (ok) stage_fetched(1);
                 break;
             default: break;
         }
