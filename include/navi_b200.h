@@ -117,6 +117,37 @@ typedef struct navi_kv {
 int navi_kv_create(navi_device * dev, int n_layer, int max_pos, int kv_dim, navi_kv ** out);
 void navi_kv_destroy(navi_kv * kv);
 
+/* ---- talker: replaces navi::qwen3tts::Talker (model/qwen3tts/talker.h:20-67) ------------- */
+
+typedef struct navi_talker navi_talker;
+
+typedef struct navi_prompt {        /* Prompt, talker.h:26-32: device rows, valid until the next build_prompt */
+    const float * prefill;          /* [n_prefill][hidden] */
+    const float * trailing;         /* [n_trailing][hidden]: frame i feeds trailing[i], then tts_pad */
+    const float * tts_pad;          /* [hidden] */
+    int n_prefill, n_trailing;
+} navi_prompt;
+
+/* Talker::create (talker.hip:200-266): the prompt / prefill scratch and the talker's KV
+ * cache (max_positions per layer). max_prompt_tokens <= 1024. */
+int navi_talker_create(navi_device * dev, const navi_weights * w, int max_prompt_tokens, int max_positions, navi_talker ** out);
+/* Talker::build_prompt (talker.hip:283-352): ids = the tokenised
+ * "<|im_start|>assistant\n{text}<|im_end|>\n<|im_start|>assistant\n" (3 header ids, the
+ * text, 5 trailer ids); language NULL, "" or "auto" for none; speaker: host [hidden]. */
+int navi_talker_build_prompt(navi_talker * t, const int32_t * ids, int n_ids, const char * language, const float * speaker,
+                             navi_prompt * out);
+/* Talker::prefill (talker.hip:355-399): the prefill rows at positions 0..n-1; fills the KV cache. */
+int navi_talker_prefill(navi_talker * t, const navi_prompt * p);
+/* Talker::kv: the talker's cache as a navi_kv (its k / v arrays belong to the talker). */
+int navi_talker_kv(navi_talker * t, navi_kv * out);
+/* Talker::d_hidden / d_logits: the last prefill row's post-norm hidden [hidden] and codec
+ * logits [talker vocab] (the inputs of navi_frame_run_first). */
+const float * navi_talker_hidden(const navi_talker * t);
+const float * navi_talker_logits(const navi_talker * t);
+/* Talker::last_ms: device time of the last prefill. */
+double navi_talker_last_ms(const navi_talker * t);
+void navi_talker_destroy(navi_talker * t);
+
 /* ---- frame: replaces navi::qwen3tts::Frame (model/qwen3tts/frame.h:24-71) --------------- */
 
 typedef struct navi_sampling {      /* Sampling, frame.h:24-31, plus top-p and the stream choice */

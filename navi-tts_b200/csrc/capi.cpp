@@ -4,6 +4,7 @@
 #include "frame.hpp"
 #include "runtime.hpp"
 #include "sample_static.hpp"
+#include "talker.hpp"
 
 #include <cstring>
 #include <memory>
@@ -19,6 +20,10 @@ struct navi_weights {
 struct navi_frame {
     std::unique_ptr<navi::qwen3tts::Frame> f;
     navi_device * dev = nullptr;
+};
+struct navi_talker {
+    std::unique_ptr<navi::qwen3tts::Talker> t;
+    int hidden = 0;
 };
 
 namespace {
@@ -341,5 +346,64 @@ int navi_sample_logits_static(navi_device * dev, const float * d_logits, int voc
         return NAVI_OK;
     });
 }
+
+int navi_talker_create(navi_device * dev, const navi_weights * w, int max_prompt_tokens, int max_positions, navi_talker ** out) {
+    return guard([&]() -> int {
+        if (!dev || !w || !out) return set_err(NAVI_E_ARG, "NULL argument");
+        auto t = std::make_unique<navi_talker>();
+        t->t = navi::qwen3tts::Talker::create(*dev->dev, *w->w, max_prompt_tokens, max_positions);
+        t->hidden = w->w->params().talker.hidden;
+        *out = t.release();
+        return NAVI_OK;
+    });
+}
+
+int navi_talker_build_prompt(navi_talker * t, const int32_t * ids, int n_ids, const char * language, const float * speaker,
+                             navi_prompt * out) {
+    return guard([&]() -> int {
+        if (!t || !ids || n_ids <= 0 || !speaker || !out) return set_err(NAVI_E_ARG, "bad argument");
+        const auto & pr = t->t->build_prompt(std::span<const std::int32_t>(ids, static_cast<size_t>(n_ids)), language ? language : "",
+                                             std::span<const float>(speaker, static_cast<size_t>(t->hidden)));
+        out->prefill = pr.prefill;
+        out->trailing = pr.trailing;
+        out->tts_pad = pr.tts_pad;
+        out->n_prefill = pr.n_prefill;
+        out->n_trailing = pr.n_trailing;
+        return NAVI_OK;
+    });
+}
+
+int navi_talker_prefill(navi_talker * t, const navi_prompt * p) {
+    return guard([&]() -> int {
+        if (!t || !p) return set_err(NAVI_E_ARG, "NULL argument");
+        navi::qwen3tts::Prompt pr;
+        pr.prefill = p->prefill;
+        pr.trailing = p->trailing;
+        pr.tts_pad = p->tts_pad;
+        pr.n_prefill = p->n_prefill;
+        pr.n_trailing = p->n_trailing;
+        t->t->prefill(pr);
+        return NAVI_OK;
+    });
+}
+
+int navi_talker_kv(navi_talker * t, navi_kv * out) {
+    return guard([&]() -> int {
+        if (!t || !out) return set_err(NAVI_E_ARG, "NULL argument");
+        auto & kv = t->t->kv();
+        out->n_layer = kv.n_layer;
+        out->max_pos = kv.max_pos;
+        out->kv_dim = kv.kv_dim;
+        out->n_used = kv.n_used;
+        out->k = kv.k;
+        out->v = kv.v;
+        return NAVI_OK;
+    });
+}
+
+const float * navi_talker_hidden(const navi_talker * t) { return t ? t->t->d_hidden() : nullptr; }
+const float * navi_talker_logits(const navi_talker * t) { return t ? t->t->d_logits() : nullptr; }
+double navi_talker_last_ms(const navi_talker * t) { return t ? t->t->last_ms() : 0.0; }
+void navi_talker_destroy(navi_talker * t) { delete t; }
 
 } // extern "C"

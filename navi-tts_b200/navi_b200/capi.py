@@ -53,6 +53,10 @@ class Sampling(ctypes.Structure):
                 ("rng", c_int)]
 
 
+class Prompt(ctypes.Structure):
+    _fields_ = [("prefill", c_void_p), ("trailing", c_void_p), ("tts_pad", c_void_p), ("n_prefill", c_int), ("n_trailing", c_int)]
+
+
 class FrameOpts(ctypes.Structure):
     _fields_ = [("blocks_per_mp", c_int), ("deadline_us", c_uint64)]
 
@@ -77,6 +81,14 @@ SIGNATURES = [
     ("navi_weights_free", None, [c_void_p]),
     ("navi_kv_create", c_int, [c_void_p, c_int, c_int, c_int, POINTER(POINTER(KV))]),
     ("navi_kv_destroy", None, [POINTER(KV)]),
+    ("navi_talker_create", c_int, [c_void_p, c_void_p, c_int, c_int, POINTER(c_void_p)]),
+    ("navi_talker_build_prompt", c_int, [c_void_p, POINTER(c_int32), c_int, c_char_p, POINTER(c_float), POINTER(Prompt)]),
+    ("navi_talker_prefill", c_int, [c_void_p, POINTER(Prompt)]),
+    ("navi_talker_kv", c_int, [c_void_p, POINTER(KV)]),
+    ("navi_talker_hidden", c_void_p, [c_void_p]),
+    ("navi_talker_logits", c_void_p, [c_void_p]),
+    ("navi_talker_last_ms", c_double, [c_void_p]),
+    ("navi_talker_destroy", None, [c_void_p]),
     ("navi_frame_create", c_int, [c_void_p, c_void_p, POINTER(FrameOpts), POINTER(c_void_p)]),
     ("navi_frame_reset", c_int, [c_void_p]),
     ("navi_frame_run_first", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, POINTER(Sampling), c_uint64, c_int,

@@ -155,6 +155,56 @@ class KvCache:
             pass
 
 
+class Talker:
+    """navi::qwen3tts::Talker (talker.h:34-67): prompt rows and the prefill that fills its KV cache."""
+
+    def __init__(self, dev: Device, w: Weights, max_prompt_tokens: int = 1024, max_positions: int = 4096):
+        h = c_void_p()
+        check(lib().navi_talker_create(dev.h, w.h, max_prompt_tokens, max_positions, byref(h)))
+        self.h, self.dev, self.w = h, dev, w
+        self.prompt = None
+
+    def build_prompt(self, ids, language: str, speaker) -> capi.Prompt:
+        import numpy as np
+        ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+        spk = np.ascontiguousarray(np.asarray(speaker, dtype=np.float32))
+        pr = capi.Prompt()
+        check(lib().navi_talker_build_prompt(self.h, ids.ctypes.data_as(POINTER(c_int32)), len(ids),
+                                             (language or "").encode(), spk.ctypes.data_as(POINTER(ctypes.c_float)), byref(pr)))
+        self.prompt = pr
+        return pr
+
+    def prefill(self, pr: capi.Prompt = None) -> None:
+        check(lib().navi_talker_prefill(self.h, byref(pr or self.prompt)))
+
+    def kv(self) -> "KvCache":
+        kv = KvCache()
+        kv.s = capi.KV()
+        check(lib().navi_talker_kv(self.h, byref(kv.s)))
+        kv._keep = (self,)
+        return kv
+
+    def d_hidden(self) -> int:
+        return lib().navi_talker_hidden(self.h)
+
+    def d_logits(self) -> int:
+        return lib().navi_talker_logits(self.h)
+
+    def last_ms(self) -> float:
+        return lib().navi_talker_last_ms(self.h)
+
+    def close(self):
+        if self.h:
+            lib().navi_talker_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def _result(r: capi.FrameResult, st: int) -> FrameResult:
     err = "" if st == capi.NAVI_OK else lib().navi_last_error().decode(errors="replace")
     return FrameResult(bool(r.ok), bool(r.eos), list(r.codes), r.us, r.status if st == capi.NAVI_OK else st, err)

@@ -171,6 +171,51 @@ def talker_step(W: Weights, step_in: torch.Tensor, kv: list, n_past: int):
     return hidden, logits
 
 
+# --- prompt and prefill ----------------------------------------------------------------------
+
+def build_prompt(W: Weights, ids, language: str, speaker: torch.Tensor):
+    """The talker prompt of the reference (talker.hip:283-352): text rows are the role header
+    ids[0:3], the text ids[3:-5], then tts_bos / tts_eos / tts_pad, each a text_embedding row
+    through text_projection (fc1 + bias, SiLU, fc2 + bias). Codec rows: the think block
+    (nothink, think_bos, think_eos; or think, think_bos, language, think_eos), codec_pad,
+    codec_bos. Prefill rows: the 3 header rows; tts_pad + each think row; tts_pad + speaker;
+    tts_bos + codec_pad; first text row + codec_bos. Trailing rows: the other text rows,
+    then tts_eos. Returns (prefill [n, H], trailing [m, H], tts_pad [H])."""
+    c = W.cfg
+    ids = [int(i) for i in ids]
+    n_text = len(ids) - 8
+    assert n_text >= 1, "prompt ids too short"
+    tids = ids[:3] + ids[3:3 + n_text] + [c.tts_bos_id, c.tts_eos_id, c.tts_pad_id]
+    i_bos, i_eos, i_pad = len(tids) - 3, len(tids) - 2, len(tids) - 1
+    rows = W["talker.model.text_embedding.weight"][torch.tensor(tids)]
+    h = silu(rows @ W["talker.text_projection.linear_fc1.weight"].T + W["talker.text_projection.linear_fc1.bias"])
+    proj = h @ W["talker.text_projection.linear_fc2.weight"].T + W["talker.text_projection.linear_fc2.bias"]
+    langs = dict(c.languages)
+    if not language or language == "auto":
+        cids = [c.codec_nothink_id, c.codec_think_bos_id, c.codec_think_eos_id]
+    else:
+        cids = [c.codec_think_id, c.codec_think_bos_id, langs[language], c.codec_think_eos_id]
+    n_think = len(cids)
+    cids += [c.codec_pad_id, c.codec_bos_id]
+    codec = W["talker.model.codec_embedding.weight"][torch.tensor(cids)]
+    pre = [proj[0], proj[1], proj[2]]
+    pre += [proj[i_pad] + codec[r] for r in range(n_think)]
+    pre += [proj[i_pad] + speaker, proj[i_bos] + codec[n_think], proj[3] + codec[n_think + 1]]
+    trailing = [proj[3 + r] for r in range(1, n_text)] + [proj[i_eos]]
+    return torch.stack(pre), torch.stack(trailing), proj[i_pad].clone()
+
+
+def prefill(W: Weights, rows: torch.Tensor, kv: list):
+    """The talker prefill (talker.hip:355-399): rows [T, H] at positions 0..T-1 through all
+    layers, causally, filling kv (per layer (kcache, vcache), f16-rounded, K after RoPE).
+    Returns (post-norm hidden of the last row [H], its codec logits [V])."""
+    x = rows.clone()
+    for l in range(W.tl.n_layer):
+        x = decoder_layer(W, "talker", l, x, kv[l][0], kv[l][1], 0)
+    hidden = rmsnorm(x[-1], W["talker.model.norm.weight"], W.tl.eps)
+    return hidden, W["talker.codec_head.weight"] @ hidden
+
+
 # --- sampling (bit-exact C restatement) -----------------------------------------------------
 
 class _SampleArgs(ctypes.Structure):
