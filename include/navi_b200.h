@@ -198,6 +198,27 @@ int navi_frame_set_step_in(navi_frame * f, const float * d_step);
 int navi_frame_grid_blocks(const navi_frame * f);
 void navi_frame_destroy(navi_frame * f);
 
+/* ---- graph: replaces navi::qwen3tts::Graph (model/qwen3tts/graph.h:22-79) ---------------- */
+
+typedef struct navi_graph navi_graph;
+
+typedef struct navi_synth_stats {   /* SynthStats, graph.h:36-41 */
+    int n_tokens, n_frames, hit_cap, eos;
+    double prefill_ms, frames_ms, total_ms;
+    double ttfc_ms;                 /* time to the first frame's codes */
+} navi_synth_stats;
+
+/* Graph::load (graph.cpp:22-44) minus the tokenizer, vocoder and speaker encoder: a talker
+ * (prompts up to max_prompt_tokens, KV for max_prompt_tokens + max_frames + 1 positions) and a
+ * frame kernel on the uploaded weights. */
+int navi_graph_create(navi_device * dev, const navi_weights * w, const navi_frame_opts * opts, int max_prompt_tokens, int max_frames,
+                      navi_graph ** out);
+/* Graph::synth (graph.cpp:52-111) from token ids (see navi_talker_build_prompt): writes the 16
+ * codes of each frame to codes[16 * i] (room for codes_cap frames) until EOS or max_frames. */
+int navi_graph_synth_ids(navi_graph * g, const int32_t * ids, int n_ids, const char * language, const float * speaker,
+                         const navi_sampling * s, uint64_t seed, int max_frames, int32_t * codes, int codes_cap, navi_synth_stats * st);
+void navi_graph_destroy(navi_graph * g);
+
 /* Inspection of the last frame (host copies): the talker's post-norm hidden [hidden],
  * its codec logits [talker vocab], and the 15 code-predictor logit rows [15][cp vocab].
  * Any pointer may be NULL. The reference keeps these in its Work buffers (frame.hip:51-70). */

@@ -5,7 +5,9 @@
 #include "runtime.hpp"
 #include "sample_static.hpp"
 #include "talker.hpp"
+#include "graph.hpp"
 
+#include <algorithm>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -23,6 +25,10 @@ struct navi_frame {
 };
 struct navi_talker {
     std::unique_ptr<navi::qwen3tts::Talker> t;
+    int hidden = 0;
+};
+struct navi_graph {
+    std::unique_ptr<navi::qwen3tts::Graph> g;
     int hidden = 0;
 };
 
@@ -405,5 +411,54 @@ const float * navi_talker_hidden(const navi_talker * t) { return t ? t->t->d_hid
 const float * navi_talker_logits(const navi_talker * t) { return t ? t->t->d_logits() : nullptr; }
 double navi_talker_last_ms(const navi_talker * t) { return t ? t->t->last_ms() : 0.0; }
 void navi_talker_destroy(navi_talker * t) { delete t; }
+
+int navi_graph_create(navi_device * dev, const navi_weights * w, const navi_frame_opts * opts, int max_prompt_tokens, int max_frames,
+                      navi_graph ** out) {
+    return guard([&]() -> int {
+        if (!dev || !w || !out) return set_err(NAVI_E_ARG, "NULL argument");
+        navi::qwen3tts::FrameOptions fo;
+        if (opts) {
+            fo.blocks_per_mp = opts->blocks_per_mp;
+            if (opts->deadline_us) fo.deadline_us = opts->deadline_us;
+        }
+        auto g = std::make_unique<navi_graph>();
+        g->g = navi::qwen3tts::Graph::create(*dev->dev, *w->w, fo, max_prompt_tokens, max_frames);
+        g->hidden = w->w->params().talker.hidden;
+        *out = g.release();
+        return NAVI_OK;
+    });
+}
+
+int navi_graph_synth_ids(navi_graph * g, const int32_t * ids, int n_ids, const char * language, const float * speaker,
+                         const navi_sampling * s, uint64_t seed, int max_frames, int32_t * codes, int codes_cap, navi_synth_stats * st) {
+    return guard([&]() -> int {
+        if (!g || !ids || n_ids <= 0 || !speaker || !codes || codes_cap <= 0) return set_err(NAVI_E_ARG, "bad argument");
+        navi::qwen3tts::SynthRequest req;
+        req.ids = std::span<const std::int32_t>(ids, static_cast<size_t>(n_ids));
+        req.language = language ? language : "";
+        req.speaker = std::span<const float>(speaker, static_cast<size_t>(g->hidden));
+        req.seed = seed;
+        req.max_frames = std::min(max_frames, codes_cap);
+        req.sampling = to_sampling(s);
+        int n = 0;
+        const auto stats = g->g->synth(req, [&](const std::int32_t * c) {
+            std::memcpy(codes + static_cast<size_t>(n) * 16, c, 16 * sizeof(int32_t));
+            ++n;
+        });
+        if (st) {
+            st->n_tokens = stats.n_tokens;
+            st->n_frames = stats.n_frames;
+            st->hit_cap = stats.hit_cap ? 1 : 0;
+            st->eos = stats.eos ? 1 : 0;
+            st->prefill_ms = stats.prefill_ms;
+            st->frames_ms = stats.frames_ms;
+            st->total_ms = stats.total_ms;
+            st->ttfc_ms = stats.ttfc_ms;
+        }
+        return NAVI_OK;
+    });
+}
+
+void navi_graph_destroy(navi_graph * g) { delete g; }
 
 } // extern "C"

@@ -57,6 +57,11 @@ class Prompt(ctypes.Structure):
     _fields_ = [("prefill", c_void_p), ("trailing", c_void_p), ("tts_pad", c_void_p), ("n_prefill", c_int), ("n_trailing", c_int)]
 
 
+class SynthStats(ctypes.Structure):
+    _fields_ = [("n_tokens", c_int), ("n_frames", c_int), ("hit_cap", c_int), ("eos", c_int), ("prefill_ms", c_double),
+                ("frames_ms", c_double), ("total_ms", c_double), ("ttfc_ms", c_double)]
+
+
 class FrameOpts(ctypes.Structure):
     _fields_ = [("blocks_per_mp", c_int), ("deadline_us", c_uint64)]
 
@@ -101,6 +106,10 @@ SIGNATURES = [
     ("navi_frame_set_step_in", c_int, [c_void_p, c_void_p]),
     ("navi_frame_grid_blocks", c_int, [c_void_p]),
     ("navi_frame_destroy", None, [c_void_p]),
+    ("navi_graph_create", c_int, [c_void_p, c_void_p, POINTER(FrameOpts), c_int, c_int, POINTER(c_void_p)]),
+    ("navi_graph_synth_ids", c_int, [c_void_p, POINTER(c_int32), c_int, c_char_p, POINTER(c_float), POINTER(Sampling), c_uint64,
+                                     c_int, POINTER(c_int32), c_int, POINTER(SynthStats)]),
+    ("navi_graph_destroy", None, [c_void_p]),
     ("navi_frame_inspect", c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
     ("navi_frame_set_profile", c_int, [c_void_p, c_int, c_int]),
     ("navi_frame_profile", c_int, [c_void_p, POINTER(c_uint64), c_int, POINTER(c_int)]),

@@ -205,6 +205,39 @@ class Talker:
             pass
 
 
+class Graph:
+    """navi::qwen3tts::Graph (graph.h:43-79) from token ids: prompt, prefill and the frame loop."""
+
+    def __init__(self, dev: Device, w: Weights, max_prompt_tokens: int = 1024, max_frames: int = 2048, deadline_us: int = 0):
+        h = c_void_p()
+        opts = capi.FrameOpts(1, deadline_us)
+        check(lib().navi_graph_create(dev.h, w.h, byref(opts), max_prompt_tokens, max_frames, byref(h)))
+        self.h, self.dev, self.w = h, dev, w
+
+    def synth_ids(self, ids, language: str, speaker, s: Sampling, seed: int, max_frames: int):
+        """(codes [n_frames, 16] int32, stats) of one utterance."""
+        import numpy as np
+        ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+        spk = np.ascontiguousarray(np.asarray(speaker, dtype=np.float32))
+        codes = np.zeros((max_frames, 16), np.int32)
+        st = capi.SynthStats()
+        check(lib().navi_graph_synth_ids(self.h, ids.ctypes.data_as(POINTER(c_int32)), len(ids), (language or "").encode(),
+                                         spk.ctypes.data_as(POINTER(ctypes.c_float)), byref(s.c()), seed, max_frames,
+                                         codes.ctypes.data_as(POINTER(c_int32)), max_frames, byref(st)))
+        return codes[:st.n_frames], st
+
+    def close(self):
+        if self.h:
+            lib().navi_graph_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def _result(r: capi.FrameResult, st: int) -> FrameResult:
     err = "" if st == capi.NAVI_OK else lib().navi_last_error().decode(errors="replace")
     return FrameResult(bool(r.ok), bool(r.eos), list(r.codes), r.us, r.status if st == capi.NAVI_OK else st, err)
