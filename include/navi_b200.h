@@ -219,6 +219,54 @@ int navi_graph_synth_ids(navi_graph * g, const int32_t * ids, int n_ids, const c
                          const navi_sampling * s, uint64_t seed, int max_frames, int32_t * codes, int codes_cap, navi_synth_stats * st);
 void navi_graph_destroy(navi_graph * g);
 
+/* ---- vocoder: replaces navi::qwen3tts::Vocoder (model/qwen3tts/vocoder.h:27-55) ----------- */
+
+typedef struct navi_vocoder navi_vocoder;
+
+/* Vocoder::create (vocoder.hip:413-610): packs the codec decoder's weights into tensor-core
+ * tiles and sizes the scratch for chunks of up to max_chunk_frames frames. max_frames is
+ * accepted for interface parity (the attention ring needs window + max_chunk_frames rows). */
+int navi_vocoder_create(navi_device * dev, const navi_weights * w, int max_chunk_frames, int max_frames, navi_vocoder ** out);
+/* Vocoder::reset (vocoder.hip:612-630): zero every conv history and the position (new utterance). */
+int navi_vocoder_reset(navi_vocoder * v);
+/* Vocoder::decode (vocoder.hip:632-651): codes [n_frames][n_q] (host) -> n_frames *
+ * samples_per_frame f32 samples in [-1, 1] written to h_pcm (host, room for cap floats).
+ * Decodes in chunks of max_chunk_frames; state carries over to the next call. Code ids outside
+ * the codebook return NAVI_E_ARG before anything runs. */
+int navi_vocoder_decode(navi_vocoder * v, const int32_t * h_codes, int n_frames, float * h_pcm, size_t cap);
+int navi_vocoder_samples_per_frame(const navi_vocoder * v);
+int navi_vocoder_max_chunk_frames(const navi_vocoder * v);
+/* Vocoder::last_ms: device time of the last decode call (copies included). */
+double navi_vocoder_last_ms(const navi_vocoder * v);
+/* Vocoder::set_stage_hook (vocoder.h:50-53): fn(user, name, d_buf, rows, cols) after each stage
+ * (rvq, pre_conv, layer<l>, pre_transformer, up<j>, dec0, dec<b>, pcm), stream synchronised;
+ * d_buf is a device buffer valid during the call. fn NULL removes the hook. */
+typedef void (*navi_stage_fn)(void * user, const char * name, const float * d_buf, int rows, int cols);
+int navi_vocoder_set_stage_hook(navi_vocoder * v, navi_stage_fn fn, void * user);
+void navi_vocoder_destroy(navi_vocoder * v);
+
+/* The implicit-GEMM causal Conv1d of the vocoder on its own (the reference's k_conv,
+ * kernels.h:72-242, with its ConvArgs), on device buffers:
+ *   y[t][co] = epi(bias[co] + sum_j sum_ci W[co][ci][j] * pro(x~[t - (K-1-j) dil][ci]))
+ * with x~ = the T input rows (row stride x_stride) preceded by the H = (K-1) dil rows of hist
+ * ([H][Cin], NULL = zeros). trans_stride > 0 instead takes w as a ConvTranspose1d weight
+ * [Cin][Cout][K * trans_stride] of that stride, giving output rows t * stride + phase
+ * (vocoder.hip:373-385; y must then be dense, y_stride = Cout * stride). Prologue: 0 none,
+ * 1 SnakeBeta (snake_a = e^alpha, snake_b = 1/(e^beta + 1e-9)), 2 silu(x[:, :Cin]) *
+ * x[:, Cin:2Cin]. Epilogue: 0 none, 1 erf GELU, 2 + resid, 3 * scale + resid (resid rows
+ * [T][y_stride]). Cin % 8 == 0, x_stride % 4 == 0, 16-byte aligned x / hist. Packs the weight
+ * and allocates its workspace on every call: a primitive for tests and tools, not the hot path. */
+typedef struct navi_conv_args {
+    const uint16_t * w;            /* f16 bits */
+    int Cout, Cin, K, dil, trans_stride;
+    const float * x; int x_stride, T;
+    const float * hist;
+    int pro; const float * snake_a, * snake_b;
+    int epi; const float * bias, * resid, * scale;
+    float * y; int y_stride;
+} navi_conv_args;
+int navi_conv1d(navi_device * dev, const navi_conv_args * a);
+
 /* Inspection of the last frame (host copies): the talker's post-norm hidden [hidden],
  * its codec logits [talker vocab], and the 15 code-predictor logit rows [15][cp vocab].
  * Any pointer may be NULL. The reference keeps these in its Work buffers (frame.hip:51-70). */

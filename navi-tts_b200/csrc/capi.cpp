@@ -6,6 +6,8 @@
 #include "sample_static.hpp"
 #include "talker.hpp"
 #include "graph.hpp"
+#include "vocoder.hpp"
+#include "conv_api.hpp"
 
 #include <algorithm>
 #include <cstring>
@@ -30,6 +32,10 @@ struct navi_talker {
 struct navi_graph {
     std::unique_ptr<navi::qwen3tts::Graph> g;
     int hidden = 0;
+};
+struct navi_vocoder {
+    std::unique_ptr<navi::qwen3tts::Vocoder> v;
+    int n_q = 0;
 };
 
 namespace {
@@ -460,5 +466,58 @@ int navi_graph_synth_ids(navi_graph * g, const int32_t * ids, int n_ids, const c
 }
 
 void navi_graph_destroy(navi_graph * g) { delete g; }
+
+int navi_vocoder_create(navi_device * dev, const navi_weights * w, int max_chunk_frames, int max_frames, navi_vocoder ** out) {
+    return guard([&]() -> int {
+        if (!dev || !w || !out) return set_err(NAVI_E_ARG, "NULL argument");
+        auto v = std::make_unique<navi_vocoder>();
+        v->v = navi::qwen3tts::Vocoder::create(*dev->dev, *w->w, max_chunk_frames, max_frames);
+        v->n_q = w->w->params().vq_n_q;
+        *out = v.release();
+        return NAVI_OK;
+    });
+}
+
+int navi_vocoder_reset(navi_vocoder * v) {
+    return guard([&]() -> int {
+        if (!v) return set_err(NAVI_E_ARG, "NULL argument");
+        v->v->reset();
+        return NAVI_OK;
+    });
+}
+
+int navi_vocoder_decode(navi_vocoder * v, const int32_t * h_codes, int n_frames, float * h_pcm, size_t cap) {
+    return guard([&]() -> int {
+        if (!v || (n_frames > 0 && (!h_codes || !h_pcm)) || n_frames < 0) return set_err(NAVI_E_ARG, "bad argument");
+        const size_t need = static_cast<size_t>(n_frames) * static_cast<size_t>(v->v->samples_per_frame());
+        if (cap < need) return set_err(NAVI_E_ARG, "pcm buffer smaller than n_frames * samples_per_frame");
+        v->v->decode_into(std::span<const std::int32_t>(h_codes, static_cast<size_t>(n_frames) * v->n_q), n_frames, h_pcm);
+        return NAVI_OK;
+    });
+}
+
+int navi_vocoder_samples_per_frame(const navi_vocoder * v) { return v ? v->v->samples_per_frame() : 0; }
+int navi_vocoder_max_chunk_frames(const navi_vocoder * v) { return v ? v->v->max_chunk_frames() : 0; }
+double navi_vocoder_last_ms(const navi_vocoder * v) { return v ? v->v->last_ms() : 0.0; }
+
+int navi_vocoder_set_stage_hook(navi_vocoder * v, navi_stage_fn fn, void * user) {
+    return guard([&]() -> int {
+        if (!v) return set_err(NAVI_E_ARG, "NULL argument");
+        if (!fn) v->v->set_stage_hook({});
+        else v->v->set_stage_hook([fn, user](const char * name, const float * d, int rows, int cols) { fn(user, name, d, rows, cols); });
+        return NAVI_OK;
+    });
+}
+
+void navi_vocoder_destroy(navi_vocoder * v) { delete v; }
+
+int navi_conv1d(navi_device * dev, const navi_conv_args * a) {
+    return guard([&]() -> int {
+        if (!dev || !a || !a->w || !a->x || !a->y) return set_err(NAVI_E_ARG, "NULL argument");
+        if (a->Cout <= 0 || a->Cin <= 0 || a->K <= 0 || a->dil <= 0 || a->T < 0 || a->trans_stride < 0) return set_err(NAVI_E_ARG, "bad shape");
+        if (a->trans_stride > 0 && (a->hist ? a->dil != 1 : false)) return set_err(NAVI_E_ARG, "transposed conv has dilation 1");
+        return navi::conv_once(*dev->dev, *a);
+    });
+}
 
 } // extern "C"

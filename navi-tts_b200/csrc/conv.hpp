@@ -1,0 +1,99 @@
+// Implicit-GEMM causal Conv1d on the sm_100a tensor cores (tcgen05, accumulator in
+// tensor memory): the vocoder's convolutions, transposed convolutions and linear layers
+// (reference: model/qwen3tts/kernels.h:72-242, k_conv, and its ConvArgs).
+//
+//   y[t][co] = epi( bias[co] + sum_j sum_ci W[co][ci][j] * pro(x~[t - (K-1-j) dil][ci]) )
+//
+// x~[r] is row r of the input for r >= 0 and row H + r of the conv's history ([H][Cin],
+// H = (K-1) dil, zeros when absent) for r < 0.  A transposed conv of stride s is the same
+// sum with its s phases folded into the output channels (co' = phase * Cout + co, rows
+// t * s + phase of a dense output), so it needs no special case here.
+//
+// GEMM view per CTA: D[co][t] (128 channels x BN rows, f32 in tensor memory) accumulates
+// over (channel block of 64, tap): A = a 128 x 64 tile of the packed weights (bulk copy
+// from global), B = the input window rows [t0 - H, t0 + BN) of that channel block in
+// shared memory, read by tap j at a start row shifted by j * dil.  Activations enter the
+// MMA as two f16 halves (hi = f16(v), lo = f16(v - hi)) against f16 weights, so the
+// products keep ~21 bits of the f32 activation.
+#pragma once
+
+#include "runtime.hpp"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <vector>
+
+namespace navi::conv {
+
+enum Pro : int { PRO_NONE = 0, PRO_SNAKE = 1, PRO_SILU_GATE = 2 };
+enum Epi : int { EPI_NONE = 0, EPI_GELU = 1, EPI_RESIDUAL = 2, EPI_SCALE_RESIDUAL = 3 };
+
+constexpr int BM = 128;                      // output channels per tile (MMA M)
+constexpr int BK = 64;                       // input channels per block
+constexpr int TILE_ELEMS = BM * BK;          // one packed weight tile: [8 k chunks][128 co][8]
+constexpr int TILE_BYTES = TILE_ELEMS * 2;
+constexpr int NSTAGE = 4;                    // weight tiles in flight per CTA
+constexpr int NTHREADS = 192;                // warp 0 weights, warp 1 MMA, warps 2-5 window + epilogue
+
+// One source block of a packed weight.  Logical weight W(co, tap, ci) for co in
+// [co0, co1), ci in [ci0, ci1):
+//   direct:  p[(co - co0) s_co + (ci - ci0) s_ci + tap s_tap]
+//   trans:   p is a ConvTranspose1d weight [ci][cout_b][k] of stride `stride`; with
+//            c = co - co0, phase = c / cout_b, m = taps - 1 - tap:
+//            p[(ci - ci0) cout_b k + (c % cout_b) k + phase + m stride]   (vocoder.hip:373-385)
+struct PackSrc {
+    const __half * p = nullptr;
+    int co0 = 0, co1 = 0, ci0 = 0, ci1 = 0;
+    long long s_co = 0, s_ci = 0, s_tap = 0;
+    int trans = 0, cout_b = 0, k = 0, stride = 0;
+};
+constexpr int MAX_PACK_SRC = 4;
+
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+inline std::size_t packed_elems(int Cout, int Cin, int K) {
+    return static_cast<std::size_t>(ceil_div(Cout, BM)) * ceil_div(Cin, BK) * K * TILE_ELEMS;
+}
+// Writes the packed tiles of a [Cout][K][Cin] logical weight (zero outside every source).
+void pack(const std::vector<PackSrc> & srcs, int Cout, int Cin, int K, __half * dst, cudaStream_t stream);
+
+struct Conv {
+    const __half * w = nullptr;              // packed tiles
+    int Cout = 0, Cin = 0, K = 1, dil = 1;
+    const float * x = nullptr;               // rows [T][x_stride]; SILU_GATE: row = [gate | up], Cin each
+    int x_stride = 0, T = 0;
+    const float * hist = nullptr;            // [H][Cin] or null
+    int pro = PRO_NONE;
+    const float * snake_a = nullptr, * snake_b = nullptr;   // e^alpha, 1/(e^beta + 1e-9)   [Cin]
+    int epi = EPI_NONE;
+    const float * bias = nullptr;            // [Cout] or null
+    const float * resid = nullptr;           // EPI_RESIDUAL / EPI_SCALE_RESIDUAL: rows [T][r_stride]
+    int r_stride = 0;
+    const float * scale = nullptr;           // EPI_SCALE_RESIDUAL: [Cout]
+    float * y = nullptr;                     // rows [T][y_stride]
+    int y_stride = 0;
+};
+
+struct Plan {
+    int BN = 16, NT = 1, MT = 1, CB = 1, splits = 1, cb_per_split = 1, lbo = 0, tmem_cols = 32;
+    std::size_t smem = 0;
+};
+Plan plan(const Conv & c, int sms);
+
+struct Workspace {
+    float * partial = nullptr;               // split-K partial sums
+    std::size_t partial_cap = 0;             // elements
+    unsigned * counters = nullptr;           // per output tile, zero between launches
+    int n_counters = 0;
+    int * err = nullptr;                     // set to 1 by a CTA whose wait timed out
+    unsigned long long timeout_ns = 2000000000ull;
+};
+// Elements of partial storage and counters a launch of `c` needs.
+std::size_t partial_need(const Conv & c, int sms);
+int counters_need(const Conv & c, int sms);
+
+void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream);
+
+} // namespace navi::conv

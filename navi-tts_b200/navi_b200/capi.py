@@ -62,6 +62,16 @@ class SynthStats(ctypes.Structure):
                 ("frames_ms", c_double), ("total_ms", c_double), ("ttfc_ms", c_double)]
 
 
+class ConvArgs(ctypes.Structure):
+    _fields_ = [("w", c_void_p), ("Cout", c_int), ("Cin", c_int), ("K", c_int), ("dil", c_int), ("trans_stride", c_int),
+                ("x", c_void_p), ("x_stride", c_int), ("T", c_int), ("hist", c_void_p), ("pro", c_int), ("snake_a", c_void_p),
+                ("snake_b", c_void_p), ("epi", c_int), ("bias", c_void_p), ("resid", c_void_p), ("scale", c_void_p),
+                ("y", c_void_p), ("y_stride", c_int)]
+
+
+STAGE_FN = ctypes.CFUNCTYPE(None, c_void_p, c_char_p, c_void_p, c_int, c_int)
+
+
 class FrameOpts(ctypes.Structure):
     _fields_ = [("blocks_per_mp", c_int), ("deadline_us", c_uint64)]
 
@@ -110,6 +120,15 @@ SIGNATURES = [
     ("navi_graph_synth_ids", c_int, [c_void_p, POINTER(c_int32), c_int, c_char_p, POINTER(c_float), POINTER(Sampling), c_uint64,
                                      c_int, POINTER(c_int32), c_int, POINTER(SynthStats)]),
     ("navi_graph_destroy", None, [c_void_p]),
+    ("navi_vocoder_create", c_int, [c_void_p, c_void_p, c_int, c_int, POINTER(c_void_p)]),
+    ("navi_vocoder_reset", c_int, [c_void_p]),
+    ("navi_vocoder_decode", c_int, [c_void_p, POINTER(c_int32), c_int, POINTER(c_float), ctypes.c_size_t]),
+    ("navi_vocoder_samples_per_frame", c_int, [c_void_p]),
+    ("navi_vocoder_max_chunk_frames", c_int, [c_void_p]),
+    ("navi_vocoder_last_ms", c_double, [c_void_p]),
+    ("navi_vocoder_set_stage_hook", c_int, [c_void_p, STAGE_FN, c_void_p]),
+    ("navi_vocoder_destroy", None, [c_void_p]),
+    ("navi_conv1d", c_int, [c_void_p, POINTER(ConvArgs)]),
     ("navi_frame_inspect", c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
     ("navi_frame_set_profile", c_int, [c_void_p, c_int, c_int]),
     ("navi_frame_profile", c_int, [c_void_p, POINTER(c_uint64), c_int, POINTER(c_int)]),

@@ -238,6 +238,77 @@ class Graph:
             pass
 
 
+class Vocoder:
+    """navi::qwen3tts::Vocoder (vocoder.h:27-55): codes [T][n_q] -> PCM [T * samples_per_frame]."""
+
+    def __init__(self, dev: Device, w: Weights, max_chunk_frames: int = 32, max_frames: int = 4096):
+        h = c_void_p()
+        check(lib().navi_vocoder_create(dev.h, w.h, max_chunk_frames, max_frames, byref(h)))
+        self.h, self.dev, self.w = h, dev, w
+        self.n_q = w.params.vq_n_q
+        self._hook = None
+
+    @property
+    def samples_per_frame(self) -> int:
+        return lib().navi_vocoder_samples_per_frame(self.h)
+
+    @property
+    def max_chunk_frames(self) -> int:
+        return lib().navi_vocoder_max_chunk_frames(self.h)
+
+    @property
+    def last_ms(self) -> float:
+        return lib().navi_vocoder_last_ms(self.h)
+
+    def reset(self) -> None:
+        check(lib().navi_vocoder_reset(self.h))
+
+    def decode(self, codes, n_frames: int | None = None):
+        """float32 numpy PCM of the frames (decoder state carries over between calls)."""
+        import numpy as np
+        codes = np.ascontiguousarray(np.asarray(codes, dtype=np.int32).reshape(-1, self.n_q))
+        n = codes.shape[0] if n_frames is None else n_frames
+        out = np.empty(max(n, 0) * self.samples_per_frame, np.float32)
+        check(lib().navi_vocoder_decode(self.h, codes.ctypes.data_as(POINTER(c_int32)), n,
+                                        out.ctypes.data_as(POINTER(ctypes.c_float)), out.size))
+        return out
+
+    def set_stage_hook(self, fn) -> None:
+        """fn(name: str, device_ptr: int, rows: int, cols: int) after each stage; None removes it."""
+        if fn is None:
+            self._hook = None
+            check(lib().navi_vocoder_set_stage_hook(self.h, capi.STAGE_FN(), None))
+            return
+        self._hook = capi.STAGE_FN(lambda _u, name, d, r, c: fn(name.decode(), d, r, c))
+        check(lib().navi_vocoder_set_stage_hook(self.h, self._hook, None))
+
+    def close(self):
+        if self.h:
+            lib().navi_vocoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+PRO_NONE, PRO_SNAKE, PRO_SILU_GATE = 0, 1, 2
+EPI_NONE, EPI_GELU, EPI_RESIDUAL, EPI_SCALE_RESIDUAL = 0, 1, 2, 3
+
+
+def conv1d(dev: Device, w_ptr: int, Cout: int, Cin: int, K: int, x_ptr: int, T: int, y_ptr: int, *, dil: int = 1,
+           trans_stride: int = 0, x_stride: int | None = None, hist_ptr: int = 0, pro: int = PRO_NONE, snake_a: int = 0,
+           snake_b: int = 0, epi: int = EPI_NONE, bias: int = 0, resid: int = 0, scale: int = 0, y_stride: int | None = None) -> None:
+    """navi_conv1d on device pointers (the implicit-GEMM conv primitive)."""
+    P = trans_stride if trans_stride > 0 else 1
+    a = capi.ConvArgs(w_ptr, Cout, Cin, K, dil, trans_stride, x_ptr, Cin if x_stride is None else x_stride, T, hist_ptr or None,
+                      pro, snake_a or None, snake_b or None, epi, bias or None, resid or None, scale or None, y_ptr,
+                      Cout * P if y_stride is None else y_stride)
+    check(lib().navi_conv1d(dev.h, byref(a)))
+
+
 def _result(r: capi.FrameResult, st: int) -> FrameResult:
     err = "" if st == capi.NAVI_OK else lib().navi_last_error().decode(errors="replace")
     return FrameResult(bool(r.ok), bool(r.eos), list(r.codes), r.us, r.status if st == capi.NAVI_OK else st, err)
