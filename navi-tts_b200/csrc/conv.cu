@@ -1,16 +1,18 @@
 // Implicit-GEMM causal Conv1d on tcgen05 (see conv.hpp for the math and the GEMM view).
 //
-// CTA = 6 warps:
-//   warp 0      one lane streams the CTA's weight tiles (16 KB each, one per (channel
+// Persistent CTA (one per SM at most) over work units = (row tile, channel tile, K split),
+// 10 warps:
+//   warp 0      one lane streams the units' weight tiles (16 KB each, one per (channel
 //               block, tap)) into a 4-deep shared-memory ring with bulk copies;
-//   warp 1      allocates the tensor-memory accumulator; one lane issues the MMAs
-//               (M = 128 channels, N = BN rows, K = 16) and commits their completion
-//               to the ring's and the window's "empty" barriers;
+//   warp 1      allocates two tensor-memory accumulators (2 x BN columns); one lane
+//               issues the MMAs (M = 128 channels, N = BN rows, K = 16) and commits their
+//               completion to the ring's, the window's and the accumulator's barriers;
 //   warps 2-5   stage the input window of each channel block (history / input rows,
-//               prologue, f16 hi/lo split) into one of two window buffers, then run the
-//               epilogue: tensor-memory loads (warp w reads lanes 32 (w % 4) ..), bias,
+//               prologue, f16 hi/lo split) into one of two window buffers;
+//   warps 6-9   epilogue: tensor-memory loads (warp w reads lanes 32 (w % 4) ..), bias,
 //               activation / residual, stores; with split-K the CTA that finishes a
 //               tile last sums the partials in split order (deterministic).
+// So unit n's epilogue, unit n+1's MMAs and unit n+2's window staging overlap.
 // Every mbarrier wait is bounded by a deadline; a CTA that passes it sets the error
 // word, stops waiting (its remaining waits return at once) and still frees its
 // tensor memory.
@@ -38,19 +40,17 @@ struct KArgs {
     const __half * w;
     const float * x, * hist, * sa, * sb, * bias, * resid, * scale;
     float * y, * partial;
-    unsigned * counters;
     int * err;
     int Cout, Cin, K, dil, H, T, x_stride, y_stride, r_stride;
-    int BN, CB, cb_per_split, splits;
+    int BN, NT, MT, CB, cb_per_split, splits;
     int lbo, wrows, tmem_cols;
     unsigned long long timeout_ns;
 };
 
 struct Bars {
-    uint64_t wfull[NSTAGE], wempty[NSTAGE], afull[2], aempty[2], done;
+    uint64_t wfull[NSTAGE], wempty[NSTAGE], afull[2], aempty[2], tfull[2], tempty[2], edone;
     uint32_t tmem;
     int abort;
-    int last;
 };
 static_assert(sizeof(Bars) <= BARS_BYTES, "barrier block");
 
@@ -73,16 +73,12 @@ __device__ bool bwait(uint64_t * bar, uint32_t parity, Bars & B, const KArgs & a
     }
 }
 
+// v already includes the bias; r is the residual row value, sc the channel's layer scale.
 template <int EPI>
-__device__ __forceinline__ float finish(float v, const KArgs & a, int t, int co) {
-    if (a.bias) v += a.bias[co];
-    if (EPI == EPI_GELU) {
-        v = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
-    } else if (EPI == EPI_RESIDUAL) {
-        v += a.resid[static_cast<std::size_t>(t) * a.r_stride + co];
-    } else if (EPI == EPI_SCALE_RESIDUAL) {
-        v = v * a.scale[co] + a.resid[static_cast<std::size_t>(t) * a.r_stride + co];
-    }
+__device__ __forceinline__ float finish(float v, float sc, float r) {
+    if (EPI == EPI_GELU) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+    if (EPI == EPI_RESIDUAL) return v + r;
+    if (EPI == EPI_SCALE_RESIDUAL) return v * sc + r;
     return v;
 }
 
@@ -92,52 +88,117 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 }
 
 // Stages one channel block's window: rows r = u/8, u/8 + 16, ... of k chunk u % 8.
+// Loads are issued SROWS rows at a time (read-only path) before any is used, so each
+// thread keeps SROWS x 32 bytes in flight.
+constexpr int SROWS = 8;
+
 template <int PRO>
 __device__ __forceinline__ void stage_window(const KArgs & a, uint8_t * hi, uint8_t * lo, int c0, int t0, int u) {
     const bool valid = c0 < a.Cin;   // Cin % 8 == 0: a chunk is wholly inside or outside
     float ca[8], cb[8];
     if (PRO == PRO_SNAKE && valid) {
-        const float4 a0 = *reinterpret_cast<const float4 *>(a.sa + c0), a1 = *reinterpret_cast<const float4 *>(a.sa + c0 + 4);
-        const float4 b0 = *reinterpret_cast<const float4 *>(a.sb + c0), b1 = *reinterpret_cast<const float4 *>(a.sb + c0 + 4);
+        const float4 a0 = __ldg(reinterpret_cast<const float4 *>(a.sa + c0)), a1 = __ldg(reinterpret_cast<const float4 *>(a.sa + c0 + 4));
+        const float4 b0 = __ldg(reinterpret_cast<const float4 *>(a.sb + c0)), b1 = __ldg(reinterpret_cast<const float4 *>(a.sb + c0 + 4));
         ca[0] = a0.x; ca[1] = a0.y; ca[2] = a0.z; ca[3] = a0.w; ca[4] = a1.x; ca[5] = a1.y; ca[6] = a1.z; ca[7] = a1.w;
         cb[0] = b0.x; cb[1] = b0.y; cb[2] = b0.z; cb[3] = b0.w; cb[4] = b1.x; cb[5] = b1.y; cb[6] = b1.z; cb[7] = b1.w;
     }
-    for (int r = u >> 3; r < a.wrows; r += 16) {
-        const int gr = t0 - a.H + r;
-        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (valid) {
-            const float * src = nullptr;
-            if (gr >= 0 && gr < a.T) src = a.x + static_cast<std::size_t>(gr) * a.x_stride + c0;
-            else if (gr < 0 && a.hist) src = a.hist + static_cast<std::size_t>(a.H + gr) * a.Cin + c0;
-            if (src) {
-                const float4 p0 = *reinterpret_cast<const float4 *>(src), p1 = *reinterpret_cast<const float4 *>(src + 4);
-                v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w; v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
-                if (PRO == PRO_SILU_GATE) {
-                    const float4 q0 = *reinterpret_cast<const float4 *>(src + a.Cin), q1 = *reinterpret_cast<const float4 *>(src + a.Cin + 4);
-                    const float up[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    for (int rb = u >> 3; rb < a.wrows; rb += 16 * SROWS) {
+        float4 p0[SROWS], p1[SROWS], q0[SROWS], q1[SROWS];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) v[i] = v[i] / (1.f + expf(-v[i])) * up[i];
-                }
+        for (int k = 0; k < SROWS; ++k) {
+            const int r = rb + 16 * k, gr = t0 - a.H + r;
+            const float * src = nullptr;
+            if (valid && r < a.wrows) {
+                if (gr >= 0 && gr < a.T) src = a.x + static_cast<std::size_t>(gr) * a.x_stride + c0;
+                else if (gr < 0 && a.hist) src = a.hist + static_cast<std::size_t>(a.H + gr) * a.Cin + c0;
             }
-            if (PRO == PRO_SNAKE) {
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            p0[k] = src ? __ldg(reinterpret_cast<const float4 *>(src)) : z;
+            p1[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + 4)) : z;
+            if (PRO == PRO_SILU_GATE) {
+                q0[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + a.Cin)) : z;
+                q1[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + a.Cin + 4)) : z;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < SROWS; ++k) {
+            const int r = rb + 16 * k;
+            if (r >= a.wrows) break;
+            float v[8] = {p0[k].x, p0[k].y, p0[k].z, p0[k].w, p1[k].x, p1[k].y, p1[k].z, p1[k].w};
+            if (PRO == PRO_SILU_GATE) {
+                const float up[8] = {q0[k].x, q0[k].y, q0[k].z, q0[k].w, q1[k].x, q1[k].y, q1[k].z, q1[k].w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = v[i] / (1.f + __expf(-v[i])) * up[i];
+            }
+            if (PRO == PRO_SNAKE && valid) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const float s = sinf(v[i] * ca[i]);
-                    v[i] += s * s * cb[i];
+                    const float sn = __sinf(v[i] * ca[i]);
+                    v[i] += sn * sn * cb[i];
                 }
             }
-        }
-        float h[8], l[8];
+            float h[8], l[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            h[i] = __half2float(__float2half_rn(v[i]));
-            l[i] = v[i] - h[i];
+            for (int i = 0; i < 8; ++i) {
+                h[i] = __half2float(__float2half_rn(v[i]));
+                l[i] = v[i] - h[i];
+            }
+            *reinterpret_cast<uint4 *>(hi + r * 16) = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]), pack_h2(h[6], h[7]));
+            *reinterpret_cast<uint4 *>(lo + r * 16) = make_uint4(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]), pack_h2(l[4], l[5]), pack_h2(l[6], l[7]));
         }
-        *reinterpret_cast<uint4 *>(hi + r * 16) = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]), pack_h2(h[6], h[7]));
-        *reinterpret_cast<uint4 *>(lo + r * 16) = make_uint4(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]), pack_h2(l[4], l[5]), pack_h2(l[6], l[7]));
     }
 }
 
+// Work unit u (row tile nt fastest, then channel tile mt, then split sp).
+struct Unit {
+    int t0, mt, sp, c_begin, nc;
+};
+__device__ __forceinline__ Unit unit_of(const KArgs & a, int u) {
+    Unit w;
+    const int nt = u % a.NT, r = u / a.NT;
+    w.mt = r % a.MT;
+    w.sp = r / a.MT;
+    w.t0 = nt * a.BN;
+    w.c_begin = w.sp * a.cb_per_split;
+    w.nc = min(a.CB, w.c_begin + a.cb_per_split) - w.c_begin;
+    return w;
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_unit(const KArgs & a, const Unit & w, uint32_t tacc, int q, int lane, bool ok) {
+    const int co = w.mt * BM + q * 32 + lane;
+    const bool live = ok && co < a.Cout;
+    const float bco = (a.bias && live && a.splits == 1) ? a.bias[co] : 0.f;
+    const float sco = (EPI == EPI_SCALE_RESIDUAL && live) ? a.scale[co] : 1.f;
+    const uint32_t tq = tacc + (static_cast<uint32_t>(q * 32) << 16);
+    for (int cc = 0; cc < a.BN; cc += 16) {
+        float v[16];
+        __syncwarp();                        // tcgen05.ld is warp-collective (.sync.aligned)
+        umma::tmem_ld16(tq + cc, v);
+        const int nv = min(16, a.T - (w.t0 + cc));
+        if (live && a.splits > 1) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if (i < nv) a.partial[(static_cast<std::size_t>(w.sp) * a.T + w.t0 + cc + i) * a.Cout + co] = v[i];
+        } else if (live) {
+            float rr[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                rr[i] = 0.f;
+                if ((EPI == EPI_RESIDUAL || EPI == EPI_SCALE_RESIDUAL) && i < nv)
+                    rr[i] = a.resid[static_cast<std::size_t>(w.t0 + cc + i) * a.r_stride + co];
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if (i < nv) a.y[static_cast<std::size_t>(w.t0 + cc + i) * a.y_stride + co] = finish<EPI>(v[i] + bco, sco, rr[i]);
+        }
+    }
+    __syncwarp();
+}
+
+// Persistent: CTA b takes units b, b + grid, ...; every role walks the same unit list,
+// so the weight ring, the two window buffers and the two accumulators run as pipelines
+// across unit boundaries.
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -147,9 +208,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
     Bars & B = *reinterpret_cast<Bars *>(win + 4 * win_bytes);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int t0 = blockIdx.x * a.BN, mt = blockIdx.y, sp = blockIdx.z;
-    const int c_begin = sp * a.cb_per_split, c_end = min(a.CB, c_begin + a.cb_per_split);
-    const int NC = c_end - c_begin;
+    const int n_units = a.NT * a.MT * a.splits;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSTAGE; ++i) {
@@ -159,13 +218,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&B.afull[i], 128);
             mbar_init(&B.aempty[i], 1);
+            mbar_init(&B.tfull[i], 1);
+            mbar_init(&B.tempty[i], 128);
         }
-        mbar_init(&B.done, 1);
+        mbar_init(&B.edone, 128);
         B.abort = 0;
-        B.last = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
+        __syncwarp();
         umma::tmem_alloc(&B.tmem, a.tmem_cols);
         umma::tmem_relinquish();
     }
@@ -176,102 +237,123 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
 
     if (warp == 0) {
         if (lane == 0) {
-            const __half * wt = a.w + static_cast<std::size_t>(mt) * a.CB * a.K * TILE_ELEMS;
-            const int NIT = NC * a.K;
-            for (int it = 0; it < NIT; ++it) {
-                const int s = it % NSTAGE;
-                if (it >= NSTAGE && !bwait(&B.wempty[s], ((it / NSTAGE) - 1) & 1, B, a)) break;
-                mbar_arrive_expect_tx(&B.wfull[s], TILE_BYTES);
-                const int c = c_begin + it / a.K, j = it % a.K;
-                bulk_g2s(ring + s * TILE_BYTES, wt + (static_cast<std::size_t>(c) * a.K + j) * TILE_ELEMS, TILE_BYTES, &B.wfull[s]);
+            int it = 0;
+            for (int un = blockIdx.x; un < n_units; un += gridDim.x) {
+                const Unit w = unit_of(a, un);
+                const __half * wt = a.w + (static_cast<std::size_t>(w.mt) * a.CB + w.c_begin) * a.K * TILE_ELEMS;
+                const int nit = w.nc * a.K;   // tiles of this unit are contiguous
+                for (int i = 0; i < nit; ++i, ++it) {
+                    const int s = it % NSTAGE;
+                    if (it >= NSTAGE && !bwait(&B.wempty[s], ((it / NSTAGE) - 1) & 1, B, a)) break;
+                    mbar_arrive_expect_tx(&B.wfull[s], TILE_BYTES);
+                    bulk_g2s(ring + s * TILE_BYTES, wt + static_cast<std::size_t>(i) * TILE_ELEMS, TILE_BYTES, &B.wfull[s]);
+                }
             }
             // tail: every issued tile has been consumed before the CTA may exit
-            for (int it = max(0, NIT - NSTAGE); it < NIT; ++it) bwait(&B.wempty[it % NSTAGE], (it / NSTAGE) & 1, B, a);
+            for (int k = max(0, it - NSTAGE); k < it; ++k) bwait(&B.wempty[k % NSTAGE], (k / NSTAGE) & 1, B, a);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t idesc = umma::idesc_f16_f32(BM, a.BN);
             const uint32_t ring_a = smem_addr(ring), win_a = smem_addr(win);
-            int it = 0;
-            for (int ci = 0; ci < NC; ++ci) {
-                const int b = ci & 1;
-                if (!bwait(&B.afull[b], (ci >> 1) & 1, B, a)) break;
+            int it = 0, cg = 0, k = 0;
+            for (int un = blockIdx.x; un < n_units; un += gridDim.x, ++k) {
+                const Unit w = unit_of(a, un);
+                const int acc = k & 1;
+                if (k >= 2 && !bwait(&B.tempty[acc], ((k >> 1) - 1) & 1, B, a)) break;
                 umma::fence_after_sync();
-                const uint32_t hi_a = win_a + (b * 2) * win_bytes, lo_a = hi_a + win_bytes;
-                for (int j = 0; j < a.K; ++j, ++it) {
-                    const int s = it % NSTAGE;
-                    if (!bwait(&B.wfull[s], (it / NSTAGE) & 1, B, a)) break;
+                const uint32_t d = tmem + static_cast<uint32_t>(acc * a.BN);
+                bool first = true;
+                for (int ci = 0; ci < w.nc; ++ci, ++cg) {
+                    const int b = cg & 1;
+                    if (!bwait(&B.afull[b], (cg >> 1) & 1, B, a)) break;
                     umma::fence_after_sync();
-                    const uint32_t sa = ring_a + s * TILE_BYTES;
-                    const uint32_t shift = static_cast<uint32_t>(j * a.dil * 16);
+                    const uint32_t hi_a = win_a + (b * 2) * win_bytes, lo_a = hi_a + win_bytes;
+                    for (int j = 0; j < a.K; ++j, ++it) {
+                        const int s = it % NSTAGE;
+                        if (!bwait(&B.wfull[s], (it / NSTAGE) & 1, B, a)) break;
+                        umma::fence_after_sync();
+                        const uint32_t sa = ring_a + s * TILE_BYTES;
+                        const uint32_t shift = static_cast<uint32_t>(j * a.dil * 16);
 #pragma unroll
-                    for (int ks = 0; ks < BK / 16; ++ks) {
-                        const uint64_t ad = umma::desc_kmajor(sa + ks * 2 * (BM * 16), BM * 16, 128);
-                        const uint64_t bh = umma::desc_kmajor(hi_a + ks * 2 * a.lbo + shift, a.lbo, 128);
-                        const uint64_t bl = umma::desc_kmajor(lo_a + ks * 2 * a.lbo + shift, a.lbo, 128);
-                        umma::mma_f16(tmem, ad, bh, idesc, (ci | j | ks) != 0);
-                        umma::mma_f16(tmem, ad, bl, idesc, true);
+                        for (int ks = 0; ks < BK / 16; ++ks) {
+                            const uint64_t ad = umma::desc_kmajor(sa + ks * 2 * (BM * 16), BM * 16, 128);
+                            const uint64_t bh = umma::desc_kmajor(hi_a + ks * 2 * a.lbo + shift, a.lbo, 128);
+                            const uint64_t bl = umma::desc_kmajor(lo_a + ks * 2 * a.lbo + shift, a.lbo, 128);
+                            umma::mma_f16(d, ad, bh, idesc, !first);
+                            umma::mma_f16(d, ad, bl, idesc, true);
+                            first = false;
+                        }
+                        umma::commit(&B.wempty[s]);
                     }
-                    umma::commit(&B.wempty[s]);
+                    umma::commit(&B.aempty[b]);
                 }
-                umma::commit(&B.aempty[b]);
+                umma::commit(&B.tfull[acc]);
             }
-            umma::commit(&B.done);
         }
-    } else {
+    } else if (warp < 6) {
         const int u = threadIdx.x - 64;                  // 0..127
         const int kc = u & 7;
-        for (int ci = 0; ci < NC; ++ci) {
-            const int b = ci & 1;
-            if (ci >= 2 && !bwait(&B.aempty[b], ((ci >> 1) - 1) & 1, B, a)) break;
-            uint8_t * hi = win + (b * 2) * win_bytes + kc * a.lbo;
-            stage_window<PRO>(a, hi, hi + win_bytes, (c_begin + ci) * BK + kc * 8, t0, u);
-            fence_proxy_async_smem();
-            mbar_arrive(&B.afull[b]);
-        }
-        const bool ok = bwait(&B.done, 0, B, a);
-        umma::fence_after_sync();
-        const int q = warp & 3;
-        const int co = mt * BM + q * 32 + lane;
-        const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16);
-        for (int cc = 0; cc < a.BN; cc += 16) {
-            float v[16];
-            umma::tmem_ld16(tq + cc, v);
-            if (!ok) continue;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int t = t0 + cc + i;
-                if (t >= a.T || co >= a.Cout) continue;
-                if (a.splits > 1) a.partial[(static_cast<std::size_t>(sp) * a.T + t) * a.Cout + co] = v[i];
-                else a.y[static_cast<std::size_t>(t) * a.y_stride + co] = finish<EPI>(v[i], a, t, co);
+        int cg = 0;
+        for (int un = blockIdx.x; un < n_units; un += gridDim.x) {
+            const Unit w = unit_of(a, un);
+            for (int ci = 0; ci < w.nc; ++ci, ++cg) {
+                const int b = cg & 1;
+                if (cg >= 2 && !bwait(&B.aempty[b], ((cg >> 1) - 1) & 1, B, a)) break;
+                uint8_t * hi = win + (b * 2) * win_bytes + kc * a.lbo;
+                stage_window<PRO>(a, hi, hi + win_bytes, (w.c_begin + ci) * BK + kc * 8, w.t0, u);
+                fence_proxy_async_smem();
+                mbar_arrive(&B.afull[b]);
             }
         }
-        if (a.splits > 1) {
-            __threadfence();
-            named_sync(1, 128);
-            const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-            if (u == 0) B.last = (atomicAdd(&a.counters[tile], 1u) == static_cast<unsigned>(a.splits - 1)) ? 1 : 0;
-            named_sync(1, 128);
-            if (B.last) {
-                __threadfence();
-                if (co < a.Cout) {
-                    const int tend = min(a.T, t0 + a.BN);
-                    for (int t = t0; t < tend; ++t) {
-                        float s = 0.f;
-                        for (int k = 0; k < a.splits; ++k) s += __ldcg(a.partial + (static_cast<std::size_t>(k) * a.T + t) * a.Cout + co);
-                        a.y[static_cast<std::size_t>(t) * a.y_stride + co] = finish<EPI>(s, a, t, co);
-                    }
-                }
-                if (u == 0) a.counters[tile] = 0u;
-            }
+    } else {
+        const int q = warp & 3;                          // tensor-memory lane quadrant of this warp
+        int k = 0;
+        for (int un = blockIdx.x; un < n_units; un += gridDim.x, ++k) {
+            const Unit w = unit_of(a, un);
+            const int acc = k & 1;
+            const bool ok = bwait(&B.tfull[acc], (k >> 1) & 1, B, a);
+            umma::fence_after_sync();
+            epilogue_unit<EPI>(a, w, tmem + static_cast<uint32_t>(acc * a.BN), q, lane, ok);
+            umma::fence_before_sync();
+            mbar_arrive(&B.tempty[acc]);
         }
+        mbar_arrive(&B.edone);                           // no tensor-memory reads after this
     }
-    umma::fence_before_sync();
-    __syncthreads();
+    // Free the accumulators only after every epilogue thread's last tensor-memory read.
     if (warp == 1) {
+        if (lane == 0) bwait(&B.edone, 0, B, a);
+        __syncwarp();
         umma::fence_after_sync();
         umma::tmem_dealloc(tmem, a.tmem_cols);
     }
+}
+
+// Split-K reduction: y[t][co] = epi(bias[co] + sum over splits, in split order, of the
+// partial sums) -- one thread per output, four splits' loads in flight at a time.
+template <int EPI>
+__global__ void k_splitk_reduce(const float * partial, int splits, int T, int Cout, const float * bias, const float * scale,
+                                const float * resid, int r_stride, float * y, int y_stride) {
+    const std::size_t n = static_cast<std::size_t>(T) * Cout;
+    const std::size_t i = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int t = static_cast<int>(i / Cout), co = static_cast<int>(i % Cout);
+    float acc = 0.f;
+    int k = 0;
+    for (; k + 4 <= splits; k += 4) {
+        const float p0 = __ldcg(partial + static_cast<std::size_t>(k) * n + i);
+        const float p1 = __ldcg(partial + static_cast<std::size_t>(k + 1) * n + i);
+        const float p2 = __ldcg(partial + static_cast<std::size_t>(k + 2) * n + i);
+        const float p3 = __ldcg(partial + static_cast<std::size_t>(k + 3) * n + i);
+        acc += p0;
+        acc += p1;
+        acc += p2;
+        acc += p3;
+    }
+    for (; k < splits; ++k) acc += __ldcg(partial + static_cast<std::size_t>(k) * n + i);
+    const float v = acc + (bias ? bias[co] : 0.f);
+    const float r = (EPI == EPI_RESIDUAL || EPI == EPI_SCALE_RESIDUAL) ? resid[static_cast<std::size_t>(t) * r_stride + co] : 0.f;
+    y[static_cast<std::size_t>(t) * y_stride + co] = finish<EPI>(v, EPI == EPI_SCALE_RESIDUAL ? scale[co] : 1.f, r);
 }
 
 struct PackArgs {
@@ -320,6 +402,11 @@ void launch_t(const KArgs & ka, dim3 grid, std::size_t smem, cudaStream_t stream
         attr.fetch_or(bit);
     }
     k_conv<PRO, EPI><<<grid, NTHREADS, smem, stream>>>(ka);
+    if (ka.splits > 1) {
+        const std::size_t n = static_cast<std::size_t>(ka.T) * ka.Cout;
+        k_splitk_reduce<EPI><<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(ka.partial, ka.splits, ka.T, ka.Cout, ka.bias, ka.scale,
+                                                                                     ka.resid, ka.r_stride, ka.y, ka.y_stride);
+    }
 }
 
 __global__ void k_fold_bias(const float * b, int n, int phases, float * out) {
@@ -350,8 +437,8 @@ Plan plan(const Conv & c, int sms) {
     int BN = 16;
     while (BN < c.T && BN < 256) BN *= 2;
     while (BN > 16 && smem_for(BN, H) > static_cast<std::size_t>(SMEM_MAX)) BN /= 2;
-    // row-heavy layers: smaller row tiles until the grid covers the SMs (not below 64 rows)
-    while (BN > 64 && p.MT * ceil_div(c.T, BN) < sms) BN /= 2;
+    // row-heavy layers: smaller row tiles until every CTA has two or more units (not below 64 rows)
+    while (BN > 64 && p.MT * ceil_div(c.T, BN) < 2 * sms) BN /= 2;
     const int target = sms * 3 / 4;
     for (;;) {
         const int tiles = p.MT * ceil_div(c.T, BN);
@@ -372,7 +459,7 @@ Plan plan(const Conv & c, int sms) {
         BN /= 2;
     }
     p.lbo = lbo_for(p.BN + H);
-    p.tmem_cols = std::max(32, p.BN);
+    p.tmem_cols = std::max(32, 2 * p.BN);   // two accumulators: the epilogue of one unit overlaps the next
     p.smem = smem_for(p.BN, H);
     if (p.smem > static_cast<std::size_t>(SMEM_MAX)) fail("conv: window of " + std::to_string(H) + " history rows does not fit", NAVI_E_SHAPE);
     return p;
@@ -381,10 +468,6 @@ Plan plan(const Conv & c, int sms) {
 std::size_t partial_need(const Conv & c, int sms) {
     const Plan p = plan(c, sms);
     return p.splits > 1 ? static_cast<std::size_t>(p.splits) * c.T * c.Cout : 0;
-}
-int counters_need(const Conv & c, int sms) {
-    const Plan p = plan(c, sms);
-    return p.splits > 1 ? p.NT * p.MT : 0;
 }
 
 void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) {
@@ -400,17 +483,17 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     if (c.epi == EPI_SCALE_RESIDUAL && !c.scale) fail("conv: layer scale missing", NAVI_E_SHAPE);
     const Plan p = plan(c, sms);
     if (p.splits > 1) {
-        if (static_cast<std::size_t>(p.splits) * c.T * c.Cout > ws.partial_cap || p.NT * p.MT > ws.n_counters)
+        if (static_cast<std::size_t>(p.splits) * c.T * c.Cout > ws.partial_cap)
             fail("conv: split-K workspace too small", NAVI_E_SHAPE);
     }
     KArgs ka{};
     ka.w = c.w; ka.x = c.x; ka.hist = c.hist; ka.sa = c.snake_a; ka.sb = c.snake_b; ka.bias = c.bias;
-    ka.resid = c.resid; ka.scale = c.scale; ka.y = c.y; ka.partial = ws.partial; ka.counters = ws.counters; ka.err = ws.err;
+    ka.resid = c.resid; ka.scale = c.scale; ka.y = c.y; ka.partial = ws.partial; ka.err = ws.err;
     ka.Cout = c.Cout; ka.Cin = c.Cin; ka.K = c.K; ka.dil = c.dil; ka.H = (c.K - 1) * c.dil; ka.T = c.T;
     ka.x_stride = c.x_stride; ka.y_stride = c.y_stride; ka.r_stride = c.r_stride;
-    ka.BN = p.BN; ka.CB = p.CB; ka.cb_per_split = p.cb_per_split; ka.splits = p.splits;
+    ka.BN = p.BN; ka.NT = p.NT; ka.MT = p.MT; ka.CB = p.CB; ka.cb_per_split = p.cb_per_split; ka.splits = p.splits;
     ka.lbo = p.lbo; ka.wrows = p.BN + ka.H; ka.tmem_cols = p.tmem_cols; ka.timeout_ns = ws.timeout_ns;
-    const dim3 grid(p.NT, p.MT, p.splits);
+    const dim3 grid(std::min(p.NT * p.MT * p.splits, sms));   // persistent: one CTA per SM at most
 #define NAVI_CONV_CASE(PR, EP) \
     if (c.pro == PR && c.epi == EP) { launch_t<PR, EP>(ka, grid, p.smem, stream); NAVI_CUDA(cudaGetLastError()); return; }
     NAVI_CONV_CASE(PRO_NONE, EPI_NONE)
@@ -473,8 +556,6 @@ int conv_once(const Device & dev, const navi_conv_args & a) {
         Workspace ws;
         ws.partial_cap = partial_need(c, sms);
         ws.partial = static_cast<float *>(alloc(ws.partial_cap * sizeof(float)));
-        ws.n_counters = std::max(1, counters_need(c, sms));
-        ws.counters = static_cast<unsigned *>(alloc(static_cast<std::size_t>(ws.n_counters) * sizeof(unsigned)));
         ws.err = static_cast<int *>(alloc(sizeof(int)));
         launch(c, ws, sms, s);
         int err = 0;

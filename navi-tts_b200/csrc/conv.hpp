@@ -36,7 +36,7 @@ constexpr int BK = 64;                       // input channels per block
 constexpr int TILE_ELEMS = BM * BK;          // one packed weight tile: [8 k chunks][128 co][8]
 constexpr int TILE_BYTES = TILE_ELEMS * 2;
 constexpr int NSTAGE = 4;                    // weight tiles in flight per CTA
-constexpr int NTHREADS = 192;                // warp 0 weights, warp 1 MMA, warps 2-5 window + epilogue
+constexpr int NTHREADS = 320;                // warp 0 weights, warp 1 MMA, warps 2-5 windows, warps 6-9 epilogue
 
 // One source block of a packed weight.  Logical weight W(co, tap, ci) for co in
 // [co0, co1), ci in [ci0, ci1):
@@ -85,14 +85,11 @@ Plan plan(const Conv & c, int sms);
 struct Workspace {
     float * partial = nullptr;               // split-K partial sums
     std::size_t partial_cap = 0;             // elements
-    unsigned * counters = nullptr;           // per output tile, zero between launches
-    int n_counters = 0;
     int * err = nullptr;                     // set to 1 by a CTA whose wait timed out
     unsigned long long timeout_ns = 2000000000ull;
 };
-// Elements of partial storage and counters a launch of `c` needs.
+// Elements of split-K partial storage a launch of `c` needs.
 std::size_t partial_need(const Conv & c, int sms);
-int counters_need(const Conv & c, int sms);
 
 void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream);
 

@@ -198,13 +198,28 @@ __global__ void k_final_conv(const __half * W, const float * bias, const float *
     float * xs = fs;                 // [Cin][NR]
     float * ws = fs + Cin * NR;      // [Cin][7]
     const int t0 = blockIdx.x * FROWS;
-    for (int i = threadIdx.x; i < NR * Cin; i += blockDim.x) {
-        const int r = i / Cin, ci = i % Cin, gr = t0 - 6 + r;
-        float v = 0.f;
-        if (gr >= 0) v = gr < T ? x[static_cast<std::size_t>(gr) * Cin + ci] : 0.f;
-        else v = hist[static_cast<std::size_t>(6 + gr) * Cin + ci];
-        const float s = sinf(v * sa[ci]);
-        xs[ci * NR + r] = v + s * s * sb[ci];
+    constexpr int U = 8;   // loads in flight per thread
+    for (int i0 = threadIdx.x; i0 < NR * Cin; i0 += FROWS * U) {
+        float v[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = i0 + k * FROWS;
+            v[k] = 0.f;
+            if (i < NR * Cin) {
+                const int r = i / Cin, ci = i % Cin, gr = t0 - 6 + r;
+                if (gr >= 0) v[k] = gr < T ? __ldg(x + static_cast<std::size_t>(gr) * Cin + ci) : 0.f;
+                else v[k] = __ldg(hist + static_cast<std::size_t>(6 + gr) * Cin + ci);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int i = i0 + k * FROWS;
+            if (i < NR * Cin) {
+                const int r = i / Cin, ci = i % Cin;
+                const float s = sinf(v[k] * __ldg(sa + ci));
+                xs[ci * NR + r] = v[k] + s * s * __ldg(sb + ci);
+            }
+        }
     }
     for (int i = threadIdx.x; i < Cin * 7; i += blockDim.x) ws[i] = __half2float(W[i]);
     __syncthreads();
@@ -604,13 +619,11 @@ std::unique_ptr<Vocoder> Vocoder::create(const Device & dev, const DeviceWeights
 
     // split-K workspace: the largest any stage needs at any chunk length up to Cmax
     std::size_t part = 0;
-    int cnt = 0;
     for (int T = 1; T <= I.Cmax; ++T) {
         auto need = [&](const CV & cv, int R) {
             conv::Conv c = cv.c;
             c.T = R;
             part = std::max(part, conv::partial_need(c, I.sms));
-            cnt = std::max(cnt, conv::counters_need(c, I.sms));
         };
         need(I.rvq_proj, T); need(I.pre_conv, T); need(I.in_proj, T); need(I.out_proj, T);
         for (auto & ly : I.layers) { need(ly.qkv, T); need(ly.o, T); need(ly.gateup, T); need(ly.down, T); }
@@ -629,8 +642,6 @@ std::unique_ptr<Vocoder> Vocoder::create(const Device & dev, const DeviceWeights
     }
     I.ws.partial = I.alloc<float>(part);
     I.ws.partial_cap = part;
-    I.ws.counters = I.alloc<unsigned>(static_cast<std::size_t>(std::max(cnt, 1)));
-    I.ws.n_counters = std::max(cnt, 1);
     I.ws.err = I.alloc<int>(1);
 
     NAVI_CUDA(cudaMallocHost(&I.h_codes, C * p.vq_n_q * sizeof(int)));
@@ -693,7 +704,6 @@ void Vocoder::decode_into(std::span<const std::int32_t> codes, int n_frames, flo
         NAVI_CUDA(cudaStreamSynchronize(I.stream));
         if (*I.h_err) {
             NAVI_CUDA(cudaMemsetAsync(I.ws.err, 0, sizeof(int), I.stream));
-            NAVI_CUDA(cudaMemsetAsync(I.ws.counters, 0, static_cast<std::size_t>(I.ws.n_counters) * sizeof(unsigned), I.stream));
             NAVI_CUDA(cudaStreamSynchronize(I.stream));
             fail("vocoder: a tensor-core conv wait passed its deadline", NAVI_E_TIMEOUT);
         }
