@@ -154,6 +154,96 @@ def cpu_baseline(L: int, n_frames: int = 3):
                       f"PyTorch fp32 oracle, {torch.get_num_threads()} threads, after 1 warm-up frame"}
 
 
+def vocoder_flops_per_frame(p) -> float:
+    """2 x multiply-adds of every GEMM / conv of the decoder per frame (vocoder.hip:261-343)."""
+    v = p.vocoder
+    L, VH, HD, FF, CD, DD = p.vq_latent, v.hidden, v.n_head * v.head_dim, v.ff, p.vq_codebook_dim, p.decoder_dim
+    macs = CD * CD + 3 * CD * L + L * VH + VH * L                       # rvq projection, pre_conv, in / out projection
+    macs += v.n_layer * (VH * 3 * HD + HD * VH + VH * 2 * FF + FF * VH)  # pre-transformer
+    rows = 1
+    for r in p.upsampling_ratios[:2]:
+        macs += rows * r * L * L                                         # transposed conv k = s
+        rows *= r
+        macs += rows * (L * 4 * L * 2)                                   # ConvNeXt pointwise pair
+    macs += rows * 7 * L * DD                                            # decoder.0
+    w = DD
+    for r in p.upsample_rates[:4]:
+        ow = w // 2
+        macs += rows * r * 2 * w * ow                                    # transposed conv k = 2s
+        rows *= r
+        macs += rows * 3 * (7 * ow * ow + ow * ow)                       # 3 residual units
+        w = ow
+    macs += rows * 7 * w                                                 # output conv
+    return 2.0 * macs
+
+
+def vocoder_weight_bytes(w) -> int:
+    """f16 bytes of the decoder's GEMM / conv weights (codebooks excluded: rows are gathered)."""
+    from navi_b200 import model_spec
+    total = 0
+    for name, shape in model_spec.tensor_table(model_spec.full_config(w.params.decoder_dim)):
+        if name.startswith("codec.decoder.") and len(shape) >= 2 and "_codebook" not in name:
+            n = 1
+            for d in shape:
+                n *= d
+            total += 2 * n
+    return total
+
+
+def vocoder_bench(dev, w, reps: int = 20):
+    """decode of 4- and 16-frame chunks of uniform random codes (device time of
+    Vocoder::decode including the codes / PCM copies, median of reps)."""
+    import numpy as np
+    from navi_b200 import engine
+    p = w.params
+    flops = vocoder_flops_per_frame(p)
+    wb = vocoder_weight_bytes(w)
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    tpeak, hpeak = float(peaks.get("bf16_tflops", 1590.0)), float(peaks.get("hbm_gbs", 6650.0))
+    rng = np.random.default_rng(3)
+    out = {}
+    for chunk in (4, 16):
+        voc = engine.Vocoder(dev, w, max_chunk_frames=chunk)
+        codes = rng.integers(0, p.vq_codebook_size, (chunk, p.vq_n_q)).astype(np.int32)
+        for _ in range(3):
+            voc.decode(codes)
+        dev_ms, wall_ms = [], []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            voc.decode(codes)
+            wall_ms.append((time.perf_counter() - t0) * 1000.0)
+            dev_ms.append(voc.last_ms)
+        ms = float(np.median(dev_ms))
+        bound_ms = max(chunk * flops / (tpeak * 1e12), wb / (hpeak * 1e9)) * 1e3
+        out[str(chunk)] = {"ms_per_chunk": round(ms, 4), "us_per_frame": round(ms * 1000.0 / chunk, 2),
+                           "e2e_ms_per_chunk": round(float(np.median(wall_ms)), 4),
+                           "tflops": round(chunk * flops / (ms * 1e-3) / 1e12, 2),
+                           "roofline_ms": round(bound_ms, 4), "roofline_frac": round(bound_ms / ms, 4)}
+        voc.close()
+    return {"workload": "configs[3]: codes [T][16] -> PCM [T*1920], decoder_dim %d, chunks of 4 and 16 frames" % p.decoder_dim,
+            "flops_per_frame": flops, "weight_bytes": wb, "chunks": out,
+            "roofline_note": "bound = max(FLOPs / measured bf16 peak, weight bytes / measured HBM); the tensor-core "
+                             "passes run f16 hi + lo activation halves, so issued MMA work is twice the FLOPs"}
+
+
+def vocoder_cpu_baseline(n_frames: int = 4):
+    """The vocoder oracle (PyTorch fp32 on the host cores) on one chunk of configs[3]."""
+    import numpy as np
+    import torch
+    from oracle import model as om
+    from oracle import vocoder as ov
+    torch.set_num_threads(os.cpu_count() or 1)
+    W = om.Weights.from_navi(BENCH_NAVI)
+    codes = np.random.default_rng(3).integers(0, W.cfg.vq_codebook_size, (n_frames, W.cfg.vq_n_q))
+    v = ov.Vocoder(W)
+    v.decode_chunk(codes)                    # warm-up
+    t0 = time.perf_counter()
+    v.decode_chunk(codes)
+    dt = time.perf_counter() - t0
+    return {"value": round(dt * 1000.0 / n_frames, 3), "unit": "ms/frame", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"one {n_frames}-frame chunk, PyTorch fp32 vocoder oracle, after 1 warm-up chunk"}
+
+
 def run_reference(args):
     rank, local, world = dist_env()
     if world > 1:
@@ -292,8 +382,12 @@ def run_ours(args):
             "phase_profile_us": {"total": round(float(prof.sum()), 1), "n_phases": int(len(prof)),
                                  "median": round(float(np.median(prof)), 2), "max": round(float(prof.max()), 2)},
         }
+        if args.vocoder:
+            line["vocoder"] = vocoder_bench(dev, w)
         if args.cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(L)
+            if args.vocoder:
+                line["vocoder"]["cpu_baseline"] = vocoder_cpu_baseline()
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
@@ -308,6 +402,7 @@ def main():
     ap.add_argument("--kv", type=int, default=512)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-vocoder", dest="vocoder", action="store_false", help="skip the configs[3] vocoder line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

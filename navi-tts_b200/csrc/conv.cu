@@ -34,7 +34,8 @@ namespace {
 using namespace navi::dev;
 
 constexpr int SMEM_MAX = 232448;      // opt-in dynamic shared memory per CTA on sm_100
-constexpr int BARS_BYTES = 256;
+constexpr int BARS_BYTES = 512;
+constexpr int MAXST = 14;             // weight tiles the ring (or the resident set) can hold
 
 struct KArgs {
     const __half * w;
@@ -44,11 +45,13 @@ struct KArgs {
     int Cout, Cin, K, dil, H, T, x_stride, y_stride, r_stride;
     int BN, NT, MT, CB, cb_per_split, splits;
     int lbo, wrows, tmem_cols;
+    int nst;                          // weight-ring stages
+    int resident;                     // 1: the CTA's tiles are loaded once and reused by every unit
     unsigned long long timeout_ns;
 };
 
 struct Bars {
-    uint64_t wfull[NSTAGE], wempty[NSTAGE], afull[2], aempty[2], tfull[2], tempty[2], edone;
+    uint64_t wfull[MAXST], wempty[MAXST], afull[2], aempty[2], tfull[2], tempty[2], edone;
     uint32_t tmem;
     int abort;
 };
@@ -87,65 +90,80 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// Stages one channel block's window: rows r = u/8, u/8 + 16, ... of k chunk u % 8.
-// Loads are issued SROWS rows at a time (read-only path) before any is used, so each
-// thread keeps SROWS x 32 bytes in flight.
-constexpr int SROWS = 8;
+// Window staging, software-pipelined: thread u owns k chunk u % 8 (channels c0..c0+7 of
+// the block) and rows u/8 + 16 i of each batch of 16 * SR<PRO> window rows.  The loads of
+// the next batch (possibly of the next channel block or unit) are issued before the
+// current batch is converted, so a thread keeps a batch in flight while it converts.
+template <int PRO> struct SR { static constexpr int n = PRO == PRO_SILU_GATE ? 2 : 4; };
 
 template <int PRO>
-__device__ __forceinline__ void stage_window(const KArgs & a, uint8_t * hi, uint8_t * lo, int c0, int t0, int u) {
+struct Rows {
+    float4 p0[SR<PRO>::n], p1[SR<PRO>::n], q0[SR<PRO>::n], q1[SR<PRO>::n];
+};
+
+template <int PRO>
+__device__ __forceinline__ void load_rows(Rows<PRO> & R, const KArgs & a, int c0, int t0, int rb) {
+    constexpr int N = SR<PRO>::n;
     const bool valid = c0 < a.Cin;   // Cin % 8 == 0: a chunk is wholly inside or outside
-    float ca[8], cb[8];
-    if (PRO == PRO_SNAKE && valid) {
-        const float4 a0 = __ldg(reinterpret_cast<const float4 *>(a.sa + c0)), a1 = __ldg(reinterpret_cast<const float4 *>(a.sa + c0 + 4));
-        const float4 b0 = __ldg(reinterpret_cast<const float4 *>(a.sb + c0)), b1 = __ldg(reinterpret_cast<const float4 *>(a.sb + c0 + 4));
-        ca[0] = a0.x; ca[1] = a0.y; ca[2] = a0.z; ca[3] = a0.w; ca[4] = a1.x; ca[5] = a1.y; ca[6] = a1.z; ca[7] = a1.w;
-        cb[0] = b0.x; cb[1] = b0.y; cb[2] = b0.z; cb[3] = b0.w; cb[4] = b1.x; cb[5] = b1.y; cb[6] = b1.z; cb[7] = b1.w;
-    }
-    for (int rb = u >> 3; rb < a.wrows; rb += 16 * SROWS) {
-        float4 p0[SROWS], p1[SROWS], q0[SROWS], q1[SROWS];
 #pragma unroll
-        for (int k = 0; k < SROWS; ++k) {
-            const int r = rb + 16 * k, gr = t0 - a.H + r;
-            const float * src = nullptr;
-            if (valid && r < a.wrows) {
-                if (gr >= 0 && gr < a.T) src = a.x + static_cast<std::size_t>(gr) * a.x_stride + c0;
-                else if (gr < 0 && a.hist) src = a.hist + static_cast<std::size_t>(a.H + gr) * a.Cin + c0;
-            }
-            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-            p0[k] = src ? __ldg(reinterpret_cast<const float4 *>(src)) : z;
-            p1[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + 4)) : z;
-            if (PRO == PRO_SILU_GATE) {
-                q0[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + a.Cin)) : z;
-                q1[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + a.Cin + 4)) : z;
-            }
+    for (int k = 0; k < N; ++k) {
+        const int r = rb + 16 * k, gr = t0 - a.H + r;
+        const float * src = nullptr;
+        if (valid && r < a.wrows) {
+            if (gr >= 0 && gr < a.T) src = a.x + static_cast<std::size_t>(gr) * a.x_stride + c0;
+            else if (gr < 0 && a.hist) src = a.hist + static_cast<std::size_t>(a.H + gr) * a.Cin + c0;
         }
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        R.p0[k] = src ? __ldg(reinterpret_cast<const float4 *>(src)) : z;
+        R.p1[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + 4)) : z;
+        if (PRO == PRO_SILU_GATE) {
+            R.q0[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + a.Cin)) : z;
+            R.q1[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + a.Cin + 4)) : z;
+        }
+    }
+}
+
+template <int PRO>
+__device__ __forceinline__ void store_rows(const Rows<PRO> & R, const KArgs & a, uint8_t * hi, uint8_t * lo, int c0, int rb) {
+    constexpr int N = SR<PRO>::n;
+    float ca[8], cb[8];
+    const bool valid = c0 < a.Cin;
+    if (PRO == PRO_SNAKE) {
+        if (valid) {
+            const float4 a0 = __ldg(reinterpret_cast<const float4 *>(a.sa + c0)), a1 = __ldg(reinterpret_cast<const float4 *>(a.sa + c0 + 4));
+            const float4 b0 = __ldg(reinterpret_cast<const float4 *>(a.sb + c0)), b1 = __ldg(reinterpret_cast<const float4 *>(a.sb + c0 + 4));
+            ca[0] = a0.x; ca[1] = a0.y; ca[2] = a0.z; ca[3] = a0.w; ca[4] = a1.x; ca[5] = a1.y; ca[6] = a1.z; ca[7] = a1.w;
+            cb[0] = b0.x; cb[1] = b0.y; cb[2] = b0.z; cb[3] = b0.w; cb[4] = b1.x; cb[5] = b1.y; cb[6] = b1.z; cb[7] = b1.w;
+        } else {
 #pragma unroll
-        for (int k = 0; k < SROWS; ++k) {
-            const int r = rb + 16 * k;
-            if (r >= a.wrows) break;
-            float v[8] = {p0[k].x, p0[k].y, p0[k].z, p0[k].w, p1[k].x, p1[k].y, p1[k].z, p1[k].w};
-            if (PRO == PRO_SILU_GATE) {
-                const float up[8] = {q0[k].x, q0[k].y, q0[k].z, q0[k].w, q1[k].x, q1[k].y, q1[k].z, q1[k].w};
+            for (int i = 0; i < 8; ++i) ca[i] = cb[i] = 0.f;
+        }
+    }
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = v[i] / (1.f + __expf(-v[i])) * up[i];
-            }
-            if (PRO == PRO_SNAKE && valid) {
+    for (int k = 0; k < N; ++k) {
+        const int r = rb + 16 * k;
+        if (r >= a.wrows) break;
+        float v[8] = {R.p0[k].x, R.p0[k].y, R.p0[k].z, R.p0[k].w, R.p1[k].x, R.p1[k].y, R.p1[k].z, R.p1[k].w};
+        if (PRO == PRO_SILU_GATE) {
+            const float up[8] = {R.q0[k].x, R.q0[k].y, R.q0[k].z, R.q0[k].w, R.q1[k].x, R.q1[k].y, R.q1[k].z, R.q1[k].w};
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float sn = __sinf(v[i] * ca[i]);
-                    v[i] += sn * sn * cb[i];
-                }
-            }
-            float h[8], l[8];
+            for (int i = 0; i < 8; ++i) v[i] = v[i] / (1.f + __expf(-v[i])) * up[i];
+        }
+        if (PRO == PRO_SNAKE) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                h[i] = __half2float(__float2half_rn(v[i]));
-                l[i] = v[i] - h[i];
+                const float sn = __sinf(v[i] * ca[i]);
+                v[i] += sn * sn * cb[i];
             }
-            *reinterpret_cast<uint4 *>(hi + r * 16) = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]), pack_h2(h[6], h[7]));
-            *reinterpret_cast<uint4 *>(lo + r * 16) = make_uint4(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]), pack_h2(l[4], l[5]), pack_h2(l[6], l[7]));
         }
+        float h[8], l[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            h[i] = __half2float(__float2half_rn(v[i]));
+            l[i] = v[i] - h[i];
+        }
+        *reinterpret_cast<uint4 *>(hi + r * 16) = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]), pack_h2(h[6], h[7]));
+        *reinterpret_cast<uint4 *>(lo + r * 16) = make_uint4(pack_h2(l[0], l[1]), pack_h2(l[2], l[3]), pack_h2(l[4], l[5]), pack_h2(l[6], l[7]));
     }
 }
 
@@ -165,32 +183,43 @@ __device__ __forceinline__ Unit unit_of(const KArgs & a, int u) {
 }
 
 template <int EPI>
+__device__ __forceinline__ void load_resid(float (&rr)[16], const KArgs & a, int t, int co, bool live) {
+    const int nv = min(16, a.T - t);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) rr[i] = (live && i < nv) ? a.resid[static_cast<std::size_t>(t + i) * a.r_stride + co] : 0.f;
+}
+
+// Stores one unit's accumulator (BN rows x this thread's channel); the residual rows of
+// the next 16-row batch are loaded before the current batch is stored.
+template <int EPI>
 __device__ __forceinline__ void epilogue_unit(const KArgs & a, const Unit & w, uint32_t tacc, int q, int lane, bool ok) {
+    constexpr bool RES = EPI == EPI_RESIDUAL || EPI == EPI_SCALE_RESIDUAL;
     const int co = w.mt * BM + q * 32 + lane;
     const bool live = ok && co < a.Cout;
     const float bco = (a.bias && live && a.splits == 1) ? a.bias[co] : 0.f;
     const float sco = (EPI == EPI_SCALE_RESIDUAL && live) ? a.scale[co] : 1.f;
     const uint32_t tq = tacc + (static_cast<uint32_t>(q * 32) << 16);
+    const bool fin = live && a.splits == 1;
+    float rr[16], rn[16];
+    if (RES) load_resid<EPI>(rr, a, w.t0, co, fin);
     for (int cc = 0; cc < a.BN; cc += 16) {
         float v[16];
         __syncwarp();                        // tcgen05.ld is warp-collective (.sync.aligned)
         umma::tmem_ld16(tq + cc, v);
+        if (RES && cc + 16 < a.BN) load_resid<EPI>(rn, a, w.t0 + cc + 16, co, fin && w.t0 + cc + 16 < a.T);
         const int nv = min(16, a.T - (w.t0 + cc));
         if (live && a.splits > 1) {
 #pragma unroll
             for (int i = 0; i < 16; ++i)
                 if (i < nv) a.partial[(static_cast<std::size_t>(w.sp) * a.T + w.t0 + cc + i) * a.Cout + co] = v[i];
         } else if (live) {
-            float rr[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                rr[i] = 0.f;
-                if ((EPI == EPI_RESIDUAL || EPI == EPI_SCALE_RESIDUAL) && i < nv)
-                    rr[i] = a.resid[static_cast<std::size_t>(w.t0 + cc + i) * a.r_stride + co];
-            }
 #pragma unroll
             for (int i = 0; i < 16; ++i)
                 if (i < nv) a.y[static_cast<std::size_t>(w.t0 + cc + i) * a.y_stride + co] = finish<EPI>(v[i] + bco, sco, rr[i]);
+        }
+        if (RES) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) rr[i] = rn[i];
         }
     }
     __syncwarp();
@@ -203,7 +232,7 @@ template <int PRO, int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t * ring = smem;
-    uint8_t * win = smem + NSTAGE * TILE_BYTES;
+    uint8_t * win = smem + a.nst * TILE_BYTES;
     const int win_bytes = 8 * a.lbo;                       // one buffer's hi (or lo) planes
     Bars & B = *reinterpret_cast<Bars *>(win + 4 * win_bytes);
 
@@ -211,7 +240,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
     const int n_units = a.NT * a.MT * a.splits;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NSTAGE; ++i) {
+        for (int i = 0; i < a.nst; ++i) {
             mbar_init(&B.wfull[i], 1);
             mbar_init(&B.wempty[i], 1);
         }
@@ -236,21 +265,29 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
     const uint32_t tmem = B.tmem;
 
     if (warp == 0) {
-        if (lane == 0) {
+        if (lane == 0 && a.resident) {
+            // one channel tile, no split: every unit of this CTA uses the same CB * K tiles
+            const int nit = a.CB * a.K;
+            for (int i = 0; i < nit; ++i) {
+                mbar_arrive_expect_tx(&B.wfull[i], TILE_BYTES);
+                bulk_g2s(ring + i * TILE_BYTES, a.w + static_cast<std::size_t>(i) * TILE_ELEMS, TILE_BYTES, &B.wfull[i]);
+            }
+        } else if (lane == 0) {
+            const int NST = a.nst;
             int it = 0;
             for (int un = blockIdx.x; un < n_units; un += gridDim.x) {
                 const Unit w = unit_of(a, un);
                 const __half * wt = a.w + (static_cast<std::size_t>(w.mt) * a.CB + w.c_begin) * a.K * TILE_ELEMS;
                 const int nit = w.nc * a.K;   // tiles of this unit are contiguous
                 for (int i = 0; i < nit; ++i, ++it) {
-                    const int s = it % NSTAGE;
-                    if (it >= NSTAGE && !bwait(&B.wempty[s], ((it / NSTAGE) - 1) & 1, B, a)) break;
+                    const int s = it % NST;
+                    if (it >= NST && !bwait(&B.wempty[s], ((it / NST) - 1) & 1, B, a)) break;
                     mbar_arrive_expect_tx(&B.wfull[s], TILE_BYTES);
                     bulk_g2s(ring + s * TILE_BYTES, wt + static_cast<std::size_t>(i) * TILE_ELEMS, TILE_BYTES, &B.wfull[s]);
                 }
             }
             // tail: every issued tile has been consumed before the CTA may exit
-            for (int k = max(0, it - NSTAGE); k < it; ++k) bwait(&B.wempty[k % NSTAGE], (k / NSTAGE) & 1, B, a);
+            for (int k = max(0, it - NST); k < it; ++k) bwait(&B.wempty[k % NST], (k / NST) & 1, B, a);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -270,8 +307,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
                     umma::fence_after_sync();
                     const uint32_t hi_a = win_a + (b * 2) * win_bytes, lo_a = hi_a + win_bytes;
                     for (int j = 0; j < a.K; ++j, ++it) {
-                        const int s = it % NSTAGE;
-                        if (!bwait(&B.wfull[s], (it / NSTAGE) & 1, B, a)) break;
+                        int s;
+                        if (a.resident) {
+                            s = (w.c_begin + ci) * a.K + j;
+                            if (k == 0 && !bwait(&B.wfull[s], 0, B, a)) break;
+                        } else {
+                            s = it % a.nst;
+                            if (!bwait(&B.wfull[s], (it / a.nst) & 1, B, a)) break;
+                        }
                         umma::fence_after_sync();
                         const uint32_t sa = ring_a + s * TILE_BYTES;
                         const uint32_t shift = static_cast<uint32_t>(j * a.dil * 16);
@@ -284,7 +327,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
                             umma::mma_f16(d, ad, bl, idesc, true);
                             first = false;
                         }
-                        umma::commit(&B.wempty[s]);
+                        if (!a.resident) umma::commit(&B.wempty[s]);
                     }
                     umma::commit(&B.aempty[b]);
                 }
@@ -292,19 +335,39 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
             }
         }
     } else if (warp < 6) {
+        // cursor over (unit, channel block, batch) of this CTA; the next position's loads
+        // are in flight while the current batch is converted and stored
         const int u = threadIdx.x - 64;                  // 0..127
         const int kc = u & 7;
-        int cg = 0;
-        for (int un = blockIdx.x; un < n_units; un += gridDim.x) {
-            const Unit w = unit_of(a, un);
-            for (int ci = 0; ci < w.nc; ++ci, ++cg) {
-                const int b = cg & 1;
-                if (cg >= 2 && !bwait(&B.aempty[b], ((cg >> 1) - 1) & 1, B, a)) break;
-                uint8_t * hi = win + (b * 2) * win_bytes + kc * a.lbo;
-                stage_window<PRO>(a, hi, hi + win_bytes, (w.c_begin + ci) * BK + kc * 8, w.t0, u);
+        const int per = 16 * SR<PRO>::n;
+        const int nb = (a.wrows + per - 1) / per;        // batches per channel block
+        int un = blockIdx.x, ci = 0, bi = 0, cg = 0;
+        Unit w = unit_of(a, un);
+        Rows<PRO> cur, nxt;
+        load_rows<PRO>(cur, a, (w.c_begin + ci) * BK + kc * 8, w.t0, (u >> 3) + bi * per);
+        while (un < n_units) {
+            int un2 = un, ci2 = ci, bi2 = bi + 1;
+            Unit w2 = w;
+            if (bi2 == nb) {
+                bi2 = 0;
+                if (++ci2 == w.nc) {
+                    ci2 = 0;
+                    un2 += gridDim.x;
+                    if (un2 < n_units) w2 = unit_of(a, un2);
+                }
+            }
+            if (un2 < n_units) load_rows<PRO>(nxt, a, (w2.c_begin + ci2) * BK + kc * 8, w2.t0, (u >> 3) + bi2 * per);
+            const int b = cg & 1;
+            if (bi == 0 && cg >= 2 && !bwait(&B.aempty[b], ((cg >> 1) - 1) & 1, B, a)) break;
+            uint8_t * hi = win + (b * 2) * win_bytes + kc * a.lbo;
+            store_rows<PRO>(cur, a, hi, hi + win_bytes, (w.c_begin + ci) * BK + kc * 8, (u >> 3) + bi * per);
+            if (bi == nb - 1) {
                 fence_proxy_async_smem();
                 mbar_arrive(&B.afull[b]);
+                ++cg;
             }
+            cur = nxt;
+            un = un2; ci = ci2; bi = bi2; w = w2;
         }
     } else {
         const int q = warp & 3;                          // tensor-memory lane quadrant of this warp
@@ -414,7 +477,8 @@ __global__ void k_fold_bias(const float * b, int n, int phases, float * out) {
 }
 
 int lbo_for(int wrows) { return ((wrows + 7) / 8 * 8 + 1) * 16; }   // plane stride = 16 (mod 128): conflict-free stores
-std::size_t smem_for(int BN, int H) { return static_cast<std::size_t>(NSTAGE) * TILE_BYTES + 4ull * 8 * lbo_for(BN + H) + BARS_BYTES; }
+std::size_t win_bytes_for(int BN, int H) { return 4ull * 8 * lbo_for(BN + H); }
+std::size_t smem_for(int BN, int H, int nst = NSTAGE) { return static_cast<std::size_t>(nst) * TILE_BYTES + win_bytes_for(BN, H) + BARS_BYTES; }
 
 } // namespace
 
@@ -460,7 +524,13 @@ Plan plan(const Conv & c, int sms) {
     }
     p.lbo = lbo_for(p.BN + H);
     p.tmem_cols = std::max(32, 2 * p.BN);   // two accumulators: the epilogue of one unit overlaps the next
-    p.smem = smem_for(p.BN, H);
+    // weight ring: every stage the shared memory left after the windows holds; the whole
+    // tile set when every unit of a CTA uses the same tiles (one channel tile, no split)
+    const int fit = static_cast<int>((SMEM_MAX - win_bytes_for(p.BN, H) - BARS_BYTES) / TILE_BYTES);
+    const int max_st = std::min(MAXST, fit);
+    p.resident = p.MT == 1 && p.splits == 1 && p.CB * c.K <= max_st;
+    p.nst = p.resident ? p.CB * c.K : std::max(NSTAGE, max_st);
+    p.smem = smem_for(p.BN, H, p.nst);
     if (p.smem > static_cast<std::size_t>(SMEM_MAX)) fail("conv: window of " + std::to_string(H) + " history rows does not fit", NAVI_E_SHAPE);
     return p;
 }
@@ -493,6 +563,7 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     ka.x_stride = c.x_stride; ka.y_stride = c.y_stride; ka.r_stride = c.r_stride;
     ka.BN = p.BN; ka.NT = p.NT; ka.MT = p.MT; ka.CB = p.CB; ka.cb_per_split = p.cb_per_split; ka.splits = p.splits;
     ka.lbo = p.lbo; ka.wrows = p.BN + ka.H; ka.tmem_cols = p.tmem_cols; ka.timeout_ns = ws.timeout_ns;
+    ka.nst = p.nst; ka.resident = p.resident ? 1 : 0;
     const dim3 grid(std::min(p.NT * p.MT * p.splits, sms));   // persistent: one CTA per SM at most
 #define NAVI_CONV_CASE(PR, EP) \
     if (c.pro == PR && c.epi == EP) { launch_t<PR, EP>(ka, grid, p.smem, stream); NAVI_CUDA(cudaGetLastError()); return; }

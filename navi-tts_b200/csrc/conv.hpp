@@ -35,7 +35,7 @@ constexpr int BM = 128;                      // output channels per tile (MMA M)
 constexpr int BK = 64;                       // input channels per block
 constexpr int TILE_ELEMS = BM * BK;          // one packed weight tile: [8 k chunks][128 co][8]
 constexpr int TILE_BYTES = TILE_ELEMS * 2;
-constexpr int NSTAGE = 4;                    // weight tiles in flight per CTA
+constexpr int NSTAGE = 4;                    // fewest weight tiles in flight per CTA
 constexpr int NTHREADS = 320;                // warp 0 weights, warp 1 MMA, warps 2-5 windows, warps 6-9 epilogue
 
 // One source block of a packed weight.  Logical weight W(co, tap, ci) for co in
@@ -78,6 +78,8 @@ struct Conv {
 
 struct Plan {
     int BN = 16, NT = 1, MT = 1, CB = 1, splits = 1, cb_per_split = 1, lbo = 0, tmem_cols = 32;
+    int nst = NSTAGE;                        // weight-ring stages
+    bool resident = false;                   // weights loaded once per CTA
     std::size_t smem = 0;
 };
 Plan plan(const Conv & c, int sms);
