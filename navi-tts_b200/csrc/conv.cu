@@ -498,29 +498,31 @@ Plan plan(const Conv & c, int sms) {
     p.MT = ceil_div(c.Cout, BM);
     p.CB = ceil_div(c.Cin, BK);
     const int H = (c.K - 1) * c.dil;
-    int BN = 16;
-    while (BN < c.T && BN < 256) BN *= 2;
-    while (BN > 16 && smem_for(BN, H) > static_cast<std::size_t>(SMEM_MAX)) BN /= 2;
-    // row-heavy layers: smaller row tiles until every CTA has two or more units (not below 64 rows)
-    while (BN > 64 && p.MT * ceil_div(c.T, BN) < 2 * sms) BN /= 2;
-    const int target = sms * 3 / 4;
-    for (;;) {
+    // Cost model (measured on B200): the MMA issuer is the bottleneck at small row tiles
+    // (about 65 ns per tcgen05.mma for N up to 128 at the clocks these short launches run
+    // at), so time ~ waves x (MMAs per unit); a unit also pays ~1 us of staging / epilogue
+    // latency, a split-K launch a reduction pass.  Candidates: row tiles 256 .. 16 that fit
+    // shared memory, channel-block splits 1 .. CB; the cheapest wins.
+    double best = 1e30;
+    for (int BN = 256; BN >= 16; BN /= 2) {
+        if (smem_for(BN, H) > static_cast<std::size_t>(SMEM_MAX)) continue;
+        if (BN > 16 && BN / 2 >= c.T) continue;                      // a smaller tile covers every row
         const int tiles = p.MT * ceil_div(c.T, BN);
-        int splits = 1, cbps = p.CB;
-        if (tiles < target && p.CB > 1) {
-            const int want = std::min(p.CB, ceil_div(sms, tiles));
-            cbps = ceil_div(p.CB, want);
-            splits = ceil_div(p.CB, cbps);
+        for (int want = 1; want <= p.CB; want = want < p.CB ? std::min(p.CB, want * 2) : p.CB + 1) {
+            const int cbps = ceil_div(p.CB, want), splits = ceil_div(p.CB, cbps);
+            const int units = tiles * splits;
+            const double waves = static_cast<double>(ceil_div(units, sms));
+            const double unit_us = cbps * c.K * (2.0 * BK / 16) * 0.065 + 1.0 + BN / 256.0;
+            double us = waves * unit_us;
+            if (splits > 1) us += 3.0 + static_cast<double>(splits + 2) * c.T * c.Cout * 4.0 / 3.0e6;
+            if (us < best - 1e-9) {
+                best = us;
+                p.BN = BN;
+                p.NT = ceil_div(c.T, BN);
+                p.splits = splits;
+                p.cb_per_split = cbps;
+            }
         }
-        const bool enough = tiles * splits >= target;
-        if (enough || BN <= 16 || ceil_div(c.T, BN / 2) == ceil_div(c.T, BN)) {
-            p.BN = BN;
-            p.NT = ceil_div(c.T, BN);
-            p.splits = splits;
-            p.cb_per_split = cbps;
-            break;
-        }
-        BN /= 2;
     }
     p.lbo = lbo_for(p.BN + H);
     p.tmem_cols = std::max(32, 2 * p.BN);   // two accumulators: the epilogue of one unit overlaps the next
