@@ -190,9 +190,9 @@ def vocoder_weight_bytes(w) -> int:
     return total
 
 
-def vocoder_bench(dev, w, reps: int = 20):
+def vocoder_bench(dev, w, reps: int = 20, chunks=(4, 16), warm: int = 3):
     """decode of 4- and 16-frame chunks of uniform random codes (device time of
-    Vocoder::decode including the codes / PCM copies, median of reps)."""
+    Vocoder::decode including the codes / PCM copies, median of reps, after `warm` decodes)."""
     import numpy as np
     from navi_b200 import engine
     p = w.params
@@ -202,10 +202,10 @@ def vocoder_bench(dev, w, reps: int = 20):
     tpeak, hpeak = float(peaks.get("bf16_tflops", 1590.0)), float(peaks.get("hbm_gbs", 6650.0))
     rng = np.random.default_rng(3)
     out = {}
-    for chunk in (4, 16):
+    for chunk in chunks:
         voc = engine.Vocoder(dev, w, max_chunk_frames=chunk)
         codes = rng.integers(0, p.vq_codebook_size, (chunk, p.vq_n_q)).astype(np.int32)
-        for _ in range(3):
+        for _ in range(warm):
             voc.decode(codes)
         dev_ms, wall_ms = [], []
         for _ in range(reps):
@@ -272,6 +272,27 @@ def combine_ranks(ms: float, e2e_ms: float, world: int, dist, device: str):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms = float(t[0]), float(t[1])
     return ms, e2e_ms, world * 1000.0 / ms, world * 1000.0 / e2e_ms
+
+
+def run_vocoder_only(args):
+    """`--vocoder-only`: the configs[3] measurement alone (one GPU), one JSON line."""
+    import torch
+    rank, local, world = dist_env()
+    if world > 1 and rank != 0:
+        return
+    torch.cuda.set_device(local)
+    ensure_weights(0, 1)
+    from navi_b200 import engine
+    dev = engine.Device(local)
+    w = engine.Weights(dev, BENCH_NAVI)
+    chunks = tuple(int(c) for c in args.voc_chunks.split(","))
+    v = vocoder_bench(dev, w, reps=args.steps, chunks=chunks, warm=args.warmup)
+    line = {"metric": "vocoder ms per frame (configs[3])", "impl": "ours", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": False, "dtype": "f16 weights / f32 activations (f16 hi+lo on the tensor cores)",
+            "data": "synthetic (seeded random-init weights N(0,0.02), uniform random codes)", "vocoder": v}
+    if args.cpu_baseline:
+        line["vocoder"]["cpu_baseline"] = vocoder_cpu_baseline()
+    print(json.dumps(line), flush=True)
 
 
 def run_ours(args):
@@ -403,11 +424,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-vocoder", dest="vocoder", action="store_false", help="skip the configs[3] vocoder line")
+    ap.add_argument("--vocoder-only", action="store_true", help="run only the configs[3] vocoder measurement")
+    ap.add_argument("--voc-chunks", default="4,16", help="vocoder chunk lengths (frames), comma separated")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.vocoder_only:
+        run_vocoder_only(args)
     else:
         run_ours(args)
 
