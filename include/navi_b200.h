@@ -254,7 +254,7 @@ void navi_vocoder_destroy(navi_vocoder * v);
  * (vocoder.hip:373-385; y must then be dense, y_stride = Cout * stride). Prologue: 0 none,
  * 1 SnakeBeta (snake_a = e^alpha, snake_b = 1/(e^beta + 1e-9)), 2 silu(x[:, :Cin]) *
  * x[:, Cin:2Cin]. Epilogue: 0 none, 1 erf GELU, 2 + resid, 3 * scale + resid (resid rows
- * [T][y_stride]). Cin % 8 == 0, x_stride % 4 == 0, 16-byte aligned x / hist. Packs the weight
+ * [T][y_stride]), 4 SiLU. Cin % 8 == 0, x_stride % 4 == 0, 16-byte aligned x / hist. Packs the weight
  * and allocates its workspace on every call: a primitive for tests and tools, not the hot path. */
 typedef struct navi_conv_args {
     const uint16_t * w;            /* f16 bits */
@@ -264,6 +264,8 @@ typedef struct navi_conv_args {
     int pro; const float * snake_a, * snake_b;
     int epi; const float * bias, * resid, * scale;
     float * y; int y_stride;
+    int rowmajor;                  /* K == 1 only: w is the layer's own row-major [Cout][Cin] matrix, read by
+                                      TMA in 128B-swizzled boxes with no packed copy (the path the prefill uses) */
 } navi_conv_args;
 int navi_conv1d(navi_device * dev, const navi_conv_args * a);
 

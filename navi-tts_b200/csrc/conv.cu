@@ -18,12 +18,16 @@
 // tensor memory.
 #include "conv.hpp"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "device.cuh"
 #include "umma.cuh"
 
 #include "conv_api.hpp"
 
 #include <algorithm>
+#include <cstring>
 #include <atomic>
 #include <string>
 
@@ -46,6 +50,7 @@ struct KArgs {
     int BN, NT, MT, CB, cb_per_split, splits;
     int lbo, wrows, tmem_cols;
     int nst;                          // weight-ring stages
+    int tmaw;                         // 1: weights are a row-major matrix read by TMA (128B-swizzled tiles)
     int resident;                     // 1: the CTA's tiles are loaded once and reused by every unit
     unsigned long long timeout_ns;
 };
@@ -82,6 +87,7 @@ __device__ __forceinline__ float finish(float v, float sc, float r) {
     if (EPI == EPI_GELU) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
     if (EPI == EPI_RESIDUAL) return v + r;
     if (EPI == EPI_SCALE_RESIDUAL) return v * sc + r;
+    if (EPI == EPI_SILU) return v / (1.f + expf(-v));
     return v;
 }
 
@@ -229,7 +235,7 @@ __device__ __forceinline__ void epilogue_unit(const KArgs & a, const Unit & w, u
 // so the weight ring, the two window buffers and the two accumulators run as pipelines
 // across unit boundaries.
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
+__global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a, const __grid_constant__ CUtensorMap tmw) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t * ring = smem;
     uint8_t * win = smem + a.nst * TILE_BYTES;
@@ -251,6 +257,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
             mbar_init(&B.tempty[i], 128);
         }
         mbar_init(&B.edone, 128);
+        if (a.tmaw && (smem_addr(ring) & 1023u)) {   // 128B-swizzled tiles need 1024-byte alignment
+            B.abort = 1;
+            atomicExch(a.err, 1);
+        }
         B.abort = 0;
         fence_mbar_init();
     }
@@ -268,9 +278,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
         if (lane == 0 && a.resident) {
             // one channel tile, no split: every unit of this CTA uses the same CB * K tiles
             const int nit = a.CB * a.K;
-            for (int i = 0; i < nit; ++i) {
+            for (int i = 0; i < nit && !B.abort; ++i) {
                 mbar_arrive_expect_tx(&B.wfull[i], TILE_BYTES);
-                bulk_g2s(ring + i * TILE_BYTES, a.w + static_cast<std::size_t>(i) * TILE_ELEMS, TILE_BYTES, &B.wfull[i]);
+                if (a.tmaw) umma::tma_load_2d(ring + i * TILE_BYTES, &tmw, (i / a.K) * BK, 0, &B.wfull[i]);
+                else bulk_g2s(ring + i * TILE_BYTES, a.w + static_cast<std::size_t>(i) * TILE_ELEMS, TILE_BYTES, &B.wfull[i]);
             }
         } else if (lane == 0) {
             const int NST = a.nst;
@@ -282,8 +293,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
                 for (int i = 0; i < nit; ++i, ++it) {
                     const int s = it % NST;
                     if (it >= NST && !bwait(&B.wempty[s], ((it / NST) - 1) & 1, B, a)) break;
+                    if (B.abort) break;
                     mbar_arrive_expect_tx(&B.wfull[s], TILE_BYTES);
-                    bulk_g2s(ring + s * TILE_BYTES, wt + static_cast<std::size_t>(i) * TILE_ELEMS, TILE_BYTES, &B.wfull[s]);
+                    if (a.tmaw) umma::tma_load_2d(ring + s * TILE_BYTES, &tmw, (w.c_begin + i / a.K) * BK, w.mt * BM, &B.wfull[s]);
+                    else bulk_g2s(ring + s * TILE_BYTES, wt + static_cast<std::size_t>(i) * TILE_ELEMS, TILE_BYTES, &B.wfull[s]);
                 }
             }
             // tail: every issued tile has been consumed before the CTA may exit
@@ -320,7 +333,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a) {
                         const uint32_t shift = static_cast<uint32_t>(j * a.dil * 16);
 #pragma unroll
                         for (int ks = 0; ks < BK / 16; ++ks) {
-                            const uint64_t ad = umma::desc_kmajor(sa + ks * 2 * (BM * 16), BM * 16, 128);
+                            const uint64_t ad = a.tmaw ? umma::desc_kmajor_sw128(sa + ks * 32)
+                                                       : umma::desc_kmajor(sa + ks * 2 * (BM * 16), BM * 16, 128);
                             const uint64_t bh = umma::desc_kmajor(hi_a + ks * 2 * a.lbo + shift, a.lbo, 128);
                             const uint64_t bl = umma::desc_kmajor(lo_a + ks * 2 * a.lbo + shift, a.lbo, 128);
                             umma::mma_f16(d, ad, bh, idesc, !first);
@@ -455,7 +469,7 @@ __global__ void k_pack(const PackArgs pa, __half * dst, std::size_t n) {
 }
 
 template <int PRO, int EPI>
-void launch_t(const KArgs & ka, dim3 grid, std::size_t smem, cudaStream_t stream) {
+void launch_t(const KArgs & ka, const CUtensorMap & tm, dim3 grid, std::size_t smem, cudaStream_t stream) {
     static std::atomic<uint64_t> attr{0};   // devices whose attribute is set, one bit per ordinal < 64
     int dev = 0;
     NAVI_CUDA(cudaGetDevice(&dev));
@@ -464,7 +478,7 @@ void launch_t(const KArgs & ka, dim3 grid, std::size_t smem, cudaStream_t stream
         NAVI_CUDA(cudaFuncSetAttribute(k_conv<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
         attr.fetch_or(bit);
     }
-    k_conv<PRO, EPI><<<grid, NTHREADS, smem, stream>>>(ka);
+    k_conv<PRO, EPI><<<grid, NTHREADS, smem, stream>>>(ka, tm);
     if (ka.splits > 1) {
         const std::size_t n = static_cast<std::size_t>(ka.T) * ka.Cout;
         k_splitk_reduce<EPI><<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(ka.partial, ka.splits, ka.T, ka.Cout, ka.bias, ka.scale,
@@ -537,6 +551,28 @@ Plan plan(const Conv & c, int sms) {
     return p;
 }
 
+void weight_map(const __half * w, int Cout, int Cin, int ld, void * out) {
+    if ((reinterpret_cast<std::uintptr_t>(w) & 15u) || ld % 8 || ld < Cin)
+        fail("conv: row-major weights need a 16-byte aligned base and a row stride multiple of 8 >= Cin", NAVI_E_SHAPE);
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(Cin), static_cast<cuuint64_t>(Cout)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    const cuuint32_t box[2] = {BK, BM};   // 64 f16 = 128 B inner (the swizzle span) x 128 rows
+    const cuuint32_t estr[2] = {1, 1};
+    // the driver entry point is looked up at run time, so the library loads without libcuda
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q{};
+        void * fn = nullptr;
+        NAVI_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !fn) fail("conv: cuTensorMapEncodeTiled unavailable", NAVI_E_CUDA);
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const CUresult r = encode(static_cast<CUtensorMap *>(out), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(w), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail("conv: cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")", NAVI_E_CUDA);
+}
+
 std::size_t partial_need(const Conv & c, int sms) {
     const Plan p = plan(c, sms);
     return p.splits > 1 ? static_cast<std::size_t>(p.splits) * c.T * c.Cout : 0;
@@ -544,7 +580,7 @@ std::size_t partial_need(const Conv & c, int sms) {
 
 void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) {
     if (c.T <= 0) return;
-    if (c.Cin % 8 || c.x_stride % 4 || c.K < 1 || c.dil < 1 || !c.w || !c.x || !c.y)
+    if (c.Cin % 8 || c.x_stride % 4 || c.K < 1 || c.dil < 1 || !(c.w || c.w_rm) || !c.x || !c.y)
         fail("conv: Cin and the input row stride must be multiples of 8 and 4", NAVI_E_SHAPE);
     if ((reinterpret_cast<std::uintptr_t>(c.x) | reinterpret_cast<std::uintptr_t>(c.hist) | reinterpret_cast<std::uintptr_t>(c.w)) & 15u)
         fail("conv: input, history and weights must be 16-byte aligned", NAVI_E_SHAPE);
@@ -566,9 +602,16 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     ka.BN = p.BN; ka.NT = p.NT; ka.MT = p.MT; ka.CB = p.CB; ka.cb_per_split = p.cb_per_split; ka.splits = p.splits;
     ka.lbo = p.lbo; ka.wrows = p.BN + ka.H; ka.tmem_cols = p.tmem_cols; ka.timeout_ns = ws.timeout_ns;
     ka.nst = p.nst; ka.resident = p.resident ? 1 : 0;
+    CUtensorMap tm;
+    std::memset(&tm, 0, sizeof tm);
+    if (c.w_rm) {
+        if (c.K != 1) fail("conv: row-major (TMA) weights are for K == 1 layers", NAVI_E_SHAPE);
+        weight_map(c.w_rm, c.Cout, c.Cin, c.w_ld, &tm);
+        ka.tmaw = 1;
+    }
     const dim3 grid(std::min(p.NT * p.MT * p.splits, sms));   // persistent: one CTA per SM at most
 #define NAVI_CONV_CASE(PR, EP) \
-    if (c.pro == PR && c.epi == EP) { launch_t<PR, EP>(ka, grid, p.smem, stream); NAVI_CUDA(cudaGetLastError()); return; }
+    if (c.pro == PR && c.epi == EP) { launch_t<PR, EP>(ka, tm, grid, p.smem, stream); NAVI_CUDA(cudaGetLastError()); return; }
     NAVI_CONV_CASE(PRO_NONE, EPI_NONE)
     NAVI_CONV_CASE(PRO_NONE, EPI_GELU)
     NAVI_CONV_CASE(PRO_NONE, EPI_SCALE_RESIDUAL)
@@ -577,6 +620,8 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     NAVI_CONV_CASE(PRO_SNAKE, EPI_RESIDUAL)
     NAVI_CONV_CASE(PRO_NONE, EPI_RESIDUAL)
     NAVI_CONV_CASE(PRO_SNAKE, EPI_GELU)
+    NAVI_CONV_CASE(PRO_NONE, EPI_SILU)
+    NAVI_CONV_CASE(PRO_SILU_GATE, EPI_RESIDUAL)
 #undef NAVI_CONV_CASE
     fail("conv: no instantiation for prologue " + std::to_string(c.pro) + " epilogue " + std::to_string(c.epi), NAVI_E_SHAPE);
 }
@@ -611,9 +656,15 @@ int conv_once(const Device & dev, const navi_conv_args & a) {
         } else {
             ps.s_co = static_cast<long long>(a.Cin) * a.K; ps.s_ci = a.K; ps.s_tap = 1;
         }
-        __half * wp = static_cast<__half *>(alloc(packed_elems(c.Cout, c.Cin, c.K) * sizeof(__half)));
-        pack({ps}, c.Cout, c.Cin, c.K, wp, s);
-        c.w = wp;
+        if (a.rowmajor) {
+            if (P > 1 || a.K != 1) fail("conv: row-major weights are for K == 1 layers", NAVI_E_ARG);
+            c.w_rm = reinterpret_cast<const __half *>(a.w);
+            c.w_ld = a.Cin;
+        } else {
+            __half * wp = static_cast<__half *>(alloc(packed_elems(c.Cout, c.Cin, c.K) * sizeof(__half)));
+            pack({ps}, c.Cout, c.Cin, c.K, wp, s);
+            c.w = wp;
+        }
         c.x = a.x; c.x_stride = a.x_stride; c.T = a.T; c.hist = a.hist;
         c.pro = a.pro; c.snake_a = a.snake_a; c.snake_b = a.snake_b;
         c.epi = a.epi; c.resid = a.resid; c.r_stride = a.y_stride; c.scale = a.scale;

@@ -29,7 +29,7 @@
 namespace navi::conv {
 
 enum Pro : int { PRO_NONE = 0, PRO_SNAKE = 1, PRO_SILU_GATE = 2 };
-enum Epi : int { EPI_NONE = 0, EPI_GELU = 1, EPI_RESIDUAL = 2, EPI_SCALE_RESIDUAL = 3 };
+enum Epi : int { EPI_NONE = 0, EPI_GELU = 1, EPI_RESIDUAL = 2, EPI_SCALE_RESIDUAL = 3, EPI_SILU = 4 };
 
 constexpr int BM = 128;                      // output channels per tile (MMA M)
 constexpr int BK = 64;                       // input channels per block
@@ -61,6 +61,10 @@ void pack(const std::vector<PackSrc> & srcs, int Cout, int Cin, int K, __half * 
 
 struct Conv {
     const __half * w = nullptr;              // packed tiles
+    // or, for K == 1 (a linear layer), the weight as stored: row-major [Cout][w_ld] f16, read
+    // by TMA in 128 x 64 boxes (16-byte aligned base, w_ld % 8 == 0); no packed copy needed
+    const __half * w_rm = nullptr;
+    int w_ld = 0;
     int Cout = 0, Cin = 0, K = 1, dil = 1;
     const float * x = nullptr;               // rows [T][x_stride]; SILU_GATE: row = [gate | up], Cin each
     int x_stride = 0, T = 0;
@@ -90,6 +94,8 @@ struct Workspace {
     int * err = nullptr;                     // set to 1 by a CTA whose wait timed out
     unsigned long long timeout_ns = 2000000000ull;
 };
+// Encodes the TMA map of a row-major [Cout][ld] f16 weight (out: a CUtensorMap).
+void weight_map(const __half * w, int Cout, int Cin, int ld, void * out);
 // Elements of split-K partial storage a launch of `c` needs.
 std::size_t partial_need(const Conv & c, int sms);
 

@@ -6,6 +6,7 @@
 // lo = f16(x - hi), so the products keep about 22 bits of the activation while the weights
 // stay exact f16; accumulation is f32.
 #include "talker.hpp"
+#include "conv.hpp"
 #include "device.cuh"
 
 #include "../../include/navi_b200.h"
@@ -64,116 +65,9 @@ __global__ void k_rmsnorm(const float * x, const float * w, int H, float eps, fl
     for (int i = threadIdx.x; i < H; i += blockDim.x) yr[i] = xr[i] * scale * w[i];
 }
 
-// ---- GEMM: y[M][N] = epi(op(x)[M][K] . W[N][K]^T + bias) -------------------------------------
-
-constexpr int GBM = 64, GBN = 64, GBK = 32, GPAD = 8, GNT = 128;
+// GEMM epilogues of the prefill (y = epi(x W^T + bias)); the GEMMs run on the tcgen05 conv
+// kernel as K = 1 layers with the weights read in place by TMA (conv.hpp).
 enum { EPI_NONE = 0, EPI_SILU = 1, EPI_RESIDUAL = 2 };
-
-struct GemmArgs {
-    const __half * W;    // [N][K]
-    const float * bias;  // [N] or null
-    const float * x;     // [M][xs]; with GATE: gate columns [0, K), up columns [K, 2K)
-    int xs;
-    int M, N, K;
-    float * y;           // [M][ys]
-    int ys;
-    const float * res;   // EPI_RESIDUAL: [M][ys] added to the result (may alias y)
-};
-
-// 4 warps in a 2 x 2 layout over a 64 x 64 tile, each 32 x 32 = 2 m16 x 4 n8 mma tiles; K in
-// blocks of 32. N a multiple of 64 and K of 32 (checked on the host); rows beyond M are zero.
-template <int EPI, bool GATE>
-__global__ void __launch_bounds__(GNT) k_gemm(const GemmArgs a) {
-    __shared__ __align__(16) __half sAh[GBM][GBK + GPAD];
-    __shared__ __align__(16) __half sAl[GBM][GBK + GPAD];
-    __shared__ __align__(16) __half sB[GBN][GBK + GPAD];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, wm = warp >> 1, wn = warp & 1;
-    const int g = lane >> 2, t4 = lane & 3;
-    const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * GBN;
-    float acc[2][4][4];
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc[i][j][q] = 0.f;
-    const int lr = tid >> 1, lc = (tid & 1) * 16;   // loader: row, first of 16 columns
-    for (int k0 = 0; k0 < a.K; k0 += GBK) {
-        {
-            const int m = m0 + lr;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                float v[4] = {0.f, 0.f, 0.f, 0.f};
-                if (m < a.M) {
-                    const float * src = a.x + static_cast<size_t>(m) * a.xs + k0 + lc + q * 4;
-                    const float4 f = *reinterpret_cast<const float4 *>(src);
-                    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
-                    if constexpr (GATE) {
-                        const float4 u = *reinterpret_cast<const float4 *>(src + a.K);
-                        v[0] = silu_f(v[0]) * u.x; v[1] = silu_f(v[1]) * u.y; v[2] = silu_f(v[2]) * u.z; v[3] = silu_f(v[3]) * u.w;
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const __half h = __float2half_rn(v[i]);
-                    sAh[lr][lc + q * 4 + i] = h;
-                    sAl[lr][lc + q * 4 + i] = __float2half_rn(v[i] - __half2float(h));
-                }
-            }
-            const __half * src = a.W + static_cast<size_t>(n0 + lr) * a.K + k0 + lc;
-            *reinterpret_cast<uint4 *>(&sB[lr][lc]) = *reinterpret_cast<const uint4 *>(src);
-            *reinterpret_cast<uint4 *>(&sB[lr][lc + 8]) = *reinterpret_cast<const uint4 *>(src + 8);
-        }
-        __syncthreads();
-#pragma unroll
-        for (int kk = 0; kk < GBK; kk += 16) {
-            uint32_t ah[2][4], al[2][4], bf[2][4];
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                // matrix lane / 8: rows (m % 2) * 8 + lane % 8, columns (m / 2) * 8
-                const int row = wm * 32 + mt * 16 + ((lane >> 3) & 1) * 8 + (lane & 7), col = kk + (lane >> 4) * 8;
-                ldsm_x4(ah[mt], &sAh[row][col]);
-                ldsm_x4(al[mt], &sAl[row][col]);
-            }
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-                // matrices: (n 0-7, k 0-7), (n 0-7, k 8-15), (n 8-15, k 0-7), (n 8-15, k 8-15)
-                const int row = wn * 32 + p * 16 + (lane >> 4) * 8 + (lane & 7), col = kk + ((lane >> 3) & 1) * 8;
-                ldsm_x4(bf[p], &sB[row][col]);
-            }
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                for (int nt = 0; nt < 4; ++nt) {
-                    const uint32_t b0 = bf[nt >> 1][(nt & 1) * 2], b1 = bf[nt >> 1][(nt & 1) * 2 + 1];
-                    mma_16816(acc[mt][nt], ah[mt], b0, b1);
-                    mma_16816(acc[mt][nt], al[mt], b0, b1);
-                }
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-            const int n = n0 + wn * 32 + nt * 8 + t4 * 2;
-            const float b0 = a.bias ? a.bias[n] : 0.f, b1 = a.bias ? a.bias[n + 1] : 0.f;
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const int m = m0 + wm * 32 + mt * 16 + g + hh * 8;
-                if (m >= a.M) continue;
-                float v0 = acc[mt][nt][2 * hh] + b0, v1 = acc[mt][nt][2 * hh + 1] + b1;
-                if constexpr (EPI == EPI_SILU) { v0 = silu_f(v0); v1 = silu_f(v1); }
-                float * dst = a.y + static_cast<size_t>(m) * a.ys + n;
-                if constexpr (EPI == EPI_RESIDUAL) {
-                    const float * r = a.res + static_cast<size_t>(m) * a.ys + n;
-                    v0 += r[0];
-                    v1 += r[1];
-                }
-                *reinterpret_cast<float2 *>(dst) = make_float2(v0, v1);
-            }
-        }
-}
 
 // Per row t (position pos0 + t): RMSNorm of every q and k head (head_dim 128: one warp per
 // head, 4 values a lane), rotate-half RoPE with the host table's cos/sin for the position, q
@@ -308,16 +202,35 @@ struct Talker::Impl {
         return static_cast<T *>(ptr);
     }
 
+    int sms = 148;
+    conv::Workspace ws;
+
+    static conv::Conv gemm_desc(const __half * W, const float * bias, int xs, int M, int K, int N, int ys, int epi, bool gate) {
+        conv::Conv c;
+        c.w_rm = W;
+        c.w_ld = K;
+        c.Cout = N;
+        c.Cin = K;
+        c.K = 1;
+        c.x_stride = xs;
+        c.T = M;
+        c.pro = gate ? conv::PRO_SILU_GATE : conv::PRO_NONE;
+        c.epi = epi == EPI_SILU ? conv::EPI_SILU : epi == EPI_RESIDUAL ? conv::EPI_RESIDUAL : conv::EPI_NONE;
+        c.bias = bias;
+        c.y_stride = ys;
+        c.r_stride = ys;
+        return c;
+    }
+
+    // y[M][N] (row stride ys) = epi(op(x)[M][K] W[N][K]^T + bias); op = silu(gate) * up when
+    // gate (x rows [gate K | up K]); EPI_RESIDUAL adds res (may alias y).
     void gemm(const __half * W, const float * bias, const float * in, int xs, int M, int K, int N, float * out, int ys, int epi,
               bool gate = false, const float * res = nullptr) {
-        if (N % GBN || K % GBK) fail("talker: GEMM shape not a multiple of the tile", NAVI_E_SHAPE);
-        GemmArgs a{W, bias, in, xs, M, N, K, out, ys, res};
-        const dim3 grid(N / GBN, (M + GBM - 1) / GBM), block(GNT);
-        if (gate) k_gemm<EPI_RESIDUAL, true><<<grid, block, 0, stream>>>(a);
-        else if (epi == EPI_NONE) k_gemm<EPI_NONE, false><<<grid, block, 0, stream>>>(a);
-        else if (epi == EPI_SILU) k_gemm<EPI_SILU, false><<<grid, block, 0, stream>>>(a);
-        else k_gemm<EPI_RESIDUAL, false><<<grid, block, 0, stream>>>(a);
-        NAVI_CUDA(cudaGetLastError());
+        conv::Conv c = gemm_desc(W, bias, xs, M, K, N, ys, epi, gate);
+        c.x = in;
+        c.y = out;
+        c.resid = res;
+        conv::launch(c, ws, sms, stream);
     }
 };
 
@@ -386,6 +299,19 @@ std::unique_ptr<Talker> Talker::create(const Device & dev, const DeviceWeights &
     I.x = I.alloc<float>(M * I.H); I.n = I.alloc<float>(M * I.H); I.qkv = I.alloc<float>(M * I.QKV);
     I.att = I.alloc<float>(M * I.Q); I.gu = I.alloc<float>(M * 2 * I.F);
     I.hid = I.alloc<float>(I.H); I.logits = I.alloc<float>(I.TV);
+    // split-K workspace of the tensor-core GEMMs: the most any of them needs at any row count
+    I.sms = dev.info().multiprocessors;
+    {
+        std::size_t part = 0;
+        const struct { int K, N, xs; bool gate; } shapes[] = {{I.TH, I.TH, I.TH, false}, {I.TH, I.H, I.TH, false}, {I.H, I.QKV, I.H, false},
+                                                             {I.Q, I.H, I.Q, false}, {I.H, 2 * I.F, I.H, false}, {I.F, I.H, 2 * I.F, true},
+                                                             {I.H, I.TV, I.H, false}};
+        for (int m = 1; m <= max_prompt_tokens + 8; ++m)
+            for (const auto & g : shapes) part = std::max(part, conv::partial_need(Impl::gemm_desc(nullptr, nullptr, g.xs, m, g.K, g.N, g.N, EPI_NONE, g.gate), I.sms));
+        I.ws.partial = I.alloc<float>(std::max<std::size_t>(part, 1));
+        I.ws.partial_cap = part;
+        I.ws.err = I.alloc<int>(1);
+    }
     NAVI_CUDA(cudaEventCreate(&I.ev0));
     NAVI_CUDA(cudaEventCreate(&I.ev1));
     return t;
@@ -496,6 +422,12 @@ void Talker::prefill(const Prompt & pr) {
     float ms = 0.f;
     NAVI_CUDA(cudaEventElapsedTime(&ms, I.ev0, I.ev1));
     I.last_ms = ms;
+    int err = 0;
+    NAVI_CUDA(cudaMemcpy(&err, I.ws.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) {
+        NAVI_CUDA(cudaMemset(I.ws.err, 0, sizeof(int)));
+        fail("talker: a tensor-core GEMM wait passed its deadline", NAVI_E_TIMEOUT);
+    }
     I.kv.n_used = T;
 }
 

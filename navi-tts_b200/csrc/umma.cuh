@@ -28,6 +28,20 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t smem_byte_addr, uint32_
     return d;
 }
 
+// The same for a K-major tile in the 128-byte swizzled layout a TMA load with
+// CU_TENSOR_MAP_SWIZZLE_128B writes (rows of 64 f16 = 128 B, 8-row atoms of 1024 B, the
+// start 1024-byte aligned): leading offset unused (1), stride offset 1024 B, layout type 2.
+// A 16-wide K step inside the atom advances the start address by 32 bytes.
+__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_byte_addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(1) << 16;
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
 // Instruction descriptor for kind::f16 with f16 A and B (both K-major), f32 accumulate:
 // D format f32 (bits 4-5 = 1), A/B format f16 (0), N >> 3 at bit 17, M >> 4 at bit 24.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
@@ -65,6 +79,17 @@ __device__ __forceinline__ void commit(uint64_t * bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
                  : "memory");
+}
+
+// ---- TMA --------------------------------------------------------------------------------------
+// 2-D tiled load of one box of `tmap` at element coordinates (x inner, y outer) into shared
+// memory, completion counted on `bar`. No multicast. x * element size must be a multiple of 16.
+__device__ __forceinline__ void tma_load_2d(void * dst, const void * tmap, int x, int y, uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+        "l"(tmap), "r"(x), "r"(y), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+        : "memory");
 }
 
 // ---- epilogue loads -----------------------------------------------------------------------------

@@ -66,7 +66,7 @@ class ConvArgs(ctypes.Structure):
     _fields_ = [("w", c_void_p), ("Cout", c_int), ("Cin", c_int), ("K", c_int), ("dil", c_int), ("trans_stride", c_int),
                 ("x", c_void_p), ("x_stride", c_int), ("T", c_int), ("hist", c_void_p), ("pro", c_int), ("snake_a", c_void_p),
                 ("snake_b", c_void_p), ("epi", c_int), ("bias", c_void_p), ("resid", c_void_p), ("scale", c_void_p),
-                ("y", c_void_p), ("y_stride", c_int)]
+                ("y", c_void_p), ("y_stride", c_int), ("rowmajor", c_int)]
 
 
 STAGE_FN = ctypes.CFUNCTYPE(None, c_void_p, c_char_p, c_void_p, c_int, c_int)

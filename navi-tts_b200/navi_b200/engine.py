@@ -295,17 +295,18 @@ class Vocoder:
 
 
 PRO_NONE, PRO_SNAKE, PRO_SILU_GATE = 0, 1, 2
-EPI_NONE, EPI_GELU, EPI_RESIDUAL, EPI_SCALE_RESIDUAL = 0, 1, 2, 3
+EPI_NONE, EPI_GELU, EPI_RESIDUAL, EPI_SCALE_RESIDUAL, EPI_SILU = 0, 1, 2, 3, 4
 
 
 def conv1d(dev: Device, w_ptr: int, Cout: int, Cin: int, K: int, x_ptr: int, T: int, y_ptr: int, *, dil: int = 1,
            trans_stride: int = 0, x_stride: int | None = None, hist_ptr: int = 0, pro: int = PRO_NONE, snake_a: int = 0,
-           snake_b: int = 0, epi: int = EPI_NONE, bias: int = 0, resid: int = 0, scale: int = 0, y_stride: int | None = None) -> None:
+           snake_b: int = 0, epi: int = EPI_NONE, bias: int = 0, resid: int = 0, scale: int = 0, y_stride: int | None = None,
+           rowmajor: bool = False) -> None:
     """navi_conv1d on device pointers (the implicit-GEMM conv primitive)."""
     P = trans_stride if trans_stride > 0 else 1
     a = capi.ConvArgs(w_ptr, Cout, Cin, K, dil, trans_stride, x_ptr, Cin if x_stride is None else x_stride, T, hist_ptr or None,
                       pro, snake_a or None, snake_b or None, epi, bias or None, resid or None, scale or None, y_ptr,
-                      Cout * P if y_stride is None else y_stride)
+                      Cout * P if y_stride is None else y_stride, 1 if rowmajor else 0)
     check(lib().navi_conv1d(dev.h, byref(a)))
 
 

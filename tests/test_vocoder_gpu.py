@@ -69,6 +69,8 @@ def _ref_conv(w, x, Cin, K, dil, hist, pro, sa, sb, epi, bias, resid, scale, P):
         y = y + torch.from_numpy(resid.astype(np.float64))
     elif epi == engine.EPI_SCALE_RESIDUAL:
         y = y * torch.from_numpy(scale.astype(np.float64)) + torch.from_numpy(resid.astype(np.float64))
+    elif epi == engine.EPI_SILU:
+        y = y / (1 + torch.exp(-y))
     return y.numpy()
 
 
@@ -90,10 +92,34 @@ CONV_CASES = [
 ]
 
 
+# K == 1 layers with the weight read in place by TMA (128B-swizzled tiles), as the prefill
+# uses them: (Cout, Cin, T, prologue, epilogue)
+TMA_CASES = [
+    (3072, 1024, 10, engine.PRO_NONE, engine.EPI_NONE),               # prefill QKV, 10-row prompt
+    (1024, 2048, 200, engine.PRO_NONE, engine.EPI_RESIDUAL),          # O projection + residual, 200 rows
+    (6144, 1024, 37, engine.PRO_NONE, engine.EPI_NONE),               # gate/up
+    (1024, 3072, 200, engine.PRO_SILU_GATE, engine.EPI_RESIDUAL),     # down: SiLU gate prologue + residual
+    (2048, 2048, 64, engine.PRO_NONE, engine.EPI_SILU),               # text projection fc1 (bias + SiLU)
+    (200, 136, 5, engine.PRO_NONE, engine.EPI_SILU),                  # ragged: TMA zero fill past Cout / Cin
+    (64, 64, 1000, engine.PRO_SNAKE, engine.EPI_RESIDUAL),            # one channel tile: weights resident
+    (3072, 1024, 1, engine.PRO_NONE, engine.EPI_NONE),                # one row (the codec head)
+]
+
+
+@pytest.mark.parametrize("case", range(len(TMA_CASES)))
+def test_conv_primitive_rowmajor_tma_weights(dev, case):
+    Cout, Cin, T, pro, epi = TMA_CASES[case]
+    _conv_case(dev, Cout, Cin, 1, 1, T, False, pro, epi, 0, 300 + case, rowmajor=True)
+
+
 @pytest.mark.parametrize("case", range(len(CONV_CASES)))
 def test_conv_primitive_matches_float64(dev, case):
     Cout, Cin, K, dil, T, use_hist, pro, epi, P = CONV_CASES[case]
-    rng = np.random.default_rng(100 + case)
+    _conv_case(dev, Cout, Cin, K, dil, T, use_hist, pro, epi, P, 100 + case)
+
+
+def _conv_case(dev, Cout, Cin, K, dil, T, use_hist, pro, epi, P, seed, rowmajor=False):
+    rng = np.random.default_rng(seed)
     H = (K - 1) * dil
     if P:
         w = (rng.standard_normal((Cin, Cout, K * P)) * 0.05).astype(np.float16)
@@ -119,7 +145,8 @@ def test_conv_primitive_matches_float64(dev, case):
     dsc = d(scale) if scale is not None else None
     engine.conv1d(dev, dw.data_ptr(), Cout, Cin, K, dx.data_ptr(), T, dy.data_ptr(), dil=dil, trans_stride=P, x_stride=xs,
                   hist_ptr=dh.data_ptr() if dh is not None else 0, pro=pro, snake_a=dsa.data_ptr(), snake_b=dsb.data_ptr(), epi=epi,
-                  bias=db.data_ptr(), resid=dy.data_ptr() if resid is not None else 0, scale=dsc.data_ptr() if dsc is not None else 0)
+                  bias=db.data_ptr(), resid=dy.data_ptr() if resid is not None else 0, scale=dsc.data_ptr() if dsc is not None else 0,
+                  rowmajor=rowmajor)
     got = dy.cpu().numpy().astype(np.float64)
     assert np.isfinite(got).all()
     err = np.linalg.norm(got - want) / np.linalg.norm(want)
