@@ -226,6 +226,41 @@ def vocoder_bench(dev, w, reps: int = 20, chunks=(4, 16), warm: int = 3):
                              "passes run f16 hi + lo activation halves, so issued MMA work is twice the FLOPs"}
 
 
+def serving_bench(dev, w, reps: int = 10, n_text: int = 200, first_frames: int = 4):
+    """configs[4], one stream on one GPU: time to first audio (TTFA) = token ids of a 200-id text
+    prompt -> prompt rows -> 28-layer prefill -> the first `first_frames` frames -> their PCM
+    through the vocoder (graph.h:29), wall clock per utterance, p50 over reps; plus the
+    prefill device time."""
+    import numpy as np
+    from navi_b200 import engine, model_spec
+    p = w.params
+    cfg = model_spec.full_config(p.decoder_dim)
+    g = engine.Graph(dev, w, max_prompt_tokens=1024, max_frames=first_frames + 8)
+    voc = engine.Vocoder(dev, w, max_chunk_frames=first_frames)
+    s = engine.Sampling(temperature=0.9, top_k=50, top_p=0.9, repetition_penalty=1.05, cp_temperature=0.9, cp_top_k=50,
+                        cp_top_p=0.9, min_frames=first_frames + 1, rng=1)
+    rng = np.random.default_rng(4)
+    spk = rng.standard_normal(p.talker.hidden).astype(np.float32)
+    ttfa, pre, rows = [], [], 0
+    for i in range(reps + 2):
+        ids = ([cfg.im_start_id, cfg.assistant_id, 198] + rng.integers(0, cfg.text_vocab, n_text).tolist()
+               + [cfg.im_end_id, 198, cfg.im_start_id, cfg.assistant_id, 198])
+        t0 = time.perf_counter()
+        codes, st = g.synth_ids(ids, "english", spk, s, 77 + i, first_frames)
+        voc.reset()
+        pcm = voc.decode(codes)
+        t1 = time.perf_counter()
+        assert codes.shape[0] == first_frames and pcm.size == first_frames * voc.samples_per_frame
+        if i >= 2:
+            ttfa.append((t1 - t0) * 1000.0)
+            pre.append(st.prefill_ms)
+    g.close()
+    voc.close()
+    return {"workload": f"configs[4] single stream: {n_text}-id text prompt, first {first_frames} frames + their PCM",
+            "ttfa_ms_p50": round(float(np.median(ttfa)), 3), "ttfa_ms_min": round(float(min(ttfa)), 3),
+            "prefill_ms_p50": round(float(np.median(pre)), 3), "reps": reps}
+
+
 def vocoder_cpu_baseline(n_frames: int = 4):
     """The vocoder oracle (PyTorch fp32 on the host cores) on one chunk of configs[3]."""
     import numpy as np
@@ -405,6 +440,7 @@ def run_ours(args):
         }
         if args.vocoder:
             line["vocoder"] = vocoder_bench(dev, w)
+            line["serving"] = serving_bench(dev, w)
         if args.cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(L)
             if args.vocoder:
