@@ -327,22 +327,42 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
         named_sync(bid, NT);
     }
     if (wid == 0) {
-        // Sequential sums in warp 0: every lane runs the same chain on values the lanes load
-        // 32 at a time and pass round by shuffles, so the loads never sit on the chain.
+        // Sequential sums in warp 0, 32 terms per block: every lane gathers the block's 32
+        // values by shuffles (independent, so they overlap), then runs the same in-order
+        // __fadd_rn chain over them straight through, keeping the running sum at its own
+        // position; a ballot finds the first position past the target. The additions are
+        // the same, in the same order, as one sequential loop, so the results are too.
         const float u = draw_uniform(c);
+        // running sums of the block v (0 past the end); returns the sum after the block and
+        // leaves in `mine` the sum after this lane's term
+        auto block_scan = [&](float acc, float v, float & mine) {
+#pragma unroll
+            for (int g = 0; g < 32; g += 8) {   // eight values gathered per group: few live registers
+                float t[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) t[q] = __shfl_sync(0xffffffffu, v, g + q);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    acc = __fadd_rn(acc, t[q]);
+                    if (g + q == lane) mine = acc;
+                }
+            }
+            return acc;
+        };
         int chosen;
         if (nucleus) {
             // the shortest prefix by rank whose cumulative probability reaches top_p: ranks <= R
             float cum = 0.f;
             int R = n - 1;
-            bool done = false;
-            for (int r0 = 0; r0 < n && !done; r0 += 32) {
-                const float p = r0 + lane < n ? __fmul_rn(e[ci[ord[r0 + lane]]], inv) : 0.f;
-                const int mq = min(32, n - r0);
-#pragma unroll 1
-                for (int q = 0; q < mq && !done; ++q) {
-                    cum = __fadd_rn(cum, __shfl_sync(0xffffffffu, p, q));
-                    if (cum >= c.top_p) { R = r0 + q; done = true; }
+            for (int r0 = 0; r0 < n; r0 += 32) {
+                const bool in = r0 + lane < n;
+                const float p = in ? __fmul_rn(e[ci[ord[r0 + lane]]], inv) : 0.f;
+                float mine = 0.f;
+                cum = block_scan(cum, p, mine);
+                const unsigned hit = __ballot_sync(0xffffffffu, in && mine >= c.top_p);
+                if (hit) {
+                    R = r0 + __ffs(hit) - 1;
+                    break;
                 }
             }
             // keep flags by candidate position (the values in s are no longer needed)
@@ -361,42 +381,39 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
                 const int ii = j < n ? ci[j] : 0;
                 const float ev = kp ? e[ii] : 0.f;
                 const unsigned km = __ballot_sync(0xffffffffu, kp);
-                const int mq = min(32, n - j0);
-#pragma unroll 1
-                for (int q = 0; q < mq; ++q) ksum = __fadd_rn(ksum, __shfl_sync(0xffffffffu, ev, q));
+                float mine = 0.f;
+                ksum = block_scan(ksum, ev, mine);
                 if (km) last = __shfl_sync(0xffffffffu, ii, 31 - __clz(km));
             }
             const float kinv = __fdiv_rn(1.0f, ksum);
             chosen = last;
             float c2 = 0.f;
-            done = false;
-            for (int j0 = 0; j0 < n && !done; j0 += 32) {
+            for (int j0 = 0; j0 < n; j0 += 32) {
                 const int j = j0 + lane;
                 const bool kp = j < n && kept[j] != 0.f;
                 const int ii = j < n ? ci[j] : 0;
                 const float pv = kp ? __fmul_rn(e[ii], kinv) : 0.f;
-                const unsigned km = __ballot_sync(0xffffffffu, kp);
-                const int mq = min(32, n - j0);
-#pragma unroll 1
-                for (int q = 0; q < mq && !done; ++q) {
-                    if (!((km >> q) & 1u)) continue;
-                    c2 = __fadd_rn(c2, __shfl_sync(0xffffffffu, pv, q));
-                    if (c2 >= u) { chosen = __shfl_sync(0xffffffffu, ii, q); done = true; }
+                float mine = 0.f;
+                c2 = block_scan(c2, pv, mine);
+                const unsigned hit = __ballot_sync(0xffffffffu, kp && mine >= u);
+                if (hit) {
+                    chosen = __shfl_sync(0xffffffffu, ii, __ffs(hit) - 1);
+                    break;
                 }
             }
         } else {
             chosen = V - 1;
             float cum = 0.f;
-            bool done = false;
-            for (int j0 = 0; j0 < n && !done; j0 += 32) {
+            for (int j0 = 0; j0 < n; j0 += 32) {
                 const int j = j0 + lane;
                 const int ii = j < n ? ci[j] : 0;
                 const float p = j < n ? __fmul_rn(e[ii], inv) : 0.f;
-                const int mq = min(32, n - j0);
-#pragma unroll 1
-                for (int q = 0; q < mq && !done; ++q) {
-                    cum = __fadd_rn(cum, __shfl_sync(0xffffffffu, p, q));
-                    if (cum >= u) { chosen = __shfl_sync(0xffffffffu, ii, q); done = true; }
+                float mine = 0.f;
+                cum = block_scan(cum, p, mine);
+                const unsigned hit = __ballot_sync(0xffffffffu, j < n && mine >= u);
+                if (hit) {
+                    chosen = __shfl_sync(0xffffffffu, ii, __ffs(hit) - 1);
+                    break;
                 }
             }
         }
