@@ -772,40 +772,74 @@ __device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, int chunk
     const auto qof = [&](int c) { return qkv + c * (GR + 2) * HD; };
     const auto kof = [&](int c) { return qkv + (c * (GR + 2) + GR) * HD; };
     const auto vof = [&](int c) { return qkv + (c * (GR + 2) + GR + 1) * HD; };
-    float * sc = qkv + 2 * (GR + 2) * HD;   // [2][MAX_GROUP][NCB] scores, then e^(s - m)
-    float * ml = sc + 2 * MAX_GROUP * NCB;  // [2][MAX_GROUP][2]
-    float * pv = ml + 4 * MAX_GROUP;        // [NCW][MAX_GROUP][HD]
     // per column: the group's q heads, then k and v of head g (rows of HD words)
     const bool ok = ll_fetch_plan(A.w.qkv, ncol, d.QKV, (GR + 2) * HD, GR, g * GR * HD, HD, 2, d.Q + g * HD, d.KV, HD, HD, ptag, qkv, A,
                                   S.ctrl, p);
     if (!consumers_ok(S, ok)) return false;
     stamp(A, p, 0);
+    // norm + RoPE of the q heads and k, one warp per vector; the warp of column c's k also
+    // writes k (f16, after RoPE) and v into the group's cache rows
+    const int lane = tid & 31;
     for (int v = tid >> 5; v < ncol * (GR + 1); v += NCW) {
         const int c = v / (GR + 1), j = v - c * (GR + 1);
         warp_norm_rope(j < GR ? qof(c) + j * HD : kof(c), j < GR ? qn : kn, A.rope_c + (pos + c) * HD, HD, d.eps_c, j == GR);
-    }
-    named_sync(BID, NCT);
-    for (int i = tid; i < ncol * HD; i += NCT) {
-        const int c = i / HD, e = i - c * HD;
-        kv[(static_cast<size_t>(pos + c) * 2 + 0) * HD + e] = __float2half_rn(kof(c)[e]);
-        kv[(static_cast<size_t>(pos + c) * 2 + 1) * HD + e] = __float2half_rn(vof(c)[e]);
+        if (j == GR) {
+            __syncwarp();
+            for (int e = lane; e < HD; e += 32) {
+                kv[(static_cast<size_t>(pos + c) * 2 + 0) * HD + e] = __float2half_rn(kof(c)[e]);
+                kv[(static_cast<size_t>(pos + c) * 2 + 1) * HD + e] = __float2half_rn(vof(c)[e]);
+            }
+        }
     }
     named_sync(BID, NCT);
     stamp(A, p, 1);
-    const float scale = rsqrtf(static_cast<float>(HD));
-    // column c attends to positions 0..pos+c (causal within the 2-column pass)
-    attn_scores(ncol, pos + ncol, GR, HD, scale, NCB, [&](int, int t) { return kv + static_cast<size_t>(t) * 2 * HD; },
-                [&](int c) { return static_cast<const float *>(qof(c)); },
-                [&](int c, int t) { return sc + c * MAX_GROUP * NCB + t; });
-    named_sync(BID, NCT);
-    attn_softmax(sc, NCB, ncol * MAX_GROUP, [&](int r) { return (r % MAX_GROUP) < GR ? pos + 1 + r / MAX_GROUP : 0; }, ml);
-    named_sync(BID, NCT);
-    attn_pv(ncol, GR, HD, [&](int c) { return pos + 1 + c; },
-            [&](int c, int j) { return static_cast<const float *>(sc + (c * MAX_GROUP + j) * NCB); },
-            [&](int, int t) { return static_cast<const __half *>(kv + (static_cast<size_t>(t) * 2 + 1) * HD); }, pv,
-            [&](int c, int j, int e, float sum) {
-                ll_store(A.w.attn + static_cast<size_t>(c) * d.Q + (g * GR + j) * HD + e, sum / ml[2 * (c * MAX_GROUP + j) + 1], tag);
-            });
+    // one warp per (column c, query head j) attends over positions 0..pos+c (<= NCB) with no
+    // CTA barrier: lanes t and t + 16 take the two halves of position t's dot product
+    // (16-byte loads rotated by t, so the 16 rows do not hit one bank), softmax in 16-lane
+    // halves by shuffles, then lane l sums dims 4l..4l+3 of P.V.
+    const int w = tid >> 5;
+    if (w < ncol * GR) {
+        const int c = w / GR, j = w - c * GR;
+        const int n = pos + c + 1;
+        const float * q = qof(c) + j * HD;
+        const int t = lane & 15, hh = lane >> 4;
+        float dot = 0.f;
+        if (t < n) {
+            const __half * kr = kv + static_cast<size_t>(t) * 2 * HD + hh * (HD / 2);
+            const float * qh = q + hh * (HD / 2);
+#pragma unroll
+            for (int i = 0; i < HD / 2; i += 8) {
+                const int o = (i + 8 * t) & (HD / 2 - 1);
+                const uint4 kk = *reinterpret_cast<const uint4 *>(kr + o);
+                const float4 qa = *reinterpret_cast<const float4 *>(qh + o), qb = *reinterpret_cast<const float4 *>(qh + o + 4);
+                dot += dot8h(kk, qa, qb);
+            }
+        }
+        dot += __shfl_xor_sync(0xffffffffu, dot, 16);
+        const float sc = t < n ? dot * rsqrtf(static_cast<float>(HD)) : -INFINITY;
+        float m = sc;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float ev = t < n ? expf(sc - m) : 0.f;
+        float z = ev;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int tt = 0; tt < n; ++tt) {
+            const float pt = __shfl_sync(0xffffffffu, ev, tt);
+            const uint2 vv = *reinterpret_cast<const uint2 *>(kv + (static_cast<size_t>(tt) * 2 + 1) * HD + lane * 4);
+            const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
+            const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+            acc[0] = fmaf(pt, v01.x, acc[0]);
+            acc[1] = fmaf(pt, v01.y, acc[1]);
+            acc[2] = fmaf(pt, v23.x, acc[2]);
+            acc[3] = fmaf(pt, v23.y, acc[3]);
+        }
+        const float inv = 1.f / z;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            ll_store(A.w.attn + static_cast<size_t>(c) * d.Q + (g * GR + j) * HD + lane * 4 + e, acc[e] * inv, tag);
+    }
     stamp(A, p, 2);
     named_sync(BID, NCT);
     return true;
