@@ -226,39 +226,65 @@ def vocoder_bench(dev, w, reps: int = 20, chunks=(4, 16), warm: int = 3):
                              "passes run f16 hi + lo activation halves, so issued MMA work is twice the FLOPs"}
 
 
-def serving_bench(dev, w, reps: int = 10, n_text: int = 200, first_frames: int = 4):
-    """configs[4], one stream on one GPU: time to first audio (TTFA) = token ids of a 200-id text
-    prompt -> prompt rows -> 28-layer prefill -> the first `first_frames` frames -> their PCM
-    through the vocoder (graph.h:29), wall clock per utterance, p50 over reps; plus the
-    prefill device time."""
+def serving_bench(dev, w, rank: int, world: int, dist, streams: int = 8, frames: int = 400, n_text: int = 200):
+    """configs[4], request-parallel: `streams` synthetic utterances (a 200-id text prompt of
+    uniform ids, prefill, `frames` frames, their PCM streamed through the vocoder 4 frames
+    first, then 16 at a time: Graph::synth, graph.cpp:52-111) dealt round-robin to the
+    ranks, each rank running its streams one after another through the public API (host ids
+    in, host PCM out). Aggregate frames/s = all frames / the slowest rank's wall time; time
+    to first audio is SynthStats::ttfa_ms of every stream."""
     import numpy as np
+    import torch
     from navi_b200 import engine, model_spec
     p = w.params
     cfg = model_spec.full_config(p.decoder_dim)
-    g = engine.Graph(dev, w, max_prompt_tokens=1024, max_frames=first_frames + 8)
-    voc = engine.Vocoder(dev, w, max_chunk_frames=first_frames)
+    g = engine.Graph(dev, w, max_prompt_tokens=1024, max_frames=frames + 8, vocoder_chunk=16)
     s = engine.Sampling(temperature=0.9, top_k=50, top_p=0.9, repetition_penalty=1.05, cp_temperature=0.9, cp_top_k=50,
-                        cp_top_p=0.9, min_frames=first_frames + 1, rng=1)
-    rng = np.random.default_rng(4)
-    spk = rng.standard_normal(p.talker.hidden).astype(np.float32)
-    ttfa, pre, rows = [], [], 0
-    for i in range(reps + 2):
-        ids = ([cfg.im_start_id, cfg.assistant_id, 198] + rng.integers(0, cfg.text_vocab, n_text).tolist()
-               + [cfg.im_end_id, 198, cfg.im_start_id, cfg.assistant_id, 198])
-        t0 = time.perf_counter()
-        codes, st = g.synth_ids(ids, "english", spk, s, 77 + i, first_frames)
-        voc.reset()
-        pcm = voc.decode(codes)
-        t1 = time.perf_counter()
-        assert codes.shape[0] == first_frames and pcm.size == first_frames * voc.samples_per_frame
-        if i >= 2:
-            ttfa.append((t1 - t0) * 1000.0)
-            pre.append(st.prefill_ms)
+                        cp_top_p=0.9, min_frames=frames, rng=1)
+    spk = np.random.default_rng(4).standard_normal(p.talker.hidden).astype(np.float32)
+
+    def ids_of(j):
+        r = np.random.default_rng(1000 + j)
+        return ([cfg.im_start_id, cfg.assistant_id, 198] + r.integers(0, cfg.text_vocab, n_text).tolist()
+                + [cfg.im_end_id, 198, cfg.im_start_id, cfg.assistant_id, 198])
+
+    for j in range(2):                      # warm-up utterances
+        g.synth(ids_of(-1 - j), "english", spk, s, 5 + j, 24, first_batch=4, vocoder_batch=16)
+    mine = [j for j in range(streams) if j % world == rank]
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    ttfa, rtf, pre, voc_ms, n_frames, pcm_samples = [], [], [], 0.0, 0, 0
+    for j in mine:
+        codes, pcm, st, _ = g.synth(ids_of(j), "english", spk, s, 77 + j, frames, first_batch=4, vocoder_batch=16)
+        assert st.n_frames == frames and pcm.size == frames * p.codec_upsample
+        ttfa.append(st.ttfa_ms)
+        rtf.append(st.rtf)
+        pre.append(st.prefill_ms)
+        voc_ms += st.vocoder_ms
+        n_frames += st.n_frames
+        pcm_samples += pcm.size
+    elapsed = time.perf_counter() - t0
     g.close()
-    voc.close()
-    return {"workload": f"configs[4] single stream: {n_text}-id text prompt, first {first_frames} frames + their PCM",
-            "ttfa_ms_p50": round(float(np.median(ttfa)), 3), "ttfa_ms_min": round(float(min(ttfa)), 3),
-            "prefill_ms_p50": round(float(np.median(pre)), 3), "reps": reps}
+    stats = {"elapsed": elapsed, "frames": n_frames, "ttfa": ttfa, "rtf": rtf, "pre": pre, "voc_ms": voc_ms}
+    if dist:
+        out = [None] * world
+        dist.all_gather_object(out, stats)
+    else:
+        out = [stats]
+    slowest = max(o["elapsed"] for o in out)
+    total = sum(o["frames"] for o in out)
+    allt = [t for o in out for t in o["ttfa"]]
+    return {"workload": f"configs[4]: {streams} streams x ({n_text}-id prompt, prefill, {frames} frames, PCM in batches "
+                        f"of 4 then 16), round-robin over {world} GPU(s), streams on a GPU one after another",
+            "frames_per_s": round(total / slowest, 2), "ttfa_ms_p50": round(float(np.median(allt)), 3),
+            "ttfa_ms_max": round(float(max(allt)), 3),
+            "prefill_ms_p50": round(float(np.median([t for o in out for t in o["pre"]])), 3),
+            "rtf_p50": round(float(np.median([t for o in out for t in o["rtf"]])), 5),
+            "vocoder_ms_per_frame": round(sum(o["voc_ms"] for o in out) / total, 4),
+            "streams": streams, "frames_per_stream": frames, "wall_s": round(slowest, 3),
+            "timing": "wall clock around Graph::synth calls (host ids in, host PCM out), max over ranks"}
 
 
 def vocoder_cpu_baseline(n_frames: int = 4):
@@ -415,6 +441,7 @@ def run_ours(args):
     frame.set_profile(False)
 
     ms, e2e_ms, value, e2e_value = combine_ranks(ms, e2e_ms, world, dist, f"cuda:{local}")
+    serving = serving_bench(dev, w, rank, world, dist, streams=args.streams) if args.streams > 0 else None
     if rank == 0:
         ab = algorithmic_bytes(p, L)
         peak, kind = measured_peak()
@@ -438,9 +465,10 @@ def run_ours(args):
             "phase_profile_us": {"total": round(float(prof.sum()), 1), "n_phases": int(len(prof)),
                                  "median": round(float(np.median(prof)), 2), "max": round(float(prof.max()), 2)},
         }
+        if serving:
+            line["serving"] = serving
         if args.vocoder:
             line["vocoder"] = vocoder_bench(dev, w)
-            line["serving"] = serving_bench(dev, w)
         if args.cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(L)
             if args.vocoder:
@@ -462,6 +490,7 @@ def main():
     ap.add_argument("--no-vocoder", dest="vocoder", action="store_false", help="skip the configs[3] vocoder line")
     ap.add_argument("--vocoder-only", action="store_true", help="run only the configs[3] vocoder measurement")
     ap.add_argument("--voc-chunks", default="4,16", help="vocoder chunk lengths (frames), comma separated")
+    ap.add_argument("--streams", type=int, default=8, help="configs[4] utterances over all GPUs (64 = the full config; 0 = skip)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -202,21 +202,37 @@ void navi_frame_destroy(navi_frame * f);
 
 typedef struct navi_graph navi_graph;
 
-typedef struct navi_synth_stats {   /* SynthStats, graph.h:36-41 */
+typedef struct navi_synth_stats {   /* SynthStats, graph.h:43-48 */
     int n_tokens, n_frames, hit_cap, eos;
     double prefill_ms, frames_ms, total_ms;
     double ttfc_ms;                 /* time to the first frame's codes */
+    double vocoder_ms;              /* wall time inside vocoder calls */
+    double ttfa_ms;                 /* time to the first PCM batch (0 for navi_graph_synth_ids) */
+    double audio_s, rtf;            /* n_frames * codec_upsample / sample_rate; total_ms / 1000 / audio_s */
 } navi_synth_stats;
 
-/* Graph::load (graph.cpp:22-44) minus the tokenizer, vocoder and speaker encoder: a talker
- * (prompts up to max_prompt_tokens, KV for max_prompt_tokens + max_frames + 1 positions) and a
- * frame kernel on the uploaded weights. */
+/* Graph::load (graph.cpp:22-44) minus the tokenizer and speaker encoder: a talker (prompts up
+ * to max_prompt_tokens, KV for max_prompt_tokens + max_frames + 1 positions), a frame kernel
+ * and, for vocoder_chunk > 0, a vocoder of vocoder_chunk frames per pass (the reference's
+ * vocoder_chunk argument, default 32) on the uploaded weights. */
 int navi_graph_create(navi_device * dev, const navi_weights * w, const navi_frame_opts * opts, int max_prompt_tokens, int max_frames,
-                      navi_graph ** out);
-/* Graph::synth (graph.cpp:52-111) from token ids (see navi_talker_build_prompt): writes the 16
- * codes of each frame to codes[16 * i] (room for codes_cap frames) until EOS or max_frames. */
+                      int vocoder_chunk, navi_graph ** out);
+/* Codes only: the loop of Graph::synth (graph.cpp:52-111) from token ids (see
+ * navi_talker_build_prompt) without the vocoder; writes the 16 codes of each frame to
+ * codes[16 * i] (room for codes_cap frames) until EOS or max_frames. */
 int navi_graph_synth_ids(navi_graph * g, const int32_t * ids, int n_ids, const char * language, const float * speaker,
                          const navi_sampling * s, uint64_t seed, int max_frames, int32_t * codes, int codes_cap, navi_synth_stats * st);
+
+/* Receives one vocoder batch of 24 kHz f32 PCM (valid during the call only). */
+typedef void (*navi_pcm_fn)(const float * pcm, int n_samples, void * user);
+/* Graph::synth (graph.cpp:52-111) with audio: as navi_graph_synth_ids, and the frames go
+ * through the vocoder in batches of first_batch, then vocoder_batch frames (0 = the
+ * vocoder's chunk; SynthRequest::first_batch / vocoder_batch, graph.h:39-40) with each
+ * batch's PCM handed to on_pcm. codes may be NULL (codes_cap is then ignored and max_frames
+ * alone bounds the loop). NAVI_E_ARG for a graph created without a vocoder. */
+int navi_graph_synth(navi_graph * g, const int32_t * ids, int n_ids, const char * language, const float * speaker,
+                     const navi_sampling * s, uint64_t seed, int max_frames, int first_batch, int vocoder_batch, int32_t * codes,
+                     int codes_cap, navi_pcm_fn on_pcm, void * user, navi_synth_stats * st);
 void navi_graph_destroy(navi_graph * g);
 
 /* ---- vocoder: replaces navi::qwen3tts::Vocoder (model/qwen3tts/vocoder.h:27-55) ----------- */

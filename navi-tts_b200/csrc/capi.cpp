@@ -419,48 +419,89 @@ double navi_talker_last_ms(const navi_talker * t) { return t ? t->t->last_ms() :
 void navi_talker_destroy(navi_talker * t) { delete t; }
 
 int navi_graph_create(navi_device * dev, const navi_weights * w, const navi_frame_opts * opts, int max_prompt_tokens, int max_frames,
-                      navi_graph ** out) {
+                      int vocoder_chunk, navi_graph ** out) {
     return guard([&]() -> int {
         if (!dev || !w || !out) return set_err(NAVI_E_ARG, "NULL argument");
+        if (vocoder_chunk < 0) return set_err(NAVI_E_ARG, "vocoder_chunk must be >= 0");
         navi::qwen3tts::FrameOptions fo;
         if (opts) {
             fo.blocks_per_mp = opts->blocks_per_mp;
             if (opts->deadline_us) fo.deadline_us = opts->deadline_us;
         }
         auto g = std::make_unique<navi_graph>();
-        g->g = navi::qwen3tts::Graph::create(*dev->dev, *w->w, fo, max_prompt_tokens, max_frames);
+        g->g = navi::qwen3tts::Graph::create(*dev->dev, *w->w, fo, max_prompt_tokens, max_frames, vocoder_chunk);
         g->hidden = w->w->params().talker.hidden;
         *out = g.release();
         return NAVI_OK;
     });
 }
 
+namespace {
+
+void put_stats(const navi::qwen3tts::SynthStats & s, navi_synth_stats * st) {
+    if (!st) return;
+    st->n_tokens = s.n_tokens;
+    st->n_frames = s.n_frames;
+    st->hit_cap = s.hit_cap ? 1 : 0;
+    st->eos = s.eos ? 1 : 0;
+    st->prefill_ms = s.prefill_ms;
+    st->frames_ms = s.frames_ms;
+    st->total_ms = s.total_ms;
+    st->ttfc_ms = s.ttfc_ms;
+    st->vocoder_ms = s.vocoder_ms;
+    st->ttfa_ms = s.ttfa_ms;
+    st->audio_s = s.audio_s;
+    st->rtf = s.rtf;
+}
+
+navi::qwen3tts::SynthRequest make_request(const navi_graph * g, const int32_t * ids, int n_ids, const char * language,
+                                          const float * speaker, const navi_sampling * s, uint64_t seed, int max_frames) {
+    navi::qwen3tts::SynthRequest req;
+    req.ids = std::span<const std::int32_t>(ids, static_cast<size_t>(n_ids));
+    req.language = language ? language : "";
+    req.speaker = std::span<const float>(speaker, static_cast<size_t>(g->hidden));
+    req.seed = seed;
+    req.max_frames = max_frames;
+    req.sampling = to_sampling(s);
+    return req;
+}
+
+} // namespace
+
 int navi_graph_synth_ids(navi_graph * g, const int32_t * ids, int n_ids, const char * language, const float * speaker,
                          const navi_sampling * s, uint64_t seed, int max_frames, int32_t * codes, int codes_cap, navi_synth_stats * st) {
     return guard([&]() -> int {
         if (!g || !ids || n_ids <= 0 || !speaker || !codes || codes_cap <= 0) return set_err(NAVI_E_ARG, "bad argument");
-        navi::qwen3tts::SynthRequest req;
-        req.ids = std::span<const std::int32_t>(ids, static_cast<size_t>(n_ids));
-        req.language = language ? language : "";
-        req.speaker = std::span<const float>(speaker, static_cast<size_t>(g->hidden));
-        req.seed = seed;
-        req.max_frames = std::min(max_frames, codes_cap);
-        req.sampling = to_sampling(s);
+        auto req = make_request(g, ids, n_ids, language, speaker, s, seed, std::min(max_frames, codes_cap));
         int n = 0;
         const auto stats = g->g->synth(req, [&](const std::int32_t * c) {
             std::memcpy(codes + static_cast<size_t>(n) * 16, c, 16 * sizeof(int32_t));
             ++n;
         });
-        if (st) {
-            st->n_tokens = stats.n_tokens;
-            st->n_frames = stats.n_frames;
-            st->hit_cap = stats.hit_cap ? 1 : 0;
-            st->eos = stats.eos ? 1 : 0;
-            st->prefill_ms = stats.prefill_ms;
-            st->frames_ms = stats.frames_ms;
-            st->total_ms = stats.total_ms;
-            st->ttfc_ms = stats.ttfc_ms;
-        }
+        put_stats(stats, st);
+        return NAVI_OK;
+    });
+}
+
+int navi_graph_synth(navi_graph * g, const int32_t * ids, int n_ids, const char * language, const float * speaker,
+                     const navi_sampling * s, uint64_t seed, int max_frames, int first_batch, int vocoder_batch, int32_t * codes,
+                     int codes_cap, navi_pcm_fn on_pcm, void * user, navi_synth_stats * st) {
+    return guard([&]() -> int {
+        if (!g || !ids || n_ids <= 0 || !speaker || !on_pcm || (codes && codes_cap <= 0)) return set_err(NAVI_E_ARG, "bad argument");
+        if (first_batch < 0 || vocoder_batch < 0) return set_err(NAVI_E_ARG, "batch sizes must be >= 0");
+        if (!g->g->vocoder()) return set_err(NAVI_E_ARG, "graph created without a vocoder (vocoder_chunk = 0)");
+        auto req = make_request(g, ids, n_ids, language, speaker, s, seed, codes ? std::min(max_frames, codes_cap) : max_frames);
+        req.first_batch = first_batch;
+        req.vocoder_batch = vocoder_batch;
+        int n = 0;
+        const auto stats = g->g->synth(
+            req,
+            [&](const std::int32_t * c) {
+                if (codes) std::memcpy(codes + static_cast<size_t>(n) * 16, c, 16 * sizeof(int32_t));
+                ++n;
+            },
+            [&](std::span<const float> pcm) { on_pcm(pcm.data(), static_cast<int>(pcm.size()), user); });
+        put_stats(stats, st);
         return NAVI_OK;
     });
 }

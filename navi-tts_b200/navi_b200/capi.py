@@ -59,7 +59,8 @@ class Prompt(ctypes.Structure):
 
 class SynthStats(ctypes.Structure):
     _fields_ = [("n_tokens", c_int), ("n_frames", c_int), ("hit_cap", c_int), ("eos", c_int), ("prefill_ms", c_double),
-                ("frames_ms", c_double), ("total_ms", c_double), ("ttfc_ms", c_double)]
+                ("frames_ms", c_double), ("total_ms", c_double), ("ttfc_ms", c_double), ("vocoder_ms", c_double),
+                ("ttfa_ms", c_double), ("audio_s", c_double), ("rtf", c_double)]
 
 
 class ConvArgs(ctypes.Structure):
@@ -70,6 +71,7 @@ class ConvArgs(ctypes.Structure):
 
 
 STAGE_FN = ctypes.CFUNCTYPE(None, c_void_p, c_char_p, c_void_p, c_int, c_int)
+PCM_FN = ctypes.CFUNCTYPE(None, POINTER(c_float), c_int, c_void_p)
 
 
 class FrameOpts(ctypes.Structure):
@@ -116,9 +118,11 @@ SIGNATURES = [
     ("navi_frame_set_step_in", c_int, [c_void_p, c_void_p]),
     ("navi_frame_grid_blocks", c_int, [c_void_p]),
     ("navi_frame_destroy", None, [c_void_p]),
-    ("navi_graph_create", c_int, [c_void_p, c_void_p, POINTER(FrameOpts), c_int, c_int, POINTER(c_void_p)]),
+    ("navi_graph_create", c_int, [c_void_p, c_void_p, POINTER(FrameOpts), c_int, c_int, c_int, POINTER(c_void_p)]),
     ("navi_graph_synth_ids", c_int, [c_void_p, POINTER(c_int32), c_int, c_char_p, POINTER(c_float), POINTER(Sampling), c_uint64,
                                      c_int, POINTER(c_int32), c_int, POINTER(SynthStats)]),
+    ("navi_graph_synth", c_int, [c_void_p, POINTER(c_int32), c_int, c_char_p, POINTER(c_float), POINTER(Sampling), c_uint64, c_int,
+                                 c_int, c_int, POINTER(c_int32), c_int, PCM_FN, c_void_p, POINTER(SynthStats)]),
     ("navi_graph_destroy", None, [c_void_p]),
     ("navi_vocoder_create", c_int, [c_void_p, c_void_p, c_int, c_int, POINTER(c_void_p)]),
     ("navi_vocoder_reset", c_int, [c_void_p]),

@@ -206,16 +206,18 @@ class Talker:
 
 
 class Graph:
-    """navi::qwen3tts::Graph (graph.h:43-79) from token ids: prompt, prefill and the frame loop."""
+    """navi::qwen3tts::Graph (graph.h:43-79) from token ids: prompt, prefill, the frame loop and,
+    with vocoder_chunk > 0, the streaming vocoder."""
 
-    def __init__(self, dev: Device, w: Weights, max_prompt_tokens: int = 1024, max_frames: int = 2048, deadline_us: int = 0):
+    def __init__(self, dev: Device, w: Weights, max_prompt_tokens: int = 1024, max_frames: int = 2048, deadline_us: int = 0,
+                 vocoder_chunk: int = 32):
         h = c_void_p()
         opts = capi.FrameOpts(1, deadline_us)
-        check(lib().navi_graph_create(dev.h, w.h, byref(opts), max_prompt_tokens, max_frames, byref(h)))
+        check(lib().navi_graph_create(dev.h, w.h, byref(opts), max_prompt_tokens, max_frames, vocoder_chunk, byref(h)))
         self.h, self.dev, self.w = h, dev, w
 
     def synth_ids(self, ids, language: str, speaker, s: Sampling, seed: int, max_frames: int):
-        """(codes [n_frames, 16] int32, stats) of one utterance."""
+        """(codes [n_frames, 16] int32, stats) of one utterance, without the vocoder."""
         import numpy as np
         ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
         spk = np.ascontiguousarray(np.asarray(speaker, dtype=np.float32))
@@ -225,6 +227,31 @@ class Graph:
                                          spk.ctypes.data_as(POINTER(ctypes.c_float)), byref(s.c()), seed, max_frames,
                                          codes.ctypes.data_as(POINTER(c_int32)), max_frames, byref(st)))
         return codes[:st.n_frames], st
+
+    def synth(self, ids, language: str, speaker, s: Sampling, seed: int, max_frames: int, first_batch: int = 4,
+              vocoder_batch: int = 16, on_pcm=None):
+        """Graph::synth (graph.cpp:52-111): (codes [n_frames, 16], PCM [n_frames * 1920] f32, stats,
+        the sample count of every vocoder batch). on_pcm(np.ndarray), if given, sees each batch
+        as it is produced."""
+        import numpy as np
+        ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+        spk = np.ascontiguousarray(np.asarray(speaker, dtype=np.float32))
+        codes = np.zeros((max_frames, 16), np.int32)
+        chunks = []
+
+        def take(ptr, n, _user):
+            a = np.ctypeslib.as_array(ptr, shape=(n,)).copy()
+            chunks.append(a)
+            if on_pcm is not None:
+                on_pcm(a)
+
+        fn = capi.PCM_FN(take)
+        st = capi.SynthStats()
+        check(lib().navi_graph_synth(self.h, ids.ctypes.data_as(POINTER(c_int32)), len(ids), (language or "").encode(),
+                                     spk.ctypes.data_as(POINTER(ctypes.c_float)), byref(s.c()), seed, max_frames, first_batch,
+                                     vocoder_batch, codes.ctypes.data_as(POINTER(c_int32)), max_frames, fn, None, byref(st)))
+        pcm = np.concatenate(chunks) if chunks else np.zeros(0, np.float32)
+        return codes[:st.n_frames], pcm, st, [len(c) for c in chunks]
 
     def close(self):
         if self.h:

@@ -6,7 +6,7 @@ repeatability; and the stop rules (EOS or max_frames)."""
 import numpy as np
 import pytest
 
-from navi_b200 import engine
+from navi_b200 import capi, engine
 from oracle import model as om
 
 pytestmark = pytest.mark.gpu
@@ -72,3 +72,53 @@ def test_graph_is_seeded(small_navi):
     c, _ = g.synth_ids(ids, "auto", spk, s, 6, 10)
     assert np.array_equal(a, b)
     assert not np.array_equal(a, c)
+
+
+def test_graph_streams_pcm_of_its_codes(small_navi):
+    """Graph::synth with audio (graph.cpp:73-108): the frames are vocoded in a first batch of
+    first_batch frames, then batches of vocoder_batch, then the remainder; the PCM equals one
+    vocoder pass over the same codes (batching never changes it), and the codes equal the
+    codes-only loop's."""
+    W = om.Weights.from_navi(small_navi)
+    dev = engine.Device(0)
+    w = engine.Weights(dev, small_navi)
+    g = engine.Graph(dev, w, max_prompt_tokens=256, max_frames=64, vocoder_chunk=8)
+    ids = _ids(W.cfg, 7, seed=5)
+    spk = np.random.default_rng(6).standard_normal(W.tl.hidden).astype(np.float32)
+    s = engine.Sampling(top_p=0.9, cp_top_p=0.9, min_frames=40)
+    seen = []
+    codes, pcm, st, sizes = g.synth(ids, "english", spk, s, 21, 23, first_batch=3, vocoder_batch=8,
+                                    on_pcm=lambda a: seen.append(a.size))
+    want_codes, _ = g.synth_ids(ids, "english", spk, s, 21, 23)
+    assert np.array_equal(codes, want_codes)
+    assert st.n_frames == 23 and st.hit_cap == 1
+    spf = W.cfg.samples_per_frame
+    assert sizes == seen == [3 * spf, 8 * spf, 8 * spf, 4 * spf]
+    voc = engine.Vocoder(dev, w, max_chunk_frames=32)
+    want = voc.decode(codes)
+    assert pcm.shape == want.shape
+    np.testing.assert_allclose(pcm, want, rtol=0, atol=1e-5)
+    assert np.abs(pcm).max() <= 1.0
+    assert st.vocoder_ms > 0 and 0 < st.ttfc_ms <= st.ttfa_ms <= st.total_ms
+    assert st.audio_s == pytest.approx(23 * spf / W.cfg.sample_rate)
+    assert st.rtf == pytest.approx(st.total_ms / 1000.0 / st.audio_s)
+    # the vocoder's chunk caps the batch; first_batch 0 = vocoder_batch
+    _, pcm2, _, sizes2 = g.synth(ids, "english", spk, s, 21, 23, first_batch=0, vocoder_batch=100)
+    assert sizes2 == [8 * spf, 8 * spf, 7 * spf]
+    np.testing.assert_allclose(pcm2, want, rtol=0, atol=1e-5)
+    g.close()
+    voc.close()
+
+
+def test_graph_without_vocoder_refuses_pcm(small_navi):
+    W = om.Weights.from_navi(small_navi)
+    dev = engine.Device(0)
+    w = engine.Weights(dev, small_navi)
+    g = engine.Graph(dev, w, max_prompt_tokens=256, max_frames=16, vocoder_chunk=0)
+    ids = _ids(W.cfg, 5, seed=1)
+    spk = np.zeros(W.tl.hidden, np.float32)
+    codes, st = g.synth_ids(ids, "english", spk, engine.Sampling(), 1, 4)
+    assert st.ttfa_ms == 0 and st.vocoder_ms == 0
+    with pytest.raises(capi.NaviError):
+        g.synth(ids, "english", spk, engine.Sampling(), 1, 4)
+    g.close()
