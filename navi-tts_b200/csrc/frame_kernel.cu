@@ -100,8 +100,13 @@ __device__ __forceinline__ const uint8_t * chunk_at(const Sm & S, int chunk, uin
     return S.ring + (x < cut ? S.meta_off[slot] + x : x - cut);
 }
 
+// The producer warp streams every phase's slice into the ring, in phase order. All 32 lanes
+// take the same ring decisions; lane 0 writes the slot's bookkeeping and arms its mbarrier
+// with the chunk's byte count, then the chunk's rows are dealt to the lanes round-robin, so
+// the many small row copies of an attention chunk (one per cached position) are issued 32 at
+// a time instead of one after another.
 __device__ void producer(const Args & A, Sm & S) {
-    if ((threadIdx.x & 31) != 0) return;
+    const int lane = threadIdx.x & 31;
     const ModelW & W = *A.mw;
     const int G = gridDim.x, b = blockIdx.x;
     const Rows R = cta_rows(A.d, b, G);
@@ -146,35 +151,44 @@ __device__ void producer(const Args & A, Sm & S) {
             }
             __nanosleep(64);
         }
+        aborted = __shfl_sync(0xffffffffu, aborted ? 1 : 0, 0) != 0;
         if (aborted) break;
         const int slot = chunk % NSLOT;
-        S.meta_off[slot] = cut > 0 ? pos : 0u;
-        S.meta_split[slot] = cut;
+        const uint32_t moff = cut > 0 ? pos : 0u;
+        if (lane == 0) {
+            S.meta_off[slot] = moff;
+            S.meta_split[slot] = cut;
+            S.meta_end[slot] = end;
+            mbar_arrive_expect_tx(&S.bars[slot], total);
+        }
         issued = end;
-        S.meta_end[slot] = issued;
-        mbar_arrive_expect_tx(&S.bars[slot], total);
+        __syncwarp();
         const bool kept = ph.op >= CQKV && ph.op <= CDOWN && ph.layer < A.cp_keep_layers;
         const uint64_t pol = kept ? keep : stream;
-        uint32_t lo = 0;   // logical offset of the next byte
+        uint32_t lo = 0;   // logical offset of the segment's first byte
+        uint32_t gr = 0;   // rows of the chunk before this segment: row gr + r goes to lane (gr + r) % 32
         for (int i = 0; i < ns; ++i) {
-            for (uint32_t r = 0; r < seg[i].rows; ++r) {
+            for (uint32_t r = (lane - gr % 32u + 32u) % 32u; r < seg[i].rows; r += 32) {
                 const char * src = static_cast<const char *>(seg[i].src) + static_cast<size_t>(r) * seg[i].stride;
+                const uint32_t rl = lo + r * seg[i].bytes;
                 for (uint32_t o = 0; o < seg[i].bytes;) {
                     // up to PIECE bytes, not across the cut
-                    const uint32_t x = lo + o;
+                    const uint32_t x = rl + o;
                     uint32_t n = min(PIECE, seg[i].bytes - o);
                     if (x < cut) n = min(n, cut - x);
-                    const uint32_t phys = x < cut ? S.meta_off[slot] + x : x - cut;
+                    const uint32_t phys = x < cut ? moff + x : x - cut;
                     bulk_g2s_hint(S.ring + phys, src + o, n, &S.bars[slot], pol);
                     o += n;
                 }
-                lo += seg[i].bytes;
             }
+            lo += seg[i].bytes * seg[i].rows;
+            gr += seg[i].rows;
         }
         ++chunk;
     }
     // Leave only when no copy into this CTA's shared memory is still in flight: on the
     // normal path the consumers have waited on every chunk; after an abort wait here.
+    if (lane != 0) return;
     const uint64_t t0 = globaltimer();
     while (S.ctrl->consumed < chunk && !S.ctrl->abort) {
         __nanosleep(256);
@@ -347,7 +361,11 @@ __device__ __forceinline__ void gemv_slice(At && at, uint32_t woff, int nr, int 
     const uint32_t kb = static_cast<uint32_t>(nr) * 16u;
     const __half * wa = reinterpret_cast<const __half *>(at(woff + static_cast<uint32_t>(k0) * kb));
     const __half * wb = PAIR ? reinterpret_cast<const __half *>(at(woff + static_cast<uint32_t>(nk + k0) * kb)) : wa;
-    // rows beyond 32 lanes (small grids) are taken in rounds of R2
+    // rows beyond 32 lanes (small grids) are taken in rounds of R2. Every loop stays rolled:
+    // this code runs with a cold instruction cache in every phase (the phases in between
+    // evict it), and an unrolled body costs more in instruction fetch than it saves in
+    // issue (measured 1,300-2,600 fewer cycles per call cold than a 4-way unrolled body).
+#pragma unroll 1
     for (int rb = 0; rb < nr; rb += R2) {
         const int row = rb + (lane & (R2 - 1));
         const bool live = row < nr;
@@ -355,60 +373,30 @@ __device__ __forceinline__ void gemv_slice(At && at, uint32_t woff, int nr, int 
 #pragma unroll
         for (int v = 0; v < NV; ++v) acc[v] = 0.f;
         if (live) {
-            // this lane's chunks: k0 + j, k0 + j + J, ... < k1; four per step, loads first
+            // this lane's chunks: k0 + j, k0 + j + J, ... < k1
             const __half * pw = wa + (static_cast<size_t>(j) * nr + row) * 8;
             const __half * pu = wb + (static_cast<size_t>(j) * nr + row) * 8;
             const float * px = xin + (k0 + j) * 8;
             const int cnt = (k0 + j < k1) ? (k1 - (k0 + j) + J - 1) >> lj : 0;
-            float a4[4][NV];
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-                for (int v = 0; v < NV; ++v) a4[q][v] = 0.f;
-            int i = 0;
-            for (; i + 4 <= cnt; i += 4) {
-                uint4 ga[4], gb[4];
-                float4 xa[4][NC], xb[4][NC];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    ga[q] = *reinterpret_cast<const uint4 *>(pw + q * cs);
-                    if constexpr (PAIR) gb[q] = *reinterpret_cast<const uint4 *>(pu + q * cs);
-#pragma unroll
-                    for (int c = 0; c < NC; ++c) {
-                        xa[q][c] = *reinterpret_cast<const float4 *>(px + c * xstride + q * J * 8);
-                        xb[q][c] = *reinterpret_cast<const float4 *>(px + c * xstride + q * J * 8 + 4);
-                    }
-                }
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-#pragma unroll
-                    for (int c = 0; c < NC; ++c) {
-                        a4[q][c * (PAIR ? 2 : 1)] += dot8h(ga[q], xa[q][c], xb[q][c]);
-                        if constexpr (PAIR) a4[q][c * 2 + 1] += dot8h(gb[q], xa[q][c], xb[q][c]);
-                    }
-                pw += 4 * cs;
-                pu += 4 * cs;
-                px += 4 * J * 8;
-            }
-            for (; i < cnt; ++i) {
-                const uint4 ga1 = *reinterpret_cast<const uint4 *>(pw);
-                uint4 gb1 = make_uint4(0, 0, 0, 0);
-                if constexpr (PAIR) gb1 = *reinterpret_cast<const uint4 *>(pu);
+#pragma unroll 1
+            for (int i = 0; i < cnt; ++i) {
+                const uint4 ga = *reinterpret_cast<const uint4 *>(pw);
+                uint4 gb = make_uint4(0, 0, 0, 0);
+                if constexpr (PAIR) gb = *reinterpret_cast<const uint4 *>(pu);
 #pragma unroll
                 for (int c = 0; c < NC; ++c) {
                     const float4 xa = *reinterpret_cast<const float4 *>(px + c * xstride);
                     const float4 xb = *reinterpret_cast<const float4 *>(px + c * xstride + 4);
-                    a4[0][c * (PAIR ? 2 : 1)] += dot8h(ga1, xa, xb);
-                    if constexpr (PAIR) a4[0][c * 2 + 1] += dot8h(gb1, xa, xb);
+                    acc[c * (PAIR ? 2 : 1)] += dot8h(ga, xa, xb);
+                    if constexpr (PAIR) acc[c * 2 + 1] += dot8h(gb, xa, xb);
                 }
                 pw += cs;
                 pu += cs;
                 px += J * 8;
             }
-#pragma unroll
-            for (int v = 0; v < NV; ++v) acc[v] = (a4[0][v] + a4[1][v]) + (a4[2][v] + a4[3][v]);
         }
         // fold the J lanes of each row (lanes row, row + R2, ...); dead lanes hold zeros
+#pragma unroll 1
         for (int s = 16; s >= R2; s >>= 1)
 #pragma unroll
             for (int v = 0; v < NV; ++v) acc[v] += __shfl_down_sync(0xffffffffu, acc[v], s);

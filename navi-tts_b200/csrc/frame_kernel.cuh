@@ -5,7 +5,7 @@
 // What it computes is the reference's k_frame (model/qwen3tts/frame.hip:517-579);
 // how it is organised is B200-specific:
 //
-//  * One CTA per SM (148), 12 consumer warps + 1 producer warp.
+//  * One CTA per SM (148), 11 consumer warps + 1 producer warp.
 //  * The producer warp walks the same phase program as the consumers and streams
 //    this CTA's slice of every weight matrix (rows [r0, r1) of the matrix; weights
 //    never depend on activations) into a shared-memory ring with cp.async.bulk on
@@ -35,7 +35,10 @@
 
 namespace navi::fk {
 
-constexpr int NCW = 12;                 // consumer warps
+// 11 consumer warps + the producer = 12 warps, 3 on each of the SM's 4 schedulers, whose
+// register files (16K registers each) then allow 168 registers a thread; a 13th warp would
+// put 4 warps on one scheduler and cap every thread at 128, where this kernel spills.
+constexpr int NCW = 11;                 // consumer warps
 constexpr int NCT = NCW * 32;           // consumer threads
 constexpr int NTHR = NCT + 32;          // + the producer warp
 constexpr int BID = 1;                  // named barrier of the consumer threads

@@ -14,7 +14,7 @@ from navi_b200 import model_spec
 NSLOT = 16
 
 
-NCW = 12   # consumer warps: weight slices may be cut at the first k-chunk of a warp's K range
+NCW = 11   # consumer warps: weight slices may be cut at the first k-chunk of a warp's K range
 
 
 def phase_chunks(cfg, b, G, n_past=512):
