@@ -17,6 +17,8 @@ ROOT = PKG.parent
 CSRC = ROOT / "csrc"
 OBJ = ROOT / "_build"
 LIB = PKG / "libnavi_b200.so"
+CLI_SRC = ROOT / "cli" / "navi_b200_cli.cpp"
+CLI = PKG / "navi-b200"          # the command-line front (info / synth), linked against LIB
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -63,6 +65,12 @@ def build(verbose: bool = False) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    if not CLI.exists() or CLI.stat().st_mtime < max(LIB.stat().st_mtime, CLI_SRC.stat().st_mtime, _headers_mtime()):
+        cmd = ["g++", "-O2", "-std=c++20", "-I", str(ROOT.parent / "include"), str(CLI_SRC), "-o", str(CLI), "-L", str(PKG), "-lnavi_b200",
+               "-Wl,-rpath,$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"CLI build failed:\n{r.stdout}\n{r.stderr}")
     return LIB
 
 
