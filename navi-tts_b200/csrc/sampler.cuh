@@ -308,21 +308,25 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
     int * ord = S.ord;   // top-p: candidate position of each rank
     if (nucleus) {
         // rank of candidate j in (value desc, index asc) order; positions are in index order.
-        // Each warp passes 32 candidate values at a time round its lanes.
-        for (int j0 = 0; j0 < n; j0 += NT) {
-            const int j = j0 + tid;
-            const float vj = j < n ? s[ci[j]] : 0.f;
-            int r = 0;
-            for (int m0 = 0; m0 < n; m0 += 32) {
-                const float vl = m0 + lane < n ? s[ci[m0 + lane]] : 0.f;
-                const int mq = min(32, n - m0);
+        // Thread j reads the other candidates' values from shared memory (every thread of a
+        // step reads the same element: a broadcast), eight independent loads per step.
+        for (int j = tid; j < n; j += NT) {
+            const float vj = s[ci[j]];
+            int r = 0, m = 0;
 #pragma unroll 1
-                for (int q = 0; q < mq; ++q) {
-                    const float vm = __shfl_sync(0xffffffffu, vl, q);
-                    r += (vm > vj || (vm == vj && m0 + q < j)) ? 1 : 0;
-                }
+            for (; m + 8 <= n; m += 8) {
+                float vm[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) vm[q] = s[ci[m + q]];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) r += (vm[q] > vj || (vm[q] == vj && m + q < j)) ? 1 : 0;
             }
-            if (j < n) ord[r] = j;
+#pragma unroll 1
+            for (; m < n; ++m) {
+                const float v = s[ci[m]];
+                r += (v > vj || (v == vj && m < j)) ? 1 : 0;
+            }
+            ord[r] = j;
         }
         named_sync(bid, NT);
     }
@@ -336,7 +340,7 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
         // running sums of the block v (0 past the end); returns the sum after the block and
         // leaves in `mine` the sum after this lane's term
         auto block_scan = [&](float acc, float v, float & mine) {
-#pragma unroll
+#pragma unroll 1
             for (int g = 0; g < 32; g += 8) {   // eight values gathered per group: few live registers
                 float t[8];
 #pragma unroll
