@@ -139,7 +139,7 @@ def test_kv_full_is_reported(small_navi):
     assert not r.ok and r.status == capi.NAVI_E_KV_FULL
 
 
-@pytest.mark.parametrize("n_past", [64, 512])
+@pytest.mark.parametrize("n_past", [64, 512, 2048])   # 2048: several 8-position steps per warp
 def test_full_size_frame_matches_oracle(full_navi, n_past):
     """configs[1]+[2] shapes: 28-layer talker at KV length n_past, 5-layer code predictor."""
     S = Setup(full_navi, max_pos=2049)
