@@ -10,8 +10,9 @@
 //   warps 2-5   stage the input window of each channel block (history / input rows,
 //               prologue, f16 hi/lo split) into one of two window buffers;
 //   warps 6-9   epilogue: tensor-memory loads (warp w reads lanes 32 (w % 4) ..), bias,
-//               activation / residual, stores; with split-K the CTA that finishes a
-//               tile last sums the partials in split order (deterministic).
+//               activation / residual, stores; with split-K each split stores its partial
+//               sums and k_splitk_reduce adds them in split order (deterministic) and
+//               applies the epilogue.
 // So unit n's epilogue, unit n+1's MMAs and unit n+2's window staging overlap.
 // Every mbarrier wait is bounded by a deadline; a CTA that passes it sets the error
 // word, stops waiting (its remaining waits return at once) and still frees its
