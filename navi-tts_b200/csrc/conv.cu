@@ -237,6 +237,8 @@ __device__ __forceinline__ void epilogue_unit(const KArgs & a, const Unit & w, u
 // across unit boundaries.
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a, const __grid_constant__ CUtensorMap tmw) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t * ring = smem;
     uint8_t * win = smem + a.nst * TILE_BYTES;
@@ -412,6 +414,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a, const __gri
 template <int EPI>
 __global__ void k_splitk_reduce(const float * partial, int splits, int T, int Cout, const float * bias, const float * scale,
                                 const float * resid, int r_stride, float * y, int y_stride) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     const std::size_t n = static_cast<std::size_t>(T) * Cout;
     const std::size_t i = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
@@ -479,11 +483,11 @@ void launch_t(const KArgs & ka, const CUtensorMap & tm, dim3 grid, std::size_t s
         NAVI_CUDA(cudaFuncSetAttribute(k_conv<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
         attr.fetch_or(bit);
     }
-    k_conv<PRO, EPI><<<grid, NTHREADS, smem, stream>>>(ka, tm);
+    NAVI_CUDA(navi::dev::launch_pdl(k_conv<PRO, EPI>, grid, dim3(NTHREADS), smem, stream, ka, tm));
     if (ka.splits > 1) {
         const std::size_t n = static_cast<std::size_t>(ka.T) * ka.Cout;
-        k_splitk_reduce<EPI><<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(ka.partial, ka.splits, ka.T, ka.Cout, ka.bias, ka.scale,
-                                                                                     ka.resid, ka.r_stride, ka.y, ka.y_stride);
+        NAVI_CUDA(navi::dev::launch_pdl(k_splitk_reduce<EPI>, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream, ka.partial,
+                                        ka.splits, ka.T, ka.Cout, ka.bias, ka.scale, ka.resid, ka.r_stride, ka.y, ka.y_stride));
     }
 }
 

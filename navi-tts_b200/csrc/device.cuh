@@ -6,6 +6,8 @@
 
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <utility>
+#include <cuda_runtime.h>
 
 namespace navi::dev {
 
@@ -43,6 +45,32 @@ __device__ __forceinline__ uint64_t globaltimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// ---- programmatic dependent launch (sm_90 and later) -------------------------------------------
+// A kernel launched with launch_pdl() may start while the kernel before it in the stream is
+// still running. griddep_wait() returns once that kernel has completed and its writes are
+// visible (at once when there is no such dependency), so every such kernel calls it before
+// its first read of another kernel's output; griddep_launch_dependents() lets the next
+// kernel start launching (its own wait still holds it until this one completes).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launches kernel<<<grid, block, smem, stream>>>(args...) with programmatic stream
+// serialisation allowed, so its launch overlaps the tail of the previous kernel.
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args &&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 __device__ __forceinline__ uint32_t smem_addr(const void * p) {

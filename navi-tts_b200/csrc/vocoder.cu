@@ -37,6 +37,8 @@ struct RvqArgs {
 
 // e[t] = [ first[c0] | sum_{q >= 1} rest_{q-1}[c_q] ]   (vocoder.hip:113-131)
 __global__ void k_rvq(const RvqArgs a) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     const int t = blockIdx.x;
     const int * c = a.codes + t * a.n_q;
     float * e = a.e + static_cast<std::size_t>(t) * 2 * a.vq;
@@ -61,6 +63,8 @@ __device__ __forceinline__ float block_sum256(float v, float * red) {
 
 // out[t] = x[t] * rsqrt(mean(x[t]^2) + eps) * w; 256 threads per row.
 __global__ void k_rmsnorm_rows(const float * x, const float * w, int H, float eps, float * out) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     __shared__ float red[8];
     const float * xr = x + static_cast<std::size_t>(blockIdx.x) * H;
     float * yr = out + static_cast<std::size_t>(blockIdx.x) * H;
@@ -73,6 +77,8 @@ __global__ void k_rmsnorm_rows(const float * x, const float * w, int H, float ep
 // Rotate-half RoPE on q (in place) and k of row t at position pos0 + t; k and v go to
 // ring slot pos & (ring - 1) (vocoder.hip:59-82).  qkv rows: [q | k | v], HD each.
 __global__ void k_rope_append(float * qkv, int nh, int hd, int pos0, int ring, const float * inv_freq, float * kc, float * vc) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     const int t = blockIdx.x, pos = pos0 + t, slot = pos & (ring - 1);
     const int HD = nh * hd, half = hd / 2;
     float * row = qkv + static_cast<std::size_t>(t) * 3 * HD;
@@ -101,6 +107,8 @@ __global__ void k_rope_append(float * qkv, int nh, int hd, int pos0, int ring, c
 // output dimension i.  window <= 128, hd <= 128.
 __global__ void k_window_attn(const float * qkv, int nh, int hd, int pos0, int window, int ring, float scale, const float * kc,
                               const float * vc, float * out) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     __shared__ float q[128], pr[128], red[4];
     const int t = blockIdx.x, h = blockIdx.y, pos = pos0 + t, tid = threadIdx.x;
     const int HD = nh * hd;
@@ -137,6 +145,8 @@ __global__ void k_window_attn(const float * qkv, int nh, int hd, int pos0, int w
 // channels (vocoder.hip:20-56).  256 threads per row, C <= 2048.
 __global__ void k_dwconv_ln(const __half * W, const float * bias, const float * x, const float * hist, int C, const float * lw,
                             const float * lb, float eps, float * y) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     __shared__ float red[8];
     const int t = blockIdx.x;
     float v[8];
@@ -175,6 +185,8 @@ __global__ void k_dwconv_ln(const __half * W, const float * bias, const float * 
 // hist <- the last H rows of [hist ; x[0..T)], in place: each block owns 32 columns and
 // reads all of its rows before writing any (vocoder.hip:133-141).
 __global__ void k_hist_update(float * hist, const float * x, int x_stride, int T, int H, int C) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     __shared__ float buf[HIST_MAX][33];
     const int c = blockIdx.x * 32 + threadIdx.x;
     for (int r = threadIdx.y; r < H; r += blockDim.y) {
@@ -193,6 +205,8 @@ __global__ void k_hist_update(float * hist, const float * x, int x_stride, int T
 constexpr int FROWS = 256;
 __global__ void k_final_conv(const __half * W, const float * bias, const float * x, const float * hist, const float * sa, const float * sb,
                              int T, int Cin, float * y) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     extern __shared__ float fs[];
     constexpr int NR = FROWS + 6;
     float * xs = fs;                 // [Cin][NR]
@@ -328,7 +342,7 @@ struct Vocoder::Impl {
     }
 
     void hist_update(float * hist, const float * xin, int x_stride, int T, int H, int C) {
-        k_hist_update<<<(C + 31) / 32, dim3(32, 8), 0, stream>>>(hist, xin, x_stride, T, H, C);
+        NAVI_CUDA(navi::dev::launch_pdl(k_hist_update, dim3((C + 31) / 32), dim3(32, 8), 0, stream, hist, xin, x_stride, T, H, C));
         NAVI_CUDA(cudaGetLastError());
     }
 
@@ -369,7 +383,7 @@ void Vocoder::Impl::decode_chunk(int T) {
         ra.e = e;
         ra.n_q = p.vq_n_q;
         ra.vq = VQ;
-        k_rvq<<<T, 256, 0, stream>>>(ra);
+        NAVI_CUDA(navi::dev::launch_pdl(k_rvq, dim3(T), dim3(256), 0, stream, ra));
         NAVI_CUDA(cudaGetLastError());
     }
     run(rvq_proj, e, T, CD, h, CD);
@@ -380,18 +394,18 @@ void Vocoder::Impl::decode_chunk(int T) {
     const float scale = 1.f / std::sqrt(static_cast<float>(hd));
     for (std::size_t l = 0; l < layers.size(); ++l) {
         Layer & ly = layers[l];
-        k_rmsnorm_rows<<<T, 256, 0, stream>>>(x, ly.ln1, VH, eps, n);
+        NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm_rows, dim3(T), dim3(256), 0, stream, x, ly.ln1, VH, eps, n));
         run(ly.qkv, n, T, VH, qkv, 3 * HD);
-        k_rope_append<<<T, 256, 0, stream>>>(qkv, nh, hd, pos0, ring, inv_freq, ly.kc, ly.vc);
-        k_window_attn<<<dim3(T, nh), 128, 0, stream>>>(qkv, nh, hd, pos0, window, ring, scale, ly.kc, ly.vc, att);
+        NAVI_CUDA(navi::dev::launch_pdl(k_rope_append, dim3(T), dim3(256), 0, stream, qkv, nh, hd, pos0, ring, inv_freq, ly.kc, ly.vc));
+        NAVI_CUDA(navi::dev::launch_pdl(k_window_attn, dim3(T, nh), dim3(128), 0, stream, qkv, nh, hd, pos0, window, ring, scale, ly.kc, ly.vc, att));
         NAVI_CUDA(cudaGetLastError());
         run(ly.o, att, T, HD, x, VH, x);
-        k_rmsnorm_rows<<<T, 256, 0, stream>>>(x, ly.ln2, VH, eps, n);
+        NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm_rows, dim3(T), dim3(256), 0, stream, x, ly.ln2, VH, eps, n));
         run(ly.gateup, n, T, VH, gu, 2 * FF);
         run(ly.down, gu, T, 2 * FF, x, VH, x);
         snap(("layer" + std::to_string(l)).c_str(), x, T, VH);
     }
-    k_rmsnorm_rows<<<T, 256, 0, stream>>>(x, final_norm, VH, eps, n);
+    NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm_rows, dim3(T), dim3(256), 0, stream, x, final_norm, VH, eps, n));
     run(out_proj, n, T, VH, u, L);
     snap("pre_transformer", u, T, L);
 
@@ -404,7 +418,7 @@ void Vocoder::Impl::decode_chunk(int T) {
         run(up_conv[j], src, R, L, dst, r * L);   // phases folded: output row t*r + phase, dense
         R *= r;
         Cnx & cx = cnx[j];
-        k_dwconv_ln<<<R, 256, 0, stream>>>(cx.dw, cx.dw_bias, dst, cx.hist, L, cx.ln_w, cx.ln_b, 1e-6f, tmp);
+        NAVI_CUDA(navi::dev::launch_pdl(k_dwconv_ln, dim3(R), dim3(256), 0, stream, cx.dw, cx.dw_bias, dst, cx.hist, L, cx.ln_w, cx.ln_b, 1e-6f, tmp));
         NAVI_CUDA(cudaGetLastError());
         hist_update(cx.hist, dst, L, R, 6, L);
         run(cx.pw1, tmp, R, L, G, 4 * L);
@@ -429,7 +443,7 @@ void Vocoder::Impl::decode_chunk(int T) {
         in = P[b];
     }
     const int fsmem = (FROWS + 6) * fin.Cin * 4 + fin.Cin * 7 * 4;
-    k_final_conv<<<(R + FROWS - 1) / FROWS, FROWS, fsmem, stream>>>(fin.w, fin.bias, in, fin.hist, fin.sa, fin.sb, R, fin.Cin, pcm);
+    NAVI_CUDA(navi::dev::launch_pdl(k_final_conv, dim3((R + FROWS - 1) / FROWS), dim3(FROWS), fsmem, stream, fin.w, fin.bias, in, fin.hist, fin.sa, fin.sb, R, fin.Cin, pcm));
     NAVI_CUDA(cudaGetLastError());
     hist_update(fin.hist, in, fin.Cin, R, 6, fin.Cin);
     snap("pcm", pcm, R, 1);
