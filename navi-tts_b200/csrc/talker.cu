@@ -50,6 +50,8 @@ __global__ void k_assemble_rows(const float * A, const float * B, const float * 
 
 // out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w; one block of 256 threads per row.
 __global__ void k_rmsnorm(const float * x, const float * w, int H, float eps, float * out) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     __shared__ float red[8];
     const float * xr = x + static_cast<size_t>(blockIdx.x) * H;
     float * yr = out + static_cast<size_t>(blockIdx.x) * H;
@@ -74,6 +76,8 @@ enum { EPI_NONE = 0, EPI_SILU = 1, EPI_RESIDUAL = 2 };
 // in place; then the f16 K (after RoPE) and V rows into the cache (talker.hip:43-80).
 __global__ void k_qk_norm_rope(float * qkv, int row_stride, const float * q_norm, const float * k_norm, int NH, int NKV, float eps,
                                const float * rope, int pos0, __half * kcache, __half * vcache) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     constexpr int HD = 128, H2 = 64;
     const int t = blockIdx.x, pos = pos0 + t, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     float * row = qkv + static_cast<size_t>(t) * row_stride;
@@ -110,6 +114,8 @@ __global__ void k_qk_norm_rope(float * qkv, int row_stride, const float * q_norm
 constexpr int MAX_KEYS = 1024;
 __global__ void k_prefill_attn(const float * qkv, int row_stride, const __half * kcache, const __half * vcache, int NH, int NKV, int pos0,
                                float * out) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
     constexpr int HD = 128;
     __shared__ float sc[MAX_KEYS];
     __shared__ float red[8];
@@ -404,17 +410,19 @@ void Talker::prefill(const Prompt & pr) {
         const Layer & ly = I.layers[static_cast<size_t>(l)];
         __half * kc = reinterpret_cast<__half *>(I.kptr[static_cast<size_t>(l)]);
         __half * vc = reinterpret_cast<__half *>(I.vptr[static_cast<size_t>(l)]);
-        k_rmsnorm<<<T, 256, 0, I.stream>>>(I.x, ly.ln1, H, tp.rms_eps, I.n);
+        NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm, dim3(T), dim3(256), 0, I.stream, I.x, ly.ln1, H, tp.rms_eps, I.n));
         I.gemm(ly.wqkv, nullptr, I.n, H, T, H, I.QKV, I.qkv, I.QKV, EPI_NONE);
-        k_qk_norm_rope<<<T, 256, 0, I.stream>>>(I.qkv, I.QKV, ly.qn, ly.kn, I.NH, I.NKV, tp.rms_eps, I.rope, 0, kc, vc);
-        k_prefill_attn<<<dim3(T, I.NH), 128, 0, I.stream>>>(I.qkv, I.QKV, kc, vc, I.NH, I.NKV, 0, I.att);
+        NAVI_CUDA(navi::dev::launch_pdl(k_qk_norm_rope, dim3(T), dim3(256), 0, I.stream, I.qkv, I.QKV, ly.qn, ly.kn, I.NH, I.NKV, tp.rms_eps,
+                                        I.rope, 0, kc, vc));
+        NAVI_CUDA(navi::dev::launch_pdl(k_prefill_attn, dim3(T, I.NH), dim3(128), 0, I.stream, I.qkv, I.QKV, kc, vc, I.NH, I.NKV, 0, I.att));
         I.gemm(ly.wo, nullptr, I.att, I.Q, T, I.Q, H, I.x, H, EPI_RESIDUAL, false, I.x);
-        k_rmsnorm<<<T, 256, 0, I.stream>>>(I.x, ly.ln2, H, tp.rms_eps, I.n);
+        NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm, dim3(T), dim3(256), 0, I.stream, I.x, ly.ln2, H, tp.rms_eps, I.n));
         I.gemm(ly.wgu, nullptr, I.n, H, T, H, 2 * I.F, I.gu, 2 * I.F, EPI_NONE);
         I.gemm(ly.wd, nullptr, I.gu, 2 * I.F, T, I.F, H, I.x, H, EPI_RESIDUAL, true, I.x);
     }
     // the last row: final norm and the codec head
-    k_rmsnorm<<<1, 256, 0, I.stream>>>(I.x + static_cast<size_t>(T - 1) * H, I.final_norm, H, tp.rms_eps, I.hid);
+    NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm, dim3(1), dim3(256), 0, I.stream, I.x + static_cast<size_t>(T - 1) * H, I.final_norm, H,
+                                    tp.rms_eps, I.hid));
     I.gemm(I.head, nullptr, I.hid, H, 1, H, I.TV, I.logits, I.TV, EPI_NONE);
     NAVI_CUDA(cudaGetLastError());
     NAVI_CUDA(cudaEventRecord(I.ev1, I.stream));
