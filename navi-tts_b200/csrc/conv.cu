@@ -53,6 +53,7 @@ struct KArgs {
     int nst;                          // weight-ring stages
     int tmaw;                         // 1: weights are a row-major matrix read by TMA (128B-swizzled tiles)
     int resident;                     // 1: the CTA's tiles are loaded once and reused by every unit
+    int early_weights;                // 1: the weight stream need not wait for the previous kernel
     unsigned long long timeout_ns;
 };
 
@@ -237,7 +238,9 @@ __device__ __forceinline__ void epilogue_unit(const KArgs & a, const Unit & w, u
 // across unit boundaries.
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a, const __grid_constant__ CUtensorMap tmw) {
-    navi::dev::griddep_wait();
+    // launched after the previous kernel of the stream may still run: every role that reads
+    // its outputs waits for it below; the weight stream (warp 0) does not when the weights
+    // are settled, so the first tiles load while the previous kernel finishes
     navi::dev::griddep_launch_dependents();
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t * ring = smem;
@@ -276,6 +279,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a, const __gri
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = B.tmem;
+    if (warp != 0 || !a.early_weights) navi::dev::griddep_wait();
 
     if (warp == 0) {
         if (lane == 0 && a.resident) {
@@ -607,6 +611,7 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     ka.BN = p.BN; ka.NT = p.NT; ka.MT = p.MT; ka.CB = p.CB; ka.cb_per_split = p.cb_per_split; ka.splits = p.splits;
     ka.lbo = p.lbo; ka.wrows = p.BN + ka.H; ka.tmem_cols = p.tmem_cols; ka.timeout_ns = ws.timeout_ns;
     ka.nst = p.nst; ka.resident = p.resident ? 1 : 0;
+    ka.early_weights = c.weights_settled ? 1 : 0;
     CUtensorMap tm;
     std::memset(&tm, 0, sizeof tm);
     if (c.w_rm) {

@@ -78,6 +78,10 @@ struct Conv {
     const float * scale = nullptr;           // EPI_SCALE_RESIDUAL: [Cout]
     float * y = nullptr;                     // rows [T][y_stride]
     int y_stride = 0;
+    // true when no kernel still in flight in the stream writes the weights (they were packed
+    // or uploaded before a synchronisation): the weight stream may then start before the
+    // previous kernel in the stream has finished
+    bool weights_settled = false;
 };
 
 struct Plan {

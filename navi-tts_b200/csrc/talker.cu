@@ -225,6 +225,7 @@ struct Talker::Impl {
         c.bias = bias;
         c.y_stride = ys;
         c.r_stride = ys;
+        c.weights_settled = true;   // the weight arena was uploaded before any prefill
         return c;
     }
 

@@ -329,6 +329,7 @@ struct Vocoder::Impl {
 
     void run(CV & cv, const float * xin, int T, int x_stride, float * y, int y_stride, const float * resid = nullptr) {
         conv::Conv c = cv.c;
+        c.weights_settled = true;   // packed in create(), which synchronises before returning
         c.x = xin;
         c.T = T;
         c.x_stride = x_stride;
