@@ -320,7 +320,7 @@ def run_reference(args):
             "config": {"workload": f"configs[1]+[2] frame at KV {args.kv}", "kv_len": args.kv, "batch": 1},
             "impl": "reference", "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def combine_ranks(ms: float, e2e_ms: float, world: int, dist, device: str):
@@ -353,7 +353,7 @@ def run_vocoder_only(args):
             "data": "synthetic (seeded random-init weights N(0,0.02), uniform random codes)", "vocoder": v}
     if args.cpu_baseline:
         line["vocoder"]["cpu_baseline"] = vocoder_cpu_baseline()
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_ours(args):
@@ -473,13 +473,28 @@ def run_ours(args):
             line["cpu_baseline"] = cpu_baseline(L)
             if args.vocoder:
                 line["vocoder"]["cpu_baseline"] = vocoder_cpu_baseline()
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
 
 
+_JSON_FD = None
+
+
+def emit(line: dict) -> None:
+    """Writes the result line to the process's real standard output (libraries' banners,
+    such as NCCL's version line, go to standard error; see main)."""
+    os.write(_JSON_FD if _JSON_FD is not None else 1, (json.dumps(line) + "\n").encode())
+
+
 def main():
+    global _JSON_FD
+    # everything written to fd 1 by this process or its libraries goes to standard error; the
+    # one JSON line goes to the original standard output
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
