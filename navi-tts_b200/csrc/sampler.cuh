@@ -169,6 +169,13 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
     // 1. codebook-0 modifications, temperature, max; histograms cleared for step 2
     const bool greedy = c.temperature <= 0.f;
     for (int i = tid; i < 512; i += NT) hist[i] = 0u;
+    // The first radix pass (top byte: sign and exponent) puts most keys in a handful of
+    // bins; one histogram per warp, summed afterwards, keeps the warps' atomics apart. They
+    // live in e and idx (2 V words, unused until step 3) when those are large enough.
+    unsigned * whist = reinterpret_cast<unsigned *>(S.e);
+    const bool priv = NW * 256 <= 2 * V;
+    if (priv && !greedy)
+        for (int i = tid; i < NW * 256; i += NT) whist[i] = 0u;
     float lmax = -INFINITY;
     for (int i = tid; i < V; i += NT) {
         float v = s[i];
@@ -209,9 +216,21 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
         for (int pass = 3; pass >= 0; --pass) {
             const int shift = pass * 8;
             unsigned * h = hist + (pass & 1) * 256;
-            for (int i = tid; i < V; i += NT) {
-                const uint32_t key = float_key(s[i]);
-                if ((key & mask) == prefix) atomicAdd(&h[(key >> shift) & 0xFFu], 1u);
+            if (pass == 3 && priv) {
+                unsigned * hw = whist + wid * 256;
+                for (int i = tid; i < V; i += NT) atomicAdd(&hw[float_key(s[i]) >> 24], 1u);
+                named_sync(bid, NT);
+                for (int b = tid; b < 256; b += NT) {
+                    unsigned t = 0;
+#pragma unroll
+                    for (int w = 0; w < NW; ++w) t += whist[w * 256 + b];
+                    h[b] = t;
+                }
+            } else {
+                for (int i = tid; i < V; i += NT) {
+                    const uint32_t key = float_key(s[i]);
+                    if ((key & mask) == prefix) atomicAdd(&h[(key >> shift) & 0xFFu], 1u);
+                }
             }
             named_sync(bid, NT);
             const int slot = 16 + 3 * (3 - pass);
