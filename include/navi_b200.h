@@ -69,6 +69,8 @@ int navi_device_open(int ordinal, navi_device ** out);
 int navi_device_get_info(const navi_device * dev, navi_device_info * info);
 /* The engine's cudaStream_t. */
 void * navi_device_stream(const navi_device * dev);
+/* Destroy every handle made on this device (weights, KV caches, talkers, frames, vocoders,
+ * graphs) first: their destroy calls use the device's stream. */
 void navi_device_close(navi_device * dev);
 
 /* ---- weights: replaces NaviFile + read_params + validate + DeviceWeights::upload

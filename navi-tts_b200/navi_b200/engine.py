@@ -48,6 +48,14 @@ class FrameResult:
     error: str = ""
 
 
+def _open(*owners) -> bool:
+    """True while every owner handle (device, weights) is still open. A handle is destroyed
+    only then: after its device is closed the native destroy would touch freed resources
+    (garbage collection of a reference cycle may finalise the device first), so such a
+    handle is dropped and the process's teardown releases its memory."""
+    return all(getattr(o, "h", None) for o in owners if o is not None)
+
+
 class Device:
     def __init__(self, ordinal: int = 0):
         h = c_void_p()
@@ -98,7 +106,8 @@ class Weights:
 
     def close(self):
         if self.h:
-            lib().navi_weights_free(self.h)
+            if _open(self.dev):
+                lib().navi_weights_free(self.h)
             self.h = None
 
     def __del__(self):
@@ -124,6 +133,7 @@ class KvCache:
         check(lib().navi_kv_create(dev.h, n_layer, max_pos, kv_dim, byref(ptr)))
         kv._owned = ptr
         kv.s = ptr.contents
+        kv.dev = dev
         return kv
 
     @staticmethod
@@ -145,7 +155,8 @@ class KvCache:
 
     def close(self):
         if self._owned is not None:
-            lib().navi_kv_destroy(self._owned)
+            if _open(getattr(self, "dev", None)):
+                lib().navi_kv_destroy(self._owned)
             self._owned = None
 
     def __del__(self):
@@ -195,7 +206,8 @@ class Talker:
 
     def close(self):
         if self.h:
-            lib().navi_talker_destroy(self.h)
+            if _open(self.dev, self.w):
+                lib().navi_talker_destroy(self.h)
             self.h = None
 
     def __del__(self):
@@ -255,7 +267,8 @@ class Graph:
 
     def close(self):
         if self.h:
-            lib().navi_graph_destroy(self.h)
+            if _open(self.dev, self.w):
+                lib().navi_graph_destroy(self.h)
             self.h = None
 
     def __del__(self):
@@ -311,7 +324,8 @@ class Vocoder:
 
     def close(self):
         if self.h:
-            lib().navi_vocoder_destroy(self.h)
+            if _open(self.dev, self.w):
+                lib().navi_vocoder_destroy(self.h)
             self.h = None
 
     def __del__(self):
@@ -425,7 +439,8 @@ class Frame:
 
     def close(self):
         if self.h:
-            lib().navi_frame_destroy(self.h)
+            if _open(self.dev, self.w):
+                lib().navi_frame_destroy(self.h)
             self.h = None
 
     def __del__(self):

@@ -122,3 +122,29 @@ def test_graph_without_vocoder_refuses_pcm(small_navi):
     with pytest.raises(capi.NaviError):
         g.synth(ids, "english", spk, engine.Sampling(), 1, 4)
     g.close()
+
+
+def test_graph_rejects_bad_requests_and_stays_usable(small_navi):
+    """Graph::synth's argument checks (graph.cpp:60-64: empty text; KV cache too small for the
+    prompt plus max_frames) fail with a status and leave the graph usable for the next
+    request, whose codes equal a fresh graph's."""
+    W = om.Weights.from_navi(small_navi)
+    dev = engine.Device(0)
+    w = engine.Weights(dev, small_navi)
+    g = engine.Graph(dev, w, max_prompt_tokens=64, max_frames=8, vocoder_chunk=4)
+    spk = np.random.default_rng(3).standard_normal(W.tl.hidden).astype(np.float32)
+    s = engine.Sampling(top_p=0.9, cp_top_p=0.9)
+    empty = _ids(W.cfg, 0, seed=1)            # the template alone: no text
+    with pytest.raises(capi.NaviError) as e:
+        g.synth_ids(empty, "english", spk, s, 1, 4)
+    assert e.value.status == capi.NAVI_E_ARG
+    ids = _ids(W.cfg, 5, seed=2)
+    with pytest.raises(capi.NaviError) as e:      # the prompt + 80 frames > the 64 + 8 + 1 positions
+        g.synth(ids, "english", spk, s, 1, 80, first_batch=2, vocoder_batch=4)
+    assert e.value.status == capi.NAVI_E_KV_FULL
+    codes, pcm, st, _ = g.synth(ids, "english", spk, s, 9, 6, first_batch=2, vocoder_batch=4)
+    fresh = engine.Graph(dev, w, max_prompt_tokens=64, max_frames=8, vocoder_chunk=4)
+    codes2, pcm2, _, _ = fresh.synth(ids, "english", spk, s, 9, 6, first_batch=2, vocoder_batch=4)
+    assert np.array_equal(codes, codes2) and np.array_equal(pcm, pcm2)
+    g.close()
+    fresh.close()
