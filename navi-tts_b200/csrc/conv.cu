@@ -46,6 +46,7 @@ struct KArgs {
     const __half * w;
     const float * x, * hist, * sa, * sb, * bias, * resid, * scale;
     float * y, * partial;
+    float * hist_out;                 // next chunk's history, or null
     int * err;
     int Cout, Cin, K, dil, H, T, x_stride, y_stride, r_stride;
     int BN, NT, MT, CB, cb_per_split, splits;
@@ -392,6 +393,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a, const __gri
         }
     } else {
         const int q = warp & 3;                          // tensor-memory lane quadrant of this warp
+        if (a.hist_out) {
+            // the next chunk's history, the last H rows of [hist; x], spread over every CTA's
+            // epilogue threads while they wait for their first accumulator
+            const int n = a.H * a.Cin, et = threadIdx.x - 6 * 32;
+            for (int e = blockIdx.x * 128 + et; e < n; e += gridDim.x * 128) {
+                const int r = e / a.Cin, ch = e - r * a.Cin, src = r + a.T;
+                a.hist_out[e] = src < a.H ? a.hist[static_cast<std::size_t>(src) * a.Cin + ch]
+                                          : a.x[static_cast<std::size_t>(src - a.H) * a.x_stride + ch];
+            }
+        }
         int k = 0;
         for (int un = blockIdx.x; un < n_units; un += gridDim.x, ++k) {
             const Unit w = unit_of(a, un);
@@ -596,6 +607,7 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     if (c.pro == PRO_SNAKE && (!c.snake_a || !c.snake_b || ((reinterpret_cast<std::uintptr_t>(c.snake_a) | reinterpret_cast<std::uintptr_t>(c.snake_b)) & 15u)))
         fail("conv: Snake coefficients missing or misaligned", NAVI_E_SHAPE);
     if (c.pro == PRO_SILU_GATE && c.hist) fail("conv: gated input has no history", NAVI_E_SHAPE);
+    if (c.hist_out && c.hist_out == c.hist) fail("conv: the next history needs a buffer of its own", NAVI_E_ARG);
     if ((c.epi == EPI_RESIDUAL || c.epi == EPI_SCALE_RESIDUAL) && !c.resid) fail("conv: residual missing", NAVI_E_SHAPE);
     if (c.epi == EPI_SCALE_RESIDUAL && !c.scale) fail("conv: layer scale missing", NAVI_E_SHAPE);
     const Plan p = plan(c, sms);
@@ -606,6 +618,7 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     KArgs ka{};
     ka.w = c.w; ka.x = c.x; ka.hist = c.hist; ka.sa = c.snake_a; ka.sb = c.snake_b; ka.bias = c.bias;
     ka.resid = c.resid; ka.scale = c.scale; ka.y = c.y; ka.partial = ws.partial; ka.err = ws.err;
+    ka.hist_out = c.hist ? c.hist_out : nullptr;
     ka.Cout = c.Cout; ka.Cin = c.Cin; ka.K = c.K; ka.dil = c.dil; ka.H = (c.K - 1) * c.dil; ka.T = c.T;
     ka.x_stride = c.x_stride; ka.y_stride = c.y_stride; ka.r_stride = c.r_stride;
     ka.BN = p.BN; ka.NT = p.NT; ka.MT = p.MT; ka.CB = p.CB; ka.cb_per_split = p.cb_per_split; ka.splits = p.splits;

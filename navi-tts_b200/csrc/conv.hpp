@@ -69,6 +69,9 @@ struct Conv {
     const float * x = nullptr;               // rows [T][x_stride]; SILU_GATE: row = [gate | up], Cin each
     int x_stride = 0, T = 0;
     const float * hist = nullptr;            // [H][Cin] or null
+    // when set (with hist): receives the last H rows of [hist; x], i.e. the next chunk's
+    // history, written by the launch itself ([H][Cin], a buffer other than hist)
+    float * hist_out = nullptr;
     int pro = PRO_NONE;
     const float * snake_a = nullptr, * snake_b = nullptr;   // e^alpha, 1/(e^beta + 1e-9)   [Cin]
     int epi = EPI_NONE;

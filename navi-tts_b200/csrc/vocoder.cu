@@ -15,6 +15,7 @@
 #include <cmath>
 #include <cstring>
 #include <string>
+#include <utility>
 
 namespace navi::qwen3tts {
 
@@ -250,7 +251,8 @@ __global__ void k_final_conv(const __half * W, const float * bias, const float *
 // One GEMM-shaped stage: its packed weights and fixed operands, plus its input history.
 struct CV {
     conv::Conv c;
-    float * hist = nullptr;
+    float * hist = nullptr;   // history [H][Cin] read by the next launch
+    float * hist2 = nullptr;  // the other buffer: the launch writes the next history there
     int H = 0;
 };
 
@@ -334,12 +336,13 @@ struct Vocoder::Impl {
         c.T = T;
         c.x_stride = x_stride;
         c.hist = cv.hist;
+        c.hist_out = cv.hist2;    // the conv kernel writes the next history itself
         c.y = y;
         c.y_stride = y_stride;
         c.resid = resid;
         c.r_stride = y_stride;
         conv::launch(c, ws, sms, stream);
-        if (cv.hist) hist_update(cv.hist, xin, x_stride, T, cv.H, cv.c.Cin);
+        std::swap(cv.hist, cv.hist2);
     }
 
     void hist_update(float * hist, const float * xin, int x_stride, int T, int H, int C) {
@@ -492,7 +495,10 @@ std::unique_ptr<Vocoder> Vocoder::create(const Device & dev, const DeviceWeights
         cv.c.Cout = Cout; cv.c.Cin = Cin; cv.c.K = K; cv.c.dil = dil; cv.c.bias = bias; cv.c.pro = pro; cv.c.epi = epi;
         cv.H = (K - 1) * dil;
         if (cv.H > HIST_MAX) fail("vocoder: conv history above " + std::to_string(HIST_MAX) + " rows", NAVI_E_SHAPE);
-        if (cv.H > 0) cv.hist = I.alloc<float>(static_cast<std::size_t>(cv.H) * Cin);
+        if (cv.H > 0) {
+            cv.hist = I.alloc<float>(static_cast<std::size_t>(cv.H) * Cin);
+            cv.hist2 = I.alloc<float>(static_cast<std::size_t>(cv.H) * Cin);
+        }
         return cv;
     };
     auto snake = [&](const std::string & prefix, CV & cv) {
@@ -687,7 +693,10 @@ void Vocoder::reset() {
     auto zero = [&](float * ptr, std::size_t n) {
         if (ptr) NAVI_CUDA(cudaMemsetAsync(ptr, 0, n * sizeof(float), I.stream));
     };
-    auto zero_cv = [&](CV & cv) { zero(cv.hist, static_cast<std::size_t>(cv.H) * cv.c.Cin); };
+    auto zero_cv = [&](CV & cv) {
+        zero(cv.hist, static_cast<std::size_t>(cv.H) * cv.c.Cin);
+        zero(cv.hist2, static_cast<std::size_t>(cv.H) * cv.c.Cin);
+    };
     zero_cv(I.pre_conv);
     zero_cv(I.dec0);
     for (auto & cx : I.cnx) zero(cx.hist, static_cast<std::size_t>(6) * I.L);
