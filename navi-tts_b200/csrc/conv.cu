@@ -12,7 +12,8 @@
 //   warps 6-9   epilogue: tensor-memory loads (warp w reads lanes 32 (w % 4) ..), bias,
 //               activation / residual, stores; with split-K each split stores its partial
 //               sums and k_splitk_reduce adds them in split order (deterministic) and
-//               applies the epilogue.
+//               applies the epilogue (k_reduce_norm, one CTA per row, when the layer
+//               after the conv starts with an RMS norm: it also writes the norm).
 // So unit n's epilogue, unit n+1's MMAs and unit n+2's window staging overlap.
 // Every mbarrier wait is bounded by a deadline; a CTA that passes it sets the error
 // word, stops waiting (its remaining waits return at once) and still frees its
@@ -56,6 +57,9 @@ struct KArgs {
     int resident;                     // 1: the CTA's tiles are loaded once and reused by every unit
     int early_weights;                // 1: the weight stream need not wait for the previous kernel
     unsigned long long timeout_ns;
+    const float * norm_w;             // row RMS norm of y into norm_out ([T][Cout]), or null
+    float * norm_out;
+    float norm_eps;
 };
 
 struct Bars {
@@ -425,7 +429,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a, const __gri
 }
 
 // Split-K reduction: y[t][co] = epi(bias[co] + sum over splits, in split order, of the
-// partial sums) -- one thread per output, four splits' loads in flight at a time.
+// partial sums) -- one thread per output, eight splits' loads in flight at a time.
 template <int EPI>
 __global__ void k_splitk_reduce(const float * partial, int splits, int T, int Cout, const float * bias, const float * scale,
                                 const float * resid, int r_stride, float * y, int y_stride) {
@@ -437,20 +441,69 @@ __global__ void k_splitk_reduce(const float * partial, int splits, int T, int Co
     const int t = static_cast<int>(i / Cout), co = static_cast<int>(i % Cout);
     float acc = 0.f;
     int k = 0;
-    for (; k + 4 <= splits; k += 4) {
-        const float p0 = __ldcg(partial + static_cast<std::size_t>(k) * n + i);
-        const float p1 = __ldcg(partial + static_cast<std::size_t>(k + 1) * n + i);
-        const float p2 = __ldcg(partial + static_cast<std::size_t>(k + 2) * n + i);
-        const float p3 = __ldcg(partial + static_cast<std::size_t>(k + 3) * n + i);
-        acc += p0;
-        acc += p1;
-        acc += p2;
-        acc += p3;
+    for (; k + 8 <= splits; k += 8) {
+        float q[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) q[u] = __ldcg(partial + static_cast<std::size_t>(k + u) * n + i);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc += q[u];
     }
     for (; k < splits; ++k) acc += __ldcg(partial + static_cast<std::size_t>(k) * n + i);
     const float v = acc + (bias ? bias[co] : 0.f);
     const float r = (EPI == EPI_RESIDUAL || EPI == EPI_SCALE_RESIDUAL) ? resid[static_cast<std::size_t>(t) * r_stride + co] : 0.f;
     y[static_cast<std::size_t>(t) * y_stride + co] = finish<EPI>(v, EPI == EPI_SCALE_RESIDUAL ? scale[co] : 1.f, r);
+}
+
+// Split-K reduction fused with the RMS norm that follows the conv, one CTA of RN_THREADS
+// threads per row t (a thread per channel, so the partial loads have the parallelism of
+// k_splitk_reduce): y[t] as k_splitk_reduce computes it (splits == 0: y[t] is already
+// final, written by the conv's own epilogue), then norm_out[t][co] = y[t][co] *
+// rsqrt(mean(y[t]^2) + eps) * norm_w[co] (the decoder transformer's RMSNorm:
+// model/qwen3tts/kernels.h:342, called at model/qwen3tts/vocoder.hip:274, 285, 291).
+constexpr int RN_THREADS = 1024;
+
+template <int EPI>
+__global__ void __launch_bounds__(RN_THREADS) k_reduce_norm(const float * partial, int splits, int T, int Cout, const float * bias,
+                                                            const float * scale, const float * resid, int r_stride, float * y,
+                                                            int y_stride, const float * norm_w, float eps, float * norm_out) {
+    griddep_wait();
+    griddep_launch_dependents();
+    __shared__ float red[RN_THREADS / 32];
+    const std::size_t n = static_cast<std::size_t>(T) * Cout;
+    const int t = blockIdx.x;
+    float * yr = y + static_cast<std::size_t>(t) * y_stride;
+    float ss = 0.f;
+    for (int co = threadIdx.x; co < Cout; co += RN_THREADS) {
+        float v;
+        if (splits > 0) {
+            const float * pp = partial + static_cast<std::size_t>(t) * Cout + co;
+            float acc = 0.f;
+            int k = 0;
+            for (; k + 8 <= splits; k += 8) {   // eight loads in flight, added in split order
+                float q[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) q[u] = __ldcg(pp + static_cast<std::size_t>(k + u) * n);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc += q[u];
+            }
+            for (; k < splits; ++k) acc += __ldcg(pp + static_cast<std::size_t>(k) * n);
+            const float r = (EPI == EPI_RESIDUAL || EPI == EPI_SCALE_RESIDUAL) ? resid[static_cast<std::size_t>(t) * r_stride + co] : 0.f;
+            v = finish<EPI>(acc + (bias ? bias[co] : 0.f), EPI == EPI_SCALE_RESIDUAL ? scale[co] : 1.f, r);
+            yr[co] = v;
+        } else {
+            v = yr[co];
+        }
+        ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < RN_THREADS / 32; ++k) tot += red[k];
+    const float inv = rsqrtf(tot / static_cast<float>(Cout) + eps);
+    float * nr = norm_out + static_cast<std::size_t>(t) * Cout;
+    for (int co = threadIdx.x; co < Cout; co += RN_THREADS) nr[co] = yr[co] * inv * norm_w[co];
 }
 
 struct PackArgs {
@@ -499,7 +552,11 @@ void launch_t(const KArgs & ka, const CUtensorMap & tm, dim3 grid, std::size_t s
         attr.fetch_or(bit);
     }
     NAVI_CUDA(navi::dev::launch_pdl(k_conv<PRO, EPI>, grid, dim3(NTHREADS), smem, stream, ka, tm));
-    if (ka.splits > 1) {
+    if (ka.norm_out) {
+        NAVI_CUDA(navi::dev::launch_pdl(k_reduce_norm<EPI>, dim3(static_cast<unsigned>(ka.T)), dim3(RN_THREADS), 0, stream, ka.partial,
+                                        ka.splits > 1 ? ka.splits : 0, ka.T, ka.Cout, ka.bias, ka.scale, ka.resid, ka.r_stride, ka.y,
+                                        ka.y_stride, ka.norm_w, ka.norm_eps, ka.norm_out));
+    } else if (ka.splits > 1) {
         const std::size_t n = static_cast<std::size_t>(ka.T) * ka.Cout;
         NAVI_CUDA(navi::dev::launch_pdl(k_splitk_reduce<EPI>, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream, ka.partial,
                                         ka.splits, ka.T, ka.Cout, ka.bias, ka.scale, ka.resid, ka.r_stride, ka.y, ka.y_stride));
@@ -610,6 +667,7 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     if (c.hist_out && c.hist_out == c.hist) fail("conv: the next history needs a buffer of its own", NAVI_E_ARG);
     if ((c.epi == EPI_RESIDUAL || c.epi == EPI_SCALE_RESIDUAL) && !c.resid) fail("conv: residual missing", NAVI_E_SHAPE);
     if (c.epi == EPI_SCALE_RESIDUAL && !c.scale) fail("conv: layer scale missing", NAVI_E_SHAPE);
+    if (c.norm_w && (!c.norm_out || c.norm_out == c.y)) fail("conv: the row norm needs an output buffer of its own", NAVI_E_ARG);
     const Plan p = plan(c, sms);
     if (p.splits > 1) {
         if (static_cast<std::size_t>(p.splits) * c.T * c.Cout > ws.partial_cap)
@@ -625,6 +683,7 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     ka.lbo = p.lbo; ka.wrows = p.BN + ka.H; ka.tmem_cols = p.tmem_cols; ka.timeout_ns = ws.timeout_ns;
     ka.nst = p.nst; ka.resident = p.resident ? 1 : 0;
     ka.early_weights = c.weights_settled ? 1 : 0;
+    ka.norm_w = c.norm_w; ka.norm_out = c.norm_w ? c.norm_out : nullptr; ka.norm_eps = c.norm_eps;
     CUtensorMap tm;
     std::memset(&tm, 0, sizeof tm);
     if (c.w_rm) {

@@ -85,6 +85,12 @@ struct Conv {
     // or uploaded before a synchronisation): the weight stream may then start before the
     // previous kernel in the stream has finished
     bool weights_settled = false;
+    // when set: also writes norm_out[t][co] = y[t][co] * rsqrt(mean_co y[t][co]^2 + norm_eps)
+    // * norm_w[co] (rows [T][Cout]), the RMS norm of a following layer, in the split-K
+    // reduction's launch (or one row-norm launch when the conv is not split)
+    const float * norm_w = nullptr;
+    float * norm_out = nullptr;
+    float norm_eps = 0.f;
 };
 
 struct Plan {

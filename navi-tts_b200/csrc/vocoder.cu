@@ -62,19 +62,6 @@ __device__ __forceinline__ float block_sum256(float v, float * red) {
     return t;
 }
 
-// out[t] = x[t] * rsqrt(mean(x[t]^2) + eps) * w; 256 threads per row.
-__global__ void k_rmsnorm_rows(const float * x, const float * w, int H, float eps, float * out) {
-    navi::dev::griddep_wait();
-    navi::dev::griddep_launch_dependents();
-    __shared__ float red[8];
-    const float * xr = x + static_cast<std::size_t>(blockIdx.x) * H;
-    float * yr = out + static_cast<std::size_t>(blockIdx.x) * H;
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xr[i] * xr[i];
-    const float scale = rsqrtf(block_sum256(ss, red) / static_cast<float>(H) + eps);
-    for (int i = threadIdx.x; i < H; i += blockDim.x) yr[i] = xr[i] * scale * w[i];
-}
-
 // Rotate-half RoPE on q (in place) and k of row t at position pos0 + t; k and v go to
 // ring slot pos & (ring - 1) (vocoder.hip:59-82).  qkv rows: [q | k | v], HD each.
 __global__ void k_rope_append(float * qkv, int nh, int hd, int pos0, int ring, const float * inv_freq, float * kc, float * vc) {
@@ -329,7 +316,9 @@ struct Vocoder::Impl {
         hook(name, buf, rows, cols);
     }
 
-    void run(CV & cv, const float * xin, int T, int x_stride, float * y, int y_stride, const float * resid = nullptr) {
+    // norm_w: also writes the rows of y RMS-normalised with these weights into norm_out
+    void run(CV & cv, const float * xin, int T, int x_stride, float * y, int y_stride, const float * resid = nullptr,
+             const float * norm_w = nullptr, float * norm_out = nullptr) {
         conv::Conv c = cv.c;
         c.weights_settled = true;   // packed in create(), which synchronises before returning
         c.x = xin;
@@ -341,6 +330,9 @@ struct Vocoder::Impl {
         c.y_stride = y_stride;
         c.resid = resid;
         c.r_stride = y_stride;
+        c.norm_w = norm_w;
+        c.norm_out = norm_out;
+        c.norm_eps = eps;
         conv::launch(c, ws, sms, stream);
         std::swap(cv.hist, cv.hist2);
     }
@@ -394,22 +386,21 @@ void Vocoder::Impl::decode_chunk(int T) {
     snap("rvq", h, T, CD);
     run(pre_conv, h, T, CD, a, L);
     snap("pre_conv", a, T, L);
-    run(in_proj, a, T, L, x, VH);
+    // Every RMSNorm of the transformer (kernels.h:342 at vocoder.hip:274, 285, 291) is
+    // applied by the launch of the conv that writes its input row: n = norm(x).
+    run(in_proj, a, T, L, x, VH, nullptr, layers.empty() ? final_norm : layers[0].ln1, n);
     const float scale = 1.f / std::sqrt(static_cast<float>(hd));
     for (std::size_t l = 0; l < layers.size(); ++l) {
         Layer & ly = layers[l];
-        NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm_rows, dim3(T), dim3(256), 0, stream, x, ly.ln1, VH, eps, n));
         run(ly.qkv, n, T, VH, qkv, 3 * HD);
         NAVI_CUDA(navi::dev::launch_pdl(k_rope_append, dim3(T), dim3(256), 0, stream, qkv, nh, hd, pos0, ring, inv_freq, ly.kc, ly.vc));
         NAVI_CUDA(navi::dev::launch_pdl(k_window_attn, dim3(T, nh), dim3(128), 0, stream, qkv, nh, hd, pos0, window, ring, scale, ly.kc, ly.vc, att));
         NAVI_CUDA(cudaGetLastError());
-        run(ly.o, att, T, HD, x, VH, x);
-        NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm_rows, dim3(T), dim3(256), 0, stream, x, ly.ln2, VH, eps, n));
+        run(ly.o, att, T, HD, x, VH, x, ly.ln2, n);
         run(ly.gateup, n, T, VH, gu, 2 * FF);
-        run(ly.down, gu, T, 2 * FF, x, VH, x);
+        run(ly.down, gu, T, 2 * FF, x, VH, x, l + 1 < layers.size() ? layers[l + 1].ln1 : final_norm, n);
         snap(("layer" + std::to_string(l)).c_str(), x, T, VH);
     }
-    NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm_rows, dim3(T), dim3(256), 0, stream, x, final_norm, VH, eps, n));
     run(out_proj, n, T, VH, u, L);
     snap("pre_transformer", u, T, L);
 
