@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a, const __gri
 }
 
 // Split-K reduction: y[t][co] = epi(bias[co] + sum over splits, in split order, of the
-// partial sums) -- one thread per output, eight splits' loads in flight at a time.
+// partial sums) -- one thread per output, up to eight splits' loads in flight at a time.
 template <int EPI>
 __global__ void k_splitk_reduce(const float * partial, int splits, int T, int Cout, const float * bias, const float * scale,
                                 const float * resid, int r_stride, float * y, int y_stride) {
@@ -439,16 +439,7 @@ __global__ void k_splitk_reduce(const float * partial, int splits, int T, int Co
     const std::size_t i = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int t = static_cast<int>(i / Cout), co = static_cast<int>(i % Cout);
-    float acc = 0.f;
-    int k = 0;
-    for (; k + 8 <= splits; k += 8) {
-        float q[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) q[u] = __ldcg(partial + static_cast<std::size_t>(k + u) * n + i);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc += q[u];
-    }
-    for (; k < splits; ++k) acc += __ldcg(partial + static_cast<std::size_t>(k) * n + i);
+    const float acc = sum_slices(partial + i, splits, n);
     const float v = acc + (bias ? bias[co] : 0.f);
     const float r = (EPI == EPI_RESIDUAL || EPI == EPI_SCALE_RESIDUAL) ? resid[static_cast<std::size_t>(t) * r_stride + co] : 0.f;
     y[static_cast<std::size_t>(t) * y_stride + co] = finish<EPI>(v, EPI == EPI_SCALE_RESIDUAL ? scale[co] : 1.f, r);
@@ -476,17 +467,7 @@ __global__ void __launch_bounds__(RN_THREADS) k_reduce_norm(const float * partia
     for (int co = threadIdx.x; co < Cout; co += RN_THREADS) {
         float v;
         if (splits > 0) {
-            const float * pp = partial + static_cast<std::size_t>(t) * Cout + co;
-            float acc = 0.f;
-            int k = 0;
-            for (; k + 8 <= splits; k += 8) {   // eight loads in flight, added in split order
-                float q[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) q[u] = __ldcg(pp + static_cast<std::size_t>(k + u) * n);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) acc += q[u];
-            }
-            for (; k < splits; ++k) acc += __ldcg(pp + static_cast<std::size_t>(k) * n);
+            const float acc = sum_slices(partial + static_cast<std::size_t>(t) * Cout + co, splits, n);
             const float r = (EPI == EPI_RESIDUAL || EPI == EPI_SCALE_RESIDUAL) ? resid[static_cast<std::size_t>(t) * r_stride + co] : 0.f;
             v = finish<EPI>(acc + (bias ? bias[co] : 0.f), EPI == EPI_SCALE_RESIDUAL ? scale[co] : 1.f, r);
             yr[co] = v;
@@ -542,7 +523,7 @@ __global__ void k_pack(const PackArgs pa, __half * dst, std::size_t n) {
 }
 
 template <int PRO, int EPI>
-void launch_t(const KArgs & ka, const CUtensorMap & tm, dim3 grid, std::size_t smem, cudaStream_t stream) {
+void launch_t(const KArgs & ka, const CUtensorMap & tm, dim3 grid, std::size_t smem, cudaStream_t stream, bool reduce) {
     static std::atomic<uint64_t> attr{0};   // devices whose attribute is set, one bit per ordinal < 64
     int dev = 0;
     NAVI_CUDA(cudaGetDevice(&dev));
@@ -552,6 +533,7 @@ void launch_t(const KArgs & ka, const CUtensorMap & tm, dim3 grid, std::size_t s
         attr.fetch_or(bit);
     }
     NAVI_CUDA(navi::dev::launch_pdl(k_conv<PRO, EPI>, grid, dim3(NTHREADS), smem, stream, ka, tm));
+    if (!reduce) return;
     if (ka.norm_out) {
         NAVI_CUDA(navi::dev::launch_pdl(k_reduce_norm<EPI>, dim3(static_cast<unsigned>(ka.T)), dim3(RN_THREADS), 0, stream, ka.partial,
                                         ka.splits > 1 ? ka.splits : 0, ka.T, ka.Cout, ka.bias, ka.scale, ka.resid, ka.r_stride, ka.y,
@@ -655,8 +637,8 @@ std::size_t partial_need(const Conv & c, int sms) {
     return p.splits > 1 ? static_cast<std::size_t>(p.splits) * c.T * c.Cout : 0;
 }
 
-void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) {
-    if (c.T <= 0) return;
+int launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) {
+    if (c.T <= 0) return 0;
     if (c.Cin % 8 || c.x_stride % 4 || c.K < 1 || c.dil < 1 || !(c.w || c.w_rm) || !c.x || !c.y)
         fail("conv: Cin and the input row stride must be multiples of 8 and 4", NAVI_E_SHAPE);
     if ((reinterpret_cast<std::uintptr_t>(c.x) | reinterpret_cast<std::uintptr_t>(c.hist) | reinterpret_cast<std::uintptr_t>(c.w)) & 15u)
@@ -668,6 +650,7 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     if ((c.epi == EPI_RESIDUAL || c.epi == EPI_SCALE_RESIDUAL) && !c.resid) fail("conv: residual missing", NAVI_E_SHAPE);
     if (c.epi == EPI_SCALE_RESIDUAL && !c.scale) fail("conv: layer scale missing", NAVI_E_SHAPE);
     if (c.norm_w && (!c.norm_out || c.norm_out == c.y)) fail("conv: the row norm needs an output buffer of its own", NAVI_E_ARG);
+    if (c.defer_reduce && (c.epi != EPI_NONE || c.norm_w)) fail("conv: a deferred split-K reduction takes no epilogue and no row norm", NAVI_E_ARG);
     const Plan p = plan(c, sms);
     if (p.splits > 1) {
         if (static_cast<std::size_t>(p.splits) * c.T * c.Cout > ws.partial_cap)
@@ -693,7 +676,11 @@ void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) 
     }
     const dim3 grid(std::min(p.NT * p.MT * p.splits, sms));   // persistent: one CTA per SM at most
 #define NAVI_CONV_CASE(PR, EP) \
-    if (c.pro == PR && c.epi == EP) { launch_t<PR, EP>(ka, tm, grid, p.smem, stream); NAVI_CUDA(cudaGetLastError()); return; }
+    if (c.pro == PR && c.epi == EP) {                                                                      \
+        launch_t<PR, EP>(ka, tm, grid, p.smem, stream, !c.defer_reduce);                                   \
+        NAVI_CUDA(cudaGetLastError());                                                                     \
+        return c.defer_reduce && p.splits > 1 ? p.splits : 0;                                              \
+    }
     NAVI_CONV_CASE(PRO_NONE, EPI_NONE)
     NAVI_CONV_CASE(PRO_NONE, EPI_GELU)
     NAVI_CONV_CASE(PRO_NONE, EPI_SCALE_RESIDUAL)

@@ -91,6 +91,9 @@ struct Conv {
     const float * norm_w = nullptr;
     float * norm_out = nullptr;
     float norm_eps = 0.f;
+    // when set: a split-K launch leaves its partial sums in the workspace for the caller to
+    // reduce (slice k at partial + k T Cout, rows [T][Cout], bias not included); EPI_NONE only
+    bool defer_reduce = false;
 };
 
 struct Plan {
@@ -112,6 +115,8 @@ void weight_map(const __half * w, int Cout, int Cin, int ld, void * out);
 // Elements of split-K partial storage a launch of `c` needs.
 std::size_t partial_need(const Conv & c, int sms);
 
-void launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream);
+// Returns the number of split-K partial slices left in ws.partial (Conv::defer_reduce), else 0
+// (y holds the result).
+int launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream);
 
 } // namespace navi::conv

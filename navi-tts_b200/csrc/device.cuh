@@ -24,6 +24,36 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// sum_{k < slices} p[k * stride] added in k order (so the result does not depend on how the
+// loads are batched), with up to eight L2 loads in flight: the split-K reductions.
+__device__ __forceinline__ float sum_slices(const float * p, int slices, std::size_t stride) {
+    float acc = 0.f;
+    int k = 0;
+    for (; k + 8 <= slices; k += 8) {
+        float q[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) q[u] = __ldcg(p + static_cast<std::size_t>(k + u) * stride);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc += q[u];
+    }
+    if (k + 4 <= slices) {
+        float q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) q[u] = __ldcg(p + static_cast<std::size_t>(k + u) * stride);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc += q[u];
+        k += 4;
+    }
+    if (k + 2 <= slices) {
+        const float q0 = __ldcg(p + static_cast<std::size_t>(k) * stride), q1 = __ldcg(p + static_cast<std::size_t>(k + 1) * stride);
+        acc += q0;
+        acc += q1;
+        k += 2;
+    }
+    if (k < slices) acc += __ldcg(p + static_cast<std::size_t>(k) * stride);
+    return acc;
+}
+
 // Named barrier over the first `nthreads` threads (a multiple of 32) of the CTA.
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

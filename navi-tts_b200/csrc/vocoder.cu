@@ -62,8 +62,58 @@ __device__ __forceinline__ float block_sum256(float v, float * red) {
     return t;
 }
 
+// Finishes QKV row t and appends it to the attention ring (vocoder.hip:59-82): the row is
+// the sum, in split order, of the QKV projection's `splits` split-K partial slices ([T][3 HD]
+// each; the projection has no bias), or, with splits == 0, already in qkv.  blockIdx.y picks
+// the part: 0 = q, rotate-half RoPE at position pos0 + t in place; 1 = k, rotated into qkv
+// and ring slot pos & (ring - 1); 2 = v, into qkv and the ring slot.  blockIdx.z picks a
+// group of QKV_THREADS / hd heads (hd <= QKV_THREADS), one thread per element for the
+// partial loads, staged in shared memory for the rotation.
+constexpr int QKV_THREADS = 256;
+// Chunks of up to this many rows take k_qkv_rope_append (one launch fewer per layer: 4-frame
+// chunk 0.840 -> 0.810 ms); a 16-frame chunk measured 1.080 -> 1.143 ms with it and keeps the
+// separate reduction + k_rope_append.
+constexpr int QKV_FUSED_ROWS = 8;
+__global__ void __launch_bounds__(QKV_THREADS) k_qkv_rope_append(const float * partial, int splits, float * qkv, int nh, int hd,
+                                                                 int pos0, int ring, const float * inv_freq, float * kc, float * vc) {
+    navi::dev::griddep_wait();
+    navi::dev::griddep_launch_dependents();
+    __shared__ float buf[QKV_THREADS];
+    const int t = blockIdx.x, part = blockIdx.y, pos = pos0 + t, slot = pos & (ring - 1);
+    const int HD = nh * hd, half = hd / 2, hpc = QKV_THREADS / hd, h0 = blockIdx.z * hpc;
+    const int nheads = min(hpc, nh - h0), cnt = nheads * hd;
+    const std::size_t n = static_cast<std::size_t>(gridDim.x) * 3 * HD;
+    const std::size_t off = static_cast<std::size_t>(part) * HD + static_cast<std::size_t>(h0) * hd;
+    float * row = qkv + static_cast<std::size_t>(t) * 3 * HD + off;
+    const int e = threadIdx.x;
+    if (e < cnt) buf[e] = splits > 0 ? navi::dev::sum_slices(partial + static_cast<std::size_t>(t) * 3 * HD + off + e, splits, n) : row[e];
+    __syncthreads();
+    if (part == 2) {
+        if (e < cnt) {
+            row[e] = buf[e];
+            vc[static_cast<std::size_t>(slot) * HD + static_cast<std::size_t>(h0) * hd + e] = buf[e];
+        }
+        return;
+    }
+    if (e < nheads * half) {
+        const int h = e / half, p = e % half;
+        const float ang = static_cast<float>(pos) * inv_freq[p];
+        const float cs = cosf(ang), sn = sinf(ang);
+        const float x0 = buf[h * hd + p], x1 = buf[h * hd + p + half];
+        const float r0 = x0 * cs - x1 * sn, r1 = x1 * cs + x0 * sn;
+        row[h * hd + p] = r0;
+        row[h * hd + p + half] = r1;
+        if (part == 1) {
+            float * kd = kc + static_cast<std::size_t>(slot) * HD + static_cast<std::size_t>(h0 + h) * hd;
+            kd[p] = r0;
+            kd[p + half] = r1;
+        }
+    }
+}
+
 // Rotate-half RoPE on q (in place) and k of row t at position pos0 + t; k and v go to
-// ring slot pos & (ring - 1) (vocoder.hip:59-82).  qkv rows: [q | k | v], HD each.
+// ring slot pos & (ring - 1) (vocoder.hip:59-82).  qkv rows: [q | k | v], HD each.  Chunks
+// of more than QKV_FUSED_ROWS rows: after the QKV projection's own split-K reduction.
 __global__ void k_rope_append(float * qkv, int nh, int hd, int pos0, int ring, const float * inv_freq, float * kc, float * vc) {
     navi::dev::griddep_wait();
     navi::dev::griddep_launch_dependents();
@@ -317,8 +367,9 @@ struct Vocoder::Impl {
     }
 
     // norm_w: also writes the rows of y RMS-normalised with these weights into norm_out
-    void run(CV & cv, const float * xin, int T, int x_stride, float * y, int y_stride, const float * resid = nullptr,
-             const float * norm_w = nullptr, float * norm_out = nullptr) {
+    // defer: a split-K launch leaves its partial sums in ws.partial; returns their slice count
+    int run(CV & cv, const float * xin, int T, int x_stride, float * y, int y_stride, const float * resid = nullptr,
+            const float * norm_w = nullptr, float * norm_out = nullptr, bool defer = false) {
         conv::Conv c = cv.c;
         c.weights_settled = true;   // packed in create(), which synchronises before returning
         c.x = xin;
@@ -333,8 +384,10 @@ struct Vocoder::Impl {
         c.norm_w = norm_w;
         c.norm_out = norm_out;
         c.norm_eps = eps;
-        conv::launch(c, ws, sms, stream);
+        c.defer_reduce = defer;
+        const int splits = conv::launch(c, ws, sms, stream);
         std::swap(cv.hist, cv.hist2);
+        return splits;
     }
 
     void hist_update(float * hist, const float * xin, int x_stride, int T, int H, int C) {
@@ -392,8 +445,15 @@ void Vocoder::Impl::decode_chunk(int T) {
     const float scale = 1.f / std::sqrt(static_cast<float>(hd));
     for (std::size_t l = 0; l < layers.size(); ++l) {
         Layer & ly = layers[l];
-        run(ly.qkv, n, T, VH, qkv, 3 * HD);
-        NAVI_CUDA(navi::dev::launch_pdl(k_rope_append, dim3(T), dim3(256), 0, stream, qkv, nh, hd, pos0, ring, inv_freq, ly.kc, ly.vc));
+        if (T <= QKV_FUSED_ROWS) {
+            const int qs = run(ly.qkv, n, T, VH, qkv, 3 * HD, nullptr, nullptr, nullptr, true);
+            const int hpc = QKV_THREADS / hd;
+            NAVI_CUDA(navi::dev::launch_pdl(k_qkv_rope_append, dim3(T, 3, (nh + hpc - 1) / hpc), dim3(QKV_THREADS), 0, stream, ws.partial, qs,
+                                            qkv, nh, hd, pos0, ring, inv_freq, ly.kc, ly.vc));
+        } else {
+            run(ly.qkv, n, T, VH, qkv, 3 * HD);
+            NAVI_CUDA(navi::dev::launch_pdl(k_rope_append, dim3(T), dim3(256), 0, stream, qkv, nh, hd, pos0, ring, inv_freq, ly.kc, ly.vc));
+        }
         NAVI_CUDA(navi::dev::launch_pdl(k_window_attn, dim3(T, nh), dim3(128), 0, stream, qkv, nh, hd, pos0, window, ring, scale, ly.kc, ly.vc, att));
         NAVI_CUDA(cudaGetLastError());
         run(ly.o, att, T, HD, x, VH, x, ly.ln2, n);
