@@ -230,13 +230,17 @@ struct Talker::Impl {
     }
 
     // y[M][N] (row stride ys) = epi(op(x)[M][K] W[N][K]^T + bias); op = silu(gate) * up when
-    // gate (x rows [gate K | up K]); EPI_RESIDUAL adds res (may alias y).
+    // gate (x rows [gate K | up K]); EPI_RESIDUAL adds res (may alias y).  norm_w: the same
+    // launch also writes the rows of y RMS-normalised with these weights into norm_out.
     void gemm(const __half * W, const float * bias, const float * in, int xs, int M, int K, int N, float * out, int ys, int epi,
-              bool gate = false, const float * res = nullptr) {
+              bool gate = false, const float * res = nullptr, const float * norm_w = nullptr, float * norm_out = nullptr) {
         conv::Conv c = gemm_desc(W, bias, xs, M, K, N, ys, epi, gate);
         c.x = in;
         c.y = out;
         c.resid = res;
+        c.norm_w = norm_w;
+        c.norm_out = norm_out;
+        c.norm_eps = p.talker.rms_eps;
         conv::launch(c, ws, sms, stream);
     }
 };
@@ -411,15 +415,18 @@ void Talker::prefill(const Prompt & pr) {
         const Layer & ly = I.layers[static_cast<size_t>(l)];
         __half * kc = reinterpret_cast<__half *>(I.kptr[static_cast<size_t>(l)]);
         __half * vc = reinterpret_cast<__half *>(I.vptr[static_cast<size_t>(l)]);
-        NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm, dim3(T), dim3(256), 0, I.stream, I.x, ly.ln1, H, tp.rms_eps, I.n));
+        if (l == 0) NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm, dim3(T), dim3(256), 0, I.stream, I.x, ly.ln1, H, tp.rms_eps, I.n));
         I.gemm(ly.wqkv, nullptr, I.n, H, T, H, I.QKV, I.qkv, I.QKV, EPI_NONE);
         NAVI_CUDA(navi::dev::launch_pdl(k_qk_norm_rope, dim3(T), dim3(256), 0, I.stream, I.qkv, I.QKV, ly.qn, ly.kn, I.NH, I.NKV, tp.rms_eps,
                                         I.rope, 0, kc, vc));
         NAVI_CUDA(navi::dev::launch_pdl(k_prefill_attn, dim3(T, I.NH), dim3(128), 0, I.stream, I.qkv, I.QKV, kc, vc, I.NH, I.NKV, 0, I.att));
-        I.gemm(ly.wo, nullptr, I.att, I.Q, T, I.Q, H, I.x, H, EPI_RESIDUAL, false, I.x);
-        NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm, dim3(T), dim3(256), 0, I.stream, I.x, ly.ln2, H, tp.rms_eps, I.n));
+        // the RMSNorms after the O projection and (but for the last layer) after the down
+        // projection are written by those GEMMs' launches
+        I.gemm(ly.wo, nullptr, I.att, I.Q, T, I.Q, H, I.x, H, EPI_RESIDUAL, false, I.x, ly.ln2, I.n);
         I.gemm(ly.wgu, nullptr, I.n, H, T, H, 2 * I.F, I.gu, 2 * I.F, EPI_NONE);
-        I.gemm(ly.wd, nullptr, I.gu, 2 * I.F, T, I.F, H, I.x, H, EPI_RESIDUAL, true, I.x);
+        const bool last = l + 1 == tp.n_layer;
+        I.gemm(ly.wd, nullptr, I.gu, 2 * I.F, T, I.F, H, I.x, H, EPI_RESIDUAL, true, I.x, last ? nullptr : I.layers[static_cast<size_t>(l + 1)].ln1,
+               last ? nullptr : I.n);
     }
     // the last row: final norm and the codec head
     NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm, dim3(1), dim3(256), 0, I.stream, I.x + static_cast<size_t>(T - 1) * H, I.final_norm, H,
