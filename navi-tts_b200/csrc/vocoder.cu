@@ -24,7 +24,6 @@ namespace {
 using namespace navi::dev;
 
 constexpr int NQ_MAX = 32;
-constexpr int HIST_MAX = 64;   // history rows the in-place update handles (largest: 6 * 9 = 54)
 
 // ---- row-local kernels ---------------------------------------------------------------------------
 
@@ -179,14 +178,29 @@ __global__ void k_window_attn(const float * qkv, int nh, int hd, int pos0, int w
     }
 }
 
+// Next chunk's history of a k = 7 conv, the last 6 rows of [hist ; x[0..T)] (x rows of C
+// floats), into hist_out, a buffer other than hist (vocoder.hip:133-141): the block that
+// reads x rows [r0, r1) copies those of them that land there; block 0 also keeps the old
+// history rows when T < 6.
+__device__ __forceinline__ void next_hist6(const float * x, const float * hist, int T, int C, int r0, int r1, float * hist_out) {
+    for (int t = max(r0, T - 6); t < min(r1, T); ++t)
+        for (int c = threadIdx.x; c < C; c += blockDim.x)
+            hist_out[static_cast<std::size_t>(t - (T - 6)) * C + c] = x[static_cast<std::size_t>(t) * C + c];
+    if (blockIdx.x == 0)
+        for (int q = 0; q < 6 - T; ++q)
+            for (int c = threadIdx.x; c < C; c += blockDim.x)
+                hist_out[static_cast<std::size_t>(q) * C + c] = hist[static_cast<std::size_t>(q + T) * C + c];
+}
+
 // ConvNeXt front: depthwise causal conv (k = 7, history of 6 rows) + LayerNorm over the
 // channels (vocoder.hip:20-56).  256 threads per row, C <= 2048.
 __global__ void k_dwconv_ln(const __half * W, const float * bias, const float * x, const float * hist, int C, const float * lw,
-                            const float * lb, float eps, float * y) {
+                            const float * lb, float eps, float * y, float * hist_out) {
     navi::dev::griddep_wait();
     navi::dev::griddep_launch_dependents();
     __shared__ float red[8];
     const int t = blockIdx.x;
+    next_hist6(x, hist, gridDim.x, C, t, t + 1, hist_out);
     float v[8];
     float s = 0.f;
 #pragma unroll
@@ -220,29 +234,11 @@ __global__ void k_dwconv_ln(const __half * W, const float * bias, const float * 
     }
 }
 
-// hist <- the last H rows of [hist ; x[0..T)], in place: each block owns 32 columns and
-// reads all of its rows before writing any (vocoder.hip:133-141).
-__global__ void k_hist_update(float * hist, const float * x, int x_stride, int T, int H, int C) {
-    navi::dev::griddep_wait();
-    navi::dev::griddep_launch_dependents();
-    __shared__ float buf[HIST_MAX][33];
-    const int c = blockIdx.x * 32 + threadIdx.x;
-    for (int r = threadIdx.y; r < H; r += blockDim.y) {
-        const int src = r + T;
-        float v = 0.f;
-        if (c < C) v = src < H ? hist[static_cast<std::size_t>(src) * C + c] : x[static_cast<std::size_t>(src - H) * x_stride + c];
-        buf[r][threadIdx.x] = v;
-    }
-    __syncthreads();
-    for (int r = threadIdx.y; r < H; r += blockDim.y)
-        if (c < C) hist[static_cast<std::size_t>(r) * C + c] = buf[r][threadIdx.x];
-}
-
 // Output conv: 1 channel, k = 7, SnakeBeta prologue, clamp to [-1, 1] (vocoder.hip:338-339).
 // 256 rows per block; the Snake'd window [t0 - 6, t0 + 256) is staged channel-major.
 constexpr int FROWS = 256;
 __global__ void k_final_conv(const __half * W, const float * bias, const float * x, const float * hist, const float * sa, const float * sb,
-                             int T, int Cin, float * y) {
+                             int T, int Cin, float * y, float * hist_out) {
     navi::dev::griddep_wait();
     navi::dev::griddep_launch_dependents();
     extern __shared__ float fs[];
@@ -250,6 +246,7 @@ __global__ void k_final_conv(const __half * W, const float * bias, const float *
     float * xs = fs;                 // [Cin][NR]
     float * ws = fs + Cin * NR;      // [Cin][7]
     const int t0 = blockIdx.x * FROWS;
+    next_hist6(x, hist, T, Cin, t0, t0 + FROWS, hist_out);
     constexpr int U = 8;   // loads in flight per thread
     for (int i0 = threadIdx.x; i0 < NR * Cin; i0 += FROWS * U) {
         float v[U];
@@ -321,7 +318,7 @@ struct Vocoder::Impl {
     struct Cnx {
         const __half * dw = nullptr;
         const float * dw_bias = nullptr, * ln_w = nullptr, * ln_b = nullptr;
-        float * hist = nullptr;
+        float * hist = nullptr, * hist2 = nullptr;   // history; the launch writes the next one into hist2
         CV pw1, pw2;
     } cnx[2];
     struct Block {
@@ -332,7 +329,7 @@ struct Vocoder::Impl {
     struct Final {
         const __half * w = nullptr;
         const float * bias = nullptr, * sa = nullptr, * sb = nullptr;
-        float * hist = nullptr;
+        float * hist = nullptr, * hist2 = nullptr;   // history; the launch writes the next one into hist2
         int Cin = 0;
     } fin;
     float * inv_freq = nullptr;
@@ -388,11 +385,6 @@ struct Vocoder::Impl {
         const int splits = conv::launch(c, ws, sms, stream);
         std::swap(cv.hist, cv.hist2);
         return splits;
-    }
-
-    void hist_update(float * hist, const float * xin, int x_stride, int T, int H, int C) {
-        NAVI_CUDA(navi::dev::launch_pdl(k_hist_update, dim3((C + 31) / 32), dim3(32, 8), 0, stream, hist, xin, x_stride, T, H, C));
-        NAVI_CUDA(cudaGetLastError());
     }
 
     void decode_chunk(int T);
@@ -473,9 +465,10 @@ void Vocoder::Impl::decode_chunk(int T) {
         run(up_conv[j], src, R, L, dst, r * L);   // phases folded: output row t*r + phase, dense
         R *= r;
         Cnx & cx = cnx[j];
-        NAVI_CUDA(navi::dev::launch_pdl(k_dwconv_ln, dim3(R), dim3(256), 0, stream, cx.dw, cx.dw_bias, dst, cx.hist, L, cx.ln_w, cx.ln_b, 1e-6f, tmp));
+        NAVI_CUDA(navi::dev::launch_pdl(k_dwconv_ln, dim3(R), dim3(256), 0, stream, cx.dw, cx.dw_bias, dst, cx.hist, L, cx.ln_w, cx.ln_b, 1e-6f, tmp,
+                                        cx.hist2));
         NAVI_CUDA(cudaGetLastError());
-        hist_update(cx.hist, dst, L, R, 6, L);
+        std::swap(cx.hist, cx.hist2);
         run(cx.pw1, tmp, R, L, G, 4 * L);
         run(cx.pw2, G, R, 4 * L, dst, L, dst);
         snap(("up" + std::to_string(j)).c_str(), dst, R, L);
@@ -498,9 +491,10 @@ void Vocoder::Impl::decode_chunk(int T) {
         in = P[b];
     }
     const int fsmem = (FROWS + 6) * fin.Cin * 4 + fin.Cin * 7 * 4;
-    NAVI_CUDA(navi::dev::launch_pdl(k_final_conv, dim3((R + FROWS - 1) / FROWS), dim3(FROWS), fsmem, stream, fin.w, fin.bias, in, fin.hist, fin.sa, fin.sb, R, fin.Cin, pcm));
+    NAVI_CUDA(navi::dev::launch_pdl(k_final_conv, dim3((R + FROWS - 1) / FROWS), dim3(FROWS), fsmem, stream, fin.w, fin.bias, in, fin.hist, fin.sa, fin.sb, R, fin.Cin, pcm,
+                                    fin.hist2));
     NAVI_CUDA(cudaGetLastError());
-    hist_update(fin.hist, in, fin.Cin, R, 6, fin.Cin);
+    std::swap(fin.hist, fin.hist2);
     snap("pcm", pcm, R, 1);
     pos0 += T;
 }
@@ -545,7 +539,6 @@ std::unique_ptr<Vocoder> Vocoder::create(const Device & dev, const DeviceWeights
         cv.c.w = pack(std::move(srcs), Cout, Cin, K);
         cv.c.Cout = Cout; cv.c.Cin = Cin; cv.c.K = K; cv.c.dil = dil; cv.c.bias = bias; cv.c.pro = pro; cv.c.epi = epi;
         cv.H = (K - 1) * dil;
-        if (cv.H > HIST_MAX) fail("vocoder: conv history above " + std::to_string(HIST_MAX) + " rows", NAVI_E_SHAPE);
         if (cv.H > 0) {
             cv.hist = I.alloc<float>(static_cast<std::size_t>(cv.H) * Cin);
             cv.hist2 = I.alloc<float>(static_cast<std::size_t>(cv.H) * Cin);
@@ -629,6 +622,7 @@ std::unique_ptr<Vocoder> Vocoder::create(const Device & dev, const DeviceWeights
         cx.ln_w = f32_of(w, up + "1.norm.weight");
         cx.ln_b = f32_of(w, up + "1.norm.bias");
         cx.hist = I.alloc<float>(static_cast<std::size_t>(6) * I.L);
+        cx.hist2 = I.alloc<float>(static_cast<std::size_t>(6) * I.L);
         cx.pw1 = make({direct(up + "1.pwconv1.weight", 0, 4 * I.L, 0, I.L, 1)}, 4 * I.L, I.L, 1, 1, f32_of(w, up + "1.pwconv1.bias"),
                       conv::PRO_NONE, conv::EPI_GELU);
         cx.pw2 = make({direct(up + "1.pwconv2.weight", 0, I.L, 0, 4 * I.L, 1)}, I.L, 4 * I.L, 1, 1, f32_of(w, up + "1.pwconv2.bias"),
@@ -670,6 +664,7 @@ std::unique_ptr<Vocoder> Vocoder::create(const Device & dev, const DeviceWeights
     I.fin.bias = f32_of(w, DEC + "decoder." + std::to_string(n_up + 2) + ".conv.bias");
     I.fin.Cin = width;
     I.fin.hist = I.alloc<float>(static_cast<std::size_t>(6) * width);
+    I.fin.hist2 = I.alloc<float>(static_cast<std::size_t>(6) * width);
     {
         CV tmp;
         snake(DEC + "decoder." + std::to_string(n_up + 1), tmp);
@@ -750,12 +745,16 @@ void Vocoder::reset() {
     };
     zero_cv(I.pre_conv);
     zero_cv(I.dec0);
-    for (auto & cx : I.cnx) zero(cx.hist, static_cast<std::size_t>(6) * I.L);
+    for (auto & cx : I.cnx) {
+        zero(cx.hist, static_cast<std::size_t>(6) * I.L);
+        zero(cx.hist2, static_cast<std::size_t>(6) * I.L);
+    }
     for (auto & bk : I.blocks) {
         zero_cv(bk.up);
         for (auto & c1 : bk.c1) zero_cv(c1);
     }
     zero(I.fin.hist, static_cast<std::size_t>(6) * I.fin.Cin);
+    zero(I.fin.hist2, static_cast<std::size_t>(6) * I.fin.Cin);
     // KV rings need no clearing: attention reads only positions <= pos, all written before use.
     NAVI_CUDA(cudaStreamSynchronize(I.stream));
 }
