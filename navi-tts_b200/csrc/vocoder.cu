@@ -70,7 +70,7 @@ __device__ __forceinline__ float block_sum256(float v, float * red) {
 // partial loads, staged in shared memory for the rotation.
 constexpr int QKV_THREADS = 256;
 // Chunks of up to this many rows take k_qkv_rope_append (one launch fewer per layer: 4-frame
-// chunk 0.840 -> 0.810 ms); a 16-frame chunk measured 1.080 -> 1.143 ms with it and keeps the
+// chunk 0.837 -> 0.808 ms); a 16-frame chunk measured 1.080 -> 1.143 ms with it and keeps the
 // separate reduction + k_rope_append.
 constexpr int QKV_FUSED_ROWS = 8;
 __global__ void __launch_bounds__(QKV_THREADS) k_qkv_rope_append(const float * partial, int splits, float * qkv, int nh, int hd,
