@@ -101,6 +101,14 @@ typedef struct navi_params {
  * arena (q/k/v and gate/up of each talker / code-predictor layer adjacent). */
 int navi_weights_upload(navi_device * dev, const char * path, navi_weights ** out);
 int navi_weights_get_params(const navi_weights * w, navi_params * p);
+/* Host only (no device): reads a .navi file's header and KV section and checks its tensor
+ * table against the model the KV section describes, as `navi-tts info` does without
+ * --upload (runtime/cli/main.cpp:247-279 -> NaviFile::open, read_params, validate;
+ * runtime/weights/navi_file.cpp:79-148, model/qwen3tts/params.cpp:59-130, 286-303).
+ * p may be NULL. n_tensors / n_missing / n_mismatched / n_unused (each may be NULL) get the
+ * table's counts; NAVI_E_FORMAT when the file is malformed or a tensor is missing or
+ * mis-shaped, with the first such name in navi_last_error(). */
+int navi_model_probe(const char * path, navi_params * p, int * n_tensors, int * n_missing, int * n_mismatched, int * n_unused);
 /* Device address of a tensor by its .navi name (NULL if absent); dtype per the .navi codes. */
 const void * navi_weights_tensor(const navi_weights * w, const char * name, int * dtype, int * ndim, uint64_t dims[4]);
 uint64_t navi_weights_bytes(const navi_weights * w);

@@ -76,6 +76,8 @@ void to_result(const navi::qwen3tts::FrameResult & r, navi_frame_result * out) {
     out->status = r.ok ? NAVI_OK : r.status;
 }
 
+void fill_params(navi_params & out, const navi::Params & p);
+
 void fill_tp(navi_transformer_params & d, const navi::TransformerParams & s) {
     d.hidden = s.hidden; d.n_layer = s.n_layer; d.n_head = s.n_head; d.n_kv_head = s.n_kv_head; d.head_dim = s.head_dim;
     d.ff = s.ff; d.vocab = s.vocab; d.max_pos = s.max_pos; d.rms_eps = s.rms_eps; d.rope_theta = s.rope_theta;
@@ -155,7 +157,35 @@ int navi_weights_upload(navi_device * dev, const char * path, navi_weights ** ou
 int navi_weights_get_params(const navi_weights * w, navi_params * o) {
     return guard([&]() -> int {
         if (!w || !o) return set_err(NAVI_E_ARG, "NULL argument");
-        const navi::Params & p = w->w->params();
+        fill_params(*o, w->w->params());
+        return NAVI_OK;
+    });
+}
+
+int navi_model_probe(const char * path, navi_params * o, int * n_tensors, int * n_missing, int * n_mismatched, int * n_unused) {
+    return guard([&]() -> int {
+        if (!path) return set_err(NAVI_E_ARG, "path is NULL");
+        navi::NaviFile f = navi::NaviFile::open(path);
+        const navi::Params p = navi::read_params(f);
+        const navi::Validation v = navi::validate(f, p);
+        if (o) fill_params(*o, p);
+        if (n_tensors) *n_tensors = static_cast<int>(f.tensors().size());
+        if (n_missing) *n_missing = static_cast<int>(v.missing.size());
+        if (n_mismatched) *n_mismatched = static_cast<int>(v.shape_mismatch.size());
+        if (n_unused) *n_unused = static_cast<int>(v.unused.size());
+        if (!v.missing.empty()) return set_err(NAVI_E_FORMAT, std::string(path) + ": tensor '" + v.missing[0] + "' is missing");
+        if (!v.shape_mismatch.empty())
+            return set_err(NAVI_E_FORMAT, std::string(path) + ": tensor '" + v.shape_mismatch[0] + "' has the wrong shape");
+        return NAVI_OK;
+    });
+}
+
+}   // extern "C"
+
+namespace {
+void fill_params(navi_params & out, const navi::Params & p) {
+    navi_params * o = &out;
+    {
         std::memset(o, 0, sizeof(*o));
         fill_tp(o->talker, p.talker);
         fill_tp(o->cp, p.cp);
@@ -172,9 +202,11 @@ int navi_weights_get_params(const navi_weights * w, navi_params * o) {
         o->codec_upsample = p.codec_upsample; o->sample_rate = p.codec_sample_rate;
         o->temperature = p.temperature; o->top_p = p.top_p; o->repetition_penalty = p.repetition_penalty;
         o->cp_temperature = p.cp_temperature; o->cp_top_p = p.cp_top_p; o->top_k = p.top_k; o->cp_top_k = p.cp_top_k;
-        return NAVI_OK;
-    });
+    }
 }
+}   // namespace
+
+extern "C" {
 
 const void * navi_weights_tensor(const navi_weights * w, const char * name, int * dtype, int * ndim, uint64_t dims[4]) {
     if (!w || !name) return nullptr;

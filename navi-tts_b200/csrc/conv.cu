@@ -81,11 +81,22 @@ __device__ bool bwait(uint64_t * bar, uint32_t parity, Bars & B, const KArgs & a
                 t0 = now;
             } else if (now - t0 > a.timeout_ns) {
                 *reinterpret_cast<volatile int *>(&B.abort) = 1;
-                atomicExch(a.err, 1);
+                atomicExch(a.err, ERR_TIMEOUT);
                 return false;
             }
         }
     }
+}
+
+// A wait that ignores the abort flag (bounded by its own, longer deadline): the tensor-memory
+// release waits so for every epilogue thread, which arrives on the barrier on every path.
+__device__ void bwait_drain(uint64_t * bar, uint32_t parity, const KArgs & a) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer() - t0 > 4 * a.timeout_ns) {
+            atomicExch(a.err, ERR_TIMEOUT);
+            return;
+        }
 }
 
 // v already includes the bias; r is the residual row value, sc the channel's layer scale.
@@ -214,6 +225,9 @@ __device__ __forceinline__ void epilogue_unit(const KArgs & a, const Unit & w, u
     const uint32_t tq = tacc + (static_cast<uint32_t>(q * 32) << 16);
     const bool fin = live && a.splits == 1;
     float rr[16], rn[16];
+    // after an abort the accumulator holds nothing to read: the warp skips its tensor-memory
+    // loads (tcgen05.ld is warp-collective, so the decision is the warp's)
+    if (!__all_sync(0xffffffffu, ok)) return;
     if (RES) load_resid<EPI>(rr, a, w.t0, co, fin);
     for (int cc = 0; cc < a.BN; cc += 16) {
         float v[16];
@@ -268,11 +282,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a, const __gri
             mbar_init(&B.tempty[i], 128);
         }
         mbar_init(&B.edone, 128);
-        if (a.tmaw && (smem_addr(ring) & 1023u)) {   // 128B-swizzled tiles need 1024-byte alignment
-            B.abort = 1;
-            atomicExch(a.err, 1);
-        }
         B.abort = 0;
+        if (a.tmaw && (smem_addr(ring) & 1023u)) {   // 128B-swizzled tiles need 1024-byte alignment
+            B.abort = 1;                              // no role issues a copy or an MMA
+            atomicExch(a.err, ERR_ALIGN);
+        }
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -421,7 +435,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_conv(const KArgs a, const __gri
     }
     // Free the accumulators only after every epilogue thread's last tensor-memory read.
     if (warp == 1) {
-        if (lane == 0) bwait(&B.edone, 0, B, a);
+        if (lane == 0) bwait_drain(&B.edone, 0, a);
         __syncwarp();
         umma::fence_after_sync();
         umma::tmem_dealloc(tmem, a.tmem_cols);
@@ -754,13 +768,14 @@ int conv_once(const Device & dev, const navi_conv_args & a) {
         int err = 0;
         NAVI_CUDA(cudaMemcpyAsync(&err, ws.err, sizeof(int), cudaMemcpyDeviceToHost, s));
         NAVI_CUDA(cudaStreamSynchronize(s));
-        if (err) st = NAVI_E_TIMEOUT;
+        if (err) st = err == ERR_ALIGN ? NAVI_E_SHAPE : NAVI_E_TIMEOUT;
     } catch (...) {
         (void) cudaStreamSynchronize(s);
         for (void * p : own) (void) cudaFree(p);
         throw;
     }
     for (void * p : own) (void) cudaFree(p);
+    if (st == NAVI_E_SHAPE) fail("conv: the weight ring is not 1024-byte aligned for the swizzled tiles", st);
     if (st != NAVI_OK) fail("conv: a tensor-core conv wait passed its deadline", st);
     return st;
 }

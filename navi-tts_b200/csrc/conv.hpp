@@ -104,10 +104,14 @@ struct Plan {
 };
 Plan plan(const Conv & c, int sms);
 
+// Values of the error word a conv launch leaves in Workspace::err (0: none).
+constexpr int ERR_TIMEOUT = 1;               // a CTA's wait passed its deadline
+constexpr int ERR_ALIGN = 2;                 // the weight ring misses the 1024-byte alignment of swizzled tiles
+
 struct Workspace {
     float * partial = nullptr;               // split-K partial sums
     std::size_t partial_cap = 0;             // elements
-    int * err = nullptr;                     // set to 1 by a CTA whose wait timed out
+    int * err = nullptr;                     // ERR_TIMEOUT / ERR_ALIGN, set by a failing CTA
     unsigned long long timeout_ns = 2000000000ull;
 };
 // Encodes the TMA map of a row-major [Cout][ld] f16 weight (out: a CUtensorMap).

@@ -160,10 +160,6 @@ __device__ __forceinline__ uint64_t l2_policy_stream() {
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
-__device__ __forceinline__ void bulk_prefetch_l2(const void * src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // ---- tagged exchange words --------------------------------------------------------------------
 // A value travels as one 64-bit word {f32 bits, u32 tag}; a 64-bit aligned store is
 // single-copy atomic, so a reader that sees the expected tag also sees the value it
@@ -174,40 +170,10 @@ __device__ __forceinline__ void ll_store(uint64_t * p, float v, uint32_t tag) {
     const uint64_t w = (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
     asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ uint64_t ll_load(const uint64_t * p) {
-    uint64_t w;
-    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-    return w;
-}
 // Two adjacent exchange words (16-byte aligned) in one load; each 64-bit element is
 // single-copy atomic on its own.
 __device__ __forceinline__ void ll_load2(const uint64_t * p, uint64_t & a, uint64_t & b) {
     asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
-}
-
-// Sum of v[j] (j < R, R = 1, 2 or 4) over the warp by a transposed butterfly: the
-// result for j lands on lanes [j * 32/R, (j+1) * 32/R); returns this lane's value.
-template <int R>
-__device__ __forceinline__ float warp_sum_multi(const float * v) {
-    const int lane = threadIdx.x & 31;
-    if constexpr (R == 1) {
-        return warp_sum(v[0]);
-    } else if constexpr (R == 2) {
-        const bool hi = lane & 16;
-        float a = (hi ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, hi ? v[0] : v[1], 16);
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        return a;
-    } else {
-        const bool hi = lane & 16;
-        const float a0 = (hi ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, hi ? v[0] : v[2], 16);
-        const float a1 = (hi ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, hi ? v[1] : v[3], 16);
-        const bool mid = lane & 8;
-        float b = (mid ? a1 : a0) + __shfl_xor_sync(0xffffffffu, mid ? a0 : a1, 8);
-#pragma unroll
-        for (int o = 4; o > 0; o >>= 1) b += __shfl_xor_sync(0xffffffffu, b, o);
-        return b;
-    }
 }
 
 __device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned * p) {
@@ -217,22 +183,6 @@ __device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned * p) {
 }
 __device__ __forceinline__ void st_relaxed_u32(unsigned * p, uint32_t v) {
     asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// ---- warp-level tensor-core tiles (batch-1 GEMV: fewer instructions per weight byte) ----------
-
-// ldmatrix: four 8x8 f16 tiles; lane l supplies the shared address of row (l & 7) of tile l >> 3.
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void * row_addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(smem_addr(row_addr))
-                 : "memory");
-}
-// D(16x8, f32) += A(16x16, f16, row) * B(16x8, f16, col)
-__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // ---- f16 helpers ---------------------------------------------------------------------------------
@@ -248,13 +198,6 @@ __device__ __forceinline__ float dot8h(uint4 w, float4 a, float4 b) {
     const float p0 = fmaf(w0.y, a.y, w0.x * a.x), p1 = fmaf(w1.y, a.w, w1.x * a.z);
     const float p2 = fmaf(w2.y, b.y, w2.x * b.x), p3 = fmaf(w3.y, b.w, w3.x * b.z);
     return (p0 + p1) + (p2 + p3);
-}
-
-// 4 f16 (8 bytes) dotted with 4 f32.
-__device__ __forceinline__ float dot4h(uint2 w, float4 x) {
-    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
-    return a.x * x.x + a.y * x.y + b.x * x.z + b.y * x.w;
 }
 
 } // namespace navi::dev

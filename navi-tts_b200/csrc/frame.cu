@@ -38,13 +38,6 @@ using namespace navi::fk;
 
 namespace {
 
-uint64_t pcg_draw_seed(uint64_t seed, int frame_index, int codebook) {
-    const uint64_t tl = navi::dev::splitmix64(seed ^ (static_cast<uint64_t>(static_cast<int64_t>(frame_index)) * 0xA24BAED4963EE407ull));
-    if (codebook == 0) return tl;
-    const uint64_t cp = navi::dev::splitmix64(tl ^ 0x9FB21C651E98DF25ull);
-    return cp + static_cast<uint64_t>(codebook) * 0xD1B54A32D192ED03ull;
-}
-
 int cdiv(int a, int b) { return (a + b - 1) / b; }
 
 // cos[hd/2] then sin[hd/2] of RoPE at integer position pos: the angle is the f32 product
@@ -161,7 +154,7 @@ struct Frame::Impl {
         A.temp = s.temperature; A.top_p = s.top_p; A.rep = s.repetition_penalty; A.top_k = s.top_k;
         A.cp_temp = s.cp_temperature; A.cp_top_p = s.cp_top_p; A.cp_top_k = s.cp_top_k;
         A.min_frames = s.min_frames; A.rng = s.rng; A.seed = seed; A.frame_index = frame_index;
-        for (int cb = 0; cb < NCB; ++cb) A.pcg_seed[cb] = pcg_draw_seed(seed, frame_index, cb);
+        for (int cb = 0; cb < NCB; ++cb) A.pcg_seed[cb] = navi::dev::pcg_draw_seed(seed, frame_index, cb);
         A.eos_id = eos;
         A.suppress_from = suppress_from;
         A.timeout_ns = timeout_ns;
@@ -519,7 +512,7 @@ int Frame::sample(const Device & dev, const float * d_logits, int vocab, const S
         c.temperature = s.cp_temperature; c.top_k = s.cp_top_k; c.top_p = s.cp_top_p;
     }
     c.rng = s.rng; c.seed = seed; c.frame_index = frame_index; c.codebook = codebook;
-    c.pcg_seed = pcg_draw_seed(seed, frame_index, codebook);
+    c.pcg_seed = navi::dev::pcg_draw_seed(seed, frame_index, codebook);
     int * d_out = nullptr;
     NAVI_CUDA(cudaMallocAsync(reinterpret_cast<void **>(&d_out), sizeof(int), dev.stream()));
     const size_t smem = static_cast<size_t>(navi::dev::sample_scratch_floats(vocab)) * sizeof(float);

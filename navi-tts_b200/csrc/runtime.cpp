@@ -39,111 +39,153 @@ uint64_t TensorInfo::numel() const {
 }
 
 // ---- .navi reader ---------------------------------------------------------------------------------
+//
+// The file is mapped read-only once; the header is decoded straight from the mapping by a
+// cursor that knows where the header ends (data_offset) and names the field and the byte
+// offset of whatever does not fit. Byte layout: the reference's docs/navi-format.md:10-47.
 
 namespace {
-constexpr uint64_t PAGE = 4096;
 
-struct Reader {
-    const uint8_t * p;
-    const uint8_t * end;
-    const std::string & path;
-    template <class T> T get() {
-        if (static_cast<size_t>(end - p) < sizeof(T)) fail(path + ": truncated header", NAVI_E_FORMAT);
+constexpr uint64_t kPage = 4096;
+constexpr uint64_t kPreambleBytes = 32;
+constexpr uint32_t kFormatVersion = 1;
+
+class HeaderCursor {
+public:
+    HeaderCursor(const uint8_t * base, uint64_t end, const std::string & file) : base_(base), end_(end), file_(file) {}
+
+    void limit(uint64_t end) { end_ = end; }
+
+    template <class T> T scalar(const char * field) {
         T v;
-        std::memcpy(&v, p, sizeof(T));
-        p += sizeof(T);
+        std::memcpy(&v, span(sizeof(T), field), sizeof(T));
         return v;
     }
-    std::string str() {
-        const auto n = get<uint32_t>();
-        if (static_cast<size_t>(end - p) < n) fail(path + ": truncated header", NAVI_E_FORMAT);
-        std::string s(reinterpret_cast<const char *>(p), n);
-        p += n;
-        return s;
+    std::string text(const char * field) {
+        const auto n = scalar<uint32_t>(field);
+        const char * p = reinterpret_cast<const char *>(span(n, field));
+        return std::string(p, n);
     }
+
+private:
+    const uint8_t * span(uint64_t n, const char * field) {
+        if (n > end_ - at_)
+            fail(file_ + ": " + field + " at header byte " + std::to_string(at_) + " needs " + std::to_string(n) +
+                     " bytes, but the header ends at byte " + std::to_string(end_),
+                 NAVI_E_FORMAT);
+        const uint8_t * p = base_ + at_;
+        at_ += n;
+        return p;
+    }
+    const uint8_t * base_;
+    uint64_t end_, at_ = 0;
+    const std::string & file_;
 };
+
+KV decode_value(HeaderCursor & c, const std::string & file, const std::string & key) {
+    KV v;
+    const auto tag = c.scalar<uint8_t>("hyperparameter type");
+    switch (tag) {
+        case static_cast<uint8_t>(KV::Type::I64): v.i64 = c.scalar<int64_t>("integer value"); break;
+        case static_cast<uint8_t>(KV::Type::F64): v.f64 = c.scalar<double>("float value"); break;
+        case static_cast<uint8_t>(KV::Type::STR): v.str = c.text("string value"); break;
+        case static_cast<uint8_t>(KV::Type::I64_ARRAY): {
+            const auto n = c.scalar<uint32_t>("array length");
+            v.arr.resize(n);
+            for (auto & x : v.arr) x = c.scalar<int64_t>("array element");
+            break;
+        }
+        default:
+            fail(file + ": hyperparameter '" + key + "' has type code " + std::to_string(tag) + ", which version 1 does not define",
+                 NAVI_E_FORMAT);
+    }
+    v.type = static_cast<KV::Type>(tag);
+    return v;
+}
+
+TensorInfo decode_tensor(HeaderCursor & c, const std::string & file, uint64_t data_offset, uint64_t file_bytes) {
+    TensorInfo t;
+    t.name = c.text("tensor name");
+    const auto code = c.scalar<uint8_t>("tensor dtype");
+    t.dtype = static_cast<DType>(code);
+    if (code > static_cast<uint8_t>(DType::U8))
+        fail(file + ": tensor '" + t.name + "' has dtype code " + std::to_string(code) + ", which version 1 does not define", NAVI_E_FORMAT);
+    t.dims.resize(c.scalar<uint8_t>("tensor rank"));
+    for (auto & d : t.dims) d = c.scalar<uint64_t>("tensor dimension");
+    t.offset = c.scalar<uint64_t>("tensor offset");
+    t.nbytes = c.scalar<uint64_t>("tensor byte length");
+    const uint64_t room = file_bytes - data_offset;
+    if (t.offset % kPage != 0) fail(file + ": tensor '" + t.name + "' starts at data byte " + std::to_string(t.offset) + ", not on a page", NAVI_E_FORMAT);
+    if (t.offset > room || t.nbytes > room - t.offset)
+        fail(file + ": tensor '" + t.name + "' (data bytes " + std::to_string(t.offset) + " + " + std::to_string(t.nbytes) +
+                 ") runs past the end of the file",
+             NAVI_E_FORMAT);
+    if (t.numel() * dtype_size(t.dtype) != t.nbytes)
+        fail(file + ": tensor '" + t.name + "' has " + std::to_string(t.numel()) + " elements but " + std::to_string(t.nbytes) + " bytes",
+             NAVI_E_FORMAT);
+    return t;
+}
+
 } // namespace
+
+void FileUnmap::operator()(const uint8_t * p) const {
+    if (p) munmap(const_cast<uint8_t *>(p), bytes);
+}
 
 NaviFile NaviFile::open(const std::string & path) {
     NaviFile f;
     f.path_ = path;
-    f.fd_ = ::open(path.c_str(), O_RDONLY | O_CLOEXEC);
-    if (f.fd_ < 0) fail(path + ": " + std::strerror(errno), NAVI_E_FORMAT);
-    struct stat st {};
-    if (fstat(f.fd_, &st) != 0) fail(path + ": fstat failed", NAVI_E_FORMAT);
-    f.size_ = static_cast<uint64_t>(st.st_size);
-    if (f.size_ < 32) fail(path + ": not a .navi file (too small)", NAVI_E_FORMAT);
-    void * m = mmap(nullptr, f.size_, PROT_READ, MAP_PRIVATE, f.fd_, 0);
-    if (m == MAP_FAILED) fail(path + ": mmap failed", NAVI_E_FORMAT);
-    f.map_ = static_cast<const uint8_t *>(m);
-    (void) madvise(m, f.size_, MADV_SEQUENTIAL);
-    Reader r{f.map_, f.map_ + f.size_, path};
-    if (std::memcmp(r.p, "NAVI", 4) != 0) fail(path + ": bad magic; not a .navi file", NAVI_E_FORMAT);
-    r.p += 4;
-    const auto version = r.get<uint32_t>();
-    if (version != 1) fail(path + ": .navi version " + std::to_string(version) + " (this build reads 1)", NAVI_E_FORMAT);
-    f.data_offset_ = r.get<uint64_t>();
-    const auto n_kv = r.get<uint32_t>();
-    const auto n_t = r.get<uint32_t>();
-    const auto size = r.get<uint64_t>();
-    if (size != f.size_) fail(path + ": header says " + std::to_string(size) + " bytes, file has " + std::to_string(f.size_), NAVI_E_FORMAT);
-    if (f.data_offset_ % PAGE != 0 || f.data_offset_ > f.size_) fail(path + ": bad data_offset", NAVI_E_FORMAT);
-    r.end = f.map_ + f.data_offset_;
-    for (uint32_t i = 0; i < n_kv; ++i) {
-        std::string key = r.str();
-        KV v;
-        v.type = static_cast<KV::Type>(r.get<uint8_t>());
-        switch (v.type) {
-            case KV::Type::I64: v.i64 = r.get<int64_t>(); break;
-            case KV::Type::F64: v.f64 = r.get<double>(); break;
-            case KV::Type::STR: v.str = r.str(); break;
-            case KV::Type::I64_ARRAY: {
-                const auto n = r.get<uint32_t>();
-                for (uint32_t k = 0; k < n; ++k) v.arr.push_back(r.get<int64_t>());
-                break;
-            }
-            default: fail(path + ": kv '" + key + "' has an unknown type", NAVI_E_FORMAT);
+    {
+        const int fd = ::open(path.c_str(), O_RDONLY | O_CLOEXEC);
+        if (fd < 0) fail("cannot open " + path + ": " + std::strerror(errno), NAVI_E_FORMAT);
+        struct stat st {};
+        const bool sized = fstat(fd, &st) == 0;
+        f.size_ = sized ? static_cast<uint64_t>(st.st_size) : 0;
+        if (!sized || f.size_ < kPreambleBytes) {
+            ::close(fd);
+            fail(path + ": " + std::to_string(f.size_) + " bytes is shorter than a .navi preamble", NAVI_E_FORMAT);
         }
-        f.kv_.emplace(std::move(key), std::move(v));
+        // the upload reads every tensor front to back once
+        (void) posix_fadvise(fd, 0, 0, POSIX_FADV_SEQUENTIAL);
+        void * m = mmap(nullptr, f.size_, PROT_READ, MAP_PRIVATE, fd, 0);
+        ::close(fd);   // the mapping outlives the descriptor
+        if (m == MAP_FAILED) fail("cannot map " + path + ": " + std::strerror(errno), NAVI_E_FORMAT);
+        f.map_ = std::unique_ptr<const uint8_t, FileUnmap>(static_cast<const uint8_t *>(m), FileUnmap{f.size_});
     }
-    for (uint32_t i = 0; i < n_t; ++i) {
-        TensorInfo t;
-        t.name = r.str();
-        t.dtype = static_cast<DType>(r.get<uint8_t>());
-        if (dtype_size(t.dtype) == 0) fail(path + ": tensor '" + t.name + "' has an unknown dtype", NAVI_E_FORMAT);
-        const auto nd = r.get<uint8_t>();
-        for (uint8_t k = 0; k < nd; ++k) t.dims.push_back(r.get<uint64_t>());
-        t.offset = r.get<uint64_t>();
-        t.nbytes = r.get<uint64_t>();
-        if (t.offset % PAGE != 0 || f.data_offset_ + t.offset + t.nbytes > f.size_)
-            fail(path + ": tensor '" + t.name + "' lies outside the file", NAVI_E_FORMAT);
-        if (t.numel() * dtype_size(t.dtype) != t.nbytes) fail(path + ": tensor '" + t.name + "' shape/length mismatch", NAVI_E_FORMAT);
-        if (!f.index_.emplace(t.name, f.tensors_.size()).second) fail(path + ": duplicate tensor '" + t.name + "'", NAVI_E_FORMAT);
+    HeaderCursor c(f.map_.get(), kPreambleBytes, path);
+    const auto magic = c.scalar<uint32_t>("magic");
+    const auto version = c.scalar<uint32_t>("format version");
+    f.data_offset_ = c.scalar<uint64_t>("data offset");
+    const auto n_kv = c.scalar<uint32_t>("hyperparameter count");
+    const auto n_tensors = c.scalar<uint32_t>("tensor count");
+    const auto declared = c.scalar<uint64_t>("file size");
+    if (std::memcmp(&magic, "NAVI", 4) != 0) fail(path + ": the first four bytes are not 'NAVI'", NAVI_E_FORMAT);
+    if (version != kFormatVersion)
+        fail(path + ": format version " + std::to_string(version) + " is not supported (only version " + std::to_string(kFormatVersion) + ")",
+             NAVI_E_FORMAT);
+    if (declared != f.size_)
+        fail(path + ": the preamble records " + std::to_string(declared) + " bytes but the file holds " + std::to_string(f.size_) +
+                 " (truncated or appended to)",
+             NAVI_E_FORMAT);
+    if (f.data_offset_ % kPage != 0 || f.data_offset_ < kPreambleBytes || f.data_offset_ > f.size_)
+        fail(path + ": data offset " + std::to_string(f.data_offset_) + " is not a page boundary inside the file", NAVI_E_FORMAT);
+    c.limit(f.data_offset_);
+    for (uint32_t i = 0; i < n_kv; ++i) {
+        std::string key = c.text("hyperparameter key");
+        KV v = decode_value(c, path, key);
+        f.kv_.insert_or_assign(std::move(key), std::move(v));
+    }
+    f.tensors_.reserve(n_tensors);
+    for (uint32_t i = 0; i < n_tensors; ++i) {
+        TensorInfo t = decode_tensor(c, path, f.data_offset_, f.size_);
+        const auto [it, fresh] = f.index_.try_emplace(t.name, f.tensors_.size());
+        if (!fresh) fail(path + ": tensor '" + t.name + "' appears twice in the tensor table", NAVI_E_FORMAT);
         f.tensors_.push_back(std::move(t));
     }
     return f;
 }
 
-void NaviFile::close() {
-    if (map_) { munmap(const_cast<uint8_t *>(map_), size_); map_ = nullptr; }
-    if (fd_ >= 0) { ::close(fd_); fd_ = -1; }
-}
-NaviFile::~NaviFile() { close(); }
-NaviFile::NaviFile(NaviFile && o) noexcept
-    : path_(std::move(o.path_)), fd_(o.fd_), map_(o.map_), size_(o.size_), data_offset_(o.data_offset_),
-      kv_(std::move(o.kv_)), tensors_(std::move(o.tensors_)), index_(std::move(o.index_)) {
-    o.fd_ = -1;
-    o.map_ = nullptr;
-}
-NaviFile & NaviFile::operator=(NaviFile && o) noexcept {
-    if (this != &o) {
-        close();
-        path_ = std::move(o.path_); fd_ = o.fd_; map_ = o.map_; size_ = o.size_; data_offset_ = o.data_offset_;
-        kv_ = std::move(o.kv_); tensors_ = std::move(o.tensors_); index_ = std::move(o.index_);
-        o.fd_ = -1; o.map_ = nullptr;
-    }
-    return *this;
-}
+void NaviFile::close() { map_.reset(); }
 
 bool NaviFile::has_kv(std::string_view k) const { return kv_.count(std::string(k)) != 0; }
 static const KV & kv_at(const std::map<std::string, KV> & m, std::string_view k, const std::string & path) {
@@ -179,8 +221,8 @@ const TensorInfo * NaviFile::find(std::string_view name) const {
     return it == index_.end() ? nullptr : &tensors_[it->second];
 }
 const void * NaviFile::data(const TensorInfo & t) const {
-    if (!map_) fail(path_ + ": file already closed", NAVI_E_FORMAT);
-    return map_ + data_offset_ + t.offset;
+    if (!map_) fail(path_ + ": the mapping was released by close()", NAVI_E_FORMAT);
+    return map_.get() + data_offset_ + t.offset;
 }
 
 // ---- parameters ---------------------------------------------------------------------------------------
@@ -362,16 +404,23 @@ std::vector<ExpectedTensor> expected_tensors(const Params & p) {
 }
 
 Validation validate(const NaviFile & f, const Params & p) {
+    // expected name -> dims; each file tensor is checked against it and crossed off, and
+    // whatever is left over afterwards is missing
+    std::map<std::string, std::vector<uint64_t>> want;
+    for (ExpectedTensor & e : expected_tensors(p)) want.emplace(std::move(e.name), std::move(e.dims));
     Validation v;
-    std::set<std::string> seen;
-    for (const ExpectedTensor & e : expected_tensors(p)) {
-        seen.insert(e.name);
-        const TensorInfo * t = f.find(e.name);
-        if (!t) { v.missing.push_back(e.name); continue; }
-        if (t->dims != e.dims) v.shape_mismatch.push_back(e.name);
+    std::set<std::string> matched;
+    for (const TensorInfo & t : f.tensors()) {
+        const auto it = want.find(t.name);
+        if (it == want.end()) {
+            v.unused.push_back(t.name);
+            continue;
+        }
+        matched.insert(t.name);
+        if (it->second != t.dims) v.shape_mismatch.push_back(t.name);
     }
-    for (const TensorInfo & t : f.tensors())
-        if (!seen.count(t.name)) v.unused.push_back(t.name);
+    for (const auto & [name, dims] : want)
+        if (!matched.count(name)) v.missing.push_back(name);
     return v;
 }
 

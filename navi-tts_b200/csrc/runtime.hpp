@@ -11,6 +11,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <map>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <string_view>
@@ -49,12 +50,19 @@ struct KV {
     std::vector<int64_t> arr;
 };
 
+// Releases a read-only file mapping of `bytes` bytes.
+struct FileUnmap {
+    uint64_t bytes = 0;
+    void operator()(const uint8_t * p) const;
+};
+
+// A mapped .navi file: the hyperparameters and the tensor table are decoded at open; tensor
+// payloads are read in place from the read-only mapping until close() or destruction.
 class NaviFile {
 public:
     static NaviFile open(const std::string & path);
-    ~NaviFile();
-    NaviFile(NaviFile &&) noexcept;
-    NaviFile & operator=(NaviFile &&) noexcept;
+    NaviFile(NaviFile &&) noexcept = default;
+    NaviFile & operator=(NaviFile &&) noexcept = default;
     NaviFile(const NaviFile &) = delete;
 
     const std::string & path() const { return path_; }
@@ -74,8 +82,7 @@ public:
 private:
     NaviFile() = default;
     std::string path_;
-    int fd_ = -1;
-    const uint8_t * map_ = nullptr;
+    std::unique_ptr<const uint8_t, FileUnmap> map_;
     uint64_t size_ = 0, data_offset_ = 0;
     std::map<std::string, KV> kv_;
     std::vector<TensorInfo> tensors_;

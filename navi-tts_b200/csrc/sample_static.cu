@@ -61,13 +61,6 @@ constexpr int MAX_DEVICES = 64;
 std::mutex g_lock[MAX_DEVICES];
 unsigned char * g_addr[MAX_DEVICES] = {};
 
-// The per-draw PCG seed of the sampler's stream (the same chain the frame kernel uses).
-uint64_t draw_seed(uint64_t seed, int frame_index, int codebook) {
-    const uint64_t tl = navi::dev::splitmix64(seed ^ (static_cast<uint64_t>(static_cast<int64_t>(frame_index)) * 0xA24BAED4963EE407ull));
-    if (codebook == 0) return tl;
-    return navi::dev::splitmix64(tl ^ 0x9FB21C651E98DF25ull) + static_cast<uint64_t>(codebook) * 0xD1B54A32D192ED03ull;
-}
-
 // Device address of the scratch array; the caller holds g_lock[ordinal] and has made the
 // device current.
 unsigned char * scratch_of(int ordinal) {
@@ -101,7 +94,7 @@ int sample_static(const Device & dev, const float * d_logits, int vocab, const S
         c.temperature = s.cp_temperature; c.top_k = s.cp_top_k; c.top_p = s.cp_top_p;
     }
     c.rng = s.rng; c.seed = seed; c.frame_index = frame_index; c.codebook = codebook;
-    c.pcg_seed = draw_seed(seed, frame_index, codebook);
+    c.pcg_seed = navi::dev::pcg_draw_seed(seed, frame_index, codebook);
 
     std::lock_guard<std::mutex> hold(g_lock[ordinal]);
     dev.make_current();

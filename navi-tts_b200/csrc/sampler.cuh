@@ -97,6 +97,16 @@ __host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
     return x ^ (x >> 31);
 }
 
+// The per-draw PCG seed (frame.hip:581-586, 658-659, 497): the talker's stream is
+// splitmix64(seed ^ frame * 0xA24BAED4963EE407); codebook c >= 1 of the code predictor uses
+// splitmix64(talker ^ 0x9FB21C651E98DF25) + c * 0xD1B54A32D192ED03. The frame launch and the
+// standalone samplers all derive their seeds here.
+__host__ __device__ __forceinline__ uint64_t pcg_draw_seed(uint64_t seed, int frame_index, int codebook) {
+    const uint64_t tl = splitmix64(seed ^ (static_cast<uint64_t>(static_cast<int64_t>(frame_index)) * 0xA24BAED4963EE407ull));
+    if (codebook == 0) return tl;
+    return splitmix64(tl ^ 0x9FB21C651E98DF25ull) + static_cast<uint64_t>(codebook) * 0xD1B54A32D192ED03ull;
+}
+
 __device__ __forceinline__ uint32_t pcg32_next(uint64_t & s) {
     const uint64_t old = s;
     s = old * 6364136223846793005ull + 1442695040888963407ull;

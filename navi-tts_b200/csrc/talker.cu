@@ -442,6 +442,7 @@ void Talker::prefill(const Prompt & pr) {
     NAVI_CUDA(cudaMemcpy(&err, I.ws.err, sizeof(int), cudaMemcpyDeviceToHost));
     if (err) {
         NAVI_CUDA(cudaMemset(I.ws.err, 0, sizeof(int)));
+        if (err == conv::ERR_ALIGN) fail("talker: a tensor-core GEMM's weight ring is misaligned for swizzled tiles", NAVI_E_SHAPE);
         fail("talker: a tensor-core GEMM wait passed its deadline", NAVI_E_TIMEOUT);
     }
     I.kv.n_used = T;

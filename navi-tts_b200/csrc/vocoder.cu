@@ -776,9 +776,10 @@ void Vocoder::decode_into(std::span<const std::int32_t> codes, int n_frames, flo
         NAVI_CUDA(cudaMemcpyAsync(I.h_pcm, I.pcm, ns * sizeof(float), cudaMemcpyDeviceToHost, I.stream));
         NAVI_CUDA(cudaMemcpyAsync(I.h_err, I.ws.err, sizeof(int), cudaMemcpyDeviceToHost, I.stream));
         NAVI_CUDA(cudaStreamSynchronize(I.stream));
-        if (*I.h_err) {
+        if (const int e = *I.h_err) {
             NAVI_CUDA(cudaMemsetAsync(I.ws.err, 0, sizeof(int), I.stream));
             NAVI_CUDA(cudaStreamSynchronize(I.stream));
+            if (e == conv::ERR_ALIGN) fail("vocoder: a tensor-core conv's weight ring is misaligned for swizzled tiles", NAVI_E_SHAPE);
             fail("vocoder: a tensor-core conv wait passed its deadline", NAVI_E_TIMEOUT);
         }
         std::memcpy(out + static_cast<std::size_t>(f0) * I.spf, I.h_pcm, ns * sizeof(float));

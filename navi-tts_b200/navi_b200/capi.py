@@ -93,6 +93,7 @@ SIGNATURES = [
     ("navi_device_close", None, [c_void_p]),
     ("navi_weights_upload", c_int, [c_void_p, c_char_p, POINTER(c_void_p)]),
     ("navi_weights_get_params", c_int, [c_void_p, POINTER(Params)]),
+    ("navi_model_probe", c_int, [c_char_p, POINTER(Params), POINTER(c_int), POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
     ("navi_weights_tensor", c_void_p, [c_void_p, c_char_p, POINTER(c_int), POINTER(c_int), POINTER(c_uint64)]),
     ("navi_weights_bytes", c_uint64, [c_void_p]),
     ("navi_weights_free", None, [c_void_p]),

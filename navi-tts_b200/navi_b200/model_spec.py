@@ -23,7 +23,7 @@ from pathlib import Path
 
 import numpy as np
 
-from .navi_file import F16, F32, U8, NaviWriter
+from .navi_file import F16, F32, U8, NaviBuilder
 
 
 @dataclass(frozen=True)
@@ -121,62 +121,62 @@ def small_config() -> ModelConfig:
 
 # --- KV section -----------------------------------------------------------------------
 
-def _transformer_kv(w: NaviWriter, ns: str, t: Transformer) -> None:
-    w.add_kv(f"{ns}.hidden_size", t.hidden)
-    w.add_kv(f"{ns}.num_hidden_layers", t.n_layer)
-    w.add_kv(f"{ns}.num_attention_heads", t.n_head)
-    w.add_kv(f"{ns}.num_key_value_heads", t.n_kv_head)
-    w.add_kv(f"{ns}.head_dim", t.head_dim)
-    w.add_kv(f"{ns}.intermediate_size", t.ff)
-    w.add_kv(f"{ns}.rms_norm_eps", float(t.eps))
-    w.add_kv(f"{ns}.rope_theta", float(t.rope_theta))
+def _transformer_kv(w: NaviBuilder, ns: str, t: Transformer) -> None:
+    w.set_kv(f"{ns}.hidden_size", t.hidden)
+    w.set_kv(f"{ns}.num_hidden_layers", t.n_layer)
+    w.set_kv(f"{ns}.num_attention_heads", t.n_head)
+    w.set_kv(f"{ns}.num_key_value_heads", t.n_kv_head)
+    w.set_kv(f"{ns}.head_dim", t.head_dim)
+    w.set_kv(f"{ns}.intermediate_size", t.ff)
+    w.set_kv(f"{ns}.rms_norm_eps", float(t.eps))
+    w.set_kv(f"{ns}.rope_theta", float(t.rope_theta))
     if t.vocab:
-        w.add_kv(f"{ns}.vocab_size", t.vocab)
-    w.add_kv(f"{ns}.max_position_embeddings", t.max_pos)
+        w.set_kv(f"{ns}.vocab_size", t.vocab)
+    w.set_kv(f"{ns}.max_position_embeddings", t.max_pos)
 
 
-def kv_entries(w: NaviWriter, c: ModelConfig) -> None:
-    w.add_kv("general.arch", "qwen3-tts")
-    w.add_kv("general.name", c.name)
-    w.add_kv("general.dtype", "f16")
-    w.add_kv("general.codec_dtype", "f16")
-    w.add_kv("general.converter", "navi-b200 synthetic (random-init, seeded)")
-    w.add_kv("general.has_codec_encoder", 0)
+def kv_entries(w: NaviBuilder, c: ModelConfig) -> None:
+    w.set_kv("general.arch", "qwen3-tts")
+    w.set_kv("general.name", c.name)
+    w.set_kv("general.dtype", "f16")
+    w.set_kv("general.codec_dtype", "f16")
+    w.set_kv("general.converter", "navi-b200 synthetic (random-init, seeded)")
+    w.set_kv("general.has_codec_encoder", 0)
     for k in ("im_start_id", "im_end_id", "assistant_id", "tts_bos_id", "tts_eos_id", "tts_pad_id"):
-        w.add_kv("text." + k, getattr(c, k))
+        w.set_kv("text." + k, getattr(c, k))
     _transformer_kv(w, "talker", c.talker)
-    w.add_kv("talker.text_hidden_size", c.text_hidden)
-    w.add_kv("talker.text_vocab_size", c.text_vocab)
-    w.add_kv("talker.num_code_groups", c.n_code_groups)
-    w.add_kv("talker.position_id_per_seconds", 13)
+    w.set_kv("talker.text_hidden_size", c.text_hidden)
+    w.set_kv("talker.text_vocab_size", c.text_vocab)
+    w.set_kv("talker.num_code_groups", c.n_code_groups)
+    w.set_kv("talker.position_id_per_seconds", 13)
     for k, key in (("codec_bos_id", "codec_bos_id"), ("codec_eos_id", "codec_eos_token_id"),
                    ("codec_pad_id", "codec_pad_id"), ("codec_think_id", "codec_think_id"),
                    ("codec_nothink_id", "codec_nothink_id"), ("codec_think_bos_id", "codec_think_bos_id"),
                    ("codec_think_eos_id", "codec_think_eos_id")):
-        w.add_kv("talker." + key, getattr(c, k))
-    w.add_kv("talker.mrope_section", [24, 20, 20])
-    w.add_kv("talker.mrope_interleaved", 1)
+        w.set_kv("talker." + key, getattr(c, k))
+    w.set_kv("talker.mrope_section", [24, 20, 20])
+    w.set_kv("talker.mrope_interleaved", 1)
     for name, lid in c.languages:
-        w.add_kv(f"talker.language.{name}", lid)
+        w.set_kv(f"talker.language.{name}", lid)
     _transformer_kv(w, "cp", c.cp)
-    w.add_kv("cp.num_code_groups", c.n_code_groups)
-    w.add_kv("speaker.enc_dim", c.spk_dim)
-    w.add_kv("speaker.sample_rate", c.sample_rate)
+    w.set_kv("cp.num_code_groups", c.n_code_groups)
+    w.set_kv("speaker.enc_dim", c.spk_dim)
+    w.set_kv("speaker.sample_rate", c.sample_rate)
     for k, v in dict(n_fft=1024, num_mels=128, hop_size=256, win_size=1024, fmin=0, fmax=12000).items():
-        w.add_kv(f"speaker.mel.{k}", v)
-    w.add_kv("codec.input_sample_rate", c.sample_rate)
-    w.add_kv("codec.output_sample_rate", c.sample_rate)
-    w.add_kv("codec.decode_upsample_rate", c.samples_per_frame)
-    w.add_kv("codec.encode_downsample_rate", c.samples_per_frame)
+        w.set_kv(f"speaker.mel.{k}", v)
+    w.set_kv("codec.input_sample_rate", c.sample_rate)
+    w.set_kv("codec.output_sample_rate", c.sample_rate)
+    w.set_kv("codec.decode_upsample_rate", c.samples_per_frame)
+    w.set_kv("codec.encode_downsample_rate", c.samples_per_frame)
     _transformer_kv(w, "codec.decoder", c.vocoder)
     for k, v in dict(latent_dim=c.vq_latent, codebook_dim=c.vq_codebook_dim, codebook_size=c.vq_codebook_size,
                      decoder_dim=c.decoder_dim, num_quantizers=c.vq_n_q,
                      num_semantic_quantizers=c.vq_n_semantic, sliding_window=c.sliding_window).items():
-        w.add_kv(f"codec.decoder.{k}", v)
-    w.add_kv("codec.decoder.upsample_rates", list(c.upsample_rates))
-    w.add_kv("codec.decoder.upsampling_ratios", list(c.upsampling_ratios))
+        w.set_kv(f"codec.decoder.{k}", v)
+    w.set_kv("codec.decoder.upsample_rates", list(c.upsample_rates))
+    w.set_kv("codec.decoder.upsampling_ratios", list(c.upsampling_ratios))
     for k, v in c.gen.items():
-        w.add_kv(f"gen.{k}", v)
+        w.set_kv(f"gen.{k}", v)
 
 
 # --- tensor table ---------------------------------------------------------------------
@@ -324,17 +324,17 @@ def write_synthetic(path: str | Path, c: ModelConfig, seed_offset: int = 0, thre
                     include: callable = None) -> int:
     """Writes a complete `.navi` for config `c` with seeded random weights.
     `include(name)` can drop tensors (they are then absent from the table)."""
-    w = NaviWriter()
+    w = NaviBuilder()
     kv_entries(w, c)
     # tokenizer files: absent from this build's scope, written as placeholders so the table validates
     for tname in ("tokenizer.vocab.json", "tokenizer.merges.txt", "tokenizer.config.json"):
-        w.add_tensor(tname, U8, np.frombuffer(b"{}", dtype=np.uint8))
+        w.put_tensor(tname, U8, np.frombuffer(b"{}", dtype=np.uint8))
     table = [(n, s) for n, s in tensor_table(c) if include is None or include(n)]
     with ThreadPoolExecutor(max_workers=threads) as ex:
         arrays = [synth_tensor(n, s, seed_offset, ex) for n, s in table]
     for (name, shape), arr in zip(table, arrays):
-        w.add_tensor(name, F16 if len(shape) >= 2 else F32, arr)
-    return w.write(path)
+        w.put_tensor(name, F16 if len(shape) >= 2 else F32, arr)
+    return w.save(path)
 
 
 def load_weights(path: str | Path) -> dict:

@@ -2,7 +2,7 @@
 
 The byte layout is the drop-in boundary with the reference engine, so it is
 kept identical to what the reference reads (runtime/weights/navi_file.cpp:79-148,
-docs/navi-format.md:10-47) and what its converter writes (tools/convert.py:77-148):
+docs/navi-format.md:10-47) and what its converter writes (tools/convert.py:106-148):
 
     0   4   magic "NAVI"
     4   u32 version (1)
@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import os
 import struct
+import tempfile
 from dataclasses import dataclass, field
 from pathlib import Path
 from typing import Iterable
@@ -38,90 +39,104 @@ _NP = {F32: np.float32, F16: np.float16, I32: np.int32, U8: np.uint8}
 _SIZE = {F32: 4, F16: 2, BF16: 2, I32: 4, U8: 1}
 
 
-def _pstr(s: str) -> bytes:
-    b = s.encode("utf-8")
-    return struct.pack("<I", len(b)) + b
-
-
 def _round_page(n: int) -> int:
-    return (n + PAGE - 1) // PAGE * PAGE
+    return -(-n // PAGE) * PAGE
 
 
-class NaviWriter:
-    """Accumulates KV entries and tensors, then writes one `.navi` file.
+def _encode_str(s: str) -> bytes:
+    raw = s.encode("utf-8")
+    return len(raw).to_bytes(4, "little") + raw
 
-    Tensors are appended in insertion order; the reader and the device upload
-    keep that order (plus adjacency groups), so callers that want two tensors
-    adjacent on the device add them consecutively.
+
+def _classify(value):
+    """(kind, normalised value) of a hyperparameter, or None when the value is absent."""
+    if value is None:
+        return None
+    if isinstance(value, (bool, int, np.integer)):
+        return KV_I64, int(value)
+    if isinstance(value, (float, np.floating)):
+        return KV_F64, float(value)
+    if isinstance(value, str):
+        return KV_STR, value
+    if isinstance(value, (list, tuple)):
+        items = list(value)
+        if all(isinstance(v, (bool, int, np.integer)) for v in items):
+            return KV_I64_ARRAY, [int(v) for v in items]
+    raise TypeError(f"a .navi hyperparameter holds an integer, a float, a string or a list of integers, "
+                    f"not {type(value).__name__}")
+
+
+_KV_BODY = {
+    KV_I64: lambda v: struct.pack("<q", v),
+    KV_F64: lambda v: struct.pack("<d", v),
+    KV_STR: _encode_str,
+    KV_I64_ARRAY: lambda v: struct.pack(f"<I{len(v)}q", len(v), *v),
+}
+
+
+class NaviBuilder:
+    """Builds one `.navi` file: hyperparameters first, then tensors, laid out in one pass.
+
+    Tensors keep the order they were put in; the reader and the device upload keep it too
+    (plus the adjacency groups), so tensors wanted side by side on the device are put in
+    one after the other.  `save` writes a temporary file beside the target and renames it
+    into place, so a reader never sees a half-written file.
     """
 
     def __init__(self) -> None:
-        self.kv: list[tuple[str, int, object]] = []
-        self.tensors: list[tuple[str, int, tuple[int, ...], np.ndarray]] = []
-        self._names: set[str] = set()
+        self._hparams: dict[str, tuple[int, object]] = {}
+        self._payloads: dict[str, tuple[int, np.ndarray]] = {}
 
-    def add_kv(self, key: str, value) -> None:
-        if value is None:
-            return
-        if isinstance(value, bool):
-            value = int(value)
-        if isinstance(value, (int, np.integer)):
-            self.kv.append((key, KV_I64, int(value)))
-        elif isinstance(value, (float, np.floating)):
-            self.kv.append((key, KV_F64, float(value)))
-        elif isinstance(value, str):
-            self.kv.append((key, KV_STR, value))
-        elif isinstance(value, (list, tuple)) and all(isinstance(v, (int, np.integer)) for v in value):
-            self.kv.append((key, KV_I64_ARRAY, [int(v) for v in value]))
-        else:
-            raise TypeError(f"{key}: a .navi KV cannot hold {type(value).__name__}")
+    def set_kv(self, key: str, value) -> None:
+        """Records a hyperparameter (None: skipped; a key set twice keeps the last value)."""
+        typed = _classify(value)
+        if typed is not None:
+            self._hparams[key] = typed
 
-    def add_tensor(self, name: str, dtype: int, arr: np.ndarray) -> None:
-        if name in self._names:
-            raise ValueError(f"duplicate tensor {name}")
-        self._names.add(name)
-        arr = np.ascontiguousarray(np.asarray(arr).astype(_NP[dtype], copy=False))
-        self.tensors.append((name, dtype, tuple(int(d) for d in arr.shape), arr))
+    def put_tensor(self, name: str, dtype: int, arr) -> None:
+        if name in self._payloads:
+            raise ValueError(f"tensor {name!r} is already in this file")
+        data = np.ascontiguousarray(np.asarray(arr), dtype=_NP[dtype])
+        self._payloads[name] = (dtype, data)
 
-    def write(self, path: str | os.PathLike) -> int:
-        path = Path(path)
-        offsets, off = [], 0
-        for _, _, _, arr in self.tensors:
-            offsets.append(off)
-            off += _round_page(arr.nbytes)
-        table = bytearray()
-        for key, kind, v in self.kv:
-            table += _pstr(key) + struct.pack("<B", kind)
-            if kind == KV_I64:
-                table += struct.pack("<q", v)
-            elif kind == KV_F64:
-                table += struct.pack("<d", v)
-            elif kind == KV_STR:
-                table += _pstr(v)
-            else:
-                table += struct.pack("<I", len(v)) + b"".join(struct.pack("<q", x) for x in v)
-        for (name, dtype, shape, arr), o in zip(self.tensors, offsets):
-            table += _pstr(name) + struct.pack("<BB", dtype, len(shape))
-            table += b"".join(struct.pack("<Q", d) for d in shape)
-            table += struct.pack("<QQ", o, arr.nbytes)
-        header_len = 32 + len(table)
-        data_offset = _round_page(header_len)
-        size = data_offset + off
-        head = b"NAVI" + struct.pack("<IQIIQ", VERSION, data_offset, len(self.kv), len(self.tensors), size)
-        tmp = path.with_name(path.name + ".tmp")
-        with open(tmp, "wb") as f:
-            f.write(head)
-            f.write(table)
-            f.write(b"\0" * (data_offset - header_len))
-            for (name, _, _, arr), o in zip(self.tensors, offsets):
-                assert f.tell() == data_offset + o, name
-                f.write(arr.tobytes())
-                pad = _round_page(arr.nbytes) - arr.nbytes
-                if pad:
-                    f.write(b"\0" * pad)
-            assert f.tell() == size
-        os.replace(tmp, path)
-        return size
+    def _layout(self) -> tuple[bytes, list[int], int]:
+        """The header bytes (page-padded), each payload's offset from the data region, and
+        the file size."""
+        offsets, cursor = [], 0
+        for _, data in self._payloads.values():
+            offsets.append(cursor)
+            cursor += _round_page(data.nbytes)
+        parts = []
+        for key, (kind, value) in self._hparams.items():
+            parts += [_encode_str(key), bytes([kind]), _KV_BODY[kind](value)]
+        for (name, (dtype, data)), off in zip(self._payloads.items(), offsets):
+            parts += [_encode_str(name), bytes([dtype, data.ndim]), struct.pack(f"<{data.ndim}Q", *data.shape),
+                      struct.pack("<QQ", off, data.nbytes)]
+        tables = b"".join(parts)
+        data_offset = _round_page(32 + len(tables))
+        total = data_offset + cursor
+        preamble = b"NAVI" + struct.pack("<IQIIQ", VERSION, data_offset, len(self._hparams), len(self._payloads), total)
+        header = (preamble + tables).ljust(data_offset, b"\0")
+        return header, offsets, total
+
+    def save(self, path: str | os.PathLike) -> int:
+        """Writes the file; returns its size in bytes."""
+        header, offsets, total = self._layout()
+        target = Path(path)
+        fd, tmp = tempfile.mkstemp(prefix=target.name + ".", suffix=".partial", dir=target.parent)
+        try:
+            with os.fdopen(fd, "wb") as out:
+                out.write(header)
+                for (_, data), off in zip(self._payloads.values(), offsets):
+                    out.seek(len(header) + off)          # the gap to the page boundary reads as zeros
+                    out.write(memoryview(data).cast("B"))
+                out.truncate(total)
+            os.replace(tmp, target)
+        except BaseException:
+            if os.path.exists(tmp):
+                os.unlink(tmp)
+            raise
+        return total
 
 
 @dataclass

@@ -1,6 +1,6 @@
 """Parity of the B200 frame path with the CPU oracle, through the C ABI.
 
-Gates: sampled codes bit-exact given identical logits (the
+Gates (the north star's): sampled codes bit-exact given identical logits (the
 GPU's own logits fed to the oracle sampler); talker hidden / codec logits and
 code-predictor logits within rel-L2 1e-2 of the fp32 oracle on the same weights
 and inputs (observed ~1e-5); plus the reference's own frame gates

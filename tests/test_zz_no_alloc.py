@@ -3,14 +3,17 @@ navi_sample_logits on the same device logits, through the C ABI.
 
 Each case makes two calls in a row of the static entry point, so the second one runs on
 scratch left over from the first; both must return the id navi_sample_logits returns
-(sampled ids are integers: the tolerance is equality).  The file name sorts last so the
-module also runs after every other test in one process; it passes on its own as well.
+(sampled ids are integers: the tolerance is equality).  Above the vocabulary the allocating
+entry point stages in shared memory, the static one is checked against the C oracle
+sampler instead, bit for bit.  The file name sorts last so the module also runs after every
+other test in one process; it passes on its own as well.
 """
 import numpy as np
 import pytest
 import torch
 
 from navi_b200 import capi, engine
+from oracle import model as om
 
 pytestmark = pytest.mark.gpu
 
@@ -67,3 +70,24 @@ def test_static_rejects_vocab_beyond_limit(dev):
         engine.sample_logits_static(dev, d.data_ptr(), V, engine.Sampling(), 1, 0, 1)
     assert e.value.status == capi.NAVI_E_ARG
     assert "32768" in str(e.value)
+
+
+@pytest.mark.parametrize("vocab", [20011, capi.NAVI_SAMPLE_STATIC_MAX_VOCAB])
+@pytest.mark.parametrize("rng", [capi.NAVI_RNG_PCG, capi.NAVI_RNG_PHILOX])
+def test_static_sampled_at_large_vocab_matches_oracle(dev, vocab, rng):
+    """Top-k 50 / top-p 0.9 / T 0.9 draws (the radix select over global scratch) at a
+    vocabulary near 20,000 and at the limit, against the C oracle on the same logits; two
+    calls in a row each time, and no device memory taken by either."""
+    x = (np.random.default_rng(vocab + rng).standard_normal(vocab) * 3).astype(np.float32)
+    d = torch.from_numpy(x).cuda()
+    s = engine.Sampling(cp_temperature=0.9, cp_top_k=50, cp_top_p=0.9, rng=rng)
+    os_ = om.Sampling(cp_temperature=0.9, cp_top_k=50, cp_top_p=0.9, rng=rng)
+    engine.sample_logits_static(dev, d.data_ptr(), vocab, s, 1, 0, 1)   # set-up call (symbol address)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for seed, fi, cb in ((11, 0, 1), (12, 7, 9), (13, 199, 15)):
+        want = om.sample(x, cb, os_, seed, fi)
+        got1 = engine.sample_logits_static(dev, d.data_ptr(), vocab, s, seed, fi, cb)
+        got2 = engine.sample_logits_static(dev, d.data_ptr(), vocab, s, seed, fi, cb)
+        assert got1 == want and got2 == want, (vocab, rng, seed, got1, got2, want)
+    assert torch.cuda.mem_get_info()[0] == free0
