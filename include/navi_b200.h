@@ -139,7 +139,8 @@ typedef struct navi_prompt {        /* Prompt, talker.h:26-32: device rows, vali
 } navi_prompt;
 
 /* Talker::create (talker.hip:200-266): the prompt / prefill scratch and the talker's KV
- * cache (max_positions per layer). max_prompt_tokens <= 1024. */
+ * cache (max_positions per layer). 9 <= max_prompt_tokens <= max_positions; the prefill
+ * attention has no key cap of its own. */
 int navi_talker_create(navi_device * dev, const navi_weights * w, int max_prompt_tokens, int max_positions, navi_talker ** out);
 /* Talker::build_prompt (talker.hip:283-352): ids = the tokenised
  * "<|im_start|>assistant\n{text}<|im_end|>\n<|im_start|>assistant\n" (3 header ids, the
@@ -195,6 +196,14 @@ int navi_frame_run_first(navi_frame * f, const float * d_hidden, const float * d
 /* Frame::run (frame.hip:798-810): talker step at n_past on the previous frame's step embedding. */
 int navi_frame_run(navi_frame * f, navi_kv * kv, int n_past, const float * d_trailing, const navi_sampling * s,
                    uint64_t seed, int frame_index, navi_frame_result * r);
+/* One talker decoder layer alone at position n_past: the layer phases of k_frame
+ * (frame.hip:300-402: RMSNorm, q/k/v, q/k norm + RoPE, K/V row n_past stored, GQA
+ * attention over positions 0..n_past, o + residual, RMSNorm, gate/up SwiGLU, down +
+ * residual) on the f32 input d_x [hidden], the f32 output written to d_out [hidden]
+ * (configs[0]'s single-layer step; the reference has no separate entry point for it).
+ * r->us is the launch's device time; r->codes are not set. */
+int navi_frame_run_layer(navi_frame * f, int layer, const float * d_x, navi_kv * kv, int n_past, float * d_out,
+                         navi_frame_result * r);
 /* Enqueue-only form of navi_frame_run (no host synchronisation, no result): for
  * pipelined loops; navi_frame_collect() then returns the last enqueued frame's result. */
 int navi_frame_enqueue(navi_frame * f, navi_kv * kv, int n_past, const float * d_trailing, const navi_sampling * s,

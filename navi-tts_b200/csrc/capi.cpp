@@ -310,6 +310,16 @@ int navi_frame_run(navi_frame * f, navi_kv * kv, int n_past, const float * d_tra
     });
 }
 
+int navi_frame_run_layer(navi_frame * f, int layer, const float * d_x, navi_kv * kv, int n_past, float * d_out, navi_frame_result * r) {
+    return guard([&]() -> int {
+        if (!f || !kv || !d_x || !d_out) return set_err(NAVI_E_ARG, "NULL argument");
+        auto k = as_kv(kv);
+        const auto res = f->f->run_layer(layer, d_x, k, n_past, d_out);
+        to_result(res, r);
+        return res.ok ? NAVI_OK : set_err(res.status, res.error);
+    });
+}
+
 int navi_frame_enqueue(navi_frame * f, navi_kv * kv, int n_past, const float * d_trailing, const navi_sampling * s, uint64_t seed,
                        int frame_index) {
     return guard([&]() -> int {

@@ -185,6 +185,14 @@ __device__ __forceinline__ void st_relaxed_u32(unsigned * p, uint32_t v) {
     asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// ---- cp.async (16-byte, L2-only) ----------------------------------------------------------------
+
+__device__ __forceinline__ void cp_async16(void * smem_dst, const void * gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // ---- f16 helpers ---------------------------------------------------------------------------------
 
 __device__ __forceinline__ float f16_round(float v) { return __half2float(__float2half_rn(v)); }

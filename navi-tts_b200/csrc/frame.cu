@@ -61,6 +61,7 @@ struct Frame::Impl {
     __half * wslices = nullptr;   // the frame's copy of its weight matrices in per-CTA slice layout
     Phase * prog_full = nullptr;
     Phase * prog_first = nullptr;
+    Phase * prog_layers = nullptr;   // [TL][LAYER_PHASES]: one talker layer alone, then XOUT
     int n_full = 0, n_first = 0;
     Work w{};
     float * inv_t = nullptr, * inv_c = nullptr;
@@ -103,13 +104,17 @@ struct Frame::Impl {
         split = std::max(1, cdiv(n_past, chunk));
     }
 
+    static constexpr int LAYER_PHASES = 6;
+
+    // layer >= 0: the single-layer program of that talker layer, from step_in into layer_out
     int launch(const float * step_in, const float * hidden_in, const float * logits_in, const float * trailing, KvCache * kv,
-               int n_past, const Sampling & s, uint64_t seed, int frame_index, std::string & err) {
+               int n_past, const Sampling & s, uint64_t seed, int frame_index, std::string & err, int layer = -1,
+               float * layer_out = nullptr) {
         NAVI_CUDA(cudaSetDevice(ordinal));
         Args A{};
         const bool first = hidden_in != nullptr;
-        A.prog = first ? prog_first : prog_full;
-        A.nphase = first ? n_first : n_full;
+        A.prog = layer >= 0 ? prog_layers + static_cast<size_t>(layer) * LAYER_PHASES : first ? prog_first : prog_full;
+        A.nphase = layer >= 0 ? LAYER_PHASES : first ? n_first : n_full;
         A.mw = dmw;
         A.d = d;
         A.w = w;
@@ -140,7 +145,7 @@ struct Frame::Impl {
         A.logits_in = logits_in;
         A.trailing = trailing;
         const int out = cur ^ 1;
-        A.step_out = step[out];
+        A.step_out = layer >= 0 ? layer_out : step[out];
         if (kv) {
             for (int l = 0; l < d.TL; ++l) {
                 A.kc[l] = reinterpret_cast<__half *>(kv->k[l]);
@@ -177,7 +182,7 @@ struct Frame::Impl {
         NAVI_CUDA(cudaEventRecord(ev1, stream));
         NAVI_CUDA(cudaMemcpyAsync(h_out, w.codes, NCB * sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
         NAVI_CUDA(cudaMemcpyAsync(h_out + NCB, w.ctl, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
-        cur = out;
+        if (layer < 0) cur = out;
         last_tag = tag;
         pending = true;
         return NAVI_OK;
@@ -311,6 +316,14 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
         return v;
     };
     const auto pf = build(true), p0 = build(false);
+    std::vector<Phase> pl;
+    for (int l = 0; l < d.TL; ++l) {
+        pl.push_back({TQKV, 1, static_cast<uint8_t>(l), POS_STEP_IN});
+        for (uint8_t op : {TATTN, TO, TGU, TDOWN}) pl.push_back({op, 1, static_cast<uint8_t>(l), 0});
+        pl.push_back({XOUT, 1, static_cast<uint8_t>(l), 0});
+    }
+    I.prog_layers = I.alloc<Phase>(pl.size());
+    NAVI_CUDA(cudaMemcpy(I.prog_layers, pl.data(), pl.size() * sizeof(Phase), cudaMemcpyHostToDevice));
     I.n_full = static_cast<int>(pf.size());
     I.n_first = static_cast<int>(p0.size());
     if (I.n_full >= 4096) fail("frame: phase program too long", NAVI_E_SHAPE);
@@ -441,6 +454,19 @@ FrameResult Frame::run(KvCache & kv, int n_past, const float * d_trailing, const
     const int st = enqueue(kv, n_past, d_trailing, s, seed, frame_index, err);
     if (st != NAVI_OK) { FrameResult r; r.status = st; r.error = err; return r; }
     return impl_->collect();
+}
+
+FrameResult Frame::run_layer(int layer, const float * d_x, KvCache & kv, int n_past, float * d_out) {
+    Impl & I = *impl_;
+    FrameResult r;
+    if (layer < 0 || layer >= I.d.TL) { r.status = NAVI_E_ARG; r.error = "layer " + std::to_string(layer) + " out of range"; return r; }
+    if (!d_x || !d_out) { r.status = NAVI_E_ARG; r.error = "NULL input or output"; return r; }
+    if (n_past < 0 || n_past >= kv.max_pos) { r.status = NAVI_E_KV_FULL; r.error = "KV cache full"; return r; }
+    if (kv.n_layer != I.d.TL || kv.kv_dim != I.d.KV) { r.status = NAVI_E_ARG; r.error = "KV cache layout does not match the talker"; return r; }
+    std::string err;
+    const int st = I.launch(d_x, nullptr, nullptr, nullptr, &kv, n_past, Sampling{}, 0, 0, err, layer, d_out);
+    if (st != NAVI_OK) { r.status = st; r.error = err; return r; }
+    return I.collect();
 }
 
 FrameResult Frame::collect() { return impl_->collect(); }

@@ -56,6 +56,11 @@ public:
     int enqueue(KvCache & kv, int n_past, const float * d_trailing, const Sampling & s, uint64_t seed, int frame_index,
                 std::string & err);
     FrameResult collect();
+    // One talker decoder layer alone (the layer phases of the frame: q/k/v, attention over
+    // positions [0, n_past) plus the new one, o, gate/up, down) on the f32 input d_x at
+    // position n_past, writing the f32 residual stream after the layer to d_out and the
+    // layer's K/V row n_past (configs[0]'s single-layer decode step).
+    FrameResult run_layer(int layer, const float * d_x, KvCache & kv, int n_past, float * d_out);
 
     const float * d_step_out() const;
     void set_step_in(const float * d_step);

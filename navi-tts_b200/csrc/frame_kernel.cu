@@ -866,6 +866,20 @@ __device__ void consumer(const Args & A, Sm & S) {
             continue;
         }
 
+        if (ph.op == XOUT) {
+            // single-layer program: the residual stream after the layer, this CTA's rows as f32
+            const bool ok = ll_fetch(A.w.x, d.H, ptag, S.xres, A, S.ctrl, p);
+            if (!consumers_ok(S, ok)) break;
+            for (int i = R.h0 + tid; i < R.h1; i += NCT) A.step_out[i] = S.xres[i];
+            if (b == 0 && tid == 0) {
+                __threadfence();
+                st_relaxed_u32(&A.w.ctl[0], A.tag_base);
+            }
+            named_sync(BID, NCT);
+            stamp(A, p, 3);
+            continue;
+        }
+
         if (ph.op == FINAL) {
             const SampleScratch sc = sampler_scratch(S, Vmax);
             const bool ok = ll_fetch(A.w.clogits + static_cast<size_t>(NCB - 2) * d.CV, d.CV, ptag, sc.s, A, S.ctrl, p);
@@ -917,7 +931,7 @@ __device__ void consumer(const Args & A, Sm & S) {
         switch (ph.op) {
             case TQKV: case CQKV: {
                 nnorm = ncol;
-                if (ph.layer == 0 && ph.op == TQKV) {
+                if (ph.op == TQKV && (ph.layer == 0 || ph.pos == POS_STEP_IN)) {
                     if (ok)
                         for (int i = tid; i < d.H; i += NCT) stage(0, i, __ldcg(A.step_in + i));
                 } else if (ph.layer == 0 && ph.pos == 0) {

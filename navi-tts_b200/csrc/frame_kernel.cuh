@@ -56,7 +56,11 @@ constexpr uint32_t PIECE = 32768;       // bulk copies are issued in pieces of a
 constexpr uint32_t CTRL_BYTES = 256;    // per-CTA control block in shared memory
 constexpr int PROF_STRIDE = 4 * 4096 + 1;   // trace words per CTA: 4 stamps x phases, then the start
 
-enum Op : uint8_t { TQKV, TATTN, TO, TGU, TDOWN, THEAD, CQKV, CATTN, CO, CGU, CDOWN, CHEAD, FINAL };
+enum Op : uint8_t { TQKV, TATTN, TO, TGU, TDOWN, THEAD, CQKV, CATTN, CO, CGU, CDOWN, CHEAD, FINAL, XOUT };
+
+// Talker QKV phase flag (Phase::pos): stage the layer input from Args::step_in instead of the
+// previous layer's output (the first phase of a single-layer program).
+constexpr uint8_t POS_STEP_IN = 1;
 
 struct Phase {
     uint8_t op, ncol, layer, pos;

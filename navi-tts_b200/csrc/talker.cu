@@ -1,10 +1,10 @@
 // Kernels and host side of the talker prompt and prefill (reference: model/qwen3tts/talker.hip:21-399).
 //
 // The prefill runs the prompt rows (T <= max_prompt_tokens) through the 28 talker layers at
-// positions 0..T-1. Its GEMMs (T x K times K x N, f16 weights) run on the tensor cores with
-// mma.sync m16n8k16: each f32 activation enters as two f16 values, hi = f16(x) and
-// lo = f16(x - hi), so the products keep about 22 bits of the activation while the weights
-// stay exact f16; accumulation is f32.
+// positions 0..T-1. Its GEMMs (T x K times K x N, f16 weights) run on the tcgen05 conv kernel
+// (conv.hpp) and its causal attention on mma.sync tiles (k_prefill_attn_mma); in both, each
+// f32 operand enters as two f16 values, hi = f16(x) and lo = f16(x - hi), so the products keep
+// about 22 bits of it while the f16 weights and cache rows stay exact; accumulation is f32.
 #include "talker.hpp"
 #include "conv.hpp"
 #include "device.cuh"
@@ -109,51 +109,215 @@ __global__ void k_qk_norm_rope(float * qkv, int row_stride, const float * q_norm
     }
 }
 
-// Causal GQA attention of the prefill: block (t, h) over keys 0..pos0 + t from the f16 cache
-// (talker.hip:86-117); scores in shared memory, softmax in f32.
-constexpr int MAX_KEYS = 1024;
-__global__ void k_prefill_attn(const float * qkv, int row_stride, const __half * kcache, const __half * vcache, int NH, int NKV, int pos0,
-                               float * out) {
+// ---- causal GQA attention of the prefill on the tensor cores ----------------------------------
+//
+// What it computes is the reference's k_prefill_attention (talker.hip:84-117): for row t at
+// position pos0 + t and query head h, softmax(q K^T / sqrt(128)) V over the cached keys
+// 0..pos0 + t of KV head h / (NH / NKV), with K (after RoPE) and V as f16 cache rows.
+//
+// How: flash-attention tiles. A CTA takes 64 query rows of one head (4 warps x 16 rows) and
+// walks the key range in tiles of 64 keys, double-buffered in shared memory by cp.async.
+// Scores and P.V run as mma.sync m16n8k16 (f16 operands, f32 accumulators) with an online
+// softmax in registers, so the key count has no cap. The f32 operands enter as two f16
+// halves: q = hi + lo against the exact f16 K rows, and p = hi + lo against the exact f16 V
+// rows, which keeps about 22 bits of q and p; softmax, the running max and sum stay f32.
+// Shared-memory rows are 256 bytes (128 f16), stored with their 16-byte chunks XOR-swizzled
+// by (row & 7) so the ldmatrix row gathers hit eight different bank groups.
+constexpr int PA_HD = 128;          // head_dim the kernel is built for
+constexpr int PA_QT = 64;           // query rows per CTA
+constexpr int PA_KT = 64;           // keys per tile
+constexpr int PA_WARPS = PA_QT / 16;
+constexpr int PA_THREADS = PA_WARPS * 32;
+constexpr uint32_t PA_ROW = PA_HD * 2;                                   // bytes per f16 row
+constexpr uint32_t PA_TILE = PA_KT * PA_ROW;                             // one K or V tile
+constexpr uint32_t PA_SMEM = 2 * PA_QT * PA_ROW + 2 * 2 * PA_TILE;       // q hi, q lo; 2 x (K, V)
+
+__device__ __forceinline__ uint32_t pa_swz(int row, int chunk) { return static_cast<uint32_t>(row) * PA_ROW + ((chunk ^ (row & 7)) << 4); }
+
+__device__ __forceinline__ void pa_ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void pa_ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+// c (16x8 f32) += a (16x16 f16, row) * b (16x8 f16, col)
+__device__ __forceinline__ void pa_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pa_pack(float lo_elem, float hi_elem) {
+    const __half2 h = __floats2half2_rn(lo_elem, hi_elem);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+// f32 pair -> (f16 hi pair, f16 lo pair) with v = hi + lo to about 22 bits
+__device__ __forceinline__ void pa_split(float a, float b, uint32_t & hi, uint32_t & lo) {
+    const float ha = __half2float(__float2half_rn(a)), hb = __half2float(__float2half_rn(b));
+    hi = pa_pack(ha, hb);
+    lo = pa_pack(a - ha, b - hb);
+}
+
+// K and V rows [k0, k0 + PA_KT) of KV head g into one buffer pair (rows past n_keys: zeros).
+__device__ __forceinline__ void pa_load_kv(uint8_t * kbuf, uint8_t * vbuf, const __half * kc, const __half * vc, int KV, int g, int k0,
+                                           int n_keys) {
+    for (int i = threadIdx.x; i < PA_KT * 16; i += PA_THREADS) {
+        const int r = i >> 4, c = i & 15, key = k0 + r;
+        const uint32_t o = pa_swz(r, c);
+        if (key < n_keys) {
+            const size_t src = static_cast<size_t>(key) * KV + g * PA_HD + c * 8;
+            cp_async16(kbuf + o, kc + src);
+            cp_async16(vbuf + o, vc + src);
+        } else {
+            *reinterpret_cast<uint4 *>(kbuf + o) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4 *>(vbuf + o) = make_uint4(0, 0, 0, 0);
+        }
+    }
+    cp_async_commit();
+}
+
+__global__ void __launch_bounds__(PA_THREADS) k_prefill_attn_mma(const float * qkv, int row_stride, const __half * kcache,
+                                                                  const __half * vcache, int T, int NH, int NKV, int pos0, float * out) {
     navi::dev::griddep_wait();
     navi::dev::griddep_launch_dependents();
-    constexpr int HD = 128;
-    __shared__ float sc[MAX_KEYS];
-    __shared__ float red[8];
-    const int t = blockIdx.x, h = blockIdx.y, n = pos0 + t + 1, g = h / (NH / NKV), KV = NKV * HD;
-    const float * q = qkv + static_cast<size_t>(t) * row_stride + h * HD;
-    const float scale = rsqrtf(static_cast<float>(HD));
-    float m = -INFINITY;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-        const __half2 * kr = reinterpret_cast<const __half2 *>(kcache + static_cast<size_t>(j) * KV + g * HD);
-        float d = 0.f;
-        for (int i = 0; i < HD / 2; ++i) {
-            const float2 kk = __half22float2(kr[i]);
-            d = fmaf(q[2 * i], kk.x, d);
-            d = fmaf(q[2 * i + 1], kk.y, d);
+    extern __shared__ __align__(128) uint8_t pa_smem[];
+    uint8_t * qhi = pa_smem;
+    uint8_t * qlo = qhi + PA_QT * PA_ROW;
+    uint8_t * kvb = qlo + PA_QT * PA_ROW;   // [2][K tile, V tile]
+    const int h = blockIdx.y, g = h / (NH / NKV), KV = NKV * PA_HD;
+    const int t0 = blockIdx.x * PA_QT, rows = min(PA_QT, T - t0);
+    const int n_keys = pos0 + t0 + rows;   // keys any row of this CTA sees
+    const int n_tiles = (n_keys + PA_KT - 1) / PA_KT;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+
+    pa_load_kv(kvb, kvb + PA_TILE, kcache, vcache, KV, g, 0, n_keys);
+    // this CTA's query rows as f16 hi / lo (rows past T: zeros)
+    for (int i = threadIdx.x; i < PA_QT * 16; i += PA_THREADS) {
+        const int r = i >> 4, c = i & 15;
+        uint4 hv = make_uint4(0, 0, 0, 0), lv = make_uint4(0, 0, 0, 0);
+        if (r < rows) {
+            const float * q = qkv + static_cast<size_t>(t0 + r) * row_stride + h * PA_HD + c * 8;
+            const float4 a = *reinterpret_cast<const float4 *>(q), b = *reinterpret_cast<const float4 *>(q + 4);
+            pa_split(a.x, a.y, hv.x, lv.x);
+            pa_split(a.z, a.w, hv.y, lv.y);
+            pa_split(b.x, b.y, hv.z, lv.z);
+            pa_split(b.z, b.w, hv.w, lv.w);
         }
-        sc[j] = d * scale;
-        m = fmaxf(m, sc[j]);
+        *reinterpret_cast<uint4 *>(qhi + pa_swz(r, c)) = hv;
+        *reinterpret_cast<uint4 *>(qlo + pa_swz(r, c)) = lv;
     }
-    m = warp_max(m);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-    __syncthreads();
-    float mx = -INFINITY;
-    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) mx = fmaxf(mx, red[k]);
-    __syncthreads();
-    float s = 0.f;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-        sc[j] = expf(sc[j] - mx);
-        s += sc[j];
+
+    const float scale = rsqrtf(static_cast<float>(PA_HD));
+    const int qrow0 = warp * 16;                       // this warp's rows within the tile
+    const int pos_a = pos0 + t0 + qrow0 + gq;          // positions of this thread's two rows
+    const int pos_b = pos_a + 8;
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+    const uint32_t sq_hi = smem_addr(qhi), sq_lo = smem_addr(qlo);
+
+    for (int kt = 0; kt < n_tiles; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < n_tiles) {
+            uint8_t * nb = kvb + (buf ^ 1) * 2 * PA_TILE;
+            pa_load_kv(nb, nb + PA_TILE, kcache, vcache, KV, g, (kt + 1) * PA_KT, n_keys);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const uint32_t sk = smem_addr(kvb + buf * 2 * PA_TILE), sv = sk + PA_TILE;
+        const int k0 = kt * PA_KT;
+        // S = q K^T for this warp's 16 rows and the tile's 64 keys
+        float s[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < PA_HD / 16; ++ks) {
+            uint32_t ah[4], al[4];
+            const int ar = qrow0 + (lane & 7) + ((lane >> 3) & 1) * 8, ac = ks * 2 + (lane >> 4);
+            pa_ldsm_x4(ah, sq_hi + pa_swz(ar, ac));
+            pa_ldsm_x4(al, sq_lo + pa_swz(ar, ac));
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {   // key n-tiles 2np, 2np + 1
+                uint32_t b[4];
+                const int kr = np * 16 + (lane & 7) + (lane >> 4) * 8, kc = ks * 2 + ((lane >> 3) & 1);
+                pa_ldsm_x4(b, sk + pa_swz(kr, kc));
+                pa_mma(s[2 * np], ah, b[0], b[1]);
+                pa_mma(s[2 * np], al, b[0], b[1]);
+                pa_mma(s[2 * np + 1], ah, b[2], b[3]);
+                pa_mma(s[2 * np + 1], al, b[2], b[3]);
+            }
+        }
+        // scale, causal mask, online softmax (rows gq and gq + 8 of the warp)
+        float mx_a = m_a, mx_b = m_b;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int key = k0 + j * 8 + 2 * tq;
+            s[j][0] = key <= pos_a ? s[j][0] * scale : -INFINITY;
+            s[j][1] = key + 1 <= pos_a ? s[j][1] * scale : -INFINITY;
+            s[j][2] = key <= pos_b ? s[j][2] * scale : -INFINITY;
+            s[j][3] = key + 1 <= pos_b ? s[j][3] * scale : -INFINITY;
+            mx_a = fmaxf(mx_a, fmaxf(s[j][0], s[j][1]));
+            mx_b = fmaxf(mx_b, fmaxf(s[j][2], s[j][3]));
+        }
+#pragma unroll
+        for (int off = 1; off < 4; off <<= 1) {
+            mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+            mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+        }
+        // key 0 is in the first tile and every row sees it, so the maxima are finite here
+        const float al_a = expf(m_a - mx_a), al_b = expf(m_b - mx_b);
+        m_a = mx_a;
+        m_b = mx_b;
+        l_a *= al_a;
+        l_b *= al_b;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            o[j][0] *= al_a; o[j][1] *= al_a;
+            o[j][2] *= al_b; o[j][3] *= al_b;
+        }
+        uint32_t ph[4][4], pl[4][4];   // P as the A operand of P.V, per 16-key step
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float p0 = expf(s[j][0] - m_a), p1 = expf(s[j][1] - m_a);
+            const float p2 = expf(s[j][2] - m_b), p3 = expf(s[j][3] - m_b);
+            l_a += p0 + p1;
+            l_b += p2 + p3;
+            const int st = j >> 1, hi_half = (j & 1) * 2;   // n-tile 2st -> a0/a1, 2st + 1 -> a2/a3
+            pa_split(p0, p1, ph[st][hi_half], pl[st][hi_half]);
+            pa_split(p2, p3, ph[st][hi_half + 1], pl[st][hi_half + 1]);
+        }
+        // O += P V over the tile's 4 key steps and the 16 dim n-tiles
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+#pragma unroll
+            for (int dp = 0; dp < 8; ++dp) {   // dim n-tiles 2dp, 2dp + 1
+                uint32_t b[4];
+                const int vr = st * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, vc = dp * 2 + (lane >> 4);
+                pa_ldsm_x4_t(b, sv + pa_swz(vr, vc));
+                pa_mma(o[2 * dp], ph[st], b[0], b[1]);
+                pa_mma(o[2 * dp], pl[st], b[0], b[1]);
+                pa_mma(o[2 * dp + 1], ph[st], b[2], b[3]);
+                pa_mma(o[2 * dp + 1], pl[st], b[2], b[3]);
+            }
+        }
+        __syncthreads();   // the buffer is refilled two tiles on
     }
-    s = warp_sum(s);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-    __syncthreads();
-    float tot = 0.f;
-    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) tot += red[k];
-    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
-        float acc = 0.f;
-        for (int j = 0; j < n; ++j) acc = fmaf(sc[j], __half2float(vcache[static_cast<size_t>(j) * KV + g * HD + i]), acc);
-        out[(static_cast<size_t>(t) * NH + h) * HD + i] = acc / tot;
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+        l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
+        l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
+    }
+    const float inv_a = 1.f / l_a, inv_b = 1.f / l_b;
+    const int ra = t0 + qrow0 + gq, rb = ra + 8;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int d = j * 8 + 2 * tq;
+        if (ra < T) *reinterpret_cast<float2 *>(out + (static_cast<size_t>(ra) * NH + h) * PA_HD + d) = make_float2(o[j][0] * inv_a, o[j][1] * inv_a);
+        if (rb < T) *reinterpret_cast<float2 *>(out + (static_cast<size_t>(rb) * NH + h) * PA_HD + d) = make_float2(o[j][2] * inv_b, o[j][3] * inv_b);
     }
 }
 
@@ -255,7 +419,7 @@ std::unique_ptr<Talker> Talker::create(const Device & dev, const DeviceWeights &
     I.p = w.params();
     const auto & tp = I.p.talker;
     if (tp.head_dim != 128) fail("talker: the prefill kernels are built for head_dim 128", NAVI_E_SHAPE);
-    if (max_prompt_tokens < 9 || max_prompt_tokens > MAX_KEYS) fail("talker: max_prompt_tokens must be in 9..1024", NAVI_E_ARG);
+    if (max_prompt_tokens < 9) fail("talker: max_prompt_tokens must be at least 9", NAVI_E_ARG);
     if (max_positions < max_prompt_tokens) fail("talker: max_positions below max_prompt_tokens", NAVI_E_ARG);
     I.H = tp.hidden; I.NH = tp.n_head; I.NKV = tp.n_kv_head; I.Q = tp.n_head * tp.head_dim; I.KVD = tp.n_kv_head * tp.head_dim;
     I.F = tp.ff; I.QKV = I.Q + 2 * I.KVD; I.TV = tp.vocab; I.TH = I.p.text_hidden;
@@ -323,6 +487,8 @@ std::unique_ptr<Talker> Talker::create(const Device & dev, const DeviceWeights &
         I.ws.partial_cap = part;
         I.ws.err = I.alloc<int>(1);
     }
+    NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_prefill_attn_mma), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(PA_SMEM)));
     NAVI_CUDA(cudaEventCreate(&I.ev0));
     NAVI_CUDA(cudaEventCreate(&I.ev1));
     return t;
@@ -419,7 +585,8 @@ void Talker::prefill(const Prompt & pr) {
         I.gemm(ly.wqkv, nullptr, I.n, H, T, H, I.QKV, I.qkv, I.QKV, EPI_NONE);
         NAVI_CUDA(navi::dev::launch_pdl(k_qk_norm_rope, dim3(T), dim3(256), 0, I.stream, I.qkv, I.QKV, ly.qn, ly.kn, I.NH, I.NKV, tp.rms_eps,
                                         I.rope, 0, kc, vc));
-        NAVI_CUDA(navi::dev::launch_pdl(k_prefill_attn, dim3(T, I.NH), dim3(128), 0, I.stream, I.qkv, I.QKV, kc, vc, I.NH, I.NKV, 0, I.att));
+        NAVI_CUDA(navi::dev::launch_pdl(k_prefill_attn_mma, dim3((T + PA_QT - 1) / PA_QT, I.NH), dim3(PA_THREADS), PA_SMEM, I.stream, I.qkv,
+                                        I.QKV, kc, vc, T, I.NH, I.NKV, 0, I.att));
         // the RMSNorms after the O projection and (but for the last layer) after the down
         // projection are written by those GEMMs' launches
         I.gemm(ly.wo, nullptr, I.att, I.Q, T, I.Q, H, I.x, H, EPI_RESIDUAL, false, I.x, ly.ln2, I.n);

@@ -113,6 +113,7 @@ SIGNATURES = [
                                      POINTER(FrameResult)]),
     ("navi_frame_run", c_int, [c_void_p, POINTER(KV), c_int, c_void_p, POINTER(Sampling), c_uint64, c_int,
                                POINTER(FrameResult)]),
+    ("navi_frame_run_layer", c_int, [c_void_p, c_int, c_void_p, POINTER(KV), c_int, c_void_p, POINTER(FrameResult)]),
     ("navi_frame_enqueue", c_int, [c_void_p, POINTER(KV), c_int, c_void_p, POINTER(Sampling), c_uint64, c_int]),
     ("navi_frame_collect", c_int, [c_void_p, POINTER(FrameResult)]),
     ("navi_frame_step_out", c_void_p, [c_void_p]),

@@ -379,6 +379,12 @@ class Frame:
         st = lib().navi_frame_run(self.h, kv.ptr(), n_past, c_void_p(d_trailing), byref(s.c()), seed, frame_index, byref(r))
         return _result(r, st)
 
+    def run_layer(self, layer: int, d_x: int, kv: KvCache, n_past: int, d_out: int) -> FrameResult:
+        """One talker decoder layer alone at position n_past: d_x -> d_out, f32 [hidden]."""
+        r = capi.FrameResult()
+        st = lib().navi_frame_run_layer(self.h, layer, c_void_p(d_x), kv.ptr(), n_past, c_void_p(d_out), byref(r))
+        return _result(r, st)
+
     def enqueue(self, kv: KvCache, n_past: int, d_trailing: int, s: Sampling, seed: int, frame_index: int) -> None:
         check(lib().navi_frame_enqueue(self.h, kv.ptr(), n_past, c_void_p(d_trailing), byref(s.c()), seed, frame_index))
 

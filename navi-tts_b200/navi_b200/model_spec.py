@@ -102,6 +102,17 @@ def full_config(decoder_dim: int = 1024) -> ModelConfig:
                        text_vocab=151936, text_hidden=2048, decoder_dim=decoder_dim)
 
 
+def layer_config() -> ModelConfig:
+    """configs[0]'s model: the benchmark shapes with a single talker layer (the layer under
+    test). Written with seed_offset=-1 (LAYER_SEED_OFFSET) its talker weights draw from seed 0.
+    The text embedding, unused by a decode layer, is cut to 4096 rows to keep the file small."""
+    c = full_config(1024)
+    return replace(c, name="synthetic-qwen3-tts-one-layer", talker=replace(c.talker, n_layer=1), text_vocab=4096)
+
+
+LAYER_SEED_OFFSET = -1   # component seed 1 (talker) - 1 = configs[0]'s seed 0
+
+
 def small_config() -> ModelConfig:
     """A reduced model for tests that the CPU oracle finishes in seconds.
     Keeps head_dim 128, 16 codebooks and the 1920x upsampling chain; shrinks widths and depth."""

@@ -147,13 +147,13 @@ def decoder_layer(W: Weights, component: str, l: int, x: torch.Tensor, kcache: t
     group = d.n_head // d.n_kv_head
     scale = 1.0 / math.sqrt(d.head_dim)
     out = torch.empty(T, d.n_head, d.head_dim)
-    for t in range(T):
-        n = pos0 + t + 1
-        for hh in range(d.n_head):
-            g = hh // group
-            s = (K[:n, g] @ q[t, hh]) * scale
-            pr = torch.softmax(s, dim=0)
-            out[t, hh] = pr @ V[:n, g]
+    n = pos0 + T
+    causal = torch.arange(n)[None, :] > (pos0 + torch.arange(T))[:, None]   # key j hidden from row t when j > pos0 + t
+    for hh in range(d.n_head):
+        g = hh // group
+        s = (q[:, hh] @ K[:n, g].T) * scale
+        s = s.masked_fill(causal, float("-inf"))
+        out[:, hh] = torch.softmax(s, dim=1) @ V[:n, g]
     x = x + out.reshape(T, -1) @ W[p + "self_attn.o_proj.weight"].T
     h2 = rmsnorm(x, W[p + "post_attention_layernorm.weight"], d.eps)
     a = silu(h2 @ W[p + "mlp.gate_proj.weight"].T) * (h2 @ W[p + "mlp.up_proj.weight"].T)

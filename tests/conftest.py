@@ -35,3 +35,12 @@ def full_navi(tmp_path_factory):
     if not os.path.exists(path):
         model_spec.write_synthetic(path, model_spec.full_config(1024))
     return path
+
+
+@pytest.fixture(scope="session")
+def layer_navi(tmp_path_factory):
+    """configs[0]'s model: the benchmark shapes with one talker layer, talker weights from seed 0."""
+    from navi_b200 import model_spec
+    path = tmp_path_factory.mktemp("navi") / "layer.navi"
+    model_spec.write_synthetic(path, model_spec.layer_config(), seed_offset=model_spec.LAYER_SEED_OFFSET)
+    return str(path)

@@ -119,13 +119,33 @@ def test_small_prefill_then_frames(small_navi):
         assert kv.n_used == pr.n_prefill + i
 
 
-def test_full_size_prompt_and_prefill(full_navi):
-    """configs[4]'s talker: full-size weights (text vocabulary 151936 x 2048), a 40-token text."""
+@pytest.mark.parametrize("n_text", [40, 200])
+def test_full_size_prompt_and_prefill(full_navi, n_text):
+    """configs[4]'s talker: full-size weights (text vocabulary 151936 x 2048), a 40-token text
+    and configs[4]'s 200-token text (208 prefill rows)."""
     W = om.Weights.from_navi(full_navi)
     dev = engine.Device(0)
     w = engine.Weights(dev, full_navi)
     tal = engine.Talker(dev, w, max_prompt_tokens=256, max_positions=2048)
-    ids = _ids(W.cfg, 40, seed=2)
+    ids = _ids(W.cfg, n_text, seed=2)
     spk = (np.random.default_rng(3).standard_normal(W.tl.hidden) * 0.05).astype(np.float32)
     pr, pre_o = _check_prompt(W, tal, ids, "english", spk)
     _check_prefill(W, tal, pr, pre_o)
+
+
+@pytest.mark.parametrize("T", [208, 1100])
+def test_full_size_long_prefill(full_navi, T):
+    """The 28-layer prefill over T arbitrary rows (T = 208: the row count of configs[4]'s
+    200-token prompt if it were prefilled whole; T = 1100: past the 1024 keys the reference's
+    prefill attention holds, talker.hip:86): last row's hidden and logits, every layer's T K/V
+    rows, against the oracle. The rows go in through navi_talker_prefill's prompt pointer."""
+    import ctypes
+    from navi_b200 import capi
+    W = om.Weights.from_navi(full_navi)
+    dev = engine.Device(0)
+    w = engine.Weights(dev, full_navi)
+    tal = engine.Talker(dev, w, max_prompt_tokens=T, max_positions=T + 16)
+    rows = torch.randn(T, W.tl.hidden, generator=torch.Generator().manual_seed(T)) * 0.5
+    d_rows = rows.cuda()
+    pr = capi.Prompt(d_rows.data_ptr(), d_rows.data_ptr(), d_rows.data_ptr(), T, 0)
+    _check_prefill(W, tal, pr, rows)
