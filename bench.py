@@ -154,6 +154,66 @@ def cpu_baseline(L: int, n_frames: int = 3):
                       f"PyTorch fp32 oracle, {torch.get_num_threads()} threads, after 1 warm-up frame"}
 
 
+LAYER_NAVI = os.environ.get("NAVI_LAYER_NAVI", "/tmp/navi_bench_layer.navi")
+
+
+def layer_bytes(t, L: int) -> int:
+    """HBM bytes of one talker decoder layer step at KV length L: f16 q/k/v/o/gate/up/down
+    weights, f32 norm weights (input, post-attention, q, k), and the cached K/V rows
+    0..L-1 plus the new row L, f16."""
+    H, Q, K, F, D = t.hidden, t.n_head * t.head_dim, t.n_kv_head * t.head_dim, t.ff, t.head_dim
+    return 2 * (Q * H + 2 * K * H + H * Q + 3 * F * H) + 4 * (2 * H + 2 * D) + 2 * (L + 1) * K * 2
+
+
+def layer_bench(dev_ordinal: int, reps: int, warm: int, L: int = 256):
+    """one talker decoder layer, one decode step at batch 1, KV length 256, seed-0
+    weights, input hidden N(0, 1), cache N(0, 1) f16. Each timed launch follows a 256 MB
+    write that flushes L2 (the layer's 32.5 MB would otherwise stay resident); the time is
+    the launch's CUDA-event device time (Frame::run_layer), median over `reps`."""
+    import numpy as np
+    import torch
+    from navi_b200 import engine, model_spec
+    if not os.path.exists(LAYER_NAVI):
+        model_spec.write_synthetic(LAYER_NAVI, model_spec.layer_config(), seed_offset=model_spec.LAYER_SEED_OFFSET)
+    dev = engine.Device(dev_ordinal)
+    w = engine.Weights(dev, LAYER_NAVI)
+    fr = engine.Frame(dev, w)
+    t = w.params.talker
+    kvd = t.n_kv_head * t.head_dim
+    cuda = f"cuda:{dev_ordinal}"
+    g = torch.Generator(device=cuda).manual_seed(0)
+    k = [torch.randn(L + 8, kvd, generator=g, device=cuda).half()]
+    v = [torch.randn(L + 8, kvd, generator=g, device=cuda).half()]
+    kv = engine.KvCache.wrap([k[0].data_ptr()], [v[0].data_ptr()], L + 8, kvd, keepalive=(k, v))
+    x = torch.randn(t.hidden, generator=g, device=cuda)
+    y = torch.empty_like(x)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=cuda)
+    stream = torch.cuda.ExternalStream(dev.stream, device=cuda)
+    us = []
+    for i in range(warm + reps):
+        with torch.cuda.stream(stream):
+            flush.fill_(i & 0xFF)
+        r = fr.run_layer(0, x.data_ptr(), kv, L, y.data_ptr())
+        assert r.ok, r.error
+        if i >= warm:
+            us.append(r.us)
+    us_med = float(np.median(us))
+    ab = layer_bytes(t, L)
+    peak, kind = measured_peak()
+    achieved = ab / (us_med * 1e-6) / 1e9
+    fr.close()
+    w.close()
+    dev.close()
+    return {"workload": f"configs[0]: one talker decoder layer (hidden {t.hidden}, {t.n_head}/{t.n_kv_head} heads x "
+                        f"{t.head_dim}, SwiGLU {t.ff}), KV {L}, batch 1, seed-0 weights",
+            "us_per_step": round(us_med, 3), "us_p10": round(float(np.percentile(us, 10)), 3),
+            "us_p90": round(float(np.percentile(us, 90)), 3), "launches": reps,
+            "l2": "flushed before every launch (256 MB write)",
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "algorithmic_bytes": ab, "peak_kind": kind,
+                         "bound_us": round(ab / (peak * 1e9) * 1e6, 3)}}
+
+
 def vocoder_flops_per_frame(p) -> float:
     """2 x multiply-adds of every GEMM / conv of the decoder per frame (vocoder.hip:261-343)."""
     v = p.vocoder
@@ -313,8 +373,10 @@ def run_reference(args):
     if rank != 0:
         return
     ensure_weights(0, 1)
-    cb = cpu_baseline(args.kv, n_frames=max(1, min(args.steps, 3)))
-    line = {"metric": METRIC, "value": cb["value"], "unit": "frames/s", "n_gpus": args.gpus, "steps": args.steps,
+    n = max(1, min(args.steps, 60))          # about 7 s of CPU time at ~9 frames/s
+    cb = cpu_baseline(args.kv, n_frames=n)
+    line = {"metric": METRIC, "value": cb["value"], "unit": "frames/s", "n_gpus": args.gpus, "steps": n,
+            "steps_requested": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, random KV)",
             "config": {"workload": f"configs[1]+[2] frame at KV {args.kv}", "kv_len": args.kv, "batch": 1},
@@ -467,6 +529,8 @@ def run_ours(args):
         }
         if serving:
             line["serving"] = serving
+        if args.layer:
+            line["layer"] = layer_bench(local, reps=max(20, min(args.steps, 200)), warm=args.warmup)
         if args.vocoder:
             line["vocoder"] = vocoder_bench(dev, w)
         if args.cpu_baseline and world == 1:
@@ -505,6 +569,7 @@ def main():
     ap.add_argument("--no-vocoder", dest="vocoder", action="store_false", help="skip the configs[3] vocoder line")
     ap.add_argument("--vocoder-only", action="store_true", help="run only the configs[3] vocoder measurement")
     ap.add_argument("--voc-chunks", default="4,16", help="vocoder chunk lengths (frames), comma separated")
+    ap.add_argument("--no-layer", dest="layer", action="store_false", help="skip the configs[0] single-layer line")
     ap.add_argument("--streams", type=int, default=8, help="configs[4] utterances over all GPUs (64 = the full config; 0 = skip)")
     args = ap.parse_args()
     if args.warmup < 3:

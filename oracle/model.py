@@ -223,7 +223,7 @@ class _SampleArgs(ctypes.Structure):
                 ("rng", ctypes.c_int), ("seed", ctypes.c_uint64), ("frame_index", ctypes.c_int),
                 ("codebook", ctypes.c_int), ("talker_mods", ctypes.c_int), ("suppress_from", ctypes.c_int),
                 ("eos_id", ctypes.c_int), ("min_frames", ctypes.c_int), ("repetition_penalty", ctypes.c_float),
-                ("seen", ctypes.c_void_p)]
+                ("seen", ctypes.c_void_p), ("exp_libm", ctypes.c_int)]
 
 
 _lib = None
@@ -262,9 +262,10 @@ class Sampling:
     rng: int = 0          # 0 PCG (the reference's stream), 1 Philox
 
 
-def sample(logits, codebook: int, s: Sampling, seed: int, frame_index: int, *, talker_mods=None) -> int:
+def sample(logits, codebook: int, s: Sampling, seed: int, frame_index: int, *, talker_mods=None, exp_libm: bool = False) -> int:
     """codebook 0: the talker draw (talker_mods = (suppress_from, eos_id, seen u8[V]));
-    codebooks 1..15: the code-predictor draws."""
+    codebooks 1..15: the code-predictor draws. exp_libm: take e_i from the C library's expf
+    (to compare with the reference's own sampler run on the host), not the specified exp."""
     lg = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
     a = _SampleArgs()
     if codebook == 0:
@@ -272,6 +273,7 @@ def sample(logits, codebook: int, s: Sampling, seed: int, frame_index: int, *, t
     else:
         a.temperature, a.top_k, a.top_p = s.cp_temperature, s.cp_top_k, s.cp_top_p
     a.rng, a.seed, a.frame_index, a.codebook = s.rng, seed & (2**64 - 1), frame_index, codebook
+    a.exp_libm = 1 if exp_libm else 0
     seen = None
     if talker_mods is not None:
         sup, eos, seen_arr = talker_mods

@@ -147,6 +147,10 @@ typedef struct {
     int suppress_from, eos_id, min_frames;
     float repetition_penalty;  /* <= 0: off */
     const uint8_t * seen;      /* [V] or null */
+    /* 1: e_i with the C library's expf instead of oracle_exp -- only to compare with the
+     * reference's own sampler compiled for the host (oracle/ref_frame_check.cpp), which
+     * calls expf from the same library */
+    int exp_libm;
 } oracle_sample_args;
 
 /* Writes the per-index working values into dbg_e (e_i, or NaN when unused) when
@@ -182,7 +186,7 @@ int oracle_sample(const float * logits, int V, const oracle_sample_args * a, flo
         threshold = key_float(keys[a->top_k - 1]);
         free(keys);
     }
-    for (int i = 0; i < V; ++i) e[i] = (s[i] >= threshold) ? oracle_exp(s[i] - mx) : 0.0f;
+    for (int i = 0; i < V; ++i) e[i] = (s[i] >= threshold) ? (a->exp_libm ? expf(s[i] - mx) : oracle_exp(s[i] - mx)) : 0.0f;
     /* the normaliser, in the reference block_sum order for a 256-thread block */
     float part[256], wsum[8];
     for (int t = 0; t < 256; ++t) {
