@@ -18,6 +18,7 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <functional>
 
 #define __global__
@@ -26,6 +27,7 @@
 #define __forceinline__ inline
 #define __launch_bounds__(...)
 #define __shared__ static
+#define __align__(n) __attribute__((aligned(n)))
 
 #define threadIdx (::simt::g_cur->tid)
 #define blockIdx (::simt::g_block_idx)
@@ -42,7 +44,11 @@ struct uint2 { unsigned x, y; };
 struct float2 { float x, y; };
 struct float4 { float x, y, z, w; };
 inline uint4 make_uint4(unsigned a, unsigned b, unsigned c, unsigned d) { return uint4{a, b, c, d}; }
+inline uint2 make_uint2(unsigned a, unsigned b) { return uint2{a, b}; }
 inline float2 make_float2(float a, float b) { return float2{a, b}; }
+inline float4 make_float4(float a, float b, float c, float d) { return float4{a, b, c, d}; }
+using std::max;
+using std::min;
 
 namespace simsim {
 template <class T> inline uint64_t to_bits(T v) {
@@ -62,9 +68,25 @@ inline LaunchRunner & launch_runner() {
     return r;
 }
 inline void set_launch_runner(LaunchRunner r) { launch_runner() = std::move(r); }
+
+// kernel<<<grid, block, smem, stream>>>(args), rewritten by oracle/hip_to_host.py: the blocks of
+// the grid run one after another (kernels without inter-block waits only)
+struct Launch {
+    dim3 grid, block;
+    template <class F, class... A> void run(F fn, A &&... args) const {
+        for (unsigned z = 0; z < grid.z; ++z)
+            for (unsigned y = 0; y < grid.y; ++y)
+                for (unsigned x = 0; x < grid.x; ++x)
+                    ::simt::run_block(block.x * block.y * block.z, ::simt::Dim{x, y, z}, ::simt::Dim{grid.x, grid.y, grid.z},
+                                      [&]() { fn(args...); });
+    }
+};
+inline Launch launch(dim3 grid, dim3 block, size_t = 0, void * = nullptr) { return Launch{grid, block}; }
 } // namespace simsim
 
 inline void __syncthreads() { ::simt::block_barrier(); }
+inline float __expf(float x) { return std::exp(x); }
+inline float __sinf(float x) { return std::sin(x); }
 inline void __threadfence() {}
 template <class T> inline T __shfl_xor(T v, int mask, int width = 32) {
     return simsim::from_bits<T>(::simt::wave_collective(::simt::Coll::ShflXor, simsim::to_bits(v), mask, width));
@@ -141,6 +163,8 @@ inline hipError_t hipEventElapsedTime(float * ms, hipEvent_t, hipEvent_t) {
     return hipSuccess;
 }
 inline hipError_t hipStreamSynchronize(hipStream_t) { return hipSuccess; }
+inline hipError_t hipEventSynchronize(hipEvent_t) { return hipSuccess; }
+inline hipError_t hipGetLastError() { return hipSuccess; }
 inline hipError_t hipDeviceSynchronize() { return hipSuccess; }
 inline hipError_t hipDeviceGetAttribute(int * v, hipDeviceAttribute_t, int) {
     *v = 1;

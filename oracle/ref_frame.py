@@ -127,3 +127,35 @@ def frame(navi: str, dims, s: RefSampling, seed: int, frame_index: int, seen, tr
             r.k_rows.append(take(np.float16, KVD))
             r.v_rows.append(take(np.float16, KVD))
     return r
+
+
+VOC_BIN = os.path.join(HERE, "_ref", "ref_vocoder_check")
+
+
+def vocoder_available() -> bool:
+    return os.path.exists(VOC_BIN)
+
+
+def vocoder_decode(navi: str, codes, max_chunk: int = 32, stages: bool = False):
+    """The reference's Vocoder::decode (oracle/_ref/ref_vocoder_check) of codes [n][16]:
+    PCM f32 [n * samples_per_frame] and, with stages=True, {name: [rows, cols]} of every
+    stage of the first chunk (the reference's stage hook)."""
+    with tempfile.TemporaryDirectory() as td:
+        cpath, ppath, sdir = os.path.join(td, "codes.bin"), os.path.join(td, "pcm.bin"), os.path.join(td, "stages")
+        np.ascontiguousarray(codes, np.int32).tofile(cpath)
+        args = [VOC_BIN, navi, cpath, ppath, str(max_chunk)]
+        if stages:
+            os.mkdir(sdir)
+            args.append(sdir)
+        r = subprocess.run(args, capture_output=True, text=True, timeout=1800)
+        if r.returncode != 0:
+            raise RuntimeError(f"ref_vocoder_check failed ({r.returncode}): {r.stderr.strip()}")
+        pcm = np.fromfile(ppath, np.float32)
+        out = {}
+        if stages:
+            for f in os.listdir(sdir):
+                if f.endswith(".f32"):
+                    name = f[:-4]
+                    rows, cols = map(int, open(os.path.join(sdir, name + ".shape")).read().split())
+                    out[name] = np.fromfile(os.path.join(sdir, f), np.float32).reshape(rows, cols)
+        return pcm, out

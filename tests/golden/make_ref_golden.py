@@ -1,8 +1,9 @@
-"""Writes tests/golden/ref_frame_small.npz: outputs of the reference engine's own frame code
-(oracle/_ref/ref_frame_check, built from the reference sources by `make -C oracle REF=...`)
-on the seeded small synthetic model -- one frame at KV 10, a set of sampler draws and a
-set of per-frame seeds -- so tests/test_reference_pins.py can pin the oracle where the
-reference tree is absent.
+"""Writes tests/golden/ref_frame_small.npz and ref_vocoder_small.npz: outputs of the reference
+engine's own frame code and vocoder (oracle/_ref/ref_frame_check, ref_vocoder_check, built from
+the reference sources by `make -C oracle REF=...`) on the seeded small synthetic model -- one
+frame at KV 10, a set of sampler draws, a set of per-frame seeds, and the PCM of 7 frames
+decoded in chunks of 3 -- so tests/test_reference_pins.py and test_reference_vocoder_pins.py
+can pin the oracle where the reference tree is absent.
 
     python tests/golden/make_ref_golden.py
 """
@@ -59,6 +60,10 @@ def main():
                             draw_logits=np.stack(logits), draw_seen=np.stack(seens),
                             seeds=np.array([(p[0], p[1], s[0], s[1]) for p, s in zip(pairs, sds)], np.uint64))
         print("wrote ref_frame_small.npz; codes", r.codes)
+        vc = np.random.default_rng(31).integers(0, W.cfg.vq_codebook_size, (7, W.cfg.vq_n_q)).astype(np.int32)
+        pcm, _ = rf.vocoder_decode(navi, vc, max_chunk=3)
+        np.savez_compressed(os.path.join(HERE, "ref_vocoder_small.npz"), codes=vc, max_chunk=3, pcm=pcm)
+        print("wrote ref_vocoder_small.npz;", pcm.size, "samples")
 
 
 if __name__ == "__main__":
