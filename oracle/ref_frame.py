@@ -159,3 +159,42 @@ def vocoder_decode(navi: str, codes, max_chunk: int = 32, stages: bool = False):
                     rows, cols = map(int, open(os.path.join(sdir, name + ".shape")).read().split())
                     out[name] = np.fromfile(os.path.join(sdir, f), np.float32).reshape(rows, cols)
         return pcm, out
+
+
+TALKER_BIN = os.path.join(HERE, "_ref", "ref_talker_check")
+
+
+def talker_available() -> bool:
+    return os.path.exists(TALKER_BIN)
+
+
+def talker_prefill(navi: str, ids, language: str, speaker, dims):
+    """The reference's Talker::build_prompt + prefill (oracle/_ref/ref_talker_check).
+    dims = (H, V, n_layer, kv_dim). Returns (prefill rows, trailing rows, tts_pad, hidden,
+    logits, [(K rows, V rows) f16 per layer])."""
+    H, V, NL, KVD = dims
+    lang = (language or "").encode()
+    req = struct.pack("<i", len(ids)) + np.asarray(ids, np.int32).tobytes() + struct.pack("<i", len(lang)) + lang
+    req += np.ascontiguousarray(speaker, np.float32).tobytes()
+    with tempfile.TemporaryDirectory() as td:
+        a, b = os.path.join(td, "req.bin"), os.path.join(td, "out.bin")
+        with open(a, "wb") as f:
+            f.write(req)
+        r = subprocess.run([TALKER_BIN, navi, a, b], capture_output=True, text=True, timeout=1800)
+        if r.returncode != 0:
+            raise RuntimeError(f"ref_talker_check failed ({r.returncode}): {r.stderr.strip()}")
+        out = open(b, "rb").read()
+    n_pre, n_tr = struct.unpack_from("<ii", out, 0)
+    o = 8
+
+    def take(dtype, n):
+        nonlocal o
+        x = np.frombuffer(out, dtype=dtype, count=n, offset=o)
+        o += x.nbytes
+        return x.copy()
+
+    pre = take(np.float32, n_pre * H).reshape(n_pre, H)
+    trail = take(np.float32, n_tr * H).reshape(n_tr, H)
+    pad, hid, lg = take(np.float32, H), take(np.float32, H), take(np.float32, V)
+    kv = [(take(np.float16, n_pre * KVD).reshape(n_pre, KVD), take(np.float16, n_pre * KVD).reshape(n_pre, KVD)) for _ in range(NL)]
+    return pre, trail, pad, hid, lg, kv

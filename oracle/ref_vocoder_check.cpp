@@ -4,8 +4,8 @@
 // oracle/hip_to_host.py for the host emulator (oracle/_build/vocoder_host.cpp), is compiled
 // with kernels.h, params.cpp, navi_file.cpp and device_weights.cpp against the host
 // stand-in for the HIP runtime (oracle/hipsim): every grid runs block after block, each block
-// as cooperative fibers. The device handle the reference's Vocoder::create takes is made
-// here (the reference's device selection, runtime/device/device.cpp, talks to a real GPU).
+// as cooperative fibers. The device handle the reference's Vocoder::create takes comes from
+// hipsim/device_standin.hpp.
 // Used as in the reference's tests/test_vocoder.cpp: DeviceWeights::upload of the decoder
 // tensors it does not own, Vocoder::create, decode.
 //
@@ -14,6 +14,7 @@
 //   STAGES (optional) a directory: every stage of the first chunk as <name>.f32 + <name>.shape
 #include "vocoder_host.cpp"
 
+#include "device_standin.hpp"
 #include "model/qwen3tts/params.h"
 #include "runtime/device/device.h"
 #include "runtime/weights/device_weights.h"
@@ -24,20 +25,6 @@
 #include <iterator>
 #include <string>
 #include <vector>
-
-// the device handle, on the host: no stream, one processor
-namespace navi {
-Device Device::open() { return Device(); }
-Device::~Device() = default;
-Device::Device(Device && o) noexcept : info_(std::move(o.info_)), stream_(o.stream_) { o.stream_ = nullptr; }
-Device & Device::operator=(Device && o) noexcept {
-    info_ = std::move(o.info_);
-    stream_ = o.stream_;
-    o.stream_ = nullptr;
-    return *this;
-}
-void Device::refresh_memory() {}
-} // namespace navi
 
 int main(int argc, char ** argv) {
     if (argc < 4) {

@@ -1,9 +1,9 @@
-"""Writes tests/golden/ref_frame_small.npz and ref_vocoder_small.npz: outputs of the reference
-engine's own frame code and vocoder (oracle/_ref/ref_frame_check, ref_vocoder_check, built from
+"""Writes tests/golden/ref_frame_small.npz, ref_vocoder_small.npz, ref_talker_small.npz: outputs of the reference
+engine's own frame code, vocoder and talker (oracle/_ref/ref_*_check, built from
 the reference sources by `make -C oracle REF=...`) on the seeded small synthetic model -- one
 frame at KV 10, a set of sampler draws, a set of per-frame seeds, and the PCM of 7 frames
-decoded in chunks of 3 -- so tests/test_reference_pins.py and test_reference_vocoder_pins.py
-can pin the oracle where the reference tree is absent.
+decoded in chunks of 3, and a talker prompt + prefill -- so tests/test_reference_*pins.py can
+pin the oracle where the reference tree is absent.
 
     python tests/golden/make_ref_golden.py
 """
@@ -64,6 +64,14 @@ def main():
         pcm, _ = rf.vocoder_decode(navi, vc, max_chunk=3)
         np.savez_compressed(os.path.join(HERE, "ref_vocoder_small.npz"), codes=vc, max_chunk=3, pcm=pcm)
         print("wrote ref_vocoder_small.npz;", pcm.size, "samples")
+        from test_reference_talker_pins import prompt_ids
+        ids = prompt_ids(W.cfg, 23, 23)
+        spk = np.random.default_rng(24).standard_normal(tl.hidden).astype(np.float32)
+        pre, trail, pad, hid, lg, kv = rf.talker_prefill(navi, ids, "english", spk, (tl.hidden, tl.vocab, tl.n_layer, tl.n_kv_head * tl.head_dim))
+        np.savez_compressed(os.path.join(HERE, "ref_talker_small.npz"), ids=np.array(ids, np.int32), language="english", speaker=spk,
+                            prefill=pre, trailing=trail, tts_pad=pad, hidden=hid, logits=lg, k=np.stack([k for k, _ in kv]),
+                            v=np.stack([v for _, v in kv]))
+        print("wrote ref_talker_small.npz;", pre.shape[0], "prefill rows")
 
 
 if __name__ == "__main__":
