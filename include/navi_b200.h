@@ -215,6 +215,33 @@ const float * navi_frame_step_out(const navi_frame * f);
 int navi_frame_set_step_in(navi_frame * f, const float * d_step);
 /* Frame::grid_blocks / occupancy_per_mp */
 int navi_frame_grid_blocks(const navi_frame * f);
+
+/* ---- batched decode (no counterpart in the reference, which decodes one stream per launch,
+ *      docs/DESIGN.md:35; the per-stream math is Frame::run's, frame.hip:798-810) ----
+ * A frame keeps NAVI_FRAME_SLOTS stream slots, each with its own repetition set and step
+ * embedding; the single-stream calls above use slot 0. navi_frame_run_batch decodes one frame
+ * of nb = 1, 2 or 4 streams in distinct slots in one launch that reads every weight once:
+ * stream i at position n_past[i] of its own KV cache kvs[i], with its own trailing row, seed and
+ * frame index; results[i] gets stream i's codes. Each stream's codes are those of
+ * navi_frame_run on that stream alone, bit for bit; its hidden state and logits agree within
+ * float rounding. KV length per stream is limited by the per-stream attention split
+ * (NAVI_E_KV_FULL beyond it: about 1000 positions at nb = 4, 2000 at nb = 2). */
+#define NAVI_FRAME_SLOTS 4
+int navi_frame_reset_slot(navi_frame * f, int slot);
+/* Frame 0 of the stream in `slot` (navi_frame_run_first for that slot). */
+int navi_frame_run_first_slot(navi_frame * f, int slot, const float * d_hidden, const float * d_logits, const float * d_trailing,
+                              const navi_sampling * s, uint64_t seed, int frame_index, navi_frame_result * r);
+int navi_frame_run_batch(navi_frame * f, int nb, const int * slots, navi_kv * const * kvs, const int * n_past,
+                         const float * const * d_trailing, const navi_sampling * s, const uint64_t * seeds, const int * frame_index,
+                         navi_frame_result * results);
+/* Enqueue-only form of navi_frame_run_batch; navi_frame_collect_batch returns its results. */
+int navi_frame_enqueue_batch(navi_frame * f, int nb, const int * slots, navi_kv * const * kvs, const int * n_past,
+                             const float * const * d_trailing, const navi_sampling * s, const uint64_t * seeds, const int * frame_index);
+int navi_frame_collect_batch(navi_frame * f, int nb, navi_frame_result * results);
+const float * navi_frame_step_out_slot(const navi_frame * f, int slot);
+int navi_frame_set_step_in_slot(navi_frame * f, int slot, const float * d_step);
+/* As navi_frame_inspect, for stream `index` of the last launch. */
+int navi_frame_inspect_stream(const navi_frame * f, int index, float * h_hidden, float * h_logits, float * h_clogits);
 void navi_frame_destroy(navi_frame * f);
 
 /* ---- graph: replaces navi::qwen3tts::Graph (model/qwen3tts/graph.h:22-79) ---------------- */

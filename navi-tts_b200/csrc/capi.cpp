@@ -341,6 +341,85 @@ int navi_frame_collect(navi_frame * f, navi_frame_result * r) {
     });
 }
 
+int navi_frame_reset_slot(navi_frame * f, int slot) {
+    return guard([&]() -> int {
+        if (!f) return set_err(NAVI_E_ARG, "NULL frame");
+        f->f->reset(slot);
+        return NAVI_OK;
+    });
+}
+
+int navi_frame_run_first_slot(navi_frame * f, int slot, const float * d_hidden, const float * d_logits, const float * d_trailing,
+                              const navi_sampling * s, uint64_t seed, int frame_index, navi_frame_result * r) {
+    return guard([&]() -> int {
+        if (!f || !d_hidden || !d_logits || !d_trailing) return set_err(NAVI_E_ARG, "NULL argument");
+        const auto res = f->f->run_first(d_hidden, d_logits, d_trailing, to_sampling(s), seed, frame_index, slot);
+        to_result(res, r);
+        return res.ok ? NAVI_OK : set_err(res.status, res.error);
+    });
+}
+
+int navi_frame_enqueue_batch(navi_frame * f, int nb, const int * slots, navi_kv * const * kvs, const int * n_past,
+                             const float * const * d_trailing, const navi_sampling * s, const uint64_t * seeds, const int * frame_index) {
+    return guard([&]() -> int {
+        if (!f || !slots || !kvs || !n_past || !d_trailing || !seeds || !frame_index) return set_err(NAVI_E_ARG, "NULL argument");
+        if (nb < 1 || nb > navi::qwen3tts::Frame::MAX_SLOTS) return set_err(NAVI_E_ARG, "stream count out of range");
+        navi::qwen3tts::KvCache k[navi::qwen3tts::Frame::MAX_SLOTS];
+        navi::qwen3tts::KvCache * kp[navi::qwen3tts::Frame::MAX_SLOTS];
+        for (int i = 0; i < nb; ++i) {
+            if (!kvs[i]) return set_err(NAVI_E_ARG, "NULL KV cache");
+            k[i] = as_kv(kvs[i]);
+            kp[i] = &k[i];
+        }
+        std::string err;
+        const int st = f->f->enqueue_batch(nb, slots, kp, n_past, d_trailing, to_sampling(s), seeds, frame_index, err);
+        if (st != NAVI_OK) return set_err(st, err);
+        for (int i = 0; i < nb; ++i) kvs[i]->n_used = k[i].n_used;
+        return NAVI_OK;
+    });
+}
+
+int navi_frame_collect_batch(navi_frame * f, int nb, navi_frame_result * results) {
+    return guard([&]() -> int {
+        if (!f || !results) return set_err(NAVI_E_ARG, "NULL argument");
+        if (nb < 1 || nb > navi::qwen3tts::Frame::MAX_SLOTS) return set_err(NAVI_E_ARG, "stream count out of range");
+        navi::qwen3tts::FrameResult res[navi::qwen3tts::Frame::MAX_SLOTS];
+        f->f->collect_batch(res);
+        int st = NAVI_OK;
+        for (int i = 0; i < nb; ++i) {
+            to_result(res[i], &results[i]);
+            if (!res[i].ok && st == NAVI_OK) st = set_err(res[i].status, res[i].error);
+        }
+        return st;
+    });
+}
+
+int navi_frame_run_batch(navi_frame * f, int nb, const int * slots, navi_kv * const * kvs, const int * n_past,
+                         const float * const * d_trailing, const navi_sampling * s, const uint64_t * seeds, const int * frame_index,
+                         navi_frame_result * results) {
+    const int st = navi_frame_enqueue_batch(f, nb, slots, kvs, n_past, d_trailing, s, seeds, frame_index);
+    if (st != NAVI_OK) return st;
+    return navi_frame_collect_batch(f, nb, results);
+}
+
+const float * navi_frame_step_out_slot(const navi_frame * f, int slot) { return f ? f->f->d_step_out(slot) : nullptr; }
+
+int navi_frame_set_step_in_slot(navi_frame * f, int slot, const float * d_step) {
+    return guard([&]() -> int {
+        if (!f || !d_step) return set_err(NAVI_E_ARG, "NULL argument");
+        f->f->set_step_in(d_step, slot);
+        return NAVI_OK;
+    });
+}
+
+int navi_frame_inspect_stream(const navi_frame * f, int index, float * h_hidden, float * h_logits, float * h_clogits) {
+    return guard([&]() -> int {
+        if (!f) return set_err(NAVI_E_ARG, "NULL frame");
+        f->f->inspect(h_hidden, h_logits, h_clogits, index);
+        return NAVI_OK;
+    });
+}
+
 const float * navi_frame_step_out(const navi_frame * f) { return f ? f->f->d_step_out() : nullptr; }
 
 int navi_frame_set_step_in(navi_frame * f, const float * d_step) {

@@ -170,6 +170,11 @@ __device__ __forceinline__ void ll_store(uint64_t * p, float v, uint32_t tag) {
     const uint64_t w = (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
     asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+__device__ __forceinline__ uint64_t ll_load1(const uint64_t * p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
 // Two adjacent exchange words (16-byte aligned) in one load; each 64-bit element is
 // single-copy atomic on its own.
 __device__ __forceinline__ void ll_load2(const uint64_t * p, uint64_t & a, uint64_t & b) {

@@ -62,25 +62,31 @@ struct Frame::Impl {
     Phase * prog_full = nullptr;
     Phase * prog_first = nullptr;
     Phase * prog_layers = nullptr;   // [TL][LAYER_PHASES]: one talker layer alone, then XOUT
+    Phase * prog_batch[MAX_B + 1] = {};   // batched programs of 2 and 4 streams
+    int n_batch[MAX_B + 1] = {};
+    int thead_phase[MAX_B + 1] = {};
+    int sample_phase[MAX_B + 1][NCB] = {};
     int n_full = 0, n_first = 0;
     Work w{};
     float * inv_t = nullptr, * inv_c = nullptr;
     std::vector<float> inv_t_h, inv_c_h;   // host copies (RoPE tables)
     float * rope_c = nullptr;               // [NCB][HD] code-predictor cos | sin at positions 0..15
-    float * step[2] = {nullptr, nullptr};
-    int cur = 0;
+    float * step[MAX_B][2] = {};   // per slot: the step embedding a frame reads and the one it writes
+    int cur[MAX_B] = {};
+    uint8_t * seen = nullptr;       // [MAX_B][TV] per slot
+    int last_nb = 1;
     uint32_t tag = 0;
     uint32_t last_tag = 0;
     bool pending = false;
     int grid = 0;
-    uint32_t ring = 0, scratch_floats = 0, part_floats = 0, smem = 0;
+    uint32_t scratch_floats = 0;
     int cp_keep_layers = 0;   // code-predictor layers held in L2 by cache policy
     uint64_t timeout_ns = 0;
     int eos = 0, suppress_from = 0;
     size_t ll_bytes = 0;
     uint64_t * ll_base = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-    int32_t * h_out = nullptr;   // pinned: 16 codes + 4 control words
+    int32_t * h_out = nullptr;   // pinned: MAX_B x 16 codes + 4 control words
     unsigned long long * prof = nullptr;
     bool prof_on = false;
     int prof_cta = 0;
@@ -95,29 +101,59 @@ struct Frame::Impl {
         return static_cast<T *>(p);
     }
 
-    // Talker attention: every KV head's cached positions in `split` ranges of `chunk`
-    // positions (at least 8 per split, at most grid / NKV splits per head), one range per CTA.
-    void attn_plan(int n_past, int & split, int & chunk) const {
-        const int per_head = std::max(1, std::min(MAX_SPLIT, grid / d.NKV));
-        split = std::min(per_head, std::max(1, cdiv(n_past, 8)));
+    // Talker attention of a stream: its KV head's cached positions in `split` ranges of
+    // `chunk` positions (at least 8 per split, at most `per` splits), one range per CTA.
+    static void attn_plan(int n_past, int per, int & split, int & chunk) {
+        split = std::min(per, std::max(1, cdiv(n_past, 8)));
         chunk = std::max(1, cdiv(n_past, split));
         split = std::max(1, cdiv(n_past, chunk));
     }
 
+    // One stream of a launch.
+    struct StreamIn {
+        int slot = 0;
+        const float * step_in = nullptr;   // null: the slot's own step embedding
+        const float * trailing = nullptr;
+        KvCache * kv = nullptr;
+        int n_past = 0;
+        uint64_t seed = 0;
+        int frame_index = 0;
+    };
+
     static constexpr int LAYER_PHASES = 6;
 
-    // layer >= 0: the single-layer program of that talker layer, from step_in into layer_out
-    int launch(const float * step_in, const float * hidden_in, const float * logits_in, const float * trailing, KvCache * kv,
-               int n_past, const Sampling & s, uint64_t seed, int frame_index, std::string & err, int layer = -1,
-               float * layer_out = nullptr) {
+    // Per-mode launch shape: streams nb -> shared-memory layout and ring.
+    struct Mode {
+        int xcols = 2, cp_slots = 1;
+        uint32_t part_floats = 0, ring = 0, smem = 0;
+    };
+    Mode modes[MAX_B + 1];
+
+    // layer >= 0: the single-layer program of that talker layer, from step_in into layer_out.
+    // hidden_in / logits_in: frame 0 of one stream (the code predictor only).
+    int launch(const StreamIn * in, int nb, const float * hidden_in, const float * logits_in, const Sampling & s, std::string & err,
+               int layer = -1, float * layer_out = nullptr) {
         NAVI_CUDA(cudaSetDevice(ordinal));
         Args A{};
         const bool first = hidden_in != nullptr;
-        A.prog = layer >= 0 ? prog_layers + static_cast<size_t>(layer) * LAYER_PHASES : first ? prog_first : prog_full;
-        A.nphase = layer >= 0 ? LAYER_PHASES : first ? n_first : n_full;
+        if (nb == 1) {
+            A.prog = layer >= 0 ? prog_layers + static_cast<size_t>(layer) * LAYER_PHASES : first ? prog_first : prog_full;
+            A.nphase = layer >= 0 ? LAYER_PHASES : first ? n_first : n_full;
+        } else {
+            A.prog = prog_batch[nb];
+            A.nphase = n_batch[nb];
+            A.thead_phase = thead_phase[nb];
+            for (int cb = 0; cb < NCB; ++cb) A.sample_phase[cb] = sample_phase[nb][cb];
+        }
         A.mw = dmw;
         A.d = d;
         A.w = w;
+        A.grid = grid;
+        A.nb = nb;
+        const Mode & M = modes[nb];
+        A.xcols = M.xcols;
+        A.cp_slots = M.cp_slots;
+        A.attn_per = std::max(1, std::min(MAX_SPLIT, grid / (d.NKV * nb)));
         if (tag > 0xF0000000u) {   // tags about to wrap: clear every exchange word once
             NAVI_CUDA(cudaMemsetAsync(ll_base, 0, ll_bytes, stream));
             NAVI_CUDA(cudaMemsetAsync(w.ctl, 0, 16, stream));
@@ -125,89 +161,109 @@ struct Frame::Impl {
         }
         tag += 4096;
         A.tag_base = tag;
-        A.n_past = n_past;
-        attn_plan(n_past, A.attn_split, A.attn_chunk);
-        if (!first) {
-            if (A.attn_chunk + 1 > MAX_ATTN_CHUNK + 1) {
-                err = "KV length " + std::to_string(n_past) + " needs " + std::to_string(A.attn_chunk) +
-                      " positions per attention split; the kernel takes at most " + std::to_string(MAX_ATTN_CHUNK);
-                return NAVI_E_KV_FULL;
+        for (int i = 0; i < nb; ++i) {
+            const StreamIn & q = in[i];
+            A.n_past[i] = q.n_past;
+            attn_plan(q.n_past, A.attn_per, A.attn_split[i], A.attn_chunk[i]);
+            if (!first) {
+                if (A.attn_chunk[i] + 1 > MAX_ATTN_CHUNK + 1) {
+                    err = "KV length " + std::to_string(q.n_past) + " needs " + std::to_string(A.attn_chunk[i]) +
+                          " positions per attention split; the kernel takes at most " + std::to_string(MAX_ATTN_CHUNK);
+                    return NAVI_E_KV_FULL;
+                }
+                const uint64_t kvb = 2ull * A.attn_chunk[i] * d.HD * 2 + 2ull * d.HD * 4;
+                if (kvb > M.ring) {
+                    err = "KV length " + std::to_string(q.n_past) + " needs " + std::to_string(kvb) + "-byte attention slices; the ring holds " +
+                          std::to_string(M.ring);
+                    return NAVI_E_KV_FULL;
+                }
             }
-            const uint64_t kvb = 2ull * A.attn_chunk * d.HD * 2 + 2ull * d.HD * 4;
-            if (kvb > ring) {
-                err = "KV length " + std::to_string(n_past) + " needs " + std::to_string(kvb) + "-byte attention slices; the ring holds " +
-                      std::to_string(ring);
-                return NAVI_E_KV_FULL;
-            }
+            const int sl = q.slot;
+            A.step_in[i] = q.step_in ? q.step_in : step[sl][cur[sl]];
+            A.trailing[i] = q.trailing;
+            A.step_out[i] = layer >= 0 ? layer_out : step[sl][cur[sl] ^ 1];
+            A.seen[i] = seen + static_cast<size_t>(sl) * d.TV;
+            if (q.kv)
+                for (int l = 0; l < d.TL; ++l) {
+                    A.kc[i][l] = reinterpret_cast<__half *>(q.kv->k[l]);
+                    A.vc[i][l] = reinterpret_cast<__half *>(q.kv->v[l]);
+                }
+            if (!first) rope_row(inv_t_h, q.n_past, A.rope_t[i]);
+            A.seed[i] = q.seed;
+            A.frame_index[i] = q.frame_index;
+            for (int cb = 0; cb < NCB; ++cb) A.pcg_seed[i][cb] = navi::dev::pcg_draw_seed(q.seed, q.frame_index, cb);
         }
-        A.step_in = step_in;
         A.hidden_in = hidden_in;
         A.logits_in = logits_in;
-        A.trailing = trailing;
-        const int out = cur ^ 1;
-        A.step_out = layer >= 0 ? layer_out : step[out];
-        if (kv) {
-            for (int l = 0; l < d.TL; ++l) {
-                A.kc[l] = reinterpret_cast<__half *>(kv->k[l]);
-                A.vc[l] = reinterpret_cast<__half *>(kv->v[l]);
-            }
-        }
         A.inv_freq_t = inv_t;
         A.inv_freq_c = inv_c;
         A.rope_c = rope_c;
-        if (!first) rope_row(inv_t_h, n_past, A.rope_t);
         A.temp = s.temperature; A.top_p = s.top_p; A.rep = s.repetition_penalty; A.top_k = s.top_k;
         A.cp_temp = s.cp_temperature; A.cp_top_p = s.cp_top_p; A.cp_top_k = s.cp_top_k;
-        A.min_frames = s.min_frames; A.rng = s.rng; A.seed = seed; A.frame_index = frame_index;
-        for (int cb = 0; cb < NCB; ++cb) A.pcg_seed[cb] = navi::dev::pcg_draw_seed(seed, frame_index, cb);
+        A.min_frames = s.min_frames; A.rng = s.rng;
         A.eos_id = eos;
         A.suppress_from = suppress_from;
         A.timeout_ns = timeout_ns;
-        A.ring_bytes = ring;
+        A.ring_bytes = M.ring;
         A.cp_keep_layers = cp_keep_layers;
         A.scratch_floats = scratch_floats;
-        A.part_floats = part_floats;
+        A.part_floats = M.part_floats;
         A.prof = prof_on ? prof : nullptr;
         if (prof_on) NAVI_CUDA(cudaMemsetAsync(prof, 0, static_cast<size_t>(PROF_STRIDE) * grid * sizeof(unsigned long long), stream));
         A.prof_cta = prof_cta;
         last_nphase = A.nphase;
         NAVI_CUDA(cudaEventRecord(ev0, stream));
         void * args[] = {&A};
-        const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(&k_frame), dim3(grid), dim3(NTHR), args, smem, stream);
+        const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(&k_frame), dim3(grid), dim3(NTHR), args, M.smem, stream);
         if (e != cudaSuccess) {
             (void) cudaGetLastError();
             err = std::string("cooperative launch failed: ") + cudaGetErrorString(e);
             return NAVI_E_LAUNCH;
         }
         NAVI_CUDA(cudaEventRecord(ev1, stream));
-        NAVI_CUDA(cudaMemcpyAsync(h_out, w.codes, NCB * sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
-        NAVI_CUDA(cudaMemcpyAsync(h_out + NCB, w.ctl, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
-        if (layer < 0) cur = out;
+        NAVI_CUDA(cudaMemcpyAsync(h_out, w.codes, static_cast<size_t>(nb) * NCB * sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
+        NAVI_CUDA(cudaMemcpyAsync(h_out + MAX_B * NCB, w.ctl, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
+        if (layer < 0)
+            for (int i = 0; i < nb; ++i) cur[in[i].slot] ^= 1;
         last_tag = tag;
+        last_nb = nb;
         pending = true;
         return NAVI_OK;
     }
 
-    FrameResult collect() {
-        FrameResult r;
-        if (!pending) { r.status = NAVI_E_ARG; r.error = "no frame enqueued"; return r; }
+    // Results of the last launch, one per stream (out[0..last_nb)).
+    void collect(FrameResult * out) {
+        const int nb = std::max(1, last_nb);
+        if (!pending) {
+            for (int i = 0; i < nb; ++i) { out[i] = FrameResult{}; out[i].status = NAVI_E_ARG; out[i].error = "no frame enqueued"; }
+            return;
+        }
         pending = false;
         NAVI_CUDA(cudaSetDevice(ordinal));
         NAVI_CUDA(cudaStreamSynchronize(stream));
         float ms = 0.f;
         NAVI_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
-        r.us = ms * 1000.0;
-        const uint32_t * ctl = reinterpret_cast<const uint32_t *>(h_out + NCB);
-        if (ctl[2] == last_tag || ctl[0] != last_tag) {
-            r.status = NAVI_E_TIMEOUT;
-            r.error = "device wait timed out in phase " + std::to_string(ctl[1]) + " (CTA " + std::to_string(ctl[3]) +
-                      "): the cooperative grid could not run to completion";
-            return r;
+        const uint32_t * ctl = reinterpret_cast<const uint32_t *>(h_out + MAX_B * NCB);
+        const bool failed = ctl[2] == last_tag || ctl[0] != last_tag;
+        for (int i = 0; i < nb; ++i) {
+            FrameResult & r = out[i];
+            r = FrameResult{};
+            r.us = ms * 1000.0;
+            if (failed) {
+                r.status = NAVI_E_TIMEOUT;
+                r.error = "device wait timed out in phase " + std::to_string(ctl[1]) + " (CTA " + std::to_string(ctl[3]) +
+                          "): the cooperative grid could not run to completion";
+                continue;
+            }
+            std::memcpy(r.codes, h_out + i * NCB, sizeof(r.codes));
+            r.eos = r.codes[0] == eos;
+            r.ok = true;
         }
-        std::memcpy(r.codes, h_out, sizeof(r.codes));
-        r.eos = r.codes[0] == eos;
-        r.ok = true;
-        return r;
+    }
+    FrameResult collect() {
+        FrameResult r[MAX_B];
+        collect(r);
+        return r[0];
     }
 };
 
@@ -331,11 +387,40 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     I.prog_first = I.alloc<Phase>(p0.size());
     NAVI_CUDA(cudaMemcpy(I.prog_full, pf.data(), pf.size() * sizeof(Phase), cudaMemcpyHostToDevice));
     NAVI_CUDA(cudaMemcpy(I.prog_first, p0.data(), p0.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+    // batched programs (nb streams, one input column each): the talker step, THEAD (which also
+    // publishes every stream's post-norm hidden), the codebook-0 draws (SAMPLE: CTA s draws
+    // stream s), code-predictor position 0 on the hidden, then for positions 1..15 the pass on
+    // the embedding of the code drawn last, its head and the draw; FINAL assembles the step
+    // embeddings from the published codes
+    for (int nb : {2, 4}) {
+        std::vector<Phase> v;
+        const uint8_t c = static_cast<uint8_t>(nb);
+        for (int l = 0; l < d.TL; ++l)
+            for (uint8_t op : {TQKV, TATTN, TO, TGU, TDOWN}) v.push_back({op, c, static_cast<uint8_t>(l), 0});
+        I.thead_phase[nb] = static_cast<int>(v.size());
+        v.push_back({THEAD, c, 0, 0});
+        I.sample_phase[nb][0] = static_cast<int>(v.size());
+        v.push_back({SAMPLE, c, 0, 0});
+        for (int pos = 0; pos < NCB; ++pos) {
+            for (int l = 0; l < d.CL; ++l)
+                for (uint8_t op : {CQKV, CATTN, CO, CGU, CDOWN}) v.push_back({op, c, static_cast<uint8_t>(l), static_cast<uint8_t>(pos)});
+            if (pos == 0) continue;
+            v.push_back({CHEAD, c, 0, static_cast<uint8_t>(pos)});
+            I.sample_phase[nb][pos] = static_cast<int>(v.size());
+            v.push_back({SAMPLE, c, 0, static_cast<uint8_t>(pos)});
+        }
+        v.push_back({FINAL, c, 0, 0});
+        if (v.size() >= 4096) fail("frame: batched phase program too long", NAVI_E_SHAPE);
+        I.n_batch[nb] = static_cast<int>(v.size());
+        I.prog_batch[nb] = I.alloc<Phase>(v.size());
+        NAVI_CUDA(cudaMemcpy(I.prog_batch[nb], v.data(), v.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+    }
 
     // exchange words (one allocation, cleared when tags wrap)
-    const size_t n_x = 2ull * d.H, n_qkv = 2ull * d.QKV, n_attn = 2ull * d.Q, n_h = 2ull * d.F, n_lg = d.TV,
-                 n_clg = static_cast<size_t>(NCB - 1) * d.CV, n_part = static_cast<size_t>(MAX_SPLIT) * d.NH * (d.HD + 2);
-    const size_t n_ll = n_x + n_qkv + n_attn + n_h + n_lg + n_clg + n_part;
+    const size_t n_x = 1ull * MAXC * d.H, n_qkv = 1ull * MAXC * d.QKV, n_attn = 1ull * MAXC * d.Q, n_h = 1ull * MAXC * d.F,
+                 n_lg = 1ull * MAX_B * d.TV, n_clg = static_cast<size_t>(MAX_B) * (NCB - 1) * d.CV,
+                 n_part = static_cast<size_t>(MAX_SPLIT) * d.NH * (d.HD + 2), n_hid = 1ull * MAX_B * d.H, n_code = 1ull * MAX_B * NCB;
+    const size_t n_ll = n_x + n_qkv + n_attn + n_h + n_lg + n_clg + n_part + n_hid + n_code;
     I.ll_base = I.alloc<uint64_t>(n_ll);
     I.ll_bytes = n_ll * sizeof(uint64_t);
     uint64_t * q = I.ll_base;
@@ -345,13 +430,17 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     I.w.h = q; q += n_h;
     I.w.logits = q; q += n_lg;
     I.w.clogits = q; q += n_clg;
-    I.w.part = q;
-    I.w.seen = I.alloc<uint8_t>(d.TV);
-    I.w.codes = I.alloc<int32_t>(NCB);
-    I.w.hidden = I.alloc<float>(d.H);
+    I.w.part = q; q += n_part;
+    I.w.hid_x = q; q += n_hid;
+    I.w.code_x = q;
+    I.seen = I.alloc<uint8_t>(static_cast<size_t>(MAX_B) * d.TV);
+    I.w.codes = I.alloc<int32_t>(static_cast<size_t>(MAX_B) * NCB);
+    I.w.hidden = I.alloc<float>(static_cast<size_t>(MAX_B) * d.H);
     I.w.ctl = I.alloc<unsigned>(4);
-    I.step[0] = I.alloc<float>(d.H);
-    I.step[1] = I.alloc<float>(d.H);
+    for (int sl = 0; sl < MAX_B; ++sl) {
+        I.step[sl][0] = I.alloc<float>(d.H);
+        I.step[sl][1] = I.alloc<float>(d.H);
+    }
     // RoPE inverse frequencies theta^(-2t/hd), computed in double, stored as f32
     auto inv = [&](double theta, std::vector<float> & v) {
         v.resize(d.HD / 2);
@@ -371,7 +460,7 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
 
     // shared memory: everything but the ring is sized from the shapes; the ring takes the rest
     const int G = I.grid, Vmax = std::max(d.TV, d.CV);
-    const uint32_t xin = 2u * std::max(d.H, std::max(d.Q, d.F));
+    const uint32_t xin = static_cast<uint32_t>(MAXC) * std::max(d.H, std::max(d.Q, d.F));
     const uint32_t samp = navi::dev::sample_scratch_floats(Vmax);
     // attention scratch: code predictor [q, k, v, scores, m/l, per-warp P.V]; talker split
     // [q, k, v, new K/V row, m/l, per-warp P.V, scores]; talker combine [splits][m, l, acc]
@@ -382,18 +471,28 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
                                    static_cast<uint32_t>(std::min(MAX_SPLIT, I.grid / d.NKV) * (d.HD + 2))});
     I.scratch_floats = std::max(xin, std::max(samp, att));
     const int max_nr = std::max({cdiv(d.QKV, G), cdiv(d.H, G), cdiv(d.F, G), cdiv(d.TV, G), cdiv(d.CV, G)});
-    I.part_floats = static_cast<uint32_t>(NCW * 4 * max_nr);
-    const SmemLayout L0 = smem_layout(d, 0, I.scratch_floats, I.part_floats);
     const uint32_t optin = static_cast<uint32_t>(dev.info().smem_optin);
-    if (L0.total + 16384 > optin) fail("frame: shared memory too small for the model shape", NAVI_E_SHAPE);
-    I.ring = (optin - L0.total) / 128 * 128;
     const uint32_t H4 = 4u * d.H;
     const uint32_t max_chunk = std::max({H4 + static_cast<uint32_t>(cdiv(d.QKV, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.H, G) * d.Q * 2),
                                          H4 + static_cast<uint32_t>(2 * cdiv(d.F, G) * d.H * 2), static_cast<uint32_t>(cdiv(d.H, G) * d.F * 2),
                                          H4 + static_cast<uint32_t>(cdiv(d.TV, G) * d.H * 2), H4 + static_cast<uint32_t>(cdiv(d.CV, G) * d.H * 2),
                                          static_cast<uint32_t>(2 * 8 * d.HD * 2 + 2 * d.HD * 4)});
-    if (max_chunk > I.ring) fail("frame: a phase's weight slice does not fit the shared-memory ring", NAVI_E_SHAPE);
-    I.smem = smem_layout(d, I.ring, I.scratch_floats, I.part_floats).total;
+    // per stream count: the residual columns and code-predictor K/V slots in shared memory, and
+    // the ring that takes the rest
+    uint32_t smem_max = 0;
+    for (int nb : {1, 2, 4}) {
+        Impl::Mode & M = I.modes[nb];
+        M.xcols = std::max(2, nb);
+        M.cp_slots = cdiv(nb * d.CL * d.NKV, G);
+        M.part_floats = static_cast<uint32_t>(NCW * 2 * M.xcols * max_nr);   // per warp: columns x (gate, up) x rows
+        if (nb * d.NKV > G) fail("frame: batched attention needs a CTA per (stream, KV head)", NAVI_E_SHAPE);
+        const SmemLayout L0 = smem_layout(d, 0, I.scratch_floats, M.part_floats, M.xcols, M.cp_slots);
+        if (L0.total + 16384 > optin) fail("frame: shared memory too small for the model shape", NAVI_E_SHAPE);
+        M.ring = (optin - L0.total) / 128 * 128;
+        if (max_chunk > M.ring) fail("frame: a phase's weight slice does not fit the shared-memory ring", NAVI_E_SHAPE);
+        M.smem = smem_layout(d, M.ring, I.scratch_floats, M.part_floats, M.xcols, M.cp_slots).total;
+        smem_max = std::max(smem_max, M.smem);
+    }
     // The code predictor's weights are read 15 times a frame; as many whole layers as fit in
     // about 70% of L2 are marked evict-last (NAVI_L2_KEEP_LAYERS overrides the count).
     {
@@ -403,14 +502,14 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
         if (const char * env = std::getenv("NAVI_L2_KEEP_LAYERS")) keep = std::atoi(env);
         I.cp_keep_layers = std::max(0, std::min(keep, d.CL));
     }
-    NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_frame), cudaFuncAttributeMaxDynamicSharedMemorySize, I.smem));
+    NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_frame), cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
     int occ = 0;
-    NAVI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, reinterpret_cast<const void *>(&k_frame), NTHR, I.smem));
-    if (occ < 1) fail("frame: k_frame cannot be resident with " + std::to_string(I.smem) + " bytes of shared memory", NAVI_E_SHAPE);
+    NAVI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, reinterpret_cast<const void *>(&k_frame), NTHR, smem_max));
+    if (occ < 1) fail("frame: k_frame cannot be resident with " + std::to_string(smem_max) + " bytes of shared memory", NAVI_E_SHAPE);
     NAVI_CUDA(cudaEventCreate(&I.ev0));
     NAVI_CUDA(cudaEventCreate(&I.ev1));
     void * h = nullptr;
-    NAVI_CUDA(cudaMallocHost(&h, (NCB + 4) * sizeof(int32_t)));
+    NAVI_CUDA(cudaMallocHost(&h, (MAX_B * NCB + 4) * sizeof(int32_t)));
     I.h_out = static_cast<int32_t *>(h);
     return f;
 }
@@ -425,28 +524,62 @@ Frame::~Frame() {
     for (void * p : impl_->owned) cudaFree(p);
 }
 
-void Frame::reset() {
-    NAVI_CUDA(cudaSetDevice(impl_->ordinal));
-    NAVI_CUDA(cudaMemsetAsync(impl_->w.seen, 0, static_cast<size_t>(impl_->d.TV), impl_->stream));
+void Frame::reset(int slot) {
+    Impl & I = *impl_;
+    if (slot < 0 || slot >= MAX_B) fail("frame: slot out of range", NAVI_E_ARG);
+    NAVI_CUDA(cudaSetDevice(I.ordinal));
+    NAVI_CUDA(cudaMemsetAsync(I.seen + static_cast<size_t>(slot) * I.d.TV, 0, static_cast<size_t>(I.d.TV), I.stream));
 }
 
 FrameResult Frame::run_first(const float * d_hidden, const float * d_logits, const float * d_trailing, const Sampling & s,
-                             uint64_t seed, int frame_index) {
+                             uint64_t seed, int frame_index, int slot) {
     Impl & I = *impl_;
+    FrameResult r;
+    if (slot < 0 || slot >= MAX_B) { r.status = NAVI_E_ARG; r.error = "slot out of range"; return r; }
     std::string err;
-    const int st = I.launch(nullptr, d_hidden, d_logits, d_trailing, nullptr, 0, s, seed, frame_index, err);
-    if (st != NAVI_OK) { FrameResult r; r.status = st; r.error = err; return r; }
+    Impl::StreamIn in;
+    in.slot = slot;
+    in.trailing = d_trailing;
+    in.seed = seed;
+    in.frame_index = frame_index;
+    const int st = I.launch(&in, 1, d_hidden, d_logits, s, err);
+    if (st != NAVI_OK) { r.status = st; r.error = err; return r; }
     return I.collect();
 }
 
+int Frame::enqueue_batch(int nb, const int * slots, KvCache * const * kvs, const int * n_past, const float * const * d_trailing,
+                         const Sampling & s, const uint64_t * seeds, const int * frame_index, std::string & err) {
+    Impl & I = *impl_;
+    if (nb != 1 && nb != 2 && nb != 4) { err = "a batched frame takes 1, 2 or 4 streams"; return NAVI_E_ARG; }
+    Impl::StreamIn in[MAX_B];
+    bool used[MAX_B] = {};
+    for (int i = 0; i < nb; ++i) {
+        KvCache & kv = *kvs[i];
+        if (slots[i] < 0 || slots[i] >= MAX_B || used[slots[i]]) { err = "stream slots must be distinct, in 0.." + std::to_string(MAX_B - 1); return NAVI_E_ARG; }
+        used[slots[i]] = true;
+        if (n_past[i] < 0 || n_past[i] >= kv.max_pos) { err = "KV cache full"; return NAVI_E_KV_FULL; }
+        if (kv.n_layer != I.d.TL || kv.kv_dim != I.d.KV) { err = "KV cache layout does not match the talker"; return NAVI_E_ARG; }
+        if (!d_trailing[i]) { err = "NULL trailing row"; return NAVI_E_ARG; }
+        in[i].slot = slots[i];
+        in[i].trailing = d_trailing[i];
+        in[i].kv = &kv;
+        in[i].n_past = n_past[i];
+        in[i].seed = seeds[i];
+        in[i].frame_index = frame_index[i];
+    }
+    const int st = I.launch(in, nb, nullptr, nullptr, s, err);
+    if (st == NAVI_OK)
+        for (int i = 0; i < nb; ++i) kvs[i]->n_used = n_past[i] + 1;
+    return st;
+}
+
+void Frame::collect_batch(FrameResult * out) { impl_->collect(out); }
+
 int Frame::enqueue(KvCache & kv, int n_past, const float * d_trailing, const Sampling & s, uint64_t seed, int frame_index,
                    std::string & err) {
-    Impl & I = *impl_;
-    if (n_past < 0 || n_past >= kv.max_pos) { err = "KV cache full"; return NAVI_E_KV_FULL; }
-    if (kv.n_layer != I.d.TL || kv.kv_dim != I.d.KV) { err = "KV cache layout does not match the talker"; return NAVI_E_ARG; }
-    const int st = I.launch(I.step[I.cur], nullptr, nullptr, d_trailing, &kv, n_past, s, seed, frame_index, err);
-    if (st == NAVI_OK) kv.n_used = n_past + 1;
-    return st;
+    const int slot = 0;
+    KvCache * k = &kv;
+    return enqueue_batch(1, &slot, &k, &n_past, &d_trailing, s, &seed, &frame_index, err);
 }
 
 FrameResult Frame::run(KvCache & kv, int n_past, const float * d_trailing, const Sampling & s, uint64_t seed, int frame_index) {
@@ -464,19 +597,28 @@ FrameResult Frame::run_layer(int layer, const float * d_x, KvCache & kv, int n_p
     if (n_past < 0 || n_past >= kv.max_pos) { r.status = NAVI_E_KV_FULL; r.error = "KV cache full"; return r; }
     if (kv.n_layer != I.d.TL || kv.kv_dim != I.d.KV) { r.status = NAVI_E_ARG; r.error = "KV cache layout does not match the talker"; return r; }
     std::string err;
-    const int st = I.launch(d_x, nullptr, nullptr, nullptr, &kv, n_past, Sampling{}, 0, 0, err, layer, d_out);
+    Impl::StreamIn in;
+    in.step_in = d_x;
+    in.kv = &kv;
+    in.n_past = n_past;
+    const int st = I.launch(&in, 1, nullptr, nullptr, Sampling{}, err, layer, d_out);
     if (st != NAVI_OK) { r.status = st; r.error = err; return r; }
     return I.collect();
 }
 
 FrameResult Frame::collect() { return impl_->collect(); }
 
-const float * Frame::d_step_out() const { return impl_->step[impl_->cur]; }
+const float * Frame::d_step_out(int slot) const {
+    if (slot < 0 || slot >= MAX_B) return nullptr;
+    return impl_->step[slot][impl_->cur[slot]];
+}
 
-void Frame::set_step_in(const float * d_step) {
+void Frame::set_step_in(const float * d_step, int slot) {
     Impl & I = *impl_;
+    if (slot < 0 || slot >= MAX_B) fail("frame: slot out of range", NAVI_E_ARG);
     NAVI_CUDA(cudaSetDevice(I.ordinal));
-    NAVI_CUDA(cudaMemcpyAsync(I.step[I.cur], d_step, static_cast<size_t>(I.d.H) * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+    NAVI_CUDA(cudaMemcpyAsync(I.step[slot][I.cur[slot]], d_step, static_cast<size_t>(I.d.H) * sizeof(float), cudaMemcpyDeviceToDevice,
+                              I.stream));
 }
 
 int Frame::grid_blocks() const { return impl_->grid; }
@@ -508,11 +650,14 @@ int Frame::profile(uint64_t * out, int cap) const {
     return n;
 }
 
-void Frame::inspect(float * hidden, float * logits, float * clogits) const {
+void Frame::inspect(float * hidden, float * logits, float * clogits, int index) const {
     const Impl & I = *impl_;
+    if (index < 0 || index >= MAX_B) fail("frame: stream index out of range", NAVI_E_ARG);
     NAVI_CUDA(cudaSetDevice(I.ordinal));
     NAVI_CUDA(cudaStreamSynchronize(I.stream));
-    if (hidden) NAVI_CUDA(cudaMemcpy(hidden, I.w.hidden, static_cast<size_t>(I.d.H) * sizeof(float), cudaMemcpyDeviceToHost));
+    if (hidden)
+        NAVI_CUDA(cudaMemcpy(hidden, I.w.hidden + static_cast<size_t>(index) * I.d.H, static_cast<size_t>(I.d.H) * sizeof(float),
+                             cudaMemcpyDeviceToHost));
     auto unpack = [](const uint64_t * src, size_t n, float * dst) {
         std::vector<uint64_t> tmp(n);
         NAVI_CUDA(cudaMemcpy(tmp.data(), src, n * sizeof(uint64_t), cudaMemcpyDeviceToHost));
@@ -521,8 +666,8 @@ void Frame::inspect(float * hidden, float * logits, float * clogits) const {
             std::memcpy(&dst[i], &b, 4);
         }
     };
-    if (logits) unpack(I.w.logits, static_cast<size_t>(I.d.TV), logits);
-    if (clogits) unpack(I.w.clogits, static_cast<size_t>(NCB - 1) * I.d.CV, clogits);
+    if (logits) unpack(I.w.logits + static_cast<size_t>(index) * I.d.TV, static_cast<size_t>(I.d.TV), logits);
+    if (clogits) unpack(I.w.clogits + static_cast<size_t>(index) * (NCB - 1) * I.d.CV, static_cast<size_t>(NCB - 1) * I.d.CV, clogits);
 }
 
 int Frame::sample(const Device & dev, const float * d_logits, int vocab, const Sampling & s, uint64_t seed, int frame_index,

@@ -48,25 +48,36 @@ public:
     static std::unique_ptr<Frame> create(const Device & dev, const DeviceWeights & w, const FrameOptions & opt = {});
     ~Frame();
 
-    void reset();
+    // The frame keeps MAX_SLOTS stream slots, each with its repetition set and step embedding;
+    // the single-stream calls use slot 0 unless told otherwise.
+    static constexpr int MAX_SLOTS = 4;
+
+    void reset(int slot = 0);
     FrameResult run_first(const float * d_hidden, const float * d_logits, const float * d_trailing, const Sampling & s,
-                          uint64_t seed, int frame_index);
+                          uint64_t seed, int frame_index, int slot = 0);
     FrameResult run(KvCache & kv, int n_past, const float * d_trailing, const Sampling & s, uint64_t seed, int frame_index);
     // launch only; collect() synchronises and returns the last launch's result
     int enqueue(KvCache & kv, int n_past, const float * d_trailing, const Sampling & s, uint64_t seed, int frame_index,
                 std::string & err);
     FrameResult collect();
+    // Batched decode: nb (1, 2 or 4) streams in distinct slots decode one frame each in one
+    // launch that reads every weight once: stream i at position n_past[i] of its own KV cache,
+    // with its own trailing row, seed and frame index. collect_batch fills out[0..nb).
+    int enqueue_batch(int nb, const int * slots, KvCache * const * kvs, const int * n_past, const float * const * d_trailing,
+                      const Sampling & s, const uint64_t * seeds, const int * frame_index, std::string & err);
+    void collect_batch(FrameResult * out);
     // One talker decoder layer alone (the layer phases of the frame: q/k/v, attention over
     // positions [0, n_past) plus the new one, o, gate/up, down) on the f32 input d_x at
     // position n_past, writing the f32 residual stream after the layer to d_out and the
     // layer's K/V row n_past (configs[0]'s single-layer decode step).
     FrameResult run_layer(int layer, const float * d_x, KvCache & kv, int n_past, float * d_out);
 
-    const float * d_step_out() const;
-    void set_step_in(const float * d_step);
+    const float * d_step_out(int slot = 0) const;
+    void set_step_in(const float * d_step, int slot = 0);
     int grid_blocks() const;
-    // host copies of the last frame's talker hidden, logits and code-predictor logits
-    void inspect(float * hidden, float * logits, float * clogits) const;
+    // host copies of the last launch's talker hidden, logits and code-predictor logits of
+    // stream `index` of that launch
+    void inspect(float * hidden, float * logits, float * clogits, int index = 0) const;
     // phase trace of the last launch on CTA `cta` (ns): start, then 4 stamps per phase
     void set_profile(bool on, int cta = 0);
     int profile(uint64_t * out, int cap) const;

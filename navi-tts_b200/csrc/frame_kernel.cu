@@ -9,7 +9,7 @@ struct Ctrl {
     volatile unsigned long long released;   // ring bytes the consumers have freed (monotonic)
     volatile int consumed;                  // chunks the consumers are done with
     volatile int abort;                     // this CTA is unwinding
-    float red[2][NCW];                      // CTA reduction scratch
+    float red[MAXC][NCW];                   // CTA reduction scratch
 };
 
 static_assert(sizeof(Ctrl) <= CTRL_BYTES, "control block outgrows its shared-memory slot");
@@ -20,7 +20,7 @@ struct Sm {
     uint32_t * meta_off;     // physical offset of the chunk's logical byte 0
     uint32_t * meta_split;   // logical offset where the chunk continues at the ring's start
     Ctrl * ctrl;
-    int * codes;
+    int * codes;        // [MAX_B][NCB]
     float * xres;
     float * hid;
     float * part;
@@ -309,6 +309,22 @@ __device__ __forceinline__ bool ll_fetch_cols(const uint64_t * src, int cols, in
     return ll_fetch_plan(src, cols, len, dstride, 1, 0, 0, 0, 0, 0, len, len, tag, dst, A, ctrl, phase);
 }
 
+// One exchange word into v once it carries `tag` (a polling thread of its own; the caller
+// decides with a barrier).
+__device__ __noinline__ bool ll_poll1(const uint64_t * src, uint32_t tag, float & v, const Args & A, Ctrl * ctrl, int phase) {
+    uint64_t t0 = 0;
+    for (uint32_t spins = 0;; ++spins) {
+        const uint64_t w = ll_load1(src);
+        if (tag_of(w) == tag) {
+            v = val_of(w);
+            return true;
+        }
+        if (t0 == 0) t0 = globaltimer();
+        if ((spins & 3u) == 3u && globaltimer() - t0 > A.timeout_ns) { raise_abort(A, phase); return false; }
+        if ((spins & 31u) == 31u && (ctrl->abort || launch_aborted(A))) return false;
+    }
+}
+
 // Visits the packed indices i < n that ll_fetch_plan gave this thread.
 template <class F>
 __device__ __forceinline__ void ll_each(int n, F && fn) {
@@ -420,17 +436,24 @@ __device__ __forceinline__ void gemv_slice(At && at, uint32_t woff, int nr, int 
         }
 }
 
-// Sum of squares of this thread's part of column c, folded into the CTA scratch; the total
-// is read after the next consumer barrier (norm_total).
-__device__ __forceinline__ void norm_partial(Sm & S, float ss0, float ss1, int ncol) {
+// gemv_slice for nc input columns (1, 2 or 4).
+template <bool PAIR, class At, class Epi>
+__device__ __forceinline__ void gemv_cols(int nc, At && at, uint32_t woff, int nr, int K, const float * xin, int xstride, float * part,
+                                          Epi && epi) {
+    if (nc == 4) gemv_slice<4, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
+    else if (nc == 2) gemv_slice<2, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
+    else gemv_slice<1, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
+}
+
+// Sums of squares of this thread's part of columns 0..ncol-1, folded per warp into the CTA
+// scratch; the totals are read after the next consumer barrier (norm_scale).
+__device__ __forceinline__ void norm_partial(Sm & S, const float (&ss)[MAXC], int ncol) {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    if (ncol > 0) {
-        const float t = warp_sum(ss0);
-        if (lane == 0) S.ctrl->red[0][wid] = t;
-    }
-    if (ncol > 1) {
-        const float t = warp_sum(ss1);
-        if (lane == 0) S.ctrl->red[1][wid] = t;
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+        if (c >= ncol) break;
+        const float t = warp_sum(ss[c]);
+        if (lane == 0) S.ctrl->red[c][wid] = t;
     }
 }
 __device__ __forceinline__ float norm_scale(Sm & S, int c, int n, float eps) {
@@ -446,20 +469,21 @@ __device__ __forceinline__ void row_f16_to_smem(const __half * row, int n, float
 
 __device__ SampleScratch sampler_scratch(Sm & S, int Vmax) { return sampler_layout(S.scratch, Vmax); }
 
-__device__ SampleCfg sample_cfg(const Args & A, int codebook) {
+// The draw of codebook `codebook` for stream s of the launch.
+__device__ SampleCfg sample_cfg(const Args & A, int codebook, int s) {
     SampleCfg c{};
     if (codebook == 0) {
         c.temperature = A.temp; c.top_k = A.top_k; c.top_p = A.top_p;
         c.talker_mods = 1;
         c.suppress_from = A.suppress_from; c.eos_id = A.eos_id; c.min_frames = A.min_frames;
         c.repetition_penalty = A.rep;
-        c.seen = A.w.seen;
+        c.seen = A.seen[s];
     } else {
         c.temperature = A.cp_temp; c.top_k = A.cp_top_k; c.top_p = A.cp_top_p;
         c.talker_mods = 0;
     }
-    c.rng = A.rng; c.seed = A.seed; c.frame_index = A.frame_index; c.codebook = codebook;
-    c.pcg_seed = A.pcg_seed[codebook];
+    c.rng = A.rng; c.seed = A.seed[s]; c.frame_index = A.frame_index[s]; c.codebook = codebook;
+    c.pcg_seed = A.pcg_seed[s][codebook];
     return c;
 }
 
@@ -647,32 +671,35 @@ __device__ __forceinline__ void attn_pv(int ngroups, int GR, int HD, NOf && n_of
     }
 }
 
-// Talker attention at position n_past (frame.hip:350-385), split over KV heads and cached
-// positions: CTA b < NKV * S (S = attn_split) takes KV head g = b / S and the positions
-// [s * chunk, (s + 1) * chunk) of split s = b % S, streamed into its ring chunk as that head's
-// 256-byte K and V row slices; split S-1 also takes the new position (and writes its K/V
-// row of head g). Scores, softmax and P.V run as CTA-wide passes over the GR query heads of
-// g. Partials (m, l, acc) go to the exchange words; CTA G-NH+h combines head h in split
-// order. A single split writes the output directly.
+// Talker attention at position n_past (frame.hip:350-385) of every stream of the launch,
+// split over (stream, KV head) groups and cached positions: CTA b in group (s, g) with split
+// sp < attn_split[s] (talker_attn_role) takes positions [sp * chunk, (sp + 1) * chunk) of
+// stream s, streamed into its ring chunk as KV head g's 256-byte K and V row slices; the last
+// split also takes the new position (and writes its K/V row of head g). Scores, softmax and P.V
+// run as CTA-wide passes over the GR query heads of g. Partials (m, l, acc) go to the
+// exchange words; CTA G - nb * NH + (s * NH + h) combines head h of stream s in split order.
+// A single split writes the output directly.
 __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int chunk, uint32_t tag, uint32_t ptag, int p) {
     const Dims & d = A.d;
     constexpr int HD = KHD, GR = KGR;
     const int NH = d.NH, tid = threadIdx.x;
-    const int G = gridDim.x, b = blockIdx.x, Sp = A.attn_split, pos = A.n_past;
+    const int G = gridDim.x, b = blockIdx.x;
     const float scale = rsqrtf(static_cast<float>(HD));
     const uint32_t WST = HD + 2;
-    const int NPS = A.attn_chunk + 1;                  // score slots per head
-    float * qs = S.scratch;                            // [GR][HD]
-    float * ks = qs + GR * HD;                         // [HD] new position
-    float * vs = ks + HD;                              // [HD]
-    __half * kh = reinterpret_cast<__half *>(vs + HD); // new K/V row slice as f16 [2][HD]
-    float * ml = vs + 2 * HD;                          // [GR][2]
-    float * pv = ml + 2 * MAX_GROUP;                   // [NCW][MAX_GROUP][HD]
-    float * sc = pv + NCW * MAX_GROUP * HD;            // [GR][NPS] scores, then e^(s - m)
-    if (b < d.NKV * Sp) {
-        const int g = b / Sp, sp = b - g * Sp;
+    int st, g, sp;
+    const bool has = talker_attn_role(A, b, st, g, sp);
+    if (has) {
+        const int Sp = A.attn_split[st], pos = A.n_past[st], ch = A.attn_chunk[st];
+        const int NPS = ch + 1;                            // score slots per head
+        float * qs = S.scratch;                            // [GR][HD]
+        float * ks = qs + GR * HD;                         // [HD] new position
+        float * vs = ks + HD;                              // [HD]
+        __half * kh = reinterpret_cast<__half *>(vs + HD); // new K/V row slice as f16 [2][HD]
+        float * ml = vs + 2 * HD;                          // [GR][2]
+        float * pv = ml + 2 * MAX_GROUP;                   // [NCW][MAX_GROUP][HD]
+        float * sc = pv + NCW * MAX_GROUP * HD;            // [GR][NPS] scores, then e^(s - m)
         // chunk segments: q norm, k norm, K rows, V rows (the chunk is only ever cut between them)
-        const int r0 = min(sp * A.attn_chunk, pos), r1 = min(r0 + A.attn_chunk, pos);
+        const int r0 = min(sp * ch, pos), r1 = min(r0 + ch, pos);
         const int nc = r1 - r0;
         const float * qn = reinterpret_cast<const float *>(chunk_at(S, chunk, 0));
         const float * kn = reinterpret_cast<const float *>(chunk_at(S, chunk, HD * 4));
@@ -680,23 +707,22 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int c
         const __half * Vc = reinterpret_cast<const __half *>(chunk_at(S, chunk, 2 * HD * 4 + nc * HD * 2));
         const bool last = sp == Sp - 1;
         const int n = nc + (last ? 1 : 0);
-        // inputs: q of the group's heads, and (last split) k, v of head g at the new position
-        // rows of HD words: the group's q heads, then (last split) k and v of head g
-        const bool ok = ll_fetch_plan(A.w.qkv, 1, 0, 0, GR, g * GR * HD, HD, last ? 2 : 0, d.Q + g * HD, d.KV, HD, HD, ptag, qs, A,
-                                      S.ctrl, p);
+        // rows of HD words: the group's q heads, then (last split) k and v of head g, of column st
+        const uint64_t * qkv = A.w.qkv + static_cast<size_t>(st) * d.QKV;
+        const bool ok = ll_fetch_plan(qkv, 1, 0, 0, GR, g * GR * HD, HD, last ? 2 : 0, d.Q + g * HD, d.KV, HD, HD, ptag, qs, A, S.ctrl, p);
         if (!consumers_ok(S, ok)) return false;
         stamp(A, p, 0);
         const int warp = tid >> 5;
         if (warp < GR + (last ? 1 : 0))
-            warp_norm_rope(warp < GR ? qs + warp * HD : ks, warp < GR ? qn : kn, A.rope_t, HD, d.eps_t, warp >= GR);
+            warp_norm_rope(warp < GR ? qs + warp * HD : ks, warp < GR ? qn : kn, A.rope_t[st], HD, d.eps_t, warp >= GR);
         named_sync(BID, NCT);
         if (last) {
             for (int i = tid; i < HD; i += NCT) {
                 const __half kq = __float2half_rn(ks[i]), vq = __float2half_rn(vs[i]);
                 kh[i] = kq;
                 kh[HD + i] = vq;
-                A.kc[ph.layer][static_cast<size_t>(pos) * d.KV + g * HD + i] = kq;
-                A.vc[ph.layer][static_cast<size_t>(pos) * d.KV + g * HD + i] = vq;
+                A.kc[st][ph.layer][static_cast<size_t>(pos) * d.KV + g * HD + i] = kq;
+                A.vc[st][ph.layer][static_cast<size_t>(pos) * d.KV + g * HD + i] = vq;
             }
             named_sync(BID, NCT);
         }
@@ -711,58 +737,65 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int c
                 [&](int, int j, int e, float sum) {
                     const int h = g * GR + j;
                     if (Sp == 1) {
-                        ll_store(A.w.attn + h * HD + e, sum / ml[2 * j + 1], tag);
+                        ll_store(A.w.attn + static_cast<size_t>(st) * d.Q + h * HD + e, sum / ml[2 * j + 1], tag);
                     } else {
-                        uint64_t * pp = A.w.part + (static_cast<size_t>(sp) * NH + h) * WST;
+                        uint64_t * pp = A.w.part + (static_cast<size_t>(st * NH + h) * A.attn_per + sp) * WST;
                         ll_store(pp + 2 + e, sum, tag);
                         if (e == 0) { ll_store(pp, ml[2 * j], tag); ll_store(pp + 1, ml[2 * j + 1], tag); }
                     }
                 });
         stamp(A, p, 2);
     }
-    // combine: CTA G - NH + h reduces head h over the splits, in split order
-    const int h = b - (G - NH);
-    if (Sp > 1 && h >= 0) {
-        named_sync(BID, NCT);                   // this CTA's own split (if any) is done with its scratch
-        float * pb = S.scratch;                 // [Sp][WST]: m, l, acc[HD] of every split
-        const bool ok = ll_fetch_plan(A.w.part + static_cast<size_t>(h) * WST, Sp, NH * WST, WST, 1, 0, 0, 0, 0, 0, WST, WST, tag, pb, A,
-                                      S.ctrl, p);
-        if (!consumers_ok(S, ok)) return false;
-        if (tid < HD) {
-            float M = -INFINITY;
-            for (int k = 0; k < Sp; ++k) M = fmaxf(M, pb[k * WST]);
-            float L = 0.f, num = 0.f;
-            for (int k = 0; k < Sp; ++k) {
-                const float wk = expf(pb[k * WST] - M);
-                L += pb[k * WST + 1] * wk;
-                num += pb[k * WST + 2 + tid] * wk;
+    // combine: CTA G - nb * NH + (s * NH + h) reduces head h of stream s over its splits, in split order
+    const int ch_ = b - (G - A.nb * NH);
+    if (ch_ >= 0) {
+        const int cs = ch_ / NH, h = ch_ - cs * NH, Sp = A.attn_split[cs];
+        if (Sp > 1) {
+            named_sync(BID, NCT);                   // this CTA's own split (if any) is done with its scratch
+            float * pb = S.scratch;                 // [Sp][WST]: m, l, acc[HD] of every split
+            const bool ok = ll_fetch_plan(A.w.part + static_cast<size_t>(cs * NH + h) * A.attn_per * WST, Sp, WST, WST, 1, 0, 0, 0, 0, 0,
+                                          WST, WST, tag, pb, A, S.ctrl, p);
+            if (!consumers_ok(S, ok)) return false;
+            if (tid < HD) {
+                float M = -INFINITY;
+                for (int k = 0; k < Sp; ++k) M = fmaxf(M, pb[k * WST]);
+                float L = 0.f, num = 0.f;
+                for (int k = 0; k < Sp; ++k) {
+                    const float wk = expf(pb[k * WST] - M);
+                    L += pb[k * WST + 1] * wk;
+                    num += pb[k * WST + 2 + tid] * wk;
+                }
+                ll_store(A.w.attn + static_cast<size_t>(cs) * d.Q + h * HD + tid, num / L, tag);
             }
-            ll_store(A.w.attn + h * HD + tid, num / L, tag);
+            named_sync(BID, NCT);
         }
-        named_sync(BID, NCT);
     }
     return true;
 }
 
-// Code-predictor attention at positions pos..pos+ncol-1 (frame.hip:555-575: its own KV,
-// positions 0..15, reset every frame): the CTA cp_attn_cta(layer, g) keeps the K/V of KV
-// head g of that layer in shared memory across the frame's positions.
+// Code-predictor attention (frame.hip:555-575: its own KV, positions 0..15, reset every
+// frame). Single stream: positions pos..pos+ncol-1 (the pass over positions 0 and 1 has two
+// columns). Batched: position pos of every stream, column c = stream c. The CTA of set
+// (layer, stream, KV head g) (cp_attn_role) keeps that K/V in shared memory slot across the
+// frame's positions.
 __device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, int chunk, uint32_t tag, uint32_t ptag, int p) {
     const Dims & d = A.d;
     constexpr int HD = KHD, GR = KGR;
-    const int tid = threadIdx.x, ncol = ph.ncol, pos = ph.pos;
-    const int g = blockIdx.x - cp_attn_cta(d, ph.layer, 0);
-    if (g < 0 || g >= d.NKV) return true;
+    const int tid = threadIdx.x;
+    int st, g, slot;
+    if (!cp_attn_role(A, blockIdx.x, ph.layer, st, g, slot)) return true;
+    const bool batched = A.nb > 1;
+    const int ncol = batched ? 1 : ph.ncol, pos = ph.pos, col0 = batched ? st : 0;
     const float * qn = reinterpret_cast<const float *>(chunk_at(S, chunk, 0));
     const float * kn = reinterpret_cast<const float *>(chunk_at(S, chunk, HD * 4));
-    __half * kv = S.cpkv;                   // [pos][K,V][HD] of (g, layer)
+    __half * kv = S.cpkv + static_cast<size_t>(slot) * (cpkv_bytes(d) / 2);   // [pos][K,V][HD] of the set
     float * qkv = S.scratch;                // [2][GR + 2][HD]: per column the q heads, k, v
     const auto qof = [&](int c) { return qkv + c * (GR + 2) * HD; };
     const auto kof = [&](int c) { return qkv + (c * (GR + 2) + GR) * HD; };
     const auto vof = [&](int c) { return qkv + (c * (GR + 2) + GR + 1) * HD; };
     // per column: the group's q heads, then k and v of head g (rows of HD words)
-    const bool ok = ll_fetch_plan(A.w.qkv, ncol, d.QKV, (GR + 2) * HD, GR, g * GR * HD, HD, 2, d.Q + g * HD, d.KV, HD, HD, ptag, qkv, A,
-                                  S.ctrl, p);
+    const bool ok = ll_fetch_plan(A.w.qkv + static_cast<size_t>(col0) * d.QKV, ncol, d.QKV, (GR + 2) * HD, GR, g * GR * HD, HD, 2,
+                                  d.Q + g * HD, d.KV, HD, HD, ptag, qkv, A, S.ctrl, p);
     if (!consumers_ok(S, ok)) return false;
     stamp(A, p, 0);
     // norm + RoPE of the q heads and k, one warp per vector; the warp of column c's k also
@@ -826,7 +859,7 @@ __device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, int chunk
         const float inv = 1.f / z;
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-            ll_store(A.w.attn + static_cast<size_t>(c) * d.Q + (g * GR + j) * HD + lane * 4 + e, acc[e] * inv, tag);
+            ll_store(A.w.attn + static_cast<size_t>(col0 + c) * d.Q + (g * GR + j) * HD + lane * 4 + e, acc[e] * inv, tag);
     }
     stamp(A, p, 2);
     named_sync(BID, NCT);
@@ -870,7 +903,7 @@ __device__ void consumer(const Args & A, Sm & S) {
             // single-layer program: the residual stream after the layer, this CTA's rows as f32
             const bool ok = ll_fetch(A.w.x, d.H, ptag, S.xres, A, S.ctrl, p);
             if (!consumers_ok(S, ok)) break;
-            for (int i = R.h0 + tid; i < R.h1; i += NCT) A.step_out[i] = S.xres[i];
+            for (int i = R.h0 + tid; i < R.h1; i += NCT) A.step_out[0][i] = S.xres[i];
             if (b == 0 && tid == 0) {
                 __threadfence();
                 st_relaxed_u32(&A.w.ctl[0], A.tag_base);
@@ -880,24 +913,74 @@ __device__ void consumer(const Args & A, Sm & S) {
             continue;
         }
 
+        if (ph.op == SAMPLE) {
+            // batched: CTA s draws codebook ph.pos of stream s from its logits (the phase
+            // before) and publishes the code; the other CTAs go on
+            const int st = b, cb = ph.pos;
+            if (st < A.nb) {
+                const SampleScratch sc = sampler_scratch(S, Vmax);
+                const int V = cb == 0 ? d.TV : d.CV;
+                const uint64_t * src = cb == 0 ? A.w.logits + static_cast<size_t>(st) * d.TV
+                                               : A.w.clogits + (static_cast<size_t>(st) * (NCB - 1) + cb - 1) * d.CV;
+                const bool ok = ll_fetch(src, V, ptag, sc.s, A, S.ctrl, p);
+                if (!consumers_ok(S, ok)) break;
+                stamp(A, p, 0);
+                const int code = sample_cta<NCT>(V, sample_cfg(A, cb, st), sc, BID);
+                if (tid == 0) ll_store(A.w.code_x + st * NCB + cb, static_cast<float>(code), tag);
+            }
+            stamp(A, p, 3);
+            continue;
+        }
+
+        if (ph.op == FINAL && A.nb > 1) {
+            // batched: every stream's 16 codes (words of the SAMPLE phases) -> step embeddings
+            bool ok = true;
+            if (tid < A.nb * NCB) {
+                float v = 0.f;
+                ok = ll_poll1(A.w.code_x + tid, A.tag_base + static_cast<uint32_t>(A.sample_phase[tid % NCB]), v, A, S.ctrl, p);
+                S.codes[tid] = static_cast<int>(v);
+            }
+            if (!consumers_ok(S, ok)) break;
+            stamp(A, p, 0);
+            for (int st = 0; st < A.nb; ++st) {
+                const int * cd = S.codes + st * NCB;
+                for (int i = R.h0 + tid; i < R.h1; i += NCT) {
+                    float v = __half2float(W.tl_emb[static_cast<size_t>(cd[0]) * d.H + i]);
+                    for (int cb = 0; cb < NCB - 1; ++cb)
+                        v = __fadd_rn(v, __half2float(W.cp_emb[cb][static_cast<size_t>(cd[cb + 1]) * d.H + i]));
+                    v = __fadd_rn(v, __ldcg(A.trailing[st] + i));
+                    A.step_out[st][i] = v;
+                }
+            }
+            if (b == 0 && tid < A.nb * NCB) A.w.codes[tid] = S.codes[tid];
+            if (b == 0 && tid < A.nb && S.codes[tid * NCB] != A.eos_id) A.seen[tid][S.codes[tid * NCB]] = 1;
+            named_sync(BID, NCT);
+            if (b == 0 && tid == 0) {
+                __threadfence();
+                st_relaxed_u32(&A.w.ctl[0], A.tag_base);
+            }
+            stamp(A, p, 3);
+            continue;
+        }
+
         if (ph.op == FINAL) {
             const SampleScratch sc = sampler_scratch(S, Vmax);
             const bool ok = ll_fetch(A.w.clogits + static_cast<size_t>(NCB - 2) * d.CV, d.CV, ptag, sc.s, A, S.ctrl, p);
             if (!consumers_ok(S, ok)) break;
             stamp(A, p, 0);
-            const int code = sample_cta<NCT>(d.CV, sample_cfg(A, NCB - 1), sc, BID);
+            const int code = sample_cta<NCT>(d.CV, sample_cfg(A, NCB - 1, 0), sc, BID);
             if (tid == 0) S.codes[NCB - 1] = code;
             named_sync(BID, NCT);
             for (int i = R.h0 + tid; i < R.h1; i += NCT) {
                 float v = __half2float(W.tl_emb[static_cast<size_t>(S.codes[0]) * d.H + i]);
                 for (int cb = 0; cb < NCB - 1; ++cb)
                     v = __fadd_rn(v, __half2float(W.cp_emb[cb][static_cast<size_t>(S.codes[cb + 1]) * d.H + i]));
-                v = __fadd_rn(v, __ldcg(A.trailing + i));
-                A.step_out[i] = v;
+                v = __fadd_rn(v, __ldcg(A.trailing[0] + i));
+                A.step_out[0][i] = v;
             }
             if (b == 0 && tid < NCB) A.w.codes[tid] = S.codes[tid];
             if (b == 0 && tid == 0) {
-                if (S.codes[0] != A.eos_id) A.w.seen[S.codes[0]] = 1;
+                if (S.codes[0] != A.eos_id) A.seen[0][S.codes[0]] = 1;
                 __threadfence();
                 st_relaxed_u32(&A.w.ctl[0], A.tag_base);
             }
@@ -913,18 +996,22 @@ __device__ void consumer(const Args & A, Sm & S) {
         const float * nw = reinterpret_cast<const float *>(chunk_at(S, chunk, 0));
         const uint32_t woff = has_norm ? d.H * 4 : 0;     // the weight slice follows the norm weights
         const auto at = [&](uint32_t x) { return chunk_at(S, chunk, x); };
-        float ss0 = 0.f, ss1 = 0.f;   // sums of squares of this thread's inputs, per column
-        int nnorm = 0;                // columns whose norm scale is needed
+        float ss0 = 0.f, ss1 = 0.f, ss2 = 0.f, ss3 = 0.f;   // sums of squares of this thread's inputs, per column
+        int nnorm = 0;                                      // columns whose norm scale is needed
+        const bool batched = A.nb > 1;
         auto stage = [&](int c, int i, float v) {
             S.xres[c * d.H + i] = v;
             xin[c * XS + i] = v * nw[i];
-            if (c == 0) ss0 += v * v;
-            else ss1 += v * v;
+            const float q = v * v;
+            if (c == 0) ss0 += q;
+            else if (c == 1) ss1 += q;
+            else if (c == 2) ss2 += q;
+            else ss3 += q;
         };
         // after ll_fetch_cols of nc columns into xres: the same thread stages its elements
         auto stage_fetched = [&](int nc) {
             ll_each(nc * d.H, [&](int i) {
-                const int c = i >= d.H ? 1 : 0;
+                const int c = (i >= d.H ? 1 : 0) + (i >= 2 * d.H ? 1 : 0) + (i >= 3 * d.H ? 1 : 0);
                 stage(c, i - c * d.H, S.xres[i]);
             });
         };
@@ -933,7 +1020,29 @@ __device__ void consumer(const Args & A, Sm & S) {
                 nnorm = ncol;
                 if (ph.op == TQKV && (ph.layer == 0 || ph.pos == POS_STEP_IN)) {
                     if (ok)
-                        for (int i = tid; i < d.H; i += NCT) stage(0, i, __ldcg(A.step_in + i));
+                        for (int c = 0; c < ncol; ++c)
+                            for (int i = tid; i < d.H; i += NCT) stage(c, i, __ldcg(A.step_in[c] + i));
+                } else if (batched && ph.layer == 0 && ph.pos == 0) {
+                    // batched position 0: every stream's post-norm talker hidden
+                    if (ok) {
+                        ok = ll_fetch_cols(A.w.hid_x, ncol, d.H, S.xres, d.H, A.tag_base + static_cast<uint32_t>(A.thead_phase), A, S.ctrl, p);
+                        if (ok) stage_fetched(ncol);
+                    }
+                } else if (batched && ph.layer == 0) {
+                    // batched position pos: the embedding rows of every stream's code pos - 1
+                    bool okc = true;
+                    const int cb = ph.pos - 1;
+                    if (tid < ncol) {
+                        float v = 0.f;
+                        okc = ll_poll1(A.w.code_x + tid * NCB + cb, A.tag_base + static_cast<uint32_t>(A.sample_phase[cb]), v, A, S.ctrl, p);
+                        S.codes[tid * NCB + cb] = static_cast<int>(v);
+                    }
+                    if (!consumers_ok(S, okc && ok)) { ok = false; break; }
+                    for (int c = 0; c < ncol; ++c) {
+                        const int code = S.codes[c * NCB + cb];
+                        const __half * row = (cb == 0 ? W.tl_emb : W.cp_emb[cb - 1]) + static_cast<size_t>(code) * d.H;
+                        for (int i = tid; i < d.H; i += NCT) stage(c, i, __half2float(row[i]));
+                    }
                 } else if (ph.layer == 0 && ph.pos == 0) {
                     // code-predictor positions 0 and 1: sample codebook 0 first
                     const SampleScratch sc = sampler_scratch(S, Vmax);
@@ -944,7 +1053,7 @@ __device__ void consumer(const Args & A, Sm & S) {
                         okl = ll_fetch(A.w.logits, d.TV, ptag, sc.s, A, S.ctrl, p);
                     }
                     if (!consumers_ok(S, okl && ok)) { ok = false; break; }
-                    const int cb0 = sample_cta<NCT>(d.TV, sample_cfg(A, 0), sc, BID);
+                    const int cb0 = sample_cta<NCT>(d.TV, sample_cfg(A, 0, 0), sc, BID);
                     if (tid == 0) S.codes[0] = cb0;
                     for (int i = tid; i < d.H; i += NCT) {
                         stage(0, i, A.hidden_in ? __ldcg(A.hidden_in + i) : S.hid[i]);
@@ -954,7 +1063,7 @@ __device__ void consumer(const Args & A, Sm & S) {
                     const SampleScratch sc = sampler_scratch(S, Vmax);
                     const bool okl = ll_fetch(A.w.clogits + static_cast<size_t>(ph.pos - 2) * d.CV, d.CV, ptag, sc.s, A, S.ctrl, p);
                     if (!consumers_ok(S, okl && ok)) { ok = false; break; }
-                    const int code = sample_cta<NCT>(d.CV, sample_cfg(A, ph.pos - 1), sc, BID);
+                    const int code = sample_cta<NCT>(d.CV, sample_cfg(A, ph.pos - 1, 0), sc, BID);
                     if (tid == 0) S.codes[ph.pos - 1] = code;
                     const __half * row = W.cp_emb[ph.pos - 2] + static_cast<size_t>(code) * d.H;
                     for (int i = tid; i < d.H; i += NCT) stage(0, i, __half2float(row[i]));
@@ -978,67 +1087,77 @@ __device__ void consumer(const Args & A, Sm & S) {
                 if (ok) ok = ll_fetch_cols(A.w.h, ncol, d.F, xin, XS, ptag, A, S.ctrl, p);
                 break;
             case THEAD:
-                nnorm = 1;
-                ok = ok && ll_fetch(A.w.x, d.H, ptag, S.xres, A, S.ctrl, p);
-                if (ok) stage_fetched(1);
+                nnorm = ncol;
+                if (ok) ok = ll_fetch_cols(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
+                if (ok) stage_fetched(ncol);
                 break;
             case CHEAD:
-                nnorm = 1;
-                ok = ok && ll_fetch(A.w.x + static_cast<size_t>(ncol - 1) * d.H, d.H, ptag, S.xres, A, S.ctrl, p);
-                if (ok) stage_fetched(1);
+                if (batched) {
+                    nnorm = ncol;
+                    if (ok) ok = ll_fetch_cols(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
+                    if (ok) stage_fetched(ncol);
+                } else {
+                    // the single-stream pass's last column is this position
+                    nnorm = 1;
+                    ok = ok && ll_fetch(A.w.x + static_cast<size_t>(ncol - 1) * d.H, d.H, ptag, S.xres, A, S.ctrl, p);
+                    if (ok) stage_fetched(1);
+                }
                 break;
             default: break;
         }
-        norm_partial(S, ss0, ss1, nnorm);
+        {
+            const float ss[MAXC] = {ss0, ss1, ss2, ss3};
+            norm_partial(S, ss, nnorm);
+        }
         if (!consumers_ok(S, ok)) break;
         stamp(A, p, 0);
         const float eps = (ph.op <= THEAD) ? d.eps_t : d.eps_c;
         const float sc0 = nnorm > 0 ? norm_scale(S, 0, d.H, eps) : 1.f;
         const float sc1 = nnorm > 1 ? norm_scale(S, 1, d.H, eps) : 1.f;
-        const int gcol = (ph.op == THEAD || ph.op == CHEAD) ? 1 : ncol;
+        const float sc2 = nnorm > 2 ? norm_scale(S, 2, d.H, eps) : 1.f;
+        const float sc3 = nnorm > 3 ? norm_scale(S, 3, d.H, eps) : 1.f;
+        const auto scale_of = [&](int c) { return c == 0 ? sc0 : c == 1 ? sc1 : c == 2 ? sc2 : sc3; };
+        const int gcol = (ph.op == CHEAD && !batched) ? 1 : ncol;
         const uint32_t t = tag;
         switch (ph.op) {
-            case TQKV: case CQKV: {
-                auto epi = [&](int u, int c, float y, float) {
-                    ll_store(A.w.qkv + static_cast<size_t>(c) * d.QKV + r0 + u, y * (c ? sc1 : sc0), t);
-                };
-                if (gcol == 2) gemv_slice<2, false>(at, woff, nr, d.H, xin, XS, S.part, epi);
-                else gemv_slice<1, false>(at, woff, nr, d.H, xin, XS, S.part, epi);
+            case TQKV: case CQKV:
+                gemv_cols<false>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
+                    ll_store(A.w.qkv + static_cast<size_t>(c) * d.QKV + r0 + u, y * scale_of(c), t);
+                });
                 break;
-            }
             case TO: case CO: case TDOWN: case CDOWN: {
                 const int K = (ph.op == TO || ph.op == CO) ? d.Q : d.F;
-                auto epi = [&](int u, int c, float y, float) {
+                gemv_cols<false>(gcol, at, woff, nr, K, xin, XS, S.part, [&](int u, int c, float y, float) {
                     ll_store(A.w.x + static_cast<size_t>(c) * d.H + r0 + u, S.xres[c * d.H + r0 + u] + y, t);
-                };
-                if (gcol == 2) gemv_slice<2, false>(at, woff, nr, K, xin, XS, S.part, epi);
-                else gemv_slice<1, false>(at, woff, nr, K, xin, XS, S.part, epi);
+                });
                 break;
             }
-            case TGU: case CGU: {
-                auto epi = [&](int u, int c, float g, float up) {
-                    const float s = c ? sc1 : sc0;
+            case TGU: case CGU:
+                gemv_cols<true>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float g, float up) {
+                    const float s = scale_of(c);
                     g *= s;
                     up *= s;
                     ll_store(A.w.h + static_cast<size_t>(c) * d.F + r0 + u, g / (1.f + expf(-g)) * up, t);
-                };
-                if (gcol == 2) gemv_slice<2, true>(at, woff, nr, d.H, xin, XS, S.part, epi);
-                else gemv_slice<1, true>(at, woff, nr, d.H, xin, XS, S.part, epi);
+                });
                 break;
-            }
             case THEAD: {
-                for (int i = tid; i < d.H; i += NCT) {
-                    const float hv = xin[i] * sc0;
-                    S.hid[i] = hv;
-                    if (b == 0) A.w.hidden[i] = hv;
+                for (int c = 0; c < ncol; ++c) {
+                    const float s = scale_of(c);
+                    for (int i = tid; i < d.H; i += NCT) {
+                        const float hv = xin[c * XS + i] * s;
+                        if (!batched) S.hid[i] = hv;
+                        else if (i >= R.h0 && i < R.h1) ll_store(A.w.hid_x + static_cast<size_t>(c) * d.H + i, hv, t);
+                        if (b == 0) A.w.hidden[static_cast<size_t>(c) * d.H + i] = hv;
+                    }
                 }
-                gemv_slice<1, false>(at, woff, nr, d.H, xin, XS, S.part,
-                                     [&](int u, int, float y, float) { ll_store(A.w.logits + r0 + u, y * sc0, t); });
+                gemv_cols<false>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
+                    ll_store(A.w.logits + static_cast<size_t>(c) * d.TV + r0 + u, y * scale_of(c), t);
+                });
                 break;
             }
             case CHEAD:
-                gemv_slice<1, false>(at, woff, nr, d.H, xin, XS, S.part, [&](int u, int, float y, float) {
-                    ll_store(A.w.clogits + static_cast<size_t>(ph.pos - 1) * d.CV + r0 + u, y * sc0, t);
+                gemv_cols<false>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
+                    ll_store(A.w.clogits + (static_cast<size_t>(c) * (NCB - 1) + ph.pos - 1) * d.CV + r0 + u, y * scale_of(c), t);
                 });
                 break;
             default: break;
@@ -1055,7 +1174,7 @@ __device__ void consumer(const Args & A, Sm & S) {
 
 __global__ void __launch_bounds__(NTHR, 1) k_frame(const __grid_constant__ Args A) {
     extern __shared__ __align__(128) char smem[];
-    const SmemLayout L = smem_layout(A.d, A.ring_bytes, A.scratch_floats, A.part_floats);
+    const SmemLayout L = smem_layout(A.d, A.ring_bytes, A.scratch_floats, A.part_floats, A.xcols, A.cp_slots);
     Sm S = carve(smem, L);
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSLOT; ++i) mbar_init(&S.bars[i], 1);

@@ -55,13 +55,18 @@ constexpr int KGR = 2;                  // query heads per KV head the attention
 constexpr uint32_t PIECE = 32768;       // bulk copies are issued in pieces of at most this
 constexpr uint32_t CTRL_BYTES = 256;    // per-CTA control block in shared memory
 constexpr int PROF_STRIDE = 4 * 4096 + 1;   // trace words per CTA: 4 stamps x phases, then the start
+constexpr int MAX_B = 4;                // streams of one batched launch (each with its own KV cache and draws)
+constexpr int MAXC = 4;                 // input columns of one GEMV phase (streams, or code-predictor positions)
+constexpr int CP_SLOTS = 2;             // code-predictor K/V sets one CTA may keep (MAX_B * layers * KV heads / grid)
 
-enum Op : uint8_t { TQKV, TATTN, TO, TGU, TDOWN, THEAD, CQKV, CATTN, CO, CGU, CDOWN, CHEAD, FINAL, XOUT };
+enum Op : uint8_t { TQKV, TATTN, TO, TGU, TDOWN, THEAD, CQKV, CATTN, CO, CGU, CDOWN, CHEAD, FINAL, XOUT, SAMPLE };
 
 // Talker QKV phase flag (Phase::pos): stage the layer input from Args::step_in instead of the
 // previous layer's output (the first phase of a single-layer program).
 constexpr uint8_t POS_STEP_IN = 1;
 
+// op, input columns (batched programs: one per stream), layer, code-predictor position
+// (SAMPLE: the codebook drawn)
 struct Phase {
     uint8_t op, ncol, layer, pos;
 };
@@ -91,17 +96,21 @@ struct Dims {
     float eps_t, eps_c;
 };
 
+// Exchange words ({value, tag}) are indexed by input column c (a stream of a batched launch,
+// or a code-predictor position of the single-stream pass over positions 0 and 1), and
+// per-stream outputs by the stream's place s in the launch.
 struct Work {
-    uint64_t * x;        // [2][H]   residual stream (talker uses column 0)
-    uint64_t * qkv;      // [2][QKV]
-    uint64_t * attn;     // [2][Q]
-    uint64_t * h;        // [2][F]
-    uint64_t * logits;   // [TV]
-    uint64_t * clogits;  // [15][CV]
-    uint64_t * part;     // [MAX_SPLIT][NH][HD + 2] talker attention partials (m, l, acc)
-    uint8_t * seen;      // [TV]
-    int32_t * codes;     // [16]
-    float * hidden;      // [H] talker post-norm hidden of the last talker step
+    uint64_t * x;        // [MAXC][H]   residual stream
+    uint64_t * qkv;      // [MAXC][QKV]
+    uint64_t * attn;     // [MAXC][Q]
+    uint64_t * h;        // [MAXC][F]
+    uint64_t * logits;   // [MAX_B][TV]
+    uint64_t * clogits;  // [MAX_B][15][CV]
+    uint64_t * part;     // [MAX_SPLIT * NH][HD + 2] talker attention partials (m, l, acc)
+    uint64_t * hid_x;    // [MAX_B][H] batched: the talker's post-norm hidden, for code-predictor position 0
+    uint64_t * code_x;   // [MAX_B][16] batched: the drawn codes
+    int32_t * codes;     // [MAX_B][16]
+    float * hidden;      // [MAX_B][H] talker post-norm hidden of the last talker step
     unsigned * ctl;      // [0] done tag, [1] failing phase, [2] abort tag, [3] failing CTA
 };
 
@@ -112,33 +121,44 @@ struct Args {
     Dims d;
     Work w;
     uint32_t tag_base;
-    int n_past;        // talker position
-    int attn_split;    // talker attention splits per KV head: CTA b < NKV * attn_split takes KV head
-                       // b / attn_split and its split b % attn_split
-    int attn_chunk;    // cached positions per split
-    const float * step_in;     // talker input row (frames >= 1)
-    const float * hidden_in;   // frame 0: the prefill's post-norm hidden
-    const float * logits_in;   // frame 0: the prefill's codec logits
-    const float * trailing;    // [H]
-    float * step_out;          // [H]
-    __half * kc[MAX_TL];
-    __half * vc[MAX_TL];
+    int grid;          // CTAs of the launch
+    int nb;            // streams of this launch (1: the single-stream program)
+    // per stream s < nb
+    int n_past[MAX_B];         // talker position
+    int attn_split[MAX_B];     // talker attention splits of each KV head (<= attn_per)
+    int attn_chunk[MAX_B];     // cached positions per split
+    int attn_per;              // CTAs per (stream, KV head): CTA b < nb * NKV * attn_per takes stream
+                               // (b / attn_per) / NKV, KV head (b / attn_per) % NKV, split b % attn_per
+    const float * step_in[MAX_B];    // talker input row (frames >= 1)
+    const float * trailing[MAX_B];   // [H]
+    float * step_out[MAX_B];         // [H]
+    uint8_t * seen[MAX_B];           // [TV] codebook-0 ids drawn so far this request
+    __half * kc[MAX_B][MAX_TL];
+    __half * vc[MAX_B][MAX_TL];
+    float rope_t[MAX_B][128];        // talker position n_past: cos[HD/2], then sin[HD/2]
+    uint64_t seed[MAX_B];
+    int frame_index[MAX_B];
+    uint64_t pcg_seed[MAX_B][NCB];
+    // batched programs: phase indices whose tags the exchange words carry
+    int thead_phase;                 // THEAD (hid_x)
+    int sample_phase[NCB];           // SAMPLE of each codebook (code_x)
+    // single stream, frame 0
+    const float * hidden_in;   // the prefill's post-norm hidden
+    const float * logits_in;   // the prefill's codec logits
     const float * inv_freq_t;  // [HD/2]
     const float * inv_freq_c;
-    float rope_t[128];         // talker position n_past: cos[HD/2], then sin[HD/2]
     const float * rope_c;      // code predictor, positions 0..15: [NCB][HD] = cos[HD/2], sin[HD/2]
-    // sampling
+    // sampling (shared by the streams)
     float temp, top_p, rep;
     int top_k;
     float cp_temp, cp_top_p;
     int cp_top_k;
     int min_frames, rng;
-    uint64_t seed;
-    int frame_index;
-    uint64_t pcg_seed[NCB];
     int eos_id, suppress_from;
     uint64_t timeout_ns;
     uint32_t ring_bytes;
+    int xcols;                 // columns of the residual copy in shared memory (max(2, nb))
+    int cp_slots;              // code-predictor K/V slots in shared memory (sets / grid, rounded up)
     int cp_keep_layers;        // code-predictor layers whose weights the producer asks L2 to keep
     uint32_t scratch_floats;
     uint32_t part_floats;
@@ -152,16 +172,19 @@ struct SmemLayout {
     uint32_t bars, meta_off, meta_split, meta_end, ctrl, codes, xres, hid, part, scratch, cpkv, ring, total;
 };
 
-// The code predictor's K/V of one (KV head, layer), kept in shared memory across the
+// The code predictor's K/V of one (stream, layer, KV head), kept in shared memory across the
 // positions of a frame by the CTA that attends for it: [position][K, V][head_dim] f16.
 __host__ __device__ inline uint32_t cpkv_bytes(const Dims & d) { return static_cast<uint32_t>(NCB) * 2 * d.HD * 2; }
 
-// The CTA that runs code-predictor attention for KV head g of layer l.
-__host__ __device__ inline int cp_attn_cta(const Dims & d, int l, int g) { return l * d.NKV + g; }
+// Code-predictor attention set i = (layer * nb + stream) * NKV + KV head lives on CTA i % G in
+// its K/V slot i / G. A layer's nb * NKV sets are consecutive, so while nb * NKV <= G a CTA
+// attends for at most one set per layer.
+__host__ __device__ inline int cp_set(const Dims & d, int nb, int l, int s, int g) { return (l * nb + s) * d.NKV + g; }
 
 __host__ __device__ inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline SmemLayout smem_layout(const Dims & d, uint32_t ring_bytes, uint32_t scratch_floats, uint32_t part_floats) {
+__host__ __device__ inline SmemLayout smem_layout(const Dims & d, uint32_t ring_bytes, uint32_t scratch_floats, uint32_t part_floats,
+                                                  int xcols, int cp_slots) {
     SmemLayout L{};
     uint32_t o = 0;
     L.bars = o;     o += NSLOT * 8;
@@ -169,13 +192,13 @@ __host__ __device__ inline SmemLayout smem_layout(const Dims & d, uint32_t ring_
     L.meta_off = o; o += NSLOT * 4;
     L.meta_split = o; o += NSLOT * 4;
     L.ctrl = o;     o += CTRL_BYTES;
-    L.codes = o;    o += NCB * 4;
+    L.codes = o;    o += MAX_B * NCB * 4;
     o = align_up(o, 16);
-    L.xres = o;     o += 2 * d.H * 4;
+    L.xres = o;     o += static_cast<uint32_t>(xcols) * d.H * 4;
     L.hid = o;      o += d.H * 4;
     L.part = o;     o += align_up(part_floats * 4, 16);
     L.scratch = o;  o += align_up(scratch_floats * 4, 16);
-    L.cpkv = o;     o += align_up(cpkv_bytes(d), 16);
+    L.cpkv = o;     o += static_cast<uint32_t>(cp_slots) * align_up(cpkv_bytes(d), 16);
     o = align_up(o, 128);
     L.ring = o;     o += ring_bytes;
     L.total = o;
@@ -237,6 +260,30 @@ __host__ __device__ inline Rows cta_rows(const Dims & d, int b, int G) {
     return r;
 }
 
+// Talker attention role of CTA b: (stream, KV head, split) while b < nb * NKV * attn_per and
+// the split holds positions (splits past attn_split[stream] have none but the last one's new row).
+__host__ __device__ inline bool talker_attn_role(const Args & A, int b, int & stream, int & g, int & sp) {
+    const int grp = b / A.attn_per;
+    if (grp >= A.nb * A.d.NKV) return false;
+    stream = grp / A.d.NKV;
+    g = grp - stream * A.d.NKV;
+    sp = b - grp * A.attn_per;
+    return sp < A.attn_split[stream];
+}
+
+// Code-predictor attention role of CTA b for layer l (cp_set): its stream, KV head and K/V slot.
+__host__ __device__ inline bool cp_attn_role(const Args & A, int b, int l, int & stream, int & g, int & slot) {
+    const int G = A.grid;
+    const int n = A.nb * A.d.NKV, first = cp_set(A.d, A.nb, l, 0, 0);
+    // the set of layer l on CTA b: first <= i < first + n with i % G == b
+    int i = first + ((b - first % G) % G + G) % G;
+    if (i >= first + n) return false;
+    stream = (i - first) / A.d.NKV;
+    g = (i - first) - stream * A.d.NKV;
+    slot = i / G;
+    return slot < A.cp_slots;
+}
+
 // The bytes phase `ph` streams into CTA b's ring chunk, in order (up to MAX_SEG segments,
 // each a multiple of 16 bytes): the phase's norm weights first, then its weight rows
 // [r0, r1); for attention, the q/k norm weights, then (talker) this split's KV head slice
@@ -282,26 +329,27 @@ __host__ __device__ inline int phase_segments(const Args & A, const ModelW & W, 
                     static_cast<uint32_t>(r1 - r0)};
             return r1 > r0 ? 2 : 0;
         case TATTN: {
-            const int S = A.attn_split;
-            if (b >= d.NKV * S) return 0;
-            const int g = b / S, sp = b - g * S;
+            int st_, g, sp;
+            if (!talker_attn_role(A, b, st_, g, sp)) return 0;
             s[0] = {L->qn, HD4};
             s[1] = {L->kn, HD4};
-            // cached positions [r0, r1) of this split, KV head g
-            r0 = min(sp * A.attn_chunk, A.n_past);
-            r1 = min(r0 + A.attn_chunk, A.n_past);
+            // cached positions [r0, r1) of this split, stream st_, KV head g
+            r0 = min(sp * A.attn_chunk[st_], A.n_past[st_]);
+            r1 = min(r0 + A.attn_chunk[st_], A.n_past[st_]);
             if (r1 <= r0) return 2;
             const size_t off = static_cast<size_t>(r0) * d.KV + static_cast<size_t>(g) * d.HD;
             const uint32_t rows = static_cast<uint32_t>(r1 - r0), rb = static_cast<uint32_t>(d.HD) * 2, st = static_cast<uint32_t>(d.KV) * 2;
-            s[2] = {A.kc[ph.layer] + off, rb, rows, st};
-            s[3] = {A.vc[ph.layer] + off, rb, rows, st};
+            s[2] = {A.kc[st_][ph.layer] + off, rb, rows, st};
+            s[3] = {A.vc[st_][ph.layer] + off, rb, rows, st};
             return 4;
         }
-        case CATTN:
-            if (b < cp_attn_cta(d, ph.layer, 0) || b >= cp_attn_cta(d, ph.layer, d.NKV)) return 0;
+        case CATTN: {
+            int st_, g, slot;
+            if (!cp_attn_role(A, b, ph.layer, st_, g, slot)) return 0;
             s[0] = {L->qn, HD4};
             s[1] = {L->kn, HD4};
             return 2;
+        }
         default:
             return 0;
     }

@@ -13,6 +13,7 @@ from ctypes import POINTER, c_char, c_char_p, c_double, c_float, c_int, c_int32,
 LIB_PATH = os.environ.get("NAVI_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "libnavi_b200.so")
 
 NAVI_OK, NAVI_E_ARG, NAVI_E_CUDA, NAVI_E_FORMAT, NAVI_E_TIMEOUT, NAVI_E_KV_FULL, NAVI_E_LAUNCH, NAVI_E_SHAPE, NAVI_E_NOMEM = range(9)
+NAVI_FRAME_SLOTS = 4
 NAVI_RNG_PCG, NAVI_RNG_PHILOX = 0, 1
 NAVI_SAMPLE_STATIC_MAX_VOCAB = 32768
 
@@ -119,6 +120,17 @@ SIGNATURES = [
     ("navi_frame_step_out", c_void_p, [c_void_p]),
     ("navi_frame_set_step_in", c_int, [c_void_p, c_void_p]),
     ("navi_frame_grid_blocks", c_int, [c_void_p]),
+    ("navi_frame_reset_slot", c_int, [c_void_p, c_int]),
+    ("navi_frame_run_first_slot", c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, POINTER(Sampling), c_uint64, c_int,
+                                          POINTER(FrameResult)]),
+    ("navi_frame_run_batch", c_int, [c_void_p, c_int, POINTER(c_int), POINTER(POINTER(KV)), POINTER(c_int), POINTER(c_void_p),
+                                     POINTER(Sampling), POINTER(c_uint64), POINTER(c_int), POINTER(FrameResult)]),
+    ("navi_frame_enqueue_batch", c_int, [c_void_p, c_int, POINTER(c_int), POINTER(POINTER(KV)), POINTER(c_int), POINTER(c_void_p),
+                                         POINTER(Sampling), POINTER(c_uint64), POINTER(c_int)]),
+    ("navi_frame_collect_batch", c_int, [c_void_p, c_int, POINTER(FrameResult)]),
+    ("navi_frame_step_out_slot", c_void_p, [c_void_p, c_int]),
+    ("navi_frame_set_step_in_slot", c_int, [c_void_p, c_int, c_void_p]),
+    ("navi_frame_inspect_stream", c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     ("navi_frame_destroy", None, [c_void_p]),
     ("navi_graph_create", c_int, [c_void_p, c_void_p, POINTER(FrameOpts), c_int, c_int, c_int, POINTER(c_void_p)]),
     ("navi_graph_synth_ids", c_int, [c_void_p, POINTER(c_int32), c_int, c_char_p, POINTER(c_float), POINTER(Sampling), c_uint64,

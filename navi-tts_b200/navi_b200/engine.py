@@ -379,6 +379,53 @@ class Frame:
         st = lib().navi_frame_run(self.h, kv.ptr(), n_past, c_void_p(d_trailing), byref(s.c()), seed, frame_index, byref(r))
         return _result(r, st)
 
+    def reset_slot(self, slot: int) -> None:
+        check(lib().navi_frame_reset_slot(self.h, slot))
+
+    def run_first_slot(self, slot: int, d_hidden: int, d_logits: int, d_trailing: int, s: Sampling, seed: int,
+                       frame_index: int) -> FrameResult:
+        r = capi.FrameResult()
+        st = lib().navi_frame_run_first_slot(self.h, slot, c_void_p(d_hidden), c_void_p(d_logits), c_void_p(d_trailing), byref(s.c()),
+                                             seed, frame_index, byref(r))
+        return _result(r, st)
+
+    def _batch_args(self, slots, kvs, n_past, d_trailing, seeds, frame_index):
+        nb = len(slots)
+        return (nb, (c_int * nb)(*slots), (ctypes.POINTER(capi.KV) * nb)(*[ctypes.pointer(k.s) for k in kvs]), (c_int * nb)(*n_past),
+                (c_void_p * nb)(*d_trailing), (ctypes.c_uint64 * nb)(*seeds), (c_int * nb)(*frame_index))
+
+    def run_batch(self, slots, kvs, n_past, d_trailing, s: Sampling, seeds, frame_index) -> list:
+        """One frame of len(slots) streams (1, 2 or 4) in one launch; a FrameResult per stream."""
+        nb, sl, kp, npst, tr, sd, fi = self._batch_args(slots, kvs, n_past, d_trailing, seeds, frame_index)
+        res = (capi.FrameResult * nb)()
+        st = lib().navi_frame_run_batch(self.h, nb, sl, kp, npst, tr, byref(s.c()), sd, fi, res)
+        return [_result(res[i], st) for i in range(nb)]
+
+    def enqueue_batch(self, slots, kvs, n_past, d_trailing, s: Sampling, seeds, frame_index) -> None:
+        nb, sl, kp, npst, tr, sd, fi = self._batch_args(slots, kvs, n_past, d_trailing, seeds, frame_index)
+        check(lib().navi_frame_enqueue_batch(self.h, nb, sl, kp, npst, tr, byref(s.c()), sd, fi))
+
+    def collect_batch(self, nb: int) -> list:
+        res = (capi.FrameResult * nb)()
+        st = lib().navi_frame_collect_batch(self.h, nb, res)
+        return [_result(res[i], st) for i in range(nb)]
+
+    def d_step_out_slot(self, slot: int) -> int:
+        return lib().navi_frame_step_out_slot(self.h, slot)
+
+    def set_step_in_slot(self, slot: int, d_step: int) -> None:
+        check(lib().navi_frame_set_step_in_slot(self.h, slot, c_void_p(d_step)))
+
+    def inspect_stream(self, index: int):
+        """(hidden [H], logits [TV], clogits [15, CV]) of stream `index` of the last launch."""
+        import numpy as np
+        p = self.w.params
+        hid = np.zeros(p.talker.hidden, np.float32)
+        lg = np.zeros(p.talker.vocab, np.float32)
+        clg = np.zeros((15, p.cp.vocab), np.float32)
+        check(lib().navi_frame_inspect_stream(self.h, index, hid.ctypes.data, lg.ctypes.data, clg.ctypes.data))
+        return hid, lg, clg
+
     def run_layer(self, layer: int, d_x: int, kv: KvCache, n_past: int, d_out: int) -> FrameResult:
         """One talker decoder layer alone at position n_past: d_x -> d_out, f32 [hidden]."""
         r = capi.FrameResult()

@@ -1,0 +1,159 @@
+"""Batched decode (navi_frame_run_batch): 2 or 4 independent streams, each with its own KV
+cache, position, trailing row, seed, frame index and repetition set, decode one frame each in
+one launch that reads every weight once. Each stream must be what the CPU oracle computes for
+that stream alone (talker step, code predictor, step embedding) and what a single-stream
+frame gives: hidden / logits / code-predictor logits within rel-L2 2e-4 of the oracle, every
+code the oracle sampler's draw on the GPU's own logits, the new K/V rows of each stream's own
+cache only. The per-stream math is the reference's Frame::run (frame.hip:798-810); the
+reference decodes one stream per launch (docs/DESIGN.md:35), so batching has no counterpart
+there.
+"""
+import numpy as np
+import pytest
+import torch
+
+from navi_b200 import capi, engine
+from oracle import model as om
+
+from frame_harness import dev_f32, oracle_sampling
+
+pytestmark = pytest.mark.gpu
+
+REL = 2e-4
+
+
+class Streams:
+    """One device, weights and frame, and nb streams with their own seeded KV caches."""
+
+    def __init__(self, navi, nb, n_pasts, max_pos=1024):
+        self.dev = engine.Device(0)
+        self.w = engine.Weights(self.dev, navi)
+        self.frame = engine.Frame(self.dev, self.w)
+        self.W = om.Weights.from_navi(navi)
+        p = self.w.params
+        self.H, self.TV, self.CV = p.talker.hidden, p.talker.vocab, p.cp.vocab
+        self.kvd = p.talker.n_kv_head * p.talker.head_dim
+        self.L = p.talker.n_layer
+        self.nb, self.n_past = nb, list(n_pasts)
+        self.k, self.v, self.kv = [], [], []
+        for s in range(nb):
+            g = torch.Generator().manual_seed(100 + s)
+            k = [torch.zeros(max_pos, self.kvd, dtype=torch.float16, device="cuda") for _ in range(self.L)]
+            v = [torch.zeros(max_pos, self.kvd, dtype=torch.float16, device="cuda") for _ in range(self.L)]
+            for l in range(self.L):
+                k[l][:n_pasts[s]] = torch.randn(n_pasts[s], self.kvd, generator=g).half().cuda()
+                v[l][:n_pasts[s]] = torch.randn(n_pasts[s], self.kvd, generator=g).half().cuda()
+            self.k.append(k)
+            self.v.append(v)
+            self.kv.append(engine.KvCache.wrap([t.data_ptr() for t in k], [t.data_ptr() for t in v], max_pos, self.kvd,
+                                               keepalive=(k, v)))
+
+    def oracle_kv(self, s):
+        return [(self.k[s][l].float().cpu().clone(), self.v[s][l].float().cpu().clone()) for l in range(self.L)]
+
+
+def _check_stream(S, i, r, step_in, trailing, kv_o, s, seed, fi, seen):
+    hid, lg, clg = S.frame.inspect_stream(i)
+    hid_o, lg_o = om.talker_step(S.W, step_in, kv_o, S.n_past[i])
+    assert om.rel_l2(hid, hid_o) < REL, (i, om.rel_l2(hid, hid_o))
+    assert om.rel_l2(lg, lg_o) < REL, (i, om.rel_l2(lg, lg_o))
+    os_ = oracle_sampling(s)
+    assert r.codes[0] == om.sample(lg, 0, os_, seed, fi, talker_mods=(S.TV - 1024, S.W.cfg.codec_eos_id, seen)), i
+    for k in range(1, 16):
+        assert r.codes[k] == om.sample(clg[k - 1], k, os_, seed, fi), (i, k)
+    _, clo = om.code_predictor(S.W, torch.from_numpy(hid), r.codes[0], os_, seed, fi, teacher_codes=r.codes)
+    worst = max(om.rel_l2(clg[k], clo[k]) for k in range(15))
+    assert worst < REL, (i, worst)
+    # the new K/V rows went to this stream's own cache
+    for l in range(S.L):
+        assert om.rel_l2(S.k[i][l][S.n_past[i]].float().cpu(), kv_o[l][0][S.n_past[i]]) < 1e-3
+        assert om.rel_l2(S.v[i][l][S.n_past[i]].float().cpu(), kv_o[l][1][S.n_past[i]]) < 1e-3
+    want = om.step_embedding(S.W, r.codes, trailing)
+    assert om.rel_l2(dev_f32(S.frame.d_step_out_slot(i), S.H), want) < 1e-6
+
+
+@pytest.mark.parametrize("nb,n_pasts", [(2, [7, 40]), (4, [1, 33, 90, 200])])
+@pytest.mark.parametrize("rng", [capi.NAVI_RNG_PCG, capi.NAVI_RNG_PHILOX])
+def test_batched_frame_matches_oracle(small_navi, nb, n_pasts, rng):
+    S = Streams(small_navi, nb, n_pasts)
+    s = engine.Sampling(top_p=0.9, cp_top_p=0.9, rng=rng)
+    g = torch.Generator().manual_seed(nb * 10 + rng)
+    steps = [torch.randn(S.H, generator=g) for _ in range(nb)]
+    trail = [torch.randn(S.H, generator=g) for _ in range(nb)]
+    sd, td = [x.cuda() for x in steps], [x.cuda() for x in trail]
+    kv_o = [S.oracle_kv(i) for i in range(nb)]
+    seeds, fis = [1000 + 7 * i for i in range(nb)], [3 + i for i in range(nb)]
+    for i in range(nb):
+        S.frame.reset_slot(i)
+        S.frame.set_step_in_slot(i, sd[i].data_ptr())
+    res = S.frame.run_batch(list(range(nb)), S.kv, S.n_past, [t.data_ptr() for t in td], s, seeds, fis)
+    for i, r in enumerate(res):
+        assert r.ok, r.error
+        _check_stream(S, i, r, steps[i], trail[i], kv_o[i], s, seeds[i], fis[i], np.zeros(S.TV, np.uint8))
+
+
+def test_batched_frames_follow_each_stream(small_navi):
+    """Five frames of four streams in slots 3, 0, 2, 1: each stream's codes and step embeddings
+    are those of its own single-stream frames (slot 0 of a second frame object), frame by frame,
+    the repetition sets included."""
+    nb = 4
+    S = Streams(small_navi, nb, [5, 17, 29, 41])
+    T = Streams(small_navi, nb, [5, 17, 29, 41])      # the same caches, for the single-stream runs
+    solo = T.frame
+    s = engine.Sampling(top_p=0.9, cp_top_p=0.9, rng=capi.NAVI_RNG_PCG)
+    slots = [3, 0, 2, 1]
+    g = torch.Generator().manual_seed(5)
+    steps = [torch.randn(S.H, generator=g).cuda() for _ in range(nb)]
+    trail = [torch.randn(S.H, generator=g).cuda() for _ in range(nb)]
+    for i in range(nb):
+        S.frame.reset_slot(slots[i])
+        S.frame.set_step_in_slot(slots[i], steps[i].data_ptr())
+    batched, single = [[] for _ in range(nb)], [[] for _ in range(nb)]
+    n_past = list(S.n_past)
+    for f in range(5):
+        res = S.frame.run_batch(slots, S.kv, n_past, [t.data_ptr() for t in trail], s, [11 + i for i in range(nb)],
+                                [f] * nb)
+        for i, r in enumerate(res):
+            assert r.ok, r.error
+            batched[i].append(r.codes)
+        n_past = [n + 1 for n in n_past]
+    for i in range(nb):
+        solo.reset()
+        solo.set_step_in(steps[i].data_ptr())
+        for f in range(5):
+            r = solo.run(T.kv[i], T.n_past[i] + f, trail[i].data_ptr(), s, 11 + i, f)
+            assert r.ok, r.error
+            single[i].append(r.codes)
+    same = sum(batched[i][f] == single[i][f] for i in range(nb) for f in range(5))
+    # float sums may differ in the last bit (different attention splits), which can move a
+    # draw that sits on a boundary; with 20 frames of 16 draws every frame must match but one
+    assert same >= 19, (same, batched, single)
+
+
+def test_full_size_batched_frame_matches_oracle(full_navi):
+    """configs[1]+[2] shapes, four streams at KV 64, 128, 256 and 512."""
+    nb = 4
+    S = Streams(full_navi, nb, [64, 128, 256, 512], max_pos=600)
+    s = engine.Sampling(top_p=0.9, cp_top_p=0.9, rng=capi.NAVI_RNG_PHILOX)
+    g = torch.Generator().manual_seed(9)
+    steps = [torch.randn(S.H, generator=g) for _ in range(nb)]
+    trail = [torch.randn(S.H, generator=g) for _ in range(nb)]
+    sd, td = [x.cuda() for x in steps], [x.cuda() for x in trail]
+    kv_o = [S.oracle_kv(i) for i in range(nb)]
+    for i in range(nb):
+        S.frame.reset_slot(i)
+        S.frame.set_step_in_slot(i, sd[i].data_ptr())
+    res = S.frame.run_batch(list(range(nb)), S.kv, S.n_past, [t.data_ptr() for t in td], s, [5, 6, 7, 8], [2, 2, 2, 2])
+    for i, r in enumerate(res):
+        assert r.ok, r.error
+        _check_stream(S, i, r, steps[i], trail[i], kv_o[i], s, 5 + i, 2, np.zeros(S.TV, np.uint8))
+
+
+def test_batch_arguments_are_checked(small_navi):
+    S = Streams(small_navi, 2, [3, 4], max_pos=16)
+    s = engine.Sampling()
+    t = torch.zeros(S.H, device="cuda")
+    bad = S.frame.run_batch([0, 0], S.kv, [3, 4], [t.data_ptr()] * 2, s, [1, 2], [1, 1])
+    assert not bad[0].ok and bad[0].status == capi.NAVI_E_ARG
+    full = S.frame.run_batch([0, 1], S.kv, [3, 16], [t.data_ptr()] * 2, s, [1, 2], [1, 1])
+    assert not full[0].ok and full[0].status == capi.NAVI_E_KV_FULL
