@@ -214,6 +214,50 @@ def layer_bench(dev_ordinal: int, reps: int, warm: int, L: int = 256):
                          "bound_us": round(ab / (peak * 1e9) * 1e6, 3)}}
 
 
+def batch_bench(frame, p, local: int, steps: int, warm: int, L: int = 512):
+    """Batched decode (Frame::enqueue_batch): nb = 1, 2 and 4 streams per launch, each at KV
+    length L in its own cache, decoding one frame each per launch; device time of `steps`
+    launches back to back (CUDA events on the engine stream), frames/s = nb * launches / time."""
+    import torch
+    from navi_b200 import engine
+    tl = p.talker
+    kvd = tl.n_kv_head * tl.head_dim
+    cuda = f"cuda:{local}"
+    g = torch.Generator(device=cuda).manual_seed(77)
+    kvs = []
+    for _ in range(4):
+        k = [torch.randn(L + 8, kvd, generator=g, device=cuda).half() for _ in range(tl.n_layer)]
+        v = [torch.randn(L + 8, kvd, generator=g, device=cuda).half() for _ in range(tl.n_layer)]
+        kvs.append(engine.KvCache.wrap([t.data_ptr() for t in k], [t.data_ptr() for t in v], L + 8, kvd, keepalive=(k, v)))
+    tr = [torch.randn(tl.hidden, generator=g, device=cuda) for _ in range(4)]
+    s = engine.Sampling(temperature=0.9, top_k=50, top_p=0.9, repetition_penalty=1.05, cp_temperature=0.9, cp_top_k=50,
+                        cp_top_p=0.9, min_frames=2, rng=1)
+    stream = torch.cuda.ExternalStream(frame.dev.stream, device=cuda)
+    out = {}
+    for nb in (1, 2, 4):
+        slots = list(range(nb))
+        args = lambda f: (slots, kvs[:nb], [L] * nb, [t.data_ptr() for t in tr[:nb]], s, [101 + i for i in range(nb)], [f] * nb)
+        for i in range(nb):
+            frame.reset_slot(i)
+            frame.set_step_in_slot(i, tr[i].data_ptr())
+        for f in range(warm):
+            frame.enqueue_batch(*args(f))
+        assert all(r.ok for r in frame.collect_batch(nb))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(local)
+        e0.record(stream)
+        for f in range(steps):
+            frame.enqueue_batch(*args(warm + f))
+        e1.record(stream)
+        res = frame.collect_batch(nb)
+        torch.cuda.synchronize(local)
+        assert all(r.ok for r in res), res[0].error
+        ms = e0.elapsed_time(e1) / steps
+        out[str(nb)] = {"ms_per_launch": round(ms, 4), "frames_per_s": round(nb * 1000.0 / ms, 1)}
+    return {"workload": f"configs[1]+[2] frames of nb independent streams per launch at KV {L} each (one weight pass)",
+            "per_gpu": out}
+
+
 def vocoder_flops_per_frame(p) -> float:
     """2 x multiply-adds of every GEMM / conv of the decoder per frame (vocoder.hip:261-343)."""
     v = p.vocoder
@@ -286,19 +330,21 @@ def vocoder_bench(dev, w, reps: int = 20, chunks=(4, 16), warm: int = 3):
                              "passes run f16 hi + lo activation halves, so issued MMA work is twice the FLOPs"}
 
 
-def serving_bench(dev, w, rank: int, world: int, dist, streams: int = 8, frames: int = 400, n_text: int = 200):
+def serving_bench(dev, w, rank: int, world: int, dist, streams: int = 64, frames: int = 400, n_text: int = 200, group: int = 4):
     """configs[4], request-parallel: `streams` synthetic utterances (a 200-id text prompt of
     uniform ids, prefill, `frames` frames, their PCM streamed through the vocoder 4 frames
-    first, then 16 at a time: Graph::synth, graph.cpp:52-111) dealt round-robin to the
-    ranks, each rank running its streams one after another through the public API (host ids
-    in, host PCM out). Aggregate frames/s = all frames / the slowest rank's wall time; time
-    to first audio is SynthStats::ttfa_ms of every stream."""
+    first, then 16 at a time) dealt round-robin to the ranks. Each rank runs its streams in
+    groups of `group` through the public API (host ids in, host PCM out): Graph::synth_batch,
+    whose streams decode their frames together in batched launches (group 1: Graph::synth,
+    graph.cpp:52-111, one stream after another). Aggregate frames/s = all frames / the slowest
+    rank's wall time; time to first audio is SynthStats::ttfa_ms of every stream, counted from
+    the start of its group's call."""
     import numpy as np
     import torch
     from navi_b200 import engine, model_spec
     p = w.params
     cfg = model_spec.full_config(p.decoder_dim)
-    g = engine.Graph(dev, w, max_prompt_tokens=1024, max_frames=frames + 8, vocoder_chunk=16)
+    g = engine.Graph(dev, w, max_prompt_tokens=1024, max_frames=frames + 8, vocoder_chunk=16, max_streams=group)
     s = engine.Sampling(temperature=0.9, top_k=50, top_p=0.9, repetition_penalty=1.05, cp_temperature=0.9, cp_top_k=50,
                         cp_top_p=0.9, min_frames=frames, rng=1)
     spk = np.random.default_rng(4).standard_normal(p.talker.hidden).astype(np.float32)
@@ -308,23 +354,25 @@ def serving_bench(dev, w, rank: int, world: int, dist, streams: int = 8, frames:
         return ([cfg.im_start_id, cfg.assistant_id, 198] + r.integers(0, cfg.text_vocab, n_text).tolist()
                 + [cfg.im_end_id, 198, cfg.im_start_id, cfg.assistant_id, 198])
 
-    for j in range(2):                      # warm-up utterances
-        g.synth(ids_of(-1 - j), "english", spk, s, 5 + j, 24, first_batch=4, vocoder_batch=16)
+    # warm-up: one group of short utterances
+    g.synth_batch([(ids_of(-1 - j), spk, 5 + j, 24) for j in range(group)], "english", s, first_batch=4, vocoder_batch=16)
     mine = [j for j in range(streams) if j % world == rank]
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
     ttfa, rtf, pre, voc_ms, n_frames, pcm_samples = [], [], [], 0.0, 0, 0
-    for j in mine:
-        codes, pcm, st, _ = g.synth(ids_of(j), "english", spk, s, 77 + j, frames, first_batch=4, vocoder_batch=16)
-        assert st.n_frames == frames and pcm.size == frames * p.codec_upsample
-        ttfa.append(st.ttfa_ms)
-        rtf.append(st.rtf)
-        pre.append(st.prefill_ms)
-        voc_ms += st.vocoder_ms
-        n_frames += st.n_frames
-        pcm_samples += pcm.size
+    for k in range(0, len(mine), group):
+        js = mine[k:k + group]
+        for (codes, pcm, st) in g.synth_batch([(ids_of(j), spk, 77 + j, frames) for j in js], "english", s, first_batch=4,
+                                              vocoder_batch=16):
+            assert st.n_frames == frames and pcm.size == frames * p.codec_upsample
+            ttfa.append(st.ttfa_ms)
+            rtf.append(st.rtf)
+            pre.append(st.prefill_ms)
+            voc_ms += st.vocoder_ms
+            n_frames += st.n_frames
+            pcm_samples += pcm.size
     elapsed = time.perf_counter() - t0
     g.close()
     stats = {"elapsed": elapsed, "frames": n_frames, "ttfa": ttfa, "rtf": rtf, "pre": pre, "voc_ms": voc_ms}
@@ -337,7 +385,8 @@ def serving_bench(dev, w, rank: int, world: int, dist, streams: int = 8, frames:
     total = sum(o["frames"] for o in out)
     allt = [t for o in out for t in o["ttfa"]]
     return {"workload": f"configs[4]: {streams} streams x ({n_text}-id prompt, prefill, {frames} frames, PCM in batches "
-                        f"of 4 then 16), round-robin over {world} GPU(s), streams on a GPU one after another",
+                        f"of 4 then 16), round-robin over {world} GPU(s), on a GPU in groups of {group} decoded together "
+                        f"(batched frames)",
             "frames_per_s": round(total / slowest, 2), "ttfa_ms_p50": round(float(np.median(allt)), 3),
             "ttfa_ms_max": round(float(max(allt)), 3),
             "prefill_ms_p50": round(float(np.median([t for o in out for t in o["pre"]])), 3),
@@ -503,7 +552,7 @@ def run_ours(args):
     frame.set_profile(False)
 
     ms, e2e_ms, value, e2e_value = combine_ranks(ms, e2e_ms, world, dist, f"cuda:{local}")
-    serving = serving_bench(dev, w, rank, world, dist, streams=args.streams) if args.streams > 0 else None
+    serving = serving_bench(dev, w, rank, world, dist, streams=args.streams, group=args.group) if args.streams > 0 else None
     if rank == 0:
         ab = algorithmic_bytes(p, L)
         peak, kind = measured_peak()
@@ -529,6 +578,7 @@ def run_ours(args):
         }
         if serving:
             line["serving"] = serving
+        line["batched_decode"] = batch_bench(frame, p, local, steps=max(10, min(args.steps, 100)), warm=args.warmup)
         if args.layer:
             line["layer"] = layer_bench(local, reps=max(20, min(args.steps, 200)), warm=args.warmup)
         if args.vocoder:
@@ -570,7 +620,8 @@ def main():
     ap.add_argument("--vocoder-only", action="store_true", help="run only the configs[3] vocoder measurement")
     ap.add_argument("--voc-chunks", default="4,16", help="vocoder chunk lengths (frames), comma separated")
     ap.add_argument("--no-layer", dest="layer", action="store_false", help="skip the configs[0] single-layer line")
-    ap.add_argument("--streams", type=int, default=8, help="configs[4] utterances over all GPUs (64 = the full config; 0 = skip)")
+    ap.add_argument("--streams", type=int, default=64, help="configs[4] utterances over all GPUs (64 = the full config; 0 = skip)")
+    ap.add_argument("--group", type=int, default=4, choices=[1, 2, 3, 4], help="configs[4] streams decoded together per GPU")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -281,6 +281,32 @@ int navi_graph_synth(navi_graph * g, const int32_t * ids, int n_ids, const char 
                      int codes_cap, navi_pcm_fn on_pcm, void * user, navi_synth_stats * st);
 void navi_graph_destroy(navi_graph * g);
 
+/* ---- several utterances at once (no counterpart in the reference, which synthesises one
+ *      request at a time, server.cpp:32-84) ---- */
+/* As navi_graph_create, for up to max_streams (1..4) utterances per navi_graph_synth_batch
+ * call: one talker (KV cache) and one vocoder per stream, one frame kernel. */
+int navi_graph_create_streams(navi_device * dev, const navi_weights * w, const navi_frame_opts * opts, int max_prompt_tokens,
+                              int max_frames, int vocoder_chunk, int max_streams, navi_graph ** out);
+typedef struct navi_synth_request { /* one utterance of a batch (SynthRequest, graph.h:32-41, per stream) */
+    const int32_t * ids;
+    int n_ids;
+    const char * language;
+    const float * speaker;          /* host [hidden] */
+    uint64_t seed;
+    int max_frames;
+    int32_t * codes;                /* optional: room for codes_cap frames x 16 */
+    int codes_cap;
+} navi_synth_request;
+/* Receives one vocoder batch of stream `stream` (its index in the request array). */
+typedef void (*navi_stream_pcm_fn)(int stream, const float * pcm, int n_samples, void * user);
+/* Graph::synth for n requests (1..max_streams) at once: prompts and prefills one after
+ * another, then the running streams decode their frames together (navi_frame_run_batch,
+ * 4 / 2 / 1 streams per launch), each until its EOS or max_frames, with its frames vocoded
+ * in batches of first_batch then vocoder_batch on its own vocoder. Shared sampling settings;
+ * stats[i] per stream, times from the start of the call. on_pcm may be NULL (codes only). */
+int navi_graph_synth_batch(navi_graph * g, int n, const navi_synth_request * reqs, const navi_sampling * s, int first_batch,
+                           int vocoder_batch, navi_stream_pcm_fn on_pcm, void * user, navi_synth_stats * stats);
+
 /* ---- vocoder: replaces navi::qwen3tts::Vocoder (model/qwen3tts/vocoder.h:27-55) ----------- */
 
 typedef struct navi_vocoder navi_vocoder;

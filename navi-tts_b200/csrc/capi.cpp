@@ -604,6 +604,57 @@ int navi_graph_synth_ids(navi_graph * g, const int32_t * ids, int n_ids, const c
     });
 }
 
+int navi_graph_create_streams(navi_device * dev, const navi_weights * w, const navi_frame_opts * opts, int max_prompt_tokens,
+                              int max_frames, int vocoder_chunk, int max_streams, navi_graph ** out) {
+    return guard([&]() -> int {
+        if (!dev || !w || !out) return set_err(NAVI_E_ARG, "NULL argument");
+        if (vocoder_chunk < 0) return set_err(NAVI_E_ARG, "vocoder_chunk must be >= 0");
+        navi::qwen3tts::FrameOptions fo;
+        if (opts) {
+            fo.blocks_per_mp = opts->blocks_per_mp;
+            if (opts->deadline_us) fo.deadline_us = opts->deadline_us;
+        }
+        auto g = std::make_unique<navi_graph>();
+        g->g = navi::qwen3tts::Graph::create(*dev->dev, *w->w, fo, max_prompt_tokens, max_frames, vocoder_chunk, max_streams);
+        g->hidden = w->w->params().talker.hidden;
+        *out = g.release();
+        return NAVI_OK;
+    });
+}
+
+int navi_graph_synth_batch(navi_graph * g, int n, const navi_synth_request * reqs, const navi_sampling * s, int first_batch,
+                           int vocoder_batch, navi_stream_pcm_fn on_pcm, void * user, navi_synth_stats * stats) {
+    return guard([&]() -> int {
+        if (!g || !reqs || n < 1 || n > g->g->max_streams()) return set_err(NAVI_E_ARG, "bad argument");
+        if (first_batch < 0 || vocoder_batch < 0) return set_err(NAVI_E_ARG, "batch sizes must be >= 0");
+        if (on_pcm && !g->g->vocoder()) return set_err(NAVI_E_ARG, "graph created without a vocoder (vocoder_chunk = 0)");
+        std::vector<navi::qwen3tts::SynthRequest> rq;
+        std::vector<int> made(static_cast<size_t>(n), 0);
+        for (int i = 0; i < n; ++i) {
+            const navi_synth_request & r = reqs[i];
+            if (!r.ids || r.n_ids <= 0 || !r.speaker || (r.codes && r.codes_cap <= 0)) return set_err(NAVI_E_ARG, "bad request");
+            auto q = make_request(g, r.ids, r.n_ids, r.language, r.speaker, s, r.seed, r.codes ? std::min(r.max_frames, r.codes_cap) : r.max_frames);
+            q.first_batch = first_batch;
+            q.vocoder_batch = vocoder_batch;
+            rq.push_back(q);
+        }
+        navi::qwen3tts::Graph::StreamPcmFn pcm_fn;
+        if (on_pcm) pcm_fn = [&](int st, std::span<const float> pcm) { on_pcm(st, pcm.data(), static_cast<int>(pcm.size()), user); };
+        const auto out = g->g->synth_batch(
+            rq,
+            [&](int st, const std::int32_t * c) {
+                const navi_synth_request & r = reqs[st];
+                int & k = made[static_cast<size_t>(st)];
+                if (r.codes) std::memcpy(r.codes + static_cast<size_t>(k) * 16, c, 16 * sizeof(int32_t));
+                ++k;
+            },
+            pcm_fn);
+        if (stats)
+            for (int i = 0; i < n; ++i) put_stats(out[static_cast<size_t>(i)], &stats[i]);
+        return NAVI_OK;
+    });
+}
+
 int navi_graph_synth(navi_graph * g, const int32_t * ids, int n_ids, const char * language, const float * speaker,
                      const navi_sampling * s, uint64_t seed, int max_frames, int first_batch, int vocoder_batch, int32_t * codes,
                      int codes_cap, navi_pcm_fn on_pcm, void * user, navi_synth_stats * st) {

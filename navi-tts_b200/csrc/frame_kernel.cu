@@ -436,13 +436,17 @@ __device__ __forceinline__ void gemv_slice(At && at, uint32_t woff, int nr, int 
         }
 }
 
-// gemv_slice for nc input columns (1, 2 or 4).
-template <bool PAIR, class At, class Epi>
+// gemv_slice for nc input columns: 2 or 4 in batched programs, 1 or 2 otherwise.
+template <bool PAIR, bool BATCHED, class At, class Epi>
 __device__ __forceinline__ void gemv_cols(int nc, At && at, uint32_t woff, int nr, int K, const float * xin, int xstride, float * part,
                                           Epi && epi) {
-    if (nc == 4) gemv_slice<4, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
-    else if (nc == 2) gemv_slice<2, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
-    else gemv_slice<1, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
+    if constexpr (BATCHED) {
+        if (nc == 4) gemv_slice<4, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
+        else gemv_slice<2, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
+    } else {
+        if (nc == 2) gemv_slice<2, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
+        else gemv_slice<1, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
+    }
 }
 
 // Sums of squares of this thread's part of columns 0..ncol-1, folded per warp into the CTA
@@ -679,7 +683,7 @@ __device__ __forceinline__ void attn_pv(int ngroups, int GR, int HD, NOf && n_of
 // run as CTA-wide passes over the GR query heads of g. Partials (m, l, acc) go to the
 // exchange words; CTA G - nb * NH + (s * NH + h) combines head h of stream s in split order.
 // A single split writes the output directly.
-__device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int chunk, uint32_t tag, uint32_t ptag, int p) {
+__device__ __forceinline__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int chunk, uint32_t tag, uint32_t ptag, int p) {
     const Dims & d = A.d;
     constexpr int HD = KHD, GR = KGR;
     const int NH = d.NH, tid = threadIdx.x;
@@ -778,7 +782,7 @@ __device__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int c
 // columns). Batched: position pos of every stream, column c = stream c. The CTA of set
 // (layer, stream, KV head g) (cp_attn_role) keeps that K/V in shared memory slot across the
 // frame's positions.
-__device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, int chunk, uint32_t tag, uint32_t ptag, int p) {
+__device__ __forceinline__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, int chunk, uint32_t tag, uint32_t ptag, int p) {
     const Dims & d = A.d;
     constexpr int HD = KHD, GR = KGR;
     const int tid = threadIdx.x;
@@ -868,6 +872,10 @@ __device__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, int chunk
 
 // ---- the consumer: the phase program ----------------------------------------------------------------
 
+// The phase program, compiled twice: for the single-stream programs (BATCHED false: at most
+// two input columns) and for the batched ones (2 or 4 streams), so that each runs only the
+// code of its own shape (the phases run with a cold instruction cache).
+template <bool BATCHED>
 __device__ void consumer(const Args & A, Sm & S) {
     const Dims & d = A.d;
     const ModelW & W = *A.mw;
@@ -899,7 +907,7 @@ __device__ void consumer(const Args & A, Sm & S) {
             continue;
         }
 
-        if (ph.op == XOUT) {
+        if (!BATCHED && ph.op == XOUT) {
             // single-layer program: the residual stream after the layer, this CTA's rows as f32
             const bool ok = ll_fetch(A.w.x, d.H, ptag, S.xres, A, S.ctrl, p);
             if (!consumers_ok(S, ok)) break;
@@ -913,7 +921,7 @@ __device__ void consumer(const Args & A, Sm & S) {
             continue;
         }
 
-        if (ph.op == SAMPLE) {
+        if (BATCHED && ph.op == SAMPLE) {
             // batched: CTA s draws codebook ph.pos of stream s from its logits (the phase
             // before) and publishes the code; the other CTAs go on
             const int st = b, cb = ph.pos;
@@ -932,7 +940,7 @@ __device__ void consumer(const Args & A, Sm & S) {
             continue;
         }
 
-        if (ph.op == FINAL && A.nb > 1) {
+        if (BATCHED && ph.op == FINAL) {
             // batched: every stream's 16 codes (words of the SAMPLE phases) -> step embeddings
             bool ok = true;
             if (tid < A.nb * NCB) {
@@ -963,7 +971,7 @@ __device__ void consumer(const Args & A, Sm & S) {
             continue;
         }
 
-        if (ph.op == FINAL) {
+        if (!BATCHED && ph.op == FINAL) {
             const SampleScratch sc = sampler_scratch(S, Vmax);
             const bool ok = ll_fetch(A.w.clogits + static_cast<size_t>(NCB - 2) * d.CV, d.CV, ptag, sc.s, A, S.ctrl, p);
             if (!consumers_ok(S, ok)) break;
@@ -998,20 +1006,26 @@ __device__ void consumer(const Args & A, Sm & S) {
         const auto at = [&](uint32_t x) { return chunk_at(S, chunk, x); };
         float ss0 = 0.f, ss1 = 0.f, ss2 = 0.f, ss3 = 0.f;   // sums of squares of this thread's inputs, per column
         int nnorm = 0;                                      // columns whose norm scale is needed
-        const bool batched = A.nb > 1;
+        constexpr bool batched = BATCHED;
         auto stage = [&](int c, int i, float v) {
             S.xres[c * d.H + i] = v;
             xin[c * XS + i] = v * nw[i];
             const float q = v * v;
-            if (c == 0) ss0 += q;
-            else if (c == 1) ss1 += q;
-            else if (c == 2) ss2 += q;
-            else ss3 += q;
+            if constexpr (BATCHED) {
+                if (c == 0) ss0 += q;
+                else if (c == 1) ss1 += q;
+                else if (c == 2) ss2 += q;
+                else ss3 += q;
+            } else {
+                if (c == 0) ss0 += q;
+                else ss1 += q;
+            }
         };
         // after ll_fetch_cols of nc columns into xres: the same thread stages its elements
         auto stage_fetched = [&](int nc) {
             ll_each(nc * d.H, [&](int i) {
-                const int c = (i >= d.H ? 1 : 0) + (i >= 2 * d.H ? 1 : 0) + (i >= 3 * d.H ? 1 : 0);
+                int c = i >= d.H ? 1 : 0;
+                if constexpr (BATCHED) c += (i >= 2 * d.H ? 1 : 0) + (i >= 3 * d.H ? 1 : 0);
                 stage(c, i - c * d.H, S.xres[i]);
             });
         };
@@ -1043,7 +1057,7 @@ __device__ void consumer(const Args & A, Sm & S) {
                         const __half * row = (cb == 0 ? W.tl_emb : W.cp_emb[cb - 1]) + static_cast<size_t>(code) * d.H;
                         for (int i = tid; i < d.H; i += NCT) stage(c, i, __half2float(row[i]));
                     }
-                } else if (ph.layer == 0 && ph.pos == 0) {
+                } else if (!batched && ph.layer == 0 && ph.pos == 0) {
                     // code-predictor positions 0 and 1: sample codebook 0 first
                     const SampleScratch sc = sampler_scratch(S, Vmax);
                     bool okl = true;
@@ -1059,7 +1073,7 @@ __device__ void consumer(const Args & A, Sm & S) {
                         stage(0, i, A.hidden_in ? __ldcg(A.hidden_in + i) : S.hid[i]);
                         stage(1, i, __half2float(W.tl_emb[static_cast<size_t>(cb0) * d.H + i]));
                     }
-                } else if (ph.layer == 0) {
+                } else if (!batched && ph.layer == 0) {
                     const SampleScratch sc = sampler_scratch(S, Vmax);
                     const bool okl = ll_fetch(A.w.clogits + static_cast<size_t>(ph.pos - 2) * d.CV, d.CV, ptag, sc.s, A, S.ctrl, p);
                     if (!consumers_ok(S, okl && ok)) { ok = false; break; }
@@ -1114,26 +1128,29 @@ __device__ void consumer(const Args & A, Sm & S) {
         const float eps = (ph.op <= THEAD) ? d.eps_t : d.eps_c;
         const float sc0 = nnorm > 0 ? norm_scale(S, 0, d.H, eps) : 1.f;
         const float sc1 = nnorm > 1 ? norm_scale(S, 1, d.H, eps) : 1.f;
-        const float sc2 = nnorm > 2 ? norm_scale(S, 2, d.H, eps) : 1.f;
-        const float sc3 = nnorm > 3 ? norm_scale(S, 3, d.H, eps) : 1.f;
-        const auto scale_of = [&](int c) { return c == 0 ? sc0 : c == 1 ? sc1 : c == 2 ? sc2 : sc3; };
+        const float sc2 = BATCHED && nnorm > 2 ? norm_scale(S, 2, d.H, eps) : 1.f;
+        const float sc3 = BATCHED && nnorm > 3 ? norm_scale(S, 3, d.H, eps) : 1.f;
+        const auto scale_of = [&](int c) {
+            if constexpr (BATCHED) return c == 0 ? sc0 : c == 1 ? sc1 : c == 2 ? sc2 : sc3;
+            else return c == 0 ? sc0 : sc1;
+        };
         const int gcol = (ph.op == CHEAD && !batched) ? 1 : ncol;
         const uint32_t t = tag;
         switch (ph.op) {
             case TQKV: case CQKV:
-                gemv_cols<false>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
+                gemv_cols<false, BATCHED>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
                     ll_store(A.w.qkv + static_cast<size_t>(c) * d.QKV + r0 + u, y * scale_of(c), t);
                 });
                 break;
             case TO: case CO: case TDOWN: case CDOWN: {
                 const int K = (ph.op == TO || ph.op == CO) ? d.Q : d.F;
-                gemv_cols<false>(gcol, at, woff, nr, K, xin, XS, S.part, [&](int u, int c, float y, float) {
+                gemv_cols<false, BATCHED>(gcol, at, woff, nr, K, xin, XS, S.part, [&](int u, int c, float y, float) {
                     ll_store(A.w.x + static_cast<size_t>(c) * d.H + r0 + u, S.xres[c * d.H + r0 + u] + y, t);
                 });
                 break;
             }
             case TGU: case CGU:
-                gemv_cols<true>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float g, float up) {
+                gemv_cols<true, BATCHED>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float g, float up) {
                     const float s = scale_of(c);
                     g *= s;
                     up *= s;
@@ -1150,13 +1167,13 @@ __device__ void consumer(const Args & A, Sm & S) {
                         if (b == 0) A.w.hidden[static_cast<size_t>(c) * d.H + i] = hv;
                     }
                 }
-                gemv_cols<false>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
+                gemv_cols<false, BATCHED>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
                     ll_store(A.w.logits + static_cast<size_t>(c) * d.TV + r0 + u, y * scale_of(c), t);
                 });
                 break;
             }
             case CHEAD:
-                gemv_cols<false>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
+                gemv_cols<false, BATCHED>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
                     ll_store(A.w.clogits + (static_cast<size_t>(c) * (NCB - 1) + ph.pos - 1) * d.CV + r0 + u, y * scale_of(c), t);
                 });
                 break;
@@ -1186,7 +1203,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_frame(const __grid_constant__ Args 
     __syncthreads();
     if (unsigned long long * pb = prof_base(A)) pb[4 * A.nphase] = globaltimer();
     if (threadIdx.x >= NCT) producer(A, S);
-    else consumer(A, S);
+    else if (A.nb > 1) consumer<true>(A, S);
+    else consumer<false>(A, S);
 }
 
 // A standalone launch of the device sampler on given logits (one CTA), for parity tests.

@@ -47,8 +47,11 @@ public:
     // A talker (prompts up to max_prompt_tokens, KV for max_prompt_tokens + max_frames + 1
     // positions), a frame kernel and, for vocoder_chunk > 0, a vocoder decoding up to
     // vocoder_chunk frames per pass (graph.cpp:22-44 without tokenizer and speaker encoder).
+    // max_streams (1..4): the streams synth_batch takes, each with its own talker (KV cache)
+    // and vocoder state.
     static std::unique_ptr<Graph> create(const Device & dev, const DeviceWeights & w, const FrameOptions & fopt = {},
-                                         int max_prompt_tokens = 1024, int max_frames = 2048, int vocoder_chunk = 32);
+                                         int max_prompt_tokens = 1024, int max_frames = 2048, int vocoder_chunk = 32,
+                                         int max_streams = 1);
     ~Graph();
 
     using CodesFn = std::function<void(const std::int32_t * codes)>;
@@ -59,6 +62,20 @@ public:
     // the end, and each batch's 24 kHz f32 PCM goes to on_pcm. Throws navi::Error on a
     // failed frame or vocoder pass.
     SynthStats synth(const SynthRequest & req, const CodesFn & on_codes, const PcmFn & on_pcm = {});
+
+    // Up to max_streams requests at once: each stream gets its prompt and prefill on its own
+    // talker (and KV cache), frame 0, then the streams still running decode their frames
+    // together in batched launches (Frame::enqueue_batch, 4 / 2 / 1 streams per launch) until
+    // each reaches EOS or its max_frames; every stream's frames go through its own vocoder as
+    // in synth(). The requests must share their sampling settings (seeds, frame caps and
+    // prompts are per stream). Callbacks get the stream's index in reqs. Stream i's codes equal synth(reqs[i])'s
+    // whenever its draws agree, which they do unless a float rounding difference of the batched
+    // attention split moves a draw that sits on a boundary. Times are from the call's start.
+    using StreamCodesFn = std::function<void(int stream, const std::int32_t * codes)>;
+    using StreamPcmFn = std::function<void(int stream, std::span<const float> pcm)>;
+    std::vector<SynthStats> synth_batch(std::span<const SynthRequest> reqs, const StreamCodesFn & on_codes,
+                                        const StreamPcmFn & on_pcm = {});
+    int max_streams() const { return static_cast<int>(talkers_.size()); }
     Talker & talker();
     Frame & frame();
     Vocoder * vocoder();          // null when created with vocoder_chunk = 0
@@ -67,9 +84,9 @@ private:
     Graph() = default;
     int hidden_ = 0;
     int sample_rate_ = 24000, upsample_ = 1920;
-    std::unique_ptr<Talker> talker_;
+    std::vector<std::unique_ptr<Talker>> talkers_;     // [0] is synth()'s
     std::unique_ptr<Frame> frame_;
-    std::unique_ptr<Vocoder> vocoder_;
+    std::vector<std::unique_ptr<Vocoder>> vocoders_;
     std::vector<std::int32_t> codes_;
     std::vector<float> pcm_;
 };

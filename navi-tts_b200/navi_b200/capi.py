@@ -71,6 +71,12 @@ class ConvArgs(ctypes.Structure):
                 ("y", c_void_p), ("y_stride", c_int), ("rowmajor", c_int)]
 
 
+class SynthRequest(ctypes.Structure):
+    _fields_ = [("ids", POINTER(c_int32)), ("n_ids", c_int), ("language", c_char_p), ("speaker", POINTER(c_float)), ("seed", c_uint64),
+                ("max_frames", c_int), ("codes", POINTER(c_int32)), ("codes_cap", c_int)]
+
+
+STREAM_PCM_FN = ctypes.CFUNCTYPE(None, c_int, POINTER(c_float), c_int, c_void_p)
 STAGE_FN = ctypes.CFUNCTYPE(None, c_void_p, c_char_p, c_void_p, c_int, c_int)
 PCM_FN = ctypes.CFUNCTYPE(None, POINTER(c_float), c_int, c_void_p)
 
@@ -138,6 +144,9 @@ SIGNATURES = [
     ("navi_graph_synth", c_int, [c_void_p, POINTER(c_int32), c_int, c_char_p, POINTER(c_float), POINTER(Sampling), c_uint64, c_int,
                                  c_int, c_int, POINTER(c_int32), c_int, PCM_FN, c_void_p, POINTER(SynthStats)]),
     ("navi_graph_destroy", None, [c_void_p]),
+    ("navi_graph_create_streams", c_int, [c_void_p, c_void_p, POINTER(FrameOpts), c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
+    ("navi_graph_synth_batch", c_int, [c_void_p, c_int, POINTER(SynthRequest), POINTER(Sampling), c_int, c_int, STREAM_PCM_FN, c_void_p,
+                                       POINTER(SynthStats)]),
     ("navi_vocoder_create", c_int, [c_void_p, c_void_p, c_int, c_int, POINTER(c_void_p)]),
     ("navi_vocoder_reset", c_int, [c_void_p]),
     ("navi_vocoder_decode", c_int, [c_void_p, POINTER(c_int32), c_int, POINTER(c_float), ctypes.c_size_t]),

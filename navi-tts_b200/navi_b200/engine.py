@@ -222,11 +222,45 @@ class Graph:
     with vocoder_chunk > 0, the streaming vocoder."""
 
     def __init__(self, dev: Device, w: Weights, max_prompt_tokens: int = 1024, max_frames: int = 2048, deadline_us: int = 0,
-                 vocoder_chunk: int = 32):
+                 vocoder_chunk: int = 32, max_streams: int = 1):
         h = c_void_p()
         opts = capi.FrameOpts(1, deadline_us)
-        check(lib().navi_graph_create(dev.h, w.h, byref(opts), max_prompt_tokens, max_frames, vocoder_chunk, byref(h)))
+        if max_streams == 1:
+            check(lib().navi_graph_create(dev.h, w.h, byref(opts), max_prompt_tokens, max_frames, vocoder_chunk, byref(h)))
+        else:
+            check(lib().navi_graph_create_streams(dev.h, w.h, byref(opts), max_prompt_tokens, max_frames, vocoder_chunk, max_streams,
+                                                  byref(h)))
         self.h, self.dev, self.w = h, dev, w
+        self.max_streams = max_streams
+
+    def synth_batch(self, requests, language: str, s: Sampling, first_batch: int = 4, vocoder_batch: int = 16, audio: bool = True):
+        """Graph::synth_batch: requests = [(ids, speaker, seed, max_frames)], up to max_streams.
+        Returns per stream (codes [n_frames, 16], PCM f32 (empty without audio), stats)."""
+        import numpy as np
+        n = len(requests)
+        keep, reqs = [], (capi.SynthRequest * n)()
+        codes = []
+        for i, (ids, spk, seed, mf) in enumerate(requests):
+            ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+            spk = np.ascontiguousarray(np.asarray(spk, dtype=np.float32))
+            c = np.zeros((mf, 16), np.int32)
+            keep += [ids, spk]
+            codes.append(c)
+            reqs[i] = capi.SynthRequest(ids.ctypes.data_as(POINTER(c_int32)), len(ids), (language or "").encode(),
+                                        spk.ctypes.data_as(POINTER(ctypes.c_float)), seed, mf, c.ctypes.data_as(POINTER(c_int32)), mf)
+        chunks = [[] for _ in range(n)]
+
+        def take(stream, ptr, k, _user):
+            chunks[stream].append(np.ctypeslib.as_array(ptr, shape=(k,)).copy())
+
+        fn = capi.STREAM_PCM_FN(take) if audio else capi.STREAM_PCM_FN()
+        stats = (capi.SynthStats * n)()
+        check(lib().navi_graph_synth_batch(self.h, n, reqs, byref(s.c()), first_batch, vocoder_batch, fn, None, stats))
+        out = []
+        for i in range(n):
+            pcm = np.concatenate(chunks[i]) if chunks[i] else np.zeros(0, np.float32)
+            out.append((codes[i][:stats[i].n_frames], pcm, stats[i]))
+        return out
 
     def synth_ids(self, ids, language: str, speaker, s: Sampling, seed: int, max_frames: int):
         """(codes [n_frames, 16] int32, stats) of one utterance, without the vocoder."""

@@ -148,3 +148,44 @@ def test_graph_rejects_bad_requests_and_stays_usable(small_navi):
     assert np.array_equal(codes, codes2) and np.array_equal(pcm, pcm2)
     g.close()
     fresh.close()
+
+
+@pytest.mark.parametrize("n", [3, 4])
+def test_synth_batch_matches_single_streams(small_navi, n):
+    """Graph::synth_batch of n utterances (different texts, speakers, seeds and frame caps; 3
+    streams run as launches of 2 + 1) against Graph::synth of each alone: the same codes and
+    the same PCM, sample for sample (at these KV lengths the batched attention splits equal
+    the single-stream ones, so every float sum is the same), and per-stream stats."""
+    W = om.Weights.from_navi(small_navi)
+    dev = engine.Device(0)
+    w = engine.Weights(dev, small_navi)
+    g = engine.Graph(dev, w, max_prompt_tokens=64, max_frames=24, vocoder_chunk=8, max_streams=4)
+    one = engine.Graph(dev, w, max_prompt_tokens=64, max_frames=24, vocoder_chunk=8)
+    s = engine.Sampling(top_p=0.9, cp_top_p=0.9, min_frames=24)
+    reqs = []
+    for i in range(n):
+        ids = _ids(W.cfg, 5 + 3 * i, seed=20 + i)
+        spk = np.random.default_rng(30 + i).standard_normal(W.tl.hidden).astype(np.float32)
+        reqs.append((ids, spk, 500 + i, 12 + 3 * i))
+    out = g.synth_batch(reqs, "english", s, first_batch=4, vocoder_batch=8)
+    for i, (ids, spk, seed, mf) in enumerate(reqs):
+        codes, pcm, st = out[i]
+        c1, p1, s1, _ = one.synth(ids, "english", spk, s, seed, mf, first_batch=4, vocoder_batch=8)
+        assert np.array_equal(codes, c1), i
+        assert pcm.shape == p1.shape and np.array_equal(pcm, p1), i
+        assert st.n_frames == s1.n_frames == mf and st.hit_cap == 1
+        assert st.ttfa_ms > 0 and st.vocoder_ms > 0 and st.total_ms >= st.ttfa_ms
+
+
+def test_synth_batch_rejects_more_streams_than_created(small_navi):
+    W = om.Weights.from_navi(small_navi)
+    dev = engine.Device(0)
+    w = engine.Weights(dev, small_navi)
+    g = engine.Graph(dev, w, max_prompt_tokens=64, max_frames=8, vocoder_chunk=0, max_streams=2)
+    spk = np.zeros(W.tl.hidden, np.float32)
+    r = (_ids(W.cfg, 4, 1), spk, 1, 4)
+    with pytest.raises(capi.NaviError) as e:
+        g.synth_batch([r, r, r], "english", engine.Sampling(), audio=False)
+    assert e.value.status == capi.NAVI_E_ARG
+    codes = g.synth_batch([r, r], "english", engine.Sampling(), audio=False)
+    assert all(c.shape == (4, 16) for c, _, _ in codes)
