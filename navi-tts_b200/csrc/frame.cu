@@ -82,6 +82,7 @@ struct Frame::Impl {
     uint32_t scratch_floats = 0;
     int cp_keep_layers = 0;   // code-predictor layers held in L2 by cache policy
     uint64_t timeout_ns = 0;
+    uint32_t poll_ns = 0;
     int eos = 0, suppress_from = 0;
     size_t ll_bytes = 0;
     uint64_t * ll_base = nullptr;
@@ -204,6 +205,7 @@ struct Frame::Impl {
         A.eos_id = eos;
         A.suppress_from = suppress_from;
         A.timeout_ns = timeout_ns;
+        A.poll_ns = poll_ns;
         A.ring_bytes = M.ring;
         A.cp_keep_layers = cp_keep_layers;
         A.scratch_floats = scratch_floats;
@@ -299,6 +301,7 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     I.eos = p.codec_eos_id;
     I.suppress_from = tp.vocab - 1024;   // HF suppress_tokens = range(vocab - 1024, vocab) minus EOS (frame.hip:760)
     I.timeout_ns = (opt.deadline_us ? opt.deadline_us : 200000ull) * 1000ull;
+    if (const char * env = std::getenv("NAVI_POLL_NS")) I.poll_ns = static_cast<uint32_t>(std::atoi(env));
 
     // weight tables: the frame streams its own copy of every matrix, re-laid out per CTA slice
     I.grid = dev.info().multiprocessors * opt.blocks_per_mp;

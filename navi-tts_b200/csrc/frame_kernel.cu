@@ -251,6 +251,7 @@ __device__ __noinline__ bool ll_fetch_plan(const uint64_t * src, int cols, int c
             }
             if (!pend) break;
             if (t0 == 0) t0 = globaltimer();
+            if (A.poll_ns) __nanosleep(A.poll_ns);
 #pragma unroll
             for (int k = 0; k < MAXK; ++k)
                 if ((pend >> k) & 1u) ll_load2(at[k], w[k][0], w[k][1]);
@@ -291,6 +292,7 @@ __device__ __noinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag,
             }
             if (!pend) break;
             if (t0 == 0) t0 = globaltimer();
+            if (A.poll_ns) __nanosleep(A.poll_ns);
 #pragma unroll
             for (int k = 0; k < MAXK; ++k)
                 if ((pend >> k) & 1u) ll_load2(src + base + 2 * NCT * k, w[k][0], w[k][1]);

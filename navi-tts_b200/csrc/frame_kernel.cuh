@@ -156,6 +156,7 @@ struct Args {
     int min_frames, rng;
     int eos_id, suppress_from;
     uint64_t timeout_ns;
+    uint32_t poll_ns;          // pause between polls of exchange words that are not there yet (0: none)
     uint32_t ring_bytes;
     int xcols;                 // columns of the residual copy in shared memory (max(2, nb))
     int cp_slots;              // code-predictor K/V slots in shared memory (sets / grid, rounded up)
