@@ -1,8 +1,11 @@
 // navi-b200: the command-line front of this build, over the C ABI (include/navi_b200.h).
-// Mirrors the reference's `info` and `synth` subcommands (runtime/cli/main.cpp:59-72,
-// 247-279) without the text tokenizer: `synth` takes the prompt's token ids.
+// Mirrors the reference's `info`, `synth` and `bench` subcommands (runtime/cli/main.cpp:59-72,
+// 219-279; runtime/bench/bench.cpp:98-155) without the text tokenizer and the speaker encoder:
+// `synth` and `bench` take the prompt's token ids and a speaker embedding.
 //
 //   navi-b200 info  [--model FILE] [--device N]
+//   navi-b200 bench --model FILE [--ids "i,j,..." | --ids-file FILE] [--speaker EMB] [--seed N]
+//                   [--repeats N] [--warmup N] [--batch N] [--max-frames N] [--out results.jsonl]
 //   navi-b200 synth --model FILE (--ids "i,j,..." | --ids-file FILE) --speaker EMB --out OUT.wav
 //                   [--seed N] [--language L] [--max-frames N] [--greedy] [--first-batch N]
 //                   [--batch N] [--device N]
@@ -13,7 +16,9 @@
 // little-endian float32. The WAV is 16-bit PCM mono at the codec's sample rate.
 #include "../../include/navi_b200.h"
 
+#include <algorithm>
 #include <chrono>
+#include <ctime>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -30,8 +35,8 @@ namespace {
 struct Args {
     std::string cmd, model, ids, ids_file, speaker, out, language = "english";
     unsigned long long seed = 0;
-    int max_frames = 600, first_batch = 4, batch = 16, device = 0;
-    bool greedy = false;
+    int max_frames = 600, first_batch = 4, batch = 16, device = 0, repeats = 1, warmup = 1;
+    bool greedy = false, seed_set = false, batch_set = false;
 };
 
 int usage(const char * argv0) {
@@ -40,8 +45,10 @@ int usage(const char * argv0) {
                  "usage: %s info  [--model FILE] [--device N]\n"
                  "       %s synth --model FILE (--ids \"i,j,...\" | --ids-file FILE) --speaker EMB(.npy|.f32) --out OUT.wav\n"
                  "                [--seed N] [--language L] [--max-frames N] [--greedy] [--first-batch N] [--batch N] [--device N]\n"
+                 "       %s bench --model FILE [--ids \"i,j,...\" | --ids-file FILE] [--speaker EMB] [--seed N] [--repeats N]\n"
+                 "                [--warmup N] [--batch N] [--max-frames N] [--device N] [--out results.jsonl]\n"
                  "  --ids: the tokenised prompt template (3 header ids, the text, 5 trailer ids)\n",
-                 navi_version(), argv0, argv0);
+                 navi_version(), argv0, argv0, argv0);
     return 2;
 }
 
@@ -61,10 +68,12 @@ Args parse(int argc, char ** argv) {
         else if (s == "--speaker") a.speaker = next("--speaker");
         else if (s == "--out") a.out = next("--out");
         else if (s == "--language") a.language = next("--language");
-        else if (s == "--seed") a.seed = std::stoull(next("--seed"));
+        else if (s == "--seed") { a.seed = std::stoull(next("--seed")); a.seed_set = true; }
+        else if (s == "--repeats") a.repeats = std::stoi(next("--repeats"));
+        else if (s == "--warmup") a.warmup = std::stoi(next("--warmup"));
         else if (s == "--max-frames") a.max_frames = std::stoi(next("--max-frames"));
         else if (s == "--first-batch") a.first_batch = std::stoi(next("--first-batch"));
-        else if (s == "--batch") a.batch = std::stoi(next("--batch"));
+        else if (s == "--batch") { a.batch = std::stoi(next("--batch")); a.batch_set = true; }
         else if (s == "--device") a.device = std::stoi(next("--device"));
         else if (s == "--greedy") a.greedy = true;
         else throw std::invalid_argument("unknown option " + s);
@@ -125,7 +134,7 @@ void put_u32(std::vector<uint8_t> & o, uint32_t v) { for (int k = 0; k < 4; ++k)
 void put_u16(std::vector<uint8_t> & o, uint16_t v) { o.push_back(static_cast<uint8_t>(v)); o.push_back(static_cast<uint8_t>(v >> 8)); }
 
 // 16-bit PCM mono RIFF/WAVE: samples clamped to [-1, 1], scaled by 32767, rounded to nearest.
-void write_wav(const std::string & path, const std::vector<float> & pcm, int rate) {
+std::vector<uint8_t> wav_bytes(const std::vector<float> & pcm, int rate) {
     const uint32_t data = static_cast<uint32_t>(pcm.size() * 2);
     std::vector<uint8_t> o;
     o.reserve(44 + data);
@@ -145,8 +154,53 @@ void write_wav(const std::string & path, const std::vector<float> & pcm, int rat
         const float c = std::fmax(-1.f, std::fmin(1.f, x));
         put_u16(o, static_cast<uint16_t>(static_cast<int16_t>(std::lrintf(c * 32767.f))));
     }
+    return o;
+}
+
+void write_wav(const std::string & path, const std::vector<float> & pcm, int rate) {
+    const std::vector<uint8_t> o = wav_bytes(pcm, rate);
     std::ofstream f(path, std::ios::binary);
     if (!f.write(reinterpret_cast<const char *>(o.data()), static_cast<std::streamsize>(o.size()))) throw std::runtime_error("cannot write " + path);
+}
+
+// SHA-256 (FIPS 180-4) of a byte string, as lowercase hex: the WAV digest the reference's bench
+// line records (bench.cpp:150-151).
+std::string sha256_hex(const std::vector<uint8_t> & msg) {
+    static const uint32_t K[64] = {
+        0x428a2f98, 0x71374491, 0xb5c0fbcf, 0xe9b5dba5, 0x3956c25b, 0x59f111f1, 0x923f82a4, 0xab1c5ed5, 0xd807aa98, 0x12835b01, 0x243185be,
+        0x550c7dc3, 0x72be5d74, 0x80deb1fe, 0x9bdc06a7, 0xc19bf174, 0xe49b69c1, 0xefbe4786, 0x0fc19dc6, 0x240ca1cc, 0x2de92c6f, 0x4a7484aa,
+        0x5cb0a9dc, 0x76f988da, 0x983e5152, 0xa831c66d, 0xb00327c8, 0xbf597fc7, 0xc6e00bf3, 0xd5a79147, 0x06ca6351, 0x14292967, 0x27b70a85,
+        0x2e1b2138, 0x4d2c6dfc, 0x53380d13, 0x650a7354, 0x766a0abb, 0x81c2c92e, 0x92722c85, 0xa2bfe8a1, 0xa81a664b, 0xc24b8b70, 0xc76c51a3,
+        0xd192e819, 0xd6990624, 0xf40e3585, 0x106aa070, 0x19a4c116, 0x1e376c08, 0x2748774c, 0x34b0bcb5, 0x391c0cb3, 0x4ed8aa4a, 0x5b9cca4f,
+        0x682e6ff3, 0x748f82ee, 0x78a5636f, 0x84c87814, 0x8cc70208, 0x90befffa, 0xa4506ceb, 0xbef9a3f7, 0xc67178f2};
+    uint32_t h[8] = {0x6a09e667, 0xbb67ae85, 0x3c6ef372, 0xa54ff53a, 0x510e527f, 0x9b05688c, 0x1f83d9ab, 0x5be0cd19};
+    std::vector<uint8_t> m(msg);
+    const uint64_t bits = static_cast<uint64_t>(msg.size()) * 8;
+    m.push_back(0x80);
+    while (m.size() % 64 != 56) m.push_back(0);
+    for (int k = 7; k >= 0; --k) m.push_back(static_cast<uint8_t>(bits >> (8 * k)));
+    auto rotr = [](uint32_t x, int n) { return (x >> n) | (x << (32 - n)); };
+    for (size_t blk = 0; blk < m.size(); blk += 64) {
+        uint32_t w[64];
+        for (int t = 0; t < 16; ++t)
+            w[t] = (uint32_t(m[blk + 4 * t]) << 24) | (uint32_t(m[blk + 4 * t + 1]) << 16) | (uint32_t(m[blk + 4 * t + 2]) << 8) |
+                   uint32_t(m[blk + 4 * t + 3]);
+        for (int t = 16; t < 64; ++t) {
+            const uint32_t s0 = rotr(w[t - 15], 7) ^ rotr(w[t - 15], 18) ^ (w[t - 15] >> 3);
+            const uint32_t s1 = rotr(w[t - 2], 17) ^ rotr(w[t - 2], 19) ^ (w[t - 2] >> 10);
+            w[t] = w[t - 16] + s0 + w[t - 7] + s1;
+        }
+        uint32_t a = h[0], b = h[1], c = h[2], d = h[3], e = h[4], f = h[5], g = h[6], hh = h[7];
+        for (int t = 0; t < 64; ++t) {
+            const uint32_t t1 = hh + (rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25)) + ((e & f) ^ (~e & g)) + K[t] + w[t];
+            const uint32_t t2 = (rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22)) + ((a & b) ^ (a & c) ^ (b & c));
+            hh = g; g = f; f = e; e = d + t1; d = c; c = b; b = a; a = t1 + t2;
+        }
+        h[0] += a; h[1] += b; h[2] += c; h[3] += d; h[4] += e; h[5] += f; h[6] += g; h[7] += hh;
+    }
+    char out[65];
+    for (int k = 0; k < 8; ++k) std::snprintf(out + 8 * k, 9, "%08x", h[k]);
+    return std::string(out, 64);
 }
 
 int cmd_info(const Args & a) {
@@ -241,6 +295,101 @@ int cmd_synth(const Args & a) {
     return 0;
 }
 
+// The reference's bench harness (runtime/bench/bench.h:27-43, bench.cpp:98-155): load, then the
+// utterance through the serving path (Graph::synth) after `warmup` untimed ones, one JSON line per
+// repeat with the same fields. This build has no tokenizer or speaker encoder: the prompt is --ids
+// (default: a fixed 20-token text in the Qwen template, for models with the full text vocabulary)
+// and the speaker --speaker (default: the zero embedding). talker_ms / cp_ms stay null, as in the
+// reference: the frame is one launch.
+int cmd_bench(const Args & a) {
+    if (a.model.empty()) throw std::invalid_argument("bench needs --model");
+    using clock = std::chrono::steady_clock;
+    auto ms_since = [](clock::time_point t) { return std::chrono::duration<double, std::milli>(clock::now() - t).count(); };
+    const auto t0 = clock::now();
+    navi_params p{};
+    int n_tensors = 0, n_missing = 0, n_bad = 0, n_unused = 0;
+    check(navi_model_probe(a.model.c_str(), &p, &n_tensors, &n_missing, &n_bad, &n_unused), "model");
+    const double map_ms = ms_since(t0);
+    std::vector<int32_t> ids;
+    if (!a.ids.empty() || !a.ids_file.empty()) {
+        std::string id_text = a.ids;
+        if (id_text.empty()) {
+            const std::vector<char> b = read_file(a.ids_file);
+            id_text.assign(b.data(), b.size());
+        }
+        ids = parse_ids(id_text);
+    } else {
+        if (p.text_vocab < 151936) throw std::invalid_argument("bench: this model's text vocabulary needs --ids");
+        ids = {151644, 77091, 198};   // <|im_start|> assistant \n
+        for (int i = 1; i <= 20; ++i) ids.push_back(static_cast<int32_t>((static_cast<uint64_t>(i) * 2654435761ull) % 150000ull));
+        for (int32_t t : {151645, 198, 151644, 77091, 198}) ids.push_back(t);
+    }
+    if (ids.size() < 9) throw std::invalid_argument("--ids: the template alone is 8 ids; the text needs at least one more");
+    std::vector<float> spk = a.speaker.empty() ? std::vector<float>(static_cast<size_t>(p.talker.hidden), 0.f) : read_f32(a.speaker);
+    if (static_cast<int>(spk.size()) != p.talker.hidden) throw std::invalid_argument("--speaker size is not the talker's hidden size");
+    navi_device * dev = nullptr;
+    check(navi_device_open(a.device, &dev), "device open");
+    navi_device_info di{};
+    check(navi_device_get_info(dev, &di), "device info");
+    const auto tu = clock::now();
+    navi_weights * w = nullptr;
+    check(navi_weights_upload(dev, a.model.c_str(), &w), "weights");
+    const double upload_ms = ms_since(tu);
+    const uint64_t wbytes = navi_weights_bytes(w);
+    // streaming batches 4 then 16 (graph.h:29-30), or --batch throughout
+    const int first = a.batch_set ? a.batch : 4, batch = a.batch_set ? a.batch : 16;
+    navi_frame_opts fo{1, 0};
+    navi_graph * g = nullptr;
+    check(navi_graph_create(dev, w, &fo, static_cast<int>(ids.size()) + 16, a.max_frames, batch, &g), "graph");
+    navi_sampling s{};
+    s.temperature = p.temperature; s.top_k = p.top_k; s.top_p = p.top_p; s.repetition_penalty = p.repetition_penalty;
+    s.cp_temperature = p.cp_temperature; s.cp_top_k = p.cp_top_k; s.cp_top_p = p.cp_top_p; s.min_frames = 2; s.rng = NAVI_RNG_PCG;
+    const uint64_t seed = a.seed_set ? a.seed : 2;   // the reference's bench seed (bench.h:21)
+    char name[512] = {0};
+    for (int r = 0; r < std::max(1, a.repeats); ++r) {
+        PcmSink sink;
+        navi_synth_stats st{};
+        for (int i = 0; i < a.warmup + 1; ++i) {
+            sink = PcmSink{};
+            check(navi_graph_synth(g, ids.data(), static_cast<int>(ids.size()), a.language.c_str(), spk.data(), &s, seed, a.max_frames, first,
+                                   batch, nullptr, 0, on_pcm, &sink, &st),
+                  "synth");
+        }
+        const std::vector<uint8_t> wav = wav_bytes(sink.pcm, p.sample_rate);
+        if (!a.out.empty() && a.out.size() > 4 && a.out.compare(a.out.size() - 4, 4, ".wav") == 0) write_wav(a.out, sink.pcm, p.sample_rate);
+        const std::time_t now = std::time(nullptr);
+        char ts[32];
+        std::strftime(ts, sizeof ts, "%Y-%m-%dT%H:%M:%SZ", std::gmtime(&now));
+        std::snprintf(name, sizeof name, "%s", a.model.c_str());
+        std::ostringstream j;
+        j.setf(std::ios::fixed);
+        j.precision(4);
+        const double nf = st.n_frames;
+        j << "{\"ts\": \"" << ts << "\", \"git\": \"" << navi_version() << "\", \"gfx\": \"sm_" << di.cc_major << di.cc_minor
+          << "a\", \"device\": \"" << di.name << "\", \"multiprocessors\": " << di.multiprocessors << ", \"model\": \"" << name
+          << "\", \"weight_bytes\": " << wbytes << ", \"load_map_ms\": " << map_ms << ", \"load_upload_ms\": " << upload_ms
+          << ", \"upload_gbps\": " << (upload_ms > 0 ? wbytes / 1e6 / upload_ms : 0.0) << ", \"prefill_ms\": " << st.prefill_ms
+          << ", \"frame_ms\": " << (nf ? st.frames_ms / nf : 0.0) << ", \"talker_ms\": null, \"cp_ms\": null, \"vocoder_ms_per_frame\": "
+          << (nf ? st.vocoder_ms / nf : 0.0) << ", \"ttfa_ms\": " << st.ttfa_ms << ", \"rtf\": " << st.rtf << ", \"n_frames\": " << st.n_frames
+          << ", \"wav_sha256\": \"" << sha256_hex(wav) << "\", \"text\": \"" << ids.size() - 8 << " text token ids\", \"seed\": " << seed
+          << "}";
+        const std::string line = j.str();
+        if (a.out.empty() || (a.out.size() > 4 && a.out.compare(a.out.size() - 4, 4, ".wav") == 0)) {
+            std::printf("%s\n", line.c_str());
+        } else {
+            std::ofstream f(a.out, std::ios::app);
+            if (!f) throw std::runtime_error("cannot open " + a.out + " for append");
+            f << line << '\n';
+            std::fprintf(stderr, "appended to %s: %d frames, prefill %.1f ms, %.2f ms/frame, ttfa %.1f ms, RTF %.4f\n", a.out.c_str(),
+                         st.n_frames, st.prefill_ms, nf ? st.frames_ms / nf : 0.0, st.ttfa_ms, st.rtf);
+        }
+    }
+    navi_graph_destroy(g);
+    navi_weights_free(w);
+    navi_device_close(dev);
+    return 0;
+}
+
 } // namespace
 
 int main(int argc, char ** argv) {
@@ -249,6 +398,7 @@ int main(int argc, char ** argv) {
         const Args a = parse(argc, argv);
         if (a.cmd == "info") return cmd_info(a);
         if (a.cmd == "synth") return cmd_synth(a);
+        if (a.cmd == "bench") return cmd_bench(a);
         return usage(argv[0]);
     } catch (const std::invalid_argument & e) {
         std::fprintf(stderr, "navi-b200: %s\n", e.what());

@@ -78,3 +78,51 @@ def test_cli_synth_matches_graph(small_navi, tmp_path):
     assert r.returncode == 0, r.stderr
     assert np.array_equal(_read_wav(out2)[1], s16)
     g.close()
+
+
+def test_cli_bench_argument_errors(small_navi):
+    r = _run("bench")
+    assert r.returncode == 2 and "bench needs --model" in r.stderr
+    r = _run("bench", "--model", small_navi)      # the small model's text vocabulary has no default prompt
+    assert r.returncode == 2 and "needs --ids" in r.stderr
+    r = _run("bench", "--repeats")
+    assert r.returncode == 2 and "--repeats needs a value" in r.stderr
+
+
+@pytest.mark.gpu
+def test_cli_bench_line(small_navi, tmp_path):
+    """`bench` (runtime/bench/bench.cpp:98-155): one JSON line per repeat with the reference's
+    BenchResult fields; the WAV digest is the SHA-256 of the WAV it makes (also written with
+    --out X.wav), and that WAV is `synth`'s for the same ids, speaker, seed and batching."""
+    import hashlib
+    import json
+    from oracle import model as om
+    W = om.Weights.from_navi(small_navi)
+    cfg = W.cfg
+    rng = np.random.default_rng(3)
+    ids = [cfg.im_start_id, cfg.assistant_id, 198 % cfg.text_vocab] + rng.integers(0, cfg.text_vocab, 6).tolist() + \
+        [cfg.im_end_id, 198 % cfg.text_vocab, cfg.im_start_id, cfg.assistant_id, 198 % cfg.text_vocab]
+    idarg = ",".join(map(str, ids))
+    out = tmp_path / "b.wav"
+    r = _run("bench", "--model", small_navi, "--ids", idarg, "--seed", "5", "--max-frames", "12", "--repeats", "2",
+             "--warmup", "1", "--out", str(out))
+    assert r.returncode == 0, r.stderr
+    lines = [json.loads(x) for x in r.stdout.strip().splitlines()]
+    assert len(lines) == 2
+    keys = {"ts", "git", "gfx", "device", "multiprocessors", "model", "weight_bytes", "load_map_ms", "load_upload_ms", "upload_gbps",
+            "prefill_ms", "frame_ms", "talker_ms", "cp_ms", "vocoder_ms_per_frame", "ttfa_ms", "rtf", "n_frames", "wav_sha256", "text",
+            "seed"}
+    for j in lines:
+        assert keys <= set(j), keys - set(j)
+        assert j["n_frames"] <= 12 and j["frame_ms"] > 0 and j["weight_bytes"] > 0 and j["talker_ms"] is None and j["seed"] == 5
+    assert lines[0]["wav_sha256"] == lines[1]["wav_sha256"] == hashlib.sha256(out.read_bytes()).hexdigest()
+    np.zeros(W.tl.hidden, np.float32).tofile(tmp_path / "zero.f32")
+    syn = tmp_path / "s.wav"
+    r = _run("synth", "--model", small_navi, "--ids", idarg, "--speaker", str(tmp_path / "zero.f32"), "--out", str(syn), "--seed", "5",
+             "--max-frames", "12", "--first-batch", "4", "--batch", "16")
+    assert r.returncode == 0, r.stderr
+    assert syn.read_bytes() == out.read_bytes()
+    jl = tmp_path / "results.jsonl"
+    r = _run("bench", "--model", small_navi, "--ids", idarg, "--seed", "5", "--max-frames", "4", "--out", str(jl))
+    assert r.returncode == 0 and "appended to" in r.stderr
+    assert len(jl.read_text().splitlines()) == 1
