@@ -165,3 +165,23 @@ class Tokenizer:
         <|im_start|>assistant\\n", tokenised -- the ids navi_talker_build_prompt and
         navi_graph_synth take."""
         return self.encode(f"<|im_start|>assistant\n{text}<|im_end|>\n<|im_start|>assistant\n")
+
+
+def main(argv=None) -> int:
+    """python -m navi_b200.tokenizer --model model.navi [--raw] TEXT: prints the prompt's ids
+    (the `--ids-file` of `navi-b200 synth`), or with --raw the ids of TEXT alone."""
+    import argparse
+    import sys
+    ap = argparse.ArgumentParser(description="Qwen3 text tokenizer of a .navi")
+    ap.add_argument("--model", required=True)
+    ap.add_argument("--raw", action="store_true", help="tokenise TEXT without the prompt template")
+    ap.add_argument("text")
+    a = ap.parse_args(argv)
+    tok = Tokenizer.from_navi(a.model)
+    ids = tok.encode(a.text) if a.raw else tok.prompt_ids(a.text)
+    sys.stdout.write(" ".join(map(str, ids)) + "\n")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -5,8 +5,10 @@ with NFC, the Qwen2 pre-tokenizer pattern (Split, isolated) + ByteLevel without 
 and the chat special tokens as added tokens -- the components of Qwen2TokenizerFast. The ids
 must be equal on every test string (scripts, digits, punctuation runs, white space and
 newlines, combining marks that NFC composes, emoji, special tokens inside the text), and
-decoding must give the NFC text back. The reference's own fixture (tests/reference/
-tokenizer_cases.json) needs the released vocabulary, which is not available.
+decoding must give the NFC text back. The reference's own tokenizer gate (tests/reference/
+tokenizer_cases.json) needs the released vocabulary; its strings are pinned instead on a
+committed synthetic vocabulary against the reference tokenizer's own outputs
+(tests/golden/ref_tokenizer_small.json).
 """
 import json
 import unicodedata
@@ -85,3 +87,36 @@ def test_prompt_template_and_navi(pair, tmp_path):
         b.put_tensor(f"tokenizer.{t}", U8, np.frombuffer((d / f).read_bytes(), dtype=np.uint8))
     b.save(tmp_path / "tok.navi")
     assert Tokenizer.from_navi(tmp_path / "tok.navi").encode("Grüße, Straße 42") == ours.encode("Grüße, Straße 42")
+
+
+def _golden():
+    import os
+    with open(os.path.join(os.path.dirname(__file__), "golden", "ref_tokenizer_small.json"), encoding="utf-8") as f:
+        return json.load(f)
+
+
+def test_reference_tokenizer_pins():
+    """The reference engine's own tokenizer (its tokenizer gate's strings and ours) on a committed
+    synthetic vocabulary, from tests/golden/make_tokenizer_golden.py: ids and decoded bytes equal."""
+    g = _golden()
+    tok = Tokenizer(g["vocab_json"], g["merges_txt"], g["config_json"])
+    assert len(g["cases"]) >= 80
+    for c in g["cases"]:
+        ids = tok.encode(c["text"])
+        assert ids == c["ref_ids"] == c["hf_ids"], c["text"]
+        assert tok.decode(ids).encode("utf-8").hex() == c["ref_decoded_hex"], c["text"]
+
+
+def test_command_line(pair, tmp_path, capsys):
+    import numpy as np
+    from navi_b200 import tokenizer as tk
+    from navi_b200.navi_file import U8, NaviBuilder
+    _, ours, d = pair
+    b = NaviBuilder()
+    for f, t in (("vocab.json", "vocab.json"), ("merges.txt", "merges.txt"), ("tokenizer_config.json", "config.json")):
+        b.put_tensor(f"tokenizer.{t}", U8, np.frombuffer((d / f).read_bytes(), dtype=np.uint8))
+    b.save(tmp_path / "m.navi")
+    assert tk.main(["--model", str(tmp_path / "m.navi"), "Hello there."]) == 0
+    assert [int(x) for x in capsys.readouterr().out.split()] == ours.prompt_ids("Hello there.")
+    assert tk.main(["--model", str(tmp_path / "m.navi"), "--raw", "Hello"]) == 0
+    assert [int(x) for x in capsys.readouterr().out.split()] == ours.encode("Hello")
