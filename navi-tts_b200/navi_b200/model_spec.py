@@ -16,6 +16,8 @@ predictor 2, codec 3, everything else 4.
 """
 from __future__ import annotations
 
+import json
+
 import zlib
 from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field, replace
@@ -331,15 +333,27 @@ def synth_tensor(name: str, shape: tuple, seed_offset: int = 0, pool=None) -> np
     return out
 
 
+def synthetic_tokenizer(c: ModelConfig) -> tuple[str, str, str]:
+    """Tokenizer files of a synthetic model: a byte-level vocabulary (ids 0..255, one per byte,
+    no merges) with the chat tokens as added tokens at the model's ids ("assistant" one of
+    them, so the prompt template has the 3-id header and 5-id trailer the talker expects)."""
+    from .tokenizer import BYTE_TO_CHAR
+    vocab = {BYTE_TO_CHAR[b]: b for b in range(256)}
+    added = {c.im_start_id: "<|im_start|>", c.im_end_id: "<|im_end|>", c.assistant_id: "assistant", c.tts_pad_id: "<|tts_pad|>",
+             c.tts_bos_id: "<|tts_text_bos|>", c.tts_eos_id: "<|tts_text_eod|>"}
+    cfg = {"added_tokens_decoder": {str(i): {"content": t, "lstrip": False, "rstrip": False, "single_word": False,
+                                             "normalized": False, "special": t.startswith("<|")} for i, t in sorted(added.items())}}
+    return json.dumps(vocab, ensure_ascii=False), "#version: 0.2\n", json.dumps(cfg)
+
+
 def write_synthetic(path: str | Path, c: ModelConfig, seed_offset: int = 0, threads: int = 8,
                     include: callable = None) -> int:
     """Writes a complete `.navi` for config `c` with seeded random weights.
     `include(name)` can drop tensors (they are then absent from the table)."""
     w = NaviBuilder()
     kv_entries(w, c)
-    # tokenizer files: absent from this build's scope, written as placeholders so the table validates
-    for tname in ("tokenizer.vocab.json", "tokenizer.merges.txt", "tokenizer.config.json"):
-        w.put_tensor(tname, U8, np.frombuffer(b"{}", dtype=np.uint8))
+    for tname, text in zip(("tokenizer.vocab.json", "tokenizer.merges.txt", "tokenizer.config.json"), synthetic_tokenizer(c)):
+        w.put_tensor(tname, U8, np.frombuffer(text.encode("utf-8"), dtype=np.uint8))
     table = [(n, s) for n, s in tensor_table(c) if include is None or include(n)]
     with ThreadPoolExecutor(max_workers=threads) as ex:
         arrays = [synth_tensor(n, s, seed_offset, ex) for n, s in table]
