@@ -126,7 +126,7 @@ struct Frame::Impl {
     // Per-mode launch shape: streams nb -> shared-memory layout and ring.
     struct Mode {
         int xcols = 2, cp_slots = 1;
-        uint32_t part_floats = 0, ring = 0, smem = 0;
+        uint32_t part_floats = 0, ysum_off = 0, ring = 0, smem = 0;
     };
     Mode modes[MAX_B + 1];
 
@@ -210,6 +210,7 @@ struct Frame::Impl {
         A.cp_keep_layers = cp_keep_layers;
         A.scratch_floats = scratch_floats;
         A.part_floats = M.part_floats;
+        A.ysum_off = M.ysum_off;
         A.prof = prof_on ? prof : nullptr;
         if (prof_on) NAVI_CUDA(cudaMemsetAsync(prof, 0, static_cast<size_t>(PROF_STRIDE) * grid * sizeof(unsigned long long), stream));
         A.prof_cta = prof_cta;
@@ -487,7 +488,9 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
         Impl::Mode & M = I.modes[nb];
         M.xcols = std::max(2, nb);
         M.cp_slots = cdiv(nb * d.CL * d.NKV, G);
-        M.part_floats = static_cast<uint32_t>(NCW * 2 * M.xcols * max_nr);   // per warp: columns x (gate, up) x rows
+        // per warp: columns x (gate, up) x rows; then the summed [columns x (gate, up)][rows]
+        M.ysum_off = static_cast<uint32_t>(NCW * 2 * M.xcols * max_nr);
+        M.part_floats = M.ysum_off + static_cast<uint32_t>(2 * M.xcols * max_nr);
         if (nb * d.NKV > G) fail("frame: batched attention needs a CTA per (stream, KV head)", NAVI_E_SHAPE);
         const SmemLayout L0 = smem_layout(d, 0, I.scratch_floats, M.part_floats, M.xcols, M.cp_slots);
         if (L0.total + 16384 > optin) fail("frame: shared memory too small for the model shape", NAVI_E_SHAPE);

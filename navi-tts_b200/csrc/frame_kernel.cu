@@ -264,9 +264,10 @@ __device__ __noinline__ bool ll_fetch_plan(const uint64_t * src, int cols, int c
 }
 
 // Exchange words [0, n) (n even) into dst[0, n): ll_fetch_plan's single-run case without
-// its index arithmetic (the common case: one input vector per phase).
+// its index arithmetic (the common case: one input vector per phase), up to 6 pair loads per
+// thread at once, so a 3,072-word vector (the down projections' input) takes one round.
 __device__ __noinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag, float * dst, const Args & A, Ctrl * ctrl, int phase) {
-    constexpr int MAXK = 4;
+    constexpr int MAXK = 6;
     for (int base = 2 * threadIdx.x; base < n; base += 2 * NCT * MAXK) {
         uint64_t w[MAXK][2];
         unsigned pend = 0;
@@ -361,9 +362,10 @@ __device__ __forceinline__ bool wait_chunk_local(const Args & A, Sm & S, int chu
 // j-interleaved, so the live lanes of a warp read consecutive 16-byte words; x chunks are
 // broadcasts. Per-warp sums are folded over j with shuffles, written to
 // part[warp][value][row], and after a consumer barrier thread (value, row) adds the NCW warp
-// sums in warp order and calls epi(unit, column, y[, y_pair]).
-template <int NC, bool PAIR, class At, class Epi>
-__device__ __forceinline__ void gemv_slice(At && at, uint32_t woff, int nr, int K, const float * xin, int xstride, float * part, Epi && epi) {
+// sums in warp order into ys[(column * 2 + value) * nr + row] (gemv_owned's mapping).
+template <int NC, bool PAIR>
+__device__ __forceinline__ void gemv_slice(const Sm & S, int chunk, uint32_t woff, int nr, int K, const float * xin, int xstride, float * part,
+                                           float * ys) {
     constexpr int NV = NC * (PAIR ? 2 : 1);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nk = K >> 3;
@@ -377,8 +379,8 @@ __device__ __forceinline__ void gemv_slice(At && at, uint32_t woff, int nr, int 
     const int j = lane >> lr;
     // this warp's K range of the slice (and of the up slice after it), each contiguous in the ring
     const uint32_t kb = static_cast<uint32_t>(nr) * 16u;
-    const __half * wa = reinterpret_cast<const __half *>(at(woff + static_cast<uint32_t>(k0) * kb));
-    const __half * wb = PAIR ? reinterpret_cast<const __half *>(at(woff + static_cast<uint32_t>(nk + k0) * kb)) : wa;
+    const __half * wa = reinterpret_cast<const __half *>(chunk_at(S, chunk, woff + static_cast<uint32_t>(k0) * kb));
+    const __half * wb = PAIR ? reinterpret_cast<const __half *>(chunk_at(S, chunk, woff + static_cast<uint32_t>(nk + k0) * kb)) : wa;
     // rows beyond 32 lanes (small grids) are taken in rounds of R2. Every loop stays rolled:
     // this code runs with a cold instruction cache in every phase (the phases in between
     // evict it), and an unrolled body costs more in instruction fetch than it saves in
@@ -434,21 +436,37 @@ __device__ __forceinline__ void gemv_slice(At && at, uint32_t woff, int nr, int 
                 y += part[(w * NV + c * (PAIR ? 2 : 1)) * nr + row];
                 if constexpr (PAIR) y2 += part[(w * NV + c * 2 + 1) * nr + row];
             }
-            epi(row, c, y, y2);
+            ys[2 * c * nr + row] = y;
+            if constexpr (PAIR) ys[(2 * c + 1) * nr + row] = y2;
         }
 }
 
-// gemv_slice for nc input columns: 2 or 4 in batched programs, 1 or 2 otherwise.
-template <bool PAIR, bool BATCHED, class At, class Epi>
-__device__ __forceinline__ void gemv_cols(int nc, At && at, uint32_t woff, int nr, int K, const float * xin, int xstride, float * part,
-                                          Epi && epi) {
+// gemv_slice for nc input columns (2 or 4 in batched programs, 1 or 2 otherwise). The phase
+// loop has one call site per shape (plain or gate/up pair), shared by every phase that streams
+// a matrix; the phases differ only in the epilogue each applies to the sums afterwards
+// (gemv_owned). So consecutive phases run the same GEMV instructions, which are then still in
+// the SM's instruction cache, instead of each phase fetching its own copy.
+template <bool PAIR, bool BATCHED>
+__device__ __forceinline__ void gemv_sums(int nc, const Sm & S, int chunk, uint32_t woff, int nr, int K, const float * xin, int xstride,
+                                          float * part, float * ys) {
     if constexpr (BATCHED) {
-        if (nc == 4) gemv_slice<4, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
-        else gemv_slice<2, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
+        if (nc == 4) gemv_slice<4, PAIR>(S, chunk, woff, nr, K, xin, xstride, part, ys);
+        else gemv_slice<2, PAIR>(S, chunk, woff, nr, K, xin, xstride, part, ys);
     } else {
-        if (nc == 2) gemv_slice<2, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
-        else gemv_slice<1, PAIR>(at, woff, nr, K, xin, xstride, part, epi);
+        if (nc == 2) gemv_slice<2, PAIR>(S, chunk, woff, nr, K, xin, xstride, part, ys);
+        else gemv_slice<1, PAIR>(S, chunk, woff, nr, K, xin, xstride, part, ys);
     }
+}
+
+// The (row, column) sums of gemv_sums that this thread wrote (column c is owned by the threads
+// [c * TPC, (c + 1) * TPC), TPC = NCT / nc), so its epilogue reads them without a barrier.
+template <class F>
+__device__ __forceinline__ void gemv_owned(int nc, int nr, F && f) {
+    const int TPC = nc == 1 ? NCT : nc == 2 ? NCT / 2 : NCT / 4;
+    const int tid = threadIdx.x;
+    const int c = (tid >= TPC) + (tid >= 2 * TPC) + (tid >= 3 * TPC);
+    if (c < nc)
+        for (int row = tid - c * TPC; row < nr; row += TPC) f(row, c);
 }
 
 // Sums of squares of this thread's part of columns 0..ncol-1, folded per warp into the CTA
@@ -896,6 +914,26 @@ __device__ void consumer(const Args & A, Sm & S) {
         const int ns = phase_segments(A, W, ph, b, R, seg, r0, r1);
         const int nr = r1 - r0;
 
+        // single stream: every draw (codebook 0 before code-predictor position 0, codebook
+        // pos - 1 before position pos, codebook 15 in FINAL) runs at this one place, so the
+        // sampler's code is shared by the sixteen draws of a frame
+        int drawn = 0;
+        if (!BATCHED && (ph.op == FINAL || (ph.op == CQKV && ph.layer == 0))) {
+            const int cb = ph.op == FINAL ? NCB - 1 : ph.pos == 0 ? 0 : ph.pos - 1;
+            const int V = cb == 0 ? d.TV : d.CV;
+            const SampleScratch sc = sampler_scratch(S, Vmax);
+            bool okl = true;
+            if (cb == 0 && A.logits_in) {
+                for (int i = tid; i < d.TV; i += NCT) sc.s[i] = __ldcg(A.logits_in + i);
+            } else {
+                okl = ll_fetch(cb == 0 ? A.w.logits : A.w.clogits + static_cast<size_t>(cb - 1) * d.CV, V, ptag, sc.s, A, S.ctrl, p);
+            }
+            if (!consumers_ok(S, okl)) break;
+            if (ph.op == FINAL) stamp(A, p, 0);
+            drawn = sample_cta<NCT>(V, sample_cfg(A, cb, 0), sc, BID);
+            if (tid == 0) S.codes[cb] = drawn;
+        }
+
         if (ph.op == TATTN || ph.op == CATTN) {
             if (ns > 0 && !wait_chunk(A, S, chunk, p)) break;
             const bool ok = ph.op == TATTN ? talker_attention(A, S, ph, chunk, tag, ptag, p) : cp_attention(A, S, ph, chunk, tag, ptag, p);
@@ -974,12 +1012,7 @@ __device__ void consumer(const Args & A, Sm & S) {
         }
 
         if (!BATCHED && ph.op == FINAL) {
-            const SampleScratch sc = sampler_scratch(S, Vmax);
-            const bool ok = ll_fetch(A.w.clogits + static_cast<size_t>(NCB - 2) * d.CV, d.CV, ptag, sc.s, A, S.ctrl, p);
-            if (!consumers_ok(S, ok)) break;
-            stamp(A, p, 0);
-            const int code = sample_cta<NCT>(d.CV, sample_cfg(A, NCB - 1, 0), sc, BID);
-            if (tid == 0) S.codes[NCB - 1] = code;
+            // codebook 15 was drawn above
             named_sync(BID, NCT);
             for (int i = R.h0 + tid; i < R.h1; i += NCT) {
                 float v = __half2float(W.tl_emb[static_cast<size_t>(S.codes[0]) * d.H + i]);
@@ -1060,29 +1093,17 @@ __device__ void consumer(const Args & A, Sm & S) {
                         for (int i = tid; i < d.H; i += NCT) stage(c, i, __half2float(row[i]));
                     }
                 } else if (!batched && ph.layer == 0 && ph.pos == 0) {
-                    // code-predictor positions 0 and 1: sample codebook 0 first
-                    const SampleScratch sc = sampler_scratch(S, Vmax);
-                    bool okl = true;
-                    if (A.logits_in) {
-                        for (int i = tid; i < d.TV; i += NCT) sc.s[i] = __ldcg(A.logits_in + i);
-                    } else {
-                        okl = ll_fetch(A.w.logits, d.TV, ptag, sc.s, A, S.ctrl, p);
-                    }
-                    if (!consumers_ok(S, okl && ok)) { ok = false; break; }
-                    const int cb0 = sample_cta<NCT>(d.TV, sample_cfg(A, 0, 0), sc, BID);
-                    if (tid == 0) S.codes[0] = cb0;
-                    for (int i = tid; i < d.H; i += NCT) {
-                        stage(0, i, A.hidden_in ? __ldcg(A.hidden_in + i) : S.hid[i]);
-                        stage(1, i, __half2float(W.tl_emb[static_cast<size_t>(cb0) * d.H + i]));
-                    }
+                    // code-predictor positions 0 and 1: the hidden and codebook 0's embedding
+                    if (ok)
+                        for (int i = tid; i < d.H; i += NCT) {
+                            stage(0, i, A.hidden_in ? __ldcg(A.hidden_in + i) : S.hid[i]);
+                            stage(1, i, __half2float(W.tl_emb[static_cast<size_t>(drawn) * d.H + i]));
+                        }
                 } else if (!batched && ph.layer == 0) {
-                    const SampleScratch sc = sampler_scratch(S, Vmax);
-                    const bool okl = ll_fetch(A.w.clogits + static_cast<size_t>(ph.pos - 2) * d.CV, d.CV, ptag, sc.s, A, S.ctrl, p);
-                    if (!consumers_ok(S, okl && ok)) { ok = false; break; }
-                    const int code = sample_cta<NCT>(d.CV, sample_cfg(A, ph.pos - 1, 0), sc, BID);
-                    if (tid == 0) S.codes[ph.pos - 1] = code;
-                    const __half * row = W.cp_emb[ph.pos - 2] + static_cast<size_t>(code) * d.H;
-                    for (int i = tid; i < d.H; i += NCT) stage(0, i, __half2float(row[i]));
+                    // position pos: the embedding of codebook pos - 1's draw
+                    const __half * row = W.cp_emb[ph.pos - 2] + static_cast<size_t>(drawn) * d.H;
+                    if (ok)
+                        for (int i = tid; i < d.H; i += NCT) stage(0, i, __half2float(row[i]));
                 } else if (ok) {
                     ok = ll_fetch_cols(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
                     if (ok) stage_fetched(ncol);
@@ -1138,45 +1159,46 @@ __device__ void consumer(const Args & A, Sm & S) {
         };
         const int gcol = (ph.op == CHEAD && !batched) ? 1 : ncol;
         const uint32_t t = tag;
+        if (ph.op == THEAD)
+            for (int c = 0; c < ncol; ++c) {
+                const float s = scale_of(c);
+                for (int i = tid; i < d.H; i += NCT) {
+                    const float hv = xin[c * XS + i] * s;
+                    if (!batched) S.hid[i] = hv;
+                    else if (i >= R.h0 && i < R.h1) ll_store(A.w.hid_x + static_cast<size_t>(c) * d.H + i, hv, t);
+                    if (b == 0) A.w.hidden[static_cast<size_t>(c) * d.H + i] = hv;
+                }
+            }
+        // the sums (one GEMV call site per shape), then this phase's epilogue on the rows this thread owns
+        float * ys = S.part + A.ysum_off;
+        {
+            const int K = (ph.op == TDOWN || ph.op == CDOWN) ? d.F : (ph.op == TO || ph.op == CO) ? d.Q : d.H;
+            if (ph.op == TGU || ph.op == CGU) gemv_sums<true, BATCHED>(gcol, S, chunk, woff, nr, K, xin, XS, S.part, ys);
+            else gemv_sums<false, BATCHED>(gcol, S, chunk, woff, nr, K, xin, XS, S.part, ys);
+        }
+        const auto y_of = [&](int u, int c) { return ys[2 * c * nr + u]; };
         switch (ph.op) {
             case TQKV: case CQKV:
-                gemv_cols<false, BATCHED>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
-                    ll_store(A.w.qkv + static_cast<size_t>(c) * d.QKV + r0 + u, y * scale_of(c), t);
+                gemv_owned(gcol, nr, [&](int u, int c) { ll_store(A.w.qkv + static_cast<size_t>(c) * d.QKV + r0 + u, y_of(u, c) * scale_of(c), t); });
+                break;
+            case TO: case CO: case TDOWN: case CDOWN:
+                gemv_owned(gcol, nr, [&](int u, int c) {
+                    ll_store(A.w.x + static_cast<size_t>(c) * d.H + r0 + u, S.xres[c * d.H + r0 + u] + y_of(u, c), t);
                 });
                 break;
-            case TO: case CO: case TDOWN: case CDOWN: {
-                const int K = (ph.op == TO || ph.op == CO) ? d.Q : d.F;
-                gemv_cols<false, BATCHED>(gcol, at, woff, nr, K, xin, XS, S.part, [&](int u, int c, float y, float) {
-                    ll_store(A.w.x + static_cast<size_t>(c) * d.H + r0 + u, S.xres[c * d.H + r0 + u] + y, t);
-                });
-                break;
-            }
             case TGU: case CGU:
-                gemv_cols<true, BATCHED>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float g, float up) {
+                gemv_owned(gcol, nr, [&](int u, int c) {
                     const float s = scale_of(c);
-                    g *= s;
-                    up *= s;
+                    const float g = y_of(u, c) * s, up = ys[(2 * c + 1) * nr + u] * s;
                     ll_store(A.w.h + static_cast<size_t>(c) * d.F + r0 + u, g / (1.f + expf(-g)) * up, t);
                 });
                 break;
-            case THEAD: {
-                for (int c = 0; c < ncol; ++c) {
-                    const float s = scale_of(c);
-                    for (int i = tid; i < d.H; i += NCT) {
-                        const float hv = xin[c * XS + i] * s;
-                        if (!batched) S.hid[i] = hv;
-                        else if (i >= R.h0 && i < R.h1) ll_store(A.w.hid_x + static_cast<size_t>(c) * d.H + i, hv, t);
-                        if (b == 0) A.w.hidden[static_cast<size_t>(c) * d.H + i] = hv;
-                    }
-                }
-                gemv_cols<false, BATCHED>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
-                    ll_store(A.w.logits + static_cast<size_t>(c) * d.TV + r0 + u, y * scale_of(c), t);
-                });
+            case THEAD:
+                gemv_owned(gcol, nr, [&](int u, int c) { ll_store(A.w.logits + static_cast<size_t>(c) * d.TV + r0 + u, y_of(u, c) * scale_of(c), t); });
                 break;
-            }
             case CHEAD:
-                gemv_cols<false, BATCHED>(gcol, at, woff, nr, d.H, xin, XS, S.part, [&](int u, int c, float y, float) {
-                    ll_store(A.w.clogits + (static_cast<size_t>(c) * (NCB - 1) + ph.pos - 1) * d.CV + r0 + u, y * scale_of(c), t);
+                gemv_owned(gcol, nr, [&](int u, int c) {
+                    ll_store(A.w.clogits + (static_cast<size_t>(c) * (NCB - 1) + ph.pos - 1) * d.CV + r0 + u, y_of(u, c) * scale_of(c), t);
                 });
                 break;
             default: break;

@@ -163,6 +163,7 @@ struct Args {
     int cp_keep_layers;        // code-predictor layers whose weights the producer asks L2 to keep
     uint32_t scratch_floats;
     uint32_t part_floats;
+    uint32_t ysum_off;         // GEMV sums [2 * columns][rows] at part + ysum_off (after the per-warp partials)
     unsigned long long * prof;   // optional trace: [4 * nphase + 1] globaltimer stamps on CTA prof_cta,
     int prof_cta;                // or, prof_cta < 0, on every CTA b at prof + b * PROF_STRIDE
 };
