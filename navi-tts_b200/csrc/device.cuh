@@ -213,4 +213,14 @@ __device__ __forceinline__ float dot8h(uint4 w, float4 a, float4 b) {
     return (p0 + p1) + (p2 + p3);
 }
 
+// 8 f16 (16 bytes) times 8 f32 accumulated on the packed fp32 pipe (FFMA2, sm_100): acc.x takes
+// the even products, acc.y the odd ones, each as a chain of fused multiply-adds.
+__device__ __forceinline__ float2 dot8h2(uint4 w, float4 a, float4 b, float2 acc) {
+    acc = __ffma2_rn(__half22float2(*reinterpret_cast<const __half2 *>(&w.x)), make_float2(a.x, a.y), acc);
+    acc = __ffma2_rn(__half22float2(*reinterpret_cast<const __half2 *>(&w.y)), make_float2(a.z, a.w), acc);
+    acc = __ffma2_rn(__half22float2(*reinterpret_cast<const __half2 *>(&w.z)), make_float2(b.x, b.y), acc);
+    acc = __ffma2_rn(__half22float2(*reinterpret_cast<const __half2 *>(&w.w)), make_float2(b.z, b.w), acc);
+    return acc;
+}
+
 } // namespace navi::dev
