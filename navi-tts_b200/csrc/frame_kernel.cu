@@ -707,6 +707,7 @@ __device__ __forceinline__ void attn_pv(int ngroups, int GR, int HD, NOf && n_of
 // run as CTA-wide passes over the GR query heads of g. Partials (m, l, acc) go to the
 // exchange words; CTA G - nb * NH + (s * NH + h) combines head h of stream s in split order.
 // A single split writes the output directly.
+template <bool BATCHED>
 __device__ __forceinline__ bool talker_attention(const Args & A, Sm & S, const Phase & ph, int chunk, uint32_t tag, uint32_t ptag, int p) {
     const Dims & d = A.d;
     constexpr int HD = KHD, GR = KGR;
@@ -716,6 +717,7 @@ __device__ __forceinline__ bool talker_attention(const Args & A, Sm & S, const P
     const uint32_t WST = HD + 2;
     int st, g, sp;
     const bool has = talker_attn_role(A, b, st, g, sp);
+    if constexpr (!BATCHED) st = 0;
     if (has) {
         const int Sp = A.attn_split[st], pos = A.n_past[st], ch = A.attn_chunk[st];
         const int NPS = ch + 1;                            // score slots per head
@@ -775,9 +777,9 @@ __device__ __forceinline__ bool talker_attention(const Args & A, Sm & S, const P
         stamp(A, p, 2);
     }
     // combine: CTA G - nb * NH + (s * NH + h) reduces head h of stream s over its splits, in split order
-    const int ch_ = b - (G - A.nb * NH);
+    const int ch_ = b - (G - (BATCHED ? A.nb : 1) * NH);
     if (ch_ >= 0) {
-        const int cs = ch_ / NH, h = ch_ - cs * NH, Sp = A.attn_split[cs];
+        const int cs = BATCHED ? ch_ / NH : 0, h = ch_ - cs * NH, Sp = A.attn_split[cs];
         if (Sp > 1) {
             named_sync(BID, NCT);                   // this CTA's own split (if any) is done with its scratch
             float * pb = S.scratch;                 // [Sp][WST]: m, l, acc[HD] of every split
@@ -806,13 +808,14 @@ __device__ __forceinline__ bool talker_attention(const Args & A, Sm & S, const P
 // columns). Batched: position pos of every stream, column c = stream c. The CTA of set
 // (layer, stream, KV head g) (cp_attn_role) keeps that K/V in shared memory slot across the
 // frame's positions.
+template <bool BATCHED>
 __device__ __forceinline__ bool cp_attention(const Args & A, Sm & S, const Phase & ph, int chunk, uint32_t tag, uint32_t ptag, int p) {
     const Dims & d = A.d;
     constexpr int HD = KHD, GR = KGR;
     const int tid = threadIdx.x;
     int st, g, slot;
     if (!cp_attn_role(A, blockIdx.x, ph.layer, st, g, slot)) return true;
-    const bool batched = A.nb > 1;
+    constexpr bool batched = BATCHED;
     const int ncol = batched ? 1 : ph.ncol, pos = ph.pos, col0 = batched ? st : 0;
     const float * qn = reinterpret_cast<const float *>(chunk_at(S, chunk, 0));
     const float * kn = reinterpret_cast<const float *>(chunk_at(S, chunk, HD * 4));
@@ -940,7 +943,7 @@ __device__ void consumer(const Args & A, Sm & S) {
 
         if (ph.op == TATTN || ph.op == CATTN) {
             if (ns > 0 && !wait_chunk(A, S, chunk, p)) break;
-            const bool ok = ph.op == TATTN ? talker_attention(A, S, ph, chunk, tag, ptag, p) : cp_attention(A, S, ph, chunk, tag, ptag, p);
+            const bool ok = ph.op == TATTN ? talker_attention<BATCHED>(A, S, ph, chunk, tag, ptag, p) : cp_attention<BATCHED>(A, S, ph, chunk, tag, ptag, p);
             if (!ok) break;
             if (ns > 0) {
                 named_sync(BID, NCT);
