@@ -14,6 +14,7 @@
 
 namespace navi::fk {
 __global__ void k_frame(const __grid_constant__ Args A);
+__global__ void k_frame_batch(const __grid_constant__ Args A);
 
 // Re-lays out an R x K row-major f16 matrix into per-CTA slices (layout in frame_kernel.cuh):
 // each thread moves one 8-column chunk (16 bytes).
@@ -217,7 +218,8 @@ struct Frame::Impl {
         last_nphase = A.nphase;
         NAVI_CUDA(cudaEventRecord(ev0, stream));
         void * args[] = {&A};
-        const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(&k_frame), dim3(grid), dim3(NTHR), args, M.smem, stream);
+        const void * kern = nb > 1 ? reinterpret_cast<const void *>(&k_frame_batch) : reinterpret_cast<const void *>(&k_frame);
+        const cudaError_t e = cudaLaunchCooperativeKernel(kern, dim3(grid), dim3(NTHR), args, M.smem, stream);
         if (e != cudaSuccess) {
             (void) cudaGetLastError();
             err = std::string("cooperative launch failed: ") + cudaGetErrorString(e);
@@ -508,10 +510,12 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
         if (const char * env = std::getenv("NAVI_L2_KEEP_LAYERS")) keep = std::atoi(env);
         I.cp_keep_layers = std::max(0, std::min(keep, d.CL));
     }
-    NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_frame), cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
-    int occ = 0;
-    NAVI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, reinterpret_cast<const void *>(&k_frame), NTHR, smem_max));
-    if (occ < 1) fail("frame: k_frame cannot be resident with " + std::to_string(smem_max) + " bytes of shared memory", NAVI_E_SHAPE);
+    for (const void * kern : {reinterpret_cast<const void *>(&k_frame), reinterpret_cast<const void *>(&k_frame_batch)}) {
+        NAVI_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
+        int occ = 0;
+        NAVI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, NTHR, smem_max));
+        if (occ < 1) fail("frame: the frame kernel cannot be resident with " + std::to_string(smem_max) + " bytes of shared memory", NAVI_E_SHAPE);
+    }
     NAVI_CUDA(cudaEventCreate(&I.ev0));
     NAVI_CUDA(cudaEventCreate(&I.ev1));
     void * h = nullptr;

@@ -216,9 +216,9 @@ __device__ __forceinline__ float val_of(uint64_t w) { return __uint_as_float(sta
 // a phase's inputs. Returns this thread's success (the caller decides with a barrier).
 // ll_each() visits the same packed elements in the same thread, so a transform needs no
 // barrier in between.
+template <int MAXK = 4>
 __device__ __noinline__ bool ll_fetch_plan(const uint64_t * src, int cols, int csrc, int cdst, int na, int offa, int stra, int nb, int offb,
                                            int strb, int len, int ldst, uint32_t tag, float * dst, const Args & A, Ctrl * ctrl, int phase) {
-    constexpr int MAXK = 4;
     const int rpc = na + nb, n = cols * rpc * len;
     for (int base = 2 * threadIdx.x; base < n; base += 2 * NCT * MAXK) {
         uint64_t w[MAXK][2];
@@ -304,10 +304,11 @@ __device__ __noinline__ bool ll_fetch(const uint64_t * src, int n, uint32_t tag,
 }
 
 // `cols` runs of len words at src + c * len into dst + c * dstride (one column: ll_fetch).
+template <bool WIDE = false>
 __device__ __forceinline__ bool ll_fetch_cols(const uint64_t * src, int cols, int len, float * dst, int dstride, uint32_t tag, const Args & A,
                                               Ctrl * ctrl, int phase) {
     if (cols == 1) return ll_fetch(src, len, tag, dst, A, ctrl, phase);
-    return ll_fetch_plan(src, cols, len, dstride, 1, 0, 0, 0, 0, 0, len, len, tag, dst, A, ctrl, phase);
+    return ll_fetch_plan<WIDE ? 6 : 4>(src, cols, len, dstride, 1, 0, 0, 0, 0, 0, len, len, tag, dst, A, ctrl, phase);
 }
 
 // One exchange word into v once it carries `tag` (a polling thread of its own; the caller
@@ -1081,7 +1082,7 @@ __device__ void consumer(const Args & A, Sm & S) {
                 } else if (batched && ph.layer == 0 && ph.pos == 0) {
                     // batched position 0: every stream's post-norm talker hidden
                     if (ok) {
-                        ok = ll_fetch_cols(A.w.hid_x, ncol, d.H, S.xres, d.H, A.tag_base + static_cast<uint32_t>(A.thead_phase), A, S.ctrl, p);
+                        ok = ll_fetch_cols<BATCHED>(A.w.hid_x, ncol, d.H, S.xres, d.H, A.tag_base + static_cast<uint32_t>(A.thead_phase), A, S.ctrl, p);
                         if (ok) stage_fetched(ncol);
                     }
                 } else if (batched && ph.layer == 0) {
@@ -1112,7 +1113,7 @@ __device__ void consumer(const Args & A, Sm & S) {
                     if (ok)
                         for (int i = tid; i < d.H; i += NCT) stage(0, i, __half2float(row[i]));
                 } else if (ok) {
-                    ok = ll_fetch_cols(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
+                    ok = ll_fetch_cols<BATCHED>(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
                     if (ok) stage_fetched(ncol);
                 }
                 break;
@@ -1120,25 +1121,25 @@ __device__ void consumer(const Args & A, Sm & S) {
             case TGU: case CGU:
                 nnorm = ncol;
                 if (ok) {
-                    ok = ll_fetch_cols(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
+                    ok = ll_fetch_cols<BATCHED>(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
                     if (ok) stage_fetched(ncol);
                 }
                 break;
             case TO: case CO:
-                if (ok) ok = ll_fetch_cols(A.w.attn, ncol, d.Q, xin, XS, ptag, A, S.ctrl, p);
+                if (ok) ok = ll_fetch_cols<BATCHED>(A.w.attn, ncol, d.Q, xin, XS, ptag, A, S.ctrl, p);
                 break;
             case TDOWN: case CDOWN:
-                if (ok) ok = ll_fetch_cols(A.w.h, ncol, d.F, xin, XS, ptag, A, S.ctrl, p);
+                if (ok) ok = ll_fetch_cols<BATCHED>(A.w.h, ncol, d.F, xin, XS, ptag, A, S.ctrl, p);
                 break;
             case THEAD:
                 nnorm = ncol;
-                if (ok) ok = ll_fetch_cols(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
+                if (ok) ok = ll_fetch_cols<BATCHED>(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
                 if (ok) stage_fetched(ncol);
                 break;
             case CHEAD:
                 if (batched) {
                     nnorm = ncol;
-                    if (ok) ok = ll_fetch_cols(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
+                    if (ok) ok = ll_fetch_cols<BATCHED>(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
                     if (ok) stage_fetched(ncol);
                 } else {
                     // the single-stream pass's last column is this position
@@ -1220,7 +1221,11 @@ __device__ void consumer(const Args & A, Sm & S) {
     }
 }
 
-__global__ void __launch_bounds__(NTHR, 1) k_frame(const __grid_constant__ Args A) {
+// One launch of a phase program: BATCHED selects the consumer compiled for 2 or 4 streams.
+// The two shapes are separate kernels, so each gets its own register allocation and code: the
+// batched program's wider fetches do not cost the single-stream frame registers.
+template <bool BATCHED>
+__device__ __forceinline__ void frame_main(const Args & A) {
     extern __shared__ __align__(128) char smem[];
     const SmemLayout L = smem_layout(A.d, A.ring_bytes, A.scratch_floats, A.part_floats, A.xcols, A.cp_slots);
     Sm S = carve(smem, L);
@@ -1234,9 +1239,13 @@ __global__ void __launch_bounds__(NTHR, 1) k_frame(const __grid_constant__ Args 
     __syncthreads();
     if (unsigned long long * pb = prof_base(A)) pb[4 * A.nphase] = globaltimer();
     if (threadIdx.x >= NCT) producer(A, S);
-    else if (A.nb > 1) consumer<true>(A, S);
-    else consumer<false>(A, S);
+    else consumer<BATCHED>(A, S);
 }
+
+// Single-stream programs (a frame, frame 0, one talker layer).
+__global__ void __launch_bounds__(NTHR, 1) k_frame(const __grid_constant__ Args A) { frame_main<false>(A); }
+// Batched programs: 2 or 4 streams, one weight pass.
+__global__ void __launch_bounds__(NTHR, 1) k_frame_batch(const __grid_constant__ Args A) { frame_main<true>(A); }
 
 // A standalone launch of the device sampler on given logits (one CTA), for parity tests.
 __global__ void __launch_bounds__(NCT, 1) k_sample(const float * logits, int V, SampleCfg cfg, int * out) {
