@@ -148,6 +148,21 @@ __device__ __forceinline__ void bulk_g2s_hint(void * dst, const void * src, uint
                  "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
                  : "memory");
 }
+// 2-D tiled TMA load of one box of the tensor map at `tmap` (device memory) at element
+// coordinates (x inner, y outer); completion counted on `bar`. No multicast. x * element size
+// must be a multiple of 16 bytes. The map must have been acquired by this thread
+// (tensormap_acquire) after it was last written.
+__device__ __forceinline__ void tma_box_2d(void * dst, const void * tmap, int x, int y, uint64_t * bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(tmap), "r"(x), "r"(y), "r"(smem_addr(bar))
+                 : "memory");
+}
+// Orders this thread's later tensor-map reads after generic-proxy writes of the map (the host's
+// copy before the launch), so a map rewritten at the same address is not read stale.
+__device__ __forceinline__ void tensormap_acquire(const void * tmap) {
+    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(tmap) : "memory");
+}
 // L2 policies: keep (evict_last) for data read again soon, stream (evict_first) for data
 // read once per frame, so the streamed bytes do not push out the kept ones.
 __device__ __forceinline__ uint64_t l2_policy_keep() {

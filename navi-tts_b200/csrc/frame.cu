@@ -6,6 +6,9 @@
 
 #include "../../include/navi_b200.h"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
@@ -86,6 +89,12 @@ struct Frame::Impl {
     uint32_t poll_ns = 0;
     int eos = 0, suppress_from = 0;
     size_t ll_bytes = 0;
+    // tensor maps of each slot's talker KV cache ([MAX_B][MAX_TL][K, V] in device memory), and
+    // the host copies with the cache pointers and length they were encoded for
+    uint8_t * kvmaps = nullptr;
+    std::vector<uint8_t> kvmap_host[MAX_B];
+    const void * kvmap_src[MAX_B][MAX_TL][2] = {};
+    int kvmap_pos[MAX_B] = {};
     uint64_t * ll_base = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     int32_t * h_out = nullptr;   // pinned: MAX_B x 16 codes + 4 control words
@@ -131,6 +140,49 @@ struct Frame::Impl {
     };
     Mode modes[MAX_B + 1];
 
+    // The tensor maps of slot sl's KV cache (boxes of KV_BOX positions x one KV head), encoded
+    // again only when the cache's pointers or length change (once per request); null when the
+    // cache's layout does not suit them (the kernel then copies the rows one by one).
+    const uint8_t * kv_maps(int sl, const KvCache & kv) {
+        bool same = kvmap_pos[sl] == kv.max_pos;
+        for (int l = 0; l < d.TL && same; ++l) same = kvmap_src[sl][l][0] == kv.k[l] && kvmap_src[sl][l][1] == kv.v[l];
+        uint8_t * dst = kvmaps + static_cast<size_t>(sl) * MAX_TL * 2 * TMAP_BYTES;
+        if (same) return kvmap_pos[sl] > 0 ? dst : nullptr;
+        static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+        if (!encode) {
+            cudaDriverEntryPointQueryResult q{};
+            void * fn = nullptr;
+            NAVI_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+            if (q != cudaDriverEntryPointSuccess || !fn) fail("frame: cuTensorMapEncodeTiled unavailable", NAVI_E_CUDA);
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        }
+        std::vector<uint8_t> & h = kvmap_host[sl];
+        h.assign(static_cast<size_t>(MAX_TL) * 2 * TMAP_BYTES, 0);
+        bool ok = kv.kv_dim == d.KV && kv.max_pos > 0;
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.KV), static_cast<cuuint64_t>(kv.max_pos)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.KV) * 2};
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(d.HD), static_cast<cuuint32_t>(KV_BOX)};
+        const cuuint32_t estr[2] = {1, 1};
+        for (int l = 0; l < d.TL && ok; ++l)
+            for (int c = 0; c < 2 && ok; ++c) {
+                const void * base = c ? static_cast<const void *>(kv.v[l]) : static_cast<const void *>(kv.k[l]);
+                if (reinterpret_cast<std::uintptr_t>(base) & 15u) { ok = false; break; }
+                CUtensorMap * m = reinterpret_cast<CUtensorMap *>(h.data() + (static_cast<size_t>(l) * 2 + c) * TMAP_BYTES);
+                ok = encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            }
+        for (int l = 0; l < d.TL; ++l) {
+            kvmap_src[sl][l][0] = kv.k[l];
+            kvmap_src[sl][l][1] = kv.v[l];
+        }
+        kvmap_pos[sl] = ok ? kv.max_pos : -1;
+        if (!ok) return nullptr;
+        NAVI_CUDA(cudaMemcpyAsync(dst, h.data(), h.size(), cudaMemcpyHostToDevice, stream));
+        NAVI_CUDA(cudaStreamSynchronize(stream));
+        return dst;
+    }
+
     // layer >= 0: the single-layer program of that talker layer, from step_in into layer_out.
     // hidden_in / logits_in: frame 0 of one stream (the code predictor only).
     int launch(const StreamIn * in, int nb, const float * hidden_in, const float * logits_in, const Sampling & s, std::string & err,
@@ -173,7 +225,8 @@ struct Frame::Impl {
                           " positions per attention split; the kernel takes at most " + std::to_string(MAX_ATTN_CHUNK);
                     return NAVI_E_KV_FULL;
                 }
-                const uint64_t kvb = 2ull * A.attn_chunk[i] * d.HD * 2 + 2ull * d.HD * 4;
+                const uint64_t krows = static_cast<uint64_t>(A.attn_chunk[i] + KV_BOX - 1) / KV_BOX * KV_BOX;   // whole boxes
+                const uint64_t kvb = 2ull * krows * d.HD * 2 + 2ull * d.HD * 4;
                 if (kvb > M.ring) {
                     err = "KV length " + std::to_string(q.n_past) + " needs " + std::to_string(kvb) + "-byte attention slices; the ring holds " +
                           std::to_string(M.ring);
@@ -185,11 +238,15 @@ struct Frame::Impl {
             A.trailing[i] = q.trailing;
             A.step_out[i] = layer >= 0 ? layer_out : step[sl][cur[sl] ^ 1];
             A.seen[i] = seen + static_cast<size_t>(sl) * d.TV;
-            if (q.kv)
+            if (q.kv) {
                 for (int l = 0; l < d.TL; ++l) {
                     A.kc[i][l] = reinterpret_cast<__half *>(q.kv->k[l]);
                     A.vc[i][l] = reinterpret_cast<__half *>(q.kv->v[l]);
                 }
+                // boxed loads pay off once a split covers several boxes' worth of positions (a
+                // 4-stream launch at KV 512: 128); a short split is faster as 32 row copies in flight
+                A.kvmap[i] = A.attn_chunk[i] > 2 * KV_BOX ? kv_maps(sl, *q.kv) : nullptr;
+            }
             if (!first) rope_row(inv_t_h, q.n_past, A.rope_t[i]);
             A.seed[i] = q.seed;
             A.frame_index[i] = q.frame_index;
@@ -440,6 +497,8 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     I.w.hid_x = q; q += n_hid;
     I.w.code_x = q;
     I.seen = I.alloc<uint8_t>(static_cast<size_t>(MAX_B) * d.TV);
+    I.kvmaps = I.alloc<uint8_t>(static_cast<size_t>(MAX_B) * MAX_TL * 2 * TMAP_BYTES + 64);
+    if (reinterpret_cast<std::uintptr_t>(I.kvmaps) & 63u) fail("frame: tensor-map storage is not 64-byte aligned", NAVI_E_CUDA);
     I.w.codes = I.alloc<int32_t>(static_cast<size_t>(MAX_B) * NCB);
     I.w.hidden = I.alloc<float>(static_cast<size_t>(MAX_B) * d.H);
     I.w.ctl = I.alloc<unsigned>(4);

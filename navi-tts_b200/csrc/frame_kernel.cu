@@ -130,7 +130,12 @@ __device__ void producer(const Args & A, Sm & S) {
         // continues at the ring's start, and the bytes between the cut point's offset and the
         // end stay unused. It may only overwrite bytes whose chunk the consumers have
         // released; unused bytes hold no data, hence the min() with the end of the issued data.
-        const uint64_t head = issued;
+        // a chunk with boxed (tensor-map) loads starts on a 128-byte boundary, as those copies'
+        // shared-memory destinations must (its segments are all multiples of 128 bytes); the
+        // bytes skipped hold no data
+        bool boxed = false;
+        for (int i = 0; i < ns; ++i) boxed = boxed || seg[i].tmap != nullptr;
+        const uint64_t head = boxed ? (issued + 127) / 128 * 128 : issued;
         const uint32_t pos = static_cast<uint32_t>(head % RB);
         uint32_t cut = total;
         uint64_t end = head + total;
@@ -168,6 +173,18 @@ __device__ void producer(const Args & A, Sm & S) {
         uint32_t lo = 0;   // logical offset of the segment's first byte
         uint32_t gr = 0;   // rows of the chunk before this segment: row gr + r goes to lane (gr + r) % 32
         for (int i = 0; i < ns; ++i) {
+            if (seg[i].tmap) {
+                // boxed loads (one per box, dealt to the lanes like rows)
+                tensormap_acquire(seg[i].tmap);
+                for (uint32_t r = (lane - gr % 32u + 32u) % 32u; r < seg[i].rows; r += 32) {
+                    const uint32_t x = lo + r * seg[i].bytes;
+                    tma_box_2d(S.ring + (x < cut ? moff + x : x - cut), seg[i].tmap, seg[i].tx, seg[i].ty + static_cast<int>(r) * KV_BOX,
+                               &S.bars[slot]);
+                }
+                lo += seg[i].bytes * seg[i].rows;
+                gr += seg[i].rows;
+                continue;
+            }
             for (uint32_t r = (lane - gr % 32u + 32u) % 32u; r < seg[i].rows; r += 32) {
                 const char * src = static_cast<const char *>(seg[i].src) + static_cast<size_t>(r) * seg[i].stride;
                 const uint32_t rl = lo + r * seg[i].bytes;
@@ -735,7 +752,9 @@ __device__ __forceinline__ bool talker_attention(const Args & A, Sm & S, const P
         const float * qn = reinterpret_cast<const float *>(chunk_at(S, chunk, 0));
         const float * kn = reinterpret_cast<const float *>(chunk_at(S, chunk, HD * 4));
         const __half * Kc = reinterpret_cast<const __half *>(chunk_at(S, chunk, 2 * HD * 4));
-        const __half * Vc = reinterpret_cast<const __half *>(chunk_at(S, chunk, 2 * HD * 4 + nc * HD * 2));
+        // V follows K: nc rows, or whole boxes of KV_BOX rows when the rows came by tensor map
+        const int krows = A.kvmap[st] ? (nc + KV_BOX - 1) / KV_BOX * KV_BOX : nc;
+        const __half * Vc = reinterpret_cast<const __half *>(chunk_at(S, chunk, 2 * HD * 4 + krows * HD * 2));
         const bool last = sp == Sp - 1;
         const int n = nc + (last ? 1 : 0);
         // rows of HD words: the group's q heads, then (last split) k and v of head g, of column st

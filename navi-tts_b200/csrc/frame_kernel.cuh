@@ -58,6 +58,8 @@ constexpr int PROF_STRIDE = 4 * 4096 + 1;   // trace words per CTA: 4 stamps x p
 constexpr int MAX_B = 4;                // streams of one batched launch (each with its own KV cache and draws)
 constexpr int MAXC = 4;                 // input columns of one GEMV phase (streams, or code-predictor positions)
 constexpr int CP_SLOTS = 2;             // code-predictor K/V sets one CTA may keep (MAX_B * layers * KV heads / grid)
+constexpr int KV_BOX = 32;              // cached positions per 2-D TMA box of a talker K or V cache
+constexpr uint32_t TMAP_BYTES = 128;    // one CUtensorMap
 
 enum Op : uint8_t { TQKV, TATTN, TO, TGU, TDOWN, THEAD, CQKV, CATTN, CO, CGU, CDOWN, CHEAD, FINAL, XOUT, SAMPLE };
 
@@ -135,6 +137,9 @@ struct Args {
     uint8_t * seen[MAX_B];           // [TV] codebook-0 ids drawn so far this request
     __half * kc[MAX_B][MAX_TL];
     __half * vc[MAX_B][MAX_TL];
+    // per stream: [MAX_TL][K, V] tensor maps of the KV cache ([max_pos][KV] f16, boxes of
+    // KV_BOX positions x head_dim), in device memory, or null (row copies instead)
+    const uint8_t * kvmap[MAX_B];
     float rope_t[MAX_B][128];        // talker position n_past: cos[HD/2], then sin[HD/2]
     uint64_t seed[MAX_B];
     int frame_index[MAX_B];
@@ -225,6 +230,10 @@ struct Seg {
     uint32_t rows = 1;
     uint32_t stride = 0;
     uint32_t nr = 0;      // a weight slice [K/8][nr][8] f16 of nr rows (0: other data)
+    // tensor segment (tmap non-null): `rows` boxes of `bytes` each, box r read by one 2-D TMA
+    // load of tmap at element coordinates (tx, ty + r * KV_BOX)
+    const void * tmap = nullptr;
+    int tx = 0, ty = 0;
 };
 
 // Where a chunk may be cut when it does not fit before the end of the ring: at the start
@@ -339,6 +348,15 @@ __host__ __device__ inline int phase_segments(const Args & A, const ModelW & W, 
             r0 = min(sp * A.attn_chunk[st_], A.n_past[st_]);
             r1 = min(r0 + A.attn_chunk[st_], A.n_past[st_]);
             if (r1 <= r0) return 2;
+            if (A.kvmap[st_]) {
+                // per cache, boxed loads of KV head g's 256-byte slices of positions [r0, r0 + nbox * KV_BOX)
+                // (positions past r1 are read and not used; past max_pos they read as zeros)
+                const uint32_t nbox = static_cast<uint32_t>((r1 - r0 + KV_BOX - 1) / KV_BOX), bb = static_cast<uint32_t>(KV_BOX * d.HD * 2);
+                const uint8_t * m = A.kvmap[st_] + static_cast<size_t>(ph.layer) * 2 * TMAP_BYTES;
+                s[2] = {nullptr, bb, nbox, 0, 0, m, g * d.HD, r0};
+                s[3] = {nullptr, bb, nbox, 0, 0, m + TMAP_BYTES, g * d.HD, r0};
+                return 4;
+            }
             const size_t off = static_cast<size_t>(r0) * d.KV + static_cast<size_t>(g) * d.HD;
             const uint32_t rows = static_cast<uint32_t>(r1 - r0), rb = static_cast<uint32_t>(d.HD) * 2, st = static_cast<uint32_t>(d.KV) * 2;
             s[2] = {A.kc[st_][ph.layer] + off, rb, rows, st};
