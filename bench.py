@@ -467,6 +467,45 @@ def run_vocoder_only(args):
     emit(line)
 
 
+def run_prefill_only(args):
+    """`--prefill-only`: the talker prefill of configs[4]'s prompt (200 uniform text ids in the
+    reference's template, 208 prefill rows) alone on one GPU: prompt rows then the 28-layer
+    prefill (Talker::build_prompt + Talker::prefill, talker.hip:283-399), device time per call
+    (Talker::last_ms, the prefill kernels only) and wall time of both calls, medians of
+    `--steps` after `--warmup`. One JSON line."""
+    import numpy as np
+    import torch
+    rank, local, world = dist_env()
+    if world > 1 and rank != 0:
+        return
+    torch.cuda.set_device(local)
+    ensure_weights(0, 1)
+    from navi_b200 import engine, model_spec
+    dev = engine.Device(local)
+    w = engine.Weights(dev, BENCH_NAVI)
+    cfg = model_spec.full_config(w.params.decoder_dim)
+    tal = engine.Talker(dev, w, max_prompt_tokens=1024, max_positions=4096)
+    r = np.random.default_rng(1000)
+    ids = [cfg.im_start_id, cfg.assistant_id, 198] + r.integers(0, cfg.text_vocab, 200).tolist() + \
+        [cfg.im_end_id, 198, cfg.im_start_id, cfg.assistant_id, 198]
+    spk = np.random.default_rng(4).standard_normal(w.params.talker.hidden).astype(np.float32)
+    dev_ms, wall_ms, rows = [], [], 0
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        pr = tal.build_prompt(ids, "english", spk)
+        tal.prefill(pr)
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            wall_ms.append((time.perf_counter() - t0) * 1e3)
+            dev_ms.append(tal.last_ms())
+        rows = pr.n_prefill
+    emit({"metric": "talker prefill ms (configs[4] prompt)", "impl": "ours", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+          "higher_is_better": False, "dtype": "f16 weights / f32 activations (f16 hi+lo on the tensor cores)",
+          "data": "synthetic (seeded random-init weights N(0,0.02), uniform random text ids)",
+          "config": {"workload": "configs[4] prompt: 200 text ids, prefill rows", "prefill_rows": rows},
+          "prefill_ms": float(np.median(dev_ms)), "prompt_and_prefill_wall_ms": float(np.median(wall_ms))})
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -618,6 +657,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-vocoder", dest="vocoder", action="store_false", help="skip the configs[3] vocoder line")
     ap.add_argument("--vocoder-only", action="store_true", help="run only the configs[3] vocoder measurement")
+    ap.add_argument("--prefill-only", action="store_true", help="run only the talker prefill of the configs[4] prompt")
     ap.add_argument("--voc-chunks", default="4,16", help="vocoder chunk lengths (frames), comma separated")
     ap.add_argument("--no-layer", dest="layer", action="store_false", help="skip the configs[0] single-layer line")
     ap.add_argument("--streams", type=int, default=64, help="configs[4] utterances over all GPUs (64 = the full config; 0 = skip)")
@@ -629,6 +669,8 @@ def main():
         run_reference(args)
     elif args.vocoder_only:
         run_vocoder_only(args)
+    elif args.prefill_only:
+        run_prefill_only(args)
     else:
         run_ours(args)
 
