@@ -839,6 +839,7 @@ __device__ __forceinline__ bool cp_attention(const Args & A, Sm & S, const Phase
     const int ncol = batched ? 1 : ph.ncol, pos = ph.pos, col0 = batched ? st : 0;
     const float * qn = reinterpret_cast<const float *>(chunk_at(S, chunk, 0));
     const float * kn = reinterpret_cast<const float *>(chunk_at(S, chunk, HD * 4));
+    const float * rc = reinterpret_cast<const float *>(chunk_at(S, chunk, 2 * HD * 4));   // RoPE rows of the columns
     __half * kv = S.cpkv + static_cast<size_t>(slot) * (cpkv_bytes(d) / 2);   // [pos][K,V][HD] of the set
     float * qkv = S.scratch;                // [2][GR + 2][HD]: per column the q heads, k, v
     const auto qof = [&](int c) { return qkv + c * (GR + 2) * HD; };
@@ -854,7 +855,7 @@ __device__ __forceinline__ bool cp_attention(const Args & A, Sm & S, const Phase
     const int lane = tid & 31;
     for (int v = tid >> 5; v < ncol * (GR + 1); v += NCW) {
         const int c = v / (GR + 1), j = v - c * (GR + 1);
-        warp_norm_rope(j < GR ? qof(c) + j * HD : kof(c), j < GR ? qn : kn, A.rope_c + (pos + c) * HD, HD, d.eps_c, j == GR);
+        warp_norm_rope(j < GR ? qof(c) + j * HD : kof(c), j < GR ? qn : kn, rc + c * HD, HD, d.eps_c, j == GR);
         if (j == GR) {
             __syncwarp();
             for (int e = lane; e < HD; e += 32) {
@@ -897,6 +898,7 @@ __device__ __forceinline__ bool cp_attention(const Args & A, Sm & S, const Phase
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
         for (int tt = 0; tt < n; ++tt) {
             const float pt = __shfl_sync(0xffffffffu, ev, tt);
             const uint2 vv = *reinterpret_cast<const uint2 *>(kv + (static_cast<size_t>(tt) * 2 + 1) * HD + lane * 4);

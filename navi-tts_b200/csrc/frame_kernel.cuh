@@ -368,7 +368,9 @@ __host__ __device__ inline int phase_segments(const Args & A, const ModelW & W, 
             if (!cp_attn_role(A, b, ph.layer, st_, g, slot)) return 0;
             s[0] = {L->qn, HD4};
             s[1] = {L->kn, HD4};
-            return 2;
+            // the RoPE rows of the phase's positions (one per column; batched streams share one)
+            s[2] = {A.rope_c + static_cast<size_t>(ph.pos) * d.HD, HD4 * static_cast<uint32_t>(A.nb > 1 ? 1 : ph.ncol)};
+            return 3;
         }
         default:
             return 0;

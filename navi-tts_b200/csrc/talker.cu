@@ -375,6 +375,15 @@ struct Talker::Impl {
     int sms = 148;
     conv::Workspace ws;
 
+    // The prefill's launches for one prompt length, captured as a CUDA graph after the first
+    // (eager) prefill of that length: about 280 launches with their host-side planning and
+    // tensor-map encoding replay as one graph launch. The launches read and write only this
+    // object's buffers, so a graph stays valid for its lifetime.
+    std::vector<std::pair<int, cudaGraphExec_t>> graphs;
+    std::vector<int> uncapturable;
+    void enqueue_prefill(int T);
+    void capture_prefill(int T);
+
     static conv::Conv gemm_desc(const __half * W, const float * bias, int xs, int M, int K, int N, int ys, int epi, bool gate) {
         conv::Conv c;
         c.w_rm = W;
@@ -499,6 +508,7 @@ Talker::~Talker() {
     cudaSetDevice(impl_->ordinal);
     if (impl_->ev0) cudaEventDestroy(impl_->ev0);
     if (impl_->ev1) cudaEventDestroy(impl_->ev1);
+    for (const auto & g : impl_->graphs) cudaGraphExecDestroy(g.second);
     for (void * ptr : impl_->owned) cudaFree(ptr);
 }
 
@@ -570,13 +580,39 @@ const Prompt & Talker::build_prompt(std::span<const std::int32_t> ids, const std
 
 void Talker::prefill(const Prompt & pr) {
     Impl & I = *impl_;
-    const auto & tp = I.p.talker;
     NAVI_CUDA(cudaSetDevice(I.ordinal));
     const int T = pr.n_prefill, H = I.H;
     if (T < 1 || T > I.max_prompt) fail("talker: prefill rows outside 1..max_prompt_tokens", NAVI_E_ARG);
     if (T > I.kv.max_pos) fail("talker: prompt exceeds the KV cache", NAVI_E_KV_FULL);
     NAVI_CUDA(cudaEventRecord(I.ev0, I.stream));
     NAVI_CUDA(cudaMemcpyAsync(I.x, pr.prefill, static_cast<size_t>(T) * H * sizeof(float), cudaMemcpyDeviceToDevice, I.stream));
+    cudaGraphExec_t ge = nullptr;
+    for (const auto & g : I.graphs)
+        if (g.first == T) ge = g.second;
+    if (ge) NAVI_CUDA(cudaGraphLaunch(ge, I.stream));
+    else I.enqueue_prefill(T);
+    NAVI_CUDA(cudaGetLastError());
+    NAVI_CUDA(cudaEventRecord(I.ev1, I.stream));
+    NAVI_CUDA(cudaEventSynchronize(I.ev1));
+    float ms = 0.f;
+    NAVI_CUDA(cudaEventElapsedTime(&ms, I.ev0, I.ev1));
+    I.last_ms = ms;
+    int err = 0;
+    NAVI_CUDA(cudaMemcpy(&err, I.ws.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) {
+        NAVI_CUDA(cudaMemset(I.ws.err, 0, sizeof(int)));
+        if (err == conv::ERR_ALIGN) fail("talker: a tensor-core GEMM's weight ring is misaligned for swizzled tiles", NAVI_E_SHAPE);
+        fail("talker: a tensor-core GEMM wait passed its deadline", NAVI_E_TIMEOUT);
+    }
+    I.kv.n_used = T;
+    if (!ge) I.capture_prefill(T);
+}
+
+// The 28 layers and the codec head over the T rows in x (the layer loop of prefill).
+void Talker::Impl::enqueue_prefill(int T) {
+    Impl & I = *this;
+    const auto & tp = I.p.talker;
+    const int H = I.H;
     for (int l = 0; l < tp.n_layer; ++l) {
         const Layer & ly = I.layers[static_cast<size_t>(l)];
         __half * kc = reinterpret_cast<__half *>(I.kptr[static_cast<size_t>(l)]);
@@ -599,20 +635,32 @@ void Talker::prefill(const Prompt & pr) {
     NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm, dim3(1), dim3(256), 0, I.stream, I.x + static_cast<size_t>(T - 1) * H, I.final_norm, H,
                                     tp.rms_eps, I.hid));
     I.gemm(I.head, nullptr, I.hid, H, 1, H, I.TV, I.logits, I.TV, EPI_NONE);
-    NAVI_CUDA(cudaGetLastError());
-    NAVI_CUDA(cudaEventRecord(I.ev1, I.stream));
-    NAVI_CUDA(cudaEventSynchronize(I.ev1));
-    float ms = 0.f;
-    NAVI_CUDA(cudaEventElapsedTime(&ms, I.ev0, I.ev1));
-    I.last_ms = ms;
-    int err = 0;
-    NAVI_CUDA(cudaMemcpy(&err, I.ws.err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (err) {
-        NAVI_CUDA(cudaMemset(I.ws.err, 0, sizeof(int)));
-        if (err == conv::ERR_ALIGN) fail("talker: a tensor-core GEMM's weight ring is misaligned for swizzled tiles", NAVI_E_SHAPE);
-        fail("talker: a tensor-core GEMM wait passed its deadline", NAVI_E_TIMEOUT);
+}
+
+// Records enqueue_prefill(T) as a CUDA graph (at most 16 lengths). A length whose capture the
+// runtime refuses keeps running eagerly; the refusal leaves no error behind.
+void Talker::Impl::capture_prefill(int T) {
+    if (graphs.size() >= 16) return;
+    for (int u : uncapturable)
+        if (u == T) return;
+    cudaGraph_t g = nullptr;
+    NAVI_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    bool enqueued = true;
+    try {
+        enqueue_prefill(T);
+    } catch (const std::exception &) {
+        enqueued = false;
     }
-    I.kv.n_used = T;
+    const cudaError_t end = cudaStreamEndCapture(stream, &g);
+    cudaGraphExec_t e = nullptr;
+    const cudaError_t inst = (enqueued && end == cudaSuccess && g) ? cudaGraphInstantiate(&e, g, 0) : cudaErrorStreamCaptureInvalidated;
+    if (g) cudaGraphDestroy(g);
+    if (inst != cudaSuccess) {
+        (void) cudaGetLastError();
+        uncapturable.push_back(T);
+        return;
+    }
+    graphs.emplace_back(T, e);
 }
 
 KvCache & Talker::kv() { return impl_->kv; }
