@@ -947,13 +947,22 @@ __device__ void consumer(const Args & A, Sm & S) {
         // pos - 1 before position pos, codebook 15 in FINAL) runs at this one place, so the
         // sampler's code is shared by the sixteen draws of a frame
         int drawn = 0;
+        const __half * etab = nullptr;   // the embedding table the draw's id indexes next (loaded before the draw)
         if (!BATCHED && (ph.op == FINAL || (ph.op == CQKV && ph.layer == 0))) {
             const int cb = ph.op == FINAL ? NCB - 1 : ph.pos == 0 ? 0 : ph.pos - 1;
             const int V = cb == 0 ? d.TV : d.CV;
             const SampleScratch sc = sampler_scratch(S, Vmax);
+            etab = cb == 0 ? W.tl_emb : W.cp_emb[cb - 1];
             bool okl = true;
             if (cb == 0 && A.logits_in) {
-                for (int i = tid; i < d.TV; i += NCT) sc.s[i] = __ldcg(A.logits_in + i);
+                for (int i0 = 0; i0 < d.TV; i0 += 4 * NCT) {
+                    float v[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) v[k] = i0 + tid + k * NCT < d.TV ? __ldcg(A.logits_in + i0 + tid + k * NCT) : 0.f;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (i0 + tid + k * NCT < d.TV) sc.s[i0 + tid + k * NCT] = v[k];
+                }
             } else {
                 okl = ll_fetch(cb == 0 ? A.w.logits : A.w.clogits + static_cast<size_t>(cb - 1) * d.CV, V, ptag, sc.s, A, S.ctrl, p);
             }
@@ -1085,6 +1094,29 @@ __device__ void consumer(const Args & A, Sm & S) {
                 else ss1 += q;
             }
         };
+        // columns c < nc of H inputs read from global memory by load(c, i): each thread issues
+        // its loads of a round before its first shared-memory store, so they are in flight
+        // together instead of one after another
+        auto stage_loaded = [&](int nc, auto && load) {
+            constexpr int MC = BATCHED ? 4 : 2;
+            for (int i0 = 0; i0 < d.H; i0 += 3 * NCT) {
+                float v[MC][3];
+#pragma unroll
+                for (int c = 0; c < MC; ++c)
+#pragma unroll
+                    for (int k = 0; k < 3; ++k) {
+                        const int i = i0 + tid + k * NCT;
+                        v[c][k] = (c < nc && i < d.H) ? load(c, i) : 0.f;
+                    }
+#pragma unroll
+                for (int c = 0; c < MC; ++c)
+#pragma unroll
+                    for (int k = 0; k < 3; ++k) {
+                        const int i = i0 + tid + k * NCT;
+                        if (c < nc && i < d.H) stage(c, i, v[c][k]);
+                    }
+            }
+        };
         // after ll_fetch_cols of nc columns into xres: the same thread stages its elements
         auto stage_fetched = [&](int nc) {
             ll_each(nc * d.H, [&](int i) {
@@ -1097,9 +1129,7 @@ __device__ void consumer(const Args & A, Sm & S) {
             case TQKV: case CQKV: {
                 nnorm = ncol;
                 if (ph.op == TQKV && (ph.layer == 0 || ph.pos == POS_STEP_IN)) {
-                    if (ok)
-                        for (int c = 0; c < ncol; ++c)
-                            for (int i = tid; i < d.H; i += NCT) stage(c, i, __ldcg(A.step_in[c] + i));
+                    if (ok) stage_loaded(ncol, [&](int c, int i) { return __ldcg(A.step_in[c] + i); });
                 } else if (batched && ph.layer == 0 && ph.pos == 0) {
                     // batched position 0: every stream's post-norm talker hidden
                     if (ok) {
@@ -1116,23 +1146,20 @@ __device__ void consumer(const Args & A, Sm & S) {
                         S.codes[tid * NCB + cb] = static_cast<int>(v);
                     }
                     if (!consumers_ok(S, okc && ok)) { ok = false; break; }
-                    for (int c = 0; c < ncol; ++c) {
-                        const int code = S.codes[c * NCB + cb];
-                        const __half * row = (cb == 0 ? W.tl_emb : W.cp_emb[cb - 1]) + static_cast<size_t>(code) * d.H;
-                        for (int i = tid; i < d.H; i += NCT) stage(c, i, __half2float(row[i]));
-                    }
+                    const __half * tab = cb == 0 ? W.tl_emb : W.cp_emb[cb - 1];
+                    stage_loaded(ncol, [&](int c, int i) { return __half2float(tab[static_cast<size_t>(S.codes[c * NCB + cb]) * d.H + i]); });
                 } else if (!batched && ph.layer == 0 && ph.pos == 0) {
                     // code-predictor positions 0 and 1: the hidden and codebook 0's embedding
-                    if (ok)
-                        for (int i = tid; i < d.H; i += NCT) {
-                            stage(0, i, A.hidden_in ? __ldcg(A.hidden_in + i) : S.hid[i]);
-                            stage(1, i, __half2float(W.tl_emb[static_cast<size_t>(drawn) * d.H + i]));
-                        }
+                    if (ok) {
+                        const __half * row = etab + static_cast<size_t>(drawn) * d.H;   // codebook 0's row
+                        stage_loaded(2, [&](int c, int i) {
+                            return c == 0 ? (A.hidden_in ? __ldcg(A.hidden_in + i) : S.hid[i]) : __half2float(row[i]);
+                        });
+                    }
                 } else if (!batched && ph.layer == 0) {
                     // position pos: the embedding of codebook pos - 1's draw
-                    const __half * row = W.cp_emb[ph.pos - 2] + static_cast<size_t>(drawn) * d.H;
-                    if (ok)
-                        for (int i = tid; i < d.H; i += NCT) stage(0, i, __half2float(row[i]));
+                    const __half * row = etab + static_cast<size_t>(drawn) * d.H;   // cp_emb[pos - 2]
+                    if (ok) stage_loaded(1, [&](int, int i) { return __half2float(row[i]); });
                 } else if (ok) {
                     ok = ll_fetch_cols<BATCHED>(A.w.x, ncol, d.H, S.xres, d.H, ptag, A, S.ctrl, p);
                     if (ok) stage_fetched(ncol);
