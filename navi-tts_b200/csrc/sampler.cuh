@@ -43,8 +43,8 @@ struct SampleScratch {
     float * s;        // [V] in: logits; then the modified, tempered values; then (top-p) keep flags
     float * e;        // [V] e^(v - max) of the candidates, 0 elsewhere
     int * idx;        // [V] candidate ids (nonzero e) in index order
-    int * ord;        // [V] compaction counts; then (top-p) candidate positions by rank
-    unsigned * hist;  // [2][256] radix histograms
+    int * ord;        // [V] candidate masks; then (top-p) candidate positions by rank
+    unsigned * hist;  // [2][256] radix histograms; [256, 384): values and e of the first 64 candidates
     float * red;      // [64]
 };
 
@@ -148,26 +148,123 @@ __device__ __forceinline__ float key_float(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
-// Samples from S.s[0..V) (the raw logits on entry). Must be called by all NT threads
-// (NT a multiple of 32, >= 256; barrier id `bid`); every thread returns the chosen id.
+// Bin of a value's distance below the block max (mx - v >= 0; +inf for v = -inf): the
+// distance's exponent and top five mantissa bits, 32 bins an octave from 2^-3 (bin 0 also
+// takes every smaller distance) to 2^5 (bin 255 also takes every larger one). The bin never
+// decreases as the distance grows, so it never increases with v: every value of a lower bin
+// is larger than every value of a higher one.
+__device__ __forceinline__ int dist_bin(float mx, float v) {
+    const int key = static_cast<int>(__float_as_uint(__fsub_rn(mx, v)) >> 18) - (124 << 5);
+    return min(max(key, 0), 255);
+}
+
+// The k-th largest of s[0..V) by monotone float keys: 8-bit radix passes, top byte first, one
+// warp resolving the digit from the histogram (2 barriers a pass); the passes stop early once
+// the bin holding the k-th key holds exactly the keys still needed (then every key of that bin
+// is a candidate, and a threshold with the low bits zero selects the same set; not used when
+// that threshold would be +0, where -0 compares equal). The top byte (sign and exponent) puts
+// most keys in a handful of bins, so that pass counts into one histogram per warp (in e and
+// idx, unused until the candidates are formed) when they fit. Called by all NT threads.
+template <int NT>
+__device__ __forceinline__ float kth_radix(int V, int kth, const SampleScratch & S, int bid) {
+    constexpr int NW = NT / 32;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const float * s = S.s;
+    unsigned * hist = S.hist;
+    int * ired = reinterpret_cast<int *>(S.red);
+    unsigned * whist = reinterpret_cast<unsigned *>(S.e);
+    const bool priv = NW * 256 <= 2 * V;
+    for (int i = tid; i < 512; i += NT) hist[i] = 0u;
+    if (priv)
+        for (int i = tid; i < NW * 256; i += NT) whist[i] = 0u;
+    named_sync(bid, NT);
+    uint32_t prefix = 0, mask = 0;
+    int need = kth;
+    for (int pass = 3; pass >= 0; --pass) {
+        const int shift = pass * 8;
+        unsigned * h = hist + (pass & 1) * 256;
+        if (pass == 3 && priv) {
+            unsigned * hw = whist + wid * 256;
+            for (int i = tid; i < V; i += NT) atomicAdd(&hw[float_key(s[i]) >> 24], 1u);
+            named_sync(bid, NT);
+            for (int b = tid; b < 256; b += NT) {
+                unsigned t = 0;
+#pragma unroll
+                for (int w = 0; w < NW; ++w) t += whist[w * 256 + b];
+                h[b] = t;
+            }
+        } else {
+            for (int i = tid; i < V; i += NT) {
+                const uint32_t key = float_key(s[i]);
+                if ((key & mask) == prefix) atomicAdd(&h[(key >> shift) & 0xFFu], 1u);
+            }
+        }
+        named_sync(bid, NT);
+        const int slot = 16 + 3 * (3 - pass);
+        if (wid == 0) {
+            // lane l holds digits 255 - 8l - k (k < 8), counted from the top digit down
+            int cnt[8], tot = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) { cnt[k] = static_cast<int>(h[255 - 8 * lane - k]); tot += cnt[k]; }
+            int incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            const int above = incl - tot;
+            if (above < need && incl >= need) {
+                int a = above;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    if (a + cnt[k] >= need) {
+                        ired[slot] = 255 - 8 * lane - k;
+                        ired[slot + 1] = need - a;
+                        ired[slot + 2] = cnt[k];
+                        break;
+                    }
+                    a += cnt[k];
+                }
+            }
+            // this buffer is used again two passes on
+#pragma unroll
+            for (int k = 0; k < 8; ++k) h[8 * lane + k] = 0u;
+        }
+        named_sync(bid, NT);
+        need = ired[slot + 1];
+        prefix |= static_cast<uint32_t>(ired[slot]) << shift;
+        mask |= 0xFFu << shift;
+        if (ired[slot + 2] == need && key_float(prefix) != 0.0f) break;
+    }
+    return key_float(prefix);
+}
+
+// Samples from S.s[0..V) (the raw logits on entry). Must be called by all NT threads (NT a
+// multiple of 32, 320..1024: at least ten warps; barrier id `bid`); every thread returns the
+// chosen id, the host oracle's bit for bit.
 //
-// Work plan (the result is the host oracle's, bit for bit):
-//  1. modifications and temperature, block max (1 barrier);
-//  2. k-th largest key by 8-bit radix passes, top byte first, one warp resolving the
-//     digit from the histogram (2 barriers per pass). The passes
-//     stop early once the bin holding the k-th key holds exactly the keys still needed:
-//     then every key of that bin is a candidate and a threshold with the low bits zero
-//     selects the same set (not used when that threshold would be +0, where -0 compares
-//     equal);
-//  3. e = exp(v - max) over candidates, compacted in index order by ballots and one
-//     warp-0 scan (3 barriers);
-//  4. the normaliser in the reference's 256-thread order, 1 barrier;
-//  5. top-p: candidate ranks in parallel; the sequential sums (top-p cut, renormaliser,
-//     draw) in warp 0, values passed lane to lane by shuffles.
+// Work plan, laid out to keep CTA barriers few (each costs the slowest warp's lag, and a frame
+// runs the sampler on its critical path sixteen times):
+//  1. modifications and temperature, block max; the barrier also ORs a NaN flag (1 barrier);
+//  2. top-k threshold, the k-th largest value: a histogram of the values' distances below the
+//     max in log-spaced bins (dist_bin; 1 barrier); every warp finds the bin where the count
+//     from the top reaches k; the values of that bin are gathered (1 barrier) and every warp
+//     finds the k-th largest among them by counting. A bin of more than 64 values, a
+//     non-finite max or a NaN take the radix select of the keys (kth_radix) instead;
+//  3. e = exp(v - max) over the candidates v >= threshold, and one ballot mask of nonzero e
+//     per 32 consecutive ids (1 barrier);
+//  4. the normaliser in the reference's 256-thread block_sum order by warps 0-7 (warp 7 also
+//     draws the uniform) while the other warps compact the candidates in index order from the
+//     masks, keeping the values and e of the first 64 (1 barrier);
+//  5. top-p ranks by (value desc, index asc): for up to 64 candidates in warp 0, else by all
+//     threads (1 more barrier); the sequential sums (top-p cut, renormaliser, draw) in warp 0,
+//     values passed lane to lane by shuffles.
 template <int NT>
 __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, int bid) {
     constexpr int NW = NT / 32;
-    static_assert(NT % 32 == 0 && NT >= 256 && NT <= 1024, "sampler thread count");
+    static_assert(NT % 32 == 0 && NT >= 320 && NT <= 1024, "sampler thread count");
+    constexpr int SMALL = 64;                                   // gathered bin / candidate list of the fast paths
+    constexpr int RB_CNT = 48, RB_U = 50, RB_CHOSEN = 60, RB_N = 61;   // slots of red
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     float * s = S.s;
     float * e = S.e;
@@ -175,18 +272,15 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
     float * red = S.red;
     int * ired = reinterpret_cast<int *>(S.red);
     unsigned * hist = S.hist;
-    const unsigned lt_mask = (1u << lane) - 1u;
-    // 1. codebook-0 modifications, temperature, max; histograms cleared for step 2
+    float * cv = reinterpret_cast<float *>(hist + 256);         // values of the first SMALL candidates
+    float * ce = reinterpret_cast<float *>(hist + 256 + SMALL); // and their e
+    // 1. codebook-0 modifications, temperature, max; the distance histogram and gather count cleared
     const bool greedy = c.temperature <= 0.f;
-    for (int i = tid; i < 512; i += NT) hist[i] = 0u;
-    // The first radix pass (top byte: sign and exponent) puts most keys in a handful of
-    // bins; one histogram per warp, summed afterwards, keeps the warps' atomics apart. They
-    // live in e and idx (2 V words, unused until step 3) when those are large enough.
-    unsigned * whist = reinterpret_cast<unsigned *>(S.e);
-    const bool priv = NW * 256 <= 2 * V;
-    if (priv && !greedy)
-        for (int i = tid; i < NW * 256; i += NT) whist[i] = 0u;
+    const bool topk = !greedy && c.top_k > 0 && c.top_k < V;
+    for (int i = tid; i < 256; i += NT) hist[i] = 0u;
+    if (tid == 0) ired[RB_CNT] = 0;
     float lmax = -INFINITY;
+    bool nan = false;
     for (int i = tid; i < V; i += NT) {
         float v = s[i];
         if (c.talker_mods) {
@@ -197,10 +291,11 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
         if (!greedy) v = __fdiv_rn(v, c.temperature);
         s[i] = v;
         lmax = fmaxf(lmax, v);
+        nan = nan || v != v;
     }
     lmax = warp_max(lmax);
     if (lane == 0) red[wid] = lmax;
-    named_sync(bid, NT);
+    const bool anynan = named_sync_or(bid, NT, nan);
     float mx = -INFINITY;
 #pragma unroll
     for (int w = 0; w < NW; ++w) mx = fmaxf(mx, red[w]);
@@ -218,72 +313,76 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
         named_sync(bid, NT);
         return b >= V ? 0 : b;
     }
-    // 2. k-th largest key, top byte first
+    // 2. the top-k threshold
     float threshold = -INFINITY;
-    if (c.top_k > 0 && c.top_k < V) {
-        uint32_t prefix = 0, mask = 0;
-        int need = c.top_k;
-        for (int pass = 3; pass >= 0; --pass) {
-            const int shift = pass * 8;
-            unsigned * h = hist + (pass & 1) * 256;
-            if (pass == 3 && priv) {
-                unsigned * hw = whist + wid * 256;
-                for (int i = tid; i < V; i += NT) atomicAdd(&hw[float_key(s[i]) >> 24], 1u);
-                named_sync(bid, NT);
-                for (int b = tid; b < 256; b += NT) {
-                    unsigned t = 0;
+    if (topk) {
+        const int k = c.top_k;
+        bool fast = !anynan && mx > -INFINITY && mx < INFINITY;
+        int bstar = 0, needb = 0, cntb = 0;
+        if (fast) {
+            for (int i = tid; i < V; i += NT) atomicAdd(&hist[dist_bin(mx, s[i])], 1u);
+            named_sync(bid, NT);
+            // every warp: lane l holds bins 8l..8l+7; the bin where the count from bin 0 reaches k
+            const uint4 h0 = reinterpret_cast<const uint4 *>(hist)[2 * lane], h1 = reinterpret_cast<const uint4 *>(hist)[2 * lane + 1];
+            const int cnt[8] = {static_cast<int>(h0.x), static_cast<int>(h0.y), static_cast<int>(h0.z), static_cast<int>(h0.w),
+                                static_cast<int>(h1.x), static_cast<int>(h1.y), static_cast<int>(h1.z), static_cast<int>(h1.w)};
+            int tot = 0;
 #pragma unroll
-                    for (int w = 0; w < NW; ++w) t += whist[w * 256 + b];
-                    h[b] = t;
-                }
-            } else {
-                for (int i = tid; i < V; i += NT) {
-                    const uint32_t key = float_key(s[i]);
-                    if ((key & mask) == prefix) atomicAdd(&h[(key >> shift) & 0xFFu], 1u);
+            for (int q = 0; q < 8; ++q) tot += cnt[q];
+            int incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            const bool mine = incl - tot < k && incl >= k;
+            int b_ = 0, n_ = 0, c_ = 0;
+            if (mine) {
+                int a = incl - tot;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    if (a + cnt[q] >= k) { b_ = 8 * lane + q; n_ = k - a; c_ = cnt[q]; break; }
+                    a += cnt[q];
                 }
             }
-            named_sync(bid, NT);
-            const int slot = 16 + 3 * (3 - pass);
-            if (wid == 0) {
-                // lane l holds digits 255 - 8l - k (k < 8), counted from the top digit down
-                int cnt[8], tot = 0;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) { cnt[k] = static_cast<int>(h[255 - 8 * lane - k]); tot += cnt[k]; }
-                int incl = tot;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += v;
-                }
-                const int above = incl - tot;
-                if (above < need && incl >= need) {
-                    int a = above;
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        if (a + cnt[k] >= need) {
-                            ired[slot] = 255 - 8 * lane - k;
-                            ired[slot + 1] = need - a;
-                            ired[slot + 2] = cnt[k];
-                            break;
-                        }
-                        a += cnt[k];
-                    }
-                }
-                // this buffer is used again two passes on
-#pragma unroll
-                for (int k = 0; k < 8; ++k) h[8 * lane + k] = 0u;
+            const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+            bstar = __shfl_sync(0xffffffffu, b_, src);
+            needb = __shfl_sync(0xffffffffu, n_, src);
+            cntb = __shfl_sync(0xffffffffu, c_, src);
+            if (cntb > SMALL) {
+                fast = false;
+                named_sync(bid, NT);   // every warp has read the histogram before kth_radix clears it
             }
-            named_sync(bid, NT);
-            need = ired[slot + 1];
-            prefix |= static_cast<uint32_t>(ired[slot]) << shift;
-            mask |= 0xFFu << shift;
-            if (ired[slot + 2] == need && key_float(prefix) != 0.0f) break;
         }
-        threshold = key_float(prefix);
+        if (fast) {
+            // the values of bin bstar, then (every warp) the needb-th largest of them: the value
+            // with fewer than needb values above it and at least needb at or above it
+            float * list = reinterpret_cast<float *>(ci);
+            for (int i = tid; i < V; i += NT) {
+                const float v = s[i];
+                if (dist_bin(mx, v) == bstar) list[atomicAdd(&ired[RB_CNT], 1)] = v;
+            }
+            named_sync(bid, NT);
+            const float x0 = lane < cntb ? list[lane] : 0.f, x1 = lane + 32 < cntb ? list[lane + 32] : 0.f;
+            int g0 = 0, e0 = 0, g1 = 0, e1 = 0;
+#pragma unroll 4
+            for (int m = 0; m < cntb; ++m) {
+                const float y = list[m];
+                g0 += y > x0 ? 1 : 0;
+                e0 += y >= x0 ? 1 : 0;
+                g1 += y > x1 ? 1 : 0;
+                e1 += y >= x1 ? 1 : 0;
+            }
+            const unsigned b0 = __ballot_sync(0xffffffffu, lane < cntb && g0 < needb && needb <= e0);
+            const unsigned b1 = __ballot_sync(0xffffffffu, lane + 32 < cntb && g1 < needb && needb <= e1);
+            threshold = b0 ? __shfl_sync(0xffffffffu, x0, __ffs(b0) - 1) : __shfl_sync(0xffffffffu, x1, __ffs(b1) - 1);
+        } else {
+            threshold = kth_radix<NT>(V, k, S, bid);
+        }
     }
-    // 3. e over candidates; nonzero e compacted in index order
+    // 3. e over the candidates; one ballot mask of nonzero e per (round, warp): 32 consecutive ids
     const int R = (V + NT - 1) / NT;
-    int * cnt = S.ord;   // [R][NW] nonzero counts per (round, warp), i.e. per 32 consecutive ids
+    unsigned * masks = reinterpret_cast<unsigned *>(S.ord);   // [R][NW]
     for (int k = 0; k < R; ++k) {
         const int i = k * NT + tid;
         float ev = 0.f;
@@ -293,52 +392,59 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
             e[i] = ev;
         }
         const unsigned m = __ballot_sync(0xffffffffu, ev != 0.f);
-        if (lane == 0) cnt[k * NW + wid] = __popc(m);
+        if (lane == 0) masks[k * NW + wid] = m;
     }
     named_sync(bid, NT);
-    if (wid == 0) {
-        int run = 0;
-        for (int b0 = 0; b0 < R * NW; b0 += 32) {
-            const int x = b0 + lane < R * NW ? cnt[b0 + lane] : 0;
-            int incl = x;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int v = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += v;
-            }
-            if (b0 + lane < R * NW) cnt[b0 + lane] = run + incl - x;
-            run += __shfl_sync(0xffffffffu, incl, 31);
-        }
-        if (lane == 0) ired[61] = run;
-    }
-    named_sync(bid, NT);
-    for (int k = 0; k < R; ++k) {
-        const int i = k * NT + tid;
-        const bool nz = i < V && e[i] != 0.f;
-        const unsigned m = __ballot_sync(0xffffffffu, nz);
-        if (nz) ci[cnt[k * NW + wid] + __popc(m & lt_mask)] = i;
-    }
-    const int n = ired[61];
-    named_sync(bid, NT);
-    // 4. normaliser in the reference's 256-thread block_sum order
-    if (tid < 256) {
+    // 4. normaliser (warps 0-7) and compaction (warps 8..NW-1, a contiguous share of the masks each)
+    if (wid < 8) {
         float acc = 0.f;
         for (int i = tid; i < V; i += 256) acc = __fadd_rn(acc, e[i]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
         if (lane == 0) red[32 + wid] = acc;
+        if (wid == 7 && lane == 0) red[RB_U] = draw_uniform(c);
+    } else {
+        constexpr int CW = NW - 8;
+        const int M = R * NW;
+        const int q0 = (M * (wid - 8)) / CW, q1 = (M * (wid - 7)) / CW;
+        int before = 0;
+        for (int q = lane; q < q0; q += 32) before += __popc(masks[q]);
+        int run = static_cast<int>(__reduce_add_sync(0xffffffffu, static_cast<unsigned>(before)));
+        for (int m0 = q0; m0 < q1; m0 += 32) {
+            const int q = m0 + lane;
+            const unsigned m = q < q1 ? masks[q] : 0u;
+            const int cnt = __popc(m);
+            int incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            // mask q covers ids (q / NW) * NT + (q % NW) * 32 + bit
+            const int first = (q / NW) * NT + (q % NW) * 32;
+            int at = run + incl - cnt;
+            for (unsigned bb = m; bb; bb &= bb - 1) {
+                const int i = first + __ffs(bb) - 1;
+                ci[at] = i;
+                if (at < SMALL) {
+                    cv[at] = s[i];
+                    ce[at] = e[i];
+                }
+                ++at;
+            }
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (wid == NW - 1 && lane == 0) ired[RB_N] = run;
     }
     named_sync(bid, NT);
-    float ssum = lane < 8 ? red[32 + lane] : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ssum = __fadd_rn(ssum, __shfl_xor_sync(0xffffffffu, ssum, o));
-    const float inv = __fdiv_rn(1.0f, ssum);
+    const int n = ired[RB_N];
+    // 5. top-p order and the draw
     const bool nucleus = c.top_p > 0.f && c.top_p < 1.f;
-    int * ord = S.ord;   // top-p: candidate position of each rank
-    if (nucleus) {
-        // rank of candidate j in (value desc, index asc) order; positions are in index order.
-        // Thread j reads the other candidates' values from shared memory (every thread of a
-        // step reads the same element: a broadcast), eight independent loads per step.
+    const bool small = n <= SMALL;
+    int * ord = S.ord;   // top-p: candidate position of each rank (the masks are no longer needed)
+    if (nucleus && !small) {
+        // thread j reads the other candidates' values from shared memory (every thread of a step
+        // reads the same element: a broadcast), eight independent loads per step
         for (int j = tid; j < n; j += NT) {
             const float vj = s[ci[j]];
             int r = 0, m = 0;
@@ -360,14 +466,31 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
         named_sync(bid, NT);
     }
     if (wid == 0) {
-        // Sequential sums in warp 0, 32 terms per block: every lane gathers the block's 32
-        // values by shuffles (independent, so they overlap), then runs the same in-order
-        // __fadd_rn chain over them straight through, keeping the running sum at its own
-        // position; a ballot finds the first position past the target. The additions are
-        // the same, in the same order, as one sequential loop, so the results are too.
-        const float u = draw_uniform(c);
-        // running sums of the block v (0 past the end); returns the sum after the block and
-        // leaves in `mine` the sum after this lane's term
+        float ssum = lane < 8 ? red[32 + lane] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ssum = __fadd_rn(ssum, __shfl_xor_sync(0xffffffffu, ssum, o));
+        const float inv = __fdiv_rn(1.0f, ssum);
+        const float u = red[RB_U];
+        const auto ev = [&](int j) { return small ? ce[j] : e[ci[j]]; };   // e of candidate position j
+        if (nucleus && small) {
+            // ranks in this warp: lane l takes positions l and l + 32
+            const float x0 = lane < n ? cv[lane] : 0.f, x1 = lane + 32 < n ? cv[lane + 32] : 0.f;
+            int r0 = 0, r1 = 0;
+#pragma unroll 4
+            for (int m = 0; m < n; ++m) {
+                const float y = cv[m];
+                r0 += (y > x0 || (y == x0 && m < lane)) ? 1 : 0;
+                r1 += (y > x1 || (y == x1 && m < lane + 32)) ? 1 : 0;
+            }
+            if (lane < n) ord[r0] = lane;
+            if (lane + 32 < n) ord[r1] = lane + 32;
+            __syncwarp();
+        }
+        // Sequential sums, 32 terms per block: every lane gathers the block's 32 values by
+        // shuffles (independent, so they overlap), then runs the same in-order __fadd_rn chain
+        // over them straight through, keeping the running sum at its own position; a ballot
+        // finds the first position past the target. The additions are the same, in the same
+        // order, as one sequential loop, so the results are too.
         auto block_scan = [&](float acc, float v, float & mine) {
 #pragma unroll 1
             for (int g = 0; g < 32; g += 8) {   // eight values gathered per group: few live registers
@@ -384,17 +507,17 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
         };
         int chosen;
         if (nucleus) {
-            // the shortest prefix by rank whose cumulative probability reaches top_p: ranks <= R
+            // the shortest prefix by rank whose cumulative probability reaches top_p: ranks <= Rk
             float cum = 0.f;
-            int R = n - 1;
+            int Rk = n - 1;
             for (int r0 = 0; r0 < n; r0 += 32) {
                 const bool in = r0 + lane < n;
-                const float p = in ? __fmul_rn(e[ci[ord[r0 + lane]]], inv) : 0.f;
+                const float p = in ? __fmul_rn(ev(ord[r0 + lane]), inv) : 0.f;
                 float mine = 0.f;
                 cum = block_scan(cum, p, mine);
                 const unsigned hit = __ballot_sync(0xffffffffu, in && mine >= c.top_p);
                 if (hit) {
-                    R = r0 + __ffs(hit) - 1;
+                    Rk = r0 + __ffs(hit) - 1;
                     break;
                 }
             }
@@ -402,7 +525,7 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
             float * kept = s;
             for (int j = lane; j < n; j += 32) kept[j] = 0.f;
             __syncwarp();
-            for (int r = lane; r <= R; r += 32) kept[ord[r]] = 1.f;
+            for (int r = lane; r <= Rk; r += 32) kept[ord[r]] = 1.f;
             __syncwarp();
             // renormalise over the kept candidates, in index order; adding the 0 of a dropped
             // candidate leaves a sum unchanged
@@ -412,10 +535,10 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
                 const int j = j0 + lane;
                 const bool kp = j < n && kept[j] != 0.f;
                 const int ii = j < n ? ci[j] : 0;
-                const float ev = kp ? e[ii] : 0.f;
+                const float evj = kp ? ev(j) : 0.f;
                 const unsigned km = __ballot_sync(0xffffffffu, kp);
                 float mine = 0.f;
-                ksum = block_scan(ksum, ev, mine);
+                ksum = block_scan(ksum, evj, mine);
                 if (km) last = __shfl_sync(0xffffffffu, ii, 31 - __clz(km));
             }
             const float kinv = __fdiv_rn(1.0f, ksum);
@@ -425,7 +548,7 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
                 const int j = j0 + lane;
                 const bool kp = j < n && kept[j] != 0.f;
                 const int ii = j < n ? ci[j] : 0;
-                const float pv = kp ? __fmul_rn(e[ii], kinv) : 0.f;
+                const float pv = kp ? __fmul_rn(ev(j), kinv) : 0.f;
                 float mine = 0.f;
                 c2 = block_scan(c2, pv, mine);
                 const unsigned hit = __ballot_sync(0xffffffffu, kp && mine >= u);
@@ -440,7 +563,7 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
             for (int j0 = 0; j0 < n; j0 += 32) {
                 const int j = j0 + lane;
                 const int ii = j < n ? ci[j] : 0;
-                const float p = j < n ? __fmul_rn(e[ii], inv) : 0.f;
+                const float p = j < n ? __fmul_rn(ev(j), inv) : 0.f;
                 float mine = 0.f;
                 cum = block_scan(cum, p, mine);
                 const unsigned hit = __ballot_sync(0xffffffffu, j < n && mine >= u);
@@ -450,10 +573,10 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
                 }
             }
         }
-        if (lane == 0) ired[60] = chosen;
+        if (lane == 0) ired[RB_CHOSEN] = chosen;
     }
     named_sync(bid, NT);
-    const int chosen = ired[60];
+    const int chosen = ired[RB_CHOSEN];
     named_sync(bid, NT);
     return chosen;
 }
