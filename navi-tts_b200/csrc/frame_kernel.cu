@@ -968,7 +968,7 @@ __device__ void consumer(const Args & A, Sm & S) {
             }
             if (!consumers_ok(S, okl)) break;
             if (ph.op == FINAL) stamp(A, p, 0);
-            drawn = sample_cta<NCT>(V, sample_cfg(A, cb, 0), sc, BID);
+            drawn = sample_cta<NCT, true>(V, sample_cfg(A, cb, 0), sc, BID);
             if (tid == 0) S.codes[cb] = drawn;
         }
 

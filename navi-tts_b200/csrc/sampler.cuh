@@ -239,6 +239,12 @@ __device__ __forceinline__ float kth_radix(int V, int kth, const SampleScratch &
     return key_float(prefix);
 }
 
+// kth_radix as a call: keeps the rarely taken radix path out of the caller's code
+template <int NT>
+__device__ __noinline__ float kth_radix_call(int V, int kth, const SampleScratch & S, int bid) {
+    return kth_radix<NT>(V, kth, S, bid);
+}
+
 // Samples from S.s[0..V) (the raw logits on entry). Must be called by all NT threads (NT a
 // multiple of 32, 320..1024: at least ten warps; barrier id `bid`); every thread returns the
 // chosen id, the host oracle's bit for bit.
@@ -259,7 +265,11 @@ __device__ __forceinline__ float kth_radix(int V, int kth, const SampleScratch &
 //  5. top-p ranks by (value desc, index asc): for up to 64 candidates in warp 0, else by all
 //     threads (1 more barrier); the sequential sums (top-p cut, renormaliser, draw) in warp 0,
 //     values passed lane to lane by shuffles.
-template <int NT>
+// OUTLINE: the radix path is a call rather than inlined. Which is faster depends on the
+// caller: the single-stream frame program is faster with the call (its loop's code is
+// smaller: one launch 2,063 -> 2,049 us), the batched one, which runs at its register limit,
+// is slower with it (3.61 -> 3.80 ms: a call constrains the register allocation around it).
+template <int NT, bool OUTLINE = false>
 __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, int bid) {
     constexpr int NW = NT / 32;
     static_assert(NT % 32 == 0 && NT >= 320 && NT <= 1024, "sampler thread count");
@@ -377,7 +387,7 @@ __device__ int sample_cta(int V, const SampleCfg & c, const SampleScratch & S, i
             const unsigned b1 = __ballot_sync(0xffffffffu, lane + 32 < cntb && g1 < needb && needb <= e1);
             threshold = b0 ? __shfl_sync(0xffffffffu, x0, __ffs(b0) - 1) : __shfl_sync(0xffffffffu, x1, __ffs(b1) - 1);
         } else {
-            threshold = kth_radix<NT>(V, k, S, bid);
+            threshold = OUTLINE ? kth_radix_call<NT>(V, k, S, bid) : kth_radix<NT>(V, k, S, bid);
         }
     }
     // 3. e over the candidates; one ballot mask of nonzero e per (round, warp): 32 consecutive ids

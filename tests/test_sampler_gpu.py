@@ -4,6 +4,10 @@ Covers the reference's sampling semantics (model/qwen3tts/frame.hip:413-500) and
 this build's additions: greedy with ties and all -inf, exact top-k with ties at the
 threshold, top-p boundaries, temperature, codebook-0 suppression / EOS gating /
 repetition penalty, both RNG streams, and the vocab sizes of the benchmark configs.
+The value kinds also drive each path of the device's top-k selection: the distance
+histogram with one bin to resolve (normal, peaked), the radix select for a crowded bin
+(ties, flat) or a k-th value beyond the bins (wide, neginf), and top-p orders over more
+than 64 candidates (top-k 200 or off).
 """
 import numpy as np
 import pytest
@@ -19,7 +23,7 @@ def _cases():
     rng = np.random.default_rng(5)
     out = []
     for V in (3072, 2048, 1536, 512):
-        for kind in ("normal", "ties", "neginf", "peaked"):
+        for kind in ("normal", "ties", "neginf", "peaked", "wide", "flat"):
             x = rng.standard_normal(V).astype(np.float32) * 3
             if kind == "ties":
                 x = np.round(x)                       # many exact ties, including at the top-k threshold
@@ -27,8 +31,13 @@ def _cases():
                 x[rng.random(V) < 0.7] = -np.inf
             elif kind == "peaked":
                 x[rng.integers(V)] += 40.0            # one dominant id: most e_i underflow to 0
+            elif kind == "wide":
+                x *= 12.0                             # the k-th largest lies beyond the distance bins
+            elif kind == "flat":
+                x = np.full(V, 0.25, np.float32)      # every value in one bin and tied
+                x[rng.integers(V, size=5)] = 1.5
             for temp, k, p in ((0.9, 50, 1.0), (0.9, 50, 0.9), (1.3, 0, 0.5), (0.7, 1, 1.0), (0.9, V, 0.01),
-                               (0.0, 50, 1.0), (1.0, 7, 0.999)):
+                               (0.0, 50, 1.0), (1.0, 7, 0.999), (0.8, 200, 0.95)):
                 for rs in (capi.NAVI_RNG_PCG, capi.NAVI_RNG_PHILOX):
                     out.append((V, kind, temp, k, p, rs, int(rng.integers(1 << 62)), int(rng.integers(200)), x))
     return out
