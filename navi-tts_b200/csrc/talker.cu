@@ -71,42 +71,49 @@ __global__ void k_rmsnorm(const float * x, const float * w, int H, float eps, fl
 // kernel as K = 1 layers with the weights read in place by TMA (conv.hpp).
 enum { EPI_NONE = 0, EPI_SILU = 1, EPI_RESIDUAL = 2 };
 
-// Per row t (position pos0 + t): RMSNorm of every q and k head (head_dim 128: one warp per
-// head, 4 values a lane), rotate-half RoPE with the host table's cos/sin for the position, q
-// in place; then the f16 K (after RoPE) and V rows into the cache (talker.hip:43-80).
-__global__ void k_qk_norm_rope(float * qkv, int row_stride, const float * q_norm, const float * k_norm, int NH, int NKV, float eps,
-                               const float * rope, int pos0, __half * kcache, __half * vcache) {
+// The QKV projection's split-K sum with the per-head q/k RMSNorm, RoPE and the KV-cache store
+// (talker.hip:43-80), one launch a layer: CTA (t, h) of 128 threads finishes head h of row t,
+// the NH q heads, then the NKV k heads, then the NKV v heads, a thread per dimension. The head is the sum, in split order, of the projection's
+// `splits` partial slices ([T][QKV] each, no bias), or, with splits == 0, already in qkv. q
+// and k heads take the RMSNorm (sum of squares: lane l adds dims l, l+32, l+64, l+96, then a
+// warp sum) and the rotate-half RoPE (pairs (i, i + 64), host cos/sin table) back into qkv;
+// k and v heads also go to the f16 cache rows at position pos0 + t.
+__global__ void __launch_bounds__(128) k_qkv_reduce_norm_rope(const float * partial, int splits, float * qkv, int row_stride,
+                                                             const float * q_norm, const float * k_norm, int NH, int NKV, float eps,
+                                                             const float * rope, int pos0, __half * kcache, __half * vcache) {
     navi::dev::griddep_wait();
     navi::dev::griddep_launch_dependents();
     constexpr int HD = 128, H2 = 64;
-    const int t = blockIdx.x, pos = pos0 + t, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    float * row = qkv + static_cast<size_t>(t) * row_stride;
-    const float * cs = rope + static_cast<size_t>(pos) * HD;
-    for (int h = warp; h < NH + NKV; h += nw) {
-        float * v = row + h * HD;   // q heads, then k heads (k follows q in the row)
-        const float * w = h < NH ? q_norm : k_norm;
-        float e[4], ss = 0.f;
+    __shared__ float buf[HD];
+    __shared__ float sc;
+    const int t = blockIdx.x, h = blockIdx.y, e = threadIdx.x, pos = pos0 + t;
+    const size_t at = static_cast<size_t>(t) * row_stride + static_cast<size_t>(h) * HD + e;
+    const float v = splits > 0 ? sum_slices(partial + at, splits, static_cast<size_t>(gridDim.x) * row_stride) : qkv[at];
+    const int KV = NKV * HD;
+    if (h >= NH + NKV) {   // v head
+        qkv[at] = v;
+        vcache[static_cast<size_t>(pos) * KV + static_cast<size_t>(h - NH - NKV) * HD + e] = __float2half_rn(v);
+        return;
+    }
+    buf[e] = v;
+    __syncthreads();
+    if (e < 32) {
+        float ss = 0.f;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) { e[k] = v[lane + 32 * k]; ss += e[k] * e[k]; }
+        for (int k = 0; k < 4; ++k) ss += buf[e + 32 * k] * buf[e + 32 * k];
         ss = warp_sum(ss);
-        const float scale = rsqrtf(ss / static_cast<float>(HD) + eps);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) e[k] = e[k] * scale * w[lane + 32 * k];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int i = lane + 32 * k;
-            const float c = cs[i], s = cs[H2 + i], x0 = e[k], x1 = e[k + 2];
-            v[i] = x0 * c - x1 * s;
-            v[i + H2] = x0 * s + x1 * c;
-        }
+        if (e == 0) sc = rsqrtf(ss / static_cast<float>(HD) + eps);
     }
     __syncthreads();
-    const int KV = NKV * HD;
-    const float * kr = row + NH * HD, * vr = kr + KV;
-    for (int i = threadIdx.x; i < KV; i += blockDim.x) {
-        kcache[static_cast<size_t>(pos) * KV + i] = __float2half_rn(kr[i]);
-        vcache[static_cast<size_t>(pos) * KV + i] = __float2half_rn(vr[i]);
-    }
+    const float x = v * sc * (h < NH ? q_norm : k_norm)[e];
+    buf[e] = x;
+    __syncthreads();
+    const float * cs = rope + static_cast<size_t>(pos) * HD;
+    const int i = e & (H2 - 1);
+    const float c = cs[i], sn = cs[H2 + i], x0 = buf[i], x1 = buf[i + H2];
+    const float r = e < H2 ? x0 * c - x1 * sn : x0 * sn + x1 * c;
+    qkv[at] = r;
+    if (h >= NH) kcache[static_cast<size_t>(pos) * KV + static_cast<size_t>(h - NH) * HD + e] = __float2half_rn(r);
 }
 
 // ---- causal GQA attention of the prefill on the tensor cores ----------------------------------
@@ -405,8 +412,10 @@ struct Talker::Impl {
     // y[M][N] (row stride ys) = epi(op(x)[M][K] W[N][K]^T + bias); op = silu(gate) * up when
     // gate (x rows [gate K | up K]); EPI_RESIDUAL adds res (may alias y).  norm_w: the same
     // launch also writes the rows of y RMS-normalised with these weights into norm_out.
-    void gemm(const __half * W, const float * bias, const float * in, int xs, int M, int K, int N, float * out, int ys, int epi,
-              bool gate = false, const float * res = nullptr, const float * norm_w = nullptr, float * norm_out = nullptr) {
+    // defer: a split-K launch leaves its partial sums in ws.partial for the caller's own
+    // reduction; returns their slice count (0: out is final)
+    int gemm(const __half * W, const float * bias, const float * in, int xs, int M, int K, int N, float * out, int ys, int epi,
+             bool gate = false, const float * res = nullptr, const float * norm_w = nullptr, float * norm_out = nullptr, bool defer = false) {
         conv::Conv c = gemm_desc(W, bias, xs, M, K, N, ys, epi, gate);
         c.x = in;
         c.y = out;
@@ -414,7 +423,8 @@ struct Talker::Impl {
         c.norm_w = norm_w;
         c.norm_out = norm_out;
         c.norm_eps = p.talker.rms_eps;
-        conv::launch(c, ws, sms, stream);
+        c.defer_reduce = defer;
+        return conv::launch(c, ws, sms, stream);
     }
 };
 
@@ -618,9 +628,11 @@ void Talker::Impl::enqueue_prefill(int T) {
         __half * kc = reinterpret_cast<__half *>(I.kptr[static_cast<size_t>(l)]);
         __half * vc = reinterpret_cast<__half *>(I.vptr[static_cast<size_t>(l)]);
         if (l == 0) NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm, dim3(T), dim3(256), 0, I.stream, I.x, ly.ln1, H, tp.rms_eps, I.n));
-        I.gemm(ly.wqkv, nullptr, I.n, H, T, H, I.QKV, I.qkv, I.QKV, EPI_NONE);
-        NAVI_CUDA(navi::dev::launch_pdl(k_qk_norm_rope, dim3(T), dim3(256), 0, I.stream, I.qkv, I.QKV, ly.qn, ly.kn, I.NH, I.NKV, tp.rms_eps,
-                                        I.rope, 0, kc, vc));
+        // the QKV projection leaves its split-K partials; one launch sums them, norms and ropes
+        // q and k, and stores the K/V cache rows
+        const int qs = I.gemm(ly.wqkv, nullptr, I.n, H, T, H, I.QKV, I.qkv, I.QKV, EPI_NONE, false, nullptr, nullptr, nullptr, true);
+        NAVI_CUDA(navi::dev::launch_pdl(k_qkv_reduce_norm_rope, dim3(T, I.NH + 2 * I.NKV), dim3(128), 0, I.stream, I.ws.partial, qs, I.qkv,
+                                        I.QKV, ly.qn, ly.kn, I.NH, I.NKV, tp.rms_eps, I.rope, 0, kc, vc));
         NAVI_CUDA(navi::dev::launch_pdl(k_prefill_attn_mma, dim3((T + PA_QT - 1) / PA_QT, I.NH), dim3(PA_THREADS), PA_SMEM, I.stream, I.qkv,
                                         I.QKV, kc, vc, T, I.NH, I.NKV, 0, I.att));
         // the RMSNorms after the O projection and (but for the last layer) after the down
