@@ -15,7 +15,9 @@
 #include <cmath>
 #include <cstring>
 #include <string>
+#include <exception>
 #include <utility>
+#include <vector>
 
 namespace navi::qwen3tts {
 
@@ -74,7 +76,8 @@ constexpr int QKV_THREADS = 256;
 // separate reduction + k_rope_append.
 constexpr int QKV_FUSED_ROWS = 8;
 __global__ void __launch_bounds__(QKV_THREADS) k_qkv_rope_append(const float * partial, int splits, float * qkv, int nh, int hd,
-                                                                 int pos0, int ring, const float * inv_freq, float * kc, float * vc) {
+                                                                 const int * pos0p, int ring, const float * inv_freq, float * kc, float * vc) {
+    const int pos0 = *pos0p;
     navi::dev::griddep_wait();
     navi::dev::griddep_launch_dependents();
     __shared__ float buf[QKV_THREADS];
@@ -113,7 +116,8 @@ __global__ void __launch_bounds__(QKV_THREADS) k_qkv_rope_append(const float * p
 // Rotate-half RoPE on q (in place) and k of row t at position pos0 + t; k and v go to
 // ring slot pos & (ring - 1) (vocoder.hip:59-82).  qkv rows: [q | k | v], HD each.  Chunks
 // of more than QKV_FUSED_ROWS rows: after the QKV projection's own split-K reduction.
-__global__ void k_rope_append(float * qkv, int nh, int hd, int pos0, int ring, const float * inv_freq, float * kc, float * vc) {
+__global__ void k_rope_append(float * qkv, int nh, int hd, const int * pos0p, int ring, const float * inv_freq, float * kc, float * vc) {
+    const int pos0 = *pos0p;
     navi::dev::griddep_wait();
     navi::dev::griddep_launch_dependents();
     const int t = blockIdx.x, pos = pos0 + t, slot = pos & (ring - 1);
@@ -142,8 +146,9 @@ __global__ void k_rope_append(float * qkv, int nh, int hd, int pos0, int ring, c
 // Sliding-window causal attention of row t, head h over keys (pos - window, pos]
 // (vocoder.hip:85-111).  128 threads: thread j scores key k0 + j; thread i < hd sums
 // output dimension i.  window <= 128, hd <= 128.
-__global__ void k_window_attn(const float * qkv, int nh, int hd, int pos0, int window, int ring, float scale, const float * kc,
+__global__ void k_window_attn(const float * qkv, int nh, int hd, const int * pos0p, int window, int ring, float scale, const float * kc,
                               const float * vc, float * out) {
+    const int pos0 = *pos0p;
     navi::dev::griddep_wait();
     navi::dev::griddep_launch_dependents();
     __shared__ float q[128], pr[128], red[4];
@@ -339,6 +344,18 @@ struct Vocoder::Impl {
           * u = nullptr, * A = nullptr, * B = nullptr, * G = nullptr, * d = nullptr, * pcm = nullptr;
     float * P[4] = {}, * Q[4] = {};
     int * h_codes = nullptr;     // pinned
+    // The chunk's first position, read by the attention kernels from device memory so that a
+    // chunk's launches are the same for every chunk of a length and history parity: those are
+    // captured as a CUDA graph (after one eager chunk of that kind) and replayed.
+    int * d_pos0 = nullptr;
+    int * h_pos0 = nullptr;      // pinned
+    int flip = 0;                // chunks decoded since create, mod 2 (every history pair swaps once a chunk)
+    struct ChunkGraph { int T, flip; cudaGraphExec_t exec; };
+    std::vector<ChunkGraph> graphs;
+    std::vector<std::pair<int, int>> seen;   // (T, flip) run eagerly once
+    std::vector<int> uncapturable;            // lengths whose capture the runtime refused
+    void run_chunk(int T);
+    void advance(int T);
     float * h_pcm = nullptr;     // pinned
     int * h_err = nullptr;       // pinned
     conv::Workspace ws;
@@ -441,12 +458,12 @@ void Vocoder::Impl::decode_chunk(int T) {
             const int qs = run(ly.qkv, n, T, VH, qkv, 3 * HD, nullptr, nullptr, nullptr, true);
             const int hpc = QKV_THREADS / hd;
             NAVI_CUDA(navi::dev::launch_pdl(k_qkv_rope_append, dim3(T, 3, (nh + hpc - 1) / hpc), dim3(QKV_THREADS), 0, stream, ws.partial, qs,
-                                            qkv, nh, hd, pos0, ring, inv_freq, ly.kc, ly.vc));
+                                            qkv, nh, hd, d_pos0, ring, inv_freq, ly.kc, ly.vc));
         } else {
             run(ly.qkv, n, T, VH, qkv, 3 * HD);
-            NAVI_CUDA(navi::dev::launch_pdl(k_rope_append, dim3(T), dim3(256), 0, stream, qkv, nh, hd, pos0, ring, inv_freq, ly.kc, ly.vc));
+            NAVI_CUDA(navi::dev::launch_pdl(k_rope_append, dim3(T), dim3(256), 0, stream, qkv, nh, hd, d_pos0, ring, inv_freq, ly.kc, ly.vc));
         }
-        NAVI_CUDA(navi::dev::launch_pdl(k_window_attn, dim3(T, nh), dim3(128), 0, stream, qkv, nh, hd, pos0, window, ring, scale, ly.kc, ly.vc, att));
+        NAVI_CUDA(navi::dev::launch_pdl(k_window_attn, dim3(T, nh), dim3(128), 0, stream, qkv, nh, hd, d_pos0, window, ring, scale, ly.kc, ly.vc, att));
         NAVI_CUDA(cudaGetLastError());
         run(ly.o, att, T, HD, x, VH, x, ly.ln2, n);
         run(ly.gateup, n, T, VH, gu, 2 * FF);
@@ -497,6 +514,86 @@ void Vocoder::Impl::decode_chunk(int T) {
     std::swap(fin.hist, fin.hist2);
     snap("pcm", pcm, R, 1);
     pos0 += T;
+    flip ^= 1;
+}
+
+// Every history pair (read by a chunk's launch, its successor written by it), in one order.
+template <class F> void each_hist_pair(Vocoder::Impl & I, F && f) {
+    const auto cv = [&](CV & c) { f(c.hist, c.hist2); };
+    cv(I.rvq_proj); cv(I.pre_conv); cv(I.in_proj);
+    for (auto & ly : I.layers) { cv(ly.qkv); cv(ly.o); cv(ly.gateup); cv(ly.down); }
+    cv(I.out_proj);
+    for (int j = 0; j < 2; ++j) {
+        cv(I.up_conv[j]);
+        f(I.cnx[j].hist, I.cnx[j].hist2);
+        cv(I.cnx[j].pw1); cv(I.cnx[j].pw2);
+    }
+    cv(I.dec0);
+    for (auto & bk : I.blocks) {
+        cv(bk.up);
+        for (int k = 0; k < 3; ++k) { cv(bk.c1[k]); cv(bk.c2[k]); }
+    }
+    f(I.fin.hist, I.fin.hist2);
+}
+
+// What decode_chunk does to the host-side state (each history pair swapped once, the position
+// advanced), for a chunk whose launches ran from a graph.
+void Vocoder::Impl::advance(int T) {
+    each_hist_pair(*this, [](float *& a, float *& b) { std::swap(a, b); });
+    pos0 += T;
+    flip ^= 1;
+}
+
+// One chunk of T frames: from its graph when one exists for (T, history parity); else eagerly,
+// the first time, and captured the second (the capture advances the host state as an eager
+// run would, and the graph's launch then runs that chunk). With a stage hook, always eagerly.
+void Vocoder::Impl::run_chunk(int T) {
+    if (hook) { decode_chunk(T); return; }
+    for (const auto & g : graphs)
+        if (g.T == T && g.flip == flip) {
+            NAVI_CUDA(cudaGraphLaunch(g.exec, stream));
+            advance(T);
+            return;
+        }
+    const std::pair<int, int> key{T, flip};
+    bool before = false;
+    for (const auto & k : seen) before = before || k == key;
+    bool refused = false;
+    for (int u : uncapturable) refused = refused || u == T;
+    if (!before || refused || graphs.size() >= 32) {
+        if (!before) seen.push_back(key);
+        decode_chunk(T);
+        return;
+    }
+    // capture: the enqueue code runs without executing, so keep the state to fall back to
+    const int f0 = flip, p0 = pos0;
+    std::vector<float *> saved;
+    each_hist_pair(*this, [&](float *& a, float *& b) { saved.push_back(a); saved.push_back(b); });
+    cudaGraph_t g = nullptr;
+    NAVI_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    bool enqueued = true;
+    try {
+        decode_chunk(T);
+    } catch (const std::exception &) {
+        enqueued = false;
+    }
+    const cudaError_t end = cudaStreamEndCapture(stream, &g);
+    cudaGraphExec_t e = nullptr;
+    const cudaError_t inst = (enqueued && end == cudaSuccess && g) ? cudaGraphInstantiate(&e, g, 0) : cudaErrorStreamCaptureInvalidated;
+    if (g) cudaGraphDestroy(g);
+    if (inst != cudaSuccess) {
+        (void) cudaGetLastError();
+        uncapturable.push_back(T);
+        // undo what the capture did to the state, then run the chunk eagerly
+        std::size_t i = 0;
+        each_hist_pair(*this, [&](float *& a, float *& b) { a = saved[i++]; b = saved[i++]; });
+        flip = f0;
+        pos0 = p0;
+        decode_chunk(T);
+        return;
+    }
+    graphs.push_back({T, f0, e});
+    NAVI_CUDA(cudaGraphLaunch(e, stream));
 }
 
 std::unique_ptr<Vocoder> Vocoder::create(const Device & dev, const DeviceWeights & w, int max_chunk_frames, int /*max_frames*/) {
@@ -712,6 +809,8 @@ std::unique_ptr<Vocoder> Vocoder::create(const Device & dev, const DeviceWeights
     I.ws.err = I.alloc<int>(1);
 
     NAVI_CUDA(cudaMallocHost(&I.h_codes, C * p.vq_n_q * sizeof(int)));
+    NAVI_CUDA(cudaMallocHost(&I.h_pos0, sizeof(int)));
+    I.d_pos0 = I.alloc<int>(1);
     NAVI_CUDA(cudaMallocHost(&I.h_pcm, C * I.spf * sizeof(float)));
     NAVI_CUDA(cudaMallocHost(&I.h_err, sizeof(int)));
     NAVI_CUDA(cudaEventCreate(&I.ev0));
@@ -727,7 +826,9 @@ Vocoder::~Vocoder() {
     (void) cudaStreamSynchronize(I.stream);
     if (I.ev0) (void) cudaEventDestroy(I.ev0);
     if (I.ev1) (void) cudaEventDestroy(I.ev1);
+    for (const auto & g : I.graphs) (void) cudaGraphExecDestroy(g.exec);
     if (I.h_codes) (void) cudaFreeHost(I.h_codes);
+    if (I.h_pos0) (void) cudaFreeHost(I.h_pos0);
     if (I.h_pcm) (void) cudaFreeHost(I.h_pcm);
     if (I.h_err) (void) cudaFreeHost(I.h_err);
     for (void * ptr : I.owned) (void) cudaFree(ptr);
@@ -771,7 +872,9 @@ void Vocoder::decode_into(std::span<const std::int32_t> codes, int n_frames, flo
         const int T = std::min(I.Cmax, n_frames - f0);
         std::memcpy(I.h_codes, codes.data() + static_cast<std::size_t>(f0) * nq, static_cast<std::size_t>(T) * nq * sizeof(int));
         NAVI_CUDA(cudaMemcpyAsync(I.d_codes, I.h_codes, static_cast<std::size_t>(T) * nq * sizeof(int), cudaMemcpyHostToDevice, I.stream));
-        I.decode_chunk(T);
+        *I.h_pos0 = I.pos0;
+        NAVI_CUDA(cudaMemcpyAsync(I.d_pos0, I.h_pos0, sizeof(int), cudaMemcpyHostToDevice, I.stream));
+        I.run_chunk(T);
         const std::size_t ns = static_cast<std::size_t>(T) * I.spf;
         NAVI_CUDA(cudaMemcpyAsync(I.h_pcm, I.pcm, ns * sizeof(float), cudaMemcpyDeviceToHost, I.stream));
         NAVI_CUDA(cudaMemcpyAsync(I.h_err, I.ws.err, sizeof(int), cudaMemcpyDeviceToHost, I.stream));
