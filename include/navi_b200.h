@@ -234,6 +234,12 @@ int navi_frame_run_first_slot(navi_frame * f, int slot, const float * d_hidden, 
 int navi_frame_run_batch(navi_frame * f, int nb, const int * slots, navi_kv * const * kvs, const int * n_past,
                          const float * const * d_trailing, const navi_sampling * s, const uint64_t * seeds, const int * frame_index,
                          navi_frame_result * results);
+/* Frame 0 of nb = 2 or 4 streams in distinct slots in one launch: navi_frame_run_first_slot of
+ * each stream together (the code predictor only), stream i from d_hidden[i] and d_logits[i] of
+ * its prefill; codes bit for bit those of navi_frame_run_first_slot on that stream alone. */
+int navi_frame_run_first_batch(navi_frame * f, int nb, const int * slots, const float * const * d_hidden, const float * const * d_logits,
+                               const float * const * d_trailing, const navi_sampling * s, const uint64_t * seeds, const int * frame_index,
+                               navi_frame_result * results);
 /* Enqueue-only form of navi_frame_run_batch; navi_frame_collect_batch returns its results. */
 int navi_frame_enqueue_batch(navi_frame * f, int nb, const int * slots, navi_kv * const * kvs, const int * n_past,
                              const float * const * d_trailing, const navi_sampling * s, const uint64_t * seeds, const int * frame_index);

@@ -379,6 +379,18 @@ int navi_frame_enqueue_batch(navi_frame * f, int nb, const int * slots, navi_kv 
     });
 }
 
+int navi_frame_run_first_batch(navi_frame * f, int nb, const int * slots, const float * const * d_hidden, const float * const * d_logits,
+                               const float * const * d_trailing, const navi_sampling * s, const uint64_t * seeds, const int * frame_index,
+                               navi_frame_result * results) {
+    const int st = guard([&]() -> int {
+        if (!f || !slots || !d_hidden || !d_logits || !d_trailing || !seeds || !frame_index || !results) return set_err(NAVI_E_ARG, "NULL argument");
+        std::string err;
+        const int e = f->f->enqueue_first_batch(nb, slots, d_hidden, d_logits, d_trailing, to_sampling(s), seeds, frame_index, err);
+        return e != NAVI_OK ? set_err(e, err) : NAVI_OK;
+    });
+    if (st != NAVI_OK) return st;
+    return navi_frame_collect_batch(f, nb, results);
+}
 int navi_frame_collect_batch(navi_frame * f, int nb, navi_frame_result * results) {
     return guard([&]() -> int {
         if (!f || !results) return set_err(NAVI_E_ARG, "NULL argument");

@@ -67,6 +67,9 @@ struct Frame::Impl {
     Phase * prog_first = nullptr;
     Phase * prog_layers = nullptr;   // [TL][LAYER_PHASES]: one talker layer alone, then XOUT
     Phase * prog_batch[MAX_B + 1] = {};   // batched programs of 2 and 4 streams
+    Phase * prog_batch_first[MAX_B + 1] = {};   // their frame-0 form (the code predictor only)
+    int n_batch_first[MAX_B + 1] = {};
+    int sample_phase_first[MAX_B + 1][NCB] = {};
     int n_batch[MAX_B + 1] = {};
     int thead_phase[MAX_B + 1] = {};
     int sample_phase[MAX_B + 1][NCB] = {};
@@ -129,6 +132,8 @@ struct Frame::Impl {
         int n_past = 0;
         uint64_t seed = 0;
         int frame_index = 0;
+        const float * hidden = nullptr;    // batched frame 0: the prefill's post-norm hidden
+        const float * logits = nullptr;    // and its codec logits
     };
 
     static constexpr int LAYER_PHASES = 6;
@@ -189,15 +194,15 @@ struct Frame::Impl {
                int layer = -1, float * layer_out = nullptr) {
         NAVI_CUDA(cudaSetDevice(ordinal));
         Args A{};
-        const bool first = hidden_in != nullptr;
+        const bool first = hidden_in != nullptr || (nb > 1 && in[0].hidden != nullptr);
         if (nb == 1) {
             A.prog = layer >= 0 ? prog_layers + static_cast<size_t>(layer) * LAYER_PHASES : first ? prog_first : prog_full;
             A.nphase = layer >= 0 ? LAYER_PHASES : first ? n_first : n_full;
         } else {
-            A.prog = prog_batch[nb];
-            A.nphase = n_batch[nb];
+            A.prog = first ? prog_batch_first[nb] : prog_batch[nb];
+            A.nphase = first ? n_batch_first[nb] : n_batch[nb];
             A.thead_phase = thead_phase[nb];
-            for (int cb = 0; cb < NCB; ++cb) A.sample_phase[cb] = sample_phase[nb][cb];
+            for (int cb = 0; cb < NCB; ++cb) A.sample_phase[cb] = first ? sample_phase_first[nb][cb] : sample_phase[nb][cb];
         }
         A.mw = dmw;
         A.d = d;
@@ -248,6 +253,8 @@ struct Frame::Impl {
                 A.kvmap[i] = A.attn_chunk[i] > 2 * KV_BOX ? kv_maps(sl, *q.kv) : nullptr;
             }
             if (!first) rope_row(inv_t_h, q.n_past, A.rope_t[i]);
+            A.first_hidden[i] = nb > 1 ? q.hidden : nullptr;
+            A.first_logits[i] = nb > 1 ? q.logits : nullptr;
             A.seed[i] = q.seed;
             A.frame_index[i] = q.frame_index;
             for (int cb = 0; cb < NCB; ++cb) A.pcg_seed[i][cb] = navi::dev::pcg_draw_seed(q.seed, q.frame_index, cb);
@@ -477,6 +484,14 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
         I.n_batch[nb] = static_cast<int>(v.size());
         I.prog_batch[nb] = I.alloc<Phase>(v.size());
         NAVI_CUDA(cudaMemcpy(I.prog_batch[nb], v.data(), v.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+        // frame 0: the same from the first SAMPLE on (codebook 0 drawn from each stream's
+        // prefill logits, position 0 on its prefill hidden)
+        const int cut = I.sample_phase[nb][0];
+        std::vector<Phase> f(v.begin() + cut, v.end());
+        for (int cb = 0; cb < NCB; ++cb) I.sample_phase_first[nb][cb] = I.sample_phase[nb][cb] - cut;
+        I.n_batch_first[nb] = static_cast<int>(f.size());
+        I.prog_batch_first[nb] = I.alloc<Phase>(f.size());
+        NAVI_CUDA(cudaMemcpy(I.prog_batch_first[nb], f.data(), f.size() * sizeof(Phase), cudaMemcpyHostToDevice));
     }
 
     // exchange words (one allocation, cleared when tags wrap)
@@ -643,6 +658,27 @@ int Frame::enqueue_batch(int nb, const int * slots, KvCache * const * kvs, const
 }
 
 void Frame::collect_batch(FrameResult * out) { impl_->collect(out); }
+
+int Frame::enqueue_first_batch(int nb, const int * slots, const float * const * d_hidden, const float * const * d_logits,
+                               const float * const * d_trailing, const Sampling & s, const uint64_t * seeds, const int * frame_index,
+                               std::string & err) {
+    Impl & I = *impl_;
+    if (nb != 2 && nb != 4) { err = "a batched frame 0 takes 2 or 4 streams"; return NAVI_E_ARG; }
+    Impl::StreamIn in[MAX_B];
+    bool used[MAX_B] = {};
+    for (int i = 0; i < nb; ++i) {
+        if (slots[i] < 0 || slots[i] >= MAX_B || used[slots[i]]) { err = "stream slots must be distinct, in 0.." + std::to_string(MAX_B - 1); return NAVI_E_ARG; }
+        used[slots[i]] = true;
+        if (!d_hidden[i] || !d_logits[i] || !d_trailing[i]) { err = "NULL hidden, logits or trailing row"; return NAVI_E_ARG; }
+        in[i].slot = slots[i];
+        in[i].hidden = d_hidden[i];
+        in[i].logits = d_logits[i];
+        in[i].trailing = d_trailing[i];
+        in[i].seed = seeds[i];
+        in[i].frame_index = frame_index[i];
+    }
+    return I.launch(in, nb, nullptr, nullptr, s, err);
+}
 
 int Frame::enqueue(KvCache & kv, int n_past, const float * d_trailing, const Sampling & s, uint64_t seed, int frame_index,
                    std::string & err) {

@@ -66,6 +66,11 @@ public:
     int enqueue_batch(int nb, const int * slots, KvCache * const * kvs, const int * n_past, const float * const * d_trailing,
                       const Sampling & s, const uint64_t * seeds, const int * frame_index, std::string & err);
     void collect_batch(FrameResult * out);
+    // Frame 0 of nb (2 or 4) streams in one launch (run_first of each, together): stream i
+    // from the post-norm hidden and codec logits of its prefill; collect_batch gives the results.
+    int enqueue_first_batch(int nb, const int * slots, const float * const * d_hidden, const float * const * d_logits,
+                            const float * const * d_trailing, const Sampling & s, const uint64_t * seeds, const int * frame_index,
+                            std::string & err);
     // One talker decoder layer alone (the layer phases of the frame: q/k/v, attention over
     // positions [0, n_past) plus the new one, o, gate/up, down) on the f32 input d_x at
     // position n_past, writing the f32 residual stream after the layer to d_out and the

@@ -1008,7 +1008,20 @@ __device__ void consumer(const Args & A, Sm & S) {
                 const int V = cb == 0 ? d.TV : d.CV;
                 const uint64_t * src = cb == 0 ? A.w.logits + static_cast<size_t>(st) * d.TV
                                                : A.w.clogits + (static_cast<size_t>(st) * (NCB - 1) + cb - 1) * d.CV;
-                const bool ok = ll_fetch(src, V, ptag, sc.s, A, S.ctrl, p);
+                bool ok = true;
+                if (cb == 0 && A.first_logits[st]) {
+                    // batched frame 0: the stream's prefill logits
+                    for (int i0 = 0; i0 < V; i0 += 4 * NCT) {
+                        float v[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) v[k] = i0 + tid + k * NCT < V ? __ldcg(A.first_logits[st] + i0 + tid + k * NCT) : 0.f;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            if (i0 + tid + k * NCT < V) sc.s[i0 + tid + k * NCT] = v[k];
+                    }
+                } else {
+                    ok = ll_fetch(src, V, ptag, sc.s, A, S.ctrl, p);
+                }
                 if (!consumers_ok(S, ok)) break;
                 stamp(A, p, 0);
                 const int code = sample_cta<NCT>(V, sample_cfg(A, cb, st), sc, BID);
@@ -1130,6 +1143,9 @@ __device__ void consumer(const Args & A, Sm & S) {
                 nnorm = ncol;
                 if (ph.op == TQKV && (ph.layer == 0 || ph.pos == POS_STEP_IN)) {
                     if (ok) stage_loaded(ncol, [&](int c, int i) { return __ldcg(A.step_in[c] + i); });
+                } else if (batched && ph.layer == 0 && ph.pos == 0 && A.first_hidden[0]) {
+                    // batched frame 0, position 0: every stream's prefill hidden
+                    if (ok) stage_loaded(ncol, [&](int c, int i) { return __ldcg(A.first_hidden[c] + i); });
                 } else if (batched && ph.layer == 0 && ph.pos == 0) {
                     // batched position 0: every stream's post-norm talker hidden
                     if (ok) {

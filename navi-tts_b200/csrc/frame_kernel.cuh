@@ -150,6 +150,9 @@ struct Args {
     // single stream, frame 0
     const float * hidden_in;   // the prefill's post-norm hidden
     const float * logits_in;   // the prefill's codec logits
+    // batched frame 0 (the code predictor only): every stream's prefill hidden and logits
+    const float * first_hidden[MAX_B];
+    const float * first_logits[MAX_B];
     const float * inv_freq_t;  // [HD/2]
     const float * inv_freq_c;
     const float * rope_c;      // code predictor, positions 0..15: [NCB][HD] = cos[HD/2], sin[HD/2]

@@ -171,7 +171,7 @@ std::vector<SynthStats> Graph::synth_batch(std::span<const SynthRequest> reqs, c
         flush(s, false);
         if (l.frame >= reqs[static_cast<size_t>(s)].max_frames) l.done = true;
     };
-    // prompts, prefills and frame 0 of every stream (graph.cpp:52-72 per stream)
+    // prompts and prefills of every stream (graph.cpp:52-72 per stream)
     for (int s = 0; s < n; ++s) {
         const SynthRequest & req = reqs[static_cast<size_t>(s)];
         SynthStats & ss = st[static_cast<size_t>(s)];
@@ -193,8 +193,36 @@ std::vector<SynthStats> Graph::synth_batch(std::span<const SynthRequest> reqs, c
             l.batch = req.vocoder_batch > 0 ? std::min(req.vocoder_batch, maxc) : maxc;
             l.first = req.first_batch > 0 ? std::min(req.first_batch, l.batch) : l.batch;
         }
-        const float * trailing = l.pr->n_trailing > 0 ? l.pr->trailing : l.pr->tts_pad;
-        take(s, frame_->run_first(tk.d_hidden(), tk.d_logits(), trailing, req.sampling, req.seed, 0, s));
+    }
+    // frame 0 of every stream: 4 or 2 at a time in one launch, a last single one alone
+    for (int s0 = 0; s0 < n;) {
+        const int left = n - s0;
+        const int nb = left >= 4 ? 4 : left >= 2 ? 2 : 1;
+        const float * hid[Frame::MAX_SLOTS], * lg[Frame::MAX_SLOTS], * trail[Frame::MAX_SLOTS];
+        int slots[Frame::MAX_SLOTS], fidx[Frame::MAX_SLOTS];
+        uint64_t seeds[Frame::MAX_SLOTS];
+        for (int j = 0; j < nb; ++j) {
+            const int s = s0 + j;
+            const Live & l = L[static_cast<size_t>(s)];
+            Talker & tk = *talkers_[static_cast<size_t>(s)];
+            hid[j] = tk.d_hidden();
+            lg[j] = tk.d_logits();
+            trail[j] = l.pr->n_trailing > 0 ? l.pr->trailing : l.pr->tts_pad;
+            slots[j] = s;
+            fidx[j] = 0;
+            seeds[j] = reqs[static_cast<size_t>(s)].seed;
+        }
+        if (nb == 1) {
+            take(s0, frame_->run_first(hid[0], lg[0], trail[0], reqs[static_cast<size_t>(s0)].sampling, seeds[0], 0, s0));
+        } else {
+            std::string err;
+            const int stt = frame_->enqueue_first_batch(nb, slots, hid, lg, trail, reqs[0].sampling, seeds, fidx, err);
+            if (stt != NAVI_OK) fail("synth_batch: " + err, stt);
+            FrameResult res[Frame::MAX_SLOTS];
+            frame_->collect_batch(res);
+            for (int j = 0; j < nb; ++j) take(s0 + j, res[j]);
+        }
+        s0 += nb;
     }
     // frames >= 1 of the running streams, together: groups of 4, 2 and 1 streams per launch
     for (;;) {

@@ -131,6 +131,8 @@ SIGNATURES = [
                                           POINTER(FrameResult)]),
     ("navi_frame_run_batch", c_int, [c_void_p, c_int, POINTER(c_int), POINTER(POINTER(KV)), POINTER(c_int), POINTER(c_void_p),
                                      POINTER(Sampling), POINTER(c_uint64), POINTER(c_int), POINTER(FrameResult)]),
+    ("navi_frame_run_first_batch", c_int, [c_void_p, c_int, POINTER(c_int), POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p),
+                                           POINTER(Sampling), POINTER(c_uint64), POINTER(c_int), POINTER(FrameResult)]),
     ("navi_frame_enqueue_batch", c_int, [c_void_p, c_int, POINTER(c_int), POINTER(POINTER(KV)), POINTER(c_int), POINTER(c_void_p),
                                          POINTER(Sampling), POINTER(c_uint64), POINTER(c_int)]),
     ("navi_frame_collect_batch", c_int, [c_void_p, c_int, POINTER(FrameResult)]),

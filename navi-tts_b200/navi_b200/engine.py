@@ -435,6 +435,16 @@ class Frame:
         st = lib().navi_frame_run_batch(self.h, nb, sl, kp, npst, tr, byref(s.c()), sd, fi, res)
         return [_result(res[i], st) for i in range(nb)]
 
+    def run_first_batch(self, slots, d_hidden, d_logits, d_trailing, s: Sampling, seeds, frame_index) -> list:
+        """Frame 0 of len(slots) streams (2 or 4) in one launch, each from its prefill's hidden and
+        logits (device pointers); a FrameResult per stream."""
+        nb = len(slots)
+        res = (capi.FrameResult * nb)()
+        st = lib().navi_frame_run_first_batch(self.h, nb, (c_int * nb)(*slots), (c_void_p * nb)(*d_hidden), (c_void_p * nb)(*d_logits),
+                                              (c_void_p * nb)(*d_trailing), byref(s.c()), (ctypes.c_uint64 * nb)(*seeds),
+                                              (c_int * nb)(*frame_index), res)
+        return [_result(res[i], st) for i in range(nb)]
+
     def enqueue_batch(self, slots, kvs, n_past, d_trailing, s: Sampling, seeds, frame_index) -> None:
         nb, sl, kp, npst, tr, sd, fi = self._batch_args(slots, kvs, n_past, d_trailing, seeds, frame_index)
         check(lib().navi_frame_enqueue_batch(self.h, nb, sl, kp, npst, tr, byref(s.c()), sd, fi))

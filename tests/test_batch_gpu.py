@@ -130,6 +130,40 @@ def test_batched_frames_follow_each_stream(small_navi):
     assert same >= 19, (same, batched, single)
 
 
+@pytest.mark.parametrize("nb", [2, 4])
+def test_batched_first_frames_match_each_stream(small_navi, nb):
+    """Frame 0 of nb streams in one launch (navi_frame_run_first_batch): each stream's codes and
+    step embedding are those of navi_frame_run_first on that stream alone, bit for bit, and its
+    code-predictor logits agree within rel-L2 2e-4 (the single-stream program runs positions 0
+    and 1 as one two-column pass, so the float sums are not in the same order)."""
+    S = Streams(small_navi, nb, [1] * nb)
+    T = Streams(small_navi, nb, [1] * nb)
+    solo = T.frame
+    s = engine.Sampling(top_p=0.9, cp_top_p=0.9, rng=capi.NAVI_RNG_PHILOX)
+    slots = [3, 0, 2, 1][:nb]
+    g = torch.Generator().manual_seed(21)
+    hid = [torch.randn(S.H, generator=g).cuda() for _ in range(nb)]
+    lg = [(torch.randn(S.TV, generator=g) * 3).cuda() for _ in range(nb)]
+    trail = [torch.randn(S.H, generator=g).cuda() for _ in range(nb)]
+    for sl in slots:
+        S.frame.reset_slot(sl)
+    res = S.frame.run_first_batch(slots, [t.data_ptr() for t in hid], [t.data_ptr() for t in lg], [t.data_ptr() for t in trail], s,
+                                  [31 + i for i in range(nb)], [0] * nb)
+    outs = []
+    for i in range(nb):
+        assert res[i].ok, res[i].error
+        _, _, clg = S.frame.inspect_stream(i)
+        outs.append((res[i].codes, clg, dev_f32(S.frame.d_step_out_slot(slots[i]), S.H)))
+    for i in range(nb):
+        solo.reset()
+        r = solo.run_first(hid[i].data_ptr(), lg[i].data_ptr(), trail[i].data_ptr(), s, 31 + i, 0)
+        assert r.ok, r.error
+        _, _, clg = solo.inspect()
+        assert r.codes == outs[i][0], (i, r.codes, outs[i][0])
+        assert om.rel_l2(np.asarray(clg), np.asarray(outs[i][1])) < REL, i
+        assert np.array_equal(dev_f32(solo.d_step_out(), S.H), outs[i][2]), i
+
+
 def test_full_size_batched_frame_matches_oracle(full_navi):
     """configs[1]+[2] shapes, four streams at KV 64, 128, 256 and 512."""
     nb = 4
