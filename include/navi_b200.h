@@ -217,7 +217,7 @@ int navi_frame_set_step_in(navi_frame * f, const float * d_step);
 int navi_frame_grid_blocks(const navi_frame * f);
 
 /* ---- batched decode (no counterpart in the reference, which decodes one stream per launch,
- *      docs/DESIGN.md:35; the per-stream math is Frame::run's, frame.hip:798-810) ----
+ *      the reference's docs/DESIGN.md:35; the per-stream math is Frame::run's, frame.hip:798-810) ----
  * A frame keeps NAVI_FRAME_SLOTS stream slots, each with its own repetition set and step
  * embedding; the single-stream calls above use slot 0. navi_frame_run_batch decodes one frame
  * of nb = 1, 2 or 4 streams in distinct slots in one launch that reads every weight once:

@@ -5,7 +5,7 @@ that stream alone (talker step, code predictor, step embedding) and what a singl
 frame gives: hidden / logits / code-predictor logits within rel-L2 2e-4 of the oracle, every
 code the oracle sampler's draw on the GPU's own logits, the new K/V rows of each stream's own
 cache only. The per-stream math is the reference's Frame::run (frame.hip:798-810); the
-reference decodes one stream per launch (docs/DESIGN.md:35), so batching has no counterpart
+reference decodes one stream per launch (its docs/DESIGN.md:35), so batching has no counterpart
 there.
 """
 import numpy as np
