@@ -573,13 +573,15 @@ def run_ours(args):
     torch.cuda.synchronize(local)
     if dist:
         dist.barrier()
+    prev_stream = torch.cuda.current_stream(local)
+    torch.cuda.set_stream(stream)   # the H2D copies go on the frame's stream, in order with the frames
     t0 = time.perf_counter()
     for i in range(args.steps):
-        with torch.cuda.stream(stream):
-            d_trailing.copy_(h_trailing, non_blocking=True)
+        d_trailing.copy_(h_trailing, non_blocking=True)
         r = frame.run(kv, L, d_trailing.data_ptr(), s, seed, args.warmup + i)
         assert r.ok, r.error
     e2e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
+    torch.cuda.set_stream(prev_stream)
     # the KV-length sweep of configs[1] (device time, fewer frames)
     sweep = {}
     for Ls in (64, 512, 2048):

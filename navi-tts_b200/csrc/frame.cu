@@ -100,7 +100,7 @@ struct Frame::Impl {
     int kvmap_pos[MAX_B] = {};
     uint64_t * ll_base = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-    int32_t * h_out = nullptr;   // pinned: MAX_B x 16 codes + 4 control words
+    int32_t * h_out = nullptr;   // pinned: 4 control words + MAX_B x 16 codes (the device block's layout)
     unsigned long long * prof = nullptr;
     bool prof_on = false;
     int prof_cta = 0;
@@ -290,8 +290,8 @@ struct Frame::Impl {
             return NAVI_E_LAUNCH;
         }
         NAVI_CUDA(cudaEventRecord(ev1, stream));
-        NAVI_CUDA(cudaMemcpyAsync(h_out, w.codes, static_cast<size_t>(nb) * NCB * sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
-        NAVI_CUDA(cudaMemcpyAsync(h_out + MAX_B * NCB, w.ctl, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
+        // the 4 control words and the codes are one block in device memory: one copy
+        NAVI_CUDA(cudaMemcpyAsync(h_out, w.ctl, (4 + static_cast<size_t>(nb) * NCB) * sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
         if (layer < 0)
             for (int i = 0; i < nb; ++i) cur[in[i].slot] ^= 1;
         last_tag = tag;
@@ -312,7 +312,7 @@ struct Frame::Impl {
         NAVI_CUDA(cudaStreamSynchronize(stream));
         float ms = 0.f;
         NAVI_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
-        const uint32_t * ctl = reinterpret_cast<const uint32_t *>(h_out + MAX_B * NCB);
+        const uint32_t * ctl = reinterpret_cast<const uint32_t *>(h_out);
         const bool failed = ctl[2] == last_tag || ctl[0] != last_tag;
         for (int i = 0; i < nb; ++i) {
             FrameResult & r = out[i];
@@ -324,7 +324,7 @@ struct Frame::Impl {
                           "): the cooperative grid could not run to completion";
                 continue;
             }
-            std::memcpy(r.codes, h_out + i * NCB, sizeof(r.codes));
+            std::memcpy(r.codes, h_out + 4 + i * NCB, sizeof(r.codes));
             r.eos = r.codes[0] == eos;
             r.ok = true;
         }
@@ -514,9 +514,10 @@ std::unique_ptr<Frame> Frame::create(const Device & dev, const DeviceWeights & w
     I.seen = I.alloc<uint8_t>(static_cast<size_t>(MAX_B) * d.TV);
     I.kvmaps = I.alloc<uint8_t>(static_cast<size_t>(MAX_B) * MAX_TL * 2 * TMAP_BYTES + 64);
     if (reinterpret_cast<std::uintptr_t>(I.kvmaps) & 63u) fail("frame: tensor-map storage is not 64-byte aligned", NAVI_E_CUDA);
-    I.w.codes = I.alloc<int32_t>(static_cast<size_t>(MAX_B) * NCB);
+    // control words [4] then the codes [MAX_B][16]: a launch's results leave in one copy
+    I.w.ctl = I.alloc<unsigned>(4 + static_cast<size_t>(MAX_B) * NCB);
+    I.w.codes = reinterpret_cast<int32_t *>(I.w.ctl + 4);
     I.w.hidden = I.alloc<float>(static_cast<size_t>(MAX_B) * d.H);
-    I.w.ctl = I.alloc<unsigned>(4);
     for (int sl = 0; sl < MAX_B; ++sl) {
         I.step[sl][0] = I.alloc<float>(d.H);
         I.step[sl][1] = I.alloc<float>(d.H);
