@@ -50,6 +50,8 @@ struct KArgs {
     float * hist_out;                 // next chunk's history, or null
     int * err;
     int Cout, Cin, K, dil, H, T, x_stride, y_stride, r_stride;
+    int x_slices;                     // 2: x holds two split-K partial slices, summed while staging
+    long long x_sstride;              // elements from one slice to the next
     int BN, NT, MT, CB, cb_per_split, splits;
     int lbo, wrows, tmem_cols;
     int nst;                          // weight-ring stages
@@ -118,11 +120,17 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 // the block) and rows u/8 + 16 i of each batch of 16 * SR<PRO> window rows.  The loads of
 // the next batch (possibly of the next channel block or unit) are issued before the
 // current batch is converted, so a thread keeps a batch in flight while it converts.
-template <int PRO> struct SR { static constexpr int n = PRO == PRO_SILU_GATE ? 2 : 4; };
+// A gated input may arrive as the two split-K partial slices of the projection that made it
+// (its reduction folded into this launch): the second slice's rows ride along in e/f.
+template <int PRO> struct SR {
+    static constexpr int n = PRO == PRO_SILU_GATE ? 2 : 4;
+    static constexpr int ne = PRO == PRO_SILU_GATE ? n : 1;
+};
 
 template <int PRO>
 struct Rows {
     float4 p0[SR<PRO>::n], p1[SR<PRO>::n], q0[SR<PRO>::n], q1[SR<PRO>::n];
+    float4 e0[SR<PRO>::ne], e1[SR<PRO>::ne], f0[SR<PRO>::ne], f1[SR<PRO>::ne];
 };
 
 template <int PRO>
@@ -140,9 +148,16 @@ __device__ __forceinline__ void load_rows(Rows<PRO> & R, const KArgs & a, int c0
         const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
         R.p0[k] = src ? __ldg(reinterpret_cast<const float4 *>(src)) : z;
         R.p1[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + 4)) : z;
-        if (PRO == PRO_SILU_GATE) {
+        if constexpr (PRO == PRO_SILU_GATE) {
             R.q0[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + a.Cin)) : z;
             R.q1[k] = src ? __ldg(reinterpret_cast<const float4 *>(src + a.Cin + 4)) : z;
+            if (a.x_slices > 1) {   // the second partial slice (gated input has no history)
+                const float * s1 = src ? src + a.x_sstride : nullptr;
+                R.e0[k] = s1 ? __ldcg(reinterpret_cast<const float4 *>(s1)) : z;
+                R.e1[k] = s1 ? __ldcg(reinterpret_cast<const float4 *>(s1 + 4)) : z;
+                R.f0[k] = s1 ? __ldcg(reinterpret_cast<const float4 *>(s1 + a.Cin)) : z;
+                R.f1[k] = s1 ? __ldcg(reinterpret_cast<const float4 *>(s1 + a.Cin + 4)) : z;
+            }
         }
     }
 }
@@ -168,8 +183,18 @@ __device__ __forceinline__ void store_rows(const Rows<PRO> & R, const KArgs & a,
         const int r = rb + 16 * k;
         if (r >= a.wrows) break;
         float v[8] = {R.p0[k].x, R.p0[k].y, R.p0[k].z, R.p0[k].w, R.p1[k].x, R.p1[k].y, R.p1[k].z, R.p1[k].w};
-        if (PRO == PRO_SILU_GATE) {
-            const float up[8] = {R.q0[k].x, R.q0[k].y, R.q0[k].z, R.q0[k].w, R.q1[k].x, R.q1[k].y, R.q1[k].z, R.q1[k].w};
+        if constexpr (PRO == PRO_SILU_GATE) {
+            float up[8] = {R.q0[k].x, R.q0[k].y, R.q0[k].z, R.q0[k].w, R.q1[k].x, R.q1[k].y, R.q1[k].z, R.q1[k].w};
+            if (a.x_slices > 1) {
+                // slice 0 + slice 1 (+ 0, the absent bias): the split-K reduction's own sum
+                const float g1[8] = {R.e0[k].x, R.e0[k].y, R.e0[k].z, R.e0[k].w, R.e1[k].x, R.e1[k].y, R.e1[k].z, R.e1[k].w};
+                const float u1[8] = {R.f0[k].x, R.f0[k].y, R.f0[k].z, R.f0[k].w, R.f1[k].x, R.f1[k].y, R.f1[k].z, R.f1[k].w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    v[i] = (v[i] + g1[i]) + 0.f;
+                    up[i] = (up[i] + u1[i]) + 0.f;
+                }
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = v[i] / (1.f + __expf(-v[i])) * up[i];
         }
@@ -660,6 +685,9 @@ int launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) {
     if (c.pro == PRO_SNAKE && (!c.snake_a || !c.snake_b || ((reinterpret_cast<std::uintptr_t>(c.snake_a) | reinterpret_cast<std::uintptr_t>(c.snake_b)) & 15u)))
         fail("conv: Snake coefficients missing or misaligned", NAVI_E_SHAPE);
     if (c.pro == PRO_SILU_GATE && c.hist) fail("conv: gated input has no history", NAVI_E_SHAPE);
+    if (c.x_slices != 1 && (c.x_slices != 2 || c.pro != PRO_SILU_GATE || c.x_slice_stride % 4 ||
+                            c.x_slice_stride < static_cast<std::size_t>(c.T) * c.x_stride))
+        fail("conv: a folded reduction takes the 2 partial slices of a gated input, 16-byte aligned and apart", NAVI_E_SHAPE);
     if (c.hist_out && c.hist_out == c.hist) fail("conv: the next history needs a buffer of its own", NAVI_E_ARG);
     if ((c.epi == EPI_RESIDUAL || c.epi == EPI_SCALE_RESIDUAL) && !c.resid) fail("conv: residual missing", NAVI_E_SHAPE);
     if (c.epi == EPI_SCALE_RESIDUAL && !c.scale) fail("conv: layer scale missing", NAVI_E_SHAPE);
@@ -676,6 +704,7 @@ int launch(const Conv & c, const Workspace & ws, int sms, cudaStream_t stream) {
     ka.hist_out = c.hist ? c.hist_out : nullptr;
     ka.Cout = c.Cout; ka.Cin = c.Cin; ka.K = c.K; ka.dil = c.dil; ka.H = (c.K - 1) * c.dil; ka.T = c.T;
     ka.x_stride = c.x_stride; ka.y_stride = c.y_stride; ka.r_stride = c.r_stride;
+    ka.x_slices = c.x_slices; ka.x_sstride = static_cast<long long>(c.x_slice_stride);
     ka.BN = p.BN; ka.NT = p.NT; ka.MT = p.MT; ka.CB = p.CB; ka.cb_per_split = p.cb_per_split; ka.splits = p.splits;
     ka.lbo = p.lbo; ka.wrows = p.BN + ka.H; ka.tmem_cols = p.tmem_cols; ka.timeout_ns = ws.timeout_ns;
     ka.nst = p.nst; ka.resident = p.resident ? 1 : 0;

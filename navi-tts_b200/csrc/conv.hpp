@@ -68,6 +68,12 @@ struct Conv {
     int Cout = 0, Cin = 0, K = 1, dil = 1;
     const float * x = nullptr;               // rows [T][x_stride]; SILU_GATE: row = [gate | up], Cin each
     int x_stride = 0, T = 0;
+    // 2: x holds the 2 split-K partial slices an earlier launch left with defer_reduce (slice 1
+    // at x + x_slice_stride, rows [T][x_stride] each); the staging sums them in slice order, the
+    // values that launch's own reduction would have written (it must have had no bias).
+    // PRO_SILU_GATE only.
+    int x_slices = 1;
+    std::size_t x_slice_stride = 0;
     const float * hist = nullptr;            // [H][Cin] or null
     // when set (with hist): receives the last H rows of [hist; x], i.e. the next chunk's
     // history, written by the launch itself ([H][Cin], a buffer other than hist)

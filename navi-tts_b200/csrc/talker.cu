@@ -381,6 +381,10 @@ struct Talker::Impl {
 
     int sms = 148;
     conv::Workspace ws;
+    // the gate/up projection's two split-K partial slices when the down projection sums them
+    // (ws_gu.partial, 2 x rows x 2 ff), for prompts of up to GU_FOLD_ROWS rows
+    static constexpr int GU_FOLD_ROWS = 64;
+    conv::Workspace ws_gu;
 
     // The prefill's launches for one prompt length, captured as a CUDA graph after the first
     // (eager) prefill of that length: about 280 launches with their host-side planning and
@@ -505,6 +509,9 @@ std::unique_ptr<Talker> Talker::create(const Device & dev, const DeviceWeights &
         I.ws.partial = I.alloc<float>(std::max<std::size_t>(part, 1));
         I.ws.partial_cap = part;
         I.ws.err = I.alloc<int>(1);
+        I.ws_gu = I.ws;
+        I.ws_gu.partial_cap = 2ull * Impl::GU_FOLD_ROWS * 2 * I.F;
+        I.ws_gu.partial = I.alloc<float>(I.ws_gu.partial_cap);
     }
     NAVI_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void *>(&k_prefill_attn_mma), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(PA_SMEM)));
@@ -638,10 +645,33 @@ void Talker::Impl::enqueue_prefill(int T) {
         // the RMSNorms after the O projection and (but for the last layer) after the down
         // projection are written by those GEMMs' launches
         I.gemm(ly.wo, nullptr, I.att, I.Q, T, I.Q, H, I.x, H, EPI_RESIDUAL, false, I.x, ly.ln2, I.n);
-        I.gemm(ly.wgu, nullptr, I.n, H, T, H, 2 * I.F, I.gu, 2 * I.F, EPI_NONE);
+        // gate/up: a launch that splits K in two leaves both partial slices, and the down
+        // projection's staging adds them (one reduction launch fewer per layer)
+        const bool fold = T <= GU_FOLD_ROWS && conv::plan(gemm_desc(ly.wgu, nullptr, H, T, H, 2 * I.F, 2 * I.F, EPI_NONE, false), sms).splits == 2;
+        if (fold) {
+            conv::Conv c = gemm_desc(ly.wgu, nullptr, H, T, H, 2 * I.F, 2 * I.F, EPI_NONE, false);
+            c.x = I.n;
+            c.y = I.gu;
+            c.defer_reduce = true;
+            if (conv::launch(c, ws_gu, sms, stream) != 2) fail("talker: the gate/up projection did not split in two", NAVI_E_SHAPE);
+        } else {
+            I.gemm(ly.wgu, nullptr, I.n, H, T, H, 2 * I.F, I.gu, 2 * I.F, EPI_NONE);
+        }
         const bool last = l + 1 == tp.n_layer;
-        I.gemm(ly.wd, nullptr, I.gu, 2 * I.F, T, I.F, H, I.x, H, EPI_RESIDUAL, true, I.x, last ? nullptr : I.layers[static_cast<size_t>(l + 1)].ln1,
-               last ? nullptr : I.n);
+        {
+            conv::Conv c = gemm_desc(ly.wd, nullptr, 2 * I.F, T, I.F, H, H, EPI_RESIDUAL, true);
+            c.x = fold ? ws_gu.partial : I.gu;
+            if (fold) {
+                c.x_slices = 2;
+                c.x_slice_stride = static_cast<std::size_t>(T) * 2 * I.F;
+            }
+            c.y = I.x;
+            c.resid = I.x;
+            c.norm_w = last ? nullptr : I.layers[static_cast<size_t>(l + 1)].ln1;
+            c.norm_out = last ? nullptr : I.n;
+            c.norm_eps = tp.rms_eps;
+            conv::launch(c, ws, sms, stream);
+        }
     }
     // the last row: final norm and the codec head
     NAVI_CUDA(navi::dev::launch_pdl(k_rmsnorm, dim3(1), dim3(256), 0, I.stream, I.x + static_cast<size_t>(T - 1) * H, I.final_norm, H,

@@ -359,6 +359,7 @@ struct Vocoder::Impl {
     float * h_pcm = nullptr;     // pinned
     int * h_err = nullptr;       // pinned
     conv::Workspace ws;
+    conv::Workspace ws_gu;   // the gate/up projections' two partial slices, read by the down projections
 
     template <class T> T * alloc(std::size_t n_elems) {
         void * ptr = nullptr;
@@ -381,9 +382,11 @@ struct Vocoder::Impl {
     }
 
     // norm_w: also writes the rows of y RMS-normalised with these weights into norm_out
-    // defer: a split-K launch leaves its partial sums in ws.partial; returns their slice count
+    // defer: a split-K launch leaves its partial sums in the workspace (wsp, else ws); returns
+    // their slice count.  x_slices 2: xin holds the 2 partial slices of such a launch, [T][x_stride] each
     int run(CV & cv, const float * xin, int T, int x_stride, float * y, int y_stride, const float * resid = nullptr,
-            const float * norm_w = nullptr, float * norm_out = nullptr, bool defer = false) {
+            const float * norm_w = nullptr, float * norm_out = nullptr, bool defer = false, const conv::Workspace * wsp = nullptr,
+            int x_slices = 1) {
         conv::Conv c = cv.c;
         c.weights_settled = true;   // packed in create(), which synchronises before returning
         c.x = xin;
@@ -399,7 +402,9 @@ struct Vocoder::Impl {
         c.norm_out = norm_out;
         c.norm_eps = eps;
         c.defer_reduce = defer;
-        const int splits = conv::launch(c, ws, sms, stream);
+        c.x_slices = x_slices;
+        c.x_slice_stride = x_slices > 1 ? static_cast<std::size_t>(T) * x_stride : 0;
+        const int splits = conv::launch(c, wsp ? *wsp : ws, sms, stream);
         std::swap(cv.hist, cv.hist2);
         return splits;
     }
@@ -466,8 +471,16 @@ void Vocoder::Impl::decode_chunk(int T) {
         NAVI_CUDA(navi::dev::launch_pdl(k_window_attn, dim3(T, nh), dim3(128), 0, stream, qkv, nh, hd, d_pos0, window, ring, scale, ly.kc, ly.vc, att));
         NAVI_CUDA(cudaGetLastError());
         run(ly.o, att, T, HD, x, VH, x, ly.ln2, n);
-        run(ly.gateup, n, T, VH, gu, 2 * FF);
-        run(ly.down, gu, T, 2 * FF, x, VH, x, l + 1 < layers.size() ? layers[l + 1].ln1 : final_norm, n);
+        // gate/up: a launch that splits K in two leaves both partial slices, and the down
+        // projection's staging adds them (one reduction launch fewer per layer)
+        conv::Conv cg = ly.gateup.c;
+        cg.T = T;
+        const bool fold = conv::plan(cg, sms).splits == 2;
+        if (fold && run(ly.gateup, n, T, VH, gu, 2 * FF, nullptr, nullptr, nullptr, true, &ws_gu) != 2)
+            fail("vocoder: the gate/up projection did not split in two", NAVI_E_SHAPE);
+        if (!fold) run(ly.gateup, n, T, VH, gu, 2 * FF);
+        run(ly.down, fold ? ws_gu.partial : gu, T, 2 * FF, x, VH, x, l + 1 < layers.size() ? layers[l + 1].ln1 : final_norm, n, false,
+            nullptr, fold ? 2 : 1);
         snap(("layer" + std::to_string(l)).c_str(), x, T, VH);
     }
     run(out_proj, n, T, VH, u, L);
@@ -807,6 +820,9 @@ std::unique_ptr<Vocoder> Vocoder::create(const Device & dev, const DeviceWeights
     I.ws.partial = I.alloc<float>(part);
     I.ws.partial_cap = part;
     I.ws.err = I.alloc<int>(1);
+    I.ws_gu = I.ws;
+    I.ws_gu.partial_cap = 2ull * I.Cmax * 2 * I.FF;
+    I.ws_gu.partial = I.alloc<float>(I.ws_gu.partial_cap);
 
     NAVI_CUDA(cudaMallocHost(&I.h_codes, C * p.vq_n_q * sizeof(int)));
     NAVI_CUDA(cudaMallocHost(&I.h_pos0, sizeof(int)));
