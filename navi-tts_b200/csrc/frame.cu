@@ -77,6 +77,18 @@ struct Frame::Impl {
     Work w{};
     float * inv_t = nullptr, * inv_c = nullptr;
     std::vector<float> inv_t_h, inv_c_h;   // host copies (RoPE tables)
+    // talker RoPE rows [cos | sin] of the positions seen so far, computed once each: a frame's
+    // launch copies its row instead of evaluating 128 double-precision cos / sin
+    std::vector<float> rope_rows;
+    const float * rope_at(int pos) {
+        const size_t hd = 2 * inv_t_h.size();
+        while (rope_rows.size() < (static_cast<size_t>(pos) + 1) * hd) {
+            const size_t at = rope_rows.size();
+            rope_rows.resize(at + hd);
+            rope_row(inv_t_h, static_cast<int>(at / hd), rope_rows.data() + at);
+        }
+        return rope_rows.data() + static_cast<size_t>(pos) * hd;
+    }
     float * rope_c = nullptr;               // [NCB][HD] code-predictor cos | sin at positions 0..15
     float * step[MAX_B][2] = {};   // per slot: the step embedding a frame reads and the one it writes
     int cur[MAX_B] = {};
@@ -252,7 +264,7 @@ struct Frame::Impl {
                 // 4-stream launch at KV 512: 128); a short split is faster as 32 row copies in flight
                 A.kvmap[i] = A.attn_chunk[i] > 2 * KV_BOX ? kv_maps(sl, *q.kv) : nullptr;
             }
-            if (!first) rope_row(inv_t_h, q.n_past, A.rope_t[i]);
+            if (!first) std::memcpy(A.rope_t[i], rope_at(q.n_past), 2 * inv_t_h.size() * sizeof(float));
             A.first_hidden[i] = nb > 1 ? q.hidden : nullptr;
             A.first_logits[i] = nb > 1 ? q.logits : nullptr;
             A.seed[i] = q.seed;
