@@ -506,6 +506,61 @@ def run_prefill_only(args):
           "prefill_ms": float(np.median(dev_ms)), "prompt_and_prefill_wall_ms": float(np.median(wall_ms))})
 
 
+def run_phase_trace(args):
+    """`--phase-trace`: per-phase device time of the configs[1]+[2] frame at --kv on one GPU.
+    After --warmup frames, --steps traced frames stamp every phase on every CTA
+    (Frame.set_profile(True, -1)); a phase ends when its last CTA stamps its end. Prints the
+    per-phase medians over the traced frames and their sums by part of the frame."""
+    import numpy as np
+    import torch
+    from navi_b200 import engine
+    ensure_weights(0, 1)
+    dev = engine.Device(0)
+    w = engine.Weights(dev, BENCH_NAVI)
+    frame = engine.Frame(dev, w)
+    tl = w.params.talker
+    kvd = tl.n_kv_head * tl.head_dim
+    max_pos = max(2048, args.kv) + 1
+    g = torch.Generator(device="cuda:0").manual_seed(1000)
+    k = [torch.randn(max_pos, kvd, generator=g, device="cuda:0").half() for _ in range(tl.n_layer)]
+    v = [torch.randn(max_pos, kvd, generator=g, device="cuda:0").half() for _ in range(tl.n_layer)]
+    kv = engine.KvCache.wrap([t.data_ptr() for t in k], [t.data_ptr() for t in v], max_pos, kvd, keepalive=(k, v))
+    step0 = torch.randn(tl.hidden, generator=g, device="cuda:0")
+    trailing = torch.randn(tl.hidden, generator=g, device="cuda:0")
+    s = engine.Sampling(temperature=0.9, top_k=50, top_p=0.9, repetition_penalty=1.05, cp_temperature=0.9, cp_top_k=50,
+                        cp_top_p=0.9, min_frames=2, rng=1)
+    frame.set_step_in(step0.data_ptr())
+    frame.reset()
+    for i in range(args.warmup):
+        assert frame.run(kv, args.kv, trailing.data_ptr(), s, 7, i).ok
+    frame.set_profile(True, -1)
+    durs = []
+    for i in range(args.steps):
+        assert frame.run(kv, args.kv, trailing.data_ptr(), s, 7, args.warmup + i).ok
+        t0, st = frame.profile_all()                        # [G], [G, phases, 4] ns
+        ends = np.concatenate([[t0.min()], st[:, :, 3].max(axis=0)])
+        durs.append(np.diff(ends) / 1000.0)
+    frame.set_profile(False)
+    d = np.median(np.array(durs), axis=0)
+    # program order: talker layers (5 phases each), codec head, code-predictor positions 0 + 1
+    # as one pass of 26 phases (its first phase stages the codebook-0 draw), 14 passes of 26
+    # (each first phase stages the previous draw), FINAL
+    L = tl.n_layer * 5
+    cp = d[L + 1:L + 27]
+    passes = d[L + 27:-1]
+    emit({"metric": "k_frame per-phase device time (us)", "impl": "ours", "n_gpus": 1, "kv_len": args.kv, "traced_frames": args.steps,
+          "total_us": round(float(d.sum()), 1), "n_phases": int(len(d)),
+          "talker": {"us": round(float(d[:L].sum()), 1),
+                     "median_by_kind_qkv_attn_o_gu_down": [round(float(x), 2) for x in np.median(d[:L].reshape(-1, 5), axis=0)]},
+          "codec_head_us": round(float(d[L]), 2), "codebook0_draw_phase_us": round(float(d[L + 1]), 2),
+          "cp_positions_0_1_us": round(float(cp.sum()), 1),
+          "cp_positions_2_15_us": round(float(passes.sum()), 1),
+          "cp_pass_us_median": round(float(np.median(passes.reshape(-1, 26).sum(axis=1))), 1) if len(passes) % 26 == 0 else None,
+          "cp_draw_phase_us_median": round(float(np.median(passes.reshape(-1, 26)[:, 0])), 2) if len(passes) % 26 == 0 else None,
+          "final_us": round(float(d[-1]), 2),
+          "phases_us": [round(float(x), 2) for x in d]})
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -660,6 +715,7 @@ def main():
     ap.add_argument("--no-vocoder", dest="vocoder", action="store_false", help="skip the configs[3] vocoder line")
     ap.add_argument("--vocoder-only", action="store_true", help="run only the configs[3] vocoder measurement")
     ap.add_argument("--prefill-only", action="store_true", help="run only the talker prefill of the configs[4] prompt")
+    ap.add_argument("--phase-trace", action="store_true", help="per-phase device time of one frame (traced, not a bench value)")
     ap.add_argument("--voc-chunks", default="4,16", help="vocoder chunk lengths (frames), comma separated")
     ap.add_argument("--no-layer", dest="layer", action="store_false", help="skip the configs[0] single-layer line")
     ap.add_argument("--streams", type=int, default=64, help="configs[4] utterances over all GPUs (64 = the full config; 0 = skip)")
@@ -673,6 +729,8 @@ def main():
         run_vocoder_only(args)
     elif args.prefill_only:
         run_prefill_only(args)
+    elif args.phase_trace:
+        run_phase_trace(args)
     else:
         run_ours(args)
 
